@@ -1,0 +1,12 @@
+"""pytest configuration: the ``gpu`` marker and import paths for the package, the oracle and the fixtures."""
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for p in (ROOT, os.path.join(ROOT, 'breeze-tts-2-flash_b200'), os.path.join(ROOT, 'tests', 'golden')):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def pytest_configure(config):
+    config.addinivalue_line('markers', 'gpu: needs a CUDA GPU (B200, sm_100a); run with -m gpu')

@@ -1,0 +1,295 @@
+"""Generate the golden fixtures in tests/golden/ from the reference's OWN PyTorch implementation.
+
+Run in the build container, where the reference checkout is readable:
+
+    python tests/golden/make_golden.py [--ref <reference root>]
+
+It imports the reference's official modules (``third_party/breeze-tts``: ``models.breeze``,
+``models.cudagraph.backbone_graph``, ``models.cudagraph.depth_decoder_graph``) and transformers' Qwen3 layers (the
+backbone arithmetic the reference calls through ``UP/models/breeze_backbone_factory.py:163-181``), runs them on the
+CPU on the seeded inputs of ``tests/golden/synth.py`` and writes their outputs as ``*.npz``.  The reference does not
+exist on the GPU box; the committed fixtures travel instead.
+
+Version shims (the reference pins transformers 4.57.3, this image has 5.5): the default rope init function is
+registered for ``BreezeRotaryEmbedding`` (``UP/models/breeze.py:156``), and ``StaticLayer.lazy_initialization``
+accepts the one-argument call of ``backbone_graph.py:199`` / ``depth_decoder_graph.py:462``.  In 5.5 the static
+cache writes at its running length instead of ``cache_position``; both flows below write exactly the slots the 4.57.3
+cache would (prefill fills [0, P) and decode appends), which the script asserts.  5.5's ``create_causal_mask`` also
+ignores ``cache_position`` for the depth graph's decode masks (every decode mask would admit slot 0 only), so the
+depth masks are rebuilt with the 4.57.3 rule: 0 where key <= cache_position, finfo(bf16).min elsewhere.
+``module.to(torch.bfloat16)`` would also round the rotary ``inv_freq`` buffer to bf16; it is restored to the fp32
+values the rotary modules compute at construction, as a checkpoint loaded in bf16 keeps them.
+
+Sampling: ``torch.multinomial(probs, 1)`` inside the official sampler is replaced by ``argmax(probs / q)`` with q a
+fixed Exp(1) draw, the identity the reference's own kernel relies on (``flash/csrc/depth_frame.cu:6-8``), so the
+fixtures are deterministic.
+"""
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+import synth  # noqa: E402
+
+
+def ref_env(ref_root):
+    up = os.path.join(ref_root, 'third_party', 'breeze-tts')
+    sys.path.insert(0, up)
+    import transformers.cache_utils as cu
+    import models.breeze as mb
+
+    def default_rope(config=None, device=None, seq_len=None, **kw):
+        base = getattr(config, 'rope_theta', None)
+        if base is None:
+            base = config.rope_parameters['rope_theta']
+        dim = getattr(config, 'head_dim', None) or config.hidden_size // config.num_attention_heads
+        inv = 1.0 / (base ** (torch.arange(0, dim, 2, dtype=torch.int64).to(device=device, dtype=torch.float) / dim))
+        return inv, 1.0
+
+    mb.ROPE_INIT_FUNCTIONS['default'] = default_rope
+    mb.BreezeRotaryEmbedding.compute_default_rope_parameters = staticmethod(default_rope)
+    orig = cu.StaticLayer.lazy_initialization
+
+    def lazy(self, k, v=None):
+        return orig(self, k, k if v is None else v)
+
+    cu.StaticLayer.lazy_initialization = lazy
+    return up
+
+
+class _Mod:
+    """Stands in for the attention module argument of eager_attention_forward."""
+
+    def __init__(self, groups):
+        self.num_key_value_groups = groups
+        self.training = False
+
+
+def gold_attention(out):
+    from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
+    c = synth.ATTN
+    q, k, v, mask = synth.attn_inputs()
+    o, _ = eager_attention_forward(_Mod(c['NH'] // c['NKV']), q, k, v, mask, scaling=c['D'] ** -0.5)
+    out['attn'] = dict(out=synth.np_bits(o), digest=synth.digest(q, k, v, mask))
+    # fp32-upcast variant (the CPU baseline form of config 1)
+    o32, _ = eager_attention_forward(_Mod(c['NH'] // c['NKV']), q.float(), k.float(), v.float(), mask.float(),
+                                     scaling=c['D'] ** -0.5)
+    out['attn']['out_fp32'] = o32.numpy()
+
+
+def gold_gemv(out):
+    import models.breeze as mb
+    c = synth.GEMV
+    x, gamma, wg, wu, wd = synth.gemv_inputs()
+    norm = mb.BreezeRMSNorm(c['K'], eps=c['eps']).to(torch.bfloat16)
+    norm.weight.data.copy_(gamma)
+    with torch.no_grad():
+        h = norm(x)
+        act = torch.nn.functional.silu(torch.nn.functional.linear(h, wg)) * torch.nn.functional.linear(h, wu)
+        y = x + torch.nn.functional.linear(act, wd)
+    out['gemv'] = dict(norm=synth.np_bits(h), act=synth.np_bits(act), y=synth.np_bits(y),
+                       digest=synth.digest(x, gamma, wg, wu, wd))
+
+
+def _qwen3_config(c):
+    from transformers import Qwen3Config
+    cfg = Qwen3Config(hidden_size=c['H'], intermediate_size=c['F'], num_hidden_layers=c['L'],
+                      num_attention_heads=c['NH'], num_key_value_heads=c['NKV'], head_dim=c['D'],
+                      rms_norm_eps=c['eps'], rope_theta=c['theta'], vocab_size=c['vocab'],
+                      max_position_embeddings=4096, attention_bias=False)
+    cfg._attn_implementation = 'eager'
+    cfg.num_codebooks = c['ncb']
+    cfg.audio_embed_size = c['H']
+    return cfg
+
+
+def gold_backbone(out):
+    from models.breeze_backbone_factory import BreezeBackboneAdapter
+    from models.cudagraph.backbone_graph import BackboneGraph
+    c = synth.BACKBONE
+    w = synth.backbone_weights()
+    cfg = _qwen3_config(c)
+    layers, norm, rot = BreezeBackboneAdapter._create_qwen3_layers(cfg)
+    model = BreezeBackboneAdapter(cfg, layers, norm, rot)
+    inv = model.rotary_emb.inv_freq.clone()
+    model = model.to(torch.bfloat16)
+    model.rotary_emb.inv_freq = inv
+    with torch.no_grad():
+        for L, lw in zip(model.layers, w['layers']):
+            a, m = L.self_attn, L.mlp
+            L.input_layernorm.weight.copy_(lw['ln1'])
+            a.q_proj.weight.copy_(lw['wq'])
+            a.k_proj.weight.copy_(lw['wk'])
+            a.v_proj.weight.copy_(lw['wv'])
+            a.q_norm.weight.copy_(lw['qn'])
+            a.k_norm.weight.copy_(lw['kn'])
+            a.o_proj.weight.copy_(lw['wo'])
+            L.post_attention_layernorm.weight.copy_(lw['ln2'])
+            m.gate_proj.weight.copy_(lw['wg'])
+            m.up_proj.weight.copy_(lw['wu'])
+            m.down_proj.weight.copy_(lw['wd'])
+        model.norm.weight.copy_(w['norm'])
+        model.embed_tokens.embed_audio_tokens.weight.copy_(w['embed'])
+    lm_head = torch.nn.Linear(c['H'], c['vocab'], bias=False)
+    with torch.no_grad():
+        lm_head.weight.copy_(w['lm_head'])
+    g = BackboneGraph(model, lm_head, model.embed_tokens, cfg, device='cpu', dtype=torch.bfloat16,
+                      max_seq_len=c['S'], guidance_scale=c['gs'], batch_size=c['B'])
+    g.prepare_eager()
+    P = c['prefill']
+    with torch.inference_mode():
+        for li, (k, v) in enumerate(w['kv']):
+            g.static_cache.layers[li].update(k, v)
+    am = torch.ones(c['B'], P, dtype=torch.long)
+    for b, p in enumerate(c['pad']):
+        am[b, :p] = 0
+    g.set_generation_state(am)
+    g._prefill_len = P
+    hidden, cfg_logits = g.run(w['ids'], 0)
+    kv_new = []
+    for li in range(c['L']):
+        K = g.static_cache.layers[li].keys
+        V = g.static_cache.layers[li].values
+        assert torch.equal(K[:, :, :P], w['kv'][li][0]), 'prefill slots moved'
+        kv_new.append((K[:, :, P].clone(), V[:, :, P].clone()))
+        assert float(K[:, :, P + 1:].abs().sum()) == 0.0, 'decode wrote past cache_position'
+    out['backbone'] = dict(hidden=synth.np_bits(hidden), logits=g.logits_buf.numpy().copy(),
+                           cfg=cfg_logits.numpy().copy(), mask=g.attn_mask.float().numpy().copy(),
+                           position_ids=g.position_ids.numpy().copy(), cache_position=g.cache_position.numpy().copy(),
+                           k_new=np.stack([synth.np_bits(k) for k, _ in kv_new]),
+                           v_new=np.stack([synth.np_bits(v) for _, v in kv_new]),
+                           digest=synth.digest(w['embed'], w['lm_head'], *[t for kv in w['kv'] for t in kv]))
+
+
+def _patched_multinomial(qsrc):
+    """torch.multinomial(probs, 1) -> argmax(probs / q[step]) for the official sampler (one q row set per call)."""
+    state = {'i': 0}
+
+    def mult(probs, n, *a, **kw):
+        q = qsrc[state['i']]
+        state['i'] += 1
+        return torch.argmax(probs / q.to(probs.dtype), dim=-1, keepdim=True)
+
+    return mult, state
+
+
+def gold_depth(out):
+    import models.breeze as mb
+    import models.breeze_base_config as bc
+    import models.cudagraph.depth_decoder_graph as ddg
+    c = synth.DEPTH
+    w = synth.depth_weights()
+    cfg = bc.BreezeDepthDecoderConfig(num_codebooks=c['ncb'], backbone_hidden_size=c['AE'], vocab_size=c['vocab'],
+                                      hidden_size=c['H'], intermediate_size=c['F'], num_hidden_layers=c['L'],
+                                      num_attention_heads=c['NH'], num_key_value_heads=c['NKV'], head_dim=c['D'],
+                                      max_position_embeddings=64, rms_norm_eps=c['eps'], rope_theta=c['theta'])
+    cfg._attn_implementation = 'eager'
+    model = mb.BreezeDepthDecoderForCausalLM(cfg)
+    inv = model.model.rotary_emb.inv_freq.clone()
+    model = model.to(torch.bfloat16)
+    model.model.rotary_emb.inv_freq = inv
+    dm = model.model
+    assert dm.backbone_hidden_state_projector is None
+    with torch.no_grad():
+        for L, lw in zip(dm.layers, w['layers']):
+            a, m = L.self_attn, L.mlp
+            L.input_layernorm.weight.copy_(lw['ln1'])
+            a.q_proj.weight.copy_(lw['wq'])
+            a.k_proj.weight.copy_(lw['wk'])
+            a.v_proj.weight.copy_(lw['wv'])
+            a.o_proj.weight.copy_(lw['wo'])
+            L.post_attention_layernorm.weight.copy_(lw['ln2'])
+            m.gate_proj.weight.copy_(lw['wg'])
+            m.up_proj.weight.copy_(lw['wu'])
+            m.down_proj.weight.copy_(lw['wd'])
+        dm.embed_tokens.weight.copy_(w['embed'])
+        dm.inputs_embeds_projector.weight.copy_(w['proj'])
+        dm.norm.weight.copy_(w['normf'])
+        model.codebooks_head.weight.data = w['head'].clone()
+    g = ddg.DepthDecoderGraph(model, cfg, device='cpu', dtype=torch.bfloat16, do_sample=True, top_k=c['topk'],
+                              top_p=c['topp'], temperature=c['temp'], guidance_scale=c['gs'],
+                              codec_codebook_size=c['codebook_size'], fast=False, debug=True, batch_size=c['B'])
+    g.prepare_eager()
+    _fix_depth_masks(g)
+    mult, st = _patched_multinomial([w['q'][s] for s in range(c['ncb'] - 1)])
+    orig = ddg.torch.multinomial
+    ddg.torch.multinomial = mult
+    try:
+        toks = g.run(w['bh'], w['first'])
+    finally:
+        ddg.torch.multinomial = orig
+    assert st['i'] == c['ncb'] - 1
+    out['depth'] = dict(tokens=g.output_tokens.numpy().copy(), logits=g.debug_logits.numpy().copy(),
+                        ret=toks.numpy().copy(), digest=synth.digest(w['embed'], w['proj'], w['head'], w['bh'], w['q']))
+
+
+def _fix_depth_masks(g):
+    mn = torch.finfo(torch.bfloat16).min
+    S = g.max_seq
+    key = torch.arange(S)
+    pm = torch.where(key[None, :] <= torch.arange(2)[:, None], 0.0, mn).to(torch.bfloat16)
+    g.prefill_attn = pm[None, None].expand(g.batch_size, 1, 2, S).contiguous()
+    g.decode_attn = [torch.where(key <= int(p[0]), 0.0, mn).to(torch.bfloat16).view(1, 1, 1, S)
+                     .expand(g.batch_size, 1, 1, S).contiguous() for p in g.decode_cache_positions]
+
+
+def gold_sampler(out):
+    import models.cudagraph.depth_decoder_graph as ddg
+    c = synth.SAMPLER
+    lc, lu, q, params = synth.sampler_cases()
+    V = c['vocab']
+    toks = []
+    for r, (gs, temp, topk, topp, ds) in enumerate(params):
+        # the official sampler, bound to a minimal object with the buffers it reads (B = 2, half = 1)
+        o = type('S', (), {})()
+        o.batch_size, o.half, o.vocab_size, o.codec_codebook_size = 2, 1, V, c['codebook_size']
+        o.guidance_scale = torch.tensor([[gs]])
+        o.temperature_buf = torch.tensor([[temp]])
+        o.top_k_buf = torch.tensor([[topk]])
+        o.top_p_buf = torch.tensor([[topp]])
+        o.do_sample_buf = torch.tensor([ds])
+        o._max_k = min(1024, V)
+        o._topk_ranks = torch.arange(o._max_k)
+        o._debug_probs_slot = None
+        o._tok_buf = torch.zeros(2, dtype=torch.long)
+        logits = torch.stack([lc[r], lu[r]])[:, None, :].clone()
+        mult, _ = _patched_multinomial([q[r][None]])
+        orig = ddg.torch.multinomial
+        ddg.torch.multinomial = mult
+        try:
+            ddg.DepthDecoderGraph._cfg_sample(o, logits)
+        finally:
+            ddg.torch.multinomial = orig
+        toks.append(int(o._tok_buf[0].clamp(0, V - 1)))
+    out['sampler'] = dict(tokens=np.asarray(toks, np.int64), digest=synth.digest(lc, lu, q))
+
+
+def gold_prefill(out):
+    from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
+    c = synth.PREFILL
+    q, k, v, mask = synth.prefill_inputs()
+    o, _ = eager_attention_forward(_Mod(c['NH'] // c['NKV']), q, k, v, mask, scaling=c['D'] ** -0.5)
+    out['prefill'] = dict(out=synth.np_bits(o), digest=synth.digest(q, k, v, mask))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--ref', default=os.environ.get('BREEZE_REF', '/root/reference'))
+    args = ap.parse_args()
+    ref_env(args.ref)
+    torch.manual_seed(0)
+    out = {}
+    for fn in (gold_attention, gold_gemv, gold_backbone, gold_depth, gold_sampler, gold_prefill):
+        fn(out)
+        print('ok', fn.__name__, flush=True)
+    for name, d in out.items():
+        np.savez_compressed(os.path.join(HERE, f'{name}.npz'), **{k: np.asarray(v) for k, v in d.items()})
+    print('wrote', sorted(out))
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,157 @@
+"""Seeded synthetic inputs shared by the golden-fixture generator and the tests (test infrastructure).
+
+Every tensor comes from ``torch.randn`` on a CPU ``torch.Generator`` seeded per fixture, scaled, then cast to bf16,
+so the generator script (run once in the build container, next to the reference) and the tests (run anywhere with
+the same torch build) see identical values.  ``digest`` fingerprints the inputs so a fixture is never compared
+against drifted inputs.
+"""
+import hashlib
+
+import numpy as np
+import torch
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(int(seed))
+
+
+def randn_bf16(g, shape, std=1.0, mean=0.0):
+    return (torch.randn(shape, generator=g) * std + mean).to(torch.bfloat16)
+
+
+def digest(*tensors):
+    h = hashlib.sha256()
+    for t in tensors:
+        t = t.detach().cpu().contiguous()
+        if t.dtype == torch.bfloat16:
+            t = t.view(torch.int16)
+        h.update(t.numpy().tobytes())
+    return h.hexdigest()[:16]
+
+
+# ---------------------------------------------------------------- decode attention (small S)
+ATTN = dict(seed=100, B=2, NH=16, NKV=4, D=128, S=80, valid=((0, 70), (5, 70)))
+
+
+def attn_inputs(c=ATTN):
+    g = gen(c['seed'])
+    q = randn_bf16(g, (c['B'], c['NH'], 1, c['D']))
+    k = randn_bf16(g, (c['B'], c['NKV'], c['S'], c['D']))
+    v = randn_bf16(g, (c['B'], c['NKV'], c['S'], c['D']))
+    mask = torch.full((c['B'], 1, 1, c['S']), torch.finfo(torch.bfloat16).min, dtype=torch.bfloat16)
+    for b, (lo, hi) in enumerate(c['valid']):
+        mask[b, 0, 0, lo:hi + 1] = 0
+    return q, k, v, mask
+
+
+# ---------------------------------------------------------------- RMSNorm + gate/up + SiLU + down (config 2, small)
+GEMV = dict(seed=101, M=2, K=512, F=384, eps=1e-6)
+
+
+def gemv_inputs(c=GEMV):
+    g = gen(c['seed'])
+    x = randn_bf16(g, (c['M'], c['K']))
+    gamma = randn_bf16(g, (c['K'],), std=0.1, mean=1.0)
+    wg = randn_bf16(g, (c['F'], c['K']), std=0.02)
+    wu = randn_bf16(g, (c['F'], c['K']), std=0.02)
+    wd = randn_bf16(g, (c['K'], c['F']), std=0.02)
+    return x, gamma, wg, wu, wd
+
+
+# ---------------------------------------------------------------- backbone decode step (config 3, reduced)
+BACKBONE = dict(seed=102, B=2, H=512, NH=8, NKV=2, D=128, F=1024, L=2, vocab=65, ncb=16, theta=1e6, eps=1e-6,
+                S=96, prefill=60, pad=(0, 3), gs=4.0)
+
+
+def backbone_weights(c=BACKBONE):
+    """Returns a dict of bf16 tensors (lm_head fp32, bf16-exact)."""
+    g = gen(c['seed'])
+    H, NH, NKV, D, F = c['H'], c['NH'], c['NKV'], c['D'], c['F']
+    layers = []
+    for _ in range(c['L']):
+        layers.append(dict(
+            ln1=randn_bf16(g, (H,), 0.1, 1.0), wq=randn_bf16(g, (NH * D, H), 0.02), wk=randn_bf16(g, (NKV * D, H), 0.02),
+            wv=randn_bf16(g, (NKV * D, H), 0.02), qn=randn_bf16(g, (D,), 0.1, 1.0), kn=randn_bf16(g, (D,), 0.1, 1.0),
+            wo=randn_bf16(g, (H, NH * D), 0.02), ln2=randn_bf16(g, (H,), 0.1, 1.0), wg=randn_bf16(g, (F, H), 0.02),
+            wu=randn_bf16(g, (F, H), 0.02), wd=randn_bf16(g, (H, F), 0.02)))
+    norm = randn_bf16(g, (H,), 0.1, 1.0)
+    embed = randn_bf16(g, (c['ncb'] * c['vocab'], H), 1.0)
+    lm_head = randn_bf16(g, (c['vocab'], H), 0.02).float()
+    kv = [(randn_bf16(g, (c['B'], NKV, c['prefill'], D)), randn_bf16(g, (c['B'], NKV, c['prefill'], D)))
+          for _ in range(c['L'])]
+    ids = torch.randint(0, c['vocab'], (c['B'], 1, c['ncb']), generator=g)
+    return dict(layers=layers, norm=norm, embed=embed, lm_head=lm_head, kv=kv, ids=ids)
+
+
+# ---------------------------------------------------------------- depth frame (config 4, reduced)
+DEPTH = dict(seed=103, B=2, H=256, AE=384, NH=2, NKV=1, D=128, F=512, L=2, vocab=64, codebook_size=60, ncb=6,
+             theta=500000.0, eps=1e-5, gs=4.0, temp=0.9, topk=50, topp=1.0, q_seed=42)
+
+
+def depth_weights(c=DEPTH):
+    g = gen(c['seed'])
+    H, AE, NH, NKV, D, F = c['H'], c['AE'], c['NH'], c['NKV'], c['D'], c['F']
+    layers = []
+    for _ in range(c['L']):
+        layers.append(dict(
+            ln1=randn_bf16(g, (H,), 0.1, 1.0), wq=randn_bf16(g, (NH * D, H), 0.02), wk=randn_bf16(g, (NKV * D, H), 0.02),
+            wv=randn_bf16(g, (NKV * D, H), 0.02), wo=randn_bf16(g, (H, NH * D), 0.02), ln2=randn_bf16(g, (H,), 0.1, 1.0),
+            wg=randn_bf16(g, (F, H), 0.02), wu=randn_bf16(g, (F, H), 0.02), wd=randn_bf16(g, (H, F), 0.02)))
+    embed = randn_bf16(g, (c['ncb'] * c['vocab'], AE), 1.0)
+    proj = randn_bf16(g, (H, AE), 0.02)
+    normf = randn_bf16(g, (H,), 0.1, 1.0)
+    head = randn_bf16(g, (c['ncb'] - 1, H, c['vocab']), 0.02).float()
+    bh = randn_bf16(g, (c['B'], AE), 1.0)
+    first = torch.randint(0, c['codebook_size'], (c['B'] // 2,), generator=g).repeat(2)
+    gq = gen(c['q_seed'])
+    q = torch.empty(c['ncb'] - 1, c['B'] // 2, c['vocab']).exponential_(1.0, generator=gq)
+    return dict(layers=layers, embed=embed, proj=proj, normf=normf, head=head, bh=bh, first=first, q=q)
+
+
+# ---------------------------------------------------------------- sampler rows (real vocab 2051, codebook 2048)
+SAMPLER = dict(seed=104, rows=48, vocab=2051, codebook_size=2048)
+
+
+def sampler_cases(c=SAMPLER):
+    """Per row: cond/uncond logits, q, and parameters (gs, temp, topk, topp, dosample) covering the edge cases."""
+    g = gen(c['seed'])
+    V = c['vocab']
+    params = []
+    ks = [50, 1, 0, 1024, 64, 65, 7, 300]
+    ps = [1.0, 0.9, 0.5, 0.0, 1.0, 0.95]
+    for r in range(c['rows']):
+        params.append((float([1.0, 4.0, 0.0, 2.5][r % 4]), float([0.9, 1.0, 0.5, 1.3][(r // 4) % 4]),
+                       int(ks[r % len(ks)]), float(ps[(r // 3) % len(ps)]), int(r % 11 != 5)))
+    lc = torch.randn((c['rows'], V), generator=g) * 3.0
+    lu = lc + torch.randn((c['rows'], V), generator=g) * 0.5
+    # exact ties in a few rows: duplicate the best logit at a higher index
+    for r in range(0, c['rows'], 6):
+        j = int(torch.argmax(lc[r]))
+        lc[r, (j + 17) % 2048] = lc[r, j]
+        lu[r, (j + 17) % 2048] = lu[r, j]
+    q = torch.empty((c['rows'], V)).exponential_(1.0, generator=g)
+    return lc, lu, q, params
+
+
+# ---------------------------------------------------------------- causal prefill attention (config 5, small L)
+PREFILL = dict(seed=105, B=2, NH=16, NKV=4, D=128, L=40, pad=(0, 6))
+
+
+def prefill_inputs(c=PREFILL):
+    g = gen(c['seed'])
+    q = randn_bf16(g, (c['B'], c['NH'], c['L'], c['D']))
+    k = randn_bf16(g, (c['B'], c['NKV'], c['L'], c['D']))
+    v = randn_bf16(g, (c['B'], c['NKV'], c['L'], c['D']))
+    L = c['L']
+    qi = torch.arange(L).view(L, 1)
+    ki = torch.arange(L).view(1, L)
+    mask = torch.full((c['B'], 1, L, L), torch.finfo(torch.bfloat16).min, dtype=torch.bfloat16)
+    for b, p in enumerate(c['pad']):
+        allowed = (ki <= qi) & (ki >= p)
+        mask[b, 0].masked_fill_(allowed, 0.0)
+    return q, k, v, mask
+
+
+def np_bits(t):
+    """bf16 tensor -> uint16 numpy array of its bit patterns."""
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)

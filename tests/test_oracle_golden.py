@@ -1,0 +1,142 @@
+"""Pins the CPU oracle to the reference: every fixture in tests/golden/ was produced by the reference's own
+PyTorch modules (tests/golden/make_golden.py); the oracle must reproduce it on the same seeded inputs."""
+import numpy as np
+import pytest
+
+import synth
+from oracle import decode as dec
+from oracle import depth as dep
+from oracle import sampler as smp
+from oracle.bf16 import bits_to_f32, from_torch as ft, round_bf16
+
+GOLD = synth.__file__.rsplit('/', 1)[0]
+
+
+def load(name):
+    return np.load(f'{GOLD}/{name}.npz')
+
+
+def rel(a, b):
+    return float(np.max(np.abs(a - b)) / max(float(np.max(np.abs(b))), 1e-30))
+
+
+def test_bf16_rounding_matches_torch():
+    import torch
+    x = torch.randn(100000, generator=torch.Generator().manual_seed(7)) * 1e3
+    x[:4] = torch.tensor([float('inf'), -float('inf'), 3.3895313892515355e38, 1.0 + 2 ** -8])
+    ref = ft(x.to(torch.bfloat16))
+    got = round_bf16(x.numpy())
+    assert np.array_equal(ref, got)
+
+
+def test_attention_decode_golden():
+    z = load('attn')
+    q, k, v, m = synth.attn_inputs()
+    assert str(z['digest']) == synth.digest(q, k, v, m)
+    out = dec.attn_decode(ft(q), ft(k), ft(v), ft(m), synth.ATTN['D'] ** -0.5)
+    assert np.array_equal(out, bits_to_f32(z['out']))
+
+
+def test_gemv_swiglu_golden():
+    z = load('gemv')
+    x, g, wg, wu, wd = synth.gemv_inputs()
+    assert str(z['digest']) == synth.digest(x, g, wg, wu, wd)
+    eps = synth.GEMV['eps']
+    assert np.array_equal(dec.rmsnorm(ft(x), ft(g), eps), bits_to_f32(z['norm']))
+    act = dec.gemv_gateup(ft(x), ft(g), eps, ft(wg), ft(wu))
+    assert np.array_equal(act, bits_to_f32(z['act']))
+    y = dec.gemv_resid(act, ft(wd), ft(x))
+    assert np.array_equal(y, bits_to_f32(z['y']))
+
+
+def _backbone_oracle():
+    c = synth.BACKBONE
+    w = synth.backbone_weights()
+    layers = [{k: ft(v) for k, v in L.items()} for L in w['layers']]
+    W = dec.BackboneWeights(layers, ft(w['norm']), ft(w['embed']), w['lm_head'].numpy(), c['vocab'], c['eps'],
+                            c['theta'])
+    S, P = c['S'], c['prefill']
+    kcs = [np.zeros((c['B'], c['NKV'], S, c['D']), np.float32) for _ in range(c['L'])]
+    vcs = [np.zeros_like(x) for x in kcs]
+    for li, (k, v) in enumerate(w['kv']):
+        kcs[li][:, :, :P] = ft(k)
+        vcs[li][:, :, :P] = ft(v)
+    return c, w, W, kcs, vcs
+
+
+def test_backbone_step_golden():
+    z = load('backbone')
+    c, w, W, kcs, vcs = _backbone_oracle()
+    assert str(z['digest']) == synth.digest(w['embed'], w['lm_head'], *[t for kv in w['kv'] for t in kv])
+    P = c['prefill']
+    h, logits, cfg = dec.backbone_step(W, w['ids'].numpy()[:, 0, :], kcs, vcs, z['mask'], P,
+                                       z['position_ids'].reshape(-1), c['gs'])
+    assert np.array_equal(h, bits_to_f32(z['hidden']).reshape(h.shape))
+    for li in range(c['L']):
+        assert np.array_equal(kcs[li][:, :, P], bits_to_f32(z['k_new'][li]))
+        assert np.array_equal(vcs[li][:, :, P], bits_to_f32(z['v_new'][li]))
+    # fp32 lm_head: only the matmul summation order differs from torch
+    assert rel(logits, z['logits']) < 1e-5
+    assert rel(cfg, z['cfg']) < 1e-5
+    assert np.array_equal(np.argmax(cfg, -1), np.argmax(z['cfg'], -1))
+
+
+def depth_oracle_weights():
+    c = synth.DEPTH
+    w = synth.depth_weights()
+    layers = [{k: ft(v) for k, v in L.items()} for L in w['layers']]
+    W = dep.DepthWeights(layers, ft(w['embed']), ft(w['proj']), ft(w['normf']), w['head'].numpy(), c['vocab'],
+                         c['codebook_size'], c['ncb'] - 1, c['eps'], c['theta'], c['NH'], c['NKV'])
+    return c, w, W
+
+
+@pytest.mark.parametrize('sampler', ['c', 'torch'])
+def test_depth_frame_golden(sampler):
+    z = load('depth')
+    c, w, W = depth_oracle_weights()
+    assert str(z['digest']) == synth.digest(w['embed'], w['proj'], w['head'], w['bh'], w['q'])
+    toks, logits, _ = dep.depth_frame(W, ft(w['bh']), w['first'].numpy(), w['q'].numpy(), [c['temp']], [c['topk']],
+                                      [c['topp']], [1], [c['gs']], sampler=sampler)
+    assert np.array_equal(toks, z['tokens'])
+    assert rel(logits, z['logits']) < 1e-5
+
+
+def test_sampler_golden_bit_exact_c():
+    z = load('sampler')
+    lc, lu, q, params = synth.sampler_cases()
+    assert str(z['digest']) == synth.digest(lc, lu, q)
+    cs = synth.SAMPLER['codebook_size']
+    toks = [smp.sample_row(lc[r].numpy(), lu[r].numpy(), cs, *params[r], q[r].numpy())[0] for r in range(len(params))]
+    assert toks == list(z['tokens'])
+
+
+def test_sampler_torch_restatement_golden():
+    z = load('sampler')
+    lc, lu, q, params = synth.sampler_cases()
+    V, cs = synth.SAMPLER['vocab'], synth.SAMPLER['codebook_size']
+    toks = [smp.sample_row_torch(lc[r].numpy(), lu[r].numpy(), V, cs, *params[r], q[r].numpy())[0]
+            for r in range(len(params))]
+    assert toks == list(z['tokens'])
+
+
+def test_prefill_attention_golden():
+    z = load('prefill')
+    q, k, v, m = synth.prefill_inputs()
+    assert str(z['digest']) == synth.digest(q, k, v, m)
+    out = dec.attention_eager(ft(q), ft(k), ft(v), ft(m), synth.PREFILL['D'] ** -0.5)
+    ref = bits_to_f32(z['out'])
+    # rows with every key masked (left padding) are 0 here, the eager mean of V there; they never reach the output
+    live = np.ones(out.shape[:2], bool)
+    for b, p in enumerate(synth.PREFILL['pad']):
+        live[b, :p] = False
+    assert np.array_equal(out[live], ref[live])
+
+
+def test_fb_exp_accuracy():
+    x = np.concatenate([np.linspace(-103, 0, 200001, dtype=np.float32), -np.logspace(-8, 1, 1000).astype(np.float32)])
+    y = smp.fb_exp(x).astype(np.float64)
+    ref = np.exp(x.astype(np.float64))
+    ok = ref > 1.2e-38
+    ulp = np.spacing(ref[ok].astype(np.float32)).astype(np.float64)
+    assert np.max(np.abs(y[ok] - ref[ok]) / ulp) <= 2.0
+    assert smp.fb_exp(np.array([-np.inf, -200.0], np.float32)).tolist() == [0.0, 0.0]
