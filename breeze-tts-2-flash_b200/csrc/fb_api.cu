@@ -1,0 +1,118 @@
+// flashb: library-level C ABI (error reporting, device error word, launch helper).
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <mutex>
+
+#include "fb_common.cuh"
+
+// The device error word: kernels whose bounded wait expires record an FB_ERR_* code here (first one wins).
+__device__ unsigned g_fb_error_word;
+
+namespace {
+thread_local char t_msg[1024] = "";
+std::mutex g_mu;
+unsigned* g_err_ptr[64] = {nullptr};
+int g_sms[64] = {0};
+int g_pdl = -1;
+}  // namespace
+
+namespace fbh {
+
+void set_msg(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_msg, sizeof(t_msg), fmt, ap);
+  va_end(ap);
+}
+
+unsigned* device_err_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_err_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fb_error_word) == cudaSuccess) g_err_ptr[dev] = (unsigned*)p;
+  }
+  return g_err_ptr[dev];
+}
+
+int num_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!g_sms[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_sms[dev] = n > 0 ? n : 148;
+  }
+  return g_sms[dev];
+}
+
+bool pdl_enabled() {
+  if (g_pdl < 0) {
+    const char* e = getenv("FLASHB_PDL");
+    g_pdl = (e && e[0] == '0') ? 0 : 1;
+  }
+  return g_pdl == 1;
+}
+
+int launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args, bool pdl,
+               int cluster_x) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (pdl && pdl_enabled()) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster_x > 0) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = cluster_x;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = na ? at : nullptr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelExC(&cfg, func, args);
+  if (e != cudaSuccess) {
+    set_msg("kernel launch (grid %u x %u x %u, block %u, smem %zu): %s", grid.x, grid.y, grid.z, block.x, smem,
+            cudaGetErrorString(e));
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}
+
+}  // namespace fbh
+
+extern "C" const char* flashb_last_error(void) { return t_msg; }
+
+extern "C" const char* flashb_version(void) { return "flashb 0.1 sm_100a"; }
+
+extern "C" void flashb_set_pdl(int enable) { g_pdl = enable ? 1 : 0; }
+
+extern "C" int flashb_device_error(int clear) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    fbh::set_msg("device error check: %s", cudaGetErrorString(e));
+    return FB_ERR_CUDA;
+  }
+  unsigned v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_fb_error_word, sizeof(v));
+  if (e != cudaSuccess) {
+    fbh::set_msg("device error check: %s", cudaGetErrorString(e));
+    return FB_ERR_CUDA;
+  }
+  if (clear && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_fb_error_word, &z, sizeof(z));
+  }
+  if (v) fbh::set_msg("device error word = %u (a bounded device-side wait expired)", v);
+  return (int)v;
+}

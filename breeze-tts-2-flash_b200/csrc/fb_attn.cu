@@ -1,0 +1,431 @@
+// flashb: GQA split-KV flash-decoding attention for the backbone single-token decode step.
+//
+// Semantics (eager attention, transformers Qwen3 / UP/models/breeze.py:259-286, for q_len == 1):
+//   s = bf16(q . k) ; s = bf16(s * scaling) ; s = s + mask (bf16 add for a bf16 mask, fp32 for an fp32 mask)
+//   p = softmax_fp32(s) ; out = bf16(p . v)
+// Keys whose additive mask is <= -1e30 are skipped; a row without any valid key gives 0.  Rounding points differ
+// from eager in one place: the probabilities stay fp32 (eager rounds p to bf16 before p . v) because each split
+// only knows its own running max; the effect is below bf16 resolution of the output.
+// Fused variant (attn_decode_fused): Qwen3 q_norm / k_norm (RMSNorm over head_dim, eager double rounding) + RoPE
+// (bf16(bf16(y*cos) + bf16(rotate_half(y)*sin))) and the KV-cache write at cache_pos, attending over
+// [0, min(S, cache_pos + 1)): the official decode mask admits no key after the written slot
+// (UP/models/cudagraph/backbone_graph.py:239-252), so the split range follows the real sequence length.
+//
+// B200 design: grid (nsplit, NKV, B) launched as thread-block clusters of nsplit CTAs (<= 16), one cluster per
+// (b, kv-head).  Each CTA streams its key range in 64-position chunks (K and V rows are contiguous per (b, kv-head):
+// one 16 KB bulk copy each, double-buffered in shared memory).  In the fused variant the first chunks are requested
+// BEFORE griddepcontrol.wait (old cache slots are not written by the preceding kernel), so the KV stream overlaps the
+// QKV GEMV's tail under PDL.  Scores use half-warp dot products from shared memory, an online softmax per q head of
+// the GQA group, and P.V with one thread per head dimension.  The split partials (m, l, o[128]) stay in each CTA's
+// shared memory; after a cluster barrier, CTA g of the cluster merges head g by reading its peers' partials through
+// distributed shared memory (in split order, so the result is deterministic) -- no global workspace, no atomics.
+#include <cooperative_groups.h>
+
+#include "fb_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace fb {
+
+constexpr int AT_D = 128;
+constexpr int AT_THREADS = 128;
+constexpr int AT_CHUNK = 64;
+constexpr int AT_MAXCLUSTER = 16;   // splits per (b, kv-head) = CTAs per cluster (non-portable size 16)
+
+struct AttnArgs {
+  const bf16* q;
+  long q_sb, q_sh;
+  const bf16* qkv;
+  long qkv_sb;
+  const bf16* qn_w;
+  const bf16* kn_w;
+  float eps;
+  const bf16* cos;
+  const bf16* sin;
+  long cs_sb;
+  bf16* kc;
+  bf16* vc;
+  long c_sb, c_sh;
+  const void* mask;
+  long m_sb;
+  int mask_bf16;
+  const long long* cache_pos;
+  float scaling;
+  float* ws;
+  int* counters;
+  bf16* out;
+  int S, NH, NKV, nsplit;
+  unsigned* err;
+};
+
+// RMSNorm over 128 dims + RoPE for one head; lane owns dims [4*lane, 4*lane + 4).
+__device__ __forceinline__ void norm_rope_head(const bf16* x, const bf16* w, float eps, const bf16* cs,
+                                               const bf16* sn, int lane, float out[4]) {
+  const int d0 = lane * 4;
+  const uint2 xv = *reinterpret_cast<const uint2*>(x + d0);
+  float v[4] = {lo_f(xv.x), hi_f(xv.x), lo_f(xv.y), hi_f(xv.y)};
+  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / (float)AT_D + eps);
+  float y[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) y[j] = rbf(b2f(w[d0 + j]) * rbf(v[j] * r));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float partner = __shfl_xor_sync(FULL, y[j], 16);
+    const float rot = lane < 16 ? -partner : partner;
+    out[j] = rbf(rbf(y[j] * b2f(cs[d0 + j])) + rbf(rot * b2f(sn[d0 + j])));
+  }
+}
+
+template <int G, bool FUSED>
+__global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  bf16* sK = reinterpret_cast<bf16*>(smem);                       // [2][CHUNK][D]
+  bf16* sV = sK + 2 * AT_CHUNK * AT_D;                            // [2][CHUNK][D]
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ float q_s[G][AT_D];
+  __shared__ float p_s[G][AT_CHUNK];
+  __shared__ float mrow[AT_CHUNK];
+  __shared__ float st_m[G], st_l[G], st_scale[G];
+  __shared__ __align__(8) bf16 newk[AT_D];
+  __shared__ __align__(8) bf16 newv[AT_D];
+  __shared__ __align__(16) float part_o[G][AT_D];                 // this split's unnormalised o, read by peers
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int nsplit = a.nsplit;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int NH = a.NH;
+
+  long long pos = -1;
+  int len = a.S;
+  if (FUSED) {
+    pos = a.cache_pos[0];
+    len = (int)min((long long)a.S, pos + 1);
+    if (len < 0) len = 0;
+  }
+  const int p_begin = (int)((long long)len * split / nsplit);
+  const int p_end = (int)((long long)len * (split + 1) / nsplit);
+  const int nchunks = (p_end - p_begin + AT_CHUNK - 1) / AT_CHUNK;
+  const bf16* kbase = a.kc + (size_t)b * a.c_sb + (size_t)h * a.c_sh;
+  const bf16* vbase = a.vc + (size_t)b * a.c_sb + (size_t)h * a.c_sh;
+
+  if (tid == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int c) {
+    const int s = c & 1;
+    const int p0 = p_begin + c * AT_CHUNK;
+    const int n = min(AT_CHUNK, p_end - p0);
+    const unsigned bytes = (unsigned)(n * AT_D * 2);
+    mbar_arrive_expect_tx(&full[s], 2 * bytes);
+    bulk_g2s(sK + (size_t)s * AT_CHUNK * AT_D, kbase + (size_t)p0 * AT_D, bytes, &full[s]);
+    bulk_g2s(sV + (size_t)s * AT_CHUNK * AT_D, vbase + (size_t)p0 * AT_D, bytes, &full[s]);
+  };
+  if (FUSED && tid == 0) {
+    for (int c = 0; c < min(2, nchunks); ++c) issue(c);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (!FUSED && tid == 0) {
+    for (int c = 0; c < min(2, nchunks); ++c) issue(c);
+  }
+
+  // ---- queries of this GQA group (and, in the owner CTA, the new key / value)
+  for (int g = warp; g < G; g += AT_THREADS / 32) {
+    const int hq = h * G + g;
+    if (FUSED) {
+      float qv[4];
+      norm_rope_head(a.qkv + (size_t)b * a.qkv_sb + (size_t)hq * AT_D, a.qn_w, a.eps, a.cos + (size_t)b * a.cs_sb,
+                     a.sin + (size_t)b * a.cs_sb, lane, qv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q_s[g][lane * 4 + j] = qv[j];
+    } else {
+      const bf16* qp = a.q + (size_t)b * a.q_sb + (size_t)hq * a.q_sh;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q_s[g][lane * 4 + j] = b2f(qp[lane * 4 + j]);
+    }
+  }
+  const bool owner = FUSED && pos >= p_begin && pos < p_end;
+  if (owner) {
+    if (warp == 0) {
+      float kv[4];
+      norm_rope_head(a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AT_D, a.kn_w, a.eps,
+                     a.cos + (size_t)b * a.cs_sb, a.sin + (size_t)b * a.cs_sb, lane, kv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) newk[lane * 4 + j] = __float2bfloat16_rn(kv[j]);
+    } else if (warp == 1) {
+      const bf16* vp = a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + a.NKV + h) * AT_D;
+      *reinterpret_cast<uint2*>(&newv[lane * 4]) = *reinterpret_cast<const uint2*>(vp + lane * 4);
+    }
+  }
+  if (tid < G) {
+    st_m[tid] = -INFINITY;
+    st_l[tid] = 0.f;
+  }
+  __syncthreads();
+  if (owner) {
+    bf16* kd = a.kc + (size_t)b * a.c_sb + (size_t)h * a.c_sh + (size_t)pos * AT_D;
+    bf16* vd = a.vc + (size_t)b * a.c_sb + (size_t)h * a.c_sh + (size_t)pos * AT_D;
+    kd[tid] = newk[tid];
+    vd[tid] = newv[tid];
+  }
+
+  float qf[G][8];
+  const int l16 = lane & 15, hw = lane >> 4;
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) qf[g][j] = q_s[g][l16 * 8 + j];
+  float o[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) o[g] = 0.f;
+
+  bool ok = true;
+  for (int c = 0; c < nchunks; ++c) {
+    const int s = c & 1;
+    const int p0 = p_begin + c * AT_CHUNK;
+    const int n = min(AT_CHUNK, p_end - p0);
+    ok = __syncthreads_and(mbar_wait(&full[s], (c >> 1) & 1, a.err));
+    if (!ok) break;
+    bf16* ks = sK + (size_t)s * AT_CHUNK * AT_D;
+    bf16* vs = sV + (size_t)s * AT_CHUNK * AT_D;
+    if (owner && pos >= p0 && pos < p0 + n) {
+      ks[(size_t)(pos - p0) * AT_D + tid] = newk[tid];
+      vs[(size_t)(pos - p0) * AT_D + tid] = newv[tid];
+    }
+    if (tid < AT_CHUNK) {
+      float m = -INFINITY;
+      if (tid < n) {
+        const size_t mi = (size_t)b * a.m_sb + p0 + tid;
+        m = a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi]) : reinterpret_cast<const float*>(a.mask)[mi];
+      }
+      mrow[tid] = m;
+    }
+    __syncthreads();
+    // scores: half-warp per key, 8 keys per pass over the 4 warps
+    for (int j0 = 0; j0 < n; j0 += 8) {
+      const int j = j0 + warp * 2 + hw;
+      float kf[8];
+      if (j < n) {
+        cvt8(*reinterpret_cast<const uint4*>(ks + (size_t)j * AT_D + l16 * 8), kf);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) kf[t] = 0.f;
+      }
+      float d[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float acc = 0.f;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) acc = fmaf(qf[g][t], kf[t], acc);
+        d[g] = acc;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) d[g] += __shfl_xor_sync(FULL, d[g], off);
+      if (l16 == 0 && j < n) {
+        const float m = mrow[j];
+        const bool valid = m > -1e30f;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float sc = rbf(rbf(d[g]) * a.scaling);
+          sc = a.mask_bf16 ? rbf(sc + m) : sc + m;
+          p_s[g][j] = valid ? sc : -INFINITY;
+        }
+      }
+    }
+    __syncthreads();
+    // online softmax statistics, one warp per head
+    for (int g = warp; g < G; g += AT_THREADS / 32) {
+      const float s0 = lane < n ? p_s[g][lane] : -INFINITY;
+      const float s1 = lane + 32 < n ? p_s[g][lane + 32] : -INFINITY;
+      const float cm = warp_max(fmaxf(s0, s1));
+      const float mold = st_m[g];
+      const float mnew = fmaxf(mold, cm);
+      const bool any = mnew > -INFINITY;
+      const float e0 = (any && s0 > -INFINITY) ? expf(s0 - mnew) : 0.f;
+      const float e1 = (any && s1 > -INFINITY) ? expf(s1 - mnew) : 0.f;
+      if (lane < n) p_s[g][lane] = e0;
+      if (lane + 32 < n) p_s[g][lane + 32] = e1;
+      const float es = warp_sum(e0 + e1);
+      if (lane == 0) {
+        const float scale = (mold > -INFINITY) ? expf(mold - mnew) : 0.f;
+        st_scale[g] = scale;
+        st_l[g] = st_l[g] * scale + es;
+        st_m[g] = mnew;
+      }
+    }
+    __syncthreads();
+    // P . V, thread = head dimension
+#pragma unroll
+    for (int g = 0; g < G; ++g) o[g] *= st_scale[g];
+    for (int j = 0; j < n; ++j) {
+      const float v = b2f(vs[(size_t)j * AT_D + tid]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) o[g] = fmaf(p_s[g][j], v, o[g]);
+    }
+    __syncthreads();
+    if (tid == 0 && c + 2 < nchunks) issue(c + 2);
+  }
+  if (!ok) {  // timed out: publish an empty partial so the cluster still completes its barriers
+#pragma unroll
+    for (int g = 0; g < G; ++g) o[g] = 0.f;
+    if (tid < G) {
+      st_m[tid] = -INFINITY;
+      st_l[tid] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) part_o[g][tid] = o[g];
+
+  // ---- merge across the cluster through distributed shared memory
+  cluster.sync();
+  for (int g = split; g < G; g += nsplit) {
+    float mv[AT_MAXCLUSTER], lv[AT_MAXCLUSTER], ov[AT_MAXCLUSTER];
+#pragma unroll
+    for (int sp = 0; sp < AT_MAXCLUSTER; ++sp) {  // all peer loads issued together
+      if (sp < nsplit) {
+        mv[sp] = *cluster.map_shared_rank(&st_m[g], sp);
+        lv[sp] = *cluster.map_shared_rank(&st_l[g], sp);
+        ov[sp] = *cluster.map_shared_rank(&part_o[g][tid], sp);
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int sp = 0; sp < AT_MAXCLUSTER; ++sp)
+      if (sp < nsplit) M = fmaxf(M, mv[sp]);
+    float L = 0.f, O = 0.f;
+    if (M > -INFINITY) {
+#pragma unroll
+      for (int sp = 0; sp < AT_MAXCLUSTER; ++sp) {
+        if (sp < nsplit && mv[sp] > -INFINITY) {
+          const float f = expf(mv[sp] - M);
+          L = fmaf(lv[sp], f, L);
+          O = fmaf(ov[sp], f, O);
+        }
+      }
+    }
+    const float r = L > 0.f ? O / L : 0.f;
+    a.out[((size_t)b * NH + h * G + g) * AT_D + tid] = __float2bfloat16_rn(r);
+  }
+  cluster.sync();  // peers' shared memory must stay alive until every merge has read it
+}
+
+}  // namespace fb
+
+namespace {
+using namespace fb;
+
+constexpr size_t AT_SMEM = 4 * (size_t)AT_CHUNK * AT_D * 2;  // K and V, two stages
+
+int pick_nsplit(int B, int NKV, int S) {
+  const int target = 2 * fbh::num_sms();
+  int ns = (target + B * NKV - 1) / (B * NKV);
+  const int cap_len = (S + 15) / 16;
+  if (ns > cap_len) ns = cap_len;
+  if (ns > AT_MAXCLUSTER) ns = AT_MAXCLUSTER;
+  return ns < 1 ? 1 : ns;
+}
+
+template <int G, bool FUSED>
+int launch_attn_t(AttnArgs& a, int B, cudaStream_t st) {
+  auto kern = attn_decode_kernel<G, FUSED>;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AT_SMEM);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) {
+      fbh::set_msg("attn: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return FB_ERR_CUDA;
+    }
+    attr_done[dev] = 1;
+  }
+  void* args[] = {(void*)&a};
+  return fbh::launch_pdl((const void*)kern, dim3(a.nsplit, a.NKV, B), dim3(AT_THREADS), AT_SMEM, st, args, true,
+                         a.nsplit);
+}
+
+template <bool FUSED>
+int dispatch_g(AttnArgs& a, int B, int G, cudaStream_t st) {
+  switch (G) {
+    case 1: return launch_attn_t<1, FUSED>(a, B, st);
+    case 2: return launch_attn_t<2, FUSED>(a, B, st);
+    case 4: return launch_attn_t<4, FUSED>(a, B, st);
+    case 8: return launch_attn_t<8, FUSED>(a, B, st);
+    default: fbh::set_msg("attn: GQA group %d not built (1, 2, 4, 8)", G); return FB_ERR_UNSUPPORTED;
+  }
+}
+
+int fill_common(AttnArgs& a, const void* kc, const void* vc, int64_t c_sb, int64_t c_sh, int B, int NH, int NKV,
+                int S, int D, const void* mask, int mask_is_bf16, int64_t m_sb, float scaling, float* ws,
+                int64_t ws_floats, int32_t* counters, void* out) {
+  (void)ws;
+  (void)ws_floats;
+  (void)counters;
+  FB_CHECK_ARG(kc && vc && mask && out, "attn: null pointer argument");
+  if (D != AT_D) {
+    fbh::set_msg("attn: head_dim %d not built (128)", D);
+    return FB_ERR_UNSUPPORTED;
+  }
+  FB_CHECK_ARG(B >= 1 && NKV >= 1 && NH >= NKV && NH % NKV == 0 && S >= 1, "attn: bad shape B=%d NH=%d NKV=%d S=%d",
+               B, NH, NKV, S);
+  FB_CHECK_ARG(((uintptr_t)kc & 15) == 0 && ((uintptr_t)vc & 15) == 0 && c_sb % 8 == 0 && c_sh % 8 == 0,
+               "attn: KV cache must be 16-byte aligned with strides multiple of 8 elements");
+  FB_CHECK_ARG(c_sh >= (int64_t)S * D && c_sb >= c_sh * NKV, "attn: KV strides overlap");
+  FB_CHECK_ARG(B <= 65535 && NKV <= 65535, "attn: grid too large");
+  a.kc = (bf16*)kc; a.vc = (bf16*)vc; a.c_sb = (long)c_sb; a.c_sh = (long)c_sh;
+  a.mask = mask; a.mask_bf16 = mask_is_bf16 ? 1 : 0; a.m_sb = (long)m_sb;
+  a.scaling = scaling; a.ws = nullptr; a.counters = nullptr; a.out = (bf16*)out;
+  a.S = S; a.NH = NH; a.NKV = NKV;
+  a.nsplit = pick_nsplit(B, NKV, S);
+  a.err = fbh::device_err_ptr();
+  return FB_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t flashb_attn_ws_floats(int B, int NH, int NKV, int S, int D) {
+  (void)B; (void)NH; (void)NKV; (void)S; (void)D;
+  return 0;  // split partials are merged in distributed shared memory; no global workspace is needed
+}
+
+extern "C" int flashb_attn_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* kc, const void* vc,
+                                  int64_t c_sb, int64_t c_sh, int B, int NH, int NKV, int S, int D, const void* mask,
+                                  int mask_is_bf16, int64_t m_sb, float scaling, float* ws, int64_t ws_floats,
+                                  int32_t* counters, void* out, void* stream) {
+  AttnArgs a{};
+  int rc = fill_common(a, kc, vc, c_sb, c_sh, B, NH, NKV, S, D, mask, mask_is_bf16, m_sb, scaling, ws, ws_floats,
+                       counters, out);
+  if (rc) return rc;
+  FB_CHECK_ARG(q && ((uintptr_t)q & 7) == 0 && q_sh % 4 == 0 && q_sb % 4 == 0, "attn_decode: q misaligned");
+  a.q = (const bf16*)q; a.q_sb = (long)q_sb; a.q_sh = (long)q_sh;
+  return dispatch_g<false>(a, B, NH / NKV, (cudaStream_t)stream);
+}
+
+extern "C" int flashb_attn_decode_fused(const void* qkv, int64_t qkv_sb, const void* qn_w, const void* kn_w,
+                                        float eps, const void* cos, const void* sin, int64_t cs_sb, void* kc,
+                                        void* vc, int64_t c_sb, int64_t c_sh, int B, int NH, int NKV, int S, int D,
+                                        const void* mask, int mask_is_bf16, int64_t m_sb, const int64_t* cache_pos,
+                                        float scaling, float* ws, int64_t ws_floats, int32_t* counters, void* out,
+                                        void* stream) {
+  AttnArgs a{};
+  int rc = fill_common(a, kc, vc, c_sb, c_sh, B, NH, NKV, S, D, mask, mask_is_bf16, m_sb, scaling, ws, ws_floats,
+                       counters, out);
+  if (rc) return rc;
+  FB_CHECK_ARG(qkv && qn_w && kn_w && cos && sin && cache_pos, "attn_decode_fused: null pointer argument");
+  FB_CHECK_ARG(((uintptr_t)qkv & 7) == 0 && qkv_sb % 4 == 0 && ((uintptr_t)cos & 7) == 0 && cs_sb % 4 == 0,
+               "attn_decode_fused: qkv/cos misaligned");
+  a.qkv = (const bf16*)qkv; a.qkv_sb = (long)qkv_sb;
+  a.qn_w = (const bf16*)qn_w; a.kn_w = (const bf16*)kn_w; a.eps = eps;
+  a.cos = (const bf16*)cos; a.sin = (const bf16*)sin; a.cs_sb = (long)cs_sb;
+  a.cache_pos = (const long long*)cache_pos;
+  return dispatch_g<true>(a, B, NH / NKV, (cudaStream_t)stream);
+}

@@ -1,0 +1,238 @@
+// flashb: the two ends of the backbone decode step that the reference leaves to eager torch ops
+// (flash/backbone.py:114-116 and :127-138; official UP/models/cudagraph/backbone_graph.py:254-285).
+//
+//   embed_rope   x[b] = bf16(sum_c table[ids[b, c] + c * vocab])  (BreezeBackboneModelEmbeddings,
+//                UP/models/breeze.py:798-803: gather per codebook, fp32 accumulation in codebook order, one rounding)
+//                + the cos/sin rows of position_ids[b] gathered from host-precomputed bf16 tables (the rotary module's
+//                own fp32 cos/sin cast to bf16, UP/models/breeze.py:159-186).
+//   lm_head_cfg  hidden = Qwen3RMSNorm(x) (bf16); logits = float(hidden) @ W32^T (fp32 lm_head); CFG combine
+//                u + gs * (c - u) with three separately rounded fp32 ops.
+// Both are small HBM streams (the lm_head reads V*H*4 bytes, 16.8 MB at the synthetic config): one warp per output
+// row, 16-byte non-allocating loads with four in flight per lane.
+#include "fb_common.cuh"
+
+namespace fb {
+
+__global__ void __launch_bounds__(256) embed_rope_kernel(const long long* __restrict__ ids, int C, int vocab,
+                                                         const bf16* __restrict__ table, int H,
+                                                         const long long* __restrict__ pos_ids,
+                                                         const bf16* __restrict__ cos_tab,
+                                                         const bf16* __restrict__ sin_tab, int D, int max_pos,
+                                                         bf16* __restrict__ x_out, bf16* __restrict__ cos_out,
+                                                         bf16* __restrict__ sin_out) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x;
+  const long long rows = (long long)C * vocab;
+  for (int j = threadIdx.x * 8; j < H; j += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < C; ++c) {
+      long long r = ids[(size_t)b * C + c] + (long long)c * vocab;
+      r = r < 0 ? 0 : (r >= rows ? rows - 1 : r);
+      float f[8];
+      cvt8(ld_nc_v4(table + (size_t)r * H + j), f);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc[t] += f[t];
+    }
+    uint4 o;
+    o.x = pack2(acc[0], acc[1]);
+    o.y = pack2(acc[2], acc[3]);
+    o.z = pack2(acc[4], acc[5]);
+    o.w = pack2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(x_out + (size_t)b * H + j) = o;
+  }
+  long long p = pos_ids[b];
+  p = p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);
+  for (int j = threadIdx.x * 8; j < D; j += blockDim.x * 8) {
+    *reinterpret_cast<uint4*>(cos_out + (size_t)b * D + j) = *reinterpret_cast<const uint4*>(cos_tab + p * D + j);
+    *reinterpret_cast<uint4*>(sin_out + (size_t)b * D + j) = *reinterpret_cast<const uint4*>(sin_tab + p * D + j);
+  }
+}
+
+constexpr int LM_MAXB = 8;
+constexpr int LM_THREADS = 256;
+
+// grid = #SMs; each CTA normalises x (redundantly) into shared memory as fp32, then one warp per vocab row.
+__global__ void __launch_bounds__(LM_THREADS) lm_head_cfg_kernel(const bf16* __restrict__ x, int B, int H,
+                                                                 const bf16* __restrict__ nw, float eps,
+                                                                 const float* __restrict__ W, int V,
+                                                                 const float* __restrict__ gs,
+                                                                 bf16* __restrict__ hidden_out,
+                                                                 float* __restrict__ logits, float* __restrict__ cfg) {
+  extern __shared__ __align__(16) float hs[];  // [B][H] fp32 values of the bf16 hidden state
+  __shared__ float red[LM_THREADS / 32][LM_MAXB];
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int b = 0; b < B; ++b) {
+    float s = 0.f;
+    for (int j = tid * 8; j < H; j += LM_THREADS * 8) {
+      float f[8];
+      cvt8(*reinterpret_cast<const uint4*>(x + (size_t)b * H + j), f);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) s = fmaf(f[t], f[t], s);
+    }
+    s = warp_sum(s);
+    if (lane == 0) red[warp][b] = s;
+  }
+  __syncthreads();
+  for (int b = 0; b < B; ++b) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < LM_THREADS / 32; ++w) tot += red[w][b];
+    const float r = 1.0f / sqrtf(tot / (float)H + eps);
+    for (int j = tid * 8; j < H; j += LM_THREADS * 8) {
+      float f[8], w8[8];
+      cvt8(*reinterpret_cast<const uint4*>(x + (size_t)b * H + j), f);
+      cvt8(*reinterpret_cast<const uint4*>(nw + j), w8);
+      float y[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) y[t] = rbf(w8[t] * rbf(f[t] * r));
+#pragma unroll
+      for (int t = 0; t < 8; ++t) hs[(size_t)b * H + j + t] = y[t];
+      if (blockIdx.x == 0) {
+        uint4 o;
+        o.x = pack2(y[0], y[1]);
+        o.y = pack2(y[2], y[3]);
+        o.z = pack2(y[4], y[5]);
+        o.w = pack2(y[6], y[7]);
+        *reinterpret_cast<uint4*>(hidden_out + (size_t)b * H + j) = o;
+      }
+    }
+  }
+  __syncthreads();
+  const int half = B >= 2 ? B / 2 : 1;
+  const float g = gs ? gs[0] : 1.0f;
+  const int nw_total = gridDim.x * (LM_THREADS / 32);
+  for (int v = blockIdx.x * (LM_THREADS / 32) + warp; v < V; v += nw_total) {
+    const float* wr = W + (size_t)v * H;
+    float acc[LM_MAXB];
+#pragma unroll
+    for (int b = 0; b < LM_MAXB; ++b) acc[b] = 0.f;
+    for (int j = lane * 4; j < H; j += 128 * 4) {
+      uint4 u[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (j + i * 128 < H) u[i] = ld_nc_v4(wr + j + i * 128);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (j + i * 128 >= H) break;
+        const float w4[4] = {__uint_as_float(u[i].x), __uint_as_float(u[i].y), __uint_as_float(u[i].z),
+                             __uint_as_float(u[i].w)};
+#pragma unroll
+        for (int b = 0; b < LM_MAXB; ++b) {
+          if (b < B) {
+            const float4 h4 = *reinterpret_cast<const float4*>(hs + (size_t)b * H + j + i * 128);
+            acc[b] = fmaf(w4[0], h4.x, acc[b]);
+            acc[b] = fmaf(w4[1], h4.y, acc[b]);
+            acc[b] = fmaf(w4[2], h4.z, acc[b]);
+            acc[b] = fmaf(w4[3], h4.w, acc[b]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < LM_MAXB; ++b)
+      if (b < B) acc[b] = warp_sum(acc[b]);
+    if (lane == 0) {
+#pragma unroll
+      for (int b = 0; b < LM_MAXB; ++b)
+        if (b < B) logits[(size_t)b * V + v] = acc[b];
+      if (B >= 2) {
+#pragma unroll
+        for (int hh = 0; hh < LM_MAXB / 2; ++hh) {
+          if (hh < half) {
+            const float c = acc[hh], u = acc[hh + half];
+            const float d = __fsub_rn(c, u);
+            cfg[(size_t)hh * V + v] = __fadd_rn(u, __fmul_rn(g, d));
+          }
+        }
+      } else {
+        cfg[v] = acc[0];
+      }
+    }
+  }
+}
+
+// Per-step position update of the streaming loop, on device so a captured frame needs no host work: cache_pos += 1,
+// position_ids[b] += 1 and the new slot of every mask row becomes valid (0).  This is what the reference's loop does
+// on the host before each backbone replay (flash/main_loop.py:123-140; UP/models/cudagraph/backbone_graph.py:
+// 239-252, 392-395).
+__global__ void step_advance_kernel(long long* cache_pos, long long* position_ids, int B, void* mask, int mask_bf16,
+                                    long m_sb, int S) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    const long long p = cache_pos[0] + 1;
+    cache_pos[0] = p;
+    for (int b = 0; b < B; ++b) {
+      position_ids[b] += 1;
+      if (p >= 0 && p < S) {
+        if (mask_bf16) reinterpret_cast<bf16*>(mask)[(size_t)b * m_sb + p] = __float2bfloat16_rn(0.f);
+        else reinterpret_cast<float*>(mask)[(size_t)b * m_sb + p] = 0.f;
+      }
+    }
+  }
+}
+
+}  // namespace fb
+
+using namespace fb;
+
+extern "C" int flashb_step_advance(int64_t* cache_pos, int64_t* position_ids, int B, void* mask, int mask_is_bf16,
+                                   int64_t m_sb, int S, void* stream) {
+  FB_CHECK_ARG(cache_pos && position_ids && mask && B >= 1 && S >= 1, "step_advance: bad argument");
+  long long* cp = (long long*)cache_pos;
+  long long* pp = (long long*)position_ids;
+  long msb = (long)m_sb;
+  void* args[] = {(void*)&cp, (void*)&pp, (void*)&B, (void*)&mask, (void*)&mask_is_bf16, (void*)&msb, (void*)&S};
+  return fbh::launch_pdl((const void*)step_advance_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, args, true);
+}
+
+extern "C" int flashb_embed_rope(const int64_t* ids, int B, int C, int vocab, const void* table, int H,
+                                 const int64_t* position_ids, const void* cos_tab, const void* sin_tab, int D,
+                                 int max_pos, void* x_out, void* cos_out, void* sin_out, void* stream) {
+  FB_CHECK_ARG(ids && table && position_ids && cos_tab && sin_tab && x_out && cos_out && sin_out,
+               "embed_rope: null pointer argument");
+  FB_CHECK_ARG(B >= 1 && C >= 1 && vocab >= 1 && H % 8 == 0 && D % 8 == 0 && max_pos >= 1,
+               "embed_rope: bad shape B=%d C=%d vocab=%d H=%d D=%d", B, C, vocab, H, D);
+  const long long* ip = (const long long*)ids;
+  const bf16* tp = (const bf16*)table;
+  const long long* pp = (const long long*)position_ids;
+  const bf16* ct = (const bf16*)cos_tab;
+  const bf16* stt = (const bf16*)sin_tab;
+  bf16* xo = (bf16*)x_out;
+  bf16* co = (bf16*)cos_out;
+  bf16* so = (bf16*)sin_out;
+  void* args[] = {(void*)&ip, (void*)&C, (void*)&vocab, (void*)&tp, (void*)&H, (void*)&pp, (void*)&ct,
+                  (void*)&stt, (void*)&D, (void*)&max_pos, (void*)&xo, (void*)&co, (void*)&so};
+  return fbh::launch_pdl((const void*)embed_rope_kernel, dim3(B), dim3(256), 0, (cudaStream_t)stream, args, true);
+}
+
+extern "C" int flashb_lm_head_cfg(const void* x, int B, int H, const void* norm_w, float eps, const float* W32,
+                                  int V, const float* gs, void* hidden_out, float* logits, float* cfg_out,
+                                  void* stream) {
+  FB_CHECK_ARG(x && norm_w && W32 && hidden_out && logits && cfg_out, "lm_head_cfg: null pointer argument");
+  FB_CHECK_ARG(B >= 1 && B <= LM_MAXB && H % 8 == 0 && V >= 1, "lm_head_cfg: bad shape B=%d H=%d V=%d", B, H, V);
+  FB_CHECK_ARG(B == 1 || gs, "lm_head_cfg: guidance scale pointer required for B >= 2");
+  const size_t smem = (size_t)B * H * 4;
+  FB_CHECK_ARG(smem <= 200 * 1024, "lm_head_cfg: B*H too large");
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && attr_done[dev] < (int)smem) {
+    cudaError_t e = cudaFuncSetAttribute(lm_head_cfg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      fbh::set_msg("lm_head_cfg: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return FB_ERR_CUDA;
+    }
+    attr_done[dev] = (int)smem;
+  }
+  const bf16* xp = (const bf16*)x;
+  const bf16* np = (const bf16*)norm_w;
+  bf16* ho = (bf16*)hidden_out;
+  void* args[] = {(void*)&xp, (void*)&B, (void*)&H, (void*)&np, (void*)&eps, (void*)&W32, (void*)&V,
+                  (void*)&gs, (void*)&ho, (void*)&logits, (void*)&cfg_out};
+  return fbh::launch_pdl((const void*)lm_head_cfg_kernel, dim3(fbh::num_sms()), dim3(LM_THREADS), smem,
+                         (cudaStream_t)stream, args, true);
+}

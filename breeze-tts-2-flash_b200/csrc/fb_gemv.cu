@@ -1,0 +1,635 @@
+// flashb: skinny bf16 GEMVs for the backbone decode step (M = 1..8 activation rows, nn.Linear weights [N, K]).
+//
+// Semantics (the eager rounding points the reference restates in flash/csrc/bb_fused.cu:1-7):
+//   y[m, n] = sum_k xin[m, k] * W[n, k]           fp32 accumulation
+//   prologue NORM: xin = bf16(w * bf16(x * rsqrt(mean(x^2) + eps)))   (Qwen3RMSNorm, per CTA, redundant)
+//   EPI 0: bf16(acc)   EPI 1: bf16(res + bf16(acc))   EPI 2: bf16(bf16(silu(bf16(acc_gate))) * bf16(acc_up))
+//
+// B200 design: the kernel is an HBM stream of the weight matrix.  Each CTA owns a contiguous range of output rows
+// (grid = #SMs, so every SM streams ~N/148 rows) and a producer warp moves the rows into a shared-memory ring with
+// 1-D bulk copies (cp.async.bulk, the TMA engine; no tensor map, no multicast) completing on mbarriers, while 8
+// consumer warps do the dot products from shared memory (one weight row per warp per stage, x staged once).  The
+// weights never depend on the previous kernel, so the producer fills the whole ring BEFORE griddepcontrol.wait: with
+// programmatic dependent launch the weight stream of GEMV i+1 starts while kernel i drains.  The ring is sized so
+// two CTAs fit on an SM (<= ~112 KB each), letting the next kernel's CTAs co-reside and prefetch.
+#include "fb_stream.cuh"
+
+namespace fb {
+
+constexpr int GV_CWARPS = 8;
+constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;
+constexpr int GV_STAGE_BYTES = 32768;
+constexpr int GV_MAX_STAGES = 12;
+constexpr int GV_SMEM_BUDGET = 112 * 1024;
+
+struct GemvArgs {
+  const bf16* x;
+  long ldx;
+  const bf16* nw;
+  float eps;
+  const bf16* W0;
+  const bf16* W1;
+  const bf16* W2;
+  int N0, N1;  // segment boundaries (EPI 0/1); EPI 2: W0 = gate, W1 = up
+  int K, N;
+  bf16* y;
+  long ldy;
+  const bf16* res;
+  long ldr;
+  int M;        // activation rows (tensor-core path)
+  int RS;       // units (output rows) per stage
+  int nstages;  // ring depth
+  int xs_bytes; // shared bytes reserved for x
+  unsigned* err;
+};
+
+// Row n of matrix `mat` (EPI 2: 0 = gate, 1 = up; else the q|k|v-style segment holding row n).
+template <int EPI>
+__device__ __forceinline__ const bf16* gv_row(const GemvArgs& a, int n, int mat) {
+  if (EPI == 2) return (mat == 0 ? a.W0 : a.W1) + (size_t)n * a.K;
+  if (n < a.N0) return a.W0 + (size_t)n * a.K;
+  if (n < a.N0 + a.N1) return a.W1 + (size_t)(n - a.N0) * a.K;
+  return a.W2 + (size_t)(n - a.N0 - a.N1) * a.K;
+}
+// First row index after n at which the segment (and so the contiguous source range) changes.
+template <int EPI>
+__device__ __forceinline__ int gv_seg_end(const GemvArgs& a, int n) {
+  if (EPI == 2) return a.N;
+  if (n < a.N0) return a.N0;
+  if (n < a.N0 + a.N1) return a.N0 + a.N1;
+  return a.N;
+}
+
+// Fallback for K % 8 == 0 but K % 16 != 0 (no whole mma k-steps): scalar FMA from shared memory.
+// A stage holds RS consecutive output rows (x NMAT matrices) in full (all K columns), copied as contiguous runs:
+// one bulk copy per matrix and segment (<= 3 per stage), each up to 32 KB.  Warps take rows round-robin; when a
+// stage has fewer rows than warps, 2 or 4 warps split each row's K range and combine their partial sums through
+// shared memory in a fixed order (deterministic results).
+template <int M, int EPI, bool NORM>
+__global__ void __launch_bounds__(GV_THREADS) gemv_fma_kernel(const GemvArgs a) {
+  constexpr int NMAT = EPI == 2 ? 2 : 1;
+  extern __shared__ __align__(128) unsigned char smem[];
+  bf16* xs = reinterpret_cast<bf16*>(smem);
+  unsigned char* ring = smem + a.xs_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)a.nstages * GV_STAGE_BYTES);
+  uint64_t* empty = full + GV_MAX_STAGES;
+  __shared__ float red[GV_CWARPS][M];
+  __shared__ float part[GV_CWARPS][NMAT][M];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, bid = blockIdx.x;
+  const int r0 = (int)((long long)a.N * bid / G), r1 = (int)((long long)a.N * (bid + 1) / G);
+  const int RS = a.RS;
+  const int T = (r1 - r0 + RS - 1) / RS;
+  const int NST = a.nstages;
+  const int K = a.K;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], GV_CWARPS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == GV_CWARPS) {
+    // ------------------------------------------------------------ producer: weights only, may run before pdl_wait
+    int issued = 0;
+    for (int t = 0; t < T; ++t) {
+      const int s = t % NST;
+      if (t >= NST) {
+        if (!mbar_wait_warp(&empty[s], ((t / NST) - 1) & 1, a.err)) break;
+      }
+      const int n0 = r0 + t * RS;
+      const int nr = min(RS, r1 - n0);
+      bf16* st = reinterpret_cast<bf16*>(ring + (size_t)s * GV_STAGE_BYTES);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], (unsigned)(nr * NMAT * K * 2));
+#pragma unroll
+        for (int mat = 0; mat < NMAT; ++mat) {
+          int n = n0;
+          while (n < n0 + nr) {
+            const int e = min(n0 + nr, gv_seg_end<EPI>(a, n));
+            bulk_g2s(st + ((size_t)mat * RS + (n - n0)) * K, gv_row<EPI>(a, n, mat), (unsigned)((e - n) * K * 2),
+                     &full[s]);
+            n = e;
+          }
+        }
+      }
+      __syncwarp();
+      ++issued;
+    }
+    // never leave with copies in flight into this CTA's shared memory
+    for (int t = max(0, issued - NST); t < issued; ++t) {
+      if (!mbar_wait_warp(&full[t % NST], (t / NST) & 1, a.err)) break;
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  pdl_wait();
+  pdl_trigger();
+  const int ctid = threadIdx.x;  // 0..255
+  const int kv = K >> 3;
+  {
+    float ss[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) ss[m] = 0.f;
+    for (int i = ctid; i < M * kv; i += GV_CWARPS * 32) {
+      const int m = i / kv, j = i - m * kv;
+      const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + (size_t)j * 8);
+      reinterpret_cast<uint4*>(xs)[i] = v;
+      if (NORM) {
+        float f[8];
+        cvt8(v, f);
+        float s = 0.f;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) s = fmaf(f[t], f[t], s);
+#pragma unroll
+        for (int mm = 0; mm < M; ++mm)
+          if (mm == m) ss[mm] += s;
+      }
+    }
+    if (NORM) {
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const float s = warp_sum(ss[m]);
+        if (lane == 0) red[warp][m] = s;
+      }
+      named_sync(1, GV_CWARPS * 32);
+      float rs[M];
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < GV_CWARPS; ++w) s += red[w][m];
+        rs[m] = 1.0f / sqrtf(s / (float)K + a.eps);
+      }
+      for (int i = ctid; i < M * kv; i += GV_CWARPS * 32) {
+        const int m = i / kv, j = i - m * kv;
+        float f[8], w[8];
+        cvt8(reinterpret_cast<const uint4*>(xs)[i], f);
+        cvt8(*reinterpret_cast<const uint4*>(a.nw + (size_t)j * 8), w);
+        float r = 0.f;
+#pragma unroll
+        for (int mm = 0; mm < M; ++mm)
+          if (mm == m) r = rs[mm];
+        uint4 o;
+        o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
+        o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
+        o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
+        o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
+        reinterpret_cast<uint4*>(xs)[i] = o;
+      }
+    }
+    named_sync(1, GV_CWARPS * 32);
+  }
+
+  for (int t = 0; t < T; ++t) {
+    const int s = t % NST;
+    if (!mbar_wait_warp(&full[s], (t / NST) & 1, a.err)) return;
+    const int n0 = r0 + t * RS;
+    const int nr = min(RS, r1 - n0);
+    // warps per row: split K when the stage has fewer rows than warps
+    const int wpr = nr >= GV_CWARPS ? 1 : (nr >= 4 ? 2 : (nr >= 2 ? 4 : 8));
+    const int kslice = ((K + 8 * wpr - 1) / (8 * wpr)) * 8;
+    const bf16* st = reinterpret_cast<const bf16*>(ring + (size_t)s * GV_STAGE_BYTES);
+    const int rows_per_pass = GV_CWARPS / wpr;
+    for (int rb = 0; rb < nr; rb += rows_per_pass) {
+      const int r = rb + warp / wpr;
+      const int ks = (warp % wpr) * kslice;
+      const int ke = min(ks + kslice, K);
+      float acc[NMAT][M];
+#pragma unroll
+      for (int q = 0; q < NMAT; ++q)
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[q][m] = 0.f;
+      if (r < nr) {
+        const bf16* wr[NMAT];
+#pragma unroll
+        for (int q = 0; q < NMAT; ++q) wr[q] = st + ((size_t)q * RS + r) * K;
+#pragma unroll 2
+        for (int c = ks + lane * 8; c < ke; c += 256) {
+          float wf[NMAT][8];
+#pragma unroll
+          for (int q = 0; q < NMAT; ++q) cvt8(*reinterpret_cast<const uint4*>(wr[q] + c), wf[q]);
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            float xf[8];
+            cvt8(*reinterpret_cast<const uint4*>(xs + (size_t)m * K + c), xf);
+#pragma unroll
+            for (int q = 0; q < NMAT; ++q)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc[q][m] = fmaf(wf[q][j], xf[j], acc[q][m]);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < NMAT; ++q)
+#pragma unroll
+          for (int m = 0; m < M; ++m) acc[q][m] = warp_sum(acc[q][m]);
+      }
+      if (wpr > 1) {
+        if (lane == 0) {
+#pragma unroll
+          for (int q = 0; q < NMAT; ++q)
+#pragma unroll
+            for (int m = 0; m < M; ++m) part[warp][q][m] = acc[q][m];
+        }
+        named_sync(1, GV_CWARPS * 32);
+        if (warp % wpr == 0 && r < nr) {
+#pragma unroll
+          for (int q = 0; q < NMAT; ++q)
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+              float v = part[warp][q][m];
+              for (int i = 1; i < wpr; ++i) v += part[warp + i][q][m];
+              acc[q][m] = v;
+            }
+        }
+        named_sync(1, GV_CWARPS * 32);
+      }
+      if (warp % wpr == 0 && r < nr) {
+        const int n = n0 + r;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          if (lane == m) {
+            float v;
+            if (EPI == 0) {
+              v = acc[0][m];
+            } else if (EPI == 1) {
+              v = b2f(a.res[(size_t)m * a.ldr + n]) + rbf(acc[0][m]);
+            } else {
+              const float g = rbf(acc[0][m]);
+              const float u = rbf(acc[NMAT - 1][m]);
+              v = rbf(g / (1.0f + expf(-g))) * u;
+            }
+            a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(v);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+
+// Tensor-core path (K % 16 == 0): a producer warp streams stages of 16 weight rows x ST_KC columns with 1-D bulk
+// copies into a ring of mbarrier-tracked slots; 8 consumer warps run mma.sync m16n8k16 on them (fb_stream.cuh).
+// NMAT = 2 (gate/up): rows 0..7 of a stage are gate rows of 8 output units, rows 8..15 the matching up rows, so a
+// unit's gate and up sums land in the same reduction slots.
+constexpr int GM_MAX_STAGES = 6;
+constexpr int GM_THREADS = (ST_CWARPS + 1) * 32;
+
+template <int EPI, bool NORM>
+__global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) {
+  constexpr int NMAT = EPI == 2 ? 2 : 1;
+  constexpr int UG = ST_ROWS / NMAT;  // output units per row group
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int M = a.M, K = a.K, NST = a.nstages;
+  const int x_pitch = K * 2 + 16;
+  unsigned char* xs = smem;
+  unsigned char* zero16 = smem + a.xs_bytes;
+  unsigned char* ring = zero16 + 128;
+  float* red = reinterpret_cast<float*>(ring + (size_t)NST * ST_BYTES);
+  float* sums = red + ST_CWARPS * 128;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sums + 128);
+  uint64_t* empty = full + GM_MAX_STAGES;
+  __shared__ float nred[ST_CWARPS][8];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x, bid = blockIdx.x;
+  const int u0 = (int)((long long)a.N * bid / G), u1 = (int)((long long)a.N * (bid + 1) / G);
+  const int ngroups = (u1 - u0 + UG - 1) / UG;
+  const int nkc = (K + ST_KC - 1) / ST_KC;
+  const int T = ngroups * nkc;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ST_CWARPS);
+    }
+    fence_mbar_init();
+  }
+  if (tid < 32) reinterpret_cast<uint32_t*>(zero16)[tid] = 0u;
+  __syncthreads();
+
+  if (warp == ST_CWARPS) {
+    // ------------------------------------------------------------ producer: weights only, runs before pdl_wait
+    int issued = 0;
+    for (int t = 0; t < T; ++t) {
+      const int s = t % NST;
+      if (t >= NST && !mbar_wait_warp(&empty[s], ((t / NST) - 1) & 1, a.err)) break;
+      const int g = t / nkc, kc = t % nkc;
+      const int n0 = u0 + g * UG;
+      const int nu = min(UG, u1 - n0);
+      const int k0 = kc * ST_KC;
+      const int kw = min(ST_KC, K - k0);
+      unsigned char* st = ring + (size_t)s * ST_BYTES;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], (unsigned)(nu * NMAT * kw * 2));
+      __syncwarp();
+      if (lane < ST_ROWS) {
+        const int i = lane % UG, mat = lane / UG;
+        if (i < nu) bulk_g2s(st + lane * ST_PITCH, gv_row<EPI>(a, n0 + i, mat) + k0, (unsigned)(kw * 2), &full[s]);
+      }
+      ++issued;
+    }
+    for (int t = max(0, issued - NST); t < issued; ++t)
+      if (!mbar_wait_warp(&full[t % NST], (t / NST) & 1, a.err)) break;
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  pdl_wait();
+  pdl_trigger();
+  const int ctid = tid;
+  const int kv = K >> 3;
+  {
+    float ss[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) ss[m] = 0.f;
+    for (int i = ctid; i < M * kv; i += ST_CWARPS * 32) {
+      const int m = i / kv, j = i - m * kv;
+      const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + (size_t)j * 8);
+      *reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16) = v;
+      if (NORM) {
+        float f[8];
+        cvt8(v, f);
+        float q = 0.f;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) q = fmaf(f[t], f[t], q);
+#pragma unroll
+        for (int mm = 0; mm < 8; ++mm)
+          if (mm == m) ss[mm] += q;
+      }
+    }
+    if (NORM) {
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const float q = warp_sum(ss[m]);
+        if (lane == 0) nred[warp][m] = q;
+      }
+      named_sync(1, ST_CWARPS * 32);
+      float rs[8];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        float q = 0.f;
+#pragma unroll
+        for (int w = 0; w < ST_CWARPS; ++w) q += nred[w][m];
+        rs[m] = 1.0f / sqrtf(q / (float)K + a.eps);
+      }
+      for (int i = ctid; i < M * kv; i += ST_CWARPS * 32) {
+        const int m = i / kv, j = i - m * kv;
+        uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
+        float f[8], w[8];
+        cvt8(*px, f);
+        cvt8(*reinterpret_cast<const uint4*>(a.nw + (size_t)j * 8), w);
+        float r = 0.f;
+#pragma unroll
+        for (int mm = 0; mm < 8; ++mm)
+          if (mm == m) r = rs[mm];
+        uint4 o;
+        o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
+        o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
+        o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
+        o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
+        *px = o;
+      }
+    }
+    named_sync(1, ST_CWARPS * 32);
+  }
+
+  int t = 0;
+  for (int g = 0; g < ngroups; ++g) {
+    const int n0 = u0 + g * UG;
+    const int nu = min(UG, u1 - n0);
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kc = 0; kc < nkc; ++kc, ++t) {
+      const int s = t % NST;
+      if (!mbar_wait_warp(&full[s], (t / NST) & 1, a.err)) return;
+      const int k0 = kc * ST_KC;
+      stage_mma(ring + (size_t)s * ST_BYTES, min(ST_KC, K - k0), xs, x_pitch, M, k0, zero16, c);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    reduce_warps(c, red, sums, 1);
+    if (ctid < nu * M) {
+      const int i = ctid / M, m = ctid - i * M;
+      const int n = n0 + i;
+      float v;
+      if (EPI == 0) {
+        v = sums[i * 8 + m];
+      } else if (EPI == 1) {
+        v = b2f(a.res[(size_t)m * a.ldr + n]) + rbf(sums[i * 8 + m]);
+      } else {
+        const float gg = rbf(sums[i * 8 + m]);
+        const float uu = rbf(sums[(i + 8) * 8 + m]);
+        v = rbf(gg / (1.0f + expf(-gg))) * uu;
+      }
+      a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// Standalone Qwen3RMSNorm over rows (one CTA per row).
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16* __restrict__ x, long ldx,
+                                                      const bf16* __restrict__ w, float eps, bf16* __restrict__ y,
+                                                      long ldy, int K) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x;
+  __shared__ float red[8];
+  const bf16* xr = x + (size_t)m * ldx;
+  float s = 0.f;
+  for (int j = threadIdx.x * 8; j < K; j += blockDim.x * 8) {
+    float f[8];
+    cvt8(*reinterpret_cast<const uint4*>(xr + j), f);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) s = fmaf(f[t], f[t], s);
+  }
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+  const float r = 1.0f / sqrtf(tot / (float)K + eps);
+  for (int j = threadIdx.x * 8; j < K; j += blockDim.x * 8) {
+    float f[8], ww[8];
+    cvt8(*reinterpret_cast<const uint4*>(xr + j), f);
+    cvt8(*reinterpret_cast<const uint4*>(w + j), ww);
+    uint4 o;
+    o.x = pack2(ww[0] * rbf(f[0] * r), ww[1] * rbf(f[1] * r));
+    o.y = pack2(ww[2] * rbf(f[2] * r), ww[3] * rbf(f[3] * r));
+    o.z = pack2(ww[4] * rbf(f[4] * r), ww[5] * rbf(f[5] * r));
+    o.w = pack2(ww[6] * rbf(f[6] * r), ww[7] * rbf(f[7] * r));
+    *reinterpret_cast<uint4*>(y + (size_t)m * ldy + j) = o;
+  }
+}
+
+}  // namespace fb
+
+namespace {
+using namespace fb;
+
+bool al16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+template <int M, int EPI, bool NORM>
+int launch_gemv_t(GemvArgs& a, cudaStream_t st) {
+  auto kern = gemv_fma_kernel<M, EPI, NORM>;
+  const size_t smem = (size_t)a.xs_bytes + (size_t)a.nstages * GV_STAGE_BYTES + 2 * GV_MAX_STAGES * 8 + 128;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && attr_done[dev] < (int)smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      fbh::set_msg("gemv: cudaFuncSetAttribute(%zu bytes): %s", smem, cudaGetErrorString(e));
+      return FB_ERR_CUDA;
+    }
+    attr_done[dev] = (int)smem;
+  }
+  const int grid = a.N < fbh::num_sms() ? a.N : fbh::num_sms();
+  void* args[] = {(void*)&a};
+  return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(GV_THREADS), smem, st, args, true);
+}
+
+template <int EPI, bool NORM>
+int launch_mma_t(GemvArgs& a, cudaStream_t st) {
+  auto kern = gemv_mma_kernel<EPI, NORM>;
+  a.xs_bytes = ((a.M * (a.K * 2 + 16)) + 127) / 128 * 128;
+  const size_t fixed = (size_t)a.xs_bytes + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * GM_MAX_STAGES * 8;
+#ifndef FB_GM_BUDGET
+#define FB_GM_BUDGET 220000
+#endif
+  int nst = (int)((FB_GM_BUDGET - fixed) / ST_BYTES);
+  if (nst < 3) nst = (int)((210 * 1024 - fixed) / ST_BYTES);
+  if (nst > GM_MAX_STAGES) nst = GM_MAX_STAGES;
+  if (nst < 2) {
+    fbh::set_msg("gemv: M*K = %d activations do not fit the shared-memory budget", a.M * a.K);
+    return FB_ERR_UNSUPPORTED;
+  }
+  a.nstages = nst;
+  const size_t smem = fixed + (size_t)nst * ST_BYTES;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && attr_done[dev] < (int)smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      fbh::set_msg("gemv: cudaFuncSetAttribute(%zu bytes): %s", smem, cudaGetErrorString(e));
+      return FB_ERR_CUDA;
+    }
+    attr_done[dev] = (int)smem;
+  }
+  const int grid = a.N < fbh::num_sms() ? a.N : fbh::num_sms();
+  void* args[] = {(void*)&a};
+  return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(GM_THREADS), smem, st, args, true);
+}
+
+template <int EPI, bool NORM>
+int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
+  a.M = M;
+  if (a.K % 16 == 0) return launch_mma_t<EPI, NORM>(a, st);
+  switch (M) {
+    case 1: return launch_gemv_t<1, EPI, NORM>(a, st);
+    case 2: return launch_gemv_t<2, EPI, NORM>(a, st);
+    case 3: return launch_gemv_t<3, EPI, NORM>(a, st);
+    case 4: return launch_gemv_t<4, EPI, NORM>(a, st);
+    case 8: return launch_gemv_t<8, EPI, NORM>(a, st);
+    default: fbh::set_msg("gemv: M=%d rows not built for K %% 16 != 0 (1, 2, 3, 4, 8)", M); return FB_ERR_UNSUPPORTED;
+  }
+}
+
+int common_checks(const void* x, int64_t ldx, int M, int K, const void* y, int64_t ldy) {
+  FB_CHECK_ARG(x && y, "gemv: null x or y");
+  FB_CHECK_ARG(M >= 1 && M <= 8, "gemv: M=%d out of range 1..8", M);
+  FB_CHECK_ARG(K > 0 && K % 8 == 0, "gemv: K=%d must be a positive multiple of 8", K);
+  FB_CHECK_ARG(ldx % 8 == 0 && ldy >= 1 && al16(x), "gemv: x row stride %lld must be a multiple of 8 and x 16B aligned",
+               (long long)ldx);
+  return FB_OK;
+}
+
+int setup_ring(GemvArgs& a, int M, int nmat) {
+  a.err = fbh::device_err_ptr();
+  if (a.K % 16 == 0) return FB_OK;  // tensor-core path: its ring is sized at launch
+  const int row_bytes = nmat * a.K * 2;
+  if (row_bytes > GV_STAGE_BYTES) {
+    fbh::set_msg("gemv: K=%d too large for one stage (max %d)", a.K, GV_STAGE_BYTES / (2 * nmat));
+    return FB_ERR_UNSUPPORTED;
+  }
+  a.RS = GV_STAGE_BYTES / row_bytes;
+  if (a.RS > 16) a.RS = 16;
+  a.xs_bytes = ((M * a.K * 2) + 127) / 128 * 128;
+  int nst = (GV_SMEM_BUDGET - a.xs_bytes) / GV_STAGE_BYTES;
+  if (nst < 2) nst = (200 * 1024 - a.xs_bytes) / GV_STAGE_BYTES;
+  if (nst > GV_MAX_STAGES) nst = GV_MAX_STAGES;
+  if (nst < 2) {
+    fbh::set_msg("gemv: M*K = %d activations do not fit the shared-memory budget", M * a.K);
+    return FB_ERR_UNSUPPORTED;
+  }
+  a.nstages = nst;
+  a.err = fbh::device_err_ptr();
+  return FB_OK;
+}
+
+}  // namespace
+
+extern "C" int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const void* nw, float eps, const void* W0,
+                               int N0, const void* W1, int N1, const void* W2, int N2, void* y, int64_t ldy,
+                               void* stream) {
+  int rc = common_checks(x, ldx, M, K, y, ldy);
+  if (rc) return rc;
+  FB_CHECK_ARG(W0 && N0 > 0 && al16(W0), "gemv_seg: W0 missing or misaligned");
+  FB_CHECK_ARG(N1 >= 0 && N2 >= 0 && (N1 == 0 || (W1 && al16(W1))) && (N2 == 0 || (W2 && al16(W2))),
+               "gemv_seg: bad W1/W2 segment");
+  FB_CHECK_ARG(!nw || al16(nw), "gemv_seg: norm weight misaligned");
+  GemvArgs a{};
+  a.x = (const bf16*)x; a.ldx = (long)ldx; a.nw = (const bf16*)nw; a.eps = eps;
+  a.W0 = (const bf16*)W0; a.W1 = N1 ? (const bf16*)W1 : a.W0; a.W2 = N2 ? (const bf16*)W2 : a.W0;
+  a.N0 = N0; a.N1 = N1; a.K = K; a.N = N0 + N1 + N2;
+  a.y = (bf16*)y; a.ldy = (long)ldy;
+  if ((rc = setup_ring(a, M, 1))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  return nw ? dispatch_m<0, true>(a, M, st) : dispatch_m<0, false>(a, M, st);
+}
+
+extern "C" int flashb_gemv_resid(const void* x, int64_t ldx, int M, int K, const void* W, int N, const void* res,
+                                 int64_t ldr, void* y, int64_t ldy, void* stream) {
+  int rc = common_checks(x, ldx, M, K, y, ldy);
+  if (rc) return rc;
+  FB_CHECK_ARG(W && N > 0 && al16(W) && res, "gemv_resid: bad W or res");
+  GemvArgs a{};
+  a.x = (const bf16*)x; a.ldx = (long)ldx;
+  a.W0 = a.W1 = a.W2 = (const bf16*)W; a.N0 = N; a.N1 = 0; a.K = K; a.N = N;
+  a.y = (bf16*)y; a.ldy = (long)ldy; a.res = (const bf16*)res; a.ldr = (long)ldr;
+  if ((rc = setup_ring(a, M, 1))) return rc;
+  return dispatch_m<1, false>(a, M, (cudaStream_t)stream);
+}
+
+extern "C" int flashb_gemv_gateup(const void* x, int64_t ldx, int M, int K, const void* nw, float eps, const void* Wg,
+                                  const void* Wu, int N, void* y, int64_t ldy, void* stream) {
+  int rc = common_checks(x, ldx, M, K, y, ldy);
+  if (rc) return rc;
+  FB_CHECK_ARG(Wg && Wu && N > 0 && al16(Wg) && al16(Wu), "gemv_gateup: bad Wg/Wu");
+  FB_CHECK_ARG(nw && al16(nw), "gemv_gateup: norm weight required and 16B aligned");
+  GemvArgs a{};
+  a.x = (const bf16*)x; a.ldx = (long)ldx; a.nw = (const bf16*)nw; a.eps = eps;
+  a.W0 = (const bf16*)Wg; a.W1 = (const bf16*)Wu; a.W2 = a.W0; a.N0 = N; a.N1 = 0; a.K = K; a.N = N;
+  a.y = (bf16*)y; a.ldy = (long)ldy;
+  if ((rc = setup_ring(a, M, 2))) return rc;
+  return dispatch_m<2, true>(a, M, (cudaStream_t)stream);
+}
+
+extern "C" int flashb_rmsnorm(const void* x, int64_t ldx, int M, int K, const void* w, float eps, void* y,
+                              int64_t ldy, void* stream) {
+  int rc = common_checks(x, ldx, M, K, y, ldy);
+  if (rc) return rc;
+  FB_CHECK_ARG(w && al16(w) && ldy % 8 == 0 && al16(y), "rmsnorm: bad weight or output stride");
+  const bf16* xp = (const bf16*)x;
+  const bf16* wp = (const bf16*)w;
+  bf16* yp = (bf16*)y;
+  long lx = (long)ldx, ly = (long)ldy;
+  void* args[] = {(void*)&xp, (void*)&lx, (void*)&wp, (void*)&eps, (void*)&yp, (void*)&ly, (void*)&K};
+  return fbh::launch_pdl((const void*)rmsnorm_kernel, dim3(M), dim3(256), 0, (cudaStream_t)stream, args, true);
+}

@@ -1,0 +1,156 @@
+// flashb: the weight-streaming GEMV core shared by the standalone GEMV kernels and the persistent step kernels.
+//
+// A skinny GEMV y[m, n] = sum_k x[m, k] W[n, k] (M <= 8 activation rows) is an HBM stream of W.  The core splits
+// the work into stages of 16 weight rows x 2048 columns (64 KB):
+//   * a producer warp moves each row slice into a shared-memory ring with one 1-D bulk copy (cp.async.bulk, the TMA
+//     engine; no tensor map, no multicast) completing on the stage's mbarrier.  Rows sit at a 4112-byte pitch (one
+//     16-byte pad per row) so that ldmatrix reads of 8 consecutive rows fall in distinct banks.  Measured on B200:
+//     the per-SM rate is set by the consumers' per-stage overhead, so stages are large (64 KB stages stream a
+//     400 MB matrix at 6.4 TB/s; 32 KB stages at 4.9 TB/s; a 16-byte cp.async staging variant at 2.3 TB/s);
+//   * 8 consumer warps split the stage's 64 k-steps; each k-step is one tensor-core mma.sync m16n8k16
+//     (bf16 x bf16 -> fp32): A = 16 weight rows x 16 columns via ldmatrix.x4, B = the 8-row activation tile (rows
+//     >= M read a zero block) via ldmatrix.x2.  One mma replaces 256 scalar FMAs plus their bf16 unpacking, so the
+//     consumer issue rate stays far below the HBM rate even with one CTA per SM;
+//   * at the end of a row group the 8 warps' fp32 accumulators are summed in shared memory in a fixed order
+//     (deterministic), and a task-specific epilogue turns the 16 x M sums into outputs.
+// Both sides walk the same static stage sequence, so the producer runs ahead of the consumers by the ring depth,
+// across task boundaries and grid barriers (weights never depend on activations).
+#pragma once
+#include "fb_common.cuh"
+
+namespace fb {
+
+constexpr int ST_ROWS = 16;                       // weight rows per stage (one mma M tile)
+#ifndef FB_ST_KC
+#define FB_ST_KC 2048
+#endif
+constexpr int ST_KC = FB_ST_KC;                   // columns per stage
+constexpr int ST_PITCH = ST_KC * 2 + 16;          // bytes per staged row
+constexpr int ST_BYTES = ST_ROWS * ST_PITCH;      // 65792 bytes per stage
+constexpr int ST_CWARPS = 8;                      // consumer warps
+constexpr int ST_KSTEPS_PER_WARP = ST_KC / 16 / ST_CWARPS;  // 16
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Consumer side of one stage: this warp's share of the k-steps of a [16 x kw] weight tile against the activation
+// rows xs (M rows at byte pitch x_pitch, columns k0.. of the full K), accumulated into the C fragment c:
+// c[0], c[1] = rows lane/4, activation rows (lane%4)*2 + {0,1}; c[2], c[3] = rows lane/4 + 8, same columns.
+__device__ __forceinline__ void stage_mma(const unsigned char* stage, int kw, const unsigned char* xs, int x_pitch,
+                                          int M, int k0, const unsigned char* zero16, float (&c)[4]) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nks = kw >> 4;
+  const int ks0 = warp * ST_KSTEPS_PER_WARP;
+  const int ks1 = min(nks, ks0 + ST_KSTEPS_PER_WARP);
+  // A: lane i supplies row (i % 8) + 8 * ((i / 8) % 2), column offset 8 * (i / 16)
+  const int arow = (lane & 7) + ((lane >> 3) & 1) * 8;
+  const uint32_t abase = smem_u32(stage) + arow * ST_PITCH + (lane >> 4) * 16;
+  // B: lanes 0-7 supply activation row n = lane at column offset 0, lanes 8-15 row lane-8 at offset 8
+  const int bn = lane & 7;
+  const bool breal = bn < M && lane < 16;
+  const uint32_t bbase = breal ? smem_u32(xs) + bn * x_pitch + (size_t)k0 * 2 + ((lane >> 3) & 1) * 16 : smem_u32(zero16);
+  const uint32_t bstep = breal ? 32u : 0u;
+#ifndef FB_MMA_NACC
+#define FB_MMA_NACC 4
+#endif
+#if FB_MMA_NACC > 1
+  // independent accumulator chains (one mma latency per NACC k-steps), summed at the end in a fixed order
+  float cc[FB_MMA_NACC][4];
+#pragma unroll
+  for (int i = 0; i < FB_MMA_NACC; ++i) cc[i][0] = cc[i][1] = cc[i][2] = cc[i][3] = 0.f;
+#pragma unroll
+  for (int i = 0; i < ST_KSTEPS_PER_WARP; ++i) {
+    const int ks = ks0 + i;
+    if (ks < ks1) {
+      uint32_t a0, a1, a2, a3, b0, b1;
+      ldsm_x4(abase + ks * 32, a0, a1, a2, a3);
+      ldsm_x2(bbase + ks * bstep, b0, b1);
+      mma_bf16_16816(cc[i % FB_MMA_NACC], a0, a1, a2, a3, b0, b1);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < FB_MMA_NACC; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[j] += cc[i][j];
+#else
+#pragma unroll 4
+  for (int ks = ks0; ks < ks1; ++ks) {
+    uint32_t a0, a1, a2, a3, b0, b1;
+    ldsm_x4(abase + ks * 32, a0, a1, a2, a3);
+    ldsm_x2(bbase + ks * bstep, b0, b1);
+    mma_bf16_16816(c, a0, a1, a2, a3, b0, b1);
+  }
+#endif
+}
+
+// Sum the 8 warps' C fragments (fixed order) into sums[16][8] (shared).  Called by all 256 consumer threads.
+__device__ __forceinline__ void reduce_warps(const float (&c)[4], float* red /* [8][16][8] */, float* sums /* [16][8] */,
+                                             int bar_id) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, m = (lane & 3) * 2;
+  float* w = red + warp * 128;
+  w[r * 8 + m] = c[0];
+  w[r * 8 + m + 1] = c[1];
+  w[(r + 8) * 8 + m] = c[2];
+  w[(r + 8) * 8 + m + 1] = c[3];
+  named_sync(bar_id, ST_CWARPS * 32);
+  if (threadIdx.x < 128) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < ST_CWARPS; ++i) s += red[i * 128 + threadIdx.x];
+    sums[threadIdx.x] = s;
+  }
+  named_sync(bar_id, ST_CWARPS * 32);
+}
+
+// cp.async 16-byte global -> shared copy (bypasses L1), group commit / wait.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_dyn(int n) {  // n in [0, 7]
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    default: cp_async_wait<7>(); break;
+  }
+}
+
+// Stage load by all `nthreads` consumer threads: rows[i] (i < nrows) -> stage row i, columns [0, kw) (kw % 8 == 0).
+// 16-byte chunks are spread across threads so consecutive threads read consecutive chunks of a row.
+template <typename RowFn>
+__device__ __forceinline__ void stage_load(unsigned char* stage, int nrows, int kw, int tid, int nthreads,
+                                           RowFn row) {
+  const int cpr = kw >> 3;  // 16-byte chunks per row
+  const int total = nrows * cpr;
+  for (int c = tid; c < total; c += nthreads) {
+    const int r = c / cpr, j = c - r * cpr;
+    const bf16* src = row(r);
+    if (src) cp_async16(stage + r * ST_PITCH + j * 16, src + j * 8);
+  }
+}
+
+}  // namespace fb

@@ -1,0 +1,109 @@
+/* flashb: C ABI of the B200 (sm_100a) kernels for the Breeze-TTS-2 streaming-decode hot path.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes, launches on the given CUDA stream
+ * (a cudaStream_t passed as void*; NULL = legacy default stream) and returns FB_OK or an FB_ERR_* code; the message
+ * of the last failure on the calling thread is flashb_last_error().  No entry point allocates device memory or
+ * synchronises the stream (flashb_device_error excepted), so all of them can be captured in a CUDA graph.  bf16
+ * arguments are IEEE bfloat16 bit patterns (uint16); fp32 arguments are float.
+ *
+ * The reference binds the same operations as pybind11 functions of JIT-built torch extensions; each declaration
+ * cites the reference function it replaces (paths relative to the reference project root).
+ */
+#ifndef FLASHB_H
+#define FLASHB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  FB_OK = 0,
+  FB_ERR_ARG = 1,         /* invalid pointer, shape, stride or alignment */
+  FB_ERR_CUDA = 2,        /* a CUDA runtime call failed (launch, attribute, occupancy) */
+  FB_ERR_UNSUPPORTED = 3, /* valid but not built: head_dim != 128, group size not in {1,2,4,8}, M > 8 ... */
+  FB_ERR_STATE = 4,       /* object not initialised / used on another device */
+  FB_ERR_TIMEOUT = 5,     /* a device-side wait ran out of time (reported through flashb_device_error) */
+  FB_ERR_DEVICE = 6       /* the device reported an error */
+};
+
+/* ---------------------------------------------------------------------------------------------- library */
+const char* flashb_last_error(void);
+const char* flashb_version(void);
+/* Reads (and with clear != 0 resets) the device error word of the current device: 0 or an FB_ERR_* code set by a
+ * kernel whose bounded wait expired.  Synchronises the device.  No reference counterpart (the reference's spin
+ * barriers are unbounded, flash/csrc/depth_common.cuh:52-65). */
+int flashb_device_error(int clear);
+/* Programmatic dependent launch on (1, default) / off (0) for all later launches of this process. */
+void flashb_set_pdl(int enable);
+
+/* ---------------------------------------------------------------------------------------------- decode attention
+ * Replaces attn_decode (flash/csrc/bb_attn.cu:416-429): GQA single-token attention of q [B, NH, 1, D] over the
+ * static KV cache kc/vc [B, NKV, S, D] (position stride D, element strides c_sb/c_sh for batch/head) with the
+ * additive mask [B|1, 1, 1, >=S] (bf16 if mask_is_bf16 else fp32; m_sb = 0 broadcasts one row).  Keys whose mask is
+ * <= -1e30 contribute nothing; a row with no valid key gives 0.  out [B, 1, NH, D] bf16 contiguous.
+ * ws / ws_floats / counters: the reference's workspace arguments, kept in the signature and unused (may be NULL):
+ * the split-KV partials are merged inside each thread-block cluster through distributed shared memory, so
+ * flashb_attn_ws_floats() returns 0.  D must be 128; NH / NKV in {1, 2, 4, 8}. */
+int64_t flashb_attn_ws_floats(int B, int NH, int NKV, int S, int D);
+int flashb_attn_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* kc, const void* vc, int64_t c_sb,
+                       int64_t c_sh, int B, int NH, int NKV, int S, int D, const void* mask, int mask_is_bf16,
+                       int64_t m_sb, float scaling, float* ws, int64_t ws_floats, int32_t* counters, void* out,
+                       void* stream);
+
+/* Replaces attn_decode_fused (flash/csrc/bb_attn.cu:433-460): qkv [B, (NH + 2 NKV) * D] raw q|k|v projections
+ * (row stride qkv_sb); Qwen3 q_norm/k_norm (weights qn_w/kn_w [D], eps) + RoPE with cos/sin [B, 1, D] bf16 (row
+ * stride cs_sb); writes the new k (normed, roped) and v at slot cache_pos[0] (device int64) of kc/vc, then attends
+ * over slots [0, min(S, cache_pos + 1)) under the mask. */
+int flashb_attn_decode_fused(const void* qkv, int64_t qkv_sb, const void* qn_w, const void* kn_w, float eps,
+                             const void* cos, const void* sin, int64_t cs_sb, void* kc, void* vc, int64_t c_sb,
+                             int64_t c_sh, int B, int NH, int NKV, int S, int D, const void* mask, int mask_is_bf16,
+                             int64_t m_sb, const int64_t* cache_pos, float scaling, float* ws, int64_t ws_floats,
+                             int32_t* counters, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------- fused GEMVs
+ * y[m, n] = sum_k xin[m, k] * W[n, k], nn.Linear layout (W [N, K] bf16 row-major contiguous), fp32 accumulation,
+ * M = 1..8 rows (x row stride ldx, y row stride ldy, both multiples of 8 elements), K % 8 == 0.  All pointers
+ * 16-byte aligned. */
+/* Replaces gemv_seg (flash/csrc/bb_fused.cu:293-316): y[:, 0:N0+N1+N2] = norm?(x) @ [W0; W1; W2]^T, where norm is
+ * the eager Qwen3 RMSNorm with weight nw [K] when nw != NULL.  W1/W2 may be NULL with N1/N2 = 0. */
+int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const void* nw, float eps, const void* W0, int N0,
+                    const void* W1, int N1, const void* W2, int N2, void* y, int64_t ldy, void* stream);
+/* Replaces gemv_resid (flash/csrc/bb_fused.cu:319-335): y = bf16(res + bf16(x @ W^T)); res row stride ldr. */
+int flashb_gemv_resid(const void* x, int64_t ldx, int M, int K, const void* W, int N, const void* res, int64_t ldr,
+                      void* y, int64_t ldy, void* stream);
+/* Replaces gemv_gateup (flash/csrc/bb_fused.cu:338-356): act = bf16(bf16(silu(bf16(n @ Wg^T))) * bf16(n @ Wu^T)),
+ * n = RMSNorm(x; nw, eps); Wg, Wu [N, K]. */
+int flashb_gemv_gateup(const void* x, int64_t ldx, int M, int K, const void* nw, float eps, const void* Wg,
+                       const void* Wu, int N, void* y, int64_t ldy, void* stream);
+/* Replaces rmsnorm (flash/csrc/bb_fused.cu:358-368): y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))). */
+int flashb_rmsnorm(const void* x, int64_t ldx, int M, int K, const void* w, float eps, void* y, int64_t ldy,
+                   void* stream);
+
+/* ---------------------------------------------------------------------------------------------- backbone step ends
+ * Replaces the eager embedding and rotary ops of the decode step (flash/backbone.py:114-116; official
+ * UP/models/cudagraph/backbone_graph.py:257-268, UP = third_party/breeze-tts): x[b] = bf16(sum_c table[ids[b, c] +
+ * c * vocab]) over C codebooks (table [C * vocab, H] bf16, ids [B, C] int64 contiguous), and cos/sin rows [B, D]
+ * gathered from the precomputed bf16 tables [max_pos, D] at position_ids[b] (int64, clamped to [0, max_pos)). */
+int flashb_embed_rope(const int64_t* ids, int B, int C, int vocab, const void* table, int H,
+                      const int64_t* position_ids, const void* cos_tab, const void* sin_tab, int D, int max_pos,
+                      void* x_out, void* cos_out, void* sin_out, void* stream);
+/* Replaces the final norm, the fp32 lm_head and CFG (flash/backbone.py:127-138): hidden = RMSNorm(x; norm_w, eps)
+ * [B, H] bf16; logits[b] = float(hidden[b]) @ W32^T (W32 [V, H] fp32); for B >= 2, cfg[h] = u + gs * (c - u) with
+ * c = logits[h], u = logits[h + B/2] (three separately rounded fp32 ops), else cfg = logits[0].  gs: device fp32
+ * scalar. */
+int flashb_lm_head_cfg(const void* x, int B, int H, const void* norm_w, float eps, const float* W32, int V,
+                       const float* gs, void* hidden_out, float* logits, float* cfg_out, void* stream);
+
+/* Device-side per-frame position update of the streaming loop (the host-side cache_position / position_ids /
+ * _set_attention_mask updates of flash/main_loop.py:123-140 and UP/models/cudagraph/backbone_graph.py:239-252,
+ * 392-395): cache_pos[0] += 1; position_ids[b] += 1; mask[b * m_sb + cache_pos[0]] = 0 for every row b. */
+int flashb_step_advance(int64_t* cache_pos, int64_t* position_ids, int B, void* mask, int mask_is_bf16, int64_t m_sb,
+                        int S, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLASHB_H */

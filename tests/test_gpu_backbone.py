@@ -1,0 +1,102 @@
+"""GPU parity of the whole backbone decode step (``flashb.backbone.fused_decode_step``) against the oracle, its
+CUDA-graph capture, the device-side position advance, and run-to-run determinism."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import assert_close, np32
+from oracle import decode as dec
+
+pytestmark = pytest.mark.gpu
+
+
+def _graph(layers=2, S=1024, valid=300, seed=2, B=2):
+    from flashb.engine import BackboneConfig, SyntheticBackboneGraph
+    cfg = BackboneConfig(layers=layers)
+    g = SyntheticBackboneGraph(cfg, batch_size=B, max_seq_len=S, seed=seed)
+    g.fill_kv(valid)
+    ids = torch.randint(0, cfg.vocab, (B, 1, cfg.codebooks), generator=torch.Generator().manual_seed(seed + 1))
+    g.input_ids_buf.copy_(ids.cuda())
+    return g
+
+
+def _oracle(g):
+    st = g._bb_state
+    layers = []
+    for L in st['layers']:
+        layers.append(dict(ln1=np32(L.ln1_w), wq=np32(L.wq), wk=np32(L.wk), wv=np32(L.wv), qn=np32(L.qn_w),
+                           kn=np32(L.kn_w), wo=np32(L.wo), ln2=np32(L.ln2_w), wg=np32(L.wg), wu=np32(L.wu),
+                           wd=np32(L.wd)))
+    W = dec.BackboneWeights(layers, np32(g.norm_w), np32(g.embed), g.lm_head32.cpu().numpy(), g.cfg.vocab,
+                            g.cfg.eps, g.cfg.theta)
+    kcs = [np32(L.keys).copy() for L in g.static_cache.layers]
+    vcs = [np32(L.values).copy() for L in g.static_cache.layers]
+    return W, kcs, vcs
+
+
+def test_backbone_step_matches_oracle():
+    g = _graph(layers=2)
+    W, kcs, vcs = _oracle(g)
+    pos = int(g.cache_position.item())
+    h_ref, lg_ref, cfg_ref = dec.backbone_step(W, g.input_ids_buf.view(2, -1).cpu().numpy(), kcs, vcs,
+                                               np32(g.attn_mask), pos, g.position_ids.view(-1).cpu().numpy(),
+                                               float(g.guidance_scale.item()))
+    g.decode_step()
+    torch.cuda.synchronize()
+    assert_close(np32(g.hidden_buf).reshape(2, -1), h_ref, what='hidden')
+    assert_close(g.logits_buf.cpu().numpy(), lg_ref, what='logits')
+    assert_close(g.cfg_logits_buf.cpu().numpy(), cfg_ref, what='cfg logits')
+    for li in range(2):
+        assert_close(np32(g.static_cache.layers[li].keys)[:, :, pos], kcs[li][:, :, pos], what='k write')
+    agree = np.mean(np.argmax(g.logits_buf.cpu().numpy(), -1) == np.argmax(lg_ref, -1))
+    assert agree == 1.0
+
+
+def test_backbone_graph_capture_and_advance_match_eager():
+    """Three captured steps (advance + step) replayed equal three eager steps, bit for bit."""
+    ga = _graph(layers=3, S=512, valid=100, seed=5)
+    gb = _graph(layers=3, S=512, valid=100, seed=5)
+    for _ in range(3):
+        ga.advance()
+        ga.decode_step()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        gb.advance()
+        gb.decode_step()            # warm-up (first step) outside the graph
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            gb.advance()
+            gb.decode_step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph.replay()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert int(ga.cache_position.item()) == int(gb.cache_position.item()) == 103
+    assert torch.equal(ga.cfg_logits_buf, gb.cfg_logits_buf)
+    assert torch.equal(ga.hidden_buf, gb.hidden_buf)
+    for la, lb in zip(ga.static_cache.layers, gb.static_cache.layers):
+        assert torch.equal(la.keys, lb.keys) and torch.equal(la.values, lb.values)
+
+
+def test_backbone_step_full_depth_argmax_and_determinism():
+    """28 layers: two runs are bitwise equal; logits stay within tolerance of the oracle."""
+    g = _graph(layers=28, S=1024, valid=1023)
+    W, kcs, vcs = _oracle(g)
+    pos = 1023
+    h_ref, lg_ref, cfg_ref = dec.backbone_step(W, g.input_ids_buf.view(2, -1).cpu().numpy(), kcs, vcs,
+                                               np32(g.attn_mask), pos, g.position_ids.view(-1).cpu().numpy(),
+                                               float(g.guidance_scale.item()))
+    k0 = [L.keys.clone() for L in g.static_cache.layers]
+    g.decode_step()
+    torch.cuda.synchronize()
+    first = g.cfg_logits_buf.clone()
+    assert_close(g.logits_buf.cpu().numpy(), lg_ref, what='28-layer logits')
+    assert np.mean(np.argmax(g.logits_buf.cpu().numpy(), -1) == np.argmax(lg_ref, -1)) == 1.0
+    for L, k in zip(g.static_cache.layers, k0):
+        L.keys.copy_(k)
+    g.decode_step()
+    torch.cuda.synchronize()
+    assert torch.equal(first, g.cfg_logits_buf)

@@ -1,0 +1,235 @@
+"""GPU parity of the individual kernels against the CPU oracle on identical seeded bf16 inputs.
+
+Tolerance: max |gpu - oracle| <= 1e-2 * max |oracle| for bf16 / fp32 outputs; the oracle is
+itself bit-exact against the reference's eager modules (tests/test_oracle_golden.py)."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import TOL, assert_close, bf16_min, np32, randn
+from oracle import decode as dec
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope='module')
+def ops():
+    from flashb import kernels
+    return kernels.fused(), kernels.attn()
+
+
+# ------------------------------------------------------------------------------------------------ GEMVs
+@pytest.mark.parametrize('M', [1, 2, 4, 8])
+def test_gemv_seg_norm_qkv(ops, M):
+    fx, _ = ops
+    K = 2048
+    x = randn((M, K), 1)
+    nw = randn((K,), 2, 0.1, 1.0)
+    Wq, Wk, Wv = randn((2048, K), 3, 0.02), randn((512, K), 4, 0.02), randn((512, K), 5, 0.02)
+    y = torch.empty(M, 3072, dtype=torch.bfloat16, device='cuda')
+    fx.gemv_seg(x, nw, 1e-6, Wq, Wk, Wv, y)
+    ref = dec.gemv_seg(np32(x), np32(nw), 1e-6, [np32(Wq), np32(Wk), np32(Wv)])
+    assert_close(np32(y), ref, what=f'gemv_seg M={M}')
+
+
+def test_gemv_seg_plain_odd_shapes(ops):
+    fx, _ = ops
+    M, K = 2, 1000   # K % 8 == 0 but not a multiple of the stage width
+    x = randn((M, K), 11)
+    W0, W1 = randn((77, K), 12, 0.05), randn((13, K), 13, 0.05)
+    y = torch.empty(M, 90, dtype=torch.bfloat16, device='cuda')
+    fx.gemv_seg(x, None, 0.0, W0, W1, None, y)
+    ref = dec.gemv_seg(np32(x), None, 0.0, [np32(W0), np32(W1)])
+    assert_close(np32(y), ref, what='gemv_seg odd')
+
+
+@pytest.mark.parametrize('M,K,N', [(2, 2048, 2048), (2, 3072, 2048), (2, 6144, 2048), (4, 4096, 1024), (1, 2048, 5)])
+def test_gemv_resid(ops, M, K, N):
+    fx, _ = ops
+    x = randn((M, K), 21)
+    W = randn((N, K), 22, 0.02)
+    res = randn((M, N), 23)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+    fx.gemv_resid(x, W, res, y)
+    ref = dec.gemv_resid(np32(x), np32(W), np32(res))
+    assert_close(np32(y), ref, what='gemv_resid')
+
+
+@pytest.mark.parametrize('M', [1, 2, 4])
+def test_config2_gateup_then_down(ops, M):
+    """RMSNorm + [6144 x 2048] gate|up GEMV + SiLU*up, then the [2048 x 3072] down GEMV."""
+    fx, _ = ops
+    g = torch.Generator().manual_seed(1)
+    x = (torch.randn(M, 2048, generator=g)).to(torch.bfloat16).cuda()
+    gamma = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).cuda()
+    W1 = (0.02 * torch.randn(6144, 2048, generator=g)).to(torch.bfloat16).cuda()
+    W2 = (0.02 * torch.randn(2048, 3072, generator=g)).to(torch.bfloat16).cuda()
+    act = torch.empty(M, 3072, dtype=torch.bfloat16, device='cuda')
+    y = torch.empty(M, 2048, dtype=torch.bfloat16, device='cuda')
+    fx.gemv_gateup(x, gamma, 1e-6, W1[:3072], W1[3072:], act)
+    fx.gemv_resid(act, W2, x, y)
+    ref_act = dec.gemv_gateup(np32(x), np32(gamma), 1e-6, np32(W1[:3072]), np32(W1[3072:]))
+    assert_close(np32(act), ref_act, what='gateup')
+    ref_y = dec.gemv_resid(np32(act), np32(W2), np32(x))
+    assert_close(np32(y), ref_y, what='down')
+    # exactness rate: identical rounding points, only the fp32 summation order differs
+    assert np.mean(np32(act) == ref_act) > 0.9
+
+
+def test_rmsnorm(ops):
+    fx, _ = ops
+    x = randn((4, 2048), 31, 3.0)
+    w = randn((2048,), 32, 0.1, 1.0)
+    y = torch.empty_like(x)
+    fx.rmsnorm(x, w, 1e-6, y)
+    ref = dec.rmsnorm(np32(x), np32(w), 1e-6)
+    assert_close(np32(y), ref, what='rmsnorm')
+    assert np.mean(np32(y) == ref) > 0.99
+
+
+def test_gemv_rejects_bad_tensors(ops):
+    fx, _ = ops
+    x = randn((2, 2048), 1)
+    W = randn((64, 1024), 2)
+    y = torch.empty(2, 64, dtype=torch.bfloat16, device='cuda')
+    with pytest.raises(RuntimeError):
+        fx.gemv_resid(x, W, y, y)          # K mismatch
+    with pytest.raises(RuntimeError):
+        fx.gemv_seg(x.float(), None, 0.0, W, None, None, y)
+
+
+# ------------------------------------------------------------------------------------------------ attention
+def _attn_ws(B, NH, NKV, S):
+    from flashb import kernels
+    n = kernels.attn_ws_floats(B, NH, NKV, S)
+    return (torch.empty(1, device='cuda'), torch.empty(1, device='cuda'), torch.empty(n, device='cuda'),
+            torch.zeros(B * NKV, dtype=torch.int32, device='cuda'))
+
+
+def _mask(B, S, valid, dtype=torch.bfloat16):
+    m = torch.full((B, 1, 1, S), bf16_min() if dtype == torch.bfloat16 else -3.4e38, dtype=torch.float32)
+    for b, (lo, hi) in enumerate(valid):
+        m[b, 0, 0, lo:hi] = 0
+    return m.to(dtype).cuda()
+
+
+@pytest.mark.parametrize('NH,NKV,S,valid', [
+    (16, 4, 1024, ((0, 1024), (0, 1024))),
+    (16, 4, 1000, ((0, 700), (13, 1000))),       # ragged S, left padding
+    (16, 8, 2048, ((0, 1500), (300, 1700))),     # real model GQA group 2
+    (16, 4, 4096, ((0, 4096), (0, 4096))),       # the 4096 sweep point, above the reference's 2048 cap
+    (8, 1, 70, ((0, 1), (69, 70))),              # single valid key
+    (16, 2, 64, ((0, 64), (0, 64))),             # group 8
+])
+def test_attn_decode(ops, NH, NKV, S, valid):
+    _, ax = ops
+    B = 2
+    q = randn((B, NH, 1, 128), 40)
+    k = randn((B, NKV, S, 128), 41)
+    v = randn((B, NKV, S, 128), 42)
+    mask = _mask(B, S, valid)
+    out = torch.empty(B, 1, NH, 128, dtype=torch.bfloat16, device='cuda')
+    sc, cm, part, cnt = _attn_ws(B, NH, NKV, S)
+    ax.attn_decode(q, k, v, mask, 128 ** -0.5, sc, cm, part, cnt, out)
+    ref = dec.attn_decode(np32(q), np32(k), np32(v), np32(mask), 128 ** -0.5)
+    assert_close(np32(out), ref, what=f'attn S={S}')
+
+
+
+def test_attn_decode_fp32_mask_and_dead_row(ops):
+    _, ax = ops
+    B, NH, NKV, S = 2, 16, 4, 300
+    q, k, v = randn((B, NH, 1, 128), 50), randn((B, NKV, S, 128), 51), randn((B, NKV, S, 128), 52)
+    m = torch.zeros(B, 1, 1, S)
+    m[0, 0, 0, 100:] = float('-inf')
+    m[1] = float('-inf')                       # batch 1: every key masked -> zero output
+    m[0, 0, 0, :50] = torch.linspace(-3, 0, 50)  # a non-trivial additive fp32 mask
+    mask = m.cuda()
+    out = torch.empty(B, 1, NH, 128, dtype=torch.bfloat16, device='cuda')
+    sc, cm, part, cnt = _attn_ws(B, NH, NKV, S)
+    ax.attn_decode(q, k, v, mask, 128 ** -0.5, sc, cm, part, cnt, out)
+    ref = dec.attn_decode(np32(q), np32(k), np32(v), np32(mask), 128 ** -0.5, mask_bf16=False)
+    assert_close(np32(out)[0], ref[0], what='fp32 mask')
+    assert float(out[1].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize('NKV,S,pos', [(4, 1024, 1023), (4, 2048, 700), (8, 512, 64), (4, 4096, 4000)])
+def test_attn_decode_fused(ops, NKV, S, pos):
+    _, ax = ops
+    B, NH = 2, 16
+    qkv = randn((B, (NH + 2 * NKV) * 128), 60, 2.0)
+    qn, kn = randn((128,), 61, 0.1, 1.0), randn((128,), 62, 0.1, 1.0)
+    kc, vc = randn((B, NKV, S, 128), 63), randn((B, NKV, S, 128), 64)
+    kc[:, :, pos:] = 0
+    vc[:, :, pos:] = 0
+    from flashb.engine import rope_table
+    cos_t, sin_t = rope_table(1e6, 128, S, 'cuda')
+    pids = torch.tensor([pos, pos - 3])
+    cos, sin = cos_t[pids].view(B, 1, 128).contiguous(), sin_t[pids].view(B, 1, 128).contiguous()
+    mask = _mask(B, S, ((0, pos + 1), (3, pos + 1)))
+    cp = torch.tensor([pos], dtype=torch.long, device='cuda')
+    out = torch.empty(B, 1, NH, 128, dtype=torch.bfloat16, device='cuda')
+    sc, cm, part, cnt = _attn_ws(B, NH, NKV, S)
+    kc_ref, vc_ref = np32(kc).copy(), np32(vc).copy()
+    ax.attn_decode_fused(qkv, qn, kn, 1e-6, cos, sin, kc, vc, mask, cp, 128 ** -0.5, sc, cm, part, cnt, out)
+    ref = dec.attn_decode_fused(np32(qkv), np32(qn), np32(kn), 1e-6, np32(cos), np32(sin), kc_ref, vc_ref,
+                                np32(mask), pos, 128 ** -0.5)
+    assert_close(np32(out), ref, what='fused attn')
+    # the cache write itself: v bit-exact, k (norm + RoPE) within one bf16 ulp
+    assert np.array_equal(np32(vc), vc_ref)
+    assert_close(np32(kc)[:, :, pos], kc_ref[:, :, pos], tol=1e-2, what='k write')
+    assert np.mean(np32(kc)[:, :, pos] == kc_ref[:, :, pos]) > 0.95
+
+
+def test_attn_determinism(ops):
+    _, ax = ops
+    B, NH, NKV, S = 2, 16, 4, 2048
+    q, k, v = randn((B, NH, 1, 128), 70), randn((B, NKV, S, 128), 71), randn((B, NKV, S, 128), 72)
+    mask = _mask(B, S, ((0, S), (0, S)))
+    sc, cm, part, cnt = _attn_ws(B, NH, NKV, S)
+    outs = []
+    for _ in range(3):
+        out = torch.empty(B, 1, NH, 128, dtype=torch.bfloat16, device='cuda')
+        ax.attn_decode(q, k, v, mask, 128 ** -0.5, sc, cm, part, cnt, out)
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+# ------------------------------------------------------------------------------------------------ step ends
+def test_embed_rope(ops):
+    fx, _ = ops
+    B, C, V, H = 2, 16, 2049, 2048
+    table = randn((C * V, H), 80)
+    ids = torch.randint(0, V, (B, C), generator=torch.Generator().manual_seed(81)).cuda()
+    from flashb.engine import rope_table
+    cos_t, sin_t = rope_table(1e6, 128, 600, 'cuda')
+    pos = torch.tensor([517, 3], dtype=torch.long, device='cuda')
+    x = torch.empty(B, H, dtype=torch.bfloat16, device='cuda')
+    cos = torch.empty(B, 1, 128, dtype=torch.bfloat16, device='cuda')
+    sin = torch.empty_like(cos)
+    fx.embed_rope(ids, V, table, pos, cos_t, sin_t, x, cos, sin)
+    ref = dec.embed_sum(np32(table), ids.cpu().numpy(), V)
+    assert_close(np32(x), ref, what='embed')
+    assert np.mean(np32(x) == ref) > 0.99
+    assert torch.equal(cos.view(B, 128), cos_t[pos.cpu()].cuda()) and torch.equal(sin.view(B, 128), sin_t[pos.cpu()])
+
+
+@pytest.mark.parametrize('B', [1, 2, 4])
+def test_lm_head_cfg(ops, B):
+    fx, _ = ops
+    H, V = 2048, 2049
+    x = randn((B, H), 90, 2.0)
+    nw = randn((H,), 91, 0.1, 1.0)
+    W = randn((V, H), 92, 0.02).float()
+    gs = torch.tensor([4.0], device='cuda')
+    hid = torch.empty(B, H, dtype=torch.bfloat16, device='cuda')
+    logits = torch.empty(B, V, device='cuda')
+    half = B // 2 if B >= 2 else 1
+    cfg = torch.empty(half, V, device='cuda')
+    fx.lm_head_cfg(x, nw, 1e-6, W, gs, hid, logits, cfg)
+    h_ref = dec.rmsnorm(np32(x), np32(nw), 1e-6)
+    assert_close(np32(hid), h_ref, what='final norm')
+    lg_ref = dec.lm_head_fp32(np32(hid), W.cpu().numpy())   # same bf16 hidden -> only summation order differs
+    assert_close(logits.cpu().numpy(), lg_ref, tol=1e-5, what='lm_head')
+    cfg_ref = dec.cfg_combine(logits.cpu().numpy(), half, 4.0) if B >= 2 else logits.cpu().numpy()[:1]
+    assert np.array_equal(cfg.cpu().numpy(), cfg_ref), 'CFG combine is elementwise: bit-exact given the logits'
