@@ -1,0 +1,228 @@
+// flashb: building blocks of the persistent (one launch per step) kernels: a bounded grid barrier and the
+// producer / consumer halves of a streamed GEMV task over the fb_stream.cuh ring.
+//
+// A persistent kernel runs one CTA per SM (cooperative launch, so all CTAs are resident).  Warps 0..7 consume, warp
+// 8 produces: it walks the kernel's static list of GEMV tasks and streams this CTA's row slice of every weight
+// matrix into the ring, stopping only when the ring is full.  Weights never depend on activations, so the producer
+// keeps streaming while the consumers wait at a grid barrier; the ring depth (up to ~200 KB per SM) covers the
+// barrier latency.
+#pragma once
+#include "fb_stream.cuh"
+
+namespace fb {
+
+constexpr int PK_MAX_STAGES = 4;
+constexpr int PK_CONSUMERS = ST_CWARPS * 32;        // 256
+constexpr int PK_THREADS = PK_CONSUMERS + 32;       // + producer warp
+
+// Grid barrier state (zero-initialised by the caller).  `count` only grows during a launch; the last CTA to leave the
+// kernel resets it (grid_exit), so every launch starts from zero.
+struct GridBar {
+  unsigned count;
+  unsigned exitc;
+  unsigned abort;
+  unsigned pad;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Barrier over the consumer warps of every CTA: arrival is one fire-and-forget release-add on a monotonic counter,
+// completion of barrier number `epoch` is count >= epoch * gridDim.x (observed with acquire loads).  The critical
+// path is one add plus one poll round trip through L2.  Waits are bounded (WAIT_LIMIT_NS); on expiry, or when another
+// CTA has aborted, every CTA returns false and the kernel winds down (the host then re-zeroes the state).
+__device__ __forceinline__ bool grid_sync(GridBar* gb, unsigned& epoch, unsigned* err, int* s_flag) {
+  named_sync(2, PK_CONSUMERS);
+  ++epoch;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const unsigned target = epoch * gridDim.x;
+    __threadfence();
+    red_release_add(&gb->count, 1u);
+    if (ld_acquire_u32(&gb->count) < target) {
+      const uint64_t t0 = globaltimer();
+      int spins = 0;
+      while (ld_acquire_u32(&gb->count) < target) {
+        if (++spins == 256) {
+          spins = 0;
+          if (ld_acquire_u32(&gb->abort)) { ok = 0; break; }
+          if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+            set_error(err, FB_ERR_TIMEOUT);
+            atomicExch(&gb->abort, 1u);
+            ok = 0;
+            break;
+          }
+        }
+      }
+    }
+    *s_flag = ok;
+  }
+  named_sync(2, PK_CONSUMERS);
+  return *s_flag != 0;
+}
+
+// Called once by consumer thread 0 of every CTA after its last barrier: the last CTA out resets the barrier.
+// Every CTA increments `exitc` only after it has observed the final barrier, so the reset races with no waiter.
+__device__ __forceinline__ void grid_exit(GridBar* gb) {
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&gb->exitc, 1u) == gridDim.x - 1) {
+      atomicExch(&gb->count, 0u);
+      atomicExch(&gb->exitc, 0u);
+    }
+  }
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// The ring of one persistent CTA.
+struct Ring {
+  unsigned char* base;
+  uint64_t* full;
+  uint64_t* empty;
+  int nst;
+};
+
+// A streamed GEMV task: `units` output units over K columns; NMAT = 2 pairs each unit with a second weight row
+// (gate/up, or the two rotary halves of a q/k head dimension).  Row pointers come from a functor row(n, mat).
+// CTA c owns units [units * c / G, units * (c + 1) / G).
+__device__ __forceinline__ void task_range(int units, int& u0, int& u1) {
+  u0 = (int)((long long)units * blockIdx.x / gridDim.x);
+  u1 = (int)((long long)units * (blockIdx.x + 1) / gridDim.x);
+}
+
+// Producer half: stream this CTA's stages of the task; t is the running stage counter.  Returns false on timeout.
+template <int NMAT, typename RowFn>
+__device__ __forceinline__ bool produce_task(Ring& rg, int& t, int units, int K, RowFn row, unsigned* err) {
+  constexpr int UG = ST_ROWS / NMAT;
+  const int lane = threadIdx.x & 31;
+  int u0, u1;
+  task_range(units, u0, u1);
+  const int nkc = (K + ST_KC - 1) / ST_KC;
+  for (int n0 = u0; n0 < u1; n0 += UG) {
+    const int nu = min(UG, u1 - n0);
+    for (int kc = 0; kc < nkc; ++kc, ++t) {
+      const int s = t % rg.nst;
+      if (t >= rg.nst && !mbar_wait_warp(&rg.empty[s], ((t / rg.nst) - 1) & 1, err)) return false;
+      const int k0 = kc * ST_KC;
+      const int kw = min(ST_KC, K - k0);
+      unsigned char* st = rg.base + (size_t)s * ST_BYTES;
+      if (lane == 0) mbar_arrive_expect_tx(&rg.full[s], (unsigned)(nu * NMAT * kw * 2));
+      __syncwarp();
+      if (lane < ST_ROWS) {
+        const int i = lane % UG, mat = lane / UG;
+        if (i < nu) bulk_g2s(st + lane * ST_PITCH, row(n0 + i, mat) + k0, (unsigned)(kw * 2), &rg.full[s]);
+      }
+    }
+  }
+  return true;
+}
+
+// L2 prefetch of this CTA's slice of a task (one bulk prefetch per weight row).  Measured on the backbone step it
+// does not pay off (the critical path is latency, not bandwidth), so the step kernels do not call it; kept as a tool.
+template <int NMAT, typename RowFn>
+__device__ __forceinline__ void prefetch_task(int units, int K, RowFn row) {
+  const int lane = threadIdx.x & 31;
+  int u0, u1;
+  task_range(units, u0, u1);
+  const int n = (u1 - u0) * NMAT;
+  for (int i = lane; i < n; i += 32) prefetch_l2(row(u0 + i / NMAT, i % NMAT), (unsigned)(K * 2));
+}
+
+// Consumer half: multiply the task's stages by the activation rows xs (M rows, byte pitch x_pitch) and hand each
+// 16-row group's sums (sums[r * 8 + m], r < 16) to epi(n0, nu, sums).  All 256 consumer threads call it.
+template <int NMAT, typename EpiFn>
+__device__ __forceinline__ bool consume_task(Ring& rg, int& t, int units, int K, const unsigned char* xs, int x_pitch,
+                                             int M, const unsigned char* zero16, float* red, float* sums, EpiFn epi,
+                                             unsigned* err) {
+  constexpr int UG = ST_ROWS / NMAT;
+  const int lane = threadIdx.x & 31;
+  int u0, u1;
+  task_range(units, u0, u1);
+  const int nkc = (K + ST_KC - 1) / ST_KC;
+  for (int n0 = u0; n0 < u1; n0 += UG) {
+    const int nu = min(UG, u1 - n0);
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kc = 0; kc < nkc; ++kc, ++t) {
+      const int s = t % rg.nst;
+      if (!mbar_wait_warp(&rg.full[s], (t / rg.nst) & 1, err)) return false;
+      const int k0 = kc * ST_KC;
+      stage_mma(rg.base + (size_t)s * ST_BYTES, min(ST_KC, K - k0), xs, x_pitch, M, k0, zero16, c);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rg.empty[s]);
+    }
+    reduce_warps(c, red, sums, 1);
+    epi(n0, nu, sums);
+  }
+  return true;
+}
+
+// Stage rows [0, M) of a global bf16 activation matrix (row stride ld) into xs, optionally applying the eager
+// Qwen3 RMSNorm with weight nw (double rounding).  Cross-CTA data: read through L2 (ld.global.cg).
+__device__ __forceinline__ void load_x(unsigned char* xs, int x_pitch, const bf16* x, long ld, int M, int K,
+                                       const bf16* nw, float eps, float* nred /* [8][8] */) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kv = K >> 3;
+  float ss[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) ss[m] = 0.f;
+  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
+    const int m = i / kv, j = i - m * kv;
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(x + (size_t)m * ld) + j);
+    *reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16) = v;
+    if (nw) {
+      float f[8];
+      cvt8(v, f);
+      float q = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) q = fmaf(f[u], f[u], q);
+#pragma unroll
+      for (int mm = 0; mm < 8; ++mm)
+        if (mm == m) ss[mm] += q;
+    }
+  }
+  if (nw) {
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const float q = warp_sum(ss[m]);
+      if (lane == 0) nred[warp * 8 + m] = q;
+    }
+    named_sync(1, PK_CONSUMERS);
+    float rs[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      float q = 0.f;
+#pragma unroll
+      for (int w = 0; w < ST_CWARPS; ++w) q += nred[w * 8 + m];
+      rs[m] = 1.0f / sqrtf(q / (float)K + eps);
+    }
+    for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
+      const int m = i / kv, j = i - m * kv;
+      uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
+      float f[8], w[8];
+      cvt8(*px, f);
+      cvt8(*reinterpret_cast<const uint4*>(nw + (size_t)j * 8), w);
+      float r = 0.f;
+#pragma unroll
+      for (int mm = 0; mm < 8; ++mm)
+        if (mm == m) r = rs[mm];
+      uint4 o;
+      o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
+      o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
+      o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
+      o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
+      *px = o;
+    }
+  }
+  named_sync(1, PK_CONSUMERS);
+}
+
+}  // namespace fb

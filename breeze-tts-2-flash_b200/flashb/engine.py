@@ -163,8 +163,8 @@ class SyntheticBackboneGraph:
                                         self.attn_mask.data_ptr(), 1, self.attn_mask.stride(0), S,
                                         torch.cuda.current_stream(self.device).cuda_stream))
 
-    def decode_step(self):
-        bb.fused_decode_step(self)
+    def decode_step(self, advance=False):
+        bb.fused_decode_step(self, advance=advance)
 
     def layer_weight_bytes(self):
         return self.cfg.weight_bytes_per_layer()
