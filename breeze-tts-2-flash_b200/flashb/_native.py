@@ -48,7 +48,23 @@ _PROTOS = {
     'flashb_bb_scratch_bytes': (L, [P]),
     'flashb_bb_layer_bytes': (L, []),
     'flashb_bb_step': (I, [P, P, P, P, P, P, P, I, L, P, I, P, P, P, P]),
+    'flashb_dd_scratch_bytes': (L, [P]),
+    'flashb_dd_layer_bytes': (L, []),
+    'flashb_dd_frame': (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
 }
+
+
+class FbDDLayer(ctypes.Structure):
+    """fb_dd_layer of include/flashb.h."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ('ln1', 'wq', 'wk', 'wv', 'wo', 'ln2', 'wg', 'wu', 'wd')]
+
+
+class FbDDConfig(ctypes.Structure):
+    """fb_dd_config of include/flashb.h."""
+    _fields_ = [('layers', I), ('batch', I), ('hidden', I), ('embed_dim', I), ('heads', I), ('kv_heads', I),
+                ('head_dim', I), ('ffn', I), ('vocab', I), ('codebook_size', I), ('n_decode', I), ('eps', F),
+                ('scaling', F), ('embed', P), ('proj', P), ('normf', P), ('head_t', P), ('cos_tab', P),
+                ('sin_tab', P)]
 
 
 class FbBBLayer(ctypes.Structure):

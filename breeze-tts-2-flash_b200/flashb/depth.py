@@ -1,0 +1,224 @@
+"""Depth decoder frame on the flashb kernel, with the reference hook's surface (``flash/depth.py:1-227``).
+
+``DepthDecoderGraph._full_loop`` (``UP/models/cudagraph/depth_decoder_graph.py:558-654``) becomes: the per-codebook
+Exp(1) draws with the official sizes and order (``q[c].exponential_(1)``, the RNG consumption of the official
+``torch.multinomial`` calls) plus ONE cooperative launch (``flashb_dd_frame``) that decodes every codebook of the frame
+and samples on the device.  The weights stay bf16 (the reference's 12-bit LN12 packing is not used); the codebook
+heads are transposed once to [n_decode, vocab, hidden] bf16 (bf16-exact, as the reference asserts).
+
+``BUILDS`` / ``GRIDS`` keep the reference's names; one build serves every batch size and the grid is always one CTA
+per SM.  Process state (``_state``) is keyed by device, so several graphs on several GPUs in one process coexist.
+"""
+import ctypes
+import json
+import time
+
+import torch
+
+from . import _native, kernels
+from ._native import check
+
+BUILDS = {1: 'full', 2: 'full', 4: 'full'}
+GRIDS = {1: 0, 2: 0, 4: 0}      # 0 = one CTA per SM
+_state = {}
+
+
+def log(msg):
+    print(f'[flashb] {msg}', flush=True)
+
+
+class DepthModelDesc:
+    """Device-side descriptors + scratch of one depth model (weights owned by the caller)."""
+
+    def __init__(self, layers, embed, proj, normf, head_t, cos_tab, sin_tab, eps, scaling, codebook_size, batch,
+                 device):
+        L0 = layers[0]
+        recs = (_native.FbDDLayer * len(layers))()
+        for i, w in enumerate(layers):
+            recs[i] = _native.FbDDLayer(*[t.data_ptr() for t in (w['ln1'], w['wq'], w['wk'], w['wv'], w['wo'],
+                                                                 w['ln2'], w['wg'], w['wu'], w['wd'])])
+        self.table = torch.frombuffer(bytearray(bytes(recs)), dtype=torch.uint8).to(device)
+        c = _native.FbDDConfig()
+        c.layers, c.batch, c.hidden, c.embed_dim = len(layers), batch, L0['wq'].shape[1], embed.shape[1]
+        c.heads, c.kv_heads, c.head_dim, c.ffn = L0['wq'].shape[0] // 128, L0['wk'].shape[0] // 128, 128, \
+            L0['wg'].shape[0]
+        c.vocab, c.codebook_size, c.n_decode = head_t.shape[1], codebook_size, head_t.shape[0]
+        c.eps, c.scaling = float(eps), float(scaling)
+        c.embed, c.proj, c.normf, c.head_t = embed.data_ptr(), proj.data_ptr(), normf.data_ptr(), head_t.data_ptr()
+        c.cos_tab, c.sin_tab = cos_tab.data_ptr(), sin_tab.data_ptr()
+        self.cfg = c
+        self.keep = (layers, embed, proj, normf, head_t, cos_tab, sin_tab)
+        n = int(_native.lib().flashb_dd_scratch_bytes(ctypes.byref(c)))
+        self.scratch = torch.zeros(n, dtype=torch.uint8, device=device)
+
+    def frame(self, first_cb, bh, tokbuf, outtok, temp, topk, topp, dosample, gs, q, dbg=None, forced=None):
+        _p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        check(_native.lib().flashb_dd_frame(
+            ctypes.byref(self.cfg), self.table.data_ptr(), self.scratch.data_ptr(), _p(first_cb), _p(bh), _p(tokbuf),
+            _p(outtok), _p(temp), _p(topk), _p(topp), _p(dosample), _p(gs), _p(q), _p(dbg), _p(forced),
+            torch.cuda.current_stream(bh.device).cuda_stream))
+
+
+class DepthOps:
+    """flash_dd_*: the reference's dd2_* entry points (flash/csrc/depth_frame.cu:923-934) on flashb_dd_frame."""
+
+    def __init__(self):
+        self.desc = {}     # batch -> DepthModelDesc
+        self.args = None
+
+    def dd2_init(self, w, bufs=None, eps=1e-5, scaling=128 ** -0.5, grid=0, codebook_size=None):
+        """w: per layer [ln1, wq, wk, wv, wo, ln2, wg, wu, wd] x NL + [embed, proj, normf, head_t, cos, sin] (bf16).
+        ``bufs`` (the reference's scratch tensors) is accepted and unused: flashb keeps its own zeroed scratch."""
+        if (len(w) - 6) % 9 != 0:
+            raise RuntimeError('bad weight count')
+        nl = (len(w) - 6) // 9
+        names = ('ln1', 'wq', 'wk', 'wv', 'wo', 'ln2', 'wg', 'wu', 'wd')
+        layers = [{n: w[l * 9 + i].contiguous() for i, n in enumerate(names)} for l in range(nl)]
+        embed, proj, normf, head_t, cos, sin = [t.contiguous() for t in w[nl * 9:]]
+        V = head_t.shape[1]
+        self.args = (layers, embed, proj, normf, head_t, cos, sin, float(eps), float(scaling),
+                     int(codebook_size if codebook_size is not None else min(V, 2048)))
+        self.desc = {}
+
+    def dd2_set_grid(self, B, grid):
+        if B not in (1, 2, 4):
+            raise RuntimeError('B must be 1, 2 or 4')
+        GRIDS[B] = int(grid)
+
+    def _desc(self, B, device):
+        d = self.desc.get(B)
+        if d is None:
+            if self.args is None:
+                raise RuntimeError('dd2_init first')
+            layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb = self.args
+            d = DepthModelDesc(layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb, B, device)
+            self.desc[B] = d
+        return d
+
+    def dd2_frame(self, first_cb, bh, tokbuf, outtok, temp, topk, topp, dosample, gs, q, dbg=None, forced=None):
+        B = int(bh.shape[0])
+        self._desc(B, bh.device).frame(first_cb, bh, tokbuf, outtok, temp, topk, topp, dosample, gs, q, dbg, forced)
+
+    def dd2_info(self):
+        a = self.args
+        return json.dumps(dict(NL=len(a[0]) if a else 0, ln12=0, pf_last=0, tab=0, grid=0,
+                               grid_B1=GRIDS[1], grid_B2=GRIDS[2], grid_B4=GRIDS[4], persisting_l2_limit=0))
+
+    def dd2_tab_build(self):
+        raise RuntimeError('the per-token step table (flash/csrc/depth_frame.cu:714-754) is not built by flashb')
+
+    def dd2_tab_set(self, pt, tt):
+        raise RuntimeError('the per-token step table (flash/csrc/depth_frame.cu:714-754) is not built by flashb')
+
+
+def _orig(mod):
+    return getattr(mod, '_orig_mod', mod)
+
+
+class DepthMegakernel:
+    """Depth frame on flashb for an official BreezeDepthDecoderForCausalLM-like object (``model`` +
+    ``codebooks_head``), as ``flash/depth.py:97-157``.  Shapes are read from the model instead of asserted."""
+    MAXB = 4
+
+    def __init__(self, depth_decoder, device='cuda', codebook_size=None):
+        model = depth_decoder.model
+        cfg = model.config
+        if getattr(model, 'backbone_hidden_state_projector', None) is not None:
+            raise RuntimeError('backbone_hidden_state_projector is not supported')
+        ws = []
+        for layer in model.layers:
+            L = _orig(layer)
+            a, mlp = L.self_attn, L.mlp
+            ws += [L.input_layernorm.weight, a.q_proj.weight, a.k_proj.weight, a.v_proj.weight, a.o_proj.weight,
+                   L.post_attention_layernorm.weight, mlp.gate_proj.weight, mlp.up_proj.weight, mlp.down_proj.weight]
+        head = _orig(depth_decoder.codebooks_head).weight            # [n_decode, hidden, vocab] (fp32 after init)
+        head_t = head.detach().permute(0, 2, 1).contiguous().to(torch.bfloat16)
+        if not torch.equal(head_t.float(), head.detach().float().permute(0, 2, 1)):
+            raise RuntimeError('codebook head is not bf16-exact')
+        n_pos = head_t.shape[0] + 2
+        pos = torch.arange(n_pos, device=device).unsqueeze(0)
+        dummy = torch.zeros(1, n_pos, cfg.hidden_size, dtype=torch.bfloat16, device=device)
+        with torch.no_grad():
+            cos, sin = model.rotary_emb(dummy, pos)
+        ws += [model.embed_tokens.weight, model.inputs_embeds_projector.weight, _orig(model.norm).weight, head_t,
+               cos[0].contiguous().to(torch.bfloat16), sin[0].contiguous().to(torch.bfloat16)]
+        self._weights = [w.detach().contiguous() for w in ws]
+        self.ops = DepthOps()
+        self.ops.dd2_init(self._weights, None, float(cfg.rms_norm_eps), 128 ** -0.5, 0, codebook_size)
+        t = time.perf_counter()
+        _state[str(device)] = dict(info=dict(layers=len(model.layers), vocab=int(head_t.shape[1]),
+                                             n_decode=int(head_t.shape[0]), init_s=round(time.perf_counter() - t, 3)))
+
+    def frame(self, first_cb, bh, tokbuf, outtok, temp, topk, topp, dosample, gs, q, dbg=None, forced=None):
+        self.ops.dd2_frame(first_cb, bh, tokbuf, outtok, temp, topk, topp, dosample, gs, q, dbg, forced)
+
+
+def _full_loop_mk(self):
+    """Drop-in for DepthDecoderGraph._full_loop: the official number of exponential_ draws in the official order,
+    then ONE frame launch that writes _tok_buf and output_tokens (``flash/depth.py:160-169``)."""
+    B = self.batch_size
+    q = self._mk2_q[B]
+    for c in range(self.num_decode_codebooks):
+        q[c].exponential_(1)
+    self._mega2.frame(self.first_cb_token_buf, self.backbone_hidden_buf, self._tok_buf, self.output_tokens,
+                      self.temperature_buf.view(-1), self.top_k_buf.view(-1), self.top_p_buf.view(-1),
+                      self.do_sample_buf.view(-1), self.guidance_scale.view(-1), q, getattr(self, '_mk2_dbg', None))
+
+
+class _DepthShim:
+    def __init__(self, graph):
+        self.model = graph.depth_model
+        self.codebooks_head = graph._orig_codebooks_head
+
+
+def _eligible(graph):
+    return all(b in (1, 2, 4) for b in (graph.bucket_sizes or [graph.batch_size]))
+
+
+def attach(graph):
+    if not _eligible(graph):
+        graph._mega2 = None
+        return graph
+    if getattr(graph, '_mega2', None) is None:
+        graph._mega2 = DepthMegakernel(_DepthShim(graph), device=graph.device,
+                                       codebook_size=getattr(graph, 'codec_codebook_size', None))
+        graph._mk2_q = {b: torch.zeros(graph.num_decode_codebooks, max(1, b // 2), graph.vocab_size,
+                                       dtype=torch.float32, device=graph.device) for b in (1, 2, 4)}
+    return graph
+
+
+def install(api=None):
+    from models.cudagraph import depth_decoder_graph as ddg
+    cls = ddg.DepthDecoderGraph
+    if getattr(cls, '_flash_depth', False):
+        return
+    kernels.depth('full')
+    orig_capture, orig_prepare, orig_set_top_k, orig_full_loop = cls.capture, cls.prepare_eager, cls.set_top_k, \
+        cls._full_loop
+
+    def capture(self, num_warmup=3):
+        attach(self)
+        return orig_capture(self, num_warmup)
+
+    def prepare_eager(self):
+        attach(self)
+        return orig_prepare(self)
+
+    def set_top_k(self, v):
+        vv = v if isinstance(v, (int, float)) else int(v.max().item())
+        if not (0 <= vv <= 1024):
+            raise ValueError('top_k out of range for the frame sampler')
+        return orig_set_top_k(self, v)
+
+    def full_loop(self):
+        if getattr(self, '_mega2', None) is not None and self.batch_size in (1, 2, 4):
+            return _full_loop_mk(self)
+        return orig_full_loop(self)
+
+    cls.capture, cls.prepare_eager, cls.set_top_k, cls._full_loop = capture, prepare_eager, set_top_k, full_loop
+    cls._flash_depth = True
+    log('installed: depth frame kernel (one launch per frame; other buckets use the official loop)')
+
+
+def manifest():
+    return {k: dict(v.get('info', {})) for k, v in _state.items()}

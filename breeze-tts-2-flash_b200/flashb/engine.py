@@ -170,6 +170,72 @@ class SyntheticBackboneGraph:
         return self.cfg.weight_bytes_per_layer()
 
 
+@dataclass
+class DepthConfig:
+    hidden: int = 1024
+    embed_dim: int = 2048
+    layers: int = 4
+    heads: int = 8
+    kv_heads: int = 2
+    ffn: int = 4096
+    vocab: int = 2048
+    codebook_size: int = 2048
+    n_decode: int = 16
+    theta: float = 500000.0
+    eps: float = 1e-5
+
+    def step_weight_bytes(self):
+        """bf16 bytes streamed per codebook step: the layers, the projector and one codebook head."""
+        H, D = self.hidden, 128
+        layer = (self.heads * D + 2 * self.kv_heads * D) * H + H * self.heads * D + 3 * self.ffn * H
+        return 2 * (self.layers * layer + H * self.embed_dim + self.vocab * H)
+
+
+class SyntheticDepth:
+    """A depth decoder with synthetic bf16 weights (heads stored transposed [n_decode, vocab, hidden]) and the
+    official graph's I/O buffers for ``batch`` rows."""
+
+    def __init__(self, cfg: DepthConfig, batch=2, device='cuda', seed=3):
+        from .depth import DepthModelDesc
+        self.cfg = cfg
+        self.device = dev = torch.device(device)
+        self.batch = B = batch
+        self.half = B // 2 if B >= 2 else 1
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        H, AE, D, NH, NKV, F = cfg.hidden, cfg.embed_dim, 128, cfg.heads, cfg.kv_heads, cfg.ffn
+        self.layers = []
+        for _ in range(cfg.layers):
+            self.layers.append(dict(
+                ln1=_randn((H,), g, dev, 0.1, 1.0), wq=_randn((NH * D, H), g, dev, 0.02),
+                wk=_randn((NKV * D, H), g, dev, 0.02), wv=_randn((NKV * D, H), g, dev, 0.02),
+                wo=_randn((H, NH * D), g, dev, 0.02), ln2=_randn((H,), g, dev, 0.1, 1.0),
+                wg=_randn((F, H), g, dev, 0.02), wu=_randn((F, H), g, dev, 0.02), wd=_randn((H, F), g, dev, 0.02)))
+        self.embed = _randn(((cfg.n_decode + 1) * cfg.vocab, AE), g, dev, 1.0)
+        self.proj = _randn((H, AE), g, dev, 0.02)
+        self.normf = _randn((H,), g, dev, 0.1, 1.0)
+        self.head_t = _randn((cfg.n_decode, cfg.vocab, H), g, dev, 0.02)
+        self.cos_tab, self.sin_tab = rope_table(cfg.theta, D, cfg.n_decode + 2, dev)
+        self.desc = DepthModelDesc(self.layers, self.embed, self.proj, self.normf, self.head_t, self.cos_tab,
+                                   self.sin_tab, cfg.eps, D ** -0.5, cfg.codebook_size, B, dev)
+        hb = self.half
+        self.backbone_hidden_buf = torch.zeros(B, AE, dtype=torch.bfloat16, device=dev)
+        self.first_cb_token_buf = torch.zeros(B, dtype=torch.long, device=dev)
+        self.output_tokens = torch.zeros(B, cfg.n_decode, dtype=torch.long, device=dev)
+        self.tok_buf = torch.zeros(B, dtype=torch.long, device=dev)
+        self.temperature = torch.full((hb,), 0.9, dtype=torch.float32, device=dev)
+        self.top_k = torch.full((hb,), 50, dtype=torch.long, device=dev)
+        self.top_p = torch.full((hb,), 1.0, dtype=torch.float32, device=dev)
+        self.do_sample = torch.ones(hb, dtype=torch.long, device=dev)
+        self.guidance_scale = torch.full((hb,), 4.0, dtype=torch.float32, device=dev)
+        self.q = torch.ones(cfg.n_decode, hb, cfg.vocab, dtype=torch.float32, device=dev)
+
+    def frame(self, dbg=None, forced=None):
+        self.desc.frame(self.first_cb_token_buf, self.backbone_hidden_buf, self.tok_buf, self.output_tokens,
+                        self.temperature, self.top_k, self.top_p, self.do_sample, self.guidance_scale, self.q, dbg,
+                        forced)
+
+
 def backbone_step_bytes(cfg: BackboneConfig, batch, kv_len, include_lm_head=True):
     """Algorithmic HBM bytes of one decode step: every weight once, the valid KV once, the fp32 lm_head once."""
     w = cfg.layers * cfg.weight_bytes_per_layer()
@@ -182,4 +248,5 @@ def launches_per_backbone_step(cfg: BackboneConfig):
     return 2 + 5 * cfg.layers
 
 
-__all__ = ['BackboneConfig', 'SyntheticBackboneGraph', 'backbone_step_bytes', 'rope_table', 'kernels']
+__all__ = ['BackboneConfig', 'SyntheticBackboneGraph', 'DepthConfig', 'SyntheticDepth', 'backbone_step_bytes',
+           'rope_table', 'kernels']

@@ -139,6 +139,39 @@ int flashb_bb_step(const fb_bb_config* cfg, const void* layers_dev, void* scratc
                    int64_t* position_ids, int64_t* cache_pos, void* mask, int mask_is_bf16, int64_t m_sb,
                    const float* gs, int advance, void* hidden_out, float* logits, float* cfg_out, void* stream);
 
+/* ---------------------------------------------------------------------------------------------- depth frame
+ * Replaces the reference's depth frame megakernel dd2_init / dd2_frame (flash/csrc/depth_frame.cu:758-853, 923-934),
+ * itself the kernel form of the official DepthDecoderGraph._full_loop (UP/models/cudagraph/depth_decoder_graph.py:
+ * 558-654): ONE cooperative launch decodes all n_decode codebooks of a frame for `batch` rows (1, or CFG pairs
+ * cond[0..half) | uncond[half..2 half)), sampling each codebook on the device (CFG u + gs (c - u), ids >= codebook_size
+ * masked, / temperature, top-k (0 -> min(1024, vocab)), top-p, softmax, token = argmax(p / q)).
+ * Layer descriptors (fb_dd_layer[layers]) in device memory; `scratch`: flashb_dd_scratch_bytes() bytes, 256-byte
+ * aligned, zeroed once (and after a reported device error).  first_cb [batch] int64; bh [batch, embed_dim] bf16;
+ * tokbuf [batch] int64 (receives the last token fed forward); outtok [batch, n_decode] int64 (sampled tokens);
+ * temp/topp/gs [half] fp32, topk/dosample [half] int64; q [n_decode, half, vocab] fp32 Exp(1) draws;
+ * dbg (optional) [n_decode, batch, vocab] fp32 logits; forced (optional) [n_decode, batch] int64 tokens fed to the
+ * next codebook instead of the sampled ones (teacher forcing, for verification). */
+typedef struct {
+  const void *ln1, *wq, *wk, *wv, *wo, *ln2, *wg, *wu, *wd; /* bf16 */
+} fb_dd_layer;
+typedef struct {
+  int layers, batch, hidden, embed_dim, heads, kv_heads, head_dim, ffn;
+  int vocab, codebook_size, n_decode;
+  float eps, scaling;
+  const void* embed;   /* [(n_decode + 1) * vocab, embed_dim] bf16 */
+  const void* proj;    /* [hidden, embed_dim] bf16 (inputs_embeds_projector) */
+  const void* normf;   /* [hidden] bf16 */
+  const void* head_t;  /* [n_decode, vocab, hidden] bf16 (codebook heads, transposed) */
+  const void* cos_tab; /* [n_decode + 2, 128] bf16 */
+  const void* sin_tab;
+} fb_dd_config;
+int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg);
+int64_t flashb_dd_layer_bytes(void);
+int flashb_dd_frame(const fb_dd_config* cfg, const void* layers_dev, void* scratch, const int64_t* first_cb,
+                    const void* bh, int64_t* tokbuf, int64_t* outtok, const float* temp, const int64_t* topk,
+                    const float* topp, const int64_t* dosample, const float* gs, const float* q, float* dbg,
+                    const int64_t* forced, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,172 @@
+"""GPU parity of the depth-decoder frame kernel (``flashb_dd_frame``) against the oracle.
+
+* teacher-forced logits of every codebook step vs ``oracle.depth.depth_frame`` (bf16 bar, argmax agreement);
+* the sampled tokens bit-exact: the C sampler oracle run on the kernel's own logits (debug tap) must pick exactly the
+  tokens the kernel wrote, for sampling, greedy, top-p and codebook-masked configurations;
+* a free-running frame equals the teacher-forced oracle driven by the kernel's own tokens;
+* run-to-run determinism and CUDA-graph replay.
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import assert_close, np32
+from oracle import depth as odepth
+from oracle import sampler as osmp
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(small=True, B=2, seed=3, **kw):
+    from flashb.engine import DepthConfig, SyntheticDepth
+    if small:
+        cfg = DepthConfig(hidden=256, embed_dim=384, layers=2, heads=2, kv_heads=1, ffn=512, vocab=64,
+                          codebook_size=60, n_decode=6)
+    else:
+        cfg = DepthConfig()
+    for k, v in kw.items():
+        setattr(cfg, k, v)
+    m = SyntheticDepth(cfg, batch=B, seed=seed)
+    g = torch.Generator(device='cpu').manual_seed(seed + 10)
+    m.backbone_hidden_buf.copy_(torch.randn(B, cfg.embed_dim, generator=g).to(torch.bfloat16))
+    m.first_cb_token_buf.copy_(torch.randint(0, cfg.codebook_size, (B,), generator=g))
+    m.q.copy_(torch.empty(m.q.shape).exponential_(1, generator=g))
+    return m
+
+
+def _weights(m):
+    c = m.cfg
+    layers = [{k: np32(v) for k, v in L.items()} for L in m.layers]
+    head32 = m.head_t.float().permute(0, 2, 1).contiguous().cpu().numpy()
+    return odepth.DepthWeights(layers, np32(m.embed), np32(m.proj), np32(m.normf), head32, c.vocab, c.codebook_size,
+                               c.n_decode, c.eps, c.theta, c.heads, c.kv_heads)
+
+
+def _params(m):
+    return (m.temperature.cpu().numpy(), m.top_k.cpu().numpy(), m.top_p.cpu().numpy(), m.do_sample.cpu().numpy(),
+            m.guidance_scale.cpu().numpy())
+
+
+def _run(m, forced=None):
+    c = m.cfg
+    dbg = torch.zeros(c.n_decode, m.batch, c.vocab, dtype=torch.float32, device='cuda')
+    f = None if forced is None else torch.as_tensor(forced, dtype=torch.long, device='cuda').contiguous()
+    m.frame(dbg=dbg, forced=f)
+    torch.cuda.synchronize()
+    return m.output_tokens.cpu().numpy().copy(), dbg.cpu().numpy(), m.tok_buf.cpu().numpy().copy()
+
+
+def _check_sampler(m, logits, outtok):
+    """Every step's kernel token == the C sampler oracle on the kernel's own logits of that step."""
+    c = m.cfg
+    temp, topk, topp, ds, gs = _params(m)
+    q = m.q.cpu().numpy()
+    half = m.half
+    for s in range(c.n_decode):
+        for h in range(half):
+            lu = logits[s, h + half] if m.batch >= 2 else None
+            t, _ = osmp.sample_row(logits[s, h], lu, c.codebook_size, gs[h], temp[h], topk[h], topp[h], ds[h],
+                                   q[s, h])
+            t = min(max(int(t), 0), c.vocab - 1)
+            assert outtok[h, s] == t, f'step {s} row {h}: kernel {outtok[h, s]} oracle {t}'
+            if m.batch >= 2:
+                assert outtok[h + half, s] == t
+
+
+SAMPLING = {
+    'sample': dict(temp=0.9, topk=50, topp=1.0, ds=1, gs=4.0),
+    'greedy': dict(temp=1.0, topk=0, topp=1.0, ds=0, gs=3.0),
+    'top_p': dict(temp=1.3, topk=0, topp=0.8, ds=1, gs=2.0),
+    'top_k1': dict(temp=0.7, topk=1, topp=0.9, ds=1, gs=1.0),
+}
+
+
+def _set(m, p):
+    m.temperature.fill_(p['temp'])
+    m.top_k.fill_(p['topk'])
+    m.top_p.fill_(p['topp'])
+    m.do_sample.fill_(p['ds'])
+    m.guidance_scale.fill_(p['gs'])
+
+
+@pytest.mark.parametrize('B', [1, 2, 4])
+def test_depth_forced_logits_match_oracle(B):
+    m = _model(B=B)
+    c = m.cfg
+    forced = np.random.default_rng(B).integers(0, c.vocab, (c.n_decode, B))
+    outtok, logits, _ = _run(m, forced)
+    W = _weights(m)
+    temp, topk, topp, ds, gs = _params(m)
+    tok_ref, lg_ref, _ = odepth.depth_frame(W, np32(m.backbone_hidden_buf), m.first_cb_token_buf.cpu().numpy(),
+                                            m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
+    for s in range(c.n_decode):
+        assert_close(logits[s], lg_ref[s], what=f'step {s} logits')
+    assert np.mean(np.argmax(logits, -1) == np.argmax(lg_ref, -1)) >= 0.999
+    np.testing.assert_array_equal(m.tok_buf.cpu().numpy(), np.clip(forced[-1], 0, c.vocab - 1))
+    _check_sampler(m, logits, outtok)
+
+
+@pytest.mark.parametrize('mode', sorted(SAMPLING))
+def test_depth_sampler_bit_exact(mode):
+    m = _model(B=2, seed=7)
+    _set(m, SAMPLING[mode])
+    outtok, logits, _ = _run(m)
+    _check_sampler(m, logits, outtok)
+
+
+def test_depth_free_running_equals_forced_oracle():
+    """Without forcing, the kernel feeds its own tokens forward: the oracle teacher-forced by those tokens reproduces
+    every step's logits."""
+    m = _model(B=2, seed=11)
+    c = m.cfg
+    outtok, logits, tok = _run(m)
+    W = _weights(m)
+    temp, topk, topp, ds, gs = _params(m)
+    _, lg_ref, _ = odepth.depth_frame(W, np32(m.backbone_hidden_buf), m.first_cb_token_buf.cpu().numpy(),
+                                      m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=outtok.T.copy())
+    for s in range(c.n_decode):
+        assert_close(logits[s], lg_ref[s], what=f'step {s} logits')
+    np.testing.assert_array_equal(tok, outtok[:, -1])
+
+
+def test_depth_full_size_forced_and_sampler():
+    """The synthetic full-size depth decoder (4 layers, hidden 1024, 16 codebooks of 2048)."""
+    m = _model(small=False, B=2, seed=5)
+    c = m.cfg
+    forced = np.random.default_rng(5).integers(0, c.vocab, (c.n_decode, 2))
+    outtok, logits, _ = _run(m, forced)
+    W = _weights(m)
+    temp, topk, topp, ds, gs = _params(m)
+    _, lg_ref, _ = odepth.depth_frame(W, np32(m.backbone_hidden_buf), m.first_cb_token_buf.cpu().numpy(),
+                                      m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
+    for s in range(c.n_decode):
+        assert_close(logits[s], lg_ref[s], what=f'step {s} logits')
+    assert np.mean(np.argmax(logits, -1) == np.argmax(lg_ref, -1)) >= 0.999
+    _check_sampler(m, logits, outtok)
+
+
+def test_depth_determinism_and_graph_replay():
+    m = _model(small=False, B=2, seed=6)
+    m.frame()
+    torch.cuda.synchronize()
+    first = m.output_tokens.clone()
+    m.frame()
+    torch.cuda.synchronize()
+    assert torch.equal(first, m.output_tokens)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            m.frame()
+    torch.cuda.current_stream().wait_stream(s)
+    m.output_tokens.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(first, m.output_tokens)
+    g = torch.Generator(device='cpu').manual_seed(99)
+    m.q.copy_(torch.empty(m.q.shape).exponential_(1, generator=g))
+    graph.replay()
+    torch.cuda.synchronize()
+    _, logits, _ = _run(m)
+    _check_sampler(m, logits, m.output_tokens.cpu().numpy())
