@@ -1,0 +1,372 @@
+#!/usr/bin/env python
+"""Streaming-decode throughput of the flashb hot path on 1..8 B200s (one replica per GPU, no collective).
+
+Workload (BASELINE config 5 with configs 3 and 4): 64 independent streams, each after a 512-token prompt (random KV,
+the prefill stand-in), spread round-robin over the ranks.  A STEP is one frame of every stream on this rank:
+
+    frame = next backbone ids from the previous frame -> 28-layer backbone decode step (B = 2 CFG rows, KV length
+            512 + t, hidden 2048, 16 q / 4 kv heads, FFN 6144, fp32 lm_head + CFG) -> codebook-0 token (greedy
+            backbone sampler) -> depth frame (4 layers, hidden 1024, 16 codebooks of 2048, CFG scale 4, top-k 50,
+            T 0.9, sampled on the device)
+
+Outputs one JSON line (rank 0): ``value`` = frames/s of the whole job with every input resident in HBM (max over
+ranks of the device time), ``e2e`` = the same through the engine API with the per-frame Exp(1) draws copied from
+pinned host memory and the frame's tokens read back to the host every frame (as the reference's loop reads its
+token), ``roofline`` for the dominant kernel (the depth frame kernel) and ``roofline_backbone`` for the backbone
+step's attention + GEMV kernels, ``cpu_baseline`` = the CPU oracle port of the same frame on this host's cores.
+
+``--impl reference`` times that CPU port alone (rank 0; other ranks exit 0), one frame per step.
+``--case depth`` / ``--case backbone`` time one part alone (profiling entry points; same JSON shape, no baselines).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [HERE, os.path.join(HERE, 'breeze-tts-2-flash_b200')]
+
+N_STREAMS = 64
+PROMPT = 512
+PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0)
+# dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch (ncu, small-case capture of the same
+# full-size depth model; see profiles/dd_frame_kernel_depth_frame.md).  None until captured.
+DD_TRAFFIC_BYTES = None
+
+
+def args_():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=30)
+    p.add_argument('--warmup', type=int, default=3)
+    p.add_argument('--impl', default='flashb', choices=['flashb', 'reference'])
+    p.add_argument('--streams', type=int, default=N_STREAMS, help='streams over the whole job')
+    p.add_argument('--prompt', type=int, default=PROMPT)
+    p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone'])
+    p.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample length')
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--no-e2e', action='store_true')
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(HERE, 'MEASURED_PEAKS.json')) as f:
+            d = json.load(f)
+        return dict(hbm_gbs=float(d['hbm_gbs']), bf16_tflops=float(d['bf16_tflops']), source='measured')
+    except Exception:
+        return dict(PEAKS_FALLBACK, source='fallback')
+
+
+# ------------------------------------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_ids):
+        self.proc, self.path = None, None
+        try:
+            import tempfile
+            fd, self.path = tempfile.mkstemp(suffix='.csv')
+            os.close(fd)
+            self.out = open(self.path, 'w')
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', ','.join(str(i) for i in gpu_ids),
+                                          f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-lms', '200'], stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                c = [x.strip() for x in line.split(',')]
+                if len(c) >= 9:
+                    rows.append(c)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        rows = rows[1:] or rows          # the first sample may predate the load
+        sm = sorted(float(r[1]) for r in rows if r[1].replace('.', '').isdigit())
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == 'active'})
+        return dict(sm_mhz=sm[len(sm) // 2] if sm else None,
+                    sm_max_mhz=float(rows[0][2]) if rows[0][2].replace('.', '').isdigit() else None,
+                    reasons=reasons, samples=len(rows))
+
+
+# ------------------------------------------------------------------------------------------------ CPU port
+def cpu_frames(seconds, max_frames=None, warmup=1, prompt=PROMPT, seed=0):
+    """The oracle port of one frame (oracle/frame.py) on this host: returns (frames/s, frames timed, threads)."""
+    import numpy as np
+    from oracle import frame as ofr
+    rng = np.random.default_rng(seed)
+    BW = ofr.synthetic_backbone(rng, 28, 2048, 16, 4, 6144, 2049, 17)
+    DW = ofr.synthetic_depth(rng, 4, 1024, 2048, 8, 2, 4096, 2048, 2048, 16)
+    n_total = warmup + (max_frames if max_frames else 10 ** 6)
+    st = ofr.FrameStream(BW, 16, prompt, prompt + min(n_total, 4096) + 2, rng, 2048)
+    q = rng.exponential(size=(16, 1, 2048)).astype(np.float32)
+    params = (np.array([0.9], np.float32), np.array([50]), np.array([1.0], np.float32), np.array([1]),
+              np.array([4.0], np.float32))
+    for _ in range(warmup):
+        ofr.frame(BW, DW, st, 2048, 4.0, params, q)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        ofr.frame(BW, DW, st, 2048, 4.0, params, q)
+        n += 1
+        el = time.perf_counter() - t0
+        if (max_frames and n >= max_frames) or (not max_frames and el >= seconds and n >= 2):
+            break
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get('num_threads', 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count()
+    return n / el, n, el, threads
+
+
+def run_reference(a):
+    """--impl reference: the CPU oracle port of the frame, one frame per step (rank 0 only)."""
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import frame as ofr
+    rng = np.random.default_rng(0)
+    BW = ofr.synthetic_backbone(rng, 28, 2048, 16, 4, 6144, 2049, 17)
+    DW = ofr.synthetic_depth(rng, 4, 1024, 2048, 8, 2, 4096, 2048, 2048, 16)
+    st = ofr.FrameStream(BW, 16, a.prompt, a.prompt + a.warmup + a.steps + 2, rng, 2048)
+    q = rng.exponential(size=(16, 1, 2048)).astype(np.float32)
+    params = (np.array([0.9], np.float32), np.array([50]), np.array([1.0], np.float32), np.array([1]),
+              np.array([4.0], np.float32))
+    for _ in range(a.warmup):
+        ofr.frame(BW, DW, st, 2048, 4.0, params, q)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        ofr.frame(BW, DW, st, 2048, 4.0, params, q)
+    el = time.perf_counter() - t0
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get('num_threads', 1) for i in threadpool_info()] or [1])
+    except Exception:
+        threads = os.cpu_count()
+    v = a.steps / el
+    sample = (f'{a.steps} frames of one stream (backbone step at KV {a.prompt}+t + 16-codebook depth frame), '
+              f'numpy oracle port, {threads} BLAS threads')
+    print(json.dumps(dict(
+        impl='reference', metric='frames/s', value=round(v, 4), unit='frames/s', n_gpus=a.gpus, steps=a.steps,
+        warmup=a.warmup, ms_per_step=round(el / a.steps * 1e3, 3), higher_is_better=True, scaling='strong',
+        vs_baseline=None, dtype='bf16', data='synthetic',
+        config=dict(workload='streaming frame: 28-layer backbone decode step + 16-codebook depth frame (CPU port)',
+                    prompt_len=a.prompt, streams=1),
+        cpu_baseline=dict(value=round(v, 4), unit='frames/s', cores=threads, kind='port', sample=sample),
+        e2e=dict(value=round(v, 4), unit='frames/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ GPU
+def main():
+    a = args_()
+    if a.impl == 'reference':
+        run_reference(a)
+        return
+    import torch
+    import torch.distributed as dist
+    rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from flashb.engine import BackboneConfig, DepthConfig, FrameEngine, backbone_step_bytes
+    bcfg = BackboneConfig(codebooks=17)
+    dcfg = DepthConfig()
+    my_streams = len(range(rank, a.streams, world))
+    total_steps = a.warmup + a.steps
+    n_runs = 1 if a.no_e2e else 2
+    eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + 1, device=dev, seed=0)
+    eng.capture()
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def maxred(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sumred(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    case = a.case
+    S = my_streams
+
+    def one_step(ev):
+        for i in range(S):
+            st = eng.streams[i]
+            if case != 'depth':
+                if ev is not None:
+                    ev.append(torch.cuda.Event(enable_timing=True))
+                    ev[-1].record(stream)
+                st.graph.replay()
+            if case != 'backbone':
+                if ev is not None:
+                    ev.append(torch.cuda.Event(enable_timing=True))
+                    ev[-1].record(stream)
+                eng.depth_part(i)
+        if ev is not None:
+            ev.append(torch.cuda.Event(enable_timing=True))
+            ev[-1].record(stream)
+
+    # ---- device-resident run
+    for _ in range(a.warmup):
+        one_step(None)
+    kv0 = int(eng.streams[0].bb.cache_position.item()) + 1
+    gpu_ids = [int(x) for x in os.environ['CUDA_VISIBLE_DEVICES'].split(',')] \
+        if os.environ.get('CUDA_VISIBLE_DEVICES', '').replace(',', '').isdigit() else list(range(world))
+    clocks = Clocks(gpu_ids[:world]) if rank == 0 else None
+    evs = []
+    barrier()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(a.steps):
+        one_step(evs)
+    t_end.record(stream)
+    barrier()
+    clk = clocks.stop() if clocks else None
+    ms = t_start.elapsed_time(t_end)
+    ms_max = maxred(ms)
+    frames = sumred(S * a.steps)
+    value = frames / (ms_max / 1e3)
+    # per-part durations from the events (frame layout: [bb] [dd] per stream, then one closing event)
+    bb_ms, dd_ms = [], []
+    k = 0
+    per = (1 if case != 'depth' else 0) + (1 if case != 'backbone' else 0)
+    for _ in range(a.steps):
+        for i in range(S):
+            marks = evs[k:k + per + 1]
+            j = 0
+            if case != 'depth':
+                bb_ms.append(marks[j].elapsed_time(marks[j + 1]))
+                j += 1
+            if case != 'backbone':
+                dd_ms.append(marks[j].elapsed_time(marks[j + 1]))
+            k += per
+        k += 1
+    kv1 = int(eng.streams[0].bb.cache_position.item()) + 1
+    pk = peaks()
+    dd_bytes = dcfg.n_decode * dcfg.step_weight_bytes()
+    bb_bytes = backbone_step_bytes(bcfg, 2, (kv0 + kv1) // 2)
+    roof = None
+    if dd_ms:
+        dd_avg = sum(dd_ms) / len(dd_ms)
+        ach = dd_bytes / (dd_avg / 1e3) / 1e9
+        roof = dict(kernel='dd_frame_kernel', bound='hbm', achieved=round(ach, 1), peak=pk['hbm_gbs'], unit='GB/s',
+                    frac=round(ach / pk['hbm_gbs'], 4), traffic=DD_TRAFFIC_BYTES,
+                    algorithmic_bytes=dd_bytes, launch_ms=round(dd_avg, 4), peak_source=pk['source'])
+    roof_bb = None
+    if bb_ms:
+        bb_avg = sum(bb_ms) / len(bb_ms)
+        ach = bb_bytes / (bb_avg / 1e3) / 1e9
+        roof_bb = dict(kernels='backbone step (GQA decode attention + fused GEMVs + ends, 146 launches as a graph)',
+                       bound='hbm', achieved=round(ach, 1), peak=pk['hbm_gbs'], unit='GB/s',
+                       frac=round(ach / pk['hbm_gbs'], 4), algorithmic_bytes=bb_bytes, step_ms=round(bb_avg, 4),
+                       peak_source=pk['source'])
+
+    # ---- end-to-end run through the engine API with host buffers
+    e2e = None
+    if not a.no_e2e and case == 'frame':
+        R = 8
+        qh = torch.empty(R, dcfg.n_decode, 1, dcfg.vocab).exponential_(1, generator=torch.Generator().manual_seed(5))
+        qh = qh.pin_memory()
+        toks_h = torch.zeros(S, 2 + 2 * dcfg.n_decode, dtype=torch.long).pin_memory()
+        done = torch.cuda.Event()
+        h2d = S * qh[0].numel() * 4
+        d2h = S * toks_h[0].numel() * 8
+
+        def e2e_step(t):
+            for i in range(S):
+                st = eng.streams[i]
+                st.q.copy_(qh[(i + t) % R], non_blocking=True)
+                eng.frame(i)
+                toks_h[i, :2].copy_(st.first_cb, non_blocking=True)
+                toks_h[i, 2:].copy_(st.outtok.view(-1), non_blocking=True)
+                done.record(stream)
+                done.synchronize()             # the frame's tokens are on the host before the next frame
+
+        for t in range(a.warmup):
+            e2e_step(t)
+        barrier()
+        w0 = torch.cuda.Event(enable_timing=True)
+        w1 = torch.cuda.Event(enable_timing=True)
+        w0.record(stream)
+        for t in range(a.steps):
+            e2e_step(t)
+        w1.record(stream)
+        barrier()
+        e_ms = maxred(w0.elapsed_time(w1))
+        e2e = dict(value=round(frames / (e_ms / 1e3), 3), unit='frames/s', h2d_bytes_per_step=h2d,
+                   d2h_bytes_per_step=d2h, ms_per_step=round(e_ms / a.steps, 3))
+
+    # ---- CPU baseline (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline and case == 'frame':
+        v, n, el, threads = cpu_frames(a.cpu_seconds, prompt=a.prompt)
+        cpu = dict(value=round(v, 4), unit='frames/s', cores=threads, kind='port',
+                   sample=f'{n} frames of one stream ({el:.1f} s after 1 warm-up frame): numpy/C oracle port of '
+                          f'backbone step (KV {a.prompt}+t) + 16-codebook depth frame, {threads} BLAS threads')
+
+    launches = eng.launches_per_frame() if case == 'frame' else (
+        1 if case == 'depth' else eng.launches_per_frame() - 1)
+    if rank == 0:
+        wl = {'frame': 'streaming frames: 28-layer backbone decode step (B=2 CFG, KV 512+t) + greedy codebook-0 + '
+                       '16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9)',
+              'depth': 'depth frame only (4 layers, hidden 1024, 16 codebooks of 2048, CFG + top-k 50 sampling)',
+              'backbone': 'backbone decode step only (28 layers, hidden 2048, B=2, KV 512+t) + frame link'}[case]
+        line = dict(
+            metric='frames/s', value=round(value, 3), unit='frames/s', n_gpus=world, steps=a.steps,
+            warmup=a.warmup, ms_per_step=round(ms_max / a.steps, 3), higher_is_better=True, scaling='strong',
+            vs_baseline=None, dtype='bf16', data='synthetic (seeded random bf16 weights, random prompt KV)',
+            config=dict(workload=wl, streams=a.streams, streams_per_gpu=my_streams, step='one frame of every stream '
+                        'on the rank', prompt_len=a.prompt, kv_len=[kv0, kv1], parallelism=f'replica x{world}',
+                        l2='inputs larger than L2: 2.70 GB backbone weights per step, 130 MB depth weights per '
+                           'codebook step; no flush', cb0='greedy (backbone sampler do_sample=False)',
+                        prefill='not timed (random prompt KV)'),
+            frames_per_s_per_gpu=round(value / world, 3), tokens_per_s=round(value * 17, 1),
+            roofline=roof, roofline_backbone=roof_bb, cpu_baseline=cpu, e2e=e2e,
+            gpu_launches=int(launches * frames), clocks=clk)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        for st in eng.streams:
+            st.graph = None
+        barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

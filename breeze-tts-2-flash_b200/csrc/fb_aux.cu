@@ -175,9 +175,94 @@ __global__ void step_advance_kernel(long long* cache_pos, long long* position_id
   }
 }
 
+// Greedy branch of the backbone sampler (sample_logits with do_sample=False is torch.argmax,
+// flash/sampling.py:56-97; UP/models/cudagraph/sampling.py): token = argmax(cfg[h, 0:n_valid]) with torch's
+// semantics (first maximal index; a NaN counts as the maximum), ids >= n_valid suppressed as the reference suppresses
+// the EOS / reserved ids with -inf.  Written to first_cb[h] and, for CFG pairs, first_cb[h + half].
+__global__ void __launch_bounds__(256) cb0_greedy_kernel(const float* __restrict__ cfg, long ld, int half, int n_valid,
+                                                         int B, long long* __restrict__ first_cb) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* row = cfg + (size_t)h * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  auto better = [](float v, int i, float w, int j) {
+    if (isnan(w)) return isnan(v) && i < j;
+    if (isnan(v)) return true;
+    return v > w || (v == w && i < j);
+  };
+  for (int i = tid; i < n_valid; i += blockDim.x) {
+    const float v = row[i];
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v = __shfl_xor_sync(FULL, bv, o);
+    const int i = __shfl_xor_sync(FULL, bi, o);
+    if (better(v, i, bv, bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (better(sv[w], si[w], bv, bi)) {
+        bv = sv[w];
+        bi = si[w];
+      }
+    if (bi == 0x7fffffff) bi = 0;
+    first_cb[h] = bi;
+    if (B >= 2) first_cb[h + half] = bi;
+  }
+}
+
+// Frame assembly of the streaming loop (flash/main_loop.py:268, 310-312: frame = [token, depth_tokens[0]], repeated
+// for both CFG rows): ids[b, 0] = first_cb[b]; ids[b, c] = depth_tok[b, c - 1] for c = 1 .. C - 1.
+__global__ void frame_ids_kernel(const long long* __restrict__ first_cb, const long long* __restrict__ depth_tok,
+                                 int n_decode, int B, int C, long long* __restrict__ ids) {
+  pdl_wait();
+  pdl_trigger();
+  for (int i = threadIdx.x; i < B * C; i += blockDim.x) {
+    const int b = i / C, c = i - b * C;
+    ids[i] = c == 0 ? first_cb[b] : depth_tok[(size_t)b * n_decode + c - 1];
+  }
+}
+
 }  // namespace fb
 
 using namespace fb;
+
+extern "C" int flashb_cb0_greedy(const float* cfg_logits, int64_t ld, int half, int n_valid, int B,
+                                 int64_t* first_cb, void* stream) {
+  FB_CHECK_ARG(cfg_logits && first_cb && half >= 1 && n_valid >= 1 && n_valid <= ld && (B == half || B == 2 * half),
+               "cb0_greedy: bad argument (half=%d n_valid=%d ld=%lld B=%d)", half, n_valid, (long long)ld, B);
+  long l = (long)ld;
+  long long* fc = (long long*)first_cb;
+  void* args[] = {(void*)&cfg_logits, (void*)&l, (void*)&half, (void*)&n_valid, (void*)&B, (void*)&fc};
+  return fbh::launch_pdl((const void*)cb0_greedy_kernel, dim3(half), dim3(256), 0, (cudaStream_t)stream, args, true);
+}
+
+extern "C" int flashb_frame_ids(const int64_t* first_cb, const int64_t* depth_tok, int n_decode, int B, int C,
+                                int64_t* ids, void* stream) {
+  FB_CHECK_ARG(first_cb && depth_tok && ids && B >= 1 && C >= 1 && C - 1 <= n_decode,
+               "frame_ids: bad argument (B=%d C=%d n_decode=%d)", B, C, n_decode);
+  const long long* fc = (const long long*)first_cb;
+  const long long* dt = (const long long*)depth_tok;
+  long long* io = (long long*)ids;
+  void* args[] = {(void*)&fc, (void*)&dt, (void*)&n_decode, (void*)&B, (void*)&C, (void*)&io};
+  return fbh::launch_pdl((const void*)frame_ids_kernel, dim3(1), dim3(128), 0, (cudaStream_t)stream, args, true);
+}
 
 extern "C" int flashb_step_advance(int64_t* cache_pos, int64_t* position_ids, int B, void* mask, int mask_is_bf16,
                                    int64_t m_sb, int S, void* stream) {

@@ -71,7 +71,10 @@ class _Cache:
 class SyntheticBackboneGraph:
     """A backbone decode graph with synthetic weights: B rows (B/2 CFG pairs), static KV cache of ``max_seq_len``."""
 
-    def __init__(self, cfg: BackboneConfig, batch_size=2, max_seq_len=2048, device='cuda', seed=2, gs=4.0):
+    def __init__(self, cfg: BackboneConfig, batch_size=2, max_seq_len=2048, device='cuda', seed=2, gs=4.0,
+                 weights_from=None):
+        """``weights_from``: another SyntheticBackboneGraph whose weights this one shares (a second stream of the same
+        replica: own KV cache and buffers, same weights)."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.batch_size = B = batch_size
@@ -82,6 +85,33 @@ class SyntheticBackboneGraph:
         dev = self.device
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
+        if weights_from is not None:
+            src = weights_from
+            if src.cfg != cfg or src.max_seq_len < S:
+                raise ValueError('weights_from: different config or shorter rotary table')
+            layers = src._bb_state['layers']
+            self._packs, self.norm_w, self.embed, self.lm_head32 = src._packs, src.norm_w, src.embed, src.lm_head32
+            cos_tab, sin_tab = src._bb_state['cos_tab'], src._bb_state['sin_tab']
+        else:
+            layers = self._make_weights(cfg, g, dev)
+            cos_tab, sin_tab = rope_table(cfg.theta, D, S + 1, dev)
+        self.static_cache = _Cache([_KV(torch.zeros(B, NKV, S, D, dtype=torch.bfloat16, device=dev),
+                                        torch.zeros(B, NKV, S, D, dtype=torch.bfloat16, device=dev))
+                                    for _ in range(cfg.layers)])
+        self.input_ids_buf = torch.zeros(B, 1, cfg.codebooks, dtype=torch.long, device=dev)
+        self.position_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        self.cache_position = torch.zeros(1, dtype=torch.long, device=dev)
+        self.attn_mask = torch.full((B, 1, 1, S), torch.finfo(torch.bfloat16).min, dtype=torch.bfloat16, device=dev)
+        self.hidden_buf = torch.zeros(B, 1, H, dtype=torch.bfloat16, device=dev)
+        self.logits_buf = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
+        self.cfg_logits_buf = torch.zeros(self.half, cfg.vocab, dtype=torch.float32, device=dev)
+        self.guidance_scale = torch.tensor([gs], dtype=torch.float32, device=dev)
+        self._bb_state = bb.make_state(B, layers, self.norm_w, cfg.eps, self.embed, cfg.vocab, self.lm_head32,
+                                       cos_tab, sin_tab, S, dev)
+        self._gen = g
+
+    def _make_weights(self, cfg, g, dev):
+        H, D, NH, NKV, F = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.ffn
         layers = []
         self._packs = []
         for _ in range(cfg.layers):
@@ -115,21 +145,7 @@ class SyntheticBackboneGraph:
         self.norm_w = _randn((H,), g, dev, 0.1, 1.0)
         self.embed = _randn((cfg.codebooks * cfg.vocab, H), g, dev, 1.0)
         self.lm_head32 = _randn((cfg.vocab, H), g, dev, 0.02).float()
-        cos_tab, sin_tab = rope_table(cfg.theta, D, S + 1, dev)
-        self.static_cache = _Cache([_KV(torch.zeros(B, NKV, S, D, dtype=torch.bfloat16, device=dev),
-                                        torch.zeros(B, NKV, S, D, dtype=torch.bfloat16, device=dev))
-                                    for _ in range(cfg.layers)])
-        self.input_ids_buf = torch.zeros(B, 1, cfg.codebooks, dtype=torch.long, device=dev)
-        self.position_ids = torch.zeros(B, 1, dtype=torch.long, device=dev)
-        self.cache_position = torch.zeros(1, dtype=torch.long, device=dev)
-        self.attn_mask = torch.full((B, 1, 1, S), torch.finfo(torch.bfloat16).min, dtype=torch.bfloat16, device=dev)
-        self.hidden_buf = torch.zeros(B, 1, H, dtype=torch.bfloat16, device=dev)
-        self.logits_buf = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
-        self.cfg_logits_buf = torch.zeros(self.half, cfg.vocab, dtype=torch.float32, device=dev)
-        self.guidance_scale = torch.tensor([gs], dtype=torch.float32, device=dev)
-        self._bb_state = bb.make_state(B, layers, self.norm_w, cfg.eps, self.embed, cfg.vocab, self.lm_head32,
-                                       cos_tab, sin_tab, S, dev)
-        self._gen = g
+        return layers
 
     # ------------------------------------------------------------------------------------------ state helpers
     def fill_kv(self, valid_len, seed=7, std=1.0):
@@ -236,6 +252,102 @@ class SyntheticDepth:
                         forced)
 
 
+class _StreamState:
+    __slots__ = ('bb', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph')
+
+
+class FrameEngine:
+    """One replica on one GPU for the streaming decode: a synthetic backbone and depth decoder whose weights are
+    shared by ``n_streams`` independent streams (own KV cache, positions and I/O buffers each).
+
+    ``frame(i)`` runs one frame of stream i on the current CUDA stream, the body of the reference's streaming loop
+    (``flash/main_loop.py:252-312``) without host synchronisation:
+
+        frame_ids    next backbone input = [cb0, depth tokens] of the previous frame            (1 launch)
+        backbone     step on those ids, position advanced on the device                         (2 + 1 + 5 x layers)
+        cb0_greedy   codebook-0 token = argmax of the CFG logits (greedy backbone sampler)      (1 launch)
+        depth frame  every depth codebook, CFG top-k sampled on the device                      (1 launch)
+
+    The first three are captured into one CUDA graph per stream (``capture()``); the depth frame is a single launch.
+    Each stream starts after a ``prompt_len``-token prompt whose KV cache is random (the prefill stand-in)."""
+
+    def __init__(self, bcfg: BackboneConfig, dcfg: DepthConfig, n_streams, prompt_len, max_frames, device='cuda',
+                 seed=0):
+        if bcfg.codebooks - 1 > dcfg.n_decode or dcfg.embed_dim != bcfg.hidden:
+            raise ValueError('backbone codebooks must be <= 1 + depth codebooks and depth embed_dim == backbone hidden')
+        self.bcfg, self.dcfg = bcfg, dcfg
+        self.device = dev = torch.device(device)
+        self.prompt_len = prompt_len
+        self.max_seq_len = S = prompt_len + max_frames + 2
+        self.n_valid = min(dcfg.codebook_size, bcfg.vocab)
+        self.depth = SyntheticDepth(dcfg, batch=2, device=dev, seed=seed + 3)
+        self.streams = []
+        first = None
+        g = torch.Generator(device='cpu').manual_seed(seed + 17)
+        for i in range(n_streams):
+            st = _StreamState()
+            st.bb = SyntheticBackboneGraph(bcfg, 2, S, dev, seed=seed + 2, weights_from=first)
+            first = first or st.bb
+            st.bb.fill_kv(prompt_len, seed=1000 + seed + i)
+            st.bb.set_position(prompt_len - 1)
+            st.first_cb = torch.randint(0, self.n_valid, (1,), generator=g).repeat(2).to(dev)
+            st.outtok = torch.randint(0, dcfg.codebook_size, (1, dcfg.n_decode), generator=g).repeat(2, 1).to(dev)
+            st.tokbuf = torch.zeros(2, dtype=torch.long, device=dev)
+            st.q = torch.empty(dcfg.n_decode, 1, dcfg.vocab).exponential_(1, generator=g).to(dev)
+            st.graph = None
+            self.streams.append(st)
+
+    # one frame, split into its backbone part (graph-capturable) and the depth launch
+    def backbone_part(self, i):
+        st = self.streams[i]
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        C = self.bcfg.codebooks
+        check(lib().flashb_frame_ids(st.first_cb.data_ptr(), st.outtok.data_ptr(), self.dcfg.n_decode, 2, C,
+                                     st.bb.input_ids_buf.data_ptr(), stream))
+        st.bb.decode_step(advance=True)
+        check(lib().flashb_cb0_greedy(st.bb.cfg_logits_buf.data_ptr(), st.bb.cfg_logits_buf.stride(0), 1,
+                                      self.n_valid, 2, st.first_cb.data_ptr(), stream))
+
+    def depth_part(self, i):
+        st, d = self.streams[i], self.depth
+        d.desc.frame(st.first_cb, st.bb.hidden_buf.view(2, -1), st.tokbuf, st.outtok, d.temperature, d.top_k,
+                     d.top_p, d.do_sample, d.guidance_scale, st.q)
+
+    def capture(self):
+        """One CUDA graph per stream for its backbone part.  Stream 0 first runs one eager frame (kernel attributes
+        are set on first use), then its position is put back."""
+        self.backbone_part(0)
+        self.depth_part(0)
+        torch.cuda.synchronize(self.device)
+        self.streams[0].bb.set_position(self.prompt_len - 1)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for i, st in enumerate(self.streams):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    self.backbone_part(i)
+                st.graph = graph
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+
+    def frame(self, i):
+        st = self.streams[i]
+        if st.graph is not None:
+            st.graph.replay()
+        else:
+            self.backbone_part(i)
+        self.depth_part(i)
+
+    def launches_per_frame(self):
+        return launches_per_backbone_step(self.bcfg) + 1 + 3
+
+    def frame_bytes(self):
+        """Algorithmic HBM bytes of one frame at the current mean KV length: backbone step + 16 depth steps."""
+        kv = int(self.streams[0].bb.cache_position.item()) + 1
+        return backbone_step_bytes(self.bcfg, 2, kv) + self.dcfg.n_decode * self.dcfg.step_weight_bytes()
+
+
 def backbone_step_bytes(cfg: BackboneConfig, batch, kv_len, include_lm_head=True):
     """Algorithmic HBM bytes of one decode step: every weight once, the valid KV once, the fp32 lm_head once."""
     w = cfg.layers * cfg.weight_bytes_per_layer()
@@ -248,5 +360,5 @@ def launches_per_backbone_step(cfg: BackboneConfig):
     return 2 + 5 * cfg.layers
 
 
-__all__ = ['BackboneConfig', 'SyntheticBackboneGraph', 'DepthConfig', 'SyntheticDepth', 'backbone_step_bytes',
-           'rope_table', 'kernels']
+__all__ = ['BackboneConfig', 'SyntheticBackboneGraph', 'DepthConfig', 'SyntheticDepth', 'FrameEngine',
+           'backbone_step_bytes', 'rope_table', 'kernels']

@@ -103,6 +103,19 @@ int flashb_lm_head_cfg(const void* x, int B, int H, const void* norm_w, float ep
 int flashb_step_advance(int64_t* cache_pos, int64_t* position_ids, int B, void* mask, int mask_is_bf16, int64_t m_sb,
                         int S, void* stream);
 
+/* Greedy backbone sampler: the do_sample=False branch of the reference's host-sync-free sample_logits
+ * (flash/sampling.py:56-97, bitwise the official UP/models/cudagraph/sampling.py), i.e. torch.argmax of the CFG logits,
+ * with every id >= n_valid suppressed (the reference's suppress_idx / EOS handling, flash/main_loop.py:98-108).
+ * cfg_logits [half, ld] fp32; the token goes to first_cb[h] and, when B == 2 * half, first_cb[h + half]. */
+int flashb_cb0_greedy(const float* cfg_logits, int64_t ld, int half, int n_valid, int B, int64_t* first_cb,
+                      void* stream);
+
+/* Frame assembly of the streaming loop (flash/main_loop.py:268 and :310-312): the backbone input of the next step is
+ * ids[b] = [first_cb[b], depth_tok[b, 0 .. C-2]] (ids [B, C] int64, depth_tok [B, n_decode] int64, C - 1 <= n_decode),
+ * built on the device instead of by torch.cat / repeat. */
+int flashb_frame_ids(const int64_t* first_cb, const int64_t* depth_tok, int n_decode, int B, int C, int64_t* ids,
+                     void* stream);
+
 /* ---------------------------------------------------------------------------------------------- whole backbone step
  * One cooperative launch per decode step (one CTA per SM) replaces the reference's per-step sequence of 28 x 5 kernels
  * plus eager ops (flash/backbone.py:106-138 fused_decode_step inside UP/models/cudagraph/backbone_graph.py:254-285

@@ -1,0 +1,132 @@
+"""GPU tests of the streaming-frame pieces: the greedy codebook-0 kernel (torch.argmax semantics), the frame-ids
+assembly, and ``FrameEngine`` (graph-captured frames) against the oracle's backbone step and the standalone depth
+frame."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import assert_close, np32
+from oracle import decode as dec
+from oracle import frame as ofr
+
+pytestmark = pytest.mark.gpu
+
+
+def _lib():
+    from flashb._native import lib
+    return lib()
+
+
+def _greedy(cfg, half, n_valid, B):
+    out = torch.full((B,), -1, dtype=torch.long, device='cuda')
+    from flashb._native import check
+    check(_lib().flashb_cb0_greedy(cfg.data_ptr(), cfg.stride(0), half, n_valid, B, out.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize('half,B', [(1, 2), (1, 1), (2, 4)])
+def test_cb0_greedy_matches_torch_argmax(half, B):
+    g = torch.Generator().manual_seed(half * 10 + B)
+    cfg = torch.randn(half, 2049, generator=g)
+    cfg[0, 2048] = 1e9                 # suppressed id (>= n_valid) must not win
+    cfg[0, 700] = cfg[0, 300] = 50.0   # tie -> lower index
+    if half > 1:
+        cfg[1, 1500] = float('nan')    # NaN counts as the maximum (torch.argmax)
+    got = _greedy(cfg.cuda(), half, 2048, B)
+    for h in range(half):
+        ref = int(torch.argmax(cfg[h, :2048]).item())
+        assert ref == ofr.greedy_cb0(cfg[h].numpy(), 2048)
+        assert got[h] == ref
+        if B == 2 * half:
+            assert got[h + half] == ref
+    assert got[0] == 300
+    if half > 1:
+        assert got[1] == 1500
+
+
+def test_frame_ids_assembly():
+    from flashb._native import check
+    B, C, n = 2, 17, 16
+    fc = torch.tensor([5, 9], dtype=torch.long, device='cuda')
+    dt = torch.arange(B * n, dtype=torch.long, device='cuda').view(B, n)
+    ids = torch.full((B, C), -1, dtype=torch.long, device='cuda')
+    check(_lib().flashb_frame_ids(fc.data_ptr(), dt.data_ptr(), n, B, C, ids.data_ptr(),
+                                  torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    ref = torch.cat([fc.view(B, 1), dt[:, :C - 1]], 1)
+    assert torch.equal(ids, ref)
+
+
+def _small_engine(streams=2, prompt=40, frames=4):
+    from flashb.engine import BackboneConfig, DepthConfig, FrameEngine
+    bcfg = BackboneConfig(hidden=512, layers=2, heads=8, kv_heads=2, ffn=1024, vocab=65, codebooks=7)
+    dcfg = DepthConfig(hidden=256, embed_dim=512, layers=2, heads=2, kv_heads=1, ffn=512, vocab=64,
+                       codebook_size=60, n_decode=6)
+    eng = FrameEngine(bcfg, dcfg, streams, prompt, frames, seed=4)
+    return eng
+
+
+def _oracle_backbone(bb):
+    st = bb._bb_state
+    layers = [dict(ln1=np32(L.ln1_w), wq=np32(L.wq), wk=np32(L.wk), wv=np32(L.wv), qn=np32(L.qn_w), kn=np32(L.kn_w),
+                   wo=np32(L.wo), ln2=np32(L.ln2_w), wg=np32(L.wg), wu=np32(L.wu), wd=np32(L.wd))
+              for L in st['layers']]
+    return dec.BackboneWeights(layers, np32(bb.norm_w), np32(bb.embed), bb.lm_head32.cpu().numpy(), bb.cfg.vocab,
+                               bb.cfg.eps, bb.cfg.theta)
+
+
+def test_frame_engine_matches_oracle_and_standalone_depth():
+    eng = _small_engine()
+    eng.capture()
+    W = _oracle_backbone(eng.streams[0].bb)
+    C = eng.bcfg.codebooks
+    for i, st in enumerate(eng.streams):
+        bb = st.bb
+        kcs = [np32(L.keys).copy() for L in bb.static_cache.layers]
+        vcs = [np32(L.values).copy() for L in bb.static_cache.layers]
+        mask = np32(bb.attn_mask).copy()
+        pos = int(bb.cache_position.item())
+        pids = bb.position_ids.view(-1).cpu().numpy().copy()
+        for f in range(3):
+            ids = np.concatenate([st.first_cb.cpu().numpy()[:, None], st.outtok.cpu().numpy()[:, :C - 1]], 1)
+            eng.frame(i)
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(bb.input_ids_buf.view(2, -1).cpu().numpy(), ids)
+            pos += 1
+            pids += 1
+            mask[..., pos] = 0.0
+            h, _, cfg = dec.backbone_step(W, ids, kcs, vcs, mask, pos, pids, float(bb.guidance_scale.item()))
+            assert int(bb.cache_position.item()) == pos
+            assert_close(np32(bb.hidden_buf).reshape(2, -1), h, what=f'stream {i} frame {f} hidden')
+            g_cfg = bb.cfg_logits_buf.cpu().numpy()
+            assert_close(g_cfg, cfg, what=f'stream {i} frame {f} cfg logits')
+            cb0 = ofr.greedy_cb0(g_cfg[0], eng.n_valid)
+            np.testing.assert_array_equal(st.first_cb.cpu().numpy(), [cb0, cb0])
+            # the engine's depth launch consumed this frame's hidden state and cb0: a standalone launch agrees
+            d = eng.depth
+            out = torch.zeros_like(st.outtok)
+            tb = torch.zeros_like(st.tokbuf)
+            d.desc.frame(st.first_cb, bb.hidden_buf.view(2, -1), tb, out, d.temperature, d.top_k, d.top_p,
+                         d.do_sample, d.guidance_scale, st.q)
+            torch.cuda.synchronize()
+            assert torch.equal(out, st.outtok)
+
+
+def test_frame_engine_graph_equals_eager():
+    ea = _small_engine(streams=1)
+    eb = _small_engine(streams=1)
+    eb.capture()
+    # capture() ran one eager frame on stream 0 and rewound its position: do the same on the eager engine
+    ea.backbone_part(0)
+    ea.depth_part(0)
+    torch.cuda.synchronize()
+    ea.streams[0].bb.set_position(ea.prompt_len - 1)
+    for _ in range(3):
+        ea.frame(0)
+        eb.frame(0)
+    torch.cuda.synchronize()
+    sa, sb = ea.streams[0], eb.streams[0]
+    assert torch.equal(sa.outtok, sb.outtok) and torch.equal(sa.first_cb, sb.first_cb)
+    assert torch.equal(sa.bb.cfg_logits_buf, sb.bb.cfg_logits_buf)
