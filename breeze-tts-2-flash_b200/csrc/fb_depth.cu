@@ -4,7 +4,7 @@
 // UP = third_party/breeze-tts) with the eager rounding points of BreezeDecoderLayer (UP/models/breeze.py:378-425), and
 // replaces the reference's depth megakernel (flash/csrc/depth_frame.cu:656-853) with a B200 design: one CTA per SM,
 // a producer warp streaming every weight slice of the frame (projector, 4 x {q|k|v, o, gate|up, down}, codebook
-// head) through the 64 KB-stage ring (fb_stream.cuh, tensor-core GEMV), consumer warps running the tasks between
+// head) through the stage ring (fb_stream.cuh, tensor-core GEMV), consumer warps running the tasks between
 // bounded grid barriers (fb_persist.cuh):
 //
 //   per codebook step s (T = 2 tokens at s = 0, else 1; M = B * T rows):
@@ -16,10 +16,19 @@
 //                S3 RMSNorm(bf16(x + o)) + gate|up GEMV + SiLU*up
 //                S4 down GEMV + residual
 //     S5  final RMSNorm + codebook-head GEMV -> fp32 logits
-//     sampler  CTA h samples half-row h: CFG, codec-id mask, temperature, top-k, top-p, softmax, argmax(p / q),
-//              with its own exp routine and fixed summation order, bit-identical to the C oracle (oracle/sampler.c)
+//     sampler  every CTA samples every half-row (redundantly, so no barrier follows): CFG, codec-id mask,
+//              temperature, top-k (radix select of the k-th largest key, then a sort of the k survivors), top-p,
+//              softmax, argmax(p / q), with its own exp routine and fixed summation order, bit-identical to the C
+//              oracle (oracle/sampler.c); CTA 0 writes the tokens out, every CTA feeds its copy to the next step
+//
+// The depth matrices are 1024 columns wide, so this unit streams 16 x 1024 stages (32 KB): a ring of five fits
+// beside the activations and the producer runs a whole task ahead.  Global -> shared staging of activations
+// (cross-CTA data) uses cp.async.cg with every chunk in flight at once: one L2 round trip per phase.  The large
+// phases are not inlined so that a step's code stays resident in the instruction cache.
 //
 // Scratch (residual stream, q, o, act, logits, KV cache, barrier) is one caller-owned buffer, zeroed once.
+#define FB_ST_KC 1024
+#define FB_PK_MAX_STAGES 8
 #include "fb_persist.cuh"
 
 namespace fb {
@@ -51,9 +60,20 @@ struct DDArgs {
   bf16 *xres, *qb, *ob, *act, *kc, *vc;
   float* logits;
   GridBar* bar;
-  int nstages, xs_bytes;
+  int nstages, xs_bytes, att_off, keep_off;
   unsigned* err;
+  unsigned long long* trace;
 };
+
+// Optional trace: thread 0 of each CTA stamps %globaltimer at the end of every task and barrier of step s
+// (row layout [grid][n_decode][11 + 9 * layers]: start, E, barrier, 9 per layer, head, barrier, 6 sampler phases).
+#define DD_TRACE_SLOTS(L) (11 + 9 * (L))
+#define DD_STAMP(s, idx)                                                                                   \
+  do {                                                                                                     \
+    if (a.trace && threadIdx.x == 0)                                                                       \
+      a.trace[((size_t)blockIdx.x * a.NCB + (s)) * DD_TRACE_SLOTS(a.L) + (idx)] =                          \
+          (unsigned long long)globaltimer();                                                               \
+  } while (0)
 
 // ------------------------------------------------------------------------------------------------ sampler math
 // exp(x) by Cody-Waite reduction and a degree-7 Taylor polynomial (Horner, fused multiply-adds); the exact operation
@@ -95,38 +115,68 @@ __device__ __forceinline__ float lane_scan(float v) {
   return v;
 }
 
-// Sampler for half-row h (all 256 consumer threads of the CTA).  `arr` is shared scratch for DD_MAXV 64-bit keys.
-__device__ void dd_sample(const DDArgs& a, int step, int h, unsigned long long* arr, int* s_int) {
+// Shared-memory layout of the sampler inside the activation buffer: V composite keys, up to 1024 sorted survivors,
+// two 256-bin histograms, the two logit rows.
+__host__ __device__ constexpr size_t dd_sampler_bytes(int V) {
+  return (size_t)V * 8 + 1024 * 8 + 2 * 256 * 4 + 2 * (size_t)V * 4;
+}
+
+// Sampler for half-row h (all 256 consumer threads of the CTA); returns the sampled token (before forcing).
+// Composite key = (order-preserving bits of cfg / temperature) << 12 | (4095 - index): descending key order is the
+// official order (value descending, ties by lower index).  The kk largest keys are found by radix selection on 8-bit
+// digits (histograms in shared memory, early exit once the boundary bin is taken whole), gathered, and sorted
+// descending by a bitonic network (one warp up to 64 survivors).  Warp 0 then runs the canonical sums of
+// oracle/sampler.c on the sorted survivors.
+__device__ __noinline__ int dd_sample(const DDArgs& a, int step, int h, unsigned char* buf, int* s_int) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int half = a.B >= 2 ? a.B / 2 : 1;
   const int V = a.V;
-  const float* lc = a.logits + (size_t)h * V;
-  const float* lu = a.B >= 2 ? a.logits + (size_t)(h + half) * V : nullptr;
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(buf);
+  unsigned long long* top = keys + V;
+  unsigned* hist = reinterpret_cast<unsigned*>(top + 1024);
+  float* lg = reinterpret_cast<float*>(hist + 512);
+  {
+    // both logit rows to shared memory in one round trip (cp.async.cg: written by other CTAs, L2 only)
+    const float* g0 = a.logits + (size_t)h * V;
+    const float* g1 = a.B >= 2 ? a.logits + (size_t)(h + half) * V : nullptr;
+    if ((V & 3) == 0) {
+      const int nch = V >> 2;
+      for (int i = tid; i < (g1 ? 2 : 1) * nch; i += PK_CONSUMERS)
+        cp_async16(lg + (size_t)i * 4, (i < nch ? g0 + (size_t)i * 4 : g1 + (size_t)(i - nch) * 4));
+      cp_async_commit();
+      cp_async_wait<0>();
+    } else {
+      for (int i = tid; i < V; i += PK_CONSUMERS) {
+        lg[i] = __ldcg(g0 + i);
+        if (g1) lg[V + i] = __ldcg(g1 + i);
+      }
+    }
+    named_sync(1, PK_CONSUMERS);
+  }
+  const float* lc = lg;
+  const float* lu = a.B >= 2 ? lg + V : nullptr;
   const float gs = a.gs[h], temp = a.temp[h], topp = a.topp[h];
   const long long tk = a.topk[h];
-  int V2 = 1;
-  while (V2 < V) V2 <<= 1;
-  // 1) CFG, codec mask, temperature -> composite keys (key desc, index asc); greedy argmax(cfg)
+  const bool dosample = a.dosample[h] != 0;
+  // 1) CFG, codec mask, temperature -> composite keys; greedy argmax(cfg)
   float gbest = -INFINITY;
   int gidx = 0x7fffffff;
-  for (int i = tid; i < V2; i += PK_CONSUMERS) {
-    unsigned long long comp = 0ull;
-    if (i < V) {
-      float cfg = __ldcg(lc + i);
-      if (lu) {
-        const float u = __ldcg(lu + i);
-        cfg = __fadd_rn(u, __fmul_rn(gs, __fsub_rn(cfg, u)));
-      }
-      if (i >= a.CB) cfg = -INFINITY;
-      if (cfg > gbest || (cfg == gbest && i < gidx)) {
-        gbest = cfg;
-        gidx = i;
-      }
-      const float key = __fdiv_rn(cfg, temp);
-      comp = ((unsigned long long)f2ord(key) << 12) | (unsigned long long)(4095 - i);
+  for (int i = tid; i < V; i += PK_CONSUMERS) {
+    float cfg = lc[i];
+    if (lu) {
+      const float u = lu[i];
+      cfg = __fadd_rn(u, __fmul_rn(gs, __fsub_rn(cfg, u)));
     }
-    arr[i] = comp;
+    if (i >= a.CB) cfg = -INFINITY;
+    if (cfg > gbest || (cfg == gbest && i < gidx)) {
+      gbest = cfg;
+      gidx = i;
+    }
+    const float key = __fdiv_rn(cfg, temp);
+    keys[i] = ((unsigned long long)f2ord(key) << 12) | (unsigned long long)(4095 - i);
   }
+  hist[tid] = 0u;
+  hist[256 + tid] = 0u;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(FULL, gbest, o);
@@ -141,8 +191,10 @@ __device__ void dd_sample(const DDArgs& a, int step, int h, unsigned long long* 
     gv[warp] = gbest;
     s_int[16 + warp] = gidx;
   }
+  if (tid == 0) s_int[12] = 0;   // survivor counter
   named_sync(1, PK_CONSUMERS);
-  if (tid == 0) {
+  DD_STAMP(step, 3 + 9 * a.L + 2);
+  if (!dosample) {
     float bv = gv[0];
     int bi = s_int[16];
     for (int w = 1; w < ST_CWARPS; ++w)
@@ -150,41 +202,118 @@ __device__ void dd_sample(const DDArgs& a, int step, int h, unsigned long long* 
         bv = gv[w];
         bi = s_int[16 + w];
       }
-    s_int[0] = bi;
+    named_sync(1, PK_CONSUMERS);
+    return bi;
   }
-  // 2) bitonic sort, descending
-  for (int k = 2; k <= V2; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < (V2 >> 1); i += PK_CONSUMERS) {
-        const int lo = 2 * i - (i & (j - 1));
-        const int hi = lo + j;
-        const unsigned long long x = arr[lo], y = arr[hi];
-        const bool desc = (lo & k) == 0;
-        if (desc ? (x < y) : (x > y)) {
-          arr[lo] = y;
-          arr[hi] = x;
+  const int maxk = V < 1024 ? V : 1024;
+  const int kk = tk > 0 ? (tk < maxk ? (int)tk : maxk) : maxk;
+  // 2) radix select of the kk-th largest key (keys are unique: the low 12 bits hold the index)
+  unsigned long long prefix = 0ull, pmask = 0ull;
+  int r = kk;
+  const int shifts[6] = {36, 28, 20, 12, 4, 0};
+  for (int p = 0; p < 6; ++p) {
+    const int sh = shifts[p];
+    unsigned* hc = hist + (p & 1) * 256;
+    for (int i = tid; i < V; i += PK_CONSUMERS) {
+      const unsigned long long k = keys[i];
+      if ((k & pmask) == prefix) atomicAdd(&hc[(unsigned)(k >> sh) & 255u], 1u);
+    }
+    named_sync(1, PK_CONSUMERS);
+    if (warp == 0) {
+      unsigned c[8];
+      unsigned tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hc[255 - 8 * lane - j];
+        tot += c[j];
+      }
+      unsigned incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const unsigned excl = incl - tot;
+      const unsigned hit = __ballot_sync(FULL, excl < (unsigned)r && (unsigned)r <= incl);
+      if (lane == __ffs(hit) - 1) {
+        int rr = r - (int)excl;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (rr > 0 && rr <= (int)c[j]) {
+            s_int[1] = 255 - 8 * lane - j;
+            s_int[2] = rr;
+            s_int[3] = (int)c[j] == rr;
+            rr = 0;
+          } else if (rr > 0) {
+            rr -= (int)c[j];
+          }
         }
       }
-      named_sync(1, PK_CONSUMERS);
     }
+    hist[((p + 1) & 1) * 256 + tid] = 0u;   // clear the other histogram for the next pass
+    named_sync(1, PK_CONSUMERS);
+    prefix |= (unsigned long long)s_int[1] << sh;
+    pmask |= 255ull << sh;
+    r = s_int[2];
+    if (s_int[3]) break;
   }
-  // 3) warp 0: top-k / top-p / softmax / argmax(p / q) with the canonical sums (lane l owns ranks l*C .. l*C+C-1)
-  if (warp == 0) {
-    const int maxk = V < 1024 ? V : 1024;
-    const int kk = tk > 0 ? (tk < maxk ? (int)tk : maxk) : maxk;
-    const int C = (kk + 31) / 32;
-    const float key0 = ord2f((unsigned)(arr[0] >> 12));
-    auto e_of = [&](int r) { return fb_exp_dev(__fsub_rn(ord2f((unsigned)(arr[r] >> 12)), key0)); };
-    float b = 0.f;
-    for (int j = 0; j < C; ++j) {
-      const int r = lane * C + j;
-      if (r < kk) b = __fadd_rn(b, e_of(r));
+  DD_STAMP(step, 3 + 9 * a.L + 3);
+  // 3) gather the kk survivors (key >= threshold; exactly kk of them), pad to a power of two, sort descending
+  int n2 = 1;
+  while (n2 < kk) n2 <<= 1;
+  for (int i = tid; i < V; i += PK_CONSUMERS) {
+    const unsigned long long k = keys[i];
+    if (k >= prefix) top[atomicAdd(&s_int[12], 1)] = k;
+  }
+  for (int i = kk + tid; i < n2; i += PK_CONSUMERS) top[i] = 0ull;
+  named_sync(1, PK_CONSUMERS);
+  if (n2 <= 64) {
+    if (warp == 0) {
+      for (int k = 2; k <= n2; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          for (int i = lane; i < (n2 >> 1); i += 32) {
+            const int lo = 2 * i - (i & (j - 1)), hi = lo + j;
+            const unsigned long long x = top[lo], y = top[hi];
+            if (((lo & k) == 0) ? (x < y) : (x > y)) {
+              top[lo] = y;
+              top[hi] = x;
+            }
+          }
+          __syncwarp();
+        }
     }
-    const float S = __shfl_sync(FULL, lane_scan(b), 31);
+  } else {
+    for (int k = 2; k <= n2; k <<= 1)
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = tid; i < (n2 >> 1); i += PK_CONSUMERS) {
+          const int lo = 2 * i - (i & (j - 1)), hi = lo + j;
+          const unsigned long long x = top[lo], y = top[hi];
+          if (((lo & k) == 0) ? (x < y) : (x > y)) {
+            top[lo] = y;
+            top[hi] = x;
+          }
+        }
+        named_sync(1, PK_CONSUMERS);
+      }
+  }
+  if (n2 <= 64) __syncwarp();
+  DD_STAMP(step, 3 + 9 * a.L + 4);
+  // 4) warp 0: top-p / softmax / argmax(p / q) with the canonical sums (lane l owns ranks l*C .. l*C+C-1)
+  if (warp == 0) {
+    const int C = (kk + 31) / 32;
+    const float key0 = ord2f((unsigned)(top[0] >> 12));
+    auto e_of = [&](int rk) { return fb_exp_dev(__fsub_rn(ord2f((unsigned)(top[rk] >> 12)), key0)); };
+    float bsum = 0.f;
+    for (int j = 0; j < C; ++j) {
+      const int rk = lane * C + j;
+      if (rk < kk) bsum = __fadd_rn(bsum, e_of(rk));
+    }
+    const float S = __shfl_sync(FULL, lane_scan(bsum), 31);
+    DD_STAMP(step, 3 + 9 * a.L + 5);
     float bp = 0.f;
     for (int j = 0; j < C; ++j) {
-      const int r = lane * C + j;
-      if (r < kk) bp = __fadd_rn(bp, __fdiv_rn(e_of(r), S));
+      const int rk = lane * C + j;
+      if (rk < kk) bp = __fadd_rn(bp, __fdiv_rn(e_of(rk), S));
     }
     const float inclp = lane_scan(bp);
     const float exclp = __shfl_up_sync(FULL, inclp, 1);
@@ -192,10 +321,10 @@ __device__ void dd_sample(const DDArgs& a, int step, int h, unsigned long long* 
     float s2 = 0.f;
     unsigned keepmask = 0u;
     for (int j = 0; j < C; ++j) {
-      const int r = lane * C + j;
-      if (r >= kk) break;
-      const float e = e_of(r);
-      const bool keep = (r == 0) || !(run > topp);
+      const int rk = lane * C + j;
+      if (rk >= kk) break;
+      const float e = e_of(rk);
+      const bool keep = (rk == 0) || !(run > topp);
       run = __fadd_rn(run, __fdiv_rn(e, S));
       if (keep) {
         s2 = __fadd_rn(s2, e);
@@ -203,14 +332,15 @@ __device__ void dd_sample(const DDArgs& a, int step, int h, unsigned long long* 
       }
     }
     const float S2 = __shfl_sync(FULL, lane_scan(s2), 31);
+    DD_STAMP(step, 3 + 9 * a.L + 6);
     const float* qrow = a.q + ((size_t)step * half + h) * V;
     float best = -1.f;
     int bidx = 0x7fffffff;
     for (int j = 0; j < C; ++j) {
       if (!((keepmask >> j) & 1u)) continue;
-      const int r = lane * C + j;
-      const int id = 4095 - (int)(arr[r] & 4095ull);
-      const float sc = __fdiv_rn(__fdiv_rn(e_of(r), S2), __ldg(qrow + id));
+      const int rk = lane * C + j;
+      const int id = 4095 - (int)(top[rk] & 4095ull);
+      const float sc = __fdiv_rn(__fdiv_rn(e_of(rk), S2), __ldg(qrow + id));
       if (sc > best || (sc == best && id < bidx)) {
         best = sc;
         bidx = id;
@@ -225,116 +355,138 @@ __device__ void dd_sample(const DDArgs& a, int step, int h, unsigned long long* 
         bidx = oi;
       }
     }
-    if (lane == 0) {
-      int tokv = a.dosample[h] ? bidx : s_int[0];
-      tokv = tokv < 0 ? 0 : (tokv > V - 1 ? V - 1 : tokv);
-      a.outtok[(size_t)h * a.NCB + step] = tokv;
-      if (a.B >= 2) a.outtok[(size_t)(h + half) * a.NCB + step] = tokv;
-      if (a.forced) {
-        const long long fc = a.forced[(size_t)step * a.B + h];
-        tokv = (int)(fc < 0 ? 0 : (fc > V - 1 ? V - 1 : fc));
-      }
-      a.tokbuf[h] = tokv;
-      if (a.B >= 2) {
-        long long tu = tokv;
-        if (a.forced) {
-          const long long fc = a.forced[(size_t)step * a.B + h + half];
-          tu = fc < 0 ? 0 : (fc > V - 1 ? V - 1 : fc);
-        }
-        a.tokbuf[h + half] = tu;
-      }
-    }
+    if (lane == 0) s_int[0] = bidx;
   }
+  named_sync(1, PK_CONSUMERS);
+  return s_int[0];
 }
 
 // ------------------------------------------------------------------------------------------------ attention (S2)
-// All M x NH query rows over the layer's cached keys 0..pos(m); one warp per row, lane = 4 head dimensions; every key
-// of the row loaded at once.  Eager rounding: s = bf16(bf16(q.k) * scaling), p = bf16(softmax_fp32(s)),
-// out = bf16(sum p v).  Output rows go to xs (the o-projection input).
+// Shared-memory bytes of the attention staging area (q rows, the layer's K and V of every position, scores).
+__host__ __device__ constexpr size_t dd_attn_bytes(int M, int NH, int B, int NKV, int P) {
+  return (size_t)M * NH * 256 + 2 * (size_t)B * NKV * P * 256 + (size_t)M * NH * 32 * 4;
+}
+
+// All M x NH query rows over the layer's cached positions 0..pos(m), computed by every CTA (the o-projection that
+// follows needs every row).  One round trip: q, K and V of every used position are staged in shared memory with
+// cp.async, then scores (one thread per (row, key)), softmax (one thread per row) and p.V (one thread per
+// (row, 8 dims)).  Eager rounding: s = bf16(bf16(q.k) * scaling), p = bf16(softmax_fp32(s)), out = bf16(sum p v).
+// Output rows go to xs (the o-projection input); `att` is the staging area.
 template <int G>
-__device__ void dd_attention(const DDArgs& a, int l, int step, int T, unsigned char* xs, int x_pitch) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int M = a.B * T;
-  const int QD = a.NH * 128;
-  constexpr int KB = 16;        // keys per load batch (all loads of a batch in flight together)
-  constexpr int MAXK = 32;      // positions 0..n_decode, n_decode <= 31
-  for (int row = warp; row < M * a.NH; row += ST_CWARPS) {
-    const int m = row / a.NH, qh = row - m * a.NH;
-    const int b = m / T, t = m - b * T;
+__device__ __noinline__ void dd_attention(const DDArgs& a, int l, int step, int T, unsigned char* xs, int x_pitch,
+                                          unsigned char* att) {
+  const int tid = threadIdx.x;
+  const int M = a.B * T, NH = a.NH, NKV = a.NKV, QD = NH * 128;
+  const int np = step == 0 ? 2 : step + 2;        // positions used by the last token of the step
+  const int nrow = M * NH;
+  bf16* qs = reinterpret_cast<bf16*>(att);
+  bf16* ks = qs + (size_t)nrow * 128;
+  bf16* vs = ks + (size_t)a.B * NKV * np * 128;
+  float* ps = reinterpret_cast<float*>(vs + (size_t)a.B * NKV * np * 128);
+  const int qch = nrow * 16, kch = a.B * NKV * np * 16;
+  for (int i = tid; i < qch + 2 * kch; i += PK_CONSUMERS) {
+    const bf16* src;
+    bf16* dst;
+    if (i < qch) {
+      const int row = i >> 4, c = i & 15, m = row / NH, qh = row - m * NH;
+      src = a.qb + (size_t)m * QD + qh * 128 + c * 8;
+      dst = qs + (size_t)row * 128 + c * 8;
+    } else {
+      int j = i - qch;
+      const bool isv = j >= kch;
+      if (isv) j -= kch;
+      const int row = j >> 4, c = j & 15, bk = row / np, p = row - bk * np;
+      const int b = bk / NKV, kvh = bk - b * NKV;
+      src = (isv ? a.vc : a.kc) + ((((size_t)l * a.B + b) * NKV + kvh) * a.P + p) * 128 + c * 8;
+      dst = (isv ? vs : ks) + (size_t)row * 128 + c * 8;
+    }
+    cp_async16(dst, src);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  named_sync(1, PK_CONSUMERS);
+  for (int i = tid; i < nrow * np; i += PK_CONSUMERS) {
+    const int row = i / np, j = i - row * np;
+    const int m = row / NH, qh = row - m * NH, b = m / T, t = m - b * T;
     const int pos = step == 0 ? t : step + 1;
-    const int kvh = qh / G;
-    const uint2 q2 = __ldcg(reinterpret_cast<const uint2*>(a.qb + (size_t)m * QD + qh * 128) + lane);
-    const float qf[4] = {lo_f(q2.x), hi_f(q2.x), lo_f(q2.y), hi_f(q2.y)};
-    const size_t base = ((((size_t)l * a.B + b) * a.NKV + kvh) * a.P) * 128;
-    float s[MAXK];
+    if (j > pos) continue;
+    const uint4* qr = reinterpret_cast<const uint4*>(qs + (size_t)row * 128);
+    const uint4* kr = reinterpret_cast<const uint4*>(ks + ((size_t)(b * NKV + qh / G) * np + j) * 128);
+    float d = 0.f;
+#pragma unroll 4
+    for (int cc = 0; cc < 16; ++cc) {
+      const int c = (cc + j) & 15;               // rotate the chunk order by key: fewer bank conflicts
+      float qf[8], kf[8];
+      cvt8(qr[c], qf);
+      cvt8(kr[c], kf);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) d = fmaf(qf[u], kf[u], d);
+    }
+    ps[row * 32 + j] = rbf(rbf(d) * a.scaling);
+  }
+  named_sync(1, PK_CONSUMERS);
+  if (tid < nrow) {
+    const int row = tid, m = row / NH, t = m - (m / T) * T;
+    const int pos = step == 0 ? t : step + 1;
+    float* pr = ps + row * 32;
     float mx = -INFINITY;
-#pragma unroll
-    for (int j0 = 0; j0 < MAXK; j0 += KB) {
-      if (j0 > pos) break;
-      uint2 kr[KB];
-#pragma unroll
-      for (int j = 0; j < KB; ++j)
-        if (j0 + j <= pos) kr[j] = __ldcg(reinterpret_cast<const uint2*>(a.kc + base + (size_t)(j0 + j) * 128) + lane);
-#pragma unroll
-      for (int j = 0; j < KB; ++j) {
-        if (j0 + j <= pos) {
-          float d = qf[0] * lo_f(kr[j].x);
-          d = fmaf(qf[1], hi_f(kr[j].x), d);
-          d = fmaf(qf[2], lo_f(kr[j].y), d);
-          d = fmaf(qf[3], hi_f(kr[j].y), d);
-          d = warp_sum(d);
-          s[j0 + j] = rbf(rbf(d) * a.scaling);
-          mx = fmaxf(mx, s[j0 + j]);
-        }
-      }
-    }
+    for (int j = 0; j <= pos; ++j) mx = fmaxf(mx, pr[j]);
     float den = 0.f;
-#pragma unroll
-    for (int j = 0; j < MAXK; ++j) {
-      if (j <= pos) {
-        s[j] = expf(s[j] - mx);
-        den += s[j];
-      }
+    for (int j = 0; j <= pos; ++j) {
+      const float e = expf(pr[j] - mx);
+      pr[j] = e;
+      den += e;
     }
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j <= pos; ++j) pr[j] = rbf(pr[j] / den);
+  }
+  named_sync(1, PK_CONSUMERS);
+  for (int i = tid; i < nrow * 16; i += PK_CONSUMERS) {
+    const int row = i >> 4, c = i & 15;
+    const int m = row / NH, qh = row - m * NH, b = m / T, t = m - b * T;
+    const int pos = step == 0 ? t : step + 1;
+    const float* pr = ps + row * 32;
+    const bf16* vb = vs + (size_t)(b * NKV + qh / G) * np * 128 + c * 8;
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j <= pos; ++j) {
+      float vf[8];
+      cvt8(*reinterpret_cast<const uint4*>(vb + (size_t)j * 128), vf);
+      const float p = pr[j];
 #pragma unroll
-    for (int j0 = 0; j0 < MAXK; j0 += KB) {
-      if (j0 > pos) break;
-      uint2 vr[KB];
-#pragma unroll
-      for (int j = 0; j < KB; ++j)
-        if (j0 + j <= pos) vr[j] = __ldcg(reinterpret_cast<const uint2*>(a.vc + base + (size_t)(j0 + j) * 128) + lane);
-#pragma unroll
-      for (int j = 0; j < KB; ++j) {
-        if (j0 + j <= pos) {
-          const float p = rbf(s[j0 + j] / den);
-          o[0] = fmaf(p, lo_f(vr[j].x), o[0]);
-          o[1] = fmaf(p, hi_f(vr[j].x), o[1]);
-          o[2] = fmaf(p, lo_f(vr[j].y), o[2]);
-          o[3] = fmaf(p, hi_f(vr[j].y), o[3]);
-        }
-      }
+      for (int u = 0; u < 8; ++u) o[u] = fmaf(p, vf[u], o[u]);
     }
-    uint2 ov;
+    uint4 ov;
     ov.x = pack2(o[0], o[1]);
     ov.y = pack2(o[2], o[3]);
-    *reinterpret_cast<uint2*>(xs + (size_t)m * x_pitch + (size_t)(qh * 128 + lane * 4) * 2) = ov;
+    ov.z = pack2(o[4], o[5]);
+    ov.w = pack2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + (size_t)(qh * 128 + c * 8) * 2) = ov;
   }
   named_sync(1, PK_CONSUMERS);
 }
 
-// x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.
-__device__ void dd_load_mid(unsigned char* xs, int x_pitch, const DDArgs& a, int M, const bf16* nw, float* nred) {
+// x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.  xres and ob arrive with cp.async (one round trip);
+// the un-normalised x_mid rows are also kept in `keep` ([M][H] bf16) for the down projection's residual.
+__device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const DDArgs& a, int M, const bf16* nw,
+                                         float* nred, bf16* keep) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int H = a.H, kv = H >> 3;
+  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
+    const int m = i / kv, j = i - m * kv;
+    cp_async16(xs + (size_t)m * x_pitch + j * 16, a.xres + (size_t)m * H + (size_t)j * 8);
+    cp_async16(keep + (size_t)m * H + (size_t)j * 8, a.ob + (size_t)m * H + (size_t)j * 8);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
   float ss[8];
 #pragma unroll
   for (int m = 0; m < 8; ++m) ss[m] = 0.f;
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
+    uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
+    uint4* pk = reinterpret_cast<uint4*>(keep + (size_t)m * H + (size_t)j * 8);
     float x[8], o[8];
-    cvt8(__ldcg(reinterpret_cast<const uint4*>(a.xres + (size_t)m * H) + j), x);
-    cvt8(__ldcg(reinterpret_cast<const uint4*>(a.ob + (size_t)m * H) + j), o);
+    cvt8(*px, x);
+    cvt8(*pk, o);
     float v[8];
     float q = 0.f;
 #pragma unroll
@@ -342,12 +494,13 @@ __device__ void dd_load_mid(unsigned char* xs, int x_pitch, const DDArgs& a, int
       v[u] = rbf(x[u] + o[u]);
       q = fmaf(v[u], v[u], q);
     }
-    uint4 pk;
-    pk.x = pack2(v[0], v[1]);
-    pk.y = pack2(v[2], v[3]);
-    pk.z = pack2(v[4], v[5]);
-    pk.w = pack2(v[6], v[7]);
-    *reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16) = pk;
+    uint4 w;
+    w.x = pack2(v[0], v[1]);
+    w.y = pack2(v[2], v[3]);
+    w.z = pack2(v[4], v[5]);
+    w.w = pack2(v[6], v[7]);
+    *px = w;
+    *pk = w;
 #pragma unroll
     for (int mm = 0; mm < 8; ++mm)
       if (mm == m) ss[mm] += q;
@@ -399,6 +552,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
   uint64_t* empty = full + PK_MAX_STAGES;
   __shared__ float nred[ST_CWARPS * 8];
   __shared__ int s_int[32];
+  __shared__ long long s_tok[DD_MAXB];   // tokens fed to the next step (this CTA's copy of the sampler result)
+  __shared__ __align__(16) bf16 s_cs[2][2][128];   // [cos|sin][step position 0|1][dim] of this step's positions
 
   const int tid = threadIdx.x, warp = tid >> 5;
   if (tid == 0) {
@@ -453,23 +608,31 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
   for (int s = 0; s < a.NCB; ++s) {
     const int T = s == 0 ? 2 : 1;
     const int M = a.B * T;
-    // E: gather embeddings into xs, projector GEMV -> xres
+    DD_STAMP(s, 0);
+    // E: gather embeddings into xs (cp.async, one round trip, with this step's rotary rows), projector GEMV -> xres
     {
       const int kv = AE >> 3;
       const long long rows = (long long)(a.NCB + 1) * V;
       for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
         const int m = i / kv, j = i - m * kv;
         const int b = m / T, tt = m - b * T;
-        const uint4* src;
+        const bf16* src;
         if (s == 0 && tt == 0) {
-          src = reinterpret_cast<const uint4*>(a.bh + (size_t)b * AE);
+          src = a.bh + (size_t)b * AE;
         } else {
-          long long id = (s == 0) ? __ldcg(a.first_cb + b) : __ldcg(a.tokbuf + b) + (long long)s * V;
+          long long id = (s == 0) ? __ldcg(a.first_cb + b) : s_tok[b] + (long long)s * V;
           id = id < 0 ? 0 : (id >= rows ? rows - 1 : id);
-          src = reinterpret_cast<const uint4*>(a.embed + (size_t)id * AE);
+          src = a.embed + (size_t)id * AE;
         }
-        *reinterpret_cast<uint4*>(xs + (size_t)m * xp_ae + j * 16) = __ldcg(src + j);
+        cp_async16(xs + (size_t)m * xp_ae + j * 16, src + (size_t)j * 8);
       }
+      if (tid < 2 * T * 16) {    // cos / sin rows of the step's T positions, 16 chunks of 16 bytes each
+        const int tab = tid / (T * 16), r = (tid / 16) % T, c = tid % 16;
+        const int pos = s == 0 ? r : s + 1;
+        cp_async16(&s_cs[tab][r][c * 8], (tab ? a.sin_tab : a.cos_tab) + (size_t)pos * 128 + c * 8);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
       named_sync(1, PK_CONSUMERS);
       if (!consume_task<1>(rg, t, H, AE, xs, xp_ae, M, zero16, red, sums,
                            [&](int n0, int nu, const float* sm) {
@@ -478,9 +641,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
                                a.xres[(size_t)m * H + n0 + i] = __float2bfloat16_rn(sm[i * 8 + m]);
                              }
                            }, a.err)) return;
+      DD_STAMP(s, 1);
       if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+      DD_STAMP(s, 2);
     }
     for (int l = 0; l < a.L; ++l) {
+      const int tb = 3 + 9 * l;
       const DDLayer W = a.layers[l];
       // S1: RMSNorm + q|k|v (rotary pairs) + RoPE + KV write
       load_x(xs, xp_h, a.xres, H, M, H, W.ln1, a.eps, nred);
@@ -493,9 +659,9 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
                                const int pos = s == 0 ? tt : s + 1;
                                float y0 = rbf(sm[i * 8 + m]), y1 = rbf(sm[(i + 8) * 8 + m]);
                                if (hh < NH + NKV) {
-                                 const float c0 = b2f(a.cos_tab[pos * 128 + d]), s0 = b2f(a.sin_tab[pos * 128 + d]);
-                                 const float c1 = b2f(a.cos_tab[pos * 128 + d + 64]);
-                                 const float s1 = b2f(a.sin_tab[pos * 128 + d + 64]);
+                                 const int pr = s == 0 ? tt : 0;
+                                 const float c0 = b2f(s_cs[0][pr][d]), s0 = b2f(s_cs[1][pr][d]);
+                                 const float c1 = b2f(s_cs[0][pr][d + 64]), s1 = b2f(s_cs[1][pr][d + 64]);
                                  const float o0 = rbf(rbf(y0 * c0) + rbf(-y1 * s0));
                                  const float o1 = rbf(rbf(y1 * c1) + rbf(y0 * s1));
                                  y0 = o0;
@@ -513,9 +679,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
                                }
                              }
                            }, a.err)) return;
+      DD_STAMP(s, tb + 0);
       if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+      DD_STAMP(s, tb + 1);
       // S2: attention (every CTA, all rows) + o GEMV
-      dd_attention<G>(a, l, s, T, xs, xp_q);
+      dd_attention<G>(a, l, s, T, xs, xp_q, xs + a.att_off);
+      DD_STAMP(s, tb + 2);
       if (!consume_task<1>(rg, t, H, QD, xs, xp_q, M, zero16, red, sums,
                            [&](int n0, int nu, const float* sm) {
                              if (tid < nu * M) {
@@ -523,9 +692,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
                                a.ob[(size_t)m * H + n0 + i] = __float2bfloat16_rn(sm[i * 8 + m]);
                              }
                            }, a.err)) return;
+      DD_STAMP(s, tb + 3);
       if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+      DD_STAMP(s, tb + 4);
       // S3: RMSNorm(bf16(x + o)) + gate|up + SiLU*up
-      dd_load_mid(xs, xp_h, a, M, W.ln2, nred);
+      bf16* xkeep = reinterpret_cast<bf16*>(xs + a.keep_off);  // x_mid rows for the down projection's residual
+      dd_load_mid(xs, xp_h, a, M, W.ln2, nred, xkeep);
       if (!consume_task<2>(rg, t, F, H, xs, xp_h, M, zero16, red, sums,
                            [&](int n0, int nu, const float* sm) {
                              if (tid < nu * M) {
@@ -535,20 +707,24 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
                                a.act[(size_t)m * F + n0 + i] = __float2bfloat16_rn(rbf(g / (1.0f + expf(-g))) * u);
                              }
                            }, a.err)) return;
+      DD_STAMP(s, tb + 5);
       if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+      DD_STAMP(s, tb + 6);
       // S4: down + residual: xres = bf16(bf16(xres + o) + bf16(d))
       load_x(xs, xp_f, a.act, F, M, F, nullptr, 0.f, nred);
       if (!consume_task<1>(rg, t, H, F, xs, xp_f, M, zero16, red, sums,
                            [&](int n0, int nu, const float* sm) {
                              if (tid < nu * M) {
                                const int i = tid / M, m = tid - i * M, n = n0 + i;
-                               const float xm = rbf(b2f(__ldcg(a.xres + (size_t)m * H + n)) +
-                                                    b2f(__ldcg(a.ob + (size_t)m * H + n)));
+                               const float xm = b2f(xkeep[(size_t)m * H + n]);
                                a.xres[(size_t)m * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * 8 + m]));
                              }
                            }, a.err)) return;
+      DD_STAMP(s, tb + 7);
       if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+      DD_STAMP(s, tb + 8);
     }
+    const int te = 3 + 9 * a.L;
     // S5: final RMSNorm of each row's last token + codebook head -> fp32 logits
     load_x(xs, xp_h, a.xres + (size_t)(T - 1) * H, (long)T * H, a.B, H, a.normf, a.eps, nred);
     if (!consume_task<1>(rg, t, V, H, xs, xp_h, a.B, zero16, red, sums,
@@ -560,9 +736,31 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
                              if (a.dbg) a.dbg[((size_t)s * a.B + b) * V + n0 + i] = v;
                            }
                          }, a.err)) return;
+    DD_STAMP(s, te + 0);
     if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-    if ((int)blockIdx.x < half) dd_sample(a, s, blockIdx.x, reinterpret_cast<unsigned long long*>(xs), s_int);
-    if (s + 1 < a.NCB && !grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+    DD_STAMP(s, te + 1);
+    // every CTA samples every half-row; CTA 0 publishes, every CTA keeps the fed-forward tokens in s_tok
+    for (int h = 0; h < half; ++h) {
+      int tokv = dd_sample(a, s, h, xs, s_int);
+      tokv = tokv < 0 ? 0 : (tokv > V - 1 ? V - 1 : tokv);
+      if (tid == 0) {
+        for (int r = 0; r < (a.B >= 2 ? 2 : 1); ++r) {
+          const int b = h + r * half;
+          long long fed = tokv;
+          if (a.forced) {
+            const long long fc = a.forced[(size_t)s * a.B + b];
+            fed = fc < 0 ? 0 : (fc > V - 1 ? V - 1 : fc);
+          }
+          s_tok[b] = fed;
+          if (blockIdx.x == 0) {
+            a.outtok[(size_t)b * a.NCB + s] = tokv;
+            a.tokbuf[b] = fed;
+          }
+        }
+      }
+    }
+    named_sync(1, PK_CONSUMERS);
+    DD_STAMP(s, te + 7);
   }
   grid_exit(a.bar);
 }
@@ -674,17 +872,29 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.act = (bf16*)(sc + Lo.act); a.kc = (bf16*)(sc + Lo.kc); a.vc = (bf16*)(sc + Lo.vc);
   a.logits = (float*)(sc + Lo.logits); a.bar = (GridBar*)(sc + Lo.bar);
   a.err = fbh::device_err_ptr();
+  a.trace = (unsigned long long*)c->trace;
   int kmax = c->embed_dim;
   if (c->ffn > kmax) kmax = c->ffn;
   if (c->heads * 128 > kmax) kmax = c->heads * 128;
   if (c->hidden > kmax) kmax = c->hidden;
   const size_t M = (size_t)c->batch * 2;
+  // one buffer, three uses: GEMV input rows (up to M x kmax); attention output rows + staging area (att_off);
+  // x_mid rows kept from S3 to S4 past the down projection's act rows (keep_off); the sampler's keys
+  const size_t att_off = al256d(M * (c->heads * 128 * 2 + 16));
+  const size_t keep_off = al256d(M * (c->ffn * 2 + 16));
   size_t xs = al256d(M * (kmax * 2 + 16));
-  if (xs < (size_t)DD_MAXV * 8) xs = (size_t)DD_MAXV * 8;  // sampler keys reuse the activation buffer
+  size_t xs_att = al256d(att_off + dd_attn_bytes((int)M, c->heads, c->batch, c->kv_heads, c->n_decode + 1));
+  const size_t xs_keep = al256d(keep_off + M * c->hidden * 2);
+  const size_t xs_smp = al256d(dd_sampler_bytes(c->vocab));
+  if (xs_keep > xs_att) xs_att = xs_keep;
+  if (xs_att > xs) xs = xs_att;
+  if (xs_smp > xs) xs = xs_smp;
   a.xs_bytes = (int)xs;
+  a.att_off = (int)att_off;
+  a.keep_off = (int)keep_off;
   const size_t fixed = xs + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * PK_MAX_STAGES * 8;
-  const size_t budget = 227 * 1024 - ST_CWARPS * 8 * 4 - 32 * 4 - 256;
-  int nst = (int)((budget - fixed) / ST_BYTES);
+  const size_t budget = 227 * 1024 - ST_CWARPS * 8 * 4 - 32 * 4 - DD_MAXB * 8 - 2 * 2 * 128 * 2 - 256;
+  int nst = fixed < budget ? (int)((budget - fixed) / ST_BYTES) : 0;
   if (nst > PK_MAX_STAGES) nst = PK_MAX_STAGES;
   if (nst < 2) {
     fbh::set_msg("dd_frame: activations too large for two ring stages");

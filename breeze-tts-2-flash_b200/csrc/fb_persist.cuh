@@ -9,9 +9,14 @@
 #pragma once
 #include "fb_stream.cuh"
 
-namespace fb {
+#ifndef FB_PK_MAX_STAGES
+#define FB_PK_MAX_STAGES 4
+#endif
 
-constexpr int PK_MAX_STAGES = 4;
+namespace fb {
+inline namespace FB_ST_NS_CAT(kc, FB_ST_KC) {
+
+constexpr int PK_MAX_STAGES = FB_PK_MAX_STAGES;
 constexpr int PK_CONSUMERS = ST_CWARPS * 32;        // 256
 constexpr int PK_THREADS = PK_CONSUMERS + 32;       // + producer warp
 
@@ -37,9 +42,8 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 // completion of barrier number `epoch` is count >= epoch * gridDim.x (observed with acquire loads).  The critical
 // path is one add plus one poll round trip through L2.  Waits are bounded (WAIT_LIMIT_NS); on expiry, or when another
 // CTA has aborted, every CTA returns false and the kernel winds down (the host then re-zeroes the state).
-__device__ __forceinline__ bool grid_sync(GridBar* gb, unsigned& epoch, unsigned* err, int* s_flag) {
+__device__ __noinline__ bool grid_sync_n(GridBar* gb, unsigned epoch, unsigned* err, int* s_flag) {
   named_sync(2, PK_CONSUMERS);
-  ++epoch;
   if (threadIdx.x == 0) {
     int ok = 1;
     const unsigned target = epoch * gridDim.x;
@@ -65,6 +69,12 @@ __device__ __forceinline__ bool grid_sync(GridBar* gb, unsigned& epoch, unsigned
   }
   named_sync(2, PK_CONSUMERS);
   return *s_flag != 0;
+}
+// Not inlined: a persistent kernel calls it at ~20 sites, and its code must stay small enough to remain in the
+// instruction cache across a whole step (cold code re-fetched from L2 costs microseconds per phase).
+__device__ __forceinline__ bool grid_sync(GridBar* gb, unsigned& epoch, unsigned* err, int* s_flag) {
+  ++epoch;
+  return grid_sync_n(gb, epoch, err, s_flag);
 }
 
 // Called once by consumer thread 0 of every CTA after its last barrier: the last CTA out resets the barrier.
@@ -99,29 +109,38 @@ __device__ __forceinline__ void task_range(int units, int& u0, int& u1) {
   u1 = (int)((long long)units * (blockIdx.x + 1) / gridDim.x);
 }
 
+// Producer half of one 16-row group: stream its nkc column chunks; `row` is this lane's weight row (lanes < nrows,
+// others pass nullptr).  Returns the new stage counter, or -1 on timeout.  Not inlined (one copy for every task).
+__device__ __noinline__ int produce_group(Ring rg, int t, const bf16* row, int nrows, int K, unsigned* err) {
+  const int lane = threadIdx.x & 31;
+  const int nkc = (K + ST_KC - 1) / ST_KC;
+  for (int kc = 0; kc < nkc; ++kc, ++t) {
+    const int s = t % rg.nst;
+    if (t >= rg.nst && !mbar_wait_warp(&rg.empty[s], ((t / rg.nst) - 1) & 1, err)) return -1;
+    const int k0 = kc * ST_KC;
+    const int kw = min(ST_KC, K - k0);
+    unsigned char* st = rg.base + (size_t)s * ST_BYTES;
+    if (lane == 0) mbar_arrive_expect_tx(&rg.full[s], (unsigned)(nrows * kw * 2));
+    __syncwarp();
+    if (row) bulk_g2s(st + lane * ST_PITCH, row + k0, (unsigned)(kw * 2), &rg.full[s]);
+  }
+  return t;
+}
+
 // Producer half: stream this CTA's stages of the task; t is the running stage counter.  Returns false on timeout.
+// NMAT = 2 pairs each unit with a second matrix row: lanes 0-7 carry matrix 0, lanes 8-15 matrix 1.
 template <int NMAT, typename RowFn>
 __device__ __forceinline__ bool produce_task(Ring& rg, int& t, int units, int K, RowFn row, unsigned* err) {
   constexpr int UG = ST_ROWS / NMAT;
   const int lane = threadIdx.x & 31;
   int u0, u1;
   task_range(units, u0, u1);
-  const int nkc = (K + ST_KC - 1) / ST_KC;
   for (int n0 = u0; n0 < u1; n0 += UG) {
     const int nu = min(UG, u1 - n0);
-    for (int kc = 0; kc < nkc; ++kc, ++t) {
-      const int s = t % rg.nst;
-      if (t >= rg.nst && !mbar_wait_warp(&rg.empty[s], ((t / rg.nst) - 1) & 1, err)) return false;
-      const int k0 = kc * ST_KC;
-      const int kw = min(ST_KC, K - k0);
-      unsigned char* st = rg.base + (size_t)s * ST_BYTES;
-      if (lane == 0) mbar_arrive_expect_tx(&rg.full[s], (unsigned)(nu * NMAT * kw * 2));
-      __syncwarp();
-      if (lane < ST_ROWS) {
-        const int i = lane % UG, mat = lane / UG;
-        if (i < nu) bulk_g2s(st + lane * ST_PITCH, row(n0 + i, mat) + k0, (unsigned)(kw * 2), &rg.full[s]);
-      }
-    }
+    const int i = lane % UG, mat = lane / UG;
+    const bf16* r = (lane < ST_ROWS && i < nu) ? row(n0 + i, mat) : nullptr;
+    t = produce_group(rg, t, r, nu * NMAT, K, err);
+    if (t < 0) return false;
   }
   return true;
 }
@@ -137,50 +156,65 @@ __device__ __forceinline__ void prefetch_task(int units, int K, RowFn row) {
   for (int i = lane; i < n; i += 32) prefetch_l2(row(u0 + i / NMAT, i % NMAT), (unsigned)(K * 2));
 }
 
-// Consumer half: multiply the task's stages by the activation rows xs (M rows, byte pitch x_pitch) and hand each
-// 16-row group's sums (sums[r * 8 + m], r < 16) to epi(n0, nu, sums).  All 256 consumer threads call it.
+// Consumer half of one 16-row group: multiply its nkc stages by the activation rows xs (M rows, byte pitch x_pitch),
+// release them, and sum the 8 warps' partials into sums[r * 8 + m] (r < 16).  Returns the new stage counter, or -1 on
+// timeout.  Not inlined: every task of a persistent kernel shares this one copy.
+__device__ __noinline__ int consume_group(Ring rg, int t, int K, const unsigned char* xs, int x_pitch, int M,
+                                          const unsigned char* zero16, float* red, float* sums, unsigned* err) {
+  const int lane = threadIdx.x & 31;
+  const int nkc = (K + ST_KC - 1) / ST_KC;
+  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int kc = 0; kc < nkc; ++kc, ++t) {
+    const int s = t % rg.nst;
+    if (!mbar_wait_warp(&rg.full[s], (t / rg.nst) & 1, err)) return -1;
+    const int k0 = kc * ST_KC;
+    stage_mma(rg.base + (size_t)s * ST_BYTES, min(ST_KC, K - k0), xs, x_pitch, M, k0, zero16, c);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&rg.empty[s]);
+  }
+  reduce_warps(c, red, sums, 1);
+  return t;
+}
+
+// Consumer half: every 16-row group of the task through consume_group, then epi(n0, nu, sums).  All 256 consumer
+// threads call it.
 template <int NMAT, typename EpiFn>
 __device__ __forceinline__ bool consume_task(Ring& rg, int& t, int units, int K, const unsigned char* xs, int x_pitch,
                                              int M, const unsigned char* zero16, float* red, float* sums, EpiFn epi,
                                              unsigned* err) {
   constexpr int UG = ST_ROWS / NMAT;
-  const int lane = threadIdx.x & 31;
   int u0, u1;
   task_range(units, u0, u1);
-  const int nkc = (K + ST_KC - 1) / ST_KC;
   for (int n0 = u0; n0 < u1; n0 += UG) {
     const int nu = min(UG, u1 - n0);
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int kc = 0; kc < nkc; ++kc, ++t) {
-      const int s = t % rg.nst;
-      if (!mbar_wait_warp(&rg.full[s], (t / rg.nst) & 1, err)) return false;
-      const int k0 = kc * ST_KC;
-      stage_mma(rg.base + (size_t)s * ST_BYTES, min(ST_KC, K - k0), xs, x_pitch, M, k0, zero16, c);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rg.empty[s]);
-    }
-    reduce_warps(c, red, sums, 1);
+    t = consume_group(rg, t, K, xs, x_pitch, M, zero16, red, sums, err);
+    if (t < 0) return false;
     epi(n0, nu, sums);
   }
   return true;
 }
 
 // Stage rows [0, M) of a global bf16 activation matrix (row stride ld) into xs, optionally applying the eager
-// Qwen3 RMSNorm with weight nw (double rounding).  Cross-CTA data: read through L2 (ld.global.cg).
-__device__ __forceinline__ void load_x(unsigned char* xs, int x_pitch, const bf16* x, long ld, int M, int K,
-                                       const bf16* nw, float eps, float* nred /* [8][8] */) {
+// Qwen3 RMSNorm with weight nw (double rounding).  Cross-CTA data: copied with cp.async.cg (L2 only), every chunk in
+// flight at once (one round trip); each thread then works on the chunks it copied itself until the norm's reduction.
+__device__ __noinline__ void load_x(unsigned char* xs, int x_pitch, const bf16* x, long ld, int M, int K,
+                                    const bf16* nw, float eps, float* nred /* [8][8] */) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kv = K >> 3;
-  float ss[8];
-#pragma unroll
-  for (int m = 0; m < 8; ++m) ss[m] = 0.f;
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
-    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(x + (size_t)m * ld) + j);
-    *reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16) = v;
-    if (nw) {
+    cp_async16(xs + (size_t)m * x_pitch + j * 16, x + (size_t)m * ld + (size_t)j * 8);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  if (nw) {
+    float ss[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) ss[m] = 0.f;
+    for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
+      const int m = i / kv, j = i - m * kv;
       float f[8];
-      cvt8(v, f);
+      cvt8(*reinterpret_cast<const uint4*>(xs + (size_t)m * x_pitch + j * 16), f);
       float q = 0.f;
 #pragma unroll
       for (int u = 0; u < 8; ++u) q = fmaf(f[u], f[u], q);
@@ -188,8 +222,6 @@ __device__ __forceinline__ void load_x(unsigned char* xs, int x_pitch, const bf1
       for (int mm = 0; mm < 8; ++mm)
         if (mm == m) ss[mm] += q;
     }
-  }
-  if (nw) {
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
       const float q = warp_sum(ss[m]);
@@ -225,4 +257,5 @@ __device__ __forceinline__ void load_x(unsigned char* xs, int x_pitch, const bf1
   named_sync(1, PK_CONSUMERS);
 }
 
+}  // inline namespace
 }  // namespace fb

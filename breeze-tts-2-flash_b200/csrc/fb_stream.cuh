@@ -18,17 +18,23 @@
 #pragma once
 #include "fb_common.cuh"
 
-namespace fb {
-
-constexpr int ST_ROWS = 16;                       // weight rows per stage (one mma M tile)
+// The stage width is a per-translation-unit choice (FB_ST_KC, default 2048 columns); everything that depends on it
+// lives in an inline namespace named after it, so units built with different widths never share a definition.
 #ifndef FB_ST_KC
 #define FB_ST_KC 2048
 #endif
+#define FB_ST_NS_CAT2(a, b) a##b
+#define FB_ST_NS_CAT(a, b) FB_ST_NS_CAT2(a, b)
+
+namespace fb {
+inline namespace FB_ST_NS_CAT(kc, FB_ST_KC) {
+
+constexpr int ST_ROWS = 16;                       // weight rows per stage (one mma M tile)
 constexpr int ST_KC = FB_ST_KC;                   // columns per stage
 constexpr int ST_PITCH = ST_KC * 2 + 16;          // bytes per staged row
-constexpr int ST_BYTES = ST_ROWS * ST_PITCH;      // 65792 bytes per stage
+constexpr int ST_BYTES = ST_ROWS * ST_PITCH;      // 65792 bytes per stage at 2048 columns
 constexpr int ST_CWARPS = 8;                      // consumer warps
-constexpr int ST_KSTEPS_PER_WARP = ST_KC / 16 / ST_CWARPS;  // 16
+constexpr int ST_KSTEPS_PER_WARP = ST_KC / 16 / ST_CWARPS;  // 16 at 2048 columns
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -153,4 +159,5 @@ __device__ __forceinline__ void stage_load(unsigned char* stage, int nrows, int 
   }
 }
 
+}  // inline namespace
 }  // namespace fb

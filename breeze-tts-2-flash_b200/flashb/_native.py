@@ -66,7 +66,7 @@ class FbDDConfig(ctypes.Structure):
     _fields_ = [('layers', I), ('batch', I), ('hidden', I), ('embed_dim', I), ('heads', I), ('kv_heads', I),
                 ('head_dim', I), ('ffn', I), ('vocab', I), ('codebook_size', I), ('n_decode', I), ('eps', F),
                 ('scaling', F), ('embed', P), ('proj', P), ('normf', P), ('head_t', P), ('cos_tab', P),
-                ('sin_tab', P)]
+                ('sin_tab', P), ('trace', P)]
 
 
 class FbBBLayer(ctypes.Structure):

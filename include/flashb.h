@@ -177,6 +177,7 @@ typedef struct {
   const void* head_t;  /* [n_decode, vocab, hidden] bf16 (codebook heads, transposed) */
   const void* cos_tab; /* [n_decode + 2, 128] bf16 */
   const void* sin_tab;
+  uint64_t* trace;     /* optional: [grid][n_decode][11 + 9 * layers] %globaltimer stamps per CTA (task ends, barriers) */
 } fb_dd_config;
 int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg);
 int64_t flashb_dd_layer_bytes(void);

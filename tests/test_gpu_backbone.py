@@ -110,8 +110,47 @@ def test_persistent_step_matches_separate_kernels():
         assert_close(np32(ka), np32(kb), tol=2e-3, what='k write')
 
 
+def test_backbone_full_depth_per_layer_parity():
+    """28 layers, KV length 1023: every layer of the GPU step, fed the GPU's own input for that layer, matches the
+    oracle layer within the bf16 bar; so does the final norm + fp32 lm_head + CFG on the GPU's final residual.
+    (Comparing only the end of 28 chained layers measures the compounding of 1-ulp bf16 rounding flips, not the
+    parity of any kernel; that end-to-end drift is bounded separately below.)"""
+    from flashb import backbone as bbm
+    from flashb import kernels
+    g = _graph(layers=28, S=1024, valid=1023)
+    W, kcs, vcs = _oracle(g)
+    st = g._bb_state
+    B, pos = 2, 1023
+    fx = kernels.fused()
+    fx.embed_rope(g.input_ids_buf.view(B, -1), st['vocab'], st['embed'], g.position_ids.view(-1), st['cos_tab'],
+                  st['sin_tab'], st['x0'], st['cos'], st['sin'])
+    pids = g.position_ids.view(-1).cpu().numpy()
+    cos, sin = dec.rope_tables(W.theta, 128, pids)
+    cos, sin = cos.reshape(B, 1, 128), sin.reshape(B, 1, 128)
+    mask = np32(g.attn_mask)
+    x = st['x0'].clone()
+    torch.cuda.synchronize()
+    assert_close(np32(x), dec.embed_sum(W.embed, g.input_ids_buf.view(B, -1).cpu().numpy(), W.vocab), what='embed')
+    for li, (L, KV) in enumerate(zip(st['layers'], g.static_cache.layers)):
+        sub = dict(st)
+        sub['layers'] = [L]
+        xin = x.clone()
+        x = bbm.run_layers(sub, xin, [(KV.keys, KV.values)], g.attn_mask, g.cache_position).clone()
+        torch.cuda.synchronize()
+        ref = dec.backbone_layer(np32(xin), W.layers[li], kcs[li], vcs[li], mask, pos, cos, sin, W.eps, 128 ** -0.5)
+        assert_close(np32(x), ref, what=f'layer {li}')
+    fx.lm_head_cfg(x, st['norm_w'], st['norm_eps'], st['lm_head32'], g.guidance_scale, g.hidden_buf.view(B, -1),
+                   g.logits_buf, g.cfg_logits_buf)
+    torch.cuda.synchronize()
+    h = dec.rmsnorm(np32(x), W.norm, W.eps)
+    lg = dec.lm_head_fp32(h, W.lm_head32)
+    assert_close(g.logits_buf.cpu().numpy(), lg, what='lm_head')
+    assert_close(g.cfg_logits_buf.cpu().numpy(), dec.cfg_combine(lg, 1, float(g.guidance_scale.item())), what='cfg')
+
+
 def test_backbone_step_full_depth_argmax_and_determinism():
-    """28 layers: two runs are bitwise equal; logits stay within tolerance of the oracle."""
+    """28 chained layers end to end: the logits' argmax agrees with the oracle's, the compounded drift stays within
+    3e-2 of max |logit| (each layer alone is held to 1e-2 above), and two runs are bitwise equal."""
     g = _graph(layers=28, S=1024, valid=1023)
     W, kcs, vcs = _oracle(g)
     pos = 1023
@@ -122,7 +161,7 @@ def test_backbone_step_full_depth_argmax_and_determinism():
     g.decode_step()
     torch.cuda.synchronize()
     first = g.cfg_logits_buf.clone()
-    assert_close(g.logits_buf.cpu().numpy(), lg_ref, what='28-layer logits')
+    assert_close(g.logits_buf.cpu().numpy(), lg_ref, tol=3e-2, what='28-layer logits (compounded)')
     assert np.mean(np.argmax(g.logits_buf.cpu().numpy(), -1) == np.argmax(lg_ref, -1)) == 1.0
     for L, k in zip(g.static_cache.layers, k0):
         L.keys.copy_(k)
