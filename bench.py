@@ -192,10 +192,11 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from flashb import replicas
     from flashb.engine import BackboneConfig, DepthConfig, FrameEngine, backbone_step_bytes
     bcfg = BackboneConfig(codebooks=17)
     dcfg = DepthConfig()
-    my_streams = len(range(rank, a.streams, world))
+    my_streams = len(replicas.streams_for_rank(a.streams, rank, world))
     total_steps = a.warmup + a.steps
     n_runs = 1 if a.no_e2e else 2
     eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + 1, device=dev, seed=0)
@@ -203,24 +204,13 @@ def main():
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
+        replicas.barrier(dev)
 
     def maxred(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return replicas.max_over_ranks(x, dev)
 
     def sumred(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return replicas.sum_over_ranks(x, dev)
 
     case = a.case
     S = my_streams
