@@ -29,6 +29,8 @@
 // Scratch (residual stream, q, o, act, logits, KV cache, barrier) is one caller-owned buffer, zeroed once.
 #define FB_ST_KC 1024
 #define FB_PK_MAX_STAGES 8
+#include <mutex>
+
 #include "fb_persist.cuh"
 
 namespace fb {
@@ -910,4 +912,58 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
     case 8: return launch_dd<8>(a, smem, st);
     default: fbh::set_msg("dd_frame: GQA group %d not built", c->heads / c->kv_heads); return FB_ERR_UNSUPPORTED;
   }
+}
+
+// ------------------------------------------------------------------------------------------------ no-allocation variant
+// Scratch of flashb_dd_frame_noalloc: a fixed 1 MiB area in device memory, reserved on every GPU that loads this
+// library until the process exits.  In host code this name is only a stand-in for the symbol, never a device
+// address; the host fetches the real address per device with cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_dd_static_scratch[FB_DD_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_dd_static_mu;
+void* g_dd_static_ptr[64] = {nullptr};
+}  // namespace
+
+extern "C" int flashb_dd_frame_noalloc(const fb_dd_config* c, const void* layers_dev, const int64_t* first_cb,
+                                       const void* bh, int64_t* tokbuf, int64_t* outtok, const float* temp,
+                                       const int64_t* topk, const float* topp, const int64_t* dosample,
+                                       const float* gs, const float* q, float* dbg, const int64_t* forced,
+                                       void* stream) {
+  FB_CHECK_ARG(c, "dd_frame_noalloc: null config");
+  const DDLayout Lo = dd_layout(c);
+  FB_CHECK_ARG(Lo.total <= (size_t)FB_DD_NOALLOC_SCRATCH_BYTES,
+               "dd_frame_noalloc: this configuration needs %zu bytes of scratch; the built-in area holds %u "
+               "(use flashb_dd_frame with a caller-owned buffer)", Lo.total, (unsigned)FB_DD_NOALLOC_SCRATCH_BYTES);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    fbh::set_msg("dd_frame_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return FB_ERR_CUDA;
+  }
+  FB_CHECK_ARG(dev >= 0 && dev < 64, "dd_frame_noalloc: device ordinal %d out of range", dev);
+  void* base = nullptr;
+  {
+    // one-time set-up per device, with that device current: the device address of the static area
+    std::lock_guard<std::mutex> lk(g_dd_static_mu);
+    if (!g_dd_static_ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_dd_static_scratch);
+      if (e != cudaSuccess || !p) {
+        fbh::set_msg("dd_frame_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        return FB_ERR_CUDA;
+      }
+      g_dd_static_ptr[dev] = p;
+    }
+    base = g_dd_static_ptr[dev];
+  }
+  // The area keeps whatever the previous call left.  Only the grid-barrier words must start at zero (a frame cut
+  // short by a timeout leaves its abort flag set); everything else a frame reads it first writes itself.
+  e = cudaMemsetAsync((unsigned char*)base + Lo.bar, 0, sizeof(GridBar), (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    fbh::set_msg("dd_frame_noalloc: clearing the barrier words: %s", cudaGetErrorString(e));
+    return FB_ERR_CUDA;
+  }
+  return flashb_dd_frame(c, layers_dev, base, first_cb, bh, tokbuf, outtok, temp, topk, topp, dosample, gs, q, dbg,
+                         forced, stream);
 }

@@ -53,6 +53,7 @@ _PROTOS = {
     'flashb_dd_scratch_bytes': (L, [P]),
     'flashb_dd_layer_bytes': (L, []),
     'flashb_dd_frame': (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
+    'flashb_dd_frame_noalloc': (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
 }
 
 

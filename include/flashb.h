@@ -186,6 +186,22 @@ int flashb_dd_frame(const fb_dd_config* cfg, const void* layers_dev, void* scrat
                     const float* topp, const int64_t* dosample, const float* gs, const float* q, float* dbg,
                     const int64_t* forced, void* stream);
 
+/* No counterpart in the reference.  flashb_dd_frame without a scratch argument, for callers that may not allocate
+ * device memory themselves: a host that reaches this library over a plain C FFI with no allocator of its own, or a
+ * serving loop that forbids cudaMalloc after start-up (it can block on the device and it can fail).  The scratch is
+ * instead a fixed area of FB_DD_NOALLOC_SCRATCH_BYTES (1 MiB) inside the library, reserved on every GPU that loads
+ * it until the process exits; configurations whose flashb_dd_scratch_bytes() exceeds it are rejected with
+ * FB_ERR_ARG.  Everything else is as for flashb_dd_frame; nothing is allocated and no allocating routine is called.
+ * The first call on a device looks up the area's device address (with that device current); make that first call
+ * before any stream capture.  Each call clears the area's barrier words on `stream` first; the rest of the area
+ * keeps the previous call's contents and needs no clearing.  All calls on a device share the one area: calls that
+ * can overlap on the GPU (different streams, no ordering between them) race and corrupt each other. */
+#define FB_DD_NOALLOC_SCRATCH_BYTES (1u << 20)
+int flashb_dd_frame_noalloc(const fb_dd_config* cfg, const void* layers_dev, const int64_t* first_cb, const void* bh,
+                            int64_t* tokbuf, int64_t* outtok, const float* temp, const int64_t* topk,
+                            const float* topp, const int64_t* dosample, const float* gs, const float* q, float* dbg,
+                            const int64_t* forced, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
