@@ -1,0 +1,386 @@
+// flashb: causal GQA prefill attention on the 5th-generation tensor cores (tcgen05, accumulators in TMEM).
+//
+// Replaces the backbone prefill attention of the reference (flash/prefill_attn.py:15-46, bz_prefill_attention, which
+// trims K/V/mask to the prefill length L and calls the eager transformers attention, UP/models/breeze.py:259-286):
+//     s = bf16(bf16(q k^T) * scaling) ; s = bf16(s + mask) ; p = bf16(softmax_fp32(s)) ; out = bf16(p v)
+// with q [B, NH, L, D], k/v [B, NKV, S, D] (GQA: q head h reads kv head h / (NH / NKV)), an additive mask
+// [B | 1, 1, L, S] (bf16 or fp32) and out [B, L, NH, D] (the eager transpose(1, 2)).
+//
+// One CTA per (128-query tile, q head, batch row); 128 threads, thread r owns query row r (TMEM lane r).
+//   * Q, K and V tiles (128 x 128 bf16, 32 KB each) are staged with cp.async directly into the canonical
+//     no-swizzle UMMA layouts: Q and K K-major (8-row x 16-byte core matrices; LBO = 128 B between the two K
+//     chunks of an MMA, SBO = 2048 B between 8-row groups), V MN-major (8-key x 8-dim core matrices; LBO = 128 B
+//     between key groups, SBO = 2048 B between dim groups).  No tensor map is involved.
+//   * Thread 0 issues tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32, M = N = 128, K = 16 per
+//     instruction) and tcgen05.commit to an mbarrier; the others wait on it (bounded).
+//   * Pass 1: S = Q K^T per key tile into TMEM columns [0, 128); every thread reads its row (tcgen05.ld
+//     32x32b), applies the eager rounding points and the mask, and keeps the row max and the fp32 sum of
+//     exp(s - max) (rescaled when the max grows).
+//   * Pass 2: S again per tile; p = bf16(exp(s - max) / sum) exactly as the eager softmax forms it, written to
+//     shared memory as the K-major A operand; O += P V on tcgen05 into TMEM columns [128, 256).
+//   * Epilogue: O row -> bf16 -> out.  Rows whose every key is masked (left padding) are written as 0 (their
+//     outputs never reach a live row; the oracle uses the same convention).
+// With `causal` the key tiles entirely above the diagonal are skipped: the mask gives them probability exactly 0.
+#include "fb_common.cuh"
+
+namespace fb {
+
+constexpr int PF_TILE = 128;                       // queries per CTA = keys per tile = TMEM lanes
+constexpr int PF_D = 128;                          // head dim
+constexpr int PF_THREADS = 128;
+constexpr int PF_OPND = PF_TILE * PF_D * 2;        // 32 KB per operand tile
+constexpr int PF_SMEM = 4 * PF_OPND + 64;          // Q, K, V, P + two mbarriers + TMEM address slot
+constexpr uint32_t PF_TMEM_COLS = 256;             // S: columns [0, 128); O: columns [128, 256)
+
+struct PFArgs {
+  const bf16 *q, *k, *v;
+  long q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl;
+  const void* mask;
+  int mask_bf16;
+  long m_sb, m_sl;
+  bf16* out;
+  long o_sb, o_sl, o_sh;
+  int B, NH, NKV, L, S, h0, causal;
+  float scaling;
+  unsigned* err;
+};
+
+// Shared-memory matrix descriptor, no swizzle: start >> 4 in [0, 14), LBO >> 4 in [16, 30), SBO >> 4 in [32, 46),
+// descriptor version 1 in [46, 48), layout type 0 (none) in [61, 64).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor of kind::f16: D fp32 (bits 4-5 = 1), A bf16 (7-9 = 1), B bf16 (10-12 = 1), A K-major
+// (bit 15 = 0), B major given (bit 16), N >> 3 in [17, 23), M >> 4 in [24, 29); M = N = 128.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_128(uint32_t b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn_major << 16) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void cp_async16_pf(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all_pf() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp w reads lanes 32w .. 32w + 31).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&f)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]);
+}
+
+// Byte offset of 16-byte chunk c (elements 8c .. 8c+7 along K) of row r in a K-major no-swizzle tile of 128 x 128.
+__device__ __forceinline__ uint32_t kmaj_off(int r, int c) { return (((r >> 3) << 4) + c) * 128 + (r & 7) * 16; }
+// Byte offset of the 16-byte chunk (key j, dims 8g .. 8g+7) in the MN-major no-swizzle V tile.
+__device__ __forceinline__ uint32_t mnmaj_off(int j, int g) { return ((g << 4) + (j >> 3)) * 128 + (j & 7) * 16; }
+
+// Mask values of this thread's row for key columns [col0, col0 + 32) (absolute key index), or 0 without a mask.
+__device__ __forceinline__ void load_mask32(const PFArgs& a, int b, int row, int col0, float (&mv)[32]) {
+  if (!a.mask) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mv[i] = 0.f;
+    return;
+  }
+  if (a.mask_bf16) {
+    const bf16* p = reinterpret_cast<const bf16*>(a.mask) + (size_t)b * a.m_sb + (size_t)row * a.m_sl + col0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mv[i] = (col0 + i < a.S) ? b2f(p[i]) : 0.f;
+  } else {
+    const float* p = reinterpret_cast<const float*>(a.mask) + (size_t)b * a.m_sb + (size_t)row * a.m_sl + col0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mv[i] = (col0 + i < a.S) ? p[i] : 0.f;
+  }
+}
+
+__global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char* sq = smem;
+  unsigned char* sk = smem + PF_OPND;
+  unsigned char* sv = smem + 2 * PF_OPND;
+  unsigned char* sp = smem + 3 * PF_OPND;
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + 4 * PF_OPND);
+  uint64_t* bar_o = bar_s + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int q0 = blockIdx.x * PF_TILE, h = a.h0 + blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (a.NH / a.NKV);
+  const int row = q0 + tid;                       // this thread's query row
+  const bool row_ok = row < a.L;
+
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
+                 "r"(PF_TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t t_s = tmem, t_o = tmem + 128;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+
+  // Q tile -> K-major A operand (rows beyond L are zero)
+  {
+    const bf16* qg = a.q + (size_t)b * a.q_sb + (size_t)h * a.q_sh;
+    for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
+      const int r = i >> 4, c = i & 15;
+      unsigned char* dst = sq + kmaj_off(r, c);
+      if (q0 + r < a.L) cp_async16_pf(dst, qg + (size_t)(q0 + r) * a.q_sl + c * 8);
+      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  const int ntile_all = (a.S + PF_TILE - 1) / PF_TILE;
+  int ntile = ntile_all;
+  if (a.causal) {
+    const int last_q = min(q0 + PF_TILE, a.L) - 1;
+    ntile = min(ntile_all, last_q / PF_TILE + 1);
+  }
+  const bf16* kg = a.k + (size_t)b * a.k_sb + (size_t)kvh * a.k_sh;
+  const bf16* vg = a.v + (size_t)b * a.v_sb + (size_t)kvh * a.v_sh;
+  const uint32_t idesc_s = umma_idesc_bf16_128(0u), idesc_o = umma_idesc_bf16_128(1u);
+  const uint32_t aq = smem_u32(sq), ak = smem_u32(sk), av = smem_u32(sv), ap = smem_u32(sp);
+  unsigned ph_s = 0, ph_o = 0;
+  float mx = -INFINITY, sum = 0.f;
+  bool fail = false;
+
+  auto stage_k = [&](int t) {
+    for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
+      const int j = i >> 4, c = i & 15, key = t * PF_TILE + j;
+      unsigned char* dst = sk + kmaj_off(j, c);
+      if (key < a.S) cp_async16_pf(dst, kg + (size_t)key * a.k_sl + c * 8);
+      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  auto stage_v = [&](int t) {
+    for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
+      const int j = i >> 4, g = i & 15, key = t * PF_TILE + j;
+      unsigned char* dst = sv + mnmaj_off(j, g);
+      if (key < a.S) cp_async16_pf(dst, vg + (size_t)key * a.v_sl + g * 8);
+      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  // S = Q K^T for the staged K tile: 8 MMAs of K = 16 (the A and B start addresses advance 256 B per step)
+  auto mma_s = [&]() {
+    cp_async_wait_all_pf();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int s = 0; s < PF_D / 16; ++s)
+        umma_bf16(t_s, umma_desc(aq + 256 * s, 128, 2048), umma_desc(ak + 256 * s, 128, 2048), idesc_s, s > 0);
+      umma_commit(bar_s);
+    }
+    const bool ok = mbar_wait(bar_s, ph_s, a.err);
+    ph_s ^= 1u;
+    if (__syncthreads_or(!ok)) return false;
+    tc_fence_after();
+    return true;
+  };
+  // score of key column (col0 + i) for this row, with the eager rounding points; -inf for keys that do not exist
+  auto scores32 = [&](int t, int c32, float (&sc)[32]) {
+    float acc[32], mv[32];
+    tmem_ld32(t_s + lane_off + c32 * 32, acc);
+    const int col0 = t * PF_TILE + c32 * 32;
+    load_mask32(a, b, row_ok ? row : 0, col0, mv);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float s = rbf(rbf(acc[i]) * a.scaling);
+      s = a.mask_bf16 ? rbf(s + mv[i]) : s + mv[i];
+      const bool exists = (col0 + i < a.S) && !(a.causal && !a.mask && col0 + i > row);
+      sc[i] = exists ? s : -INFINITY;
+    }
+  };
+
+  // ---------------------------------------------------------------- pass 1: row max and sum of exp
+  for (int t = 0; t < ntile && !fail; ++t) {
+    stage_k(t);
+    if (!mma_s()) {
+      fail = true;
+      break;
+    }
+#pragma unroll 1
+    for (int c32 = 0; c32 < 4; ++c32) {
+      float sc[32];
+      scores32(t, c32, sc);
+      float tm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) tm = fmaxf(tm, sc[i]);
+      const float nm = fmaxf(mx, tm);
+      if (nm > -INFINITY) {
+        float add = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) add += expf(sc[i] - nm);
+        sum = (mx > -INFINITY ? sum * expf(mx - nm) : 0.f) + add;
+        mx = nm;
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  const bool dead = !(mx > -1e30f);
+
+  // ---------------------------------------------------------------- pass 2: P = softmax, O += P V
+  for (int t = 0; t < ntile && !fail; ++t) {
+    if (t > 0) {                                   // the previous P V must be done before K, V, P are replaced
+      const bool ok = mbar_wait(bar_o, ph_o, a.err);
+      ph_o ^= 1u;
+      if (__syncthreads_or(!ok)) {
+        fail = true;
+        break;
+      }
+    }
+    stage_k(t);
+    stage_v(t);
+    if (!mma_s()) {
+      fail = true;
+      break;
+    }
+#pragma unroll 1
+    for (int c32 = 0; c32 < 4; ++c32) {
+      float sc[32];
+      scores32(t, c32, sc);
+      float p[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) p[i] = (dead || !row_ok) ? 0.f : rbf(expf(sc[i] - mx) / sum);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint4 w;
+        w.x = pack2(p[c * 8 + 0], p[c * 8 + 1]);
+        w.y = pack2(p[c * 8 + 2], p[c * 8 + 3]);
+        w.z = pack2(p[c * 8 + 4], p[c * 8 + 5]);
+        w.w = pack2(p[c * 8 + 6], p[c * 8 + 7]);
+        *reinterpret_cast<uint4*>(sp + kmaj_off(tid, c32 * 4 + c)) = w;
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int s = 0; s < PF_TILE / 16; ++s)
+        umma_bf16(t_o, umma_desc(ap + 256 * s, 128, 2048), umma_desc(av + 256 * s, 128, 2048), idesc_o,
+                  (t > 0 || s > 0) ? 1u : 0u);
+      umma_commit(bar_o);
+    }
+  }
+  if (!fail && ntile > 0) {
+    const bool ok = mbar_wait(bar_o, ph_o, a.err);
+    if (__syncthreads_or(!ok)) fail = true;
+    tc_fence_after();
+  }
+
+  // ---------------------------------------------------------------- epilogue: O -> bf16 -> out [B, L, NH, D]
+  if (!fail) {
+    bf16* og = a.out + (size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)(row_ok ? row : 0) * a.o_sl;
+#pragma unroll 1
+    for (int c32 = 0; c32 < 4; ++c32) {
+      float o[32];
+      if (ntile > 0) tmem_ld32(t_o + lane_off + c32 * 32, o);
+      if (row_ok) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 w;
+          const float* f = o + c * 8;
+          const bool z = dead || ntile == 0;
+          w.x = z ? 0u : pack2(f[0], f[1]);
+          w.y = z ? 0u : pack2(f[2], f[3]);
+          w.z = z ? 0u : pack2(f[4], f[5]);
+          w.w = z ? 0u : pack2(f[6], f[7]);
+          *reinterpret_cast<uint4*>(og + c32 * 32 + c * 8) = w;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_TMEM_COLS) : "memory");
+  }
+}
+
+}  // namespace fb
+
+// ------------------------------------------------------------------------------------------------ host API
+using namespace fb;
+
+extern "C" int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl, const void* k,
+                                   int64_t k_sb, int64_t k_sh, int64_t k_sl, const void* v, int64_t v_sb,
+                                   int64_t v_sh, int64_t v_sl, const void* mask, int mask_is_bf16, int64_t m_sb,
+                                   int64_t m_sl, int B, int NH, int NKV, int L, int S, int D, float scaling,
+                                   int causal, int h0, int h1, void* out, int64_t o_sb, int64_t o_sl, int64_t o_sh,
+                                   void* stream) {
+  FB_CHECK_ARG(q && k && v && out, "prefill_attn: null pointer argument");
+  FB_CHECK_ARG(D == PF_D, "prefill_attn: head_dim must be 128 (got %d)", D);
+  FB_CHECK_ARG(B >= 1 && NH >= 1 && NKV >= 1 && NH % NKV == 0 && L >= 1 && S >= 1 && L <= 65535 * PF_TILE,
+               "prefill_attn: bad shape B=%d NH=%d NKV=%d L=%d S=%d", B, NH, NKV, L, S);
+  FB_CHECK_ARG(0 <= h0 && h0 < h1 && h1 <= NH, "prefill_attn: head range [%d, %d) outside [0, %d)", h0, h1, NH);
+  const uintptr_t align = (uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out;
+  const int64_t strides = q_sb | q_sh | q_sl | k_sb | k_sh | k_sl | v_sb | v_sh | v_sl | o_sb | o_sl | o_sh;
+  FB_CHECK_ARG((align & 15) == 0 && (strides & 7) == 0,
+               "prefill_attn: q/k/v/out must be 16-byte aligned with strides that are multiples of 8 elements");
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+    if (e != cudaSuccess) {
+      fbh::set_msg("prefill_attn: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return FB_ERR_CUDA;
+    }
+    attr_done[dev] = 1;
+  }
+  PFArgs a{};
+  a.q = (const bf16*)q; a.k = (const bf16*)k; a.v = (const bf16*)v;
+  a.q_sb = (long)q_sb; a.q_sh = (long)q_sh; a.q_sl = (long)q_sl;
+  a.k_sb = (long)k_sb; a.k_sh = (long)k_sh; a.k_sl = (long)k_sl;
+  a.v_sb = (long)v_sb; a.v_sh = (long)v_sh; a.v_sl = (long)v_sl;
+  a.mask = mask; a.mask_bf16 = mask_is_bf16; a.m_sb = (long)m_sb; a.m_sl = (long)m_sl;
+  a.out = (bf16*)out; a.o_sb = (long)o_sb; a.o_sl = (long)o_sl; a.o_sh = (long)o_sh;
+  a.B = B; a.NH = NH; a.NKV = NKV; a.L = L; a.S = S; a.h0 = h0; a.causal = causal; a.scaling = scaling;
+  a.err = fbh::device_err_ptr();
+  void* args[] = {(void*)&a};
+  const dim3 grid((L + PF_TILE - 1) / PF_TILE, h1 - h0, B);
+  cudaError_t e = cudaLaunchKernel((const void*)prefill_attn_kernel, grid, dim3(PF_THREADS), args, PF_SMEM,
+                                   (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    fbh::set_msg("prefill_attn launch: %s", cudaGetErrorString(e));
+    return FB_ERR_CUDA;
+  }
+  return FB_OK;
+}

@@ -50,6 +50,8 @@ _PROTOS = {
     'flashb_bb_step': (I, [P, P, P, P, P, P, P, I, L, P, I, P, P, P, P]),
     'flashb_cb0_greedy': (I, [P, L, I, I, I, P, P]),
     'flashb_frame_ids': (I, [P, P, I, I, I, P, P]),
+    'flashb_prefill_attn': (I, [P, L, L, L, P, L, L, L, P, L, L, L, P, I, L, L, I, I, I, I, I, I, F, I, I, I, P, L, L,
+                                L, P]),
     'flashb_dd_scratch_bytes': (L, [P]),
     'flashb_dd_layer_bytes': (L, []),
     'flashb_dd_frame': (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),

@@ -253,7 +253,7 @@ class SyntheticDepth:
 
 
 class _StreamState:
-    __slots__ = ('bb', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph')
+    __slots__ = ('bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph')
 
 
 class FrameEngine:
@@ -272,7 +272,9 @@ class FrameEngine:
     Each stream starts after a ``prompt_len``-token prompt whose KV cache is random (the prefill stand-in)."""
 
     def __init__(self, bcfg: BackboneConfig, dcfg: DepthConfig, n_streams, prompt_len, max_frames, device='cuda',
-                 seed=0):
+                 seed=0, depth_only=False):
+        """``depth_only``: no backbone (a random hidden state per stream feeds the depth frame) -- for timing or
+        profiling the depth frame alone on a small device footprint."""
         if bcfg.codebooks - 1 > dcfg.n_decode or dcfg.embed_dim != bcfg.hidden:
             raise ValueError('backbone codebooks must be <= 1 + depth codebooks and depth embed_dim == backbone hidden')
         self.bcfg, self.dcfg = bcfg, dcfg
@@ -286,10 +288,15 @@ class FrameEngine:
         g = torch.Generator(device='cpu').manual_seed(seed + 17)
         for i in range(n_streams):
             st = _StreamState()
-            st.bb = SyntheticBackboneGraph(bcfg, 2, S, dev, seed=seed + 2, weights_from=first)
-            first = first or st.bb
-            st.bb.fill_kv(prompt_len, seed=1000 + seed + i)
-            st.bb.set_position(prompt_len - 1)
+            if depth_only:
+                st.bb = None
+                st.bh = torch.randn(2, dcfg.embed_dim, generator=g).to(torch.bfloat16).to(dev)
+            else:
+                st.bb = SyntheticBackboneGraph(bcfg, 2, S, dev, seed=seed + 2, weights_from=first)
+                first = first or st.bb
+                st.bb.fill_kv(prompt_len, seed=1000 + seed + i)
+                st.bb.set_position(prompt_len - 1)
+                st.bh = st.bb.hidden_buf.view(2, -1)
             st.first_cb = torch.randint(0, self.n_valid, (1,), generator=g).repeat(2).to(dev)
             st.outtok = torch.randint(0, dcfg.codebook_size, (1, dcfg.n_decode), generator=g).repeat(2, 1).to(dev)
             st.tokbuf = torch.zeros(2, dtype=torch.long, device=dev)
@@ -310,12 +317,16 @@ class FrameEngine:
 
     def depth_part(self, i):
         st, d = self.streams[i], self.depth
-        d.desc.frame(st.first_cb, st.bb.hidden_buf.view(2, -1), st.tokbuf, st.outtok, d.temperature, d.top_k,
-                     d.top_p, d.do_sample, d.guidance_scale, st.q)
+        d.desc.frame(st.first_cb, st.bh, st.tokbuf, st.outtok, d.temperature, d.top_k, d.top_p, d.do_sample,
+                     d.guidance_scale, st.q)
 
     def capture(self):
         """One CUDA graph per stream for its backbone part.  Stream 0 first runs one eager frame (kernel attributes
-        are set on first use), then its position is put back."""
+        are set on first use), then its position is put back.  Nothing to capture without a backbone."""
+        if self.streams[0].bb is None:
+            self.depth_part(0)
+            torch.cuda.synchronize(self.device)
+            return
         self.backbone_part(0)
         self.depth_part(0)
         torch.cuda.synchronize(self.device)
@@ -333,7 +344,9 @@ class FrameEngine:
 
     def frame(self, i):
         st = self.streams[i]
-        if st.graph is not None:
+        if st.bb is None:
+            pass
+        elif st.graph is not None:
             st.graph.replay()
         else:
             self.backbone_part(i)
@@ -344,6 +357,8 @@ class FrameEngine:
 
     def frame_bytes(self):
         """Algorithmic HBM bytes of one frame at the current mean KV length: backbone step + 16 depth steps."""
+        if self.streams[0].bb is None:
+            return self.dcfg.n_decode * self.dcfg.step_weight_bytes()
         kv = int(self.streams[0].bb.cache_position.item()) + 1
         return backbone_step_bytes(self.bcfg, 2, kv) + self.dcfg.n_decode * self.dcfg.step_weight_bytes()
 

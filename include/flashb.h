@@ -116,6 +116,21 @@ int flashb_cb0_greedy(const float* cfg_logits, int64_t ld, int half, int n_valid
 int flashb_frame_ids(const int64_t* first_cb, const int64_t* depth_tok, int n_decode, int B, int C, int64_t* ids,
                      void* stream);
 
+/* Replaces the backbone prefill attention (flash/prefill_attn.py:15-46 bz_prefill_attention -> the eager
+ * transformers attention, UP/models/breeze.py:259-286) with a tcgen05 kernel: causal GQA attention of
+ * q [B, NH, L, 128] over k/v [B, NKV, S, 128] (bf16; strides per batch / head / position in elements, multiples of
+ * 8, 16-byte aligned base) with the eager rounding points s = bf16(bf16(q k^T) * scaling), s = bf16(s + mask),
+ * p = bf16(softmax_fp32(s)), out = bf16(p v).  mask: additive [B | 1, 1, L, S] (bf16 if mask_is_bf16, else fp32;
+ * m_sb = 0 broadcasts one mask), or NULL.  causal != 0 promises that every key j > i is masked for query i (the
+ * reference's prefill mask), so key tiles above the diagonal are skipped (they carry probability exactly 0).
+ * Computes q heads [h0, h1) only (a head-group shard); out [B, L, NH, 128] bf16 with strides o_sb, o_sl, o_sh.
+ * Rows whose every key is masked are written as 0. */
+int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl, const void* k, int64_t k_sb,
+                        int64_t k_sh, int64_t k_sl, const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sl,
+                        const void* mask, int mask_is_bf16, int64_t m_sb, int64_t m_sl, int B, int NH, int NKV, int L,
+                        int S, int D, float scaling, int causal, int h0, int h1, void* out, int64_t o_sb,
+                        int64_t o_sl, int64_t o_sh, void* stream);
+
 /* ---------------------------------------------------------------------------------------------- whole backbone step
  * One cooperative launch per decode step (one CTA per SM) replaces the reference's per-step sequence of 28 x 5 kernels
  * plus eager ops (flash/backbone.py:106-138 fused_decode_step inside UP/models/cudagraph/backbone_graph.py:254-285

@@ -140,3 +140,24 @@ def test_fb_exp_accuracy():
     ulp = np.spacing(ref[ok].astype(np.float32)).astype(np.float64)
     assert np.max(np.abs(y[ok] - ref[ok]) / ulp) <= 2.0
     assert smp.fb_exp(np.array([-np.inf, -200.0], np.float32)).tolist() == [0.0, 0.0]
+
+
+def test_prefill_trim_rule_changes_nothing():
+    """The reference trims K/V/mask to the prefill length when the mask covers a longer static cache; slots >= L
+    are masked with finfo.min, so the untrimmed eager result is identical on live rows."""
+    import torch
+    from oracle import prefill as opf
+    q, k, v, m = synth.prefill_inputs()
+    c = synth.PREFILL
+    L, pad = c['L'], 24
+    kp = torch.cat([k, torch.randn(c['B'], c['NKV'], pad, c['D']).to(k.dtype)], 2)
+    vp = torch.cat([v, torch.randn(c['B'], c['NKV'], pad, c['D']).to(v.dtype)], 2)
+    mp = torch.cat([m, torch.full((c['B'], 1, L, pad), torch.finfo(torch.bfloat16).min, dtype=m.dtype)], 3)
+    kt, vt, mt = opf.trim(ft(q), ft(kp), ft(vp), ft(mp))
+    assert kt.shape[2] == L and mt.shape[-1] == L
+    a = opf.prefill_attention(ft(q), ft(kp), ft(vp), ft(mp), c['D'] ** -0.5)
+    b = dec.attention_eager(ft(q), ft(kp), ft(vp), ft(mp), c['D'] ** -0.5)
+    live = np.ones(a.shape[:2], bool)
+    for bb, p in enumerate(c['pad']):
+        live[bb, :p] = False
+    assert np.array_equal(a[live], b[live])

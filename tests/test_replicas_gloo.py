@@ -80,3 +80,49 @@ def test_streams_for_rank_rejects_bad_rank():
     with pytest.raises(ValueError):
         replicas.streams_for_rank(8, 2, 2)
     assert replicas.streams_for_rank(5, 1, 4) == [1]
+
+
+def _prefill_worker(rank, world, port, out):
+    """Two CPU ranks: each computes its KV-head group's q heads with the oracle (the stand-in for the kernel on a
+    GPU rank) and the shards are gathered with flashb.prefill_attn.gather_head_shards."""
+    sys.path.insert(0, PKG)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from flashb import prefill_attn
+    from oracle import prefill as opf
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        g = torch.Generator().manual_seed(3)
+        B, NH, NKV, L = 1, 8, 2, 24
+        q = torch.randn(B, NH, L, 128, generator=g).to(torch.bfloat16).float().numpy()
+        k = torch.randn(B, NKV, L, 128, generator=g).to(torch.bfloat16).float().numpy()
+        v = torch.randn(B, NKV, L, 128, generator=g).to(torch.bfloat16).float().numpy()
+        mask = np.where(np.arange(L)[None, :] <= np.arange(L)[:, None], 0.0, -3.3895313892515355e38)
+        mask = mask.astype(np.float32)[None, None]
+        h0, h1 = prefill_attn.shard_heads(NH, NKV, world, rank)
+        G = NH // NKV
+        kv0, kv1 = h0 // G, h1 // G
+        part = opf.prefill_attention(q[:, h0:h1], k[:, kv0:kv1], v[:, kv0:kv1], mask, 128 ** -0.5)
+        full = prefill_attn.gather_head_shards(torch.from_numpy(np.ascontiguousarray(part)))
+        ref = opf.prefill_attention(q, k, v, mask, 128 ** -0.5)
+        out.put((rank, bool(np.array_equal(full.numpy(), ref)), (h0, h1)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_prefill_head_shards_gather_to_the_full_output():
+    ctx = mp.get_context('spawn')
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_prefill_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert [p.exitcode for p in procs] == [0, 0]
+    res = sorted(q.get() for _ in range(2))
+    assert res == [(0, True, (0, 4)), (1, True, (4, 8))]
