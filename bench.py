@@ -31,9 +31,10 @@ sys.path[:0] = [HERE, os.path.join(HERE, 'breeze-tts-2-flash_b200')]
 N_STREAMS = 64
 PROMPT = 512
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0)
-# dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch (ncu, small-case capture of the same
-# full-size depth model; see profiles/dd_frame_kernel_depth_frame.md).  None until captured.
-DD_TRAFFIC_BYTES = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch: ncu --set full capture of the same
+# full-size depth model (bench.py --case depth), 2.097653 GB read + 30.227456 MB written; profiles/ holds the summary.
+DD_TRAFFIC_BYTES = 2127880456
+PREFILL_CFG = dict(B=2, NH=16, NKV=4, L=512, D=128, pads=(0, 37))
 
 
 def args_():
@@ -44,7 +45,7 @@ def args_():
     p.add_argument('--impl', default='flashb', choices=['flashb', 'reference'])
     p.add_argument('--streams', type=int, default=N_STREAMS, help='streams over the whole job')
     p.add_argument('--prompt', type=int, default=PROMPT)
-    p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone'])
+    p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone', 'prefill'])
     p.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample length')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
@@ -176,6 +177,56 @@ def run_reference(a):
         e2e=dict(value=round(v, 4), unit='frames/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------ prefill
+def prefill_flops(B, NH, L, D):
+    """Algorithmic FLOPs of causal attention: q k^T and p v over the L (L + 1) / 2 admitted (query, key) pairs."""
+    return 4 * B * NH * D * L * (L + 1) // 2
+
+
+def measure_prefill(dev, world, rank, iters=50, warmup=5):
+    """Config 5's causal GQA prefill attention on the tcgen05 kernel, inputs resident.  With 2 or 4 ranks every
+    rank computes its KV-head group's q heads and one NCCL all-gather assembles the output; otherwise each rank
+    runs the whole call.  Returns the bench line's ``prefill`` object (rank 0) with TFLOP/s of the whole call."""
+    import torch
+    from flashb import prefill_attn, replicas
+    c = PREFILL_CFG
+    B, NH, NKV, L, D = c['B'], c['NH'], c['NKV'], c['L'], c['D']
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn(B, NH, L, D, generator=g).to(torch.bfloat16).to(dev)
+    k = torch.randn(B, NKV, L, D, generator=g).to(torch.bfloat16).to(dev)
+    v = torch.randn(B, NKV, L, D, generator=g).to(torch.bfloat16).to(dev)
+    qi, ki = torch.arange(L).view(L, 1), torch.arange(L).view(1, L)
+    m = torch.full((B, 1, L, L), torch.finfo(torch.bfloat16).min)
+    for b, p in enumerate(c['pads']):
+        m[b, 0].masked_fill_((ki <= qi) & (ki >= p), 0.0)
+    m = m.to(torch.bfloat16).to(dev)
+    sharded = world in (2, 4)
+
+    def call():
+        if sharded:
+            return prefill_attn.prefill_attention_sharded(q, k, v, m, D ** -0.5)
+        return prefill_attn.prefill_attention(q, k, v, m, D ** -0.5)
+
+    for _ in range(warmup):
+        call()
+    replicas.barrier(dev)
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(iters):
+        call()
+    e1.record(st)
+    replicas.barrier(dev)
+    ms = replicas.max_over_ranks(e0.elapsed_time(e1) / iters, dev)
+    fl = prefill_flops(B, NH, L, D)
+    peak = peaks()['bf16_tflops']
+    ach = fl / (ms / 1e3) / 1e12
+    return dict(kernel='prefill_attn_kernel (tcgen05)', config=f'B={B} L={L} NH={NH} NKV={NKV} D={D} causal, pads '
+                f'{list(c["pads"])}', parallel='KV-head groups + NCCL all-gather' if sharded else 'whole call per rank',
+                ms=round(ms, 4), algorithmic_flops=fl, achieved=round(ach, 2), unit='TFLOP/s', bound='tensor',
+                peak=peak, frac=round(ach / peak, 4), launches_per_call=1 + (1 if sharded else 0))
+
+
 # ------------------------------------------------------------------------------------------------ GPU
 def main():
     a = args_()
@@ -194,12 +245,27 @@ def main():
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
     from flashb import replicas
     from flashb.engine import BackboneConfig, DepthConfig, FrameEngine, backbone_step_bytes
+    if a.case == 'prefill':
+        pf = measure_prefill(dev, world, rank, iters=a.steps, warmup=max(3, a.warmup))
+        if rank == 0:
+            print(json.dumps(dict(metric='prefill TFLOP/s', value=pf['achieved'], unit='TFLOP/s', n_gpus=world,
+                                  steps=a.steps, warmup=a.warmup, ms_per_step=pf['ms'], higher_is_better=True,
+                                  scaling='strong', vs_baseline=None, dtype='bf16', data='synthetic',
+                                  config=dict(workload='causal GQA prefill attention, ' + pf['config']),
+                                  roofline=dict(bound='tensor', achieved=pf['achieved'], peak=pf['peak'],
+                                                unit='TFLOP/s', frac=pf['frac'], traffic=None),
+                                  gpu_launches=a.steps * pf['launches_per_call'])), flush=True)
+        if world > 1:
+            replicas.barrier(dev)
+            dist.destroy_process_group()
+        return
     bcfg = BackboneConfig(codebooks=17)
     dcfg = DepthConfig()
     my_streams = len(replicas.streams_for_rank(a.streams, rank, world))
     total_steps = a.warmup + a.steps
     n_runs = 1 if a.no_e2e else 2
-    eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + 1, device=dev, seed=0)
+    eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + 1, device=dev, seed=0,
+                      depth_only=(a.case == 'depth'))
     eng.capture()
     stream = torch.cuda.current_stream(dev)
 
@@ -235,7 +301,7 @@ def main():
     # ---- device-resident run
     for _ in range(a.warmup):
         one_step(None)
-    kv0 = int(eng.streams[0].bb.cache_position.item()) + 1
+    kv0 = int(eng.streams[0].bb.cache_position.item()) + 1 if eng.streams[0].bb is not None else 0
     gpu_ids = [int(x) for x in os.environ['CUDA_VISIBLE_DEVICES'].split(',')] \
         if os.environ.get('CUDA_VISIBLE_DEVICES', '').replace(',', '').isdigit() else list(range(world))
     clocks = Clocks(gpu_ids[:world]) if rank == 0 else None
@@ -268,7 +334,7 @@ def main():
                 dd_ms.append(marks[j].elapsed_time(marks[j + 1]))
             k += per
         k += 1
-    kv1 = int(eng.streams[0].bb.cache_position.item()) + 1
+    kv1 = int(eng.streams[0].bb.cache_position.item()) + 1 if eng.streams[0].bb is not None else 0
     pk = peaks()
     dd_bytes = dcfg.n_decode * dcfg.step_weight_bytes()
     bb_bytes = backbone_step_bytes(bcfg, 2, (kv0 + kv1) // 2)
@@ -331,6 +397,7 @@ def main():
                    sample=f'{n} frames of one stream ({el:.1f} s after 1 warm-up frame): numpy/C oracle port of '
                           f'backbone step (KV {a.prompt}+t) + 16-codebook depth frame, {threads} BLAS threads')
 
+    prefill = measure_prefill(dev, world, rank) if case == 'frame' else None
     launches = eng.launches_per_frame() if case == 'frame' else (
         1 if case == 'depth' else eng.launches_per_frame() - 1)
     if rank == 0:
@@ -348,7 +415,7 @@ def main():
                            'codebook step; no flush', cb0='greedy (backbone sampler do_sample=False)',
                         prefill='not timed (random prompt KV)'),
             frames_per_s_per_gpu=round(value / world, 3), tokens_per_s=round(value * 17, 1),
-            roofline=roof, roofline_backbone=roof_bb, cpu_baseline=cpu, e2e=e2e,
+            roofline=roof, roofline_backbone=roof_bb, prefill=prefill, cpu_baseline=cpu, e2e=e2e,
             gpu_launches=int(launches * frames), clocks=clk)
         print(json.dumps(line), flush=True)
     if world > 1:

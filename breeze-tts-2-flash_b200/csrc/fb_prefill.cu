@@ -6,16 +6,17 @@
 // with q [B, NH, L, D], k/v [B, NKV, S, D] (GQA: q head h reads kv head h / (NH / NKV)), an additive mask
 // [B | 1, 1, L, S] (bf16 or fp32) and out [B, L, NH, D] (the eager transpose(1, 2)).
 //
-// One CTA per (128-query tile, q head, batch row); 128 threads, thread r owns query row r (TMEM lane r).
+// One CTA per (128-query tile, q head, batch row); 16 warps: warp w reads TMEM lanes 32 (w % 4) .. (query rows) and
+// owns key / output columns [32 (w / 4), 32 (w / 4) + 32) of every tile, so four threads share a row.
 //   * Q, K and V tiles (128 x 128 bf16, 32 KB each) are staged with cp.async directly into the canonical
 //     no-swizzle UMMA layouts: Q and K K-major (8-row x 16-byte core matrices; LBO = 128 B between the two K
 //     chunks of an MMA, SBO = 2048 B between 8-row groups), V MN-major (8-key x 8-dim core matrices; LBO = 128 B
 //     between key groups, SBO = 2048 B between dim groups).  No tensor map is involved.
 //   * Thread 0 issues tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32, M = N = 128, K = 16 per
 //     instruction) and tcgen05.commit to an mbarrier; the others wait on it (bounded).
-//   * Pass 1: S = Q K^T per key tile into TMEM columns [0, 128); every thread reads its row (tcgen05.ld
-//     32x32b), applies the eager rounding points and the mask, and keeps the row max and the fp32 sum of
-//     exp(s - max) (rescaled when the max grows).
+//   * Pass 1: S = Q K^T per key tile into TMEM columns [0, 128); every thread reads its 32 scores (tcgen05.ld
+//     32x32b), applies the eager rounding points and the mask, and keeps a running max and fp32 sum of
+//     exp(s - max) (rescaled when the max grows); the four quarters of a row are merged after the pass.
 //   * Pass 2: S again per tile; p = bf16(exp(s - max) / sum) exactly as the eager softmax forms it, written to
 //     shared memory as the K-major A operand; O += P V on tcgen05 into TMEM columns [128, 256).
 //   * Epilogue: O row -> bf16 -> out.  Rows whose every key is masked (left padding) are written as 0 (their
@@ -27,9 +28,12 @@ namespace fb {
 
 constexpr int PF_TILE = 128;                       // queries per CTA = keys per tile = TMEM lanes
 constexpr int PF_D = 128;                          // head dim
-constexpr int PF_THREADS = 128;
+constexpr int PF_QUARTERS = 4;                     // column quarters per row (one warp per lane quarter each)
+constexpr int PF_THREADS = 128 * PF_QUARTERS;     // 16 warps
 constexpr int PF_OPND = PF_TILE * PF_D * 2;        // 32 KB per operand tile
-constexpr int PF_SMEM = 4 * PF_OPND + 64;          // Q, K, V, P + two mbarriers + TMEM address slot
+constexpr int PF_MPITCH = PF_TILE * 2 + 16;       // bytes per staged bf16 mask row (padded: fewer bank conflicts)
+constexpr int PF_MASK = PF_TILE * PF_MPITCH;       // the bf16 mask tile of the current key tile
+constexpr int PF_SMEM = 4 * PF_OPND + PF_MASK + 64;  // Q, K, V, P, mask + two mbarriers + TMEM address slot
 constexpr uint32_t PF_TMEM_COLS = 256;             // S: columns [0, 128); O: columns [128, 256)
 
 struct PFArgs {
@@ -99,17 +103,41 @@ __device__ __forceinline__ uint32_t kmaj_off(int r, int c) { return (((r >> 3) <
 // Byte offset of the 16-byte chunk (key j, dims 8g .. 8g+7) in the MN-major no-swizzle V tile.
 __device__ __forceinline__ uint32_t mnmaj_off(int j, int g) { return ((g << 4) + (j >> 3)) * 128 + (j & 7) * 16; }
 
+// Stage the bf16 mask tile of key tile t (rows q0.., columns 128 t..) into smem rows of PF_MPITCH bytes: 16-byte
+// cp.async chunks where aligned and in range, element loads at ragged edges.
+__device__ __forceinline__ void stage_mask(const PFArgs& a, int b, int q0, int t, unsigned char* sm) {
+  const bf16* mb = reinterpret_cast<const bf16*>(a.mask) + (size_t)b * a.m_sb;
+  for (int i = threadIdx.x; i < PF_TILE * 16; i += PF_THREADS) {
+    const int r = i >> 4, c = i & 15, row = q0 + r, col = t * PF_TILE + c * 8;
+    unsigned char* dst = sm + r * PF_MPITCH + c * 16;
+    const bf16* src = mb + (size_t)(row < a.L ? row : 0) * a.m_sl + col;
+    if (row < a.L && col + 8 <= a.S && (((uintptr_t)src) & 15) == 0) {
+      cp_async16_pf(dst, src);
+    } else {
+      bf16* d = reinterpret_cast<bf16*>(dst);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d[e] = (row < a.L && col + e < a.S) ? src[e] : __float2bfloat16_rn(0.f);
+    }
+  }
+}
+
 // Mask values of this thread's row for key columns [col0, col0 + 32) (absolute key index), or 0 without a mask.
-__device__ __forceinline__ void load_mask32(const PFArgs& a, int b, int row, int col0, float (&mv)[32]) {
+// bf16 masks come from the staged tile (`srow` = this thread's row, `c0` = column offset in the tile).
+__device__ __forceinline__ void load_mask32(const PFArgs& a, int b, int row, int col0, const unsigned char* srow,
+                                            int c0, float (&mv)[32]) {
   if (!a.mask) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) mv[i] = 0.f;
     return;
   }
   if (a.mask_bf16) {
-    const bf16* p = reinterpret_cast<const bf16*>(a.mask) + (size_t)b * a.m_sb + (size_t)row * a.m_sl + col0;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mv[i] = (col0 + i < a.S) ? b2f(p[i]) : 0.f;
+    for (int c = 0; c < 4; ++c) {
+      float f[8];
+      cvt8(*reinterpret_cast<const uint4*>(srow + (c0 + c * 8) * 2), f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mv[c * 8 + e] = f[e];
+    }
   } else {
     const float* p = reinterpret_cast<const float*>(a.mask) + (size_t)b * a.m_sb + (size_t)row * a.m_sl + col0;
 #pragma unroll
@@ -123,14 +151,18 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   unsigned char* sk = smem + PF_OPND;
   unsigned char* sv = smem + 2 * PF_OPND;
   unsigned char* sp = smem + 3 * PF_OPND;
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + 4 * PF_OPND);
+  unsigned char* sm = smem + 4 * PF_OPND;
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + 4 * PF_OPND + PF_MASK);
   uint64_t* bar_o = bar_s + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 2);
+  __shared__ float s_stat[2][PF_QUARTERS][PF_TILE];   // per (column quarter, row): running max, sum
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // TMEM lane quarter (warp % 4) x column quarter (warp / 4): this thread owns row r, columns [32 cq, 32 cq + 32)
+  const int r = (warp & 3) * 32 + lane, cq = warp >> 2;
   const int q0 = blockIdx.x * PF_TILE, h = a.h0 + blockIdx.y, b = blockIdx.z;
   const int kvh = h / (a.NH / a.NKV);
-  const int row = q0 + tid;                       // this thread's query row
+  const int row = q0 + r;
   const bool row_ok = row < a.L;
 
   if (tid == 0) {
@@ -149,15 +181,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   tc_fence_after();
   const uint32_t tmem = *tslot;
   const uint32_t t_s = tmem, t_o = tmem + 128;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t my_taddr = ((uint32_t)((warp & 3) * 32) << 16) + cq * 32;
 
   // Q tile -> K-major A operand (rows beyond L are zero)
   {
     const bf16* qg = a.q + (size_t)b * a.q_sb + (size_t)h * a.q_sh;
     for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
-      const int r = i >> 4, c = i & 15;
-      unsigned char* dst = sq + kmaj_off(r, c);
-      if (q0 + r < a.L) cp_async16_pf(dst, qg + (size_t)(q0 + r) * a.q_sl + c * 8);
+      const int rr = i >> 4, c = i & 15;
+      unsigned char* dst = sq + kmaj_off(rr, c);
+      if (q0 + rr < a.L) cp_async16_pf(dst, qg + (size_t)(q0 + rr) * a.q_sl + c * 8);
       else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
     }
   }
@@ -174,8 +206,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   unsigned ph_s = 0, ph_o = 0;
   float mx = -INFINITY, sum = 0.f;
   bool fail = false;
+  const bool mask_smem = a.mask && a.mask_bf16;
 
   auto stage_k = [&](int t) {
+    if (mask_smem) stage_mask(a, b, q0, t, sm);
     for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
       const int j = i >> 4, c = i & 15, key = t * PF_TILE + j;
       unsigned char* dst = sk + kmaj_off(j, c);
@@ -210,12 +244,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     tc_fence_after();
     return true;
   };
-  // score of key column (col0 + i) for this row, with the eager rounding points; -inf for keys that do not exist
-  auto scores32 = [&](int t, int c32, float (&sc)[32]) {
+  // this thread's 32 scores of key tile t with the eager rounding points; -inf for keys that do not exist
+  auto scores32 = [&](int t, float (&sc)[32]) {
     float acc[32], mv[32];
-    tmem_ld32(t_s + lane_off + c32 * 32, acc);
-    const int col0 = t * PF_TILE + c32 * 32;
-    load_mask32(a, b, row_ok ? row : 0, col0, mv);
+    tmem_ld32(t_s + my_taddr, acc);
+    const int col0 = t * PF_TILE + cq * 32;
+    load_mask32(a, b, row_ok ? row : 0, col0, sm + r * PF_MPITCH, cq * 32, mv);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       float s = rbf(rbf(acc[i]) * a.scaling);
@@ -232,24 +266,40 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       fail = true;
       break;
     }
-#pragma unroll 1
-    for (int c32 = 0; c32 < 4; ++c32) {
-      float sc[32];
-      scores32(t, c32, sc);
-      float tm = -INFINITY;
+    float sc[32];
+    scores32(t, sc);
+    float tm = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) tm = fmaxf(tm, sc[i]);
-      const float nm = fmaxf(mx, tm);
-      if (nm > -INFINITY) {
-        float add = 0.f;
+    for (int i = 0; i < 32; ++i) tm = fmaxf(tm, sc[i]);
+    const float nm = fmaxf(mx, tm);
+    if (nm > -INFINITY) {
+      float add = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) add += expf(sc[i] - nm);
-        sum = (mx > -INFINITY ? sum * expf(mx - nm) : 0.f) + add;
-        mx = nm;
-      }
+      for (int i = 0; i < 32; ++i) add += expf(sc[i] - nm);
+      sum = (mx > -INFINITY ? sum * expf(mx - nm) : 0.f) + add;
+      mx = nm;
     }
     tc_fence_before();
     __syncthreads();
+  }
+  // merge the four column quarters of every row (the same result in all four threads of a row)
+  s_stat[0][cq][r] = mx;
+  s_stat[1][cq][r] = sum;
+  __syncthreads();
+  {
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < PF_QUARTERS; ++k) m = fmaxf(m, s_stat[0][k][r]);
+    float l = 0.f;
+    if (m > -INFINITY) {
+#pragma unroll
+      for (int k = 0; k < PF_QUARTERS; ++k) {
+        const float mk = s_stat[0][k][r];
+        if (mk > -INFINITY) l += s_stat[1][k][r] * expf(mk - m);
+      }
+    }
+    mx = m;
+    sum = l;
   }
   const bool dead = !(mx > -1e30f);
 
@@ -269,22 +319,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       fail = true;
       break;
     }
-#pragma unroll 1
-    for (int c32 = 0; c32 < 4; ++c32) {
-      float sc[32];
-      scores32(t, c32, sc);
-      float p[32];
+    float sc[32];
+    scores32(t, sc);
+    float p[32];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) p[i] = (dead || !row_ok) ? 0.f : rbf(expf(sc[i] - mx) / sum);
+    for (int i = 0; i < 32; ++i) p[i] = (dead || !row_ok) ? 0.f : rbf(expf(sc[i] - mx) / sum);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint4 w;
-        w.x = pack2(p[c * 8 + 0], p[c * 8 + 1]);
-        w.y = pack2(p[c * 8 + 2], p[c * 8 + 3]);
-        w.z = pack2(p[c * 8 + 4], p[c * 8 + 5]);
-        w.w = pack2(p[c * 8 + 6], p[c * 8 + 7]);
-        *reinterpret_cast<uint4*>(sp + kmaj_off(tid, c32 * 4 + c)) = w;
-      }
+    for (int c = 0; c < 4; ++c) {
+      uint4 w;
+      w.x = pack2(p[c * 8 + 0], p[c * 8 + 1]);
+      w.y = pack2(p[c * 8 + 2], p[c * 8 + 3]);
+      w.z = pack2(p[c * 8 + 4], p[c * 8 + 5]);
+      w.w = pack2(p[c * 8 + 6], p[c * 8 + 7]);
+      *reinterpret_cast<uint4*>(sp + kmaj_off(r, cq * 4 + c)) = w;
     }
     fence_async_smem();
     tc_fence_before();
@@ -306,23 +353,20 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
 
   // ---------------------------------------------------------------- epilogue: O -> bf16 -> out [B, L, NH, D]
   if (!fail) {
-    bf16* og = a.out + (size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)(row_ok ? row : 0) * a.o_sl;
-#pragma unroll 1
-    for (int c32 = 0; c32 < 4; ++c32) {
-      float o[32];
-      if (ntile > 0) tmem_ld32(t_o + lane_off + c32 * 32, o);
-      if (row_ok) {
+    float o[32];
+    if (ntile > 0) tmem_ld32(t_o + my_taddr, o);
+    if (row_ok) {
+      bf16* og = a.out + (size_t)b * a.o_sb + (size_t)h * a.o_sh + (size_t)row * a.o_sl + cq * 32;
+      const bool z = dead || ntile == 0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4 w;
-          const float* f = o + c * 8;
-          const bool z = dead || ntile == 0;
-          w.x = z ? 0u : pack2(f[0], f[1]);
-          w.y = z ? 0u : pack2(f[2], f[3]);
-          w.z = z ? 0u : pack2(f[4], f[5]);
-          w.w = z ? 0u : pack2(f[6], f[7]);
-          *reinterpret_cast<uint4*>(og + c32 * 32 + c * 8) = w;
-        }
+      for (int c = 0; c < 4; ++c) {
+        uint4 w;
+        const float* f = o + c * 8;
+        w.x = z ? 0u : pack2(f[0], f[1]);
+        w.y = z ? 0u : pack2(f[2], f[3]);
+        w.z = z ? 0u : pack2(f[4], f[5]);
+        w.w = z ? 0u : pack2(f[6], f[7]);
+        *reinterpret_cast<uint4*>(og + c * 8) = w;
       }
     }
   }
