@@ -46,6 +46,8 @@ def args_():
     p.add_argument('--streams', type=int, default=N_STREAMS, help='streams over the whole job')
     p.add_argument('--prompt', type=int, default=PROMPT)
     p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone', 'prefill'])
+    p.add_argument('--group', type=int, default=2, choices=[1, 2],
+                   help='streams decoded together per launch (their GEMV rows share every weight read)')
     p.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample length')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
@@ -264,8 +266,11 @@ def main():
     my_streams = len(replicas.streams_for_rank(a.streams, rank, world))
     total_steps = a.warmup + a.steps
     n_runs = 1 if a.no_e2e else 2
-    eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + 1, device=dev, seed=0,
-                      depth_only=(a.case == 'depth'))
+    if my_streams % a.group:
+        raise SystemExit(f'{my_streams} streams per rank do not split into groups of {a.group}')
+    LAT_FRAMES = 20
+    eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + LAT_FRAMES + 8, device=dev, seed=0,
+                      depth_only=(a.case == 'depth'), group=a.group, single_slot=(a.case == 'frame'))
     eng.capture()
     stream = torch.cuda.current_stream(dev)
 
@@ -279,7 +284,7 @@ def main():
         return replicas.sum_over_ranks(x, dev)
 
     case = a.case
-    S = my_streams
+    S = len(eng.streams)          # slots of a.group streams each
 
     def one_step(ev):
         for i in range(S):
@@ -317,7 +322,7 @@ def main():
     clk = clocks.stop() if clocks else None
     ms = t_start.elapsed_time(t_end)
     ms_max = maxred(ms)
-    frames = sumred(S * a.steps)
+    frames = sumred(S * a.group * a.steps)
     value = frames / (ms_max / 1e3)
     # per-part durations from the events (frame layout: [bb] [dd] per stream, then one closing event)
     bb_ms, dd_ms = [], []
@@ -337,7 +342,7 @@ def main():
     kv1 = int(eng.streams[0].bb.cache_position.item()) + 1 if eng.streams[0].bb is not None else 0
     pk = peaks()
     dd_bytes = dcfg.n_decode * dcfg.step_weight_bytes()
-    bb_bytes = backbone_step_bytes(bcfg, 2, (kv0 + kv1) // 2)
+    bb_bytes = backbone_step_bytes(bcfg, 2 * a.group, (kv0 + kv1) // 2)
     roof = None
     if dd_ms:
         dd_avg = sum(dd_ms) / len(dd_ms)
@@ -358,9 +363,10 @@ def main():
     e2e = None
     if not a.no_e2e and case == 'frame':
         R = 8
-        qh = torch.empty(R, dcfg.n_decode, 1, dcfg.vocab).exponential_(1, generator=torch.Generator().manual_seed(5))
+        G = a.group
+        qh = torch.empty(R, dcfg.n_decode, G, dcfg.vocab).exponential_(1, generator=torch.Generator().manual_seed(5))
         qh = qh.pin_memory()
-        toks_h = torch.zeros(S, 2 + 2 * dcfg.n_decode, dtype=torch.long).pin_memory()
+        toks_h = torch.zeros(S, 2 * G + 2 * G * dcfg.n_decode, dtype=torch.long).pin_memory()
         done = torch.cuda.Event()
         h2d = S * qh[0].numel() * 4
         d2h = S * toks_h[0].numel() * 8
@@ -370,8 +376,8 @@ def main():
                 st = eng.streams[i]
                 st.q.copy_(qh[(i + t) % R], non_blocking=True)
                 eng.frame(i)
-                toks_h[i, :2].copy_(st.first_cb, non_blocking=True)
-                toks_h[i, 2:].copy_(st.outtok.view(-1), non_blocking=True)
+                toks_h[i, :2 * G].copy_(st.first_cb, non_blocking=True)
+                toks_h[i, 2 * G:].copy_(st.outtok.view(-1), non_blocking=True)
                 done.record(stream)
                 done.synchronize()             # the frame's tokens are on the host before the next frame
 
@@ -397,12 +403,26 @@ def main():
                    sample=f'{n} frames of one stream ({el:.1f} s after 1 warm-up frame): numpy/C oracle port of '
                           f'backbone step (KV {a.prompt}+t) + 16-codebook depth frame, {threads} BLAS threads')
 
+    # frame latency of ONE stream (its own single-stream slot on the same weights), graph-replayed back to back
+    lat = None
+    if case == 'frame' and eng.single is not None:
+        for _ in range(3):
+            eng.frame('single')
+        barrier()
+        l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0.record(stream)
+        for _ in range(LAT_FRAMES):
+            eng.frame('single')
+        l1.record(stream)
+        barrier()
+        lat = round(maxred(l0.elapsed_time(l1) / LAT_FRAMES), 4)
     prefill = measure_prefill(dev, world, rank) if case == 'frame' else None
     launches = eng.launches_per_frame() if case == 'frame' else (
         1 if case == 'depth' else eng.launches_per_frame() - 1)
     if rank == 0:
-        wl = {'frame': 'streaming frames: 28-layer backbone decode step (B=2 CFG, KV 512+t) + greedy codebook-0 + '
-                       '16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9)',
+        wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + greedy '
+                       f'codebook-0 + 16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9); '
+                       f'{a.group} stream(s) per launch share the weight reads',
               'depth': 'depth frame only (4 layers, hidden 1024, 16 codebooks of 2048, CFG + top-k 50 sampling)',
               'backbone': 'backbone decode step only (28 layers, hidden 2048, B=2, KV 512+t) + frame link'}[case]
         line = dict(
@@ -410,16 +430,18 @@ def main():
             warmup=a.warmup, ms_per_step=round(ms_max / a.steps, 3), higher_is_better=True, scaling='strong',
             vs_baseline=None, dtype='bf16', data='synthetic (seeded random bf16 weights, random prompt KV)',
             config=dict(workload=wl, streams=a.streams, streams_per_gpu=my_streams, step='one frame of every stream '
-                        'on the rank', prompt_len=a.prompt, kv_len=[kv0, kv1], parallelism=f'replica x{world}',
+                        'on the rank', streams_per_launch=a.group, prompt_len=a.prompt, kv_len=[kv0, kv1],
+                        parallelism=f'replica x{world}',
                         l2='inputs larger than L2: 2.70 GB backbone weights per step, 130 MB depth weights per '
                            'codebook step; no flush', cb0='greedy (backbone sampler do_sample=False)',
                         prefill='not timed (random prompt KV)'),
             frames_per_s_per_gpu=round(value / world, 3), tokens_per_s=round(value * 17, 1),
+            frame_ms_single_stream=lat,
             roofline=roof, roofline_backbone=roof_bb, prefill=prefill, cpu_baseline=cpu, e2e=e2e,
-            gpu_launches=int(launches * frames), clocks=clk)
+            gpu_launches=int(launches * frames / a.group), clocks=clk)
         print(json.dumps(line), flush=True)
     if world > 1:
-        for st in eng.streams:
+        for st in eng.streams + ([eng.single] if eng.single is not None else []):
             st.graph = None
         barrier()
         dist.destroy_process_group()

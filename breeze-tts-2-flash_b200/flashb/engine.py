@@ -252,15 +252,21 @@ class SyntheticDepth:
                         forced)
 
 
-class _StreamState:
-    __slots__ = ('bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph')
+class _Slot:
+    """``g`` streams decoded together: one backbone graph and one depth launch over 2 g rows laid out
+    [cond_0 .. cond_{g-1}, uncond_0 .. uncond_{g-1}] (the CFG pair of stream k is rows k and k + g), which is the row
+    order every kernel on the path already uses for B = 2 g."""
+    __slots__ = ('g', 'bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph', 'desc')
 
 
 class FrameEngine:
     """One replica on one GPU for the streaming decode: a synthetic backbone and depth decoder whose weights are
     shared by ``n_streams`` independent streams (own KV cache, positions and I/O buffers each).
 
-    ``frame(i)`` runs one frame of stream i on the current CUDA stream, the body of the reference's streaming loop
+    Streams are served in slots of ``group`` streams (1 or 2): a slot's streams share every weight read of the
+    backbone step (GEMV rows M = 2 g) and of the depth frame (B = 2 g), and advance in lockstep (same cache
+    position; the bench's streams all start after the same prompt length).  ``frame(i)`` runs one frame of every
+    stream of slot i on the current CUDA stream, the body of the reference's streaming loop
     (``flash/main_loop.py:252-312``) without host synchronisation:
 
         frame_ids    next backbone input = [cb0, depth tokens] of the previous frame            (1 launch)
@@ -268,73 +274,102 @@ class FrameEngine:
         cb0_greedy   codebook-0 token = argmax of the CFG logits (greedy backbone sampler)      (1 launch)
         depth frame  every depth codebook, CFG top-k sampled on the device                      (1 launch)
 
-    The first three are captured into one CUDA graph per stream (``capture()``); the depth frame is a single launch.
-    Each stream starts after a ``prompt_len``-token prompt whose KV cache is random (the prefill stand-in)."""
+    The first three are captured into one CUDA graph per slot (``capture()``); the depth frame is a single launch.
+    Each stream starts after a ``prompt_len``-token prompt whose KV cache is random (the prefill stand-in).
+    ``single_slot`` adds one extra single-stream slot on the same weights (``self.single``), for frame latency."""
 
     def __init__(self, bcfg: BackboneConfig, dcfg: DepthConfig, n_streams, prompt_len, max_frames, device='cuda',
-                 seed=0, depth_only=False):
+                 seed=0, depth_only=False, group=1, single_slot=False):
         """``depth_only``: no backbone (a random hidden state per stream feeds the depth frame) -- for timing or
         profiling the depth frame alone on a small device footprint."""
         if bcfg.codebooks - 1 > dcfg.n_decode or dcfg.embed_dim != bcfg.hidden:
             raise ValueError('backbone codebooks must be <= 1 + depth codebooks and depth embed_dim == backbone hidden')
-        self.bcfg, self.dcfg = bcfg, dcfg
+        if group not in (1, 2) or n_streams % group:
+            raise ValueError('group must be 1 or 2 and divide the number of streams')
+        self.bcfg, self.dcfg, self.group = bcfg, dcfg, group
         self.device = dev = torch.device(device)
         self.prompt_len = prompt_len
-        self.max_seq_len = S = prompt_len + max_frames + 2
+        self.max_seq_len = prompt_len + max_frames + 2
         self.n_valid = min(dcfg.codebook_size, bcfg.vocab)
-        self.depth = SyntheticDepth(dcfg, batch=2, device=dev, seed=seed + 3)
-        self.streams = []
-        first = None
-        g = torch.Generator(device='cpu').manual_seed(seed + 17)
-        for i in range(n_streams):
-            st = _StreamState()
-            if depth_only:
-                st.bb = None
-                st.bh = torch.randn(2, dcfg.embed_dim, generator=g).to(torch.bfloat16).to(dev)
-            else:
-                st.bb = SyntheticBackboneGraph(bcfg, 2, S, dev, seed=seed + 2, weights_from=first)
-                first = first or st.bb
-                st.bb.fill_kv(prompt_len, seed=1000 + seed + i)
-                st.bb.set_position(prompt_len - 1)
-                st.bh = st.bb.hidden_buf.view(2, -1)
-            st.first_cb = torch.randint(0, self.n_valid, (1,), generator=g).repeat(2).to(dev)
-            st.outtok = torch.randint(0, dcfg.codebook_size, (1, dcfg.n_decode), generator=g).repeat(2, 1).to(dev)
-            st.tokbuf = torch.zeros(2, dtype=torch.long, device=dev)
-            st.q = torch.empty(dcfg.n_decode, 1, dcfg.vocab).exponential_(1, generator=g).to(dev)
-            st.graph = None
-            self.streams.append(st)
+        self.depth_only = depth_only
+        self.depth = SyntheticDepth(dcfg, batch=2 * group, device=dev, seed=seed + 3)
+        self._gen = torch.Generator(device='cpu').manual_seed(seed + 17)
+        self._first_bb = None
+        self._seed = seed
+        self.streams = [self._slot(group, 1000 + seed + i) for i in range(n_streams // group)]
+        self.single = None
+        if single_slot:
+            from .depth import DepthModelDesc
+            d = self.depth
+            self.single = self._slot(1, 999 + seed)
+            self.single.desc = d.desc if group == 1 else DepthModelDesc(
+                d.layers, d.embed, d.proj, d.normf, d.head_t, d.cos_tab, d.sin_tab, dcfg.eps, 128 ** -0.5,
+                dcfg.codebook_size, 2, dev)
+
+    def _slot(self, g, kv_seed):
+        dcfg, dev, gen = self.dcfg, self.device, self._gen
+        st = _Slot()
+        st.g = g
+        if self.depth_only:
+            st.bb = None
+            st.bh = torch.randn(2 * g, dcfg.embed_dim, generator=gen).to(torch.bfloat16).to(dev)
+        else:
+            st.bb = SyntheticBackboneGraph(self.bcfg, 2 * g, self.max_seq_len, dev, seed=self._seed + 2,
+                                           weights_from=self._first_bb)
+            self._first_bb = self._first_bb or st.bb
+            st.bb.fill_kv(self.prompt_len, seed=kv_seed)
+            st.bb.set_position(self.prompt_len - 1)
+            st.bh = st.bb.hidden_buf.view(2 * g, -1)
+        st.first_cb = torch.randint(0, self.n_valid, (g,), generator=gen).repeat(2).to(dev)
+        st.outtok = torch.randint(0, dcfg.codebook_size, (g, dcfg.n_decode), generator=gen).repeat(2, 1).to(dev)
+        st.tokbuf = torch.zeros(2 * g, dtype=torch.long, device=dev)
+        st.q = torch.empty(dcfg.n_decode, g, dcfg.vocab).exponential_(1, generator=gen).to(dev)
+        st.graph = None
+        st.desc = self.depth.desc
+        return st
+
+    def _get(self, i):
+        return self.single if i == 'single' else self.streams[i]
 
     # one frame, split into its backbone part (graph-capturable) and the depth launch
     def backbone_part(self, i):
-        st = self.streams[i]
+        st = self._get(i)
+        g = st.g
         stream = torch.cuda.current_stream(self.device).cuda_stream
         C = self.bcfg.codebooks
-        check(lib().flashb_frame_ids(st.first_cb.data_ptr(), st.outtok.data_ptr(), self.dcfg.n_decode, 2, C,
+        check(lib().flashb_frame_ids(st.first_cb.data_ptr(), st.outtok.data_ptr(), self.dcfg.n_decode, 2 * g, C,
                                      st.bb.input_ids_buf.data_ptr(), stream))
         st.bb.decode_step(advance=True)
-        check(lib().flashb_cb0_greedy(st.bb.cfg_logits_buf.data_ptr(), st.bb.cfg_logits_buf.stride(0), 1,
-                                      self.n_valid, 2, st.first_cb.data_ptr(), stream))
+        check(lib().flashb_cb0_greedy(st.bb.cfg_logits_buf.data_ptr(), st.bb.cfg_logits_buf.stride(0), g,
+                                      self.n_valid, 2 * g, st.first_cb.data_ptr(), stream))
 
     def depth_part(self, i):
-        st, d = self.streams[i], self.depth
-        d.desc.frame(st.first_cb, st.bh, st.tokbuf, st.outtok, d.temperature, d.top_k, d.top_p, d.do_sample,
-                     d.guidance_scale, st.q)
+        st, d = self._get(i), self.depth
+        g = st.g
+        st.desc.frame(st.first_cb, st.bh, st.tokbuf, st.outtok, d.temperature[:g], d.top_k[:g], d.top_p[:g],
+                      d.do_sample[:g], d.guidance_scale[:g], st.q)
+
+    def _slots(self):
+        return list(enumerate(self.streams)) + ([('single', self.single)] if self.single is not None else [])
 
     def capture(self):
-        """One CUDA graph per stream for its backbone part.  Stream 0 first runs one eager frame (kernel attributes
-        are set on first use), then its position is put back.  Nothing to capture without a backbone."""
-        if self.streams[0].bb is None:
-            self.depth_part(0)
+        """One CUDA graph per slot for its backbone part.  Every slot first runs one eager frame (kernel attributes
+        are set on first use, per batch size), then its position is put back.  Nothing to capture without a
+        backbone."""
+        if self.depth_only:
+            for i, _ in self._slots():
+                self.depth_part(i)
             torch.cuda.synchronize(self.device)
             return
-        self.backbone_part(0)
-        self.depth_part(0)
-        torch.cuda.synchronize(self.device)
-        self.streams[0].bb.set_position(self.prompt_len - 1)
+        for i, st in self._slots()[:1] + ([self._slots()[-1]] if self.single is not None else []):
+            self.backbone_part(i)
+            self.depth_part(i)
+            torch.cuda.synchronize(self.device)
+            st.bb.set_position(self.prompt_len - 1)
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
-            for i, st in enumerate(self.streams):
+            for i, st in self._slots():
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(graph, stream=side):
                     self.backbone_part(i)
@@ -343,7 +378,7 @@ class FrameEngine:
         torch.cuda.synchronize(self.device)
 
     def frame(self, i):
-        st = self.streams[i]
+        st = self._get(i)
         if st.bb is None:
             pass
         elif st.graph is not None:
@@ -353,14 +388,15 @@ class FrameEngine:
         self.depth_part(i)
 
     def launches_per_frame(self):
+        """Kernel launches per slot frame (the same for any group size)."""
         return launches_per_backbone_step(self.bcfg) + 1 + 3
 
     def frame_bytes(self):
-        """Algorithmic HBM bytes of one frame at the current mean KV length: backbone step + 16 depth steps."""
-        if self.streams[0].bb is None:
+        """Algorithmic HBM bytes of one slot frame at the current KV length: backbone step + 16 depth steps."""
+        if self.depth_only:
             return self.dcfg.n_decode * self.dcfg.step_weight_bytes()
         kv = int(self.streams[0].bb.cache_position.item()) + 1
-        return backbone_step_bytes(self.bcfg, 2, kv) + self.dcfg.n_decode * self.dcfg.step_weight_bytes()
+        return backbone_step_bytes(self.bcfg, 2 * self.group, kv) + self.dcfg.n_decode * self.dcfg.step_weight_bytes()
 
 
 def backbone_step_bytes(cfg: BackboneConfig, batch, kv_len, include_lm_head=True):
