@@ -31,9 +31,10 @@ sys.path[:0] = [HERE, os.path.join(HERE, 'breeze-tts-2-flash_b200')]
 N_STREAMS = 64
 PROMPT = 512
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0)
-# dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch: ncu --set full capture of the same
-# full-size depth model (bench.py --case depth), 2.097653 GB read + 30.227456 MB written; profiles/ holds the summary.
-DD_TRAFFIC_BYTES = 2127880456
+# dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch for a pair of streams (B = 4 rows, the
+# bench's default): ncu --set full capture of the full-size depth model, 2.099728 GB read + 30.472448 MB written
+# (profiles/dd_frame_kernel_depth_frame_pair.md).
+DD_TRAFFIC_BYTES = 2130200448
 PREFILL_CFG = dict(B=2, NH=16, NKV=4, L=512, D=128, pads=(0, 37))
 
 
