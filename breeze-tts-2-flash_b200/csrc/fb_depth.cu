@@ -35,7 +35,7 @@
 
 namespace fb {
 
-constexpr int DD_MAXB = 4;      // batch rows (two CFG pairs)
+constexpr int DD_MAXB = 8;      // batch rows (four CFG pairs)
 constexpr int DD_MAXV = 4096;   // sampler vocabulary bound (composite key packs 12 index bits)
 
 struct DDLayer {
@@ -62,7 +62,7 @@ struct DDArgs {
   bf16 *xres, *qb, *ob, *act, *kc, *vc;
   float* logits;
   GridBar* bar;
-  int nstages, xs_bytes, att_off, keep_off;
+  int nstages, xs_bytes, att_off, keep_off, att_bc;
   unsigned* err;
   unsigned long long* trace;
 };
@@ -263,26 +263,40 @@ __device__ __noinline__ int dd_sample(const DDArgs& a, int step, int h, unsigned
   // 3) gather the kk survivors (key >= threshold; exactly kk of them), pad to a power of two, sort descending
   int n2 = 1;
   while (n2 < kk) n2 <<= 1;
+  if (n2 < 64) n2 = 64;                      // up to 64 survivors: one register sort in warp 0
   for (int i = tid; i < V; i += PK_CONSUMERS) {
     const unsigned long long k = keys[i];
     if (k >= prefix) top[atomicAdd(&s_int[12], 1)] = k;
   }
   for (int i = kk + tid; i < n2; i += PK_CONSUMERS) top[i] = 0ull;
   named_sync(1, PK_CONSUMERS);
-  if (n2 <= 64) {
+  if (n2 == 64) {
     if (warp == 0) {
-      for (int k = 2; k <= n2; k <<= 1)
+      // bitonic network over elements i = lane (e0) and i = lane + 32 (e1), partners exchanged by shuffles; the
+      // position with bit j clear keeps the larger key in a descending block (bit k clear), the smaller otherwise
+      unsigned long long e0 = top[lane], e1 = top[lane + 32];
+#pragma unroll
+      for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
         for (int j = k >> 1; j > 0; j >>= 1) {
-          for (int i = lane; i < (n2 >> 1); i += 32) {
-            const int lo = 2 * i - (i & (j - 1)), hi = lo + j;
-            const unsigned long long x = top[lo], y = top[hi];
-            if (((lo & k) == 0) ? (x < y) : (x > y)) {
-              top[lo] = y;
-              top[hi] = x;
+          if (j == 32) {
+            if (e0 < e1) {                   // k = 64: one descending block; position lane is the lower one
+              const unsigned long long x = e0;
+              e0 = e1;
+              e1 = x;
             }
+          } else {
+            const unsigned long long o0 = __shfl_xor_sync(FULL, e0, j), o1 = __shfl_xor_sync(FULL, e1, j);
+            const bool lo = (lane & j) == 0;
+            const bool d0 = (lane & k) == 0, d1 = ((lane + 32) & k) == 0;
+            e0 = (d0 == lo) ? (e0 > o0 ? e0 : o0) : (e0 < o0 ? e0 : o0);
+            e1 = (d1 == lo) ? (e1 > o1 ? e1 : o1) : (e1 < o1 ? e1 : o1);
           }
-          __syncwarp();
         }
+      }
+      top[lane] = e0;
+      top[lane + 32] = e1;
+      __syncwarp();
     }
   } else {
     for (int k = 2; k <= n2; k <<= 1)
@@ -298,7 +312,6 @@ __device__ __noinline__ int dd_sample(const DDArgs& a, int step, int h, unsigned
         named_sync(1, PK_CONSUMERS);
       }
   }
-  if (n2 <= 64) __syncwarp();
   DD_STAMP(step, 3 + 9 * a.L + 4);
   // 4) warp 0: top-p / softmax / argmax(p / q) with the canonical sums (lane l owns ranks l*C .. l*C+C-1)
   if (warp == 0) {
@@ -364,106 +377,106 @@ __device__ __noinline__ int dd_sample(const DDArgs& a, int step, int h, unsigned
 }
 
 // ------------------------------------------------------------------------------------------------ attention (S2)
-// Shared-memory bytes of the attention staging area (q rows, the layer's K and V of every position, scores).
-__host__ __device__ constexpr size_t dd_attn_bytes(int M, int NH, int B, int NKV, int P) {
-  return (size_t)M * NH * 256 + 2 * (size_t)B * NKV * P * 256 + (size_t)M * NH * 32 * 4;
+// Shared-memory bytes of the attention staging area for a chunk of `bc` batch rows (their q rows, the layer's K and
+// V of every position for their KV heads, scores).
+__host__ __device__ constexpr size_t dd_attn_bytes(int bc, int NH, int NKV, int P) {
+  return (size_t)bc * NH * 256 + 2 * (size_t)bc * NKV * P * 256 + (size_t)bc * NH * 32 * 4;
 }
 
-// All M x NH query rows over the layer's cached positions 0..pos(m), computed by every CTA (the o-projection that
-// follows needs every row).  One round trip: q, K and V of every used position are staged in shared memory with
-// cp.async, then scores (one thread per (row, key)), softmax (one thread per row) and p.V (one thread per
-// (row, 8 dims)).  Eager rounding: s = bf16(bf16(q.k) * scaling), p = bf16(softmax_fp32(s)), out = bf16(sum p v).
-// Output rows go to xs (the o-projection input); `att` is the staging area.
+// The step's token at position `pos` of every batch row, all NH query heads, over the layer's cached positions
+// 0..pos, computed by every CTA (the o-projection that follows needs every row).  Batch rows go in chunks of
+// a.att_bc; per chunk one round trip stages q, K and V in shared memory with cp.async, then scores (one thread per
+// (row, key)), softmax (one thread per row) and p.V (one thread per (row, 8 dims)).  Eager rounding:
+// s = bf16(bf16(q.k) * scaling), p = bf16(softmax_fp32(s)), out = bf16(sum p v).  Output rows go to xs (the
+// o-projection input); `att` is the staging area.
 template <int G>
-__device__ __noinline__ void dd_attention(const DDArgs& a, int l, int step, int T, unsigned char* xs, int x_pitch,
+__device__ __noinline__ void dd_attention(const DDArgs& a, int l, int pos, unsigned char* xs, int x_pitch,
                                           unsigned char* att) {
   const int tid = threadIdx.x;
-  const int M = a.B * T, NH = a.NH, NKV = a.NKV, QD = NH * 128;
-  const int np = step == 0 ? 2 : step + 2;        // positions used by the last token of the step
-  const int nrow = M * NH;
-  bf16* qs = reinterpret_cast<bf16*>(att);
-  bf16* ks = qs + (size_t)nrow * 128;
-  bf16* vs = ks + (size_t)a.B * NKV * np * 128;
-  float* ps = reinterpret_cast<float*>(vs + (size_t)a.B * NKV * np * 128);
-  const int qch = nrow * 16, kch = a.B * NKV * np * 16;
-  for (int i = tid; i < qch + 2 * kch; i += PK_CONSUMERS) {
-    const bf16* src;
-    bf16* dst;
-    if (i < qch) {
-      const int row = i >> 4, c = i & 15, m = row / NH, qh = row - m * NH;
-      src = a.qb + (size_t)m * QD + qh * 128 + c * 8;
-      dst = qs + (size_t)row * 128 + c * 8;
-    } else {
-      int j = i - qch;
-      const bool isv = j >= kch;
-      if (isv) j -= kch;
-      const int row = j >> 4, c = j & 15, bk = row / np, p = row - bk * np;
-      const int b = bk / NKV, kvh = bk - b * NKV;
-      src = (isv ? a.vc : a.kc) + ((((size_t)l * a.B + b) * NKV + kvh) * a.P + p) * 128 + c * 8;
-      dst = (isv ? vs : ks) + (size_t)row * 128 + c * 8;
+  const int NH = a.NH, NKV = a.NKV, QD = NH * 128;
+  const int np = pos + 1;
+  for (int b0 = 0; b0 < a.B; b0 += a.att_bc) {
+    const int nb = min(a.att_bc, a.B - b0);
+    const int nrow = nb * NH;
+    bf16* qs = reinterpret_cast<bf16*>(att);
+    bf16* ks = qs + (size_t)nrow * 128;
+    bf16* vs = ks + (size_t)nb * NKV * np * 128;
+    float* ps = reinterpret_cast<float*>(vs + (size_t)nb * NKV * np * 128);
+    const int qch = nrow * 16, kch = nb * NKV * np * 16;
+    for (int i = tid; i < qch + 2 * kch; i += PK_CONSUMERS) {
+      const bf16* src;
+      bf16* dst;
+      if (i < qch) {
+        const int row = i >> 4, c = i & 15, bb = row / NH, qh = row - bb * NH;
+        src = a.qb + (size_t)(b0 + bb) * QD + qh * 128 + c * 8;
+        dst = qs + (size_t)row * 128 + c * 8;
+      } else {
+        int j = i - qch;
+        const bool isv = j >= kch;
+        if (isv) j -= kch;
+        const int row = j >> 4, c = j & 15, bk = row / np, p = row - bk * np;
+        const int bb = bk / NKV, kvh = bk - bb * NKV;
+        src = (isv ? a.vc : a.kc) + ((((size_t)l * a.B + b0 + bb) * NKV + kvh) * a.P + p) * 128 + c * 8;
+        dst = (isv ? vs : ks) + (size_t)row * 128 + c * 8;
+      }
+      cp_async16(dst, src);
     }
-    cp_async16(dst, src);
-  }
-  cp_async_commit();
-  cp_async_wait<0>();
-  named_sync(1, PK_CONSUMERS);
-  for (int i = tid; i < nrow * np; i += PK_CONSUMERS) {
-    const int row = i / np, j = i - row * np;
-    const int m = row / NH, qh = row - m * NH, b = m / T, t = m - b * T;
-    const int pos = step == 0 ? t : step + 1;
-    if (j > pos) continue;
-    const uint4* qr = reinterpret_cast<const uint4*>(qs + (size_t)row * 128);
-    const uint4* kr = reinterpret_cast<const uint4*>(ks + ((size_t)(b * NKV + qh / G) * np + j) * 128);
-    float d = 0.f;
+    cp_async_commit();
+    cp_async_wait<0>();
+    named_sync(1, PK_CONSUMERS);
+    for (int i = tid; i < nrow * np; i += PK_CONSUMERS) {
+      const int row = i / np, j = i - row * np;
+      const int bb = row / NH, qh = row - bb * NH;
+      const uint4* qr = reinterpret_cast<const uint4*>(qs + (size_t)row * 128);
+      const uint4* kr = reinterpret_cast<const uint4*>(ks + ((size_t)(bb * NKV + qh / G) * np + j) * 128);
+      float d = 0.f;
 #pragma unroll 4
-    for (int cc = 0; cc < 16; ++cc) {
-      const int c = (cc + j) & 15;               // rotate the chunk order by key: fewer bank conflicts
-      float qf[8], kf[8];
-      cvt8(qr[c], qf);
-      cvt8(kr[c], kf);
+      for (int cc = 0; cc < 16; ++cc) {
+        const int c = (cc + j) & 15;               // rotate the chunk order by key: fewer bank conflicts
+        float qf[8], kf[8];
+        cvt8(qr[c], qf);
+        cvt8(kr[c], kf);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) d = fmaf(qf[u], kf[u], d);
+        for (int u = 0; u < 8; ++u) d = fmaf(qf[u], kf[u], d);
+      }
+      ps[row * 32 + j] = rbf(rbf(d) * a.scaling);
     }
-    ps[row * 32 + j] = rbf(rbf(d) * a.scaling);
-  }
-  named_sync(1, PK_CONSUMERS);
-  if (tid < nrow) {
-    const int row = tid, m = row / NH, t = m - (m / T) * T;
-    const int pos = step == 0 ? t : step + 1;
-    float* pr = ps + row * 32;
-    float mx = -INFINITY;
-    for (int j = 0; j <= pos; ++j) mx = fmaxf(mx, pr[j]);
-    float den = 0.f;
-    for (int j = 0; j <= pos; ++j) {
-      const float e = expf(pr[j] - mx);
-      pr[j] = e;
-      den += e;
+    named_sync(1, PK_CONSUMERS);
+    if (tid < nrow) {
+      float* pr = ps + tid * 32;
+      float mx = -INFINITY;
+      for (int j = 0; j < np; ++j) mx = fmaxf(mx, pr[j]);
+      float den = 0.f;
+      for (int j = 0; j < np; ++j) {
+        const float e = expf(pr[j] - mx);
+        pr[j] = e;
+        den += e;
+      }
+      for (int j = 0; j < np; ++j) pr[j] = rbf(pr[j] / den);
     }
-    for (int j = 0; j <= pos; ++j) pr[j] = rbf(pr[j] / den);
-  }
-  named_sync(1, PK_CONSUMERS);
-  for (int i = tid; i < nrow * 16; i += PK_CONSUMERS) {
-    const int row = i >> 4, c = i & 15;
-    const int m = row / NH, qh = row - m * NH, b = m / T, t = m - b * T;
-    const int pos = step == 0 ? t : step + 1;
-    const float* pr = ps + row * 32;
-    const bf16* vb = vs + (size_t)(b * NKV + qh / G) * np * 128 + c * 8;
-    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j <= pos; ++j) {
-      float vf[8];
-      cvt8(*reinterpret_cast<const uint4*>(vb + (size_t)j * 128), vf);
-      const float p = pr[j];
+    named_sync(1, PK_CONSUMERS);
+    for (int i = tid; i < nrow * 16; i += PK_CONSUMERS) {
+      const int row = i >> 4, c = i & 15;
+      const int bb = row / NH, qh = row - bb * NH;
+      const float* pr = ps + row * 32;
+      const bf16* vb = vs + (size_t)(bb * NKV + qh / G) * np * 128 + c * 8;
+      float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < np; ++j) {
+        float vf[8];
+        cvt8(*reinterpret_cast<const uint4*>(vb + (size_t)j * 128), vf);
+        const float p = pr[j];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) o[u] = fmaf(p, vf[u], o[u]);
+        for (int u = 0; u < 8; ++u) o[u] = fmaf(p, vf[u], o[u]);
+      }
+      uint4 ov;
+      ov.x = pack2(o[0], o[1]);
+      ov.y = pack2(o[2], o[3]);
+      ov.z = pack2(o[4], o[5]);
+      ov.w = pack2(o[6], o[7]);
+      *reinterpret_cast<uint4*>(xs + (size_t)(b0 + bb) * x_pitch + (size_t)(qh * 128 + c * 8) * 2) = ov;
     }
-    uint4 ov;
-    ov.x = pack2(o[0], o[1]);
-    ov.y = pack2(o[2], o[3]);
-    ov.z = pack2(o[4], o[5]);
-    ov.w = pack2(o[6], o[7]);
-    *reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + (size_t)(qh * 128 + c * 8) * 2) = ov;
+    named_sync(1, PK_CONSUMERS);
   }
-  named_sync(1, PK_CONSUMERS);
 }
 
 // x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.  xres and ob arrive with cp.async (one round trip);
@@ -554,8 +567,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
   uint64_t* empty = full + PK_MAX_STAGES;
   __shared__ float nred[ST_CWARPS * 8];
   __shared__ int s_int[32];
-  __shared__ long long s_tok[DD_MAXB];   // tokens fed to the next step (this CTA's copy of the sampler result)
-  __shared__ __align__(16) bf16 s_cs[2][2][128];   // [cos|sin][step position 0|1][dim] of this step's positions
+  __shared__ long long s_tok[DD_MAXB];     // tokens fed to the next step (this CTA's copy of the sampler result)
+  __shared__ __align__(16) bf16 s_cs[2][128];   // [cos|sin][dim] of the sub-step's position
 
   const int tid = threadIdx.x, warp = tid >> 5;
   if (tid == 0) {
@@ -578,20 +591,24 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
     };
   };
 
+  // Codebook step 0 feeds two tokens (positions 0 and 1); they run as two sub-steps of one token each, which gives
+  // the same values (GEMV rows are independent, position 0 does not attend to position 1) with M = B rows always.
   if (warp == ST_CWARPS) {
     // ------------------------------------------------------------------ producer
     int t = 0;
     bool ok = true;
     for (int s = 0; s < a.NCB && ok; ++s) {
-      ok = ok && produce_task<1>(rg, t, H, AE, [&](int n, int) { return a.proj + (size_t)n * AE; }, a.err);
-      for (int l = 0; l < a.L && ok; ++l) {
-        const DDLayer W = a.layers[l];
-        ok = ok && produce_task<2>(rg, t, QKVU, H, qkv_row(W), a.err);
-        ok = ok && produce_task<1>(rg, t, H, NH * 128, [&](int n, int) { return W.wo + (size_t)n * NH * 128; },
-                                   a.err);
-        ok = ok && produce_task<2>(rg, t, F, H, [&](int n, int mat) { return (mat ? W.wu : W.wg) + (size_t)n * H; },
-                                   a.err);
-        ok = ok && produce_task<1>(rg, t, H, F, [&](int n, int) { return W.wd + (size_t)n * F; }, a.err);
+      for (int sub = 0; sub < (s == 0 ? 2 : 1) && ok; ++sub) {
+        ok = ok && produce_task<1>(rg, t, H, AE, [&](int n, int) { return a.proj + (size_t)n * AE; }, a.err);
+        for (int l = 0; l < a.L && ok; ++l) {
+          const DDLayer W = a.layers[l];
+          ok = ok && produce_task<2>(rg, t, QKVU, H, qkv_row(W), a.err);
+          ok = ok && produce_task<1>(rg, t, H, NH * 128, [&](int n, int) { return W.wo + (size_t)n * NH * 128; },
+                                     a.err);
+          ok = ok && produce_task<2>(rg, t, F, H,
+                                     [&](int n, int mat) { return (mat ? W.wu : W.wg) + (size_t)n * H; }, a.err);
+          ok = ok && produce_task<1>(rg, t, H, F, [&](int n, int) { return W.wd + (size_t)n * F; }, a.err);
+        }
       }
       ok = ok && produce_task<1>(rg, t, V, H, [&](int n, int) { return a.head_t + ((size_t)s * V + n) * H; },
                                  a.err);
@@ -605,134 +622,131 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
   unsigned epoch = 0;
   int t = 0;
   const int half = a.B >= 2 ? a.B / 2 : 1;
+  const int M = a.B;
   const int QD = NH * 128;
   const int xp_ae = AE * 2 + 16, xp_h = H * 2 + 16, xp_q = QD * 2 + 16, xp_f = F * 2 + 16;
   for (int s = 0; s < a.NCB; ++s) {
-    const int T = s == 0 ? 2 : 1;
-    const int M = a.B * T;
-    DD_STAMP(s, 0);
-    // E: gather embeddings into xs (cp.async, one round trip, with this step's rotary rows), projector GEMV -> xres
-    {
-      const int kv = AE >> 3;
-      const long long rows = (long long)(a.NCB + 1) * V;
-      for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
-        const int m = i / kv, j = i - m * kv;
-        const int b = m / T, tt = m - b * T;
-        const bf16* src;
-        if (s == 0 && tt == 0) {
-          src = a.bh + (size_t)b * AE;
-        } else {
-          long long id = (s == 0) ? __ldcg(a.first_cb + b) : s_tok[b] + (long long)s * V;
-          id = id < 0 ? 0 : (id >= rows ? rows - 1 : id);
-          src = a.embed + (size_t)id * AE;
+    for (int sub = 0; sub < (s == 0 ? 2 : 1); ++sub) {
+      const int pos = s == 0 ? sub : s + 1;
+      DD_STAMP(s, 0);
+      // E: gather the token embeddings (cp.async, one round trip, with the position's rotary rows) -> projector
+      {
+        const int kv = AE >> 3;
+        const long long rows = (long long)(a.NCB + 1) * V;
+        for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
+          const int b = i / kv, j = i - b * kv;
+          const bf16* src;
+          if (s == 0 && sub == 0) {
+            src = a.bh + (size_t)b * AE;
+          } else {
+            long long id = (s == 0) ? __ldcg(a.first_cb + b) : s_tok[b] + (long long)s * V;
+            id = id < 0 ? 0 : (id >= rows ? rows - 1 : id);
+            src = a.embed + (size_t)id * AE;
+          }
+          cp_async16(xs + (size_t)b * xp_ae + j * 16, src + (size_t)j * 8);
         }
-        cp_async16(xs + (size_t)m * xp_ae + j * 16, src + (size_t)j * 8);
-      }
-      if (tid < 2 * T * 16) {    // cos / sin rows of the step's T positions, 16 chunks of 16 bytes each
-        const int tab = tid / (T * 16), r = (tid / 16) % T, c = tid % 16;
-        const int pos = s == 0 ? r : s + 1;
-        cp_async16(&s_cs[tab][r][c * 8], (tab ? a.sin_tab : a.cos_tab) + (size_t)pos * 128 + c * 8);
-      }
-      cp_async_commit();
-      cp_async_wait<0>();
-      named_sync(1, PK_CONSUMERS);
-      if (!consume_task<1>(rg, t, H, AE, xs, xp_ae, M, zero16, red, sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, m = tid - i * M;
-                               a.xres[(size_t)m * H + n0 + i] = __float2bfloat16_rn(sm[i * 8 + m]);
-                             }
-                           }, a.err)) return;
-      DD_STAMP(s, 1);
-      if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-      DD_STAMP(s, 2);
-    }
-    for (int l = 0; l < a.L; ++l) {
-      const int tb = 3 + 9 * l;
-      const DDLayer W = a.layers[l];
-      // S1: RMSNorm + q|k|v (rotary pairs) + RoPE + KV write
-      load_x(xs, xp_h, a.xres, H, M, H, W.ln1, a.eps, nred);
-      if (!consume_task<2>(rg, t, QKVU, H, xs, xp_h, M, zero16, red, sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, m = tid - i * M;
-                               const int u = n0 + i, hh = u >> 6, d = u & 63;
-                               const int b = m / T, tt = m - b * T;
-                               const int pos = s == 0 ? tt : s + 1;
-                               float y0 = rbf(sm[i * 8 + m]), y1 = rbf(sm[(i + 8) * 8 + m]);
-                               if (hh < NH + NKV) {
-                                 const int pr = s == 0 ? tt : 0;
-                                 const float c0 = b2f(s_cs[0][pr][d]), s0 = b2f(s_cs[1][pr][d]);
-                                 const float c1 = b2f(s_cs[0][pr][d + 64]), s1 = b2f(s_cs[1][pr][d + 64]);
-                                 const float o0 = rbf(rbf(y0 * c0) + rbf(-y1 * s0));
-                                 const float o1 = rbf(rbf(y1 * c1) + rbf(y0 * s1));
-                                 y0 = o0;
-                                 y1 = o1;
+        if (tid < 32) {    // cos / sin rows of the position, 16 chunks of 16 bytes each
+          const int tab = tid >> 4, c = tid & 15;
+          cp_async16(&s_cs[tab][c * 8], (tab ? a.sin_tab : a.cos_tab) + (size_t)pos * 128 + c * 8);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        named_sync(1, PK_CONSUMERS);
+        if (!consume_task<1>(rg, t, H, AE, xs, xp_ae, M, zero16, red, sums,
+                             [&](int n0, int nu, const float* sm) {
+                               if (tid < nu * M) {
+                                 const int i = tid / M, m = tid - i * M;
+                                 a.xres[(size_t)m * H + n0 + i] = __float2bfloat16_rn(sm[i * 8 + m]);
                                }
-                               if (hh < NH) {
-                                 a.qb[(size_t)m * QD + hh * 128 + d] = __float2bfloat16_rn(y0);
-                                 a.qb[(size_t)m * QD + hh * 128 + d + 64] = __float2bfloat16_rn(y1);
-                               } else {
-                                 const int kvh = hh < NH + NKV ? hh - NH : hh - NH - NKV;
-                                 bf16* cache = hh < NH + NKV ? a.kc : a.vc;
-                                 bf16* dst = cache + ((((size_t)l * a.B + b) * NKV + kvh) * a.P + pos) * 128;
-                                 dst[d] = __float2bfloat16_rn(y0);
-                                 dst[d + 64] = __float2bfloat16_rn(y1);
+                             }, a.err)) return;
+        DD_STAMP(s, 1);
+        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+        DD_STAMP(s, 2);
+      }
+      for (int l = 0; l < a.L; ++l) {
+        const int tb = 3 + 9 * l;
+        const DDLayer W = a.layers[l];
+        // S1: RMSNorm + q|k|v (rotary pairs) + RoPE + KV write
+        load_x(xs, xp_h, a.xres, H, M, H, W.ln1, a.eps, nred);
+        if (!consume_task<2>(rg, t, QKVU, H, xs, xp_h, M, zero16, red, sums,
+                             [&](int n0, int nu, const float* sm) {
+                               if (tid < nu * M) {
+                                 const int i = tid / M, b = tid - i * M;
+                                 const int u = n0 + i, hh = u >> 6, d = u & 63;
+                                 float y0 = rbf(sm[i * 8 + b]), y1 = rbf(sm[(i + 8) * 8 + b]);
+                                 if (hh < NH + NKV) {
+                                   const float c0 = b2f(s_cs[0][d]), s0 = b2f(s_cs[1][d]);
+                                   const float c1 = b2f(s_cs[0][d + 64]), s1 = b2f(s_cs[1][d + 64]);
+                                   const float o0 = rbf(rbf(y0 * c0) + rbf(-y1 * s0));
+                                   const float o1 = rbf(rbf(y1 * c1) + rbf(y0 * s1));
+                                   y0 = o0;
+                                   y1 = o1;
+                                 }
+                                 if (hh < NH) {
+                                   a.qb[(size_t)b * QD + hh * 128 + d] = __float2bfloat16_rn(y0);
+                                   a.qb[(size_t)b * QD + hh * 128 + d + 64] = __float2bfloat16_rn(y1);
+                                 } else {
+                                   const int kvh = hh < NH + NKV ? hh - NH : hh - NH - NKV;
+                                   bf16* cache = hh < NH + NKV ? a.kc : a.vc;
+                                   bf16* dst = cache + ((((size_t)l * a.B + b) * NKV + kvh) * a.P + pos) * 128;
+                                   dst[d] = __float2bfloat16_rn(y0);
+                                   dst[d + 64] = __float2bfloat16_rn(y1);
+                                 }
                                }
-                             }
-                           }, a.err)) return;
-      DD_STAMP(s, tb + 0);
-      if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-      DD_STAMP(s, tb + 1);
-      // S2: attention (every CTA, all rows) + o GEMV
-      dd_attention<G>(a, l, s, T, xs, xp_q, xs + a.att_off);
-      DD_STAMP(s, tb + 2);
-      if (!consume_task<1>(rg, t, H, QD, xs, xp_q, M, zero16, red, sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, m = tid - i * M;
-                               a.ob[(size_t)m * H + n0 + i] = __float2bfloat16_rn(sm[i * 8 + m]);
-                             }
-                           }, a.err)) return;
-      DD_STAMP(s, tb + 3);
-      if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-      DD_STAMP(s, tb + 4);
-      // S3: RMSNorm(bf16(x + o)) + gate|up + SiLU*up
-      bf16* xkeep = reinterpret_cast<bf16*>(xs + a.keep_off);  // x_mid rows for the down projection's residual
-      dd_load_mid(xs, xp_h, a, M, W.ln2, nred, xkeep);
-      if (!consume_task<2>(rg, t, F, H, xs, xp_h, M, zero16, red, sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, m = tid - i * M;
-                               const float g = rbf(sm[i * 8 + m]);
-                               const float u = rbf(sm[(i + 8) * 8 + m]);
-                               a.act[(size_t)m * F + n0 + i] = __float2bfloat16_rn(rbf(g / (1.0f + expf(-g))) * u);
-                             }
-                           }, a.err)) return;
-      DD_STAMP(s, tb + 5);
-      if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-      DD_STAMP(s, tb + 6);
-      // S4: down + residual: xres = bf16(bf16(xres + o) + bf16(d))
-      load_x(xs, xp_f, a.act, F, M, F, nullptr, 0.f, nred);
-      if (!consume_task<1>(rg, t, H, F, xs, xp_f, M, zero16, red, sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, m = tid - i * M, n = n0 + i;
-                               const float xm = b2f(xkeep[(size_t)m * H + n]);
-                               a.xres[(size_t)m * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * 8 + m]));
-                             }
-                           }, a.err)) return;
-      DD_STAMP(s, tb + 7);
-      if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-      DD_STAMP(s, tb + 8);
+                             }, a.err)) return;
+        DD_STAMP(s, tb + 0);
+        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+        DD_STAMP(s, tb + 1);
+        // S2: attention (every CTA, all rows) + o GEMV
+        dd_attention<G>(a, l, pos, xs, xp_q, xs + a.att_off);
+        DD_STAMP(s, tb + 2);
+        if (!consume_task<1>(rg, t, H, QD, xs, xp_q, M, zero16, red, sums,
+                             [&](int n0, int nu, const float* sm) {
+                               if (tid < nu * M) {
+                                 const int i = tid / M, m = tid - i * M;
+                                 a.ob[(size_t)m * H + n0 + i] = __float2bfloat16_rn(sm[i * 8 + m]);
+                               }
+                             }, a.err)) return;
+        DD_STAMP(s, tb + 3);
+        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+        DD_STAMP(s, tb + 4);
+        // S3: RMSNorm(bf16(x + o)) + gate|up + SiLU*up
+        bf16* xkeep = reinterpret_cast<bf16*>(xs + a.keep_off);  // x_mid rows for the down projection's residual
+        dd_load_mid(xs, xp_h, a, M, W.ln2, nred, xkeep);
+        if (!consume_task<2>(rg, t, F, H, xs, xp_h, M, zero16, red, sums,
+                             [&](int n0, int nu, const float* sm) {
+                               if (tid < nu * M) {
+                                 const int i = tid / M, m = tid - i * M;
+                                 const float g = rbf(sm[i * 8 + m]);
+                                 const float u = rbf(sm[(i + 8) * 8 + m]);
+                                 a.act[(size_t)m * F + n0 + i] = __float2bfloat16_rn(rbf(g / (1.0f + expf(-g))) * u);
+                               }
+                             }, a.err)) return;
+        DD_STAMP(s, tb + 5);
+        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+        DD_STAMP(s, tb + 6);
+        // S4: down + residual: xres = bf16(bf16(xres + o) + bf16(d))
+        load_x(xs, xp_f, a.act, F, M, F, nullptr, 0.f, nred);
+        if (!consume_task<1>(rg, t, H, F, xs, xp_f, M, zero16, red, sums,
+                             [&](int n0, int nu, const float* sm) {
+                               if (tid < nu * M) {
+                                 const int i = tid / M, m = tid - i * M, n = n0 + i;
+                                 const float xm = b2f(xkeep[(size_t)m * H + n]);
+                                 a.xres[(size_t)m * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * 8 + m]));
+                               }
+                             }, a.err)) return;
+        DD_STAMP(s, tb + 7);
+        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+        DD_STAMP(s, tb + 8);
+      }
     }
     const int te = 3 + 9 * a.L;
-    // S5: final RMSNorm of each row's last token + codebook head -> fp32 logits
-    load_x(xs, xp_h, a.xres + (size_t)(T - 1) * H, (long)T * H, a.B, H, a.normf, a.eps, nred);
-    if (!consume_task<1>(rg, t, V, H, xs, xp_h, a.B, zero16, red, sums,
+    // S5: final RMSNorm + codebook head -> fp32 logits
+    load_x(xs, xp_h, a.xres, H, M, H, a.normf, a.eps, nred);
+    if (!consume_task<1>(rg, t, V, H, xs, xp_h, M, zero16, red, sums,
                          [&](int n0, int nu, const float* sm) {
-                           if (tid < nu * a.B) {
-                             const int i = tid / a.B, b = tid - i * a.B;
+                           if (tid < nu * M) {
+                             const int i = tid / M, b = tid - i * M;
                              const float v = sm[i * 8 + b];
                              a.logits[(size_t)b * V + n0 + i] = v;
                              if (a.dbg) a.dbg[((size_t)s * a.B + b) * V + n0 + i] = v;
@@ -741,8 +755,13 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
     DD_STAMP(s, te + 0);
     if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
     DD_STAMP(s, te + 1);
-    // every CTA samples every half-row; CTA 0 publishes, every CTA keeps the fed-forward tokens in s_tok
-    for (int h = 0; h < half; ++h) {
+    // one CFG pair: every CTA samples it (no barrier follows), CTA 0 publishes.  Several pairs: CTA h samples
+    // pair h and publishes it, then one barrier hands every CTA the fed-forward tokens (one barrier instead of
+    // `half` samplers in series on every CTA).
+    const bool redundant = half == 1;
+    const int h_begin = redundant ? 0 : (int)blockIdx.x;
+    const int h_end = redundant ? 1 : ((int)blockIdx.x < half ? (int)blockIdx.x + 1 : 0);
+    for (int h = h_begin; h < h_end; ++h) {
       int tokv = dd_sample(a, s, h, xs, s_int);
       tokv = tokv < 0 ? 0 : (tokv > V - 1 ? V - 1 : tokv);
       if (tid == 0) {
@@ -754,12 +773,16 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
             fed = fc < 0 ? 0 : (fc > V - 1 ? V - 1 : fc);
           }
           s_tok[b] = fed;
-          if (blockIdx.x == 0) {
+          if (blockIdx.x == 0 || !redundant) {
             a.outtok[(size_t)b * a.NCB + s] = tokv;
             a.tokbuf[b] = fed;
           }
         }
       }
+    }
+    if (!redundant && s + 1 < a.NCB) {
+      if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+      if (tid < a.B) s_tok[tid] = __ldcg(a.tokbuf + tid);
     }
     named_sync(1, PK_CONSUMERS);
     DD_STAMP(s, te + 7);
@@ -780,7 +803,7 @@ size_t al256d(size_t v) { return (v + 255) / 256 * 256; }
 
 DDLayout dd_layout(const fb_dd_config* c) {
   DDLayout s{};
-  const size_t M = (size_t)c->batch * 2;
+  const size_t M = (size_t)c->batch;       // one token per row per sub-step
   const size_t P = (size_t)c->n_decode + 1;
   size_t o = 0;
   s.xres = o; o = al256d(o + M * c->hidden * 2);
@@ -851,7 +874,7 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   FB_CHECK_ARG(c && layers_dev && scratch && first_cb && bh && tokbuf && outtok && temp && topk && topp && dosample &&
                    gs && q, "dd_frame: null pointer argument");
   FB_CHECK_ARG(c->head_dim == 128 && c->batch >= 1 && c->batch <= DD_MAXB && (c->batch == 1 || c->batch % 2 == 0),
-               "dd_frame: head_dim must be 128, batch 1, 2 or 4");
+               "dd_frame: head_dim must be 128, batch 1 or an even number up to %d", DD_MAXB);
   FB_CHECK_ARG(c->vocab >= 1 && c->vocab <= DD_MAXV && c->codebook_size >= 1 && c->codebook_size <= c->vocab,
                "dd_frame: vocab must be <= %d and codebook_size <= vocab", DD_MAXV);
   FB_CHECK_ARG(c->n_decode >= 1 && c->n_decode <= 31, "dd_frame: n_decode must be 1..31");
@@ -879,29 +902,48 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   if (c->ffn > kmax) kmax = c->ffn;
   if (c->heads * 128 > kmax) kmax = c->heads * 128;
   if (c->hidden > kmax) kmax = c->hidden;
-  const size_t M = (size_t)c->batch * 2;
+  const size_t M = (size_t)c->batch;
   // one buffer, three uses: GEMV input rows (up to M x kmax); attention output rows + staging area (att_off);
   // x_mid rows kept from S3 to S4 past the down projection's act rows (keep_off); the sampler's keys
   const size_t att_off = al256d(M * (c->heads * 128 * 2 + 16));
   const size_t keep_off = al256d(M * (c->ffn * 2 + 16));
-  size_t xs = al256d(M * (kmax * 2 + 16));
-  size_t xs_att = al256d(att_off + dd_attn_bytes((int)M, c->heads, c->batch, c->kv_heads, c->n_decode + 1));
+  size_t base = al256d(M * (kmax * 2 + 16));
   const size_t xs_keep = al256d(keep_off + M * c->hidden * 2);
   const size_t xs_smp = al256d(dd_sampler_bytes(c->vocab));
-  if (xs_keep > xs_att) xs_att = xs_keep;
-  if (xs_att > xs) xs = xs_att;
-  if (xs_smp > xs) xs = xs_smp;
-  a.xs_bytes = (int)xs;
-  a.att_off = (int)att_off;
-  a.keep_off = (int)keep_off;
-  const size_t fixed = xs + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * PK_MAX_STAGES * 8;
-  const size_t budget = 227 * 1024 - ST_CWARPS * 8 * 4 - 32 * 4 - DD_MAXB * 8 - 2 * 2 * 128 * 2 - 256;
-  int nst = fixed < budget ? (int)((budget - fixed) / ST_BYTES) : 0;
-  if (nst > PK_MAX_STAGES) nst = PK_MAX_STAGES;
-  if (nst < 2) {
+  if (xs_keep > base) base = xs_keep;
+  if (xs_smp > base) base = xs_smp;
+  const size_t budget = 227 * 1024 - ST_CWARPS * 8 * 4 - 32 * 4 - DD_MAXB * 8 - 2 * 128 * 2 - 256;
+  auto stages_for = [&](size_t xsb) {
+    const size_t fixed = xsb + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * PK_MAX_STAGES * 8;
+    int n = fixed < budget ? (int)((budget - fixed) / ST_BYTES) : 0;
+    return n > PK_MAX_STAGES ? PK_MAX_STAGES : n;
+  };
+  // attention chunk: the most batch rows per round trip that still leave 4 ring stages (else 3, else 2)
+  int bc = 0, nst = 0;
+  size_t xs = base;
+  for (int want = 4; want >= 2 && !bc; --want) {
+    for (int cand = c->batch; cand >= 1; cand = cand > 1 ? (cand + 1) / 2 : 0) {
+      size_t need = al256d(att_off + dd_attn_bytes(cand, c->heads, c->kv_heads, c->n_decode + 1));
+      if (need < base) need = base;
+      const int n = stages_for(need);
+      if (n >= want) {
+        bc = cand;
+        nst = n;
+        xs = need;
+        break;
+      }
+      if (cand == 1) break;
+    }
+  }
+  if (!bc) {
     fbh::set_msg("dd_frame: activations too large for two ring stages");
     return FB_ERR_UNSUPPORTED;
   }
+  a.xs_bytes = (int)xs;
+  a.att_off = (int)att_off;
+  a.keep_off = (int)keep_off;
+  a.att_bc = bc;
+  const size_t fixed = xs + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * PK_MAX_STAGES * 8;
   a.nstages = nst;
   const size_t smem = fixed + (size_t)nst * ST_BYTES;
   cudaStream_t st = (cudaStream_t)stream;

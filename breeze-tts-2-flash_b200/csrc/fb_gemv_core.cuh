@@ -1,0 +1,252 @@
+// flashb: the tensor-core GEMV kernel (see fb_gemv.cu for the semantics), shared by two translation units that
+// build it for two stage widths: fb_gemv.cu (FB_ST_KC = 2048, 64 KB stages) and fb_gemv_narrow.cu (1024, 32 KB
+// stages, used when the activation rows leave no room for two 64 KB stages).  The kernel and its launcher live in
+// the stage-width inline namespace of fb_stream.cuh; the argument block and the row helpers do not depend on it.
+#pragma once
+#include "fb_stream.cuh"
+
+namespace fb {
+
+#ifndef FB_GEMV_ARGS_DEFINED
+#define FB_GEMV_ARGS_DEFINED
+struct GemvArgs {
+  const bf16* x;
+  long ldx;
+  const bf16* nw;
+  float eps;
+  const bf16* W0;
+  const bf16* W1;
+  const bf16* W2;
+  int N0, N1;  // segment boundaries (EPI 0/1); EPI 2: W0 = gate, W1 = up
+  int K, N;
+  bf16* y;
+  long ldy;
+  const bf16* res;
+  long ldr;
+  int M;        // activation rows (tensor-core path)
+  int RS;       // units (output rows) per stage
+  int nstages;  // ring depth
+  int xs_bytes; // shared bytes reserved for x
+  unsigned* err;
+};
+
+// Row n of matrix `mat` (EPI 2: 0 = gate, 1 = up; else the q|k|v-style segment holding row n).
+template <int EPI>
+__device__ __forceinline__ const bf16* gv_row(const GemvArgs& a, int n, int mat) {
+  if (EPI == 2) return (mat == 0 ? a.W0 : a.W1) + (size_t)n * a.K;
+  if (n < a.N0) return a.W0 + (size_t)n * a.K;
+  if (n < a.N0 + a.N1) return a.W1 + (size_t)(n - a.N0) * a.K;
+  return a.W2 + (size_t)(n - a.N0 - a.N1) * a.K;
+}
+// First row index after n at which the segment (and so the contiguous source range) changes.
+template <int EPI>
+__device__ __forceinline__ int gv_seg_end(const GemvArgs& a, int n) {
+  if (EPI == 2) return a.N;
+  if (n < a.N0) return a.N0;
+  if (n < a.N0 + a.N1) return a.N0 + a.N1;
+  return a.N;
+}
+
+
+#endif
+
+// Launches the 32 KB-stage build (fb_gemv_narrow.cu); epi / norm select the instantiation.
+int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st);
+
+inline namespace FB_ST_NS_CAT(kc, FB_ST_KC) {
+
+// Tensor-core path (K % 16 == 0): a producer warp streams stages of 16 weight rows x ST_KC columns with 1-D bulk
+// copies into a ring of mbarrier-tracked slots; 8 consumer warps run mma.sync m16n8k16 on them (fb_stream.cuh).
+// NMAT = 2 (gate/up): rows 0..7 of a stage are gate rows of 8 output units, rows 8..15 the matching up rows, so a
+// unit's gate and up sums land in the same reduction slots.
+constexpr int GM_MAX_STAGES = 6;
+constexpr int GM_THREADS = (ST_CWARPS + 1) * 32;
+
+template <int EPI, bool NORM>
+__global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) {
+  constexpr int NMAT = EPI == 2 ? 2 : 1;
+  constexpr int UG = ST_ROWS / NMAT;  // output units per row group
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int M = a.M, K = a.K, NST = a.nstages;
+  const int x_pitch = K * 2 + 16;
+  unsigned char* xs = smem;
+  unsigned char* zero16 = smem + a.xs_bytes;
+  unsigned char* ring = zero16 + 128;
+  float* red = reinterpret_cast<float*>(ring + (size_t)NST * ST_BYTES);
+  float* sums = red + ST_CWARPS * 128;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sums + 128);
+  uint64_t* empty = full + GM_MAX_STAGES;
+  __shared__ float nred[ST_CWARPS][8];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x, bid = blockIdx.x;
+  const int u0 = (int)((long long)a.N * bid / G), u1 = (int)((long long)a.N * (bid + 1) / G);
+  const int ngroups = (u1 - u0 + UG - 1) / UG;
+  const int nkc = (K + ST_KC - 1) / ST_KC;
+  const int T = ngroups * nkc;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ST_CWARPS);
+    }
+    fence_mbar_init();
+  }
+  if (tid < 32) reinterpret_cast<uint32_t*>(zero16)[tid] = 0u;
+  __syncthreads();
+
+  if (warp == ST_CWARPS) {
+    // ------------------------------------------------------------ producer: weights only, runs before pdl_wait
+    int issued = 0;
+    for (int t = 0; t < T; ++t) {
+      const int s = t % NST;
+      if (t >= NST && !mbar_wait_warp(&empty[s], ((t / NST) - 1) & 1, a.err)) break;
+      const int g = t / nkc, kc = t % nkc;
+      const int n0 = u0 + g * UG;
+      const int nu = min(UG, u1 - n0);
+      const int k0 = kc * ST_KC;
+      const int kw = min(ST_KC, K - k0);
+      unsigned char* st = ring + (size_t)s * ST_BYTES;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], (unsigned)(nu * NMAT * kw * 2));
+      __syncwarp();
+      if (lane < ST_ROWS) {
+        const int i = lane % UG, mat = lane / UG;
+        if (i < nu) bulk_g2s(st + lane * ST_PITCH, gv_row<EPI>(a, n0 + i, mat) + k0, (unsigned)(kw * 2), &full[s]);
+      }
+      ++issued;
+    }
+    for (int t = max(0, issued - NST); t < issued; ++t)
+      if (!mbar_wait_warp(&full[t % NST], (t / NST) & 1, a.err)) break;
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  pdl_wait();
+  pdl_trigger();
+  const int ctid = tid;
+  const int kv = K >> 3;
+  {
+    float ss[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) ss[m] = 0.f;
+    for (int i = ctid; i < M * kv; i += ST_CWARPS * 32) {
+      const int m = i / kv, j = i - m * kv;
+      const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + (size_t)j * 8);
+      *reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16) = v;
+      if (NORM) {
+        float f[8];
+        cvt8(v, f);
+        float q = 0.f;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) q = fmaf(f[t], f[t], q);
+#pragma unroll
+        for (int mm = 0; mm < 8; ++mm)
+          if (mm == m) ss[mm] += q;
+      }
+    }
+    if (NORM) {
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const float q = warp_sum(ss[m]);
+        if (lane == 0) nred[warp][m] = q;
+      }
+      named_sync(1, ST_CWARPS * 32);
+      float rs[8];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        float q = 0.f;
+#pragma unroll
+        for (int w = 0; w < ST_CWARPS; ++w) q += nred[w][m];
+        rs[m] = 1.0f / sqrtf(q / (float)K + a.eps);
+      }
+      for (int i = ctid; i < M * kv; i += ST_CWARPS * 32) {
+        const int m = i / kv, j = i - m * kv;
+        uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
+        float f[8], w[8];
+        cvt8(*px, f);
+        cvt8(*reinterpret_cast<const uint4*>(a.nw + (size_t)j * 8), w);
+        float r = 0.f;
+#pragma unroll
+        for (int mm = 0; mm < 8; ++mm)
+          if (mm == m) r = rs[mm];
+        uint4 o;
+        o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
+        o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
+        o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
+        o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
+        *px = o;
+      }
+    }
+    named_sync(1, ST_CWARPS * 32);
+  }
+
+  int t = 0;
+  for (int g = 0; g < ngroups; ++g) {
+    const int n0 = u0 + g * UG;
+    const int nu = min(UG, u1 - n0);
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kc = 0; kc < nkc; ++kc, ++t) {
+      const int s = t % NST;
+      if (!mbar_wait_warp(&full[s], (t / NST) & 1, a.err)) return;
+      const int k0 = kc * ST_KC;
+      stage_mma(ring + (size_t)s * ST_BYTES, min(ST_KC, K - k0), xs, x_pitch, M, k0, zero16, c);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    reduce_warps(c, red, sums, 1);
+    if (ctid < nu * M) {
+      const int i = ctid / M, m = ctid - i * M;
+      const int n = n0 + i;
+      float v;
+      if (EPI == 0) {
+        v = sums[i * 8 + m];
+      } else if (EPI == 1) {
+        v = b2f(a.res[(size_t)m * a.ldr + n]) + rbf(sums[i * 8 + m]);
+      } else {
+        const float gg = rbf(sums[i * 8 + m]);
+        const float uu = rbf(sums[(i + 8) * 8 + m]);
+        v = rbf(gg / (1.0f + expf(-gg))) * uu;
+      }
+      a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+
+// Ring depth and launch for this stage width; returns FB_ERR_UNSUPPORTED when fewer than two stages fit.
+template <int EPI, bool NORM>
+inline int launch_mma_t(GemvArgs& a, cudaStream_t st) {
+  auto kern = gemv_mma_kernel<EPI, NORM>;
+  a.xs_bytes = ((a.M * (a.K * 2 + 16)) + 127) / 128 * 128;
+  const size_t fixed = (size_t)a.xs_bytes + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * GM_MAX_STAGES * 8;
+#ifndef FB_GM_BUDGET
+#define FB_GM_BUDGET 220000
+#endif
+  int nst = (int)((FB_GM_BUDGET - fixed) / ST_BYTES);
+  if (nst < 3) nst = (int)((210 * 1024 - fixed) / ST_BYTES);
+  if (nst > GM_MAX_STAGES) nst = GM_MAX_STAGES;
+  if (nst < 2) {
+    fbh::set_msg("gemv: M*K = %d activations do not fit the shared-memory budget", a.M * a.K);
+    return FB_ERR_UNSUPPORTED;
+  }
+  a.nstages = nst;
+  const size_t smem = fixed + (size_t)nst * ST_BYTES;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && attr_done[dev] < (int)smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      fbh::set_msg("gemv: cudaFuncSetAttribute(%zu bytes): %s", smem, cudaGetErrorString(e));
+      return FB_ERR_CUDA;
+    }
+    attr_done[dev] = (int)smem;
+  }
+  const int grid = a.N < fbh::num_sms() ? a.N : fbh::num_sms();
+  void* args[] = {(void*)&a};
+  return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(GM_THREADS), smem, st, args, true);
+}
+
+
+}  // inline namespace
+}  // namespace fb

@@ -1,0 +1,18 @@
+// flashb: the tensor-core GEMV built for 32 KB stages (16 rows x 1024 columns): used for activation rows too large
+// to leave room for two 64 KB stages (e.g. 8 rows of the 6144-wide down projection, four streams served together).
+#define FB_ST_KC 1024
+#include "fb_gemv_core.cuh"
+
+namespace fb {
+
+int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st) {
+  if (epi == 0 && norm) return launch_mma_t<0, true>(a, st);
+  if (epi == 0) return launch_mma_t<0, false>(a, st);
+  if (epi == 1) return launch_mma_t<1, false>(a, st);
+  if (epi == 2 && norm) return launch_mma_t<2, true>(a, st);
+  if (epi == 2) return launch_mma_t<2, false>(a, st);
+  fbh::set_msg("gemv: no 32 KB-stage build for epilogue %d", epi);
+  return FB_ERR_UNSUPPORTED;
+}
+
+}  // namespace fb

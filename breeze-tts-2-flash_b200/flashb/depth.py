@@ -18,8 +18,8 @@ import torch
 from . import _native, kernels
 from ._native import check
 
-BUILDS = {1: 'full', 2: 'full', 4: 'full'}
-GRIDS = {1: 0, 2: 0, 4: 0}      # 0 = one CTA per SM
+BUILDS = {1: 'full', 2: 'full', 4: 'full', 8: 'full'}
+GRIDS = {1: 0, 2: 0, 4: 0, 8: 0}      # 0 = one CTA per SM
 _state = {}
 
 
@@ -81,8 +81,8 @@ class DepthOps:
         self.desc = {}
 
     def dd2_set_grid(self, B, grid):
-        if B not in (1, 2, 4):
-            raise RuntimeError('B must be 1, 2 or 4')
+        if B not in BUILDS:
+            raise RuntimeError('B must be 1, 2, 4 or 8')
         GRIDS[B] = int(grid)
 
     def _desc(self, B, device):
@@ -118,7 +118,7 @@ def _orig(mod):
 class DepthMegakernel:
     """Depth frame on flashb for an official BreezeDepthDecoderForCausalLM-like object (``model`` +
     ``codebooks_head``), as ``flash/depth.py:97-157``.  Shapes are read from the model instead of asserted."""
-    MAXB = 4
+    MAXB = 8
 
     def __init__(self, depth_decoder, device='cuda', codebook_size=None):
         model = depth_decoder.model
@@ -172,7 +172,7 @@ class _DepthShim:
 
 
 def _eligible(graph):
-    return all(b in (1, 2, 4) for b in (graph.bucket_sizes or [graph.batch_size]))
+    return all(b in BUILDS for b in (graph.bucket_sizes or [graph.batch_size]))
 
 
 def attach(graph):
@@ -183,7 +183,7 @@ def attach(graph):
         graph._mega2 = DepthMegakernel(_DepthShim(graph), device=graph.device,
                                        codebook_size=getattr(graph, 'codec_codebook_size', None))
         graph._mk2_q = {b: torch.zeros(graph.num_decode_codebooks, max(1, b // 2), graph.vocab_size,
-                                       dtype=torch.float32, device=graph.device) for b in (1, 2, 4)}
+                                       dtype=torch.float32, device=graph.device) for b in BUILDS}
     return graph
 
 
@@ -211,7 +211,7 @@ def install(api=None):
         return orig_set_top_k(self, v)
 
     def full_loop(self):
-        if getattr(self, '_mega2', None) is not None and self.batch_size in (1, 2, 4):
+        if getattr(self, '_mega2', None) is not None and self.batch_size in BUILDS:
             return _full_loop_mk(self)
         return orig_full_loop(self)
 

@@ -170,8 +170,8 @@ int flashb_bb_step(const fb_bb_config* cfg, const void* layers_dev, void* scratc
 /* ---------------------------------------------------------------------------------------------- depth frame
  * Replaces the reference's depth frame megakernel dd2_init / dd2_frame (flash/csrc/depth_frame.cu:758-853, 923-934),
  * itself the kernel form of the official DepthDecoderGraph._full_loop (UP/models/cudagraph/depth_decoder_graph.py:
- * 558-654): ONE cooperative launch decodes all n_decode codebooks of a frame for `batch` rows (1, or CFG pairs
- * cond[0..half) | uncond[half..2 half)), sampling each codebook on the device (CFG u + gs (c - u), ids >= codebook_size
+ * 558-654): ONE cooperative launch decodes all n_decode codebooks of a frame for `batch` rows (1, or up to 4 CFG
+ * pairs cond[0..half) | uncond[half..2 half), e.g. several streams served together), sampling each codebook on the device (CFG u + gs (c - u), ids >= codebook_size
  * masked, / temperature, top-k (0 -> min(1024, vocab)), top-p, softmax, token = argmax(p / q)).
  * Layer descriptors (fb_dd_layer[layers]) in device memory; `scratch`: flashb_dd_scratch_bytes() bytes, 256-byte
  * aligned, zeroed once (and after a reported device error).  first_cb [batch] int64; bh [batch, embed_dim] bf16;

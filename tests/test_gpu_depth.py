@@ -89,7 +89,7 @@ def _set(m, p):
     m.guidance_scale.fill_(p['gs'])
 
 
-@pytest.mark.parametrize('B', [1, 2, 4])
+@pytest.mark.parametrize('B', [1, 2, 4, 8])
 def test_depth_forced_logits_match_oracle(B):
     m = _model(B=B)
     c = m.cfg
