@@ -62,7 +62,7 @@ struct DDArgs {
   bf16 *xres, *qb, *ob, *act, *kc, *vc;
   float* logits;
   GridBar* bar;
-  int nstages, xs_bytes, att_off, keep_off, att_bc;
+  int nstages, xs_bytes, att_off, keep_off, att_bc, att_split;
   unsigned* err;
   unsigned long long* trace;
 };
@@ -479,6 +479,86 @@ __device__ __noinline__ void dd_attention(const DDArgs& a, int l, int pos, unsig
   }
 }
 
+// Attention of ONE (batch row b, KV head kvh) pair -- its G query heads -- for the distributed mode (used when the
+// whole batch's K/V would not fit one staging round): the CTA stages q, K and V of the pair, computes as
+// dd_attention does, and writes the output over the pair's q slice in a.qb (no other CTA reads that slice before the
+// barrier that follows).
+template <int G>
+__device__ __noinline__ void dd_attention_pair(const DDArgs& a, int l, int pos, int b, int kvh, unsigned char* att) {
+  const int tid = threadIdx.x;
+  const int QD = a.NH * 128;
+  const int np = pos + 1;
+  bf16* qs = reinterpret_cast<bf16*>(att);
+  bf16* ks = qs + G * 128;
+  bf16* vs = ks + (size_t)np * 128;
+  float* ps = reinterpret_cast<float*>(vs + (size_t)np * 128);
+  bf16* qg = a.qb + (size_t)b * QD + (size_t)kvh * G * 128;
+  const size_t kvoff = ((((size_t)l * a.B + b) * a.NKV + kvh) * a.P) * 128;
+  const int qch = G * 16, kch = np * 16;
+  for (int i = tid; i < qch + 2 * kch; i += PK_CONSUMERS) {
+    if (i < qch) {
+      cp_async16(qs + (size_t)i * 8, qg + (size_t)i * 8);
+    } else {
+      int j = i - qch;
+      const bool isv = j >= kch;
+      if (isv) j -= kch;
+      cp_async16((isv ? vs : ks) + (size_t)j * 8, (isv ? a.vc : a.kc) + kvoff + (size_t)j * 8);
+    }
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  named_sync(1, PK_CONSUMERS);
+  for (int i = tid; i < G * np; i += PK_CONSUMERS) {
+    const int hq = i / np, j = i - hq * np;
+    const uint4* qr = reinterpret_cast<const uint4*>(qs + (size_t)hq * 128);
+    const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)j * 128);
+    float d = 0.f;
+#pragma unroll 4
+    for (int cc = 0; cc < 16; ++cc) {
+      const int c = (cc + j) & 15;
+      float qf[8], kf[8];
+      cvt8(qr[c], qf);
+      cvt8(kr[c], kf);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) d = fmaf(qf[u], kf[u], d);
+    }
+    ps[hq * 32 + j] = rbf(rbf(d) * a.scaling);
+  }
+  named_sync(1, PK_CONSUMERS);
+  if (tid < G) {
+    float* pr = ps + tid * 32;
+    float mx = -INFINITY;
+    for (int j = 0; j < np; ++j) mx = fmaxf(mx, pr[j]);
+    float den = 0.f;
+    for (int j = 0; j < np; ++j) {
+      const float e = expf(pr[j] - mx);
+      pr[j] = e;
+      den += e;
+    }
+    for (int j = 0; j < np; ++j) pr[j] = rbf(pr[j] / den);
+  }
+  named_sync(1, PK_CONSUMERS);
+  for (int i = tid; i < G * 16; i += PK_CONSUMERS) {
+    const int hq = i >> 4, c = i & 15;
+    const float* pr = ps + hq * 32;
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < np; ++j) {
+      float vf[8];
+      cvt8(*reinterpret_cast<const uint4*>(vs + (size_t)j * 128 + c * 8), vf);
+      const float p = pr[j];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o[u] = fmaf(p, vf[u], o[u]);
+    }
+    uint4 ov;
+    ov.x = pack2(o[0], o[1]);
+    ov.y = pack2(o[2], o[3]);
+    ov.z = pack2(o[4], o[5]);
+    ov.w = pack2(o[6], o[7]);
+    *reinterpret_cast<uint4*>(qg + (size_t)hq * 128 + c * 8) = ov;
+  }
+  named_sync(1, PK_CONSUMERS);
+}
+
 // x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.  xres and ob arrive with cp.async (one round trip);
 // the un-normalised x_mid rows are also kept in `keep` ([M][H] bf16) for the down projection's residual.
 __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const DDArgs& a, int M, const bf16* nw,
@@ -697,8 +777,16 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a)
         DD_STAMP(s, tb + 0);
         if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
         DD_STAMP(s, tb + 1);
-        // S2: attention (every CTA, all rows) + o GEMV
-        dd_attention<G>(a, l, pos, xs, xp_q, xs + a.att_off);
+        // S2: attention + o GEMV.  Small batches: every CTA computes every row (no barrier).  Otherwise CTA i takes
+        // (batch row, KV head) pair i, writes it over its q slice, and a barrier precedes the o-projection.
+        if (a.att_split) {
+          if ((int)blockIdx.x < a.B * NKV)
+            dd_attention_pair<G>(a, l, pos, (int)blockIdx.x / NKV, (int)blockIdx.x % NKV, xs + a.att_off);
+          if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
+          load_x(xs, xp_q, a.qb, QD, M, QD, nullptr, 0.f, nred);
+        } else {
+          dd_attention<G>(a, l, pos, xs, xp_q, xs + a.att_off);
+        }
         DD_STAMP(s, tb + 2);
         if (!consume_task<1>(rg, t, H, QD, xs, xp_q, M, zero16, red, sums,
                              [&](int n0, int nu, const float* sm) {
@@ -918,31 +1006,32 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
     int n = fixed < budget ? (int)((budget - fixed) / ST_BYTES) : 0;
     return n > PK_MAX_STAGES ? PK_MAX_STAGES : n;
   };
-  // attention chunk: the most batch rows per round trip that still leave 4 ring stages (else 3, else 2)
-  int bc = 0, nst = 0;
-  size_t xs = base;
-  for (int want = 4; want >= 2 && !bc; --want) {
-    for (int cand = c->batch; cand >= 1; cand = cand > 1 ? (cand + 1) / 2 : 0) {
-      size_t need = al256d(att_off + dd_attn_bytes(cand, c->heads, c->kv_heads, c->n_decode + 1));
-      if (need < base) need = base;
-      const int n = stages_for(need);
-      if (n >= want) {
-        bc = cand;
-        nst = n;
-        xs = need;
-        break;
-      }
-      if (cand == 1) break;
+  // attention: the whole batch in one staging round when that still leaves 4 ring stages; otherwise one
+  // (batch row, KV head) pair per CTA (distributed mode: one extra grid barrier per layer, small staging)
+  const int G = c->heads / c->kv_heads;
+  size_t xs = al256d(att_off + dd_attn_bytes(c->batch, c->heads, c->kv_heads, c->n_decode + 1));
+  if (xs < base) xs = base;
+  int nst = stages_for(xs);
+  a.att_bc = c->batch;
+  a.att_split = 0;
+  if (nst < 4) {
+    const size_t pair = (size_t)G * 256 + 2 * (size_t)(c->n_decode + 1) * 256 + (size_t)G * 32 * 4;
+    xs = al256d(att_off + pair);
+    if (xs < base) xs = base;
+    nst = stages_for(xs);
+    a.att_split = 1;
+    if (c->batch * c->kv_heads > fbh::num_sms()) {
+      fbh::set_msg("dd_frame: batch x kv_heads exceeds the number of SMs");
+      return FB_ERR_UNSUPPORTED;
     }
   }
-  if (!bc) {
+  if (nst < 2) {
     fbh::set_msg("dd_frame: activations too large for two ring stages");
     return FB_ERR_UNSUPPORTED;
   }
   a.xs_bytes = (int)xs;
   a.att_off = (int)att_off;
   a.keep_off = (int)keep_off;
-  a.att_bc = bc;
   const size_t fixed = xs + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * PK_MAX_STAGES * 8;
   a.nstages = nst;
   const size_t smem = fixed + (size_t)nst * ST_BYTES;

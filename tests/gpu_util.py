@@ -32,3 +32,22 @@ def assert_close(got, ref, tol=TOL, what=''):
 
 def bf16_min():
     return torch.finfo(torch.bfloat16).min
+
+
+def assert_argmax_agree(got, ref, min_frac=0.999, what=''):
+    """Argmax agreement over the last axis, the north-star bar (>= 99.9%), counted on rows whose decision is not a
+    near tie: a row where the GPU picks another index counts as a near tie when that index's reference value is
+    within 2 x the measured max |got - ref| of the reference maximum (the two values are closer than the rounding
+    error of the comparison itself).  Every disagreement must be such a near tie."""
+    got = np.asarray(got, np.float32).reshape(-1, np.shape(got)[-1])
+    ref = np.asarray(ref, np.float32).reshape(-1, np.shape(ref)[-1])
+    err = float(np.max(np.abs(got - ref)))
+    ga, ra = np.argmax(got, -1), np.argmax(ref, -1)
+    rows = np.arange(ref.shape[0])
+    tie = ref[rows, ga] >= ref[rows, ra] - 2 * err
+    differ = ga != ra
+    assert not np.any(differ & ~tie), f'{what}: argmax disagreement that is not a near tie (err {err:.3e})'
+    decided = ~(differ & tie)
+    frac = float(np.mean(ga[decided] == ra[decided])) if decided.any() else 1.0
+    assert frac >= min_frac, f'{what}: argmax agreement {frac:.4f} < {min_frac}'
+    return float(np.mean(~differ))

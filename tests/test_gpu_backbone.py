@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import assert_close, np32
+from gpu_util import assert_argmax_agree, assert_close, np32
 from oracle import decode as dec
 
 pytestmark = pytest.mark.gpu
@@ -57,8 +57,7 @@ def test_backbone_step_matches_oracle(step_mode):
     assert_close(g.cfg_logits_buf.cpu().numpy(), cfg_ref, what='cfg logits')
     for li in range(2):
         assert_close(np32(g.static_cache.layers[li].keys)[:, :, pos], kcs[li][:, :, pos], what='k write')
-    agree = np.mean(np.argmax(g.logits_buf.cpu().numpy(), -1) == np.argmax(lg_ref, -1))
-    assert agree == 1.0
+    assert_argmax_agree(g.logits_buf.cpu().numpy(), lg_ref, what='logits')
 
 
 def test_backbone_graph_capture_and_advance_match_eager(step_mode):
@@ -162,7 +161,7 @@ def test_backbone_step_full_depth_argmax_and_determinism():
     torch.cuda.synchronize()
     first = g.cfg_logits_buf.clone()
     assert_close(g.logits_buf.cpu().numpy(), lg_ref, tol=3e-2, what='28-layer logits (compounded)')
-    assert np.mean(np.argmax(g.logits_buf.cpu().numpy(), -1) == np.argmax(lg_ref, -1)) == 1.0
+    assert_argmax_agree(g.logits_buf.cpu().numpy(), lg_ref, what='28-layer logits')
     for L, k in zip(g.static_cache.layers, k0):
         L.keys.copy_(k)
     g.decode_step()

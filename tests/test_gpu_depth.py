@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import assert_close, np32
+from gpu_util import assert_argmax_agree, assert_close, np32
 from oracle import depth as odepth
 from oracle import sampler as osmp
 
@@ -101,7 +101,7 @@ def test_depth_forced_logits_match_oracle(B):
                                             m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
     for s in range(c.n_decode):
         assert_close(logits[s], lg_ref[s], what=f'step {s} logits')
-    assert np.mean(np.argmax(logits, -1) == np.argmax(lg_ref, -1)) >= 0.999
+    assert_argmax_agree(logits, lg_ref, what='depth logits')
     np.testing.assert_array_equal(m.tok_buf.cpu().numpy(), np.clip(forced[-1], 0, c.vocab - 1))
     _check_sampler(m, logits, outtok)
 
@@ -129,11 +129,13 @@ def test_depth_free_running_equals_forced_oracle():
     np.testing.assert_array_equal(tok, outtok[:, -1])
 
 
-def test_depth_full_size_forced_and_sampler():
-    """The synthetic full-size depth decoder (4 layers, hidden 1024, 16 codebooks of 2048)."""
-    m = _model(small=False, B=2, seed=5)
+@pytest.mark.parametrize('B', [2, 8])
+def test_depth_full_size_forced_and_sampler(B):
+    """The synthetic full-size depth decoder (4 layers, hidden 1024, 16 codebooks of 2048).  B = 8 (four CFG pairs)
+    runs the distributed attention mode (one (row, KV head) pair per CTA) and one sampler CTA per pair."""
+    m = _model(small=False, B=B, seed=5)
     c = m.cfg
-    forced = np.random.default_rng(5).integers(0, c.vocab, (c.n_decode, 2))
+    forced = np.random.default_rng(5).integers(0, c.vocab, (c.n_decode, B))
     outtok, logits, _ = _run(m, forced)
     W = _weights(m)
     temp, topk, topp, ds, gs = _params(m)
@@ -141,7 +143,7 @@ def test_depth_full_size_forced_and_sampler():
                                       m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
     for s in range(c.n_decode):
         assert_close(logits[s], lg_ref[s], what=f'step {s} logits')
-    assert np.mean(np.argmax(logits, -1) == np.argmax(lg_ref, -1)) >= 0.999
+    assert_argmax_agree(logits, lg_ref, what='depth logits')
     _check_sampler(m, logits, outtok)
 
 

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import synth
-from gpu_util import TOL, assert_close, np32
+from gpu_util import TOL, assert_argmax_agree, assert_close, np32
 from oracle import prefill as opf
 from oracle.bf16 import bits_to_f32
 
@@ -67,8 +67,7 @@ def test_prefill_matches_oracle(L, pads):
     ref = opf.prefill_attention(np32(q), np32(k), np32(v), np32(m), 128 ** -0.5)
     live = _live(B, L, pads)
     assert_close(np32(out)[live], ref[live], what=f'L={L}')
-    agree = np.mean(np.argmax(np32(out)[live], -1) == np.argmax(ref[live], -1))
-    assert agree >= 0.999
+    assert_argmax_agree(np32(out)[live], ref[live], what=f'L={L}')
 
 
 def test_prefill_fp32_mask_noncausal_and_no_mask():
