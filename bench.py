@@ -47,7 +47,7 @@ def args_():
     p.add_argument('--streams', type=int, default=N_STREAMS, help='streams over the whole job')
     p.add_argument('--prompt', type=int, default=PROMPT)
     p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone', 'prefill'])
-    p.add_argument('--group', type=int, default=4, choices=[1, 2, 4],
+    p.add_argument('--group', type=int, default=8, choices=[1, 2, 4, 8],
                    help='streams decoded together per launch (their GEMV rows share every weight read)')
     p.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample length')
     p.add_argument('--no-cpu-baseline', action='store_true')

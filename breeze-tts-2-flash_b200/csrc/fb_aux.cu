@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(256) embed_rope_kernel(const long long* __rest
   }
 }
 
-constexpr int LM_MAXB = 8;
+constexpr int LM_MAXB = 16;
 constexpr int LM_THREADS = 256;
 
 // grid = #SMs; each CTA normalises x (redundantly) into shared memory as fp32, then one warp per vocab row.

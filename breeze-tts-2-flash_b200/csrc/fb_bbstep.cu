@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) bb_step_kernel(const BBArgs a) 
   uint64_t* full = reinterpret_cast<uint64_t*>(sums + 128);
   uint64_t* empty = full + PK_MAX_STAGES;
   __shared__ __align__(16) AttSmem att;
-  __shared__ float nred[ST_CWARPS * 8];
+  __shared__ float nred[ST_CWARPS * 16];   // load_x keeps up to 16 rows of norm partials
   __shared__ int s_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

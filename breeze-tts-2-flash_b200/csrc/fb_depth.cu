@@ -35,7 +35,7 @@
 
 namespace fb {
 
-constexpr int DD_MAXB = 8;      // batch rows (four CFG pairs)
+constexpr int DD_MAXB = 16;     // batch rows (eight CFG pairs)
 constexpr int DD_MAXV = 4096;   // sampler vocabulary bound (composite key packs 12 index bits)
 
 struct DDLayer {
@@ -62,7 +62,7 @@ struct DDArgs {
   bf16 *xres, *qb, *ob, *act, *kc, *vc;
   float* logits;
   GridBar* bar;
-  int nstages, xs_bytes, att_off, keep_off, att_bc, att_split;
+  int nstages, xs_bytes, att_off, keep_off, att_bc, att_split, d_xchunk;
   unsigned* err;
   unsigned long long* trace;
 };
@@ -563,7 +563,7 @@ __device__ __noinline__ void dd_attention_pair(const DDArgs& a, int l, int pos, 
 // the un-normalised x_mid rows are also kept in `keep` ([M][H] bf16) for the down projection's residual.
 __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const DDArgs& a, int M, const bf16* nw,
                                          float* nred, bf16* keep) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x;
   const int H = a.H, kv = H >> 3;
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
@@ -572,9 +572,6 @@ __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const D
   }
   cp_async_commit();
   cp_async_wait<0>();
-  float ss[8];
-#pragma unroll
-  for (int m = 0; m < 8; ++m) ss[m] = 0.f;
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
     uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
@@ -583,12 +580,8 @@ __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const D
     cvt8(*px, x);
     cvt8(*pk, o);
     float v[8];
-    float q = 0.f;
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      v[u] = rbf(x[u] + o[u]);
-      q = fmaf(v[u], v[u], q);
-    }
+    for (int u = 0; u < 8; ++u) v[u] = rbf(x[u] + o[u]);
     uint4 w;
     w.x = pack2(v[0], v[1]);
     w.y = pack2(v[2], v[3]);
@@ -596,284 +589,383 @@ __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const D
     w.w = pack2(v[6], v[7]);
     *px = w;
     *pk = w;
-#pragma unroll
-    for (int mm = 0; mm < 8; ++mm)
-      if (mm == m) ss[mm] += q;
-  }
-#pragma unroll
-  for (int m = 0; m < 8; ++m) {
-    const float q = warp_sum(ss[m]);
-    if (lane == 0) nred[warp * 8 + m] = q;
   }
   named_sync(1, PK_CONSUMERS);
-  float rs[8];
-#pragma unroll
-  for (int m = 0; m < 8; ++m) {
-    float q = 0.f;
-#pragma unroll
-    for (int w = 0; w < ST_CWARPS; ++w) q += nred[w * 8 + m];
-    rs[m] = 1.0f / sqrtf(q / (float)H + a.eps);
-  }
-  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
-    const int m = i / kv, j = i - m * kv;
-    uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
-    float f[8], w[8];
-    cvt8(*px, f);
-    cvt8(*reinterpret_cast<const uint4*>(nw + (size_t)j * 8), w);
-    float r = 0.f;
-#pragma unroll
-    for (int mm = 0; mm < 8; ++mm)
-      if (mm == m) r = rs[mm];
-    uint4 o;
-    o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
-    o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
-    o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
-    o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
-    *px = o;
-  }
+  row_rms(xs, x_pitch, M, H, a.eps, nred);
+  apply_rms(xs, x_pitch, M, H, nw, nred);
   named_sync(1, PK_CONSUMERS);
 }
 
-template <int G>
-__global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const DDArgs a) {
+// ------------------------------------------------------------------------------------------------ frame kernel
+// The kernel body only sequences the phases below; every phase is a separate (non-inlined) function with its own
+// register budget: 9 warps per CTA cap a thread at 168 registers, and spilled values would reload from L2 (the L1
+// left beside 220 KB of shared memory is small).  Per-CTA state the phases share lives in file-scope shared memory.
+__shared__ float g_dd_nred[ST_CWARPS * 16];
+__shared__ int g_dd_int[32];
+__shared__ long long g_dd_tok[DD_MAXB];            // tokens fed to the next step (this CTA's copy)
+__shared__ __align__(16) bf16 g_dd_cs[2][128];     // [cos|sin][dim] of the sub-step's position
+
+struct DDSm {
+  unsigned char* xs;
+  unsigned char* zero16;
+  float* red;
+  float* sums;
+  Ring rg;
+};
+template <int NT>
+__device__ __forceinline__ DDSm dd_smem(const DDArgs& a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  const int H = a.H, AE = a.AE, NH = a.NH, NKV = a.NKV, F = a.F, V = a.V, NST = a.nstages;
-  unsigned char* xs = smem;
-  unsigned char* zero16 = smem + a.xs_bytes;
-  unsigned char* ringb = zero16 + 128;
-  float* red = reinterpret_cast<float*>(ringb + (size_t)NST * ST_BYTES);
-  float* sums = red + ST_CWARPS * 128;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sums + 128);
-  uint64_t* empty = full + PK_MAX_STAGES;
-  __shared__ float nred[ST_CWARPS * 8];
-  __shared__ int s_int[32];
-  __shared__ long long s_tok[DD_MAXB];     // tokens fed to the next step (this CTA's copy of the sampler result)
-  __shared__ __align__(16) bf16 s_cs[2][128];   // [cos|sin][dim] of the sub-step's position
+  DDSm m;
+  m.xs = smem;
+  m.zero16 = smem + a.xs_bytes;
+  unsigned char* ringb = m.zero16 + 128;
+  m.red = reinterpret_cast<float*>(ringb + (size_t)a.nstages * ST_BYTES);
+  m.sums = m.red + ST_CWARPS * 128 * NT;
+  uint64_t* full = reinterpret_cast<uint64_t*>(m.sums + 128 * NT);
+  m.rg = Ring{ringb, full, full + PK_MAX_STAGES, a.nstages};
+  return m;
+}
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  if (tid == 0) {
-    for (int s = 0; s < NST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], ST_CWARPS);
-    }
-    fence_mbar_init();
-  }
-  if (tid < 32) reinterpret_cast<uint32_t*>(zero16)[tid] = 0u;
-  __syncthreads();
-  Ring rg{ringb, full, empty, NST};
+// Consumer cursor: ring stage counter, grid-barrier epoch, ok (0 once a bounded wait gave up).
+struct DDCur {
+  int t;
+  unsigned epoch;
+  int ok;
+};
+
+// Producer warp: every weight slice of the frame, in the consumers' order, through the ring.
+template <int NT>
+__device__ __noinline__ void dd_producer(const DDArgs& a) {
+  DDSm m = dd_smem<NT>(a);
+  const int H = a.H, AE = a.AE, NH = a.NH, NKV = a.NKV, F = a.F, V = a.V;
   const int QKVU = (NH + 2 * NKV) * 64;  // rotary pair units
-  auto qkv_row = [&](const DDLayer& W) {
-    return [&W, NH, NKV, H](int u, int mat) -> const bf16* {
-      const int hh = u >> 6, d = (u & 63) + mat * 64;
-      if (hh < NH) return W.wq + (size_t)(hh * 128 + d) * H;
-      if (hh < NH + NKV) return W.wk + (size_t)((hh - NH) * 128 + d) * H;
-      return W.wv + (size_t)((hh - NH - NKV) * 128 + d) * H;
-    };
-  };
+  const int L = a.L, NCB = a.NCB;
+  const bf16 *const proj = a.proj, *const head_t = a.head_t;
+  const DDLayer* const layers = a.layers;
+  unsigned* const err = a.err;
+  int t = 0;
+  bool ok = true;
+  for (int s = 0; s < NCB && ok; ++s) {
+    for (int sub = 0; sub < (s == 0 ? 2 : 1) && ok; ++sub) {
+      ok = ok && produce_task<1>(m.rg, t, H, AE, [&](int n, int) { return proj + (size_t)n * AE; }, err);
+      for (int l = 0; l < L && ok; ++l) {
+        const DDLayer W = layers[l];   // by value: the row lambdas below then read registers only
+        ok = ok && produce_task<2>(m.rg, t, QKVU, H, [&](int u, int mat) -> const bf16* {
+          const int hh = u >> 6, d = (u & 63) + mat * 64;
+          if (hh < NH) return W.wq + (size_t)(hh * 128 + d) * H;
+          if (hh < NH + NKV) return W.wk + (size_t)((hh - NH) * 128 + d) * H;
+          return W.wv + (size_t)((hh - NH - NKV) * 128 + d) * H;
+        }, err);
+        ok = ok && produce_task<1>(m.rg, t, H, NH * 128,
+                                   [&](int n, int) { return W.wo + (size_t)n * NH * 128; }, err);
+        ok = ok && produce_task<2>(m.rg, t, F, H,
+                                   [&](int n, int mat) { return (mat ? W.wu : W.wg) + (size_t)n * H; }, err);
+        ok = ok && produce_task<1>(m.rg, t, H, F, [&](int n, int) { return W.wd + (size_t)n * F; }, err);
+      }
+    }
+    ok = ok && produce_task<1>(m.rg, t, V, H, [&](int n, int) { return head_t + ((size_t)s * V + n) * H; }, err);
+  }
+  // never leave with copies in flight into this CTA's shared memory
+  for (int u = max(0, t - m.rg.nst); u < t; ++u)
+    if (!mbar_wait_warp(&m.rg.full[u % m.rg.nst], (u / m.rg.nst) & 1, err)) break;
+}
 
-  // Codebook step 0 feeds two tokens (positions 0 and 1); they run as two sub-steps of one token each, which gives
-  // the same values (GEMV rows are independent, position 0 does not attend to position 1) with M = B rows always.
-  if (warp == ST_CWARPS) {
-    // ------------------------------------------------------------------ producer
-    int t = 0;
-    bool ok = true;
-    for (int s = 0; s < a.NCB && ok; ++s) {
-      for (int sub = 0; sub < (s == 0 ? 2 : 1) && ok; ++sub) {
-        ok = ok && produce_task<1>(rg, t, H, AE, [&](int n, int) { return a.proj + (size_t)n * AE; }, a.err);
-        for (int l = 0; l < a.L && ok; ++l) {
-          const DDLayer W = a.layers[l];
-          ok = ok && produce_task<2>(rg, t, QKVU, H, qkv_row(W), a.err);
-          ok = ok && produce_task<1>(rg, t, H, NH * 128, [&](int n, int) { return W.wo + (size_t)n * NH * 128; },
-                                     a.err);
-          ok = ok && produce_task<2>(rg, t, F, H,
-                                     [&](int n, int mat) { return (mat ? W.wu : W.wg) + (size_t)n * H; }, a.err);
-          ok = ok && produce_task<1>(rg, t, H, F, [&](int n, int) { return W.wd + (size_t)n * F; }, a.err);
+// E: gather the token embeddings (cp.async, one round trip, with the position's rotary rows) -> projector -> xres
+template <int NT>
+__device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int sub, int pos) {
+  constexpr int MS = 8 * NT;
+  DDSm m = dd_smem<NT>(a);
+  const int tid = threadIdx.x, M = a.B, AE = a.AE, H = a.H, V = a.V;
+  const int xp_ae = AE * 2 + 16;
+  bf16* const xres = a.xres;   // locals: stores through them cannot alias the argument block
+  DD_STAMP(s, 0);
+  const int kv = AE >> 3;
+  const long long rows = (long long)(a.NCB + 1) * V;
+  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
+    const int b = i / kv, j = i - b * kv;
+    const bf16* src;
+    if (s == 0 && sub == 0) {
+      src = a.bh + (size_t)b * AE;
+    } else {
+      long long id = (s == 0) ? __ldcg(a.first_cb + b) : g_dd_tok[b] + (long long)s * V;
+      id = id < 0 ? 0 : (id >= rows ? rows - 1 : id);
+      src = a.embed + (size_t)id * AE;
+    }
+    cp_async16(m.xs + (size_t)b * xp_ae + j * 16, src + (size_t)j * 8);
+  }
+  if (tid < 32) {    // cos / sin rows of the position, 16 chunks of 16 bytes each
+    const int tab = tid >> 4, cc = tid & 15;
+    cp_async16(&g_dd_cs[tab][cc * 8], (tab ? a.sin_tab : a.cos_tab) + (size_t)pos * 128 + cc * 8);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  named_sync(1, PK_CONSUMERS);
+  if (!consume_task<1, NT>(m.rg, c.t, H, AE, m.xs, xp_ae, M, m.zero16, m.red, m.sums,
+                           [&](int n0, int nu, const float* sm) {
+                             if (tid < nu * M) {
+                               const int i = tid / M, r = tid - i * M;
+                               xres[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
+                             }
+                           }, a.err)) {
+    c.ok = 0;
+    return c;
+  }
+  DD_STAMP(s, 1);
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  DD_STAMP(s, 2);
+  return c;
+}
+
+// S1: RMSNorm + q|k|v (rotary pairs) + RoPE + KV write at `pos`
+template <int NT>
+__device__ __noinline__ DDCur dd_phase_s1(const DDArgs& a, DDCur c, int s, int pos, int l) {
+  constexpr int MS = 8 * NT;
+  DDSm m = dd_smem<NT>(a);
+  const int tid = threadIdx.x, M = a.B, H = a.H, NH = a.NH, NKV = a.NKV, QD = NH * 128;
+  const int tb = 3 + 9 * l;
+  const int P = a.P;
+  bf16 *const qb = a.qb, *const kcache = a.kc, *const vcache = a.vc;
+  load_x(m.xs, H * 2 + 16, a.xres, H, M, H, a.layers[l].ln1, a.eps, g_dd_nred);
+  if (!consume_task<2, NT>(m.rg, c.t, (NH + 2 * NKV) * 64, H, m.xs, H * 2 + 16, M, m.zero16, m.red, m.sums,
+                           [&](int n0, int nu, const float* sm) {
+                             if (tid < nu * M) {
+                               const int i = tid / M, b = tid - i * M;
+                               const int u = n0 + i, hh = u >> 6, d = u & 63;
+                               float y0 = rbf(sm[i * MS + b]), y1 = rbf(sm[(i + 8) * MS + b]);
+                               if (hh < NH + NKV) {
+                                 const float c0 = b2f(g_dd_cs[0][d]), s0 = b2f(g_dd_cs[1][d]);
+                                 const float c1 = b2f(g_dd_cs[0][d + 64]), s1 = b2f(g_dd_cs[1][d + 64]);
+                                 const float o0 = rbf(rbf(y0 * c0) + rbf(-y1 * s0));
+                                 const float o1 = rbf(rbf(y1 * c1) + rbf(y0 * s1));
+                                 y0 = o0;
+                                 y1 = o1;
+                               }
+                               if (hh < NH) {
+                                 qb[(size_t)b * QD + hh * 128 + d] = __float2bfloat16_rn(y0);
+                                 qb[(size_t)b * QD + hh * 128 + d + 64] = __float2bfloat16_rn(y1);
+                               } else {
+                                 const int kvh = hh < NH + NKV ? hh - NH : hh - NH - NKV;
+                                 bf16* cache = hh < NH + NKV ? kcache : vcache;
+                                 bf16* dst = cache + ((((size_t)l * M + b) * NKV + kvh) * P + pos) * 128;
+                                 dst[d] = __float2bfloat16_rn(y0);
+                                 dst[d + 64] = __float2bfloat16_rn(y1);
+                               }
+                             }
+                           }, a.err)) {
+    c.ok = 0;
+    return c;
+  }
+  DD_STAMP(s, tb + 0);
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  DD_STAMP(s, tb + 1);
+  return c;
+}
+
+// S2: attention + o GEMV.  Small batches: every CTA computes every row (no barrier).  Otherwise CTA i takes
+// (batch row, KV head) pair i, writes it over its q slice, and a barrier precedes the o-projection.
+template <int G, int NT>
+__device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int pos, int l) {
+  constexpr int MS = 8 * NT;
+  DDSm m = dd_smem<NT>(a);
+  const int tid = threadIdx.x, M = a.B, H = a.H, NKV = a.NKV, QD = a.NH * 128;
+  const int xp_q = QD * 2 + 16;
+  const int tb = 3 + 9 * l;
+  bf16* const ob = a.ob;
+  if (a.att_split) {
+    if ((int)blockIdx.x < a.B * NKV)
+      dd_attention_pair<G>(a, l, pos, (int)blockIdx.x / NKV, (int)blockIdx.x % NKV, m.xs + a.att_off);
+    if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) {
+      c.ok = 0;
+      return c;
+    }
+    load_x(m.xs, xp_q, a.qb, QD, M, QD, nullptr, 0.f, g_dd_nred);
+  } else {
+    dd_attention<G>(a, l, pos, m.xs, xp_q, m.xs + a.att_off);
+  }
+  DD_STAMP(s, tb + 2);
+  if (!consume_task<1, NT>(m.rg, c.t, H, QD, m.xs, xp_q, M, m.zero16, m.red, m.sums,
+                           [&](int n0, int nu, const float* sm) {
+                             if (tid < nu * M) {
+                               const int i = tid / M, r = tid - i * M;
+                               ob[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
+                             }
+                           }, a.err)) {
+    c.ok = 0;
+    return c;
+  }
+  DD_STAMP(s, tb + 3);
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  DD_STAMP(s, tb + 4);
+  return c;
+}
+
+// S3: RMSNorm(bf16(x + o)) + gate|up + SiLU*up; the un-normalised x_mid rows stay in shared memory for S4
+template <int NT>
+__device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l) {
+  constexpr int MS = 8 * NT;
+  DDSm m = dd_smem<NT>(a);
+  const int tid = threadIdx.x, M = a.B, H = a.H, F = a.F;
+  const int tb = 3 + 9 * l;
+  bf16* xkeep = reinterpret_cast<bf16*>(m.xs + a.keep_off);
+  bf16* const act = a.act;
+  dd_load_mid(m.xs, H * 2 + 16, a, M, a.layers[l].ln2, g_dd_nred, xkeep);
+  if (!consume_task<2, NT>(m.rg, c.t, F, H, m.xs, H * 2 + 16, M, m.zero16, m.red, m.sums,
+                           [&](int n0, int nu, const float* sm) {
+                             if (tid < nu * M) {
+                               const int i = tid / M, r = tid - i * M;
+                               const float g = rbf(sm[i * MS + r]);
+                               const float u = rbf(sm[(i + 8) * MS + r]);
+                               act[(size_t)r * F + n0 + i] = __float2bfloat16_rn(rbf(g / (1.0f + expf(-g))) * u);
+                             }
+                           }, a.err)) {
+    c.ok = 0;
+    return c;
+  }
+  DD_STAMP(s, tb + 5);
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  DD_STAMP(s, tb + 6);
+  return c;
+}
+
+// S4: down + residual: xres = bf16(x_mid + bf16(d)); act rows too large to stage whole go in column chunks
+template <int NT>
+__device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l) {
+  constexpr int MS = 8 * NT;
+  DDSm m = dd_smem<NT>(a);
+  const int tid = threadIdx.x, M = a.B, H = a.H, F = a.F;
+  const int tb = 3 + 9 * l;
+  const bf16* xkeep = reinterpret_cast<const bf16*>(m.xs + a.keep_off);
+  bf16* const xres = a.xres;
+  if (!a.d_xchunk) load_x(m.xs, F * 2 + 16, a.act, F, M, F, nullptr, 0.f, g_dd_nred);
+  if (!consume_task<1, NT>(m.rg, c.t, H, F, m.xs, a.d_xchunk ? ST_KC * 2 + 16 : F * 2 + 16, M, m.zero16, m.red,
+                           m.sums,
+                           [&](int n0, int nu, const float* sm) {
+                             if (tid < nu * M) {
+                               const int i = tid / M, r = tid - i * M, n = n0 + i;
+                               const float xm = b2f(xkeep[(size_t)r * H + n]);
+                               xres[(size_t)r * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * MS + r]));
+                             }
+                           }, a.err, a.d_xchunk ? a.act : nullptr, F)) {
+    c.ok = 0;
+    return c;
+  }
+  DD_STAMP(s, tb + 7);
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  DD_STAMP(s, tb + 8);
+  return c;
+}
+
+// S5: final RMSNorm + codebook head -> fp32 logits
+template <int NT>
+__device__ __noinline__ DDCur dd_phase_s5(const DDArgs& a, DDCur c, int s) {
+  constexpr int MS = 8 * NT;
+  DDSm m = dd_smem<NT>(a);
+  const int tid = threadIdx.x, M = a.B, H = a.H, V = a.V;
+  const int te = 3 + 9 * a.L;
+  float *const logits = a.logits, *const dbg = a.dbg;
+  load_x(m.xs, H * 2 + 16, a.xres, H, M, H, a.normf, a.eps, g_dd_nred);
+  if (!consume_task<1, NT>(m.rg, c.t, V, H, m.xs, H * 2 + 16, M, m.zero16, m.red, m.sums,
+                           [&](int n0, int nu, const float* sm) {
+                             if (tid < nu * M) {
+                               const int i = tid / M, b = tid - i * M;
+                               const float v = sm[i * MS + b];
+                               logits[(size_t)b * V + n0 + i] = v;
+                               if (dbg) dbg[((size_t)s * M + b) * V + n0 + i] = v;
+                             }
+                           }, a.err)) {
+    c.ok = 0;
+    return c;
+  }
+  DD_STAMP(s, te + 0);
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  DD_STAMP(s, te + 1);
+  return c;
+}
+
+// Sampling.  One CFG pair: every CTA samples it (no barrier follows), CTA 0 publishes.  Several pairs: CTA h samples
+// pair h and publishes it, then one barrier hands every CTA the fed-forward tokens (one barrier instead of `half`
+// samplers in series on every CTA).
+__device__ __noinline__ DDCur dd_phase_sample(const DDArgs& a, DDCur c, int s) {
+  const int tid = threadIdx.x, V = a.V;
+  const int half = a.B >= 2 ? a.B / 2 : 1;
+  const int te = 3 + 9 * a.L;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const bool redundant = half == 1;
+  const int h_begin = redundant ? 0 : (int)blockIdx.x;
+  const int h_end = redundant ? 1 : ((int)blockIdx.x < half ? (int)blockIdx.x + 1 : 0);
+  for (int h = h_begin; h < h_end; ++h) {
+    int tokv = dd_sample(a, s, h, smem, g_dd_int);
+    tokv = tokv < 0 ? 0 : (tokv > V - 1 ? V - 1 : tokv);
+    if (tid == 0) {
+      for (int r = 0; r < (a.B >= 2 ? 2 : 1); ++r) {
+        const int b = h + r * half;
+        long long fed = tokv;
+        if (a.forced) {
+          const long long fc = a.forced[(size_t)s * a.B + b];
+          fed = fc < 0 ? 0 : (fc > V - 1 ? V - 1 : fc);
+        }
+        g_dd_tok[b] = fed;
+        if (blockIdx.x == 0 || !redundant) {
+          a.outtok[(size_t)b * a.NCB + s] = tokv;
+          a.tokbuf[b] = fed;
         }
       }
-      ok = ok && produce_task<1>(rg, t, V, H, [&](int n, int) { return a.head_t + ((size_t)s * V + n) * H; },
-                                 a.err);
     }
-    for (int u = max(0, t - NST); u < t; ++u)
-      if (!mbar_wait_warp(&full[u % NST], (u / NST) & 1, a.err)) break;
+  }
+  if (!redundant && s + 1 < a.NCB) {
+    if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) {
+      c.ok = 0;
+      return c;
+    }
+    if (tid < a.B) g_dd_tok[tid] = __ldcg(a.tokbuf + tid);
+  }
+  named_sync(1, PK_CONSUMERS);
+  DD_STAMP(s, te + 7);
+  return c;
+}
+
+template <int G, int NT>
+__global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_constant__ DDArgs a) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  {
+    DDSm m = dd_smem<NT>(a);
+    if (tid == 0) {
+      for (int s = 0; s < m.rg.nst; ++s) {
+        mbar_init(&m.rg.full[s], 1);
+        mbar_init(&m.rg.empty[s], ST_CWARPS);
+      }
+      fence_mbar_init();
+    }
+    if (tid < 32) reinterpret_cast<uint32_t*>(m.zero16)[tid] = 0u;
+  }
+  __syncthreads();
+  if (warp == ST_CWARPS) {
+    dd_producer<NT>(a);
     return;
   }
-
-  // ------------------------------------------------------------------ consumers
-  unsigned epoch = 0;
-  int t = 0;
-  const int half = a.B >= 2 ? a.B / 2 : 1;
-  const int M = a.B;
-  const int QD = NH * 128;
-  const int xp_ae = AE * 2 + 16, xp_h = H * 2 + 16, xp_q = QD * 2 + 16, xp_f = F * 2 + 16;
+  // Codebook step 0 feeds two tokens (positions 0 and 1); they run as two sub-steps of one token each, which gives
+  // the same values (GEMV rows are independent, position 0 does not attend to position 1) with M = B rows always.
+  DDCur c{0, 0u, 1};
   for (int s = 0; s < a.NCB; ++s) {
     for (int sub = 0; sub < (s == 0 ? 2 : 1); ++sub) {
       const int pos = s == 0 ? sub : s + 1;
-      DD_STAMP(s, 0);
-      // E: gather the token embeddings (cp.async, one round trip, with the position's rotary rows) -> projector
-      {
-        const int kv = AE >> 3;
-        const long long rows = (long long)(a.NCB + 1) * V;
-        for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
-          const int b = i / kv, j = i - b * kv;
-          const bf16* src;
-          if (s == 0 && sub == 0) {
-            src = a.bh + (size_t)b * AE;
-          } else {
-            long long id = (s == 0) ? __ldcg(a.first_cb + b) : s_tok[b] + (long long)s * V;
-            id = id < 0 ? 0 : (id >= rows ? rows - 1 : id);
-            src = a.embed + (size_t)id * AE;
-          }
-          cp_async16(xs + (size_t)b * xp_ae + j * 16, src + (size_t)j * 8);
-        }
-        if (tid < 32) {    // cos / sin rows of the position, 16 chunks of 16 bytes each
-          const int tab = tid >> 4, c = tid & 15;
-          cp_async16(&s_cs[tab][c * 8], (tab ? a.sin_tab : a.cos_tab) + (size_t)pos * 128 + c * 8);
-        }
-        cp_async_commit();
-        cp_async_wait<0>();
-        named_sync(1, PK_CONSUMERS);
-        if (!consume_task<1>(rg, t, H, AE, xs, xp_ae, M, zero16, red, sums,
-                             [&](int n0, int nu, const float* sm) {
-                               if (tid < nu * M) {
-                                 const int i = tid / M, m = tid - i * M;
-                                 a.xres[(size_t)m * H + n0 + i] = __float2bfloat16_rn(sm[i * 8 + m]);
-                               }
-                             }, a.err)) return;
-        DD_STAMP(s, 1);
-        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-        DD_STAMP(s, 2);
-      }
+      c = dd_phase_e<NT>(a, c, s, sub, pos);
+      if (!c.ok) return;
       for (int l = 0; l < a.L; ++l) {
-        const int tb = 3 + 9 * l;
-        const DDLayer W = a.layers[l];
-        // S1: RMSNorm + q|k|v (rotary pairs) + RoPE + KV write
-        load_x(xs, xp_h, a.xres, H, M, H, W.ln1, a.eps, nred);
-        if (!consume_task<2>(rg, t, QKVU, H, xs, xp_h, M, zero16, red, sums,
-                             [&](int n0, int nu, const float* sm) {
-                               if (tid < nu * M) {
-                                 const int i = tid / M, b = tid - i * M;
-                                 const int u = n0 + i, hh = u >> 6, d = u & 63;
-                                 float y0 = rbf(sm[i * 8 + b]), y1 = rbf(sm[(i + 8) * 8 + b]);
-                                 if (hh < NH + NKV) {
-                                   const float c0 = b2f(s_cs[0][d]), s0 = b2f(s_cs[1][d]);
-                                   const float c1 = b2f(s_cs[0][d + 64]), s1 = b2f(s_cs[1][d + 64]);
-                                   const float o0 = rbf(rbf(y0 * c0) + rbf(-y1 * s0));
-                                   const float o1 = rbf(rbf(y1 * c1) + rbf(y0 * s1));
-                                   y0 = o0;
-                                   y1 = o1;
-                                 }
-                                 if (hh < NH) {
-                                   a.qb[(size_t)b * QD + hh * 128 + d] = __float2bfloat16_rn(y0);
-                                   a.qb[(size_t)b * QD + hh * 128 + d + 64] = __float2bfloat16_rn(y1);
-                                 } else {
-                                   const int kvh = hh < NH + NKV ? hh - NH : hh - NH - NKV;
-                                   bf16* cache = hh < NH + NKV ? a.kc : a.vc;
-                                   bf16* dst = cache + ((((size_t)l * a.B + b) * NKV + kvh) * a.P + pos) * 128;
-                                   dst[d] = __float2bfloat16_rn(y0);
-                                   dst[d + 64] = __float2bfloat16_rn(y1);
-                                 }
-                               }
-                             }, a.err)) return;
-        DD_STAMP(s, tb + 0);
-        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-        DD_STAMP(s, tb + 1);
-        // S2: attention + o GEMV.  Small batches: every CTA computes every row (no barrier).  Otherwise CTA i takes
-        // (batch row, KV head) pair i, writes it over its q slice, and a barrier precedes the o-projection.
-        if (a.att_split) {
-          if ((int)blockIdx.x < a.B * NKV)
-            dd_attention_pair<G>(a, l, pos, (int)blockIdx.x / NKV, (int)blockIdx.x % NKV, xs + a.att_off);
-          if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-          load_x(xs, xp_q, a.qb, QD, M, QD, nullptr, 0.f, nred);
-        } else {
-          dd_attention<G>(a, l, pos, xs, xp_q, xs + a.att_off);
-        }
-        DD_STAMP(s, tb + 2);
-        if (!consume_task<1>(rg, t, H, QD, xs, xp_q, M, zero16, red, sums,
-                             [&](int n0, int nu, const float* sm) {
-                               if (tid < nu * M) {
-                                 const int i = tid / M, m = tid - i * M;
-                                 a.ob[(size_t)m * H + n0 + i] = __float2bfloat16_rn(sm[i * 8 + m]);
-                               }
-                             }, a.err)) return;
-        DD_STAMP(s, tb + 3);
-        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-        DD_STAMP(s, tb + 4);
-        // S3: RMSNorm(bf16(x + o)) + gate|up + SiLU*up
-        bf16* xkeep = reinterpret_cast<bf16*>(xs + a.keep_off);  // x_mid rows for the down projection's residual
-        dd_load_mid(xs, xp_h, a, M, W.ln2, nred, xkeep);
-        if (!consume_task<2>(rg, t, F, H, xs, xp_h, M, zero16, red, sums,
-                             [&](int n0, int nu, const float* sm) {
-                               if (tid < nu * M) {
-                                 const int i = tid / M, m = tid - i * M;
-                                 const float g = rbf(sm[i * 8 + m]);
-                                 const float u = rbf(sm[(i + 8) * 8 + m]);
-                                 a.act[(size_t)m * F + n0 + i] = __float2bfloat16_rn(rbf(g / (1.0f + expf(-g))) * u);
-                               }
-                             }, a.err)) return;
-        DD_STAMP(s, tb + 5);
-        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-        DD_STAMP(s, tb + 6);
-        // S4: down + residual: xres = bf16(bf16(xres + o) + bf16(d))
-        load_x(xs, xp_f, a.act, F, M, F, nullptr, 0.f, nred);
-        if (!consume_task<1>(rg, t, H, F, xs, xp_f, M, zero16, red, sums,
-                             [&](int n0, int nu, const float* sm) {
-                               if (tid < nu * M) {
-                                 const int i = tid / M, m = tid - i * M, n = n0 + i;
-                                 const float xm = b2f(xkeep[(size_t)m * H + n]);
-                                 a.xres[(size_t)m * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * 8 + m]));
-                               }
-                             }, a.err)) return;
-        DD_STAMP(s, tb + 7);
-        if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-        DD_STAMP(s, tb + 8);
+        c = dd_phase_s1<NT>(a, c, s, pos, l);
+        if (!c.ok) return;
+        c = dd_phase_s2<G, NT>(a, c, s, pos, l);
+        if (!c.ok) return;
+        c = dd_phase_s3<NT>(a, c, s, l);
+        if (!c.ok) return;
+        c = dd_phase_s4<NT>(a, c, s, l);
+        if (!c.ok) return;
       }
     }
-    const int te = 3 + 9 * a.L;
-    // S5: final RMSNorm + codebook head -> fp32 logits
-    load_x(xs, xp_h, a.xres, H, M, H, a.normf, a.eps, nred);
-    if (!consume_task<1>(rg, t, V, H, xs, xp_h, M, zero16, red, sums,
-                         [&](int n0, int nu, const float* sm) {
-                           if (tid < nu * M) {
-                             const int i = tid / M, b = tid - i * M;
-                             const float v = sm[i * 8 + b];
-                             a.logits[(size_t)b * V + n0 + i] = v;
-                             if (a.dbg) a.dbg[((size_t)s * a.B + b) * V + n0 + i] = v;
-                           }
-                         }, a.err)) return;
-    DD_STAMP(s, te + 0);
-    if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-    DD_STAMP(s, te + 1);
-    // one CFG pair: every CTA samples it (no barrier follows), CTA 0 publishes.  Several pairs: CTA h samples
-    // pair h and publishes it, then one barrier hands every CTA the fed-forward tokens (one barrier instead of
-    // `half` samplers in series on every CTA).
-    const bool redundant = half == 1;
-    const int h_begin = redundant ? 0 : (int)blockIdx.x;
-    const int h_end = redundant ? 1 : ((int)blockIdx.x < half ? (int)blockIdx.x + 1 : 0);
-    for (int h = h_begin; h < h_end; ++h) {
-      int tokv = dd_sample(a, s, h, xs, s_int);
-      tokv = tokv < 0 ? 0 : (tokv > V - 1 ? V - 1 : tokv);
-      if (tid == 0) {
-        for (int r = 0; r < (a.B >= 2 ? 2 : 1); ++r) {
-          const int b = h + r * half;
-          long long fed = tokv;
-          if (a.forced) {
-            const long long fc = a.forced[(size_t)s * a.B + b];
-            fed = fc < 0 ? 0 : (fc > V - 1 ? V - 1 : fc);
-          }
-          s_tok[b] = fed;
-          if (blockIdx.x == 0 || !redundant) {
-            a.outtok[(size_t)b * a.NCB + s] = tokv;
-            a.tokbuf[b] = fed;
-          }
-        }
-      }
-    }
-    if (!redundant && s + 1 < a.NCB) {
-      if (!grid_sync(a.bar, epoch, a.err, &s_int[31])) return;
-      if (tid < a.B) s_tok[tid] = __ldcg(a.tokbuf + tid);
-    }
-    named_sync(1, PK_CONSUMERS);
-    DD_STAMP(s, te + 7);
+    c = dd_phase_s5<NT>(a, c, s);
+    if (!c.ok) return;
+    c = dd_phase_sample(a, c, s);
+    if (!c.ok) return;
   }
   grid_exit(a.bar);
 }
@@ -906,9 +998,9 @@ DDLayout dd_layout(const fb_dd_config* c) {
   return s;
 }
 
-template <int G>
+template <int G, int NT>
 int launch_dd(DDArgs& a, size_t smem, cudaStream_t st) {
-  auto kern = dd_frame_kernel<G>;
+  auto kern = dd_frame_kernel<G, NT>;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -986,26 +1078,39 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.logits = (float*)(sc + Lo.logits); a.bar = (GridBar*)(sc + Lo.bar);
   a.err = fbh::device_err_ptr();
   a.trace = (unsigned long long*)c->trace;
-  int kmax = c->embed_dim;
-  if (c->ffn > kmax) kmax = c->ffn;
-  if (c->heads * 128 > kmax) kmax = c->heads * 128;
-  if (c->hidden > kmax) kmax = c->hidden;
   const size_t M = (size_t)c->batch;
-  // one buffer, three uses: GEMV input rows (up to M x kmax); attention output rows + staging area (att_off);
-  // x_mid rows kept from S3 to S4 past the down projection's act rows (keep_off); the sampler's keys
+  const int NT = c->batch > 8 ? 2 : 1;          // activation tiles of 8 rows
+  // One buffer, several uses, sized for the largest:
+  //   GEMV input rows of every phase (E: embed_dim, S1 / S3 / S5: hidden, S2: heads x 128; S4: ffn, whole or as
+  //   two column-chunk buffers when whole rows would leave fewer than 3 ring stages);
+  //   x_mid rows kept from S3 to S4 (keep_off, past the S4 input region); attention output rows + staging (att_off);
+  //   the sampler's keys.
+  const size_t xp_kc = ST_KC * 2 + 16;
+  size_t rows = M * (c->embed_dim * 2 + 16);
+  if (M * (c->hidden * 2 + 16) > rows) rows = M * (c->hidden * 2 + 16);
+  if (M * (c->heads * 128 * 2 + 16) > rows) rows = M * (c->heads * 128 * 2 + 16);
   const size_t att_off = al256d(M * (c->heads * 128 * 2 + 16));
-  const size_t keep_off = al256d(M * (c->ffn * 2 + 16));
-  size_t base = al256d(M * (kmax * 2 + 16));
-  const size_t xs_keep = al256d(keep_off + M * c->hidden * 2);
   const size_t xs_smp = al256d(dd_sampler_bytes(c->vocab));
-  if (xs_keep > base) base = xs_keep;
-  if (xs_smp > base) base = xs_smp;
-  const size_t budget = 227 * 1024 - ST_CWARPS * 8 * 4 - 32 * 4 - DD_MAXB * 8 - 2 * 128 * 2 - 256;
+  const size_t budget = 227 * 1024 - ST_CWARPS * 16 * 4 - 32 * 4 - DD_MAXB * 8 - 2 * 128 * 2 - 256;
   auto stages_for = [&](size_t xsb) {
-    const size_t fixed = xsb + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * PK_MAX_STAGES * 8;
+    const size_t fixed = xsb + 128 + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * PK_MAX_STAGES * 8;
     int n = fixed < budget ? (int)((budget - fixed) / ST_BYTES) : 0;
     return n > PK_MAX_STAGES ? PK_MAX_STAGES : n;
   };
+  auto layout = [&](int d_chunk, size_t& keep_off, size_t& base) {
+    const size_t d_region = d_chunk ? 2 * M * xp_kc : M * (c->ffn * 2 + 16);
+    keep_off = al256d(d_region > rows ? d_region : rows);
+    base = al256d(keep_off + M * c->hidden * 2);
+    if (al256d(rows) > base) base = al256d(rows);
+    if (xs_smp > base) base = xs_smp;
+  };
+  size_t keep_off = 0, base = 0;
+  a.d_xchunk = 0;
+  layout(0, keep_off, base);
+  if (stages_for(base) < 3) {
+    a.d_xchunk = 1;
+    layout(1, keep_off, base);
+  }
   // attention: the whole batch in one staging round when that still leaves 4 ring stages; otherwise one
   // (batch row, KV head) pair per CTA (distributed mode: one extra grid barrier per layer, small staging)
   const int G = c->heads / c->kv_heads;
@@ -1032,15 +1137,20 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.xs_bytes = (int)xs;
   a.att_off = (int)att_off;
   a.keep_off = (int)keep_off;
-  const size_t fixed = xs + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * PK_MAX_STAGES * 8;
+  const size_t fixed = xs + 128 + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * PK_MAX_STAGES * 8;
   a.nstages = nst;
   const size_t smem = fixed + (size_t)nst * ST_BYTES;
   cudaStream_t st = (cudaStream_t)stream;
-  switch (c->heads / c->kv_heads) {
-    case 1: return launch_dd<1>(a, smem, st);
-    case 2: return launch_dd<2>(a, smem, st);
-    case 4: return launch_dd<4>(a, smem, st);
-    case 8: return launch_dd<8>(a, smem, st);
+  const int key = (c->heads / c->kv_heads) * 10 + NT;
+  switch (key) {
+    case 11: return launch_dd<1, 1>(a, smem, st);
+    case 12: return launch_dd<1, 2>(a, smem, st);
+    case 21: return launch_dd<2, 1>(a, smem, st);
+    case 22: return launch_dd<2, 2>(a, smem, st);
+    case 41: return launch_dd<4, 1>(a, smem, st);
+    case 42: return launch_dd<4, 2>(a, smem, st);
+    case 81: return launch_dd<8, 1>(a, smem, st);
+    case 82: return launch_dd<8, 2>(a, smem, st);
     default: fbh::set_msg("dd_frame: GQA group %d not built", c->heads / c->kv_heads); return FB_ERR_UNSUPPORTED;
   }
 }

@@ -303,9 +303,12 @@ template <int EPI, bool NORM>
 int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
   a.M = M;
   if (a.K % 16 == 0) {
-    const int rc = launch_mma_t<EPI, NORM>(a, st);
-    // activation rows too large for two 64 KB stages: the 32 KB-stage build (three or more stages)
-    if (rc == FB_ERR_UNSUPPORTED) return gemv_mma_narrow(a, EPI, NORM, st);
+    // x staged whole with 64 KB stages; else whole with 32 KB stages (three or more); else (no norm) x in
+    // double-buffered column chunks, 64 KB stages then 32 KB stages
+    int rc = launch_mma_t<EPI, NORM>(a, st, 0);
+    if (rc == FB_ERR_UNSUPPORTED) rc = gemv_mma_narrow(a, EPI, NORM, st, 0);
+    if (rc == FB_ERR_UNSUPPORTED && !NORM) rc = launch_mma_t<EPI, NORM>(a, st, 1);
+    if (rc == FB_ERR_UNSUPPORTED && !NORM) rc = gemv_mma_narrow(a, EPI, NORM, st, 1);
     return rc;
   }
   switch (M) {
@@ -320,7 +323,7 @@ int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
 
 int common_checks(const void* x, int64_t ldx, int M, int K, const void* y, int64_t ldy) {
   FB_CHECK_ARG(x && y, "gemv: null x or y");
-  FB_CHECK_ARG(M >= 1 && M <= 8, "gemv: M=%d out of range 1..8", M);
+  FB_CHECK_ARG(M >= 1 && M <= 16, "gemv: M=%d out of range 1..16", M);
   FB_CHECK_ARG(K > 0 && K % 8 == 0, "gemv: K=%d must be a positive multiple of 8", K);
   FB_CHECK_ARG(ldx % 8 == 0 && ldy >= 1 && al16(x), "gemv: x row stride %lld must be a multiple of 8 and x 16B aligned",
                (long long)ldx);

@@ -27,6 +27,7 @@ struct GemvArgs {
   int RS;       // units (output rows) per stage
   int nstages;  // ring depth
   int xs_bytes; // shared bytes reserved for x
+  int xchunk;   // 1: x staged per column chunk (too large to stage whole)
   unsigned* err;
 };
 
@@ -50,8 +51,8 @@ __device__ __forceinline__ int gv_seg_end(const GemvArgs& a, int n) {
 
 #endif
 
-// Launches the 32 KB-stage build (fb_gemv_narrow.cu); epi / norm select the instantiation.
-int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st);
+// Launches the 32 KB-stage build (fb_gemv_narrow.cu); epi / norm select the instantiation, xchunk the staging.
+int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st, int xchunk);
 
 inline namespace FB_ST_NS_CAT(kc, FB_ST_KC) {
 
@@ -62,21 +63,24 @@ inline namespace FB_ST_NS_CAT(kc, FB_ST_KC) {
 constexpr int GM_MAX_STAGES = 6;
 constexpr int GM_THREADS = (ST_CWARPS + 1) * 32;
 
-template <int EPI, bool NORM>
+// NT tiles of 8 activation rows (M <= 8 NT).  a.xchunk: x does not fit whole, so it is staged per column chunk
+// (ST_KC columns, double-buffered, the next chunk in flight while this one is multiplied); only without NORM.
+template <int EPI, bool NORM, int NT>
 __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) {
   constexpr int NMAT = EPI == 2 ? 2 : 1;
   constexpr int UG = ST_ROWS / NMAT;  // output units per row group
+  constexpr int MS = 8 * NT;          // activation-row slots per reduced output row
   extern __shared__ __align__(128) unsigned char smem[];
   const int M = a.M, K = a.K, NST = a.nstages;
-  const int x_pitch = K * 2 + 16;
+  const int x_pitch = a.xchunk ? ST_KC * 2 + 16 : K * 2 + 16;
   unsigned char* xs = smem;
   unsigned char* zero16 = smem + a.xs_bytes;
   unsigned char* ring = zero16 + 128;
   float* red = reinterpret_cast<float*>(ring + (size_t)NST * ST_BYTES);
-  float* sums = red + ST_CWARPS * 128;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sums + 128);
+  float* sums = red + ST_CWARPS * 128 * NT;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sums + 128 * NT);
   uint64_t* empty = full + GM_MAX_STAGES;
-  __shared__ float nred[ST_CWARPS][8];
+  __shared__ float nred[ST_CWARPS][MS];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, bid = blockIdx.x;
@@ -125,10 +129,10 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
   pdl_trigger();
   const int ctid = tid;
   const int kv = K >> 3;
-  {
-    float ss[8];
+  if (!a.xchunk) {
+    float ss[MS];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) ss[m] = 0.f;
+    for (int m = 0; m < MS; ++m) ss[m] = 0.f;
     for (int i = ctid; i < M * kv; i += ST_CWARPS * 32) {
       const int m = i / kv, j = i - m * kv;
       const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + (size_t)j * 8);
@@ -140,20 +144,20 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
 #pragma unroll
         for (int t = 0; t < 8; ++t) q = fmaf(f[t], f[t], q);
 #pragma unroll
-        for (int mm = 0; mm < 8; ++mm)
+        for (int mm = 0; mm < MS; ++mm)
           if (mm == m) ss[mm] += q;
       }
     }
     if (NORM) {
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
+      for (int m = 0; m < MS; ++m) {
         const float q = warp_sum(ss[m]);
         if (lane == 0) nred[warp][m] = q;
       }
       named_sync(1, ST_CWARPS * 32);
-      float rs[8];
+      float rs[MS];
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
+      for (int m = 0; m < MS; ++m) {
         float q = 0.f;
 #pragma unroll
         for (int w = 0; w < ST_CWARPS; ++w) q += nred[w][m];
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
         cvt8(*reinterpret_cast<const uint4*>(a.nw + (size_t)j * 8), w);
         float r = 0.f;
 #pragma unroll
-        for (int mm = 0; mm < 8; ++mm)
+        for (int mm = 0; mm < MS; ++mm)
           if (mm == m) r = rs[mm];
         uint4 o;
         o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
@@ -181,30 +185,58 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
   }
 
   int t = 0;
+  const int cbuf = M * x_pitch;                 // bytes of one x chunk buffer (chunked mode)
+  auto load_chunk = [&](int kc) {               // x[:, kc * ST_KC ..] -> chunk buffer kc & 1 (chunked mode)
+    const int k0 = kc * ST_KC, kvc = min(ST_KC, K - k0) >> 3;
+    unsigned char* dst = xs + (size_t)(kc & 1) * cbuf;
+    for (int i = ctid; i < M * kvc; i += ST_CWARPS * 32) {
+      const int m = i / kvc, j = i - m * kvc;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + (size_t)m * x_pitch + j * 16)),
+                   "l"(a.x + (size_t)m * a.ldx + k0 + (size_t)j * 8)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
   for (int g = 0; g < ngroups; ++g) {
     const int n0 = u0 + g * UG;
     const int nu = min(UG, u1 - n0);
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    float c[NT][4];
+#pragma unroll
+    for (int q = 0; q < NT; ++q) c[q][0] = c[q][1] = c[q][2] = c[q][3] = 0.f;
+    if (a.xchunk) load_chunk(0);
     for (int kc = 0; kc < nkc; ++kc, ++t) {
       const int s = t % NST;
+      const unsigned char* xk = xs;
+      int kx = kc * ST_KC;
+      if (a.xchunk) {
+        if (kc + 1 < nkc) {
+          load_chunk(kc + 1);
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+          asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        named_sync(1, ST_CWARPS * 32);
+        xk = xs + (size_t)(kc & 1) * cbuf;
+        kx = 0;
+      }
       if (!mbar_wait_warp(&full[s], (t / NST) & 1, a.err)) return;
-      const int k0 = kc * ST_KC;
-      stage_mma(ring + (size_t)s * ST_BYTES, min(ST_KC, K - k0), xs, x_pitch, M, k0, zero16, c);
+      stage_mma_nt<NT>(ring + (size_t)s * ST_BYTES, min(ST_KC, K - kc * ST_KC), xk, x_pitch, M, kx, zero16, c);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+      if (a.xchunk) named_sync(1, ST_CWARPS * 32);   // chunk buffer kc & 1 is refilled two chunks later
     }
-    reduce_warps(c, red, sums, 1);
+    reduce_warps_nt<NT>(c, red, sums, 1);
     if (ctid < nu * M) {
       const int i = ctid / M, m = ctid - i * M;
       const int n = n0 + i;
       float v;
       if (EPI == 0) {
-        v = sums[i * 8 + m];
+        v = sums[i * MS + m];
       } else if (EPI == 1) {
-        v = b2f(a.res[(size_t)m * a.ldr + n]) + rbf(sums[i * 8 + m]);
+        v = b2f(a.res[(size_t)m * a.ldr + n]) + rbf(sums[i * MS + m]);
       } else {
-        const float gg = rbf(sums[i * 8 + m]);
-        const float uu = rbf(sums[(i + 8) * 8 + m]);
+        const float gg = rbf(sums[i * MS + m]);
+        const float uu = rbf(sums[(i + 8) * MS + m]);
         v = rbf(gg / (1.0f + expf(-gg))) * uu;
       }
       a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(v);
@@ -212,18 +244,19 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
   }
 }
 
-
-// Ring depth and launch for this stage width; returns FB_ERR_UNSUPPORTED when fewer than two stages fit.
-template <int EPI, bool NORM>
-inline int launch_mma_t(GemvArgs& a, cudaStream_t st) {
-  auto kern = gemv_mma_kernel<EPI, NORM>;
-  a.xs_bytes = ((a.M * (a.K * 2 + 16)) + 127) / 128 * 128;
-  const size_t fixed = (size_t)a.xs_bytes + 128 + ST_CWARPS * 128 * 4 + 128 * 4 + 2 * GM_MAX_STAGES * 8;
+// Ring depth and launch for this stage width: x whole (xchunk = 0) or in double-buffered column chunks (1, only
+// without NORM).  Returns FB_ERR_UNSUPPORTED when fewer than two ring stages fit.
+template <int EPI, bool NORM, int NT>
+inline int launch_mma_nt(GemvArgs& a, cudaStream_t st, int xchunk) {
+  auto kern = gemv_mma_kernel<EPI, NORM, NT>;
+  a.xchunk = xchunk;
+  a.xs_bytes = xchunk ? ((2 * a.M * (ST_KC * 2 + 16)) + 127) / 128 * 128 : ((a.M * (a.K * 2 + 16)) + 127) / 128 * 128;
+  const size_t fixed = (size_t)a.xs_bytes + 128 + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * GM_MAX_STAGES * 8;
 #ifndef FB_GM_BUDGET
 #define FB_GM_BUDGET 220000
 #endif
-  int nst = (int)((FB_GM_BUDGET - fixed) / ST_BYTES);
-  if (nst < 3) nst = (int)((210 * 1024 - fixed) / ST_BYTES);
+  int nst = fixed < FB_GM_BUDGET ? (int)((FB_GM_BUDGET - fixed) / ST_BYTES) : 0;
+  if (nst < 3 && fixed < 210 * 1024) nst = (int)((210 * 1024 - fixed) / ST_BYTES);
   if (nst > GM_MAX_STAGES) nst = GM_MAX_STAGES;
   if (nst < 2) {
     fbh::set_msg("gemv: M*K = %d activations do not fit the shared-memory budget", a.M * a.K);
@@ -247,6 +280,16 @@ inline int launch_mma_t(GemvArgs& a, cudaStream_t st) {
   return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(GM_THREADS), smem, st, args, true);
 }
 
+// This build's launch for M <= 16 rows: one or two activation tiles, x whole or chunked.
+template <int EPI, bool NORM>
+inline int launch_mma_t(GemvArgs& a, cudaStream_t st, int xchunk = 0) {
+  if (xchunk && NORM) {
+    fbh::set_msg("gemv: chunked activations need the norm-free kernel");
+    return FB_ERR_UNSUPPORTED;
+  }
+  if (a.M <= 8) return launch_mma_nt<EPI, NORM, 1>(a, st, xchunk);
+  return launch_mma_nt<EPI, NORM, 2>(a, st, xchunk);
+}
 
 }  // inline namespace
 }  // namespace fb

@@ -5,12 +5,12 @@
 
 namespace fb {
 
-int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st) {
-  if (epi == 0 && norm) return launch_mma_t<0, true>(a, st);
-  if (epi == 0) return launch_mma_t<0, false>(a, st);
-  if (epi == 1) return launch_mma_t<1, false>(a, st);
-  if (epi == 2 && norm) return launch_mma_t<2, true>(a, st);
-  if (epi == 2) return launch_mma_t<2, false>(a, st);
+int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st, int xchunk) {
+  if (epi == 0 && norm) return launch_mma_t<0, true>(a, st, xchunk);
+  if (epi == 0) return launch_mma_t<0, false>(a, st, xchunk);
+  if (epi == 1) return launch_mma_t<1, false>(a, st, xchunk);
+  if (epi == 2 && norm) return launch_mma_t<2, true>(a, st, xchunk);
+  if (epi == 2) return launch_mma_t<2, false>(a, st, xchunk);
   fbh::set_msg("gemv: no 32 KB-stage build for epilogue %d", epi);
   return FB_ERR_UNSUPPORTED;
 }

@@ -156,105 +156,131 @@ __device__ __forceinline__ void prefetch_task(int units, int K, RowFn row) {
   for (int i = lane; i < n; i += 32) prefetch_l2(row(u0 + i / NMAT, i % NMAT), (unsigned)(K * 2));
 }
 
-// Consumer half of one 16-row group: multiply its nkc stages by the activation rows xs (M rows, byte pitch x_pitch),
-// release them, and sum the 8 warps' partials into sums[r * 8 + m] (r < 16).  Returns the new stage counter, or -1 on
-// timeout.  Not inlined: every task of a persistent kernel shares this one copy.
-__device__ __noinline__ int consume_group(Ring rg, int t, int K, const unsigned char* xs, int x_pitch, int M,
-                                          const unsigned char* zero16, float* red, float* sums, unsigned* err) {
+// Consumer half of one 16-row group: multiply its nkc stages by the activation rows xs (M <= 8 NT rows, byte pitch
+// x_pitch), release them, and sum the 8 warps' partials into sums[r * 8 NT + m] (r < 16).  With xg != nullptr the
+// activations are too large to stage whole: each ST_KC-column chunk of the global rows xg (row stride ldx) is
+// brought into one of two chunk buffers at xs (pitch x_pitch = ST_KC * 2 + 16), the next one in flight while this
+// one is multiplied.  Returns the new stage counter, or -1 on timeout.  Not inlined: one copy per NT.
+template <int NT>
+__device__ __noinline__ int consume_group_nt(Ring rg, int t, int K, const unsigned char* xs, int x_pitch, int M,
+                                             const unsigned char* zero16, float* red, float* sums, unsigned* err,
+                                             const bf16* xg, long ldx) {
   const int lane = threadIdx.x & 31;
   const int nkc = (K + ST_KC - 1) / ST_KC;
-  float c[4] = {0.f, 0.f, 0.f, 0.f};
+  const int cbuf = M * x_pitch;
+  auto load_chunk = [&](int kc) {
+    const int k0 = kc * ST_KC, kvc = min(ST_KC, K - k0) >> 3;
+    unsigned char* dst = const_cast<unsigned char*>(xs) + (size_t)(kc & 1) * cbuf;
+    for (int i = threadIdx.x; i < M * kvc; i += PK_CONSUMERS) {
+      const int m = i / kvc, j = i - m * kvc;
+      cp_async16(dst + (size_t)m * x_pitch + j * 16, xg + (size_t)m * ldx + k0 + (size_t)j * 8);
+    }
+    cp_async_commit();
+  };
+  float c[NT][4];
+#pragma unroll
+  for (int q = 0; q < NT; ++q) c[q][0] = c[q][1] = c[q][2] = c[q][3] = 0.f;
+  if (xg) load_chunk(0);
   for (int kc = 0; kc < nkc; ++kc, ++t) {
     const int s = t % rg.nst;
+    const unsigned char* xk = xs;
+    int kx = kc * ST_KC;
+    if (xg) {
+      if (kc + 1 < nkc) {
+        load_chunk(kc + 1);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      named_sync(1, PK_CONSUMERS);
+      xk = xs + (size_t)(kc & 1) * cbuf;
+      kx = 0;
+    }
     if (!mbar_wait_warp(&rg.full[s], (t / rg.nst) & 1, err)) return -1;
-    const int k0 = kc * ST_KC;
-    stage_mma(rg.base + (size_t)s * ST_BYTES, min(ST_KC, K - k0), xs, x_pitch, M, k0, zero16, c);
+    stage_mma_nt<NT>(rg.base + (size_t)s * ST_BYTES, min(ST_KC, K - kc * ST_KC), xk, x_pitch, M, kx, zero16, c);
     __syncwarp();
     if (lane == 0) mbar_arrive(&rg.empty[s]);
+    if (xg) named_sync(1, PK_CONSUMERS);        // chunk buffer kc & 1 is refilled two chunks later
   }
-  reduce_warps(c, red, sums, 1);
+  reduce_warps_nt<NT>(c, red, sums, 1);
   return t;
 }
 
-// Consumer half: every 16-row group of the task through consume_group, then epi(n0, nu, sums).  All 256 consumer
-// threads call it.
-template <int NMAT, typename EpiFn>
+// Consumer half: every 16-row group of the task through consume_group_nt, then epi(n0, nu, sums).  All 256
+// consumer threads call it.  Chunked activations (xg) need a task of one row group per CTA or accept re-loading.
+template <int NMAT, int NT = 1, typename EpiFn>
 __device__ __forceinline__ bool consume_task(Ring& rg, int& t, int units, int K, const unsigned char* xs, int x_pitch,
                                              int M, const unsigned char* zero16, float* red, float* sums, EpiFn epi,
-                                             unsigned* err) {
+                                             unsigned* err, const bf16* xg = nullptr, long ldx = 0) {
   constexpr int UG = ST_ROWS / NMAT;
   int u0, u1;
   task_range(units, u0, u1);
   for (int n0 = u0; n0 < u1; n0 += UG) {
     const int nu = min(UG, u1 - n0);
-    t = consume_group(rg, t, K, xs, x_pitch, M, zero16, red, sums, err);
+    t = consume_group_nt<NT>(rg, t, K, xs, x_pitch, M, zero16, red, sums, err, xg, ldx);
     if (t < 0) return false;
     epi(n0, nu, sums);
   }
   return true;
 }
 
-// Stage rows [0, M) of a global bf16 activation matrix (row stride ld) into xs, optionally applying the eager
-// Qwen3 RMSNorm with weight nw (double rounding).  Cross-CTA data: copied with cp.async.cg (L2 only), every chunk in
-// flight at once (one round trip); each thread then works on the chunks it copied itself until the norm's reduction.
-__device__ __noinline__ void load_x(unsigned char* xs, int x_pitch, const bf16* x, long ld, int M, int K,
-                                    const bf16* nw, float eps, float* nred /* [8][8] */) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// Per-row RMS factors of M <= 16 staged rows: warp w reduces rows w and w + 8 (each lane's chunks in order, then a
+// butterfly), and rs[m] = 1 / sqrt(mean(x^2) + eps).  Every staged chunk must be visible to every consumer thread.
+__device__ __noinline__ void row_rms(const unsigned char* xs, int x_pitch, int M, int K, float eps, float* rs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv = K >> 3;
-  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
+  for (int m = warp; m < M; m += ST_CWARPS) {
+    float q = 0.f;
+    for (int j = lane; j < kv; j += 32) {
+      float f[8];
+      cvt8(*reinterpret_cast<const uint4*>(xs + (size_t)m * x_pitch + j * 16), f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) q = fmaf(f[u], f[u], q);
+    }
+    q = warp_sum(q);
+    if (lane == 0) rs[m] = 1.0f / sqrtf(q / (float)K + eps);
+  }
+  named_sync(1, PK_CONSUMERS);
+}
+
+// Eager Qwen3 RMSNorm in place on staged rows (double rounding: bf16(w * bf16(x * r))), r from row_rms.
+__device__ __forceinline__ void apply_rms(unsigned char* xs, int x_pitch, int M, int K, const bf16* nw,
+                                          const float* rs) {
+  const int kv = K >> 3;
+  for (int i = threadIdx.x; i < M * kv; i += PK_CONSUMERS) {
+    const int m = i / kv, j = i - m * kv;
+    uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
+    float f[8], w[8];
+    cvt8(*px, f);
+    cvt8(*reinterpret_cast<const uint4*>(nw + (size_t)j * 8), w);
+    const float r = rs[m];
+    uint4 o;
+    o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
+    o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
+    o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
+    o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
+    *px = o;
+  }
+}
+
+// Stage rows [0, M) (M <= 16) of a global bf16 activation matrix (row stride ld) into xs, optionally applying the
+// eager Qwen3 RMSNorm with weight nw.  Cross-CTA data: copied with cp.async.cg (L2 only), every chunk in flight at
+// once (one round trip).  nred holds at least 16 floats.
+__device__ __noinline__ void load_x(unsigned char* xs, int x_pitch, const bf16* x, long ld, int M, int K,
+                                    const bf16* nw, float eps, float* nred) {
+  const int kv = K >> 3;
+  for (int i = threadIdx.x; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
     cp_async16(xs + (size_t)m * x_pitch + j * 16, x + (size_t)m * ld + (size_t)j * 8);
   }
   cp_async_commit();
   cp_async_wait<0>();
-  if (nw) {
-    float ss[8];
-#pragma unroll
-    for (int m = 0; m < 8; ++m) ss[m] = 0.f;
-    for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
-      const int m = i / kv, j = i - m * kv;
-      float f[8];
-      cvt8(*reinterpret_cast<const uint4*>(xs + (size_t)m * x_pitch + j * 16), f);
-      float q = 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) q = fmaf(f[u], f[u], q);
-#pragma unroll
-      for (int mm = 0; mm < 8; ++mm)
-        if (mm == m) ss[mm] += q;
-    }
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      const float q = warp_sum(ss[m]);
-      if (lane == 0) nred[warp * 8 + m] = q;
-    }
-    named_sync(1, PK_CONSUMERS);
-    float rs[8];
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      float q = 0.f;
-#pragma unroll
-      for (int w = 0; w < ST_CWARPS; ++w) q += nred[w * 8 + m];
-      rs[m] = 1.0f / sqrtf(q / (float)K + eps);
-    }
-    for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
-      const int m = i / kv, j = i - m * kv;
-      uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
-      float f[8], w[8];
-      cvt8(*px, f);
-      cvt8(*reinterpret_cast<const uint4*>(nw + (size_t)j * 8), w);
-      float r = 0.f;
-#pragma unroll
-      for (int mm = 0; mm < 8; ++mm)
-        if (mm == m) r = rs[mm];
-      uint4 o;
-      o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
-      o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
-      o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
-      o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
-      *px = o;
-    }
-  }
   named_sync(1, PK_CONSUMERS);
+  if (nw) {
+    row_rms(xs, x_pitch, M, K, eps, nred);
+    apply_rms(xs, x_pitch, M, K, nw, nred);
+    named_sync(1, PK_CONSUMERS);
+  }
 }
 
 }  // inline namespace

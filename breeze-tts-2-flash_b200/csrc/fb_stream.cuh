@@ -123,6 +123,85 @@ __device__ __forceinline__ void reduce_warps(const float (&c)[4], float* red /* 
   named_sync(bar_id, ST_CWARPS * 32);
 }
 
+// NT tiles of 8 activation rows (M <= 8 NT): each k-step's weight fragment (ldmatrix.x4) is loaded once and
+// multiplied by every tile's activation fragment; tile t covers activation rows 8t .. 8t+7 (rows >= M read zeros).
+// Two independent accumulator chains per tile, summed at the end in a fixed order.
+template <int NT>
+__device__ __forceinline__ void stage_mma_nt(const unsigned char* stage, int kw, const unsigned char* xs, int x_pitch,
+                                             int M, int k0, const unsigned char* zero16, float (&c)[NT][4]) {
+  if constexpr (NT == 1) {
+    stage_mma(stage, kw, xs, x_pitch, M, k0, zero16, c[0]);
+  } else {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nks = kw >> 4;
+    const int ks0 = warp * ST_KSTEPS_PER_WARP;
+    const int ks1 = min(nks, ks0 + ST_KSTEPS_PER_WARP);
+    const int arow = (lane & 7) + ((lane >> 3) & 1) * 8;
+    const uint32_t abase = smem_u32(stage) + arow * ST_PITCH + (lane >> 4) * 16;
+    const int bn = lane & 7;
+    uint32_t bbase[NT], bstep[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const bool breal = bn + 8 * t < M && lane < 16;
+      bbase[t] = breal ? smem_u32(xs) + (bn + 8 * t) * x_pitch + (size_t)k0 * 2 + ((lane >> 3) & 1) * 16
+                       : smem_u32(zero16);
+      bstep[t] = breal ? 32u : 0u;
+    }
+    float cc[2][NT][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int t = 0; t < NT; ++t) cc[h][t][0] = cc[h][t][1] = cc[h][t][2] = cc[h][t][3] = 0.f;
+#pragma unroll
+    for (int i = 0; i < ST_KSTEPS_PER_WARP; ++i) {
+      const int ks = ks0 + i;
+      if (ks < ks1) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(abase + ks * 32, a0, a1, a2, a3);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          uint32_t b0, b1;
+          ldsm_x2(bbase[t] + ks * bstep[t], b0, b1);
+          mma_bf16_16816(cc[i & 1][t], a0, a1, a2, a3, b0, b1);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c[t][j] += cc[0][t][j] + cc[1][t][j];
+  }
+}
+
+// Sum the 8 warps' fragments of NT tiles (fixed order) into sums[16][8 NT] (row r, activation row m at
+// sums[r * 8 NT + m]).  red holds [8 warps][16][8 NT] floats.  Called by all 256 consumer threads.
+template <int NT>
+__device__ __forceinline__ void reduce_warps_nt(const float (&c)[NT][4], float* red, float* sums, int bar_id) {
+  if constexpr (NT == 1) {
+    reduce_warps(c[0], red, sums, bar_id);
+  } else {
+    constexpr int MS = 8 * NT;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = lane >> 2, m = (lane & 3) * 2;
+    float* w = red + warp * 16 * MS;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      w[r * MS + 8 * t + m] = c[t][0];
+      w[r * MS + 8 * t + m + 1] = c[t][1];
+      w[(r + 8) * MS + 8 * t + m] = c[t][2];
+      w[(r + 8) * MS + 8 * t + m + 1] = c[t][3];
+    }
+    named_sync(bar_id, ST_CWARPS * 32);
+    for (int i = threadIdx.x; i < 16 * MS; i += ST_CWARPS * 32) {
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < ST_CWARPS; ++k) s += red[k * 16 * MS + i];
+      sums[i] = s;
+    }
+    named_sync(bar_id, ST_CWARPS * 32);
+  }
+}
+
 // cp.async 16-byte global -> shared copy (bypasses L1), group commit / wait.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");

@@ -18,8 +18,8 @@ import torch
 from . import _native, kernels
 from ._native import check
 
-BUILDS = {1: 'full', 2: 'full', 4: 'full', 8: 'full'}
-GRIDS = {1: 0, 2: 0, 4: 0, 8: 0}      # 0 = one CTA per SM
+BUILDS = {1: 'full', 2: 'full', 4: 'full', 8: 'full', 16: 'full'}
+GRIDS = {1: 0, 2: 0, 4: 0, 8: 0, 16: 0}      # 0 = one CTA per SM
 _state = {}
 
 
@@ -82,7 +82,7 @@ class DepthOps:
 
     def dd2_set_grid(self, B, grid):
         if B not in BUILDS:
-            raise RuntimeError('B must be 1, 2, 4 or 8')
+            raise RuntimeError('B must be 1, 2, 4, 8 or 16')
         GRIDS[B] = int(grid)
 
     def _desc(self, B, device):
@@ -118,7 +118,7 @@ def _orig(mod):
 class DepthMegakernel:
     """Depth frame on flashb for an official BreezeDepthDecoderForCausalLM-like object (``model`` +
     ``codebooks_head``), as ``flash/depth.py:97-157``.  Shapes are read from the model instead of asserted."""
-    MAXB = 8
+    MAXB = 16
 
     def __init__(self, depth_decoder, device='cuda', codebook_size=None):
         model = depth_decoder.model

@@ -263,7 +263,7 @@ class FrameEngine:
     """One replica on one GPU for the streaming decode: a synthetic backbone and depth decoder whose weights are
     shared by ``n_streams`` independent streams (own KV cache, positions and I/O buffers each).
 
-    Streams are served in slots of ``group`` streams (1, 2 or 4): a slot's streams share every weight read of the
+    Streams are served in slots of ``group`` streams (1, 2, 4 or 8): a slot's streams share every weight read of the
     backbone step (GEMV rows M = 2 g) and of the depth frame (B = 2 g), and advance in lockstep (same cache
     position; the bench's streams all start after the same prompt length).  ``frame(i)`` runs one frame of every
     stream of slot i on the current CUDA stream, the body of the reference's streaming loop
@@ -284,8 +284,8 @@ class FrameEngine:
         profiling the depth frame alone on a small device footprint."""
         if bcfg.codebooks - 1 > dcfg.n_decode or dcfg.embed_dim != bcfg.hidden:
             raise ValueError('backbone codebooks must be <= 1 + depth codebooks and depth embed_dim == backbone hidden')
-        if group not in (1, 2, 4) or n_streams % group:
-            raise ValueError('group must be 1, 2 or 4 and divide the number of streams')
+        if group not in (1, 2, 4, 8) or n_streams % group:
+            raise ValueError('group must be 1, 2, 4 or 8 and divide the number of streams')
         self.bcfg, self.dcfg, self.group = bcfg, dcfg, group
         self.device = dev = torch.device(device)
         self.prompt_len = prompt_len

@@ -89,7 +89,7 @@ def _set(m, p):
     m.guidance_scale.fill_(p['gs'])
 
 
-@pytest.mark.parametrize('B', [1, 2, 4, 8])
+@pytest.mark.parametrize('B', [1, 2, 4, 8, 16])
 def test_depth_forced_logits_match_oracle(B):
     m = _model(B=B)
     c = m.cfg
@@ -129,7 +129,7 @@ def test_depth_free_running_equals_forced_oracle():
     np.testing.assert_array_equal(tok, outtok[:, -1])
 
 
-@pytest.mark.parametrize('B', [2, 8])
+@pytest.mark.parametrize('B', [2, 8, 16])
 def test_depth_full_size_forced_and_sampler(B):
     """The synthetic full-size depth decoder (4 layers, hidden 1024, 16 codebooks of 2048).  B = 8 (four CFG pairs)
     runs the distributed attention mode (one (row, KV head) pair per CTA) and one sampler CTA per pair."""

@@ -77,7 +77,7 @@ def _oracle_backbone(bb):
                                bb.cfg.eps, bb.cfg.theta)
 
 
-@pytest.mark.parametrize('group', [1, 2, 4])
+@pytest.mark.parametrize('group', [1, 2, 4, 8])
 def test_frame_engine_matches_oracle_and_standalone_depth(group):
     """group 2: two streams share one slot (rows [c0, c1, u0, u1]); every row must still match the oracle."""
     eng = _small_engine(streams=max(2, group), group=group)

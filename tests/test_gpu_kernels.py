@@ -19,7 +19,7 @@ def ops():
 
 
 # ------------------------------------------------------------------------------------------------ GEMVs
-@pytest.mark.parametrize('M', [1, 2, 4, 8])
+@pytest.mark.parametrize('M', [1, 2, 4, 8, 12, 16])
 def test_gemv_seg_norm_qkv(ops, M):
     fx, _ = ops
     K = 2048
@@ -44,7 +44,8 @@ def test_gemv_seg_plain_odd_shapes(ops):
 
 
 @pytest.mark.parametrize('M,K,N', [(2, 2048, 2048), (2, 3072, 2048), (2, 6144, 2048), (4, 4096, 1024), (1, 2048, 5),
-                                   (8, 6144, 2048), (8, 6144, 37)])   # M x K too large for 64 KB stages: 32 KB build
+                                   (8, 6144, 2048), (8, 6144, 37),    # M x K too large for 64 KB stages: 32 KB build
+                                   (16, 2048, 2048), (16, 6144, 2048), (12, 6144, 300)])  # two row tiles; x chunked
 def test_gemv_resid(ops, M, K, N):
     fx, _ = ops
     x = randn((M, K), 21)
@@ -56,7 +57,7 @@ def test_gemv_resid(ops, M, K, N):
     assert_close(np32(y), ref, what='gemv_resid')
 
 
-@pytest.mark.parametrize('M', [1, 2, 4, 8])
+@pytest.mark.parametrize('M', [1, 2, 4, 8, 16])
 def test_config2_gateup_then_down(ops, M):
     """RMSNorm + [6144 x 2048] gate|up GEMV + SiLU*up, then the [2048 x 3072] down GEMV."""
     fx, _ = ops
