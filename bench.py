@@ -1,8 +1,10 @@
 #!/usr/bin/env python
 """Streaming-decode throughput of the flashb hot path on 1..8 B200s (one replica per GPU, no collective).
 
-Workload (BASELINE config 5 with configs 3 and 4): 64 independent streams, each after a 512-token prompt (random KV,
-the prefill stand-in), spread round-robin over the ranks.  A STEP is one frame of every stream on this rank:
+Workload (BASELINE config 5 with configs 3 and 4): 64 independent streams per GPU (64 N for the job: weak scaling,
+streams assigned round-robin, one replica per GPU), each after a 512-token prompt (random KV, the prefill stand-in).
+Streams are decoded 8 per launch (--group) and the GPU runs 8 lanes of slots side by side (--lanes), each lane on
+its own CUDA stream with its kernels sized for 1/8 of the SMs.  A STEP is one frame of every stream on this rank:
 
     frame = next backbone ids from the previous frame -> 28-layer backbone decode step (B = 2 CFG rows, KV length
             512 + t, hidden 2048, 16 q / 4 kv heads, FFN 6144, fp32 lm_head + CFG) -> codebook-0 token (greedy
@@ -11,8 +13,8 @@ the prefill stand-in), spread round-robin over the ranks.  A STEP is one frame o
 
 Outputs one JSON line (rank 0): ``value`` = frames/s of the whole job with every input resident in HBM (max over
 ranks of the device time), ``e2e`` = the same through the engine API with the per-frame Exp(1) draws copied from
-pinned host memory and the frame's tokens read back to the host every frame (as the reference's loop reads its
-token), ``roofline`` for the dominant kernel (the depth frame kernel) and ``roofline_backbone`` for the backbone
+pinned host memory before each frame and the frame's tokens read back to the host after it, every step (as the
+reference's loop reads its tokens), ``roofline`` for the dominant kernel (the depth frame kernel) and ``roofline_backbone`` for the backbone
 step's attention + GEMV kernels, ``cpu_baseline`` = the CPU oracle port of the same frame on this host's cores.
 
 ``--impl reference`` times that CPU port alone (rank 0; other ranks exit 0), one frame per step.
@@ -44,11 +46,14 @@ def args_():
     p.add_argument('--steps', type=int, default=30)
     p.add_argument('--warmup', type=int, default=3)
     p.add_argument('--impl', default='flashb', choices=['flashb', 'reference'])
-    p.add_argument('--streams', type=int, default=N_STREAMS, help='streams over the whole job')
+    p.add_argument('--streams', type=int, default=N_STREAMS,
+                   help='streams per GPU (the job serves streams x N: weak scaling, one replica per GPU)')
     p.add_argument('--prompt', type=int, default=PROMPT)
     p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone', 'prefill'])
     p.add_argument('--group', type=int, default=8, choices=[1, 2, 4, 8],
                    help='streams decoded together per launch (their GEMV rows share every weight read)')
+    p.add_argument('--lanes', type=int, default=8,
+                   help='GPU lanes: slots run on this many CUDA streams side by side, each sized for 1/lanes of the SMs')
     p.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample length')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
@@ -264,14 +269,17 @@ def main():
         return
     bcfg = BackboneConfig(codebooks=17)
     dcfg = DepthConfig()
-    my_streams = len(replicas.streams_for_rank(a.streams, rank, world))
+    total_streams = a.streams * world
+    my_streams = len(replicas.streams_for_rank(total_streams, rank, world))
     total_steps = a.warmup + a.steps
     n_runs = 1 if a.no_e2e else 2
     if my_streams % a.group:
         raise SystemExit(f'{my_streams} streams per rank do not split into groups of {a.group}')
     LAT_FRAMES = 20
+    lanes = max(1, min(a.lanes, my_streams // a.group)) if a.case == 'frame' else 1
     eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + LAT_FRAMES + 8, device=dev, seed=0,
-                      depth_only=(a.case == 'depth'), group=a.group, single_slot=(a.case == 'frame'))
+                      depth_only=(a.case == 'depth'), group=a.group, single_slot=(a.case == 'frame'),
+                      lanes=lanes)
     eng.capture()
     stream = torch.cuda.current_stream(dev)
 
@@ -288,21 +296,25 @@ def main():
     S = len(eng.streams)          # slots of a.group streams each
 
     def one_step(ev):
+        """One frame of every slot; with ev (a list) an event is recorded before each part on the stream the part
+        runs on, and once per lane stream at the end: ev gets (lane stream, kind, event) in issue order."""
+        def mark(kind, i, s):
+            if ev is not None:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record(s)
+                ev.append((s, kind, e))
+        if case == 'frame':
+            eng.step(mark)
+            return
+        # one part alone, on the current stream (one lane)
         for i in range(S):
-            st = eng.streams[i]
-            if case != 'depth':
-                if ev is not None:
-                    ev.append(torch.cuda.Event(enable_timing=True))
-                    ev[-1].record(stream)
-                st.graph.replay()
-            if case != 'backbone':
-                if ev is not None:
-                    ev.append(torch.cuda.Event(enable_timing=True))
-                    ev[-1].record(stream)
+            if case == 'backbone':
+                mark('bb', i, stream)
+                eng.streams[i].graph.replay()
+            else:
+                mark('dd', i, stream)
                 eng.depth_part(i)
-        if ev is not None:
-            ev.append(torch.cuda.Event(enable_timing=True))
-            ev[-1].record(stream)
+        mark('end', None, stream)
 
     # ---- device-resident run
     for _ in range(a.warmup):
@@ -325,21 +337,14 @@ def main():
     ms_max = maxred(ms)
     frames = sumred(S * a.group * a.steps)
     value = frames / (ms_max / 1e3)
-    # per-part durations from the events (frame layout: [bb] [dd] per stream, then one closing event)
+    # per-part durations: each part runs from its event to the next event recorded on the same (lane) stream
     bb_ms, dd_ms = [], []
-    k = 0
-    per = (1 if case != 'depth' else 0) + (1 if case != 'backbone' else 0)
-    for _ in range(a.steps):
-        for i in range(S):
-            marks = evs[k:k + per + 1]
-            j = 0
-            if case != 'depth':
-                bb_ms.append(marks[j].elapsed_time(marks[j + 1]))
-                j += 1
-            if case != 'backbone':
-                dd_ms.append(marks[j].elapsed_time(marks[j + 1]))
-            k += per
-        k += 1
+    last = {}
+    for s_, kind, e in evs:
+        prev = last.get(s_.cuda_stream)
+        if prev is not None:
+            (bb_ms if prev[0] == 'bb' else dd_ms).append(prev[1].elapsed_time(e))
+        last[s_.cuda_stream] = None if kind == 'end' else (kind, e)
     kv1 = int(eng.streams[0].bb.cache_position.item()) + 1 if eng.streams[0].bb is not None else 0
     pk = peaks()
     dd_bytes = dcfg.n_decode * dcfg.step_weight_bytes()
@@ -350,7 +355,10 @@ def main():
         ach = dd_bytes / (dd_avg / 1e3) / 1e9
         roof = dict(kernel='dd_frame_kernel', bound='hbm', achieved=round(ach, 1), peak=pk['hbm_gbs'], unit='GB/s',
                     frac=round(ach / pk['hbm_gbs'], 4), traffic=DD_TRAFFIC_BYTES,
-                    algorithmic_bytes=dd_bytes, launch_ms=round(dd_avg, 4), peak_source=pk['source'])
+                    algorithmic_bytes=dd_bytes, launch_ms=round(dd_avg, 4), peak_source=pk['source'],
+                    grid=eng.lane_sms or torch.cuda.get_device_properties(dev).multi_processor_count,
+                    concurrent_launches=lanes, achieved_all_lanes=round(ach * lanes, 1),
+                    frac_all_lanes=round(ach * lanes / pk['hbm_gbs'], 4))
     roof_bb = None
     if bb_ms:
         bb_avg = sum(bb_ms) / len(bb_ms)
@@ -358,7 +366,8 @@ def main():
         roof_bb = dict(kernels='backbone step (GQA decode attention + fused GEMVs + ends, 146 launches as a graph)',
                        bound='hbm', achieved=round(ach, 1), peak=pk['hbm_gbs'], unit='GB/s',
                        frac=round(ach / pk['hbm_gbs'], 4), algorithmic_bytes=bb_bytes, step_ms=round(bb_avg, 4),
-                       peak_source=pk['source'])
+                       peak_source=pk['source'], concurrent_steps=lanes, achieved_all_lanes=round(ach * lanes, 1),
+                       frac_all_lanes=round(ach * lanes / pk['hbm_gbs'], 4))
 
     # ---- end-to-end run through the engine API with host buffers
     e2e = None
@@ -373,14 +382,20 @@ def main():
         d2h = S * toks_h[0].numel() * 8
 
         def e2e_step(t):
-            for i in range(S):
+            # every slot: its Exp(1) draws in from pinned host memory before the frame, its tokens out after it (on
+            # the slot's lane stream); the host holds every stream's tokens of this step before the next step
+            def h2d_q(kind, i, s):
+                if kind == 'bb':
+                    eng.streams[i].q.copy_(qh[(i + t) % R], non_blocking=True)
+
+            def d2h_tokens(kind, i, s):
                 st = eng.streams[i]
-                st.q.copy_(qh[(i + t) % R], non_blocking=True)
-                eng.frame(i)
                 toks_h[i, :2 * G].copy_(st.first_cb, non_blocking=True)
                 toks_h[i, 2 * G:].copy_(st.outtok.view(-1), non_blocking=True)
-                done.record(stream)
-                done.synchronize()             # the frame's tokens are on the host before the next frame
+
+            eng.step(h2d_q, d2h_tokens)
+            done.record(stream)
+            done.synchronize()
 
         for t in range(a.warmup):
             e2e_step(t)
@@ -423,16 +438,18 @@ def main():
     if rank == 0:
         wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + greedy '
                        f'codebook-0 + 16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9); '
-                       f'{a.group} stream(s) per launch share the weight reads',
+                       f'{a.group} stream(s) per launch share the weight reads; {lanes} lane(s) of the GPU side by '
+                       f'side',
               'depth': 'depth frame only (4 layers, hidden 1024, 16 codebooks of 2048, CFG + top-k 50 sampling)',
               'backbone': 'backbone decode step only (28 layers, hidden 2048, B=2, KV 512+t) + frame link'}[case]
         line = dict(
             metric='frames/s', value=round(value, 3), unit='frames/s', n_gpus=world, steps=a.steps,
-            warmup=a.warmup, ms_per_step=round(ms_max / a.steps, 3), higher_is_better=True, scaling='strong',
+            warmup=a.warmup, ms_per_step=round(ms_max / a.steps, 3), higher_is_better=True, scaling='weak',
             vs_baseline=None, dtype='bf16', data='synthetic (seeded random bf16 weights, random prompt KV)',
-            config=dict(workload=wl, streams=a.streams, streams_per_gpu=my_streams, step='one frame of every stream '
+            config=dict(workload=wl, streams=total_streams, streams_per_gpu=my_streams, step='one frame of every stream '
                         'on the rank', streams_per_launch=a.group, prompt_len=a.prompt, kv_len=[kv0, kv1],
-                        parallelism=f'replica x{world}',
+                        parallelism=f'replica x{world}', lanes=lanes,
+                        lane_sms=eng.lane_sms or torch.cuda.get_device_properties(dev).multi_processor_count,
                         l2='inputs larger than L2: 2.70 GB backbone weights per step, 130 MB depth weights per '
                            'codebook step; no flush', cb0='greedy (backbone sampler do_sample=False)',
                         prefill='not timed (random prompt KV)'),

@@ -15,6 +15,7 @@ std::mutex g_mu;
 unsigned* g_err_ptr[64] = {nullptr};
 int g_sms[64] = {0};
 int g_pdl = -1;
+thread_local int t_sm_budget = 0;   // SMs the calling thread's launches may size their grids for (0: all)
 }  // namespace
 
 namespace fbh {
@@ -47,6 +48,11 @@ int num_sms() {
     g_sms[dev] = n > 0 ? n : 148;
   }
   return g_sms[dev];
+}
+
+int grid_sms() {
+  const int n = num_sms();
+  return (t_sm_budget > 0 && t_sm_budget < n) ? t_sm_budget : n;
 }
 
 bool pdl_enabled() {
@@ -96,6 +102,10 @@ extern "C" const char* flashb_last_error(void) { return t_msg; }
 extern "C" const char* flashb_version(void) { return "flashb 0.1 sm_100a"; }
 
 extern "C" void flashb_set_pdl(int enable) { g_pdl = enable ? 1 : 0; }
+
+extern "C" void flashb_set_sm_budget(int sms) { t_sm_budget = sms > 0 ? sms : 0; }
+
+extern "C" int flashb_sm_budget(void) { return fbh::grid_sms(); }
 
 extern "C" int flashb_device_error(int clear) {
   cudaError_t e = cudaDeviceSynchronize();

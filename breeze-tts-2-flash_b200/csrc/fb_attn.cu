@@ -325,7 +325,7 @@ using namespace fb;
 constexpr size_t AT_SMEM = 4 * (size_t)AT_CHUNK * AT_D * 2;  // K and V, two stages
 
 int pick_nsplit(int B, int NKV, int S) {
-  const int target = 2 * fbh::num_sms();
+  const int target = 2 * fbh::grid_sms();
   int ns = (target + B * NKV - 1) / (B * NKV);
   const int cap_len = (S + 15) / 16;
   if (ns > cap_len) ns = cap_len;

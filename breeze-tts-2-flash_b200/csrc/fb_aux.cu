@@ -318,6 +318,6 @@ extern "C" int flashb_lm_head_cfg(const void* x, int B, int H, const void* norm_
   bf16* ho = (bf16*)hidden_out;
   void* args[] = {(void*)&xp, (void*)&B, (void*)&H, (void*)&np, (void*)&eps, (void*)&W32, (void*)&V,
                   (void*)&gs, (void*)&ho, (void*)&logits, (void*)&cfg_out};
-  return fbh::launch_pdl((const void*)lm_head_cfg_kernel, dim3(fbh::num_sms()), dim3(LM_THREADS), smem,
+  return fbh::launch_pdl((const void*)lm_head_cfg_kernel, dim3(fbh::grid_sms()), dim3(LM_THREADS), smem,
                          (cudaStream_t)stream, args, true);
 }

@@ -152,6 +152,7 @@ int launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_
                int cluster_x = 0);
 bool pdl_enabled();
 int num_sms();
+int grid_sms();  // num_sms(), or the calling thread's SM budget when one is set (flashb_set_sm_budget)
 }  // namespace fbh
 
 #define FB_CHECK_ARG(cond, ...)          \

@@ -999,7 +999,7 @@ DDLayout dd_layout(const fb_dd_config* c) {
 }
 
 template <int G, int NT>
-int launch_dd(DDArgs& a, size_t smem, cudaStream_t st) {
+int launch_dd(DDArgs& a, size_t smem, int grid, cudaStream_t st) {
   auto kern = dd_frame_kernel<G, NT>;
   static int attr_done[64] = {0};
   int dev = 0;
@@ -1019,7 +1019,7 @@ int launch_dd(DDArgs& a, size_t smem, cudaStream_t st) {
     return FB_ERR_CUDA;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(fbh::num_sms());
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(PK_THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -1080,6 +1080,12 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.trace = (unsigned long long*)c->trace;
   const size_t M = (size_t)c->batch;
   const int NT = c->batch > 8 ? 2 : 1;          // activation tiles of 8 rows
+  const int grid = c->grid > 0 ? c->grid : fbh::grid_sms();
+  if (grid > fbh::num_sms() || grid < (c->batch >= 2 ? c->batch / 2 : 1)) {
+    fbh::set_msg("dd_frame: grid %d outside [%d, %d] (one CTA per SM, one per CFG pair at least)", grid,
+                 c->batch >= 2 ? c->batch / 2 : 1, fbh::num_sms());
+    return FB_ERR_ARG;
+  }
   // One buffer, several uses, sized for the largest:
   //   GEMV input rows of every phase (E: embed_dim, S1 / S3 / S5: hidden, S2: heads x 128; S4: ffn, whole or as
   //   two column-chunk buffers when whole rows would leave fewer than 3 ring stages);
@@ -1112,23 +1118,27 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
     layout(1, keep_off, base);
   }
   // attention: the whole batch in one staging round when that still leaves 4 ring stages; otherwise one
-  // (batch row, KV head) pair per CTA (distributed mode: one extra grid barrier per layer, small staging)
+  // (batch row, KV head) pair per CTA (distributed mode: one extra grid barrier per layer, small staging), or, with
+  // fewer CTAs than pairs, the batch in chunks of rows on every CTA
   const int G = c->heads / c->kv_heads;
   size_t xs = al256d(att_off + dd_attn_bytes(c->batch, c->heads, c->kv_heads, c->n_decode + 1));
   if (xs < base) xs = base;
   int nst = stages_for(xs);
   a.att_bc = c->batch;
   a.att_split = 0;
-  if (nst < 4) {
+  if (nst < 4 && c->batch * c->kv_heads <= grid) {
     const size_t pair = (size_t)G * 256 + 2 * (size_t)(c->n_decode + 1) * 256 + (size_t)G * 32 * 4;
     xs = al256d(att_off + pair);
     if (xs < base) xs = base;
     nst = stages_for(xs);
     a.att_split = 1;
-    if (c->batch * c->kv_heads > fbh::num_sms()) {
-      fbh::set_msg("dd_frame: batch x kv_heads exceeds the number of SMs");
-      return FB_ERR_UNSUPPORTED;
-    }
+  }
+  // too few CTAs for one (row, KV head) pair each: every CTA stages the batch's K/V in chunks of rows instead
+  while (nst < 4 && !a.att_split && a.att_bc > 1) {
+    a.att_bc = (a.att_bc + 1) / 2;
+    xs = al256d(att_off + dd_attn_bytes(a.att_bc, c->heads, c->kv_heads, c->n_decode + 1));
+    if (xs < base) xs = base;
+    nst = stages_for(xs);
   }
   if (nst < 2) {
     fbh::set_msg("dd_frame: activations too large for two ring stages");
@@ -1143,14 +1153,14 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   cudaStream_t st = (cudaStream_t)stream;
   const int key = (c->heads / c->kv_heads) * 10 + NT;
   switch (key) {
-    case 11: return launch_dd<1, 1>(a, smem, st);
-    case 12: return launch_dd<1, 2>(a, smem, st);
-    case 21: return launch_dd<2, 1>(a, smem, st);
-    case 22: return launch_dd<2, 2>(a, smem, st);
-    case 41: return launch_dd<4, 1>(a, smem, st);
-    case 42: return launch_dd<4, 2>(a, smem, st);
-    case 81: return launch_dd<8, 1>(a, smem, st);
-    case 82: return launch_dd<8, 2>(a, smem, st);
+    case 11: return launch_dd<1, 1>(a, smem, grid, st);
+    case 12: return launch_dd<1, 2>(a, smem, grid, st);
+    case 21: return launch_dd<2, 1>(a, smem, grid, st);
+    case 22: return launch_dd<2, 2>(a, smem, grid, st);
+    case 41: return launch_dd<4, 1>(a, smem, grid, st);
+    case 42: return launch_dd<4, 2>(a, smem, grid, st);
+    case 81: return launch_dd<8, 1>(a, smem, grid, st);
+    case 82: return launch_dd<8, 2>(a, smem, grid, st);
     default: fbh::set_msg("dd_frame: GQA group %d not built", c->heads / c->kv_heads); return FB_ERR_UNSUPPORTED;
   }
 }

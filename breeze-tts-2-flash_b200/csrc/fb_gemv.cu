@@ -294,7 +294,7 @@ int launch_gemv_t(GemvArgs& a, cudaStream_t st) {
     }
     attr_done[dev] = (int)smem;
   }
-  const int grid = a.N < fbh::num_sms() ? a.N : fbh::num_sms();
+  const int grid = a.N < fbh::grid_sms() ? a.N : fbh::grid_sms();
   void* args[] = {(void*)&a};
   return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(GV_THREADS), smem, st, args, true);
 }

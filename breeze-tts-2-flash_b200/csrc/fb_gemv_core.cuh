@@ -275,7 +275,7 @@ inline int launch_mma_nt(GemvArgs& a, cudaStream_t st, int xchunk) {
     }
     attr_done[dev] = (int)smem;
   }
-  const int grid = a.N < fbh::num_sms() ? a.N : fbh::num_sms();
+  const int grid = a.N < fbh::grid_sms() ? a.N : fbh::grid_sms();
   void* args[] = {(void*)&a};
   return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(GM_THREADS), smem, st, args, true);
 }

@@ -34,6 +34,8 @@ _PROTOS = {
     'flashb_version': (ctypes.c_char_p, []),
     'flashb_device_error': (I, [I]),
     'flashb_set_pdl': (None, [I]),
+    'flashb_set_sm_budget': (None, [I]),
+    'flashb_sm_budget': (I, []),
     'flashb_attn_ws_floats': (L, [I, I, I, I, I]),
     'flashb_attn_decode': (I, [P, L, L, P, P, L, L, I, I, I, I, I, P, I, L, F, P, L, P, P, P]),
     'flashb_attn_decode_fused': (I, [P, L, P, P, F, P, P, L, P, P, L, L, I, I, I, I, I, P, I, L, P, F, P, L, P, P,
@@ -69,7 +71,7 @@ class FbDDConfig(ctypes.Structure):
     _fields_ = [('layers', I), ('batch', I), ('hidden', I), ('embed_dim', I), ('heads', I), ('kv_heads', I),
                 ('head_dim', I), ('ffn', I), ('vocab', I), ('codebook_size', I), ('n_decode', I), ('eps', F),
                 ('scaling', F), ('embed', P), ('proj', P), ('normf', P), ('head_t', P), ('cos_tab', P),
-                ('sin_tab', P), ('trace', P)]
+                ('sin_tab', P), ('trace', P), ('grid', I)]
 
 
 class FbBBLayer(ctypes.Structure):

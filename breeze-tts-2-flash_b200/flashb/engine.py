@@ -256,7 +256,23 @@ class _Slot:
     """``g`` streams decoded together: one backbone graph and one depth launch over 2 g rows laid out
     [cond_0 .. cond_{g-1}, uncond_0 .. uncond_{g-1}] (the CFG pair of stream k is rows k and k + g), which is the row
     order every kernel on the path already uses for B = 2 g."""
-    __slots__ = ('g', 'bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph', 'desc')
+    __slots__ = ('g', 'bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph', 'desc', 'lane')
+
+
+class sm_budget:
+    """Context manager: launches issued by this host thread inside it (directly or into a CUDA graph being captured)
+    size their grids for at most ``sms`` SMs (``flashb_set_sm_budget``); 0 = every SM."""
+
+    def __init__(self, sms):
+        self.sms = int(sms)
+
+    def __enter__(self):
+        lib().flashb_set_sm_budget(self.sms)
+        return self
+
+    def __exit__(self, *exc):
+        lib().flashb_set_sm_budget(0)
+        return False
 
 
 class FrameEngine:
@@ -276,32 +292,57 @@ class FrameEngine:
 
     The first three are captured into one CUDA graph per slot (``capture()``); the depth frame is a single launch.
     Each stream starts after a ``prompt_len``-token prompt whose KV cache is random (the prefill stand-in).
-    ``single_slot`` adds one extra single-stream slot on the same weights (``self.single``), for frame latency."""
+    ``single_slot`` adds one extra single-stream slot on the same weights (``self.single``), for frame latency.
+
+    ``lanes`` > 1 splits the GPU: slot i belongs to lane i % lanes, every lane has its own CUDA stream, depth scratch
+    and an SM budget of num_sms // lanes (grids of its persistent kernels, split counts of its attention), and
+    ``step()`` runs the lanes side by side.  Every kernel here is latency-bound at decode sizes, so two half-GPU
+    lanes finish two slots sooner than one whole-GPU lane finishes them one after the other."""
 
     def __init__(self, bcfg: BackboneConfig, dcfg: DepthConfig, n_streams, prompt_len, max_frames, device='cuda',
-                 seed=0, depth_only=False, group=1, single_slot=False):
+                 seed=0, depth_only=False, group=1, single_slot=False, lanes=1):
         """``depth_only``: no backbone (a random hidden state per stream feeds the depth frame) -- for timing or
         profiling the depth frame alone on a small device footprint."""
         if bcfg.codebooks - 1 > dcfg.n_decode or dcfg.embed_dim != bcfg.hidden:
             raise ValueError('backbone codebooks must be <= 1 + depth codebooks and depth embed_dim == backbone hidden')
         if group not in (1, 2, 4, 8) or n_streams % group:
             raise ValueError('group must be 1, 2, 4 or 8 and divide the number of streams')
+        if lanes < 1 or lanes > max(1, n_streams // group):
+            raise ValueError('lanes must be between 1 and the number of slots')
         self.bcfg, self.dcfg, self.group = bcfg, dcfg, group
         self.device = dev = torch.device(device)
+        self.lanes = lanes
+        nsm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == 'cuda' else 0
+        self.lane_sms = 0 if lanes == 1 else nsm // lanes
         self.prompt_len = prompt_len
         self.max_seq_len = prompt_len + max_frames + 2
         self.n_valid = min(dcfg.codebook_size, bcfg.vocab)
         self.depth_only = depth_only
         self.depth = SyntheticDepth(dcfg, batch=2 * group, device=dev, seed=seed + 3)
+        self.lane_desc = [self.depth.desc]
+        self.lane_stream = [None]
+        if lanes > 1:
+            from .depth import DepthModelDesc
+            d = self.depth
+            self.lane_desc = [DepthModelDesc(d.layers, d.embed, d.proj, d.normf, d.head_t, d.cos_tab, d.sin_tab,
+                                             dcfg.eps, 128 ** -0.5, dcfg.codebook_size, 2 * group, dev)
+                              for _ in range(lanes)]
+            for ld in self.lane_desc:
+                ld.cfg.grid = self.lane_sms
+            self.lane_stream = [torch.cuda.Stream(dev) for _ in range(lanes)]
         self._gen = torch.Generator(device='cpu').manual_seed(seed + 17)
         self._first_bb = None
         self._seed = seed
         self.streams = [self._slot(group, 1000 + seed + i) for i in range(n_streams // group)]
+        for i, st in enumerate(self.streams):
+            st.lane = i % lanes
+            st.desc = self.lane_desc[st.lane]
         self.single = None
         if single_slot:
             from .depth import DepthModelDesc
             d = self.depth
             self.single = self._slot(1, 999 + seed)
+            self.single.lane = None
             self.single.desc = d.desc if group == 1 else DepthModelDesc(
                 d.layers, d.embed, d.proj, d.normf, d.head_t, d.cos_tab, d.sin_tab, dcfg.eps, 128 ** -0.5,
                 dcfg.codebook_size, 2, dev)
@@ -326,6 +367,7 @@ class FrameEngine:
         st.q = torch.empty(dcfg.n_decode, g, dcfg.vocab).exponential_(1, generator=gen).to(dev)
         st.graph = None
         st.desc = self.depth.desc
+        st.lane = 0
         return st
 
     def _get(self, i):
@@ -362,8 +404,9 @@ class FrameEngine:
             torch.cuda.synchronize(self.device)
             return
         for i, st in self._slots()[:1] + ([self._slots()[-1]] if self.single is not None else []):
-            self.backbone_part(i)
-            self.depth_part(i)
+            with sm_budget(self._budget(st)):
+                self.backbone_part(i)
+                self.depth_part(i)
             torch.cuda.synchronize(self.device)
             st.bb.set_position(self.prompt_len - 1)
         side = torch.cuda.Stream(self.device)
@@ -371,21 +414,54 @@ class FrameEngine:
         with torch.cuda.stream(side):
             for i, st in self._slots():
                 graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph, stream=side):
+                with sm_budget(self._budget(st)), torch.cuda.graph(graph, stream=side):
                     self.backbone_part(i)
                 st.graph = graph
         torch.cuda.current_stream(self.device).wait_stream(side)
         torch.cuda.synchronize(self.device)
 
-    def frame(self, i):
+    def _budget(self, st):
+        return 0 if st.lane is None else self.lane_sms
+
+    def step(self, before_part=None, after_part=None):
+        """One frame of every slot (not the single-stream slot), lanes side by side, ordered after the work already
+        on the current stream; the current stream waits for every lane at the end.  ``before_part(kind, i, stream)``,
+        if given, is called before each part ('bb' or 'dd') of slot i with the CUDA stream it is issued on, and with
+        ('end', None, stream) once per lane stream after its last part; ``after_part('dd', i, stream)`` after the depth
+        part of slot i."""
+        cur = torch.cuda.current_stream(self.device)
+        if self.lanes == 1:
+            for i in range(len(self.streams)):
+                self.frame(i, before_part, after_part)
+            if before_part is not None:
+                before_part('end', None, cur)
+            return
+        for ls in self.lane_stream:
+            ls.wait_stream(cur)
+        for i, st in enumerate(self.streams):
+            with torch.cuda.stream(self.lane_stream[st.lane]):
+                self.frame(i, before_part, after_part)
+        for ls in self.lane_stream:
+            if before_part is not None:
+                before_part('end', None, ls)
+            cur.wait_stream(ls)
+
+    def frame(self, i, before_part=None, after_part=None):
         st = self._get(i)
+        stream = torch.cuda.current_stream(self.device)
+        if before_part is not None and st.bb is not None:
+            before_part('bb', i, stream)
         if st.bb is None:
             pass
         elif st.graph is not None:
             st.graph.replay()
         else:
             self.backbone_part(i)
+        if before_part is not None:
+            before_part('dd', i, stream)
         self.depth_part(i)
+        if after_part is not None:
+            after_part('dd', i, stream)
 
     def launches_per_frame(self):
         """Kernel launches per slot frame (the same for any group size)."""

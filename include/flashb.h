@@ -38,6 +38,15 @@ const char* flashb_version(void);
 int flashb_device_error(int clear);
 /* Programmatic dependent launch on (1, default) / off (0) for all later launches of this process. */
 void flashb_set_pdl(int enable);
+/* SM budget of the calling host thread (0, the default: every SM).  Launches issued later by this thread -- directly
+ * or while it captures a CUDA graph -- size their grids for at most `sms` SMs (persistent GEMV and LM-head grids,
+ * decode-attention split counts, depth-frame grids when fb_dd_config.grid is 0), so that work on two streams, each
+ * sized for part of the GPU, runs side by side instead of queueing for SMs.  The kernels are latency-bound at these
+ * sizes, which makes two half-GPU lanes faster in aggregate than one whole-GPU lane.  No reference counterpart
+ * (the reference decodes one request at a time). */
+void flashb_set_sm_budget(int sms);
+/* The grid size (SMs) the calling thread's launches use now. */
+int flashb_sm_budget(void);
 
 /* ---------------------------------------------------------------------------------------------- decode attention
  * Replaces attn_decode (flash/csrc/bb_attn.cu:416-429): GQA single-token attention of q [B, NH, 1, D] over the
@@ -193,6 +202,7 @@ typedef struct {
   const void* cos_tab; /* [n_decode + 2, 128] bf16 */
   const void* sin_tab;
   uint64_t* trace;     /* optional: [grid][n_decode][11 + 9 * layers] %globaltimer stamps per CTA (task ends, barriers) */
+  int grid;            /* CTAs of the launch, one per SM: 0 = every SM; fewer leave SMs to work on other streams */
 } fb_dd_config;
 int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg);
 int64_t flashb_dd_layer_bytes(void);

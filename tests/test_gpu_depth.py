@@ -129,11 +129,14 @@ def test_depth_free_running_equals_forced_oracle():
     np.testing.assert_array_equal(tok, outtok[:, -1])
 
 
-@pytest.mark.parametrize('B', [2, 8, 16])
-def test_depth_full_size_forced_and_sampler(B):
+@pytest.mark.parametrize('B,grid', [(2, 0), (8, 0), (16, 0), (16, 74), (16, 18)])
+def test_depth_full_size_forced_and_sampler(B, grid):
     """The synthetic full-size depth decoder (4 layers, hidden 1024, 16 codebooks of 2048).  B = 8 (four CFG pairs)
-    runs the distributed attention mode (one (row, KV head) pair per CTA) and one sampler CTA per pair."""
+    runs the distributed attention mode (one (row, KV head) pair per CTA) and one sampler CTA per pair.  A grid of
+    fewer CTAs than SMs (a lane of the GPU) spreads the same tasks over fewer CTAs; with fewer CTAs than (row, KV
+    head) pairs (18 < 16 x 2) every CTA stages the batch's K/V in chunks of rows instead."""
     m = _model(small=False, B=B, seed=5)
+    m.desc.cfg.grid = grid
     c = m.cfg
     forced = np.random.default_rng(5).integers(0, c.vocab, (c.n_decode, B))
     outtok, logits, _ = _run(m, forced)

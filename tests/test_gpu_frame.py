@@ -59,12 +59,12 @@ def test_frame_ids_assembly():
     assert torch.equal(ids, ref)
 
 
-def _small_engine(streams=2, prompt=40, frames=4, group=1):
+def _small_engine(streams=2, prompt=40, frames=4, group=1, lanes=1):
     from flashb.engine import BackboneConfig, DepthConfig, FrameEngine
     bcfg = BackboneConfig(hidden=512, layers=2, heads=8, kv_heads=2, ffn=1024, vocab=65, codebooks=7)
     dcfg = DepthConfig(hidden=256, embed_dim=512, layers=2, heads=2, kv_heads=1, ffn=512, vocab=64,
                        codebook_size=60, n_decode=6)
-    eng = FrameEngine(bcfg, dcfg, streams, prompt, frames, seed=4, group=group)
+    eng = FrameEngine(bcfg, dcfg, streams, prompt, frames, seed=4, group=group, lanes=lanes)
     return eng
 
 
@@ -77,35 +77,45 @@ def _oracle_backbone(bb):
                                bb.cfg.eps, bb.cfg.theta)
 
 
-@pytest.mark.parametrize('group', [1, 2, 4, 8])
-def test_frame_engine_matches_oracle_and_standalone_depth(group):
-    """group 2: two streams share one slot (rows [c0, c1, u0, u1]); every row must still match the oracle."""
-    eng = _small_engine(streams=max(2, group), group=group)
+@pytest.mark.parametrize('group,lanes', [(1, 1), (2, 1), (4, 1), (8, 1), (1, 2), (2, 3)])
+def test_frame_engine_matches_oracle_and_standalone_depth(group, lanes):
+    """group 2: two streams share one slot (rows [c0, c1, u0, u1]); every row must still match the oracle.
+    lanes > 1: the slots' frames run on several CUDA streams side by side, each lane sized for part of the SMs."""
+    n_slots = max(1, lanes) * (2 if lanes > 1 else 1)
+    eng = _small_engine(streams=max(2, group) * n_slots if lanes > 1 else max(2, group), group=group, lanes=lanes)
     eng.capture()
     R = 2 * group
     W = _oracle_backbone(eng.streams[0].bb)
     C = eng.bcfg.codebooks
-    for i, st in enumerate(eng.streams):
+    state = []
+    for st in eng.streams:
         bb = st.bb
-        mask = np32(bb.attn_mask).copy()
-        pos = int(bb.cache_position.item())
-        pids = bb.position_ids.view(-1).cpu().numpy().copy()
-        for f in range(3):
-            # each frame is checked from the device's own state (its KV cache so far), so the comparison is per
-            # frame and does not compound earlier frames' rounding differences
-            kcs = [np32(L.keys).copy() for L in bb.static_cache.layers]
-            vcs = [np32(L.values).copy() for L in bb.static_cache.layers]
-            ids = np.concatenate([st.first_cb.cpu().numpy()[:, None], st.outtok.cpu().numpy()[:, :C - 1]], 1)
-            eng.frame(i)
-            torch.cuda.synchronize()
-            np.testing.assert_array_equal(bb.input_ids_buf.view(R, -1).cpu().numpy(), ids)
-            pos += 1
-            pids += 1
-            mask[..., pos] = 0.0
+        state.append(dict(mask=np32(bb.attn_mask).copy(), pos=int(bb.cache_position.item()),
+                          pids=bb.position_ids.view(-1).cpu().numpy().copy()))
+    for f in range(3):
+        # each frame is checked from the device's own state (its KV cache so far), so the comparison is per frame and
+        # does not compound earlier frames' rounding differences
+        before = []
+        for st in eng.streams:
+            bb = st.bb
+            before.append(dict(kcs=[np32(L.keys).copy() for L in bb.static_cache.layers],
+                               vcs=[np32(L.values).copy() for L in bb.static_cache.layers],
+                               ids=np.concatenate([st.first_cb.cpu().numpy()[:, None],
+                                                   st.outtok.cpu().numpy()[:, :C - 1]], 1)))
+        eng.step()
+        torch.cuda.synchronize()
+        for i, st in enumerate(eng.streams):
+            bb, sv, bf = st.bb, state[i], before[i]
+            np.testing.assert_array_equal(bb.input_ids_buf.view(R, -1).cpu().numpy(), bf['ids'])
+            sv['pos'] += 1
+            sv['pids'] += 1
+            sv['mask'][..., sv['pos']] = 0.0
             gs = float(bb.guidance_scale.item())
-            h, lg, _ = dec.backbone_step(W, ids, kcs, vcs, mask, pos, pids, gs)
-            assert int(bb.cache_position.item()) == pos
-            assert_close(np32(bb.hidden_buf).reshape(R, -1), h, what=f'slot {i} frame {f} hidden')
+            h, lg, _ = dec.backbone_step(W, bf['ids'], bf['kcs'], bf['vcs'], sv['mask'], sv['pos'], sv['pids'], gs)
+            assert int(bb.cache_position.item()) == sv['pos']
+            # the hidden state leaves a stack of layers, each held to 1e-2 alone (test_gpu_backbone); through the
+            # stack 1-ulp bf16 flips of the residual adds compound, so it gets the stack's 3e-2 bound
+            assert_close(np32(bb.hidden_buf).reshape(R, -1), h, tol=3e-2, what=f'slot {i} frame {f} hidden')
             g_lg = bb.logits_buf.cpu().numpy()
             assert_close(g_lg, lg, what=f'slot {i} frame {f} logits')
             # CFG u + gs (c - u) amplifies logit rounding differences ~(2 gs - 1)x by construction; the combine
@@ -122,6 +132,8 @@ def test_frame_engine_matches_oracle_and_standalone_depth(group):
                           d.top_p[:group], d.do_sample[:group], d.guidance_scale[:group], st.q)
             torch.cuda.synchronize()
             assert torch.equal(out, st.outtok)
+    from flashb._native import device_error
+    assert device_error() == 0
 
 
 def test_frame_engine_graph_equals_eager():
