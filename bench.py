@@ -33,10 +33,10 @@ sys.path[:0] = [HERE, os.path.join(HERE, 'breeze-tts-2-flash_b200')]
 N_STREAMS = 64
 PROMPT = 512
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0)
-# dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch for a pair of streams (B = 4 rows, the
-# bench's default): ncu --set full capture of the full-size depth model, 2.099728 GB read + 30.472448 MB written
-# (profiles/dd_frame_kernel_depth_frame_pair.md).
-DD_TRAFFIC_BYTES = 2130200448
+# dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch at the bench's default shape (8 streams
+# per launch, B = 16 rows, one lane's grid of 18 CTAs): ncu --set full capture of the full-size depth model, 2,177,250,048
+# B read + 8,066,304 B written (profiles/dd_frame_kernel_depth_frame_8streams_grid18.md).
+DD_TRAFFIC_BYTES = 2185316352
 PREFILL_CFG = dict(B=2, NH=16, NKV=4, L=512, D=128, pads=(0, 37))
 
 
@@ -276,7 +276,7 @@ def main():
     if my_streams % a.group:
         raise SystemExit(f'{my_streams} streams per rank do not split into groups of {a.group}')
     LAT_FRAMES = 20
-    lanes = max(1, min(a.lanes, my_streams // a.group)) if a.case == 'frame' else 1
+    lanes = max(1, min(a.lanes, my_streams // a.group)) if a.case in ('frame', 'depth') else 1
     eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + LAT_FRAMES + 8, device=dev, seed=0,
                       depth_only=(a.case == 'depth'), group=a.group, single_slot=(a.case == 'frame'),
                       lanes=lanes)
@@ -303,17 +303,13 @@ def main():
                 e = torch.cuda.Event(enable_timing=True)
                 e.record(s)
                 ev.append((s, kind, e))
-        if case == 'frame':
-            eng.step(mark)
+        if case != 'backbone':
+            eng.step(mark)       # the frame, or the depth part alone (an engine without backbone)
             return
-        # one part alone, on the current stream (one lane)
+        # the backbone part alone, on the current stream (one lane)
         for i in range(S):
-            if case == 'backbone':
-                mark('bb', i, stream)
-                eng.streams[i].graph.replay()
-            else:
-                mark('dd', i, stream)
-                eng.depth_part(i)
+            mark('bb', i, stream)
+            eng.streams[i].graph.replay()
         mark('end', None, stream)
 
     # ---- device-resident run
