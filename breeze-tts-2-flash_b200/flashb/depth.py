@@ -6,8 +6,8 @@ Exp(1) draws with the official sizes and order (``q[c].exponential_(1)``, the RN
 and samples on the device.  The weights stay bf16 (the reference's 12-bit LN12 packing is not used); the codebook
 heads are transposed once to [n_decode, vocab, hidden] bf16 (bf16-exact, as the reference asserts).
 
-``BUILDS`` / ``GRIDS`` keep the reference's names; one build serves every batch size and the grid is always one CTA
-per SM.  Process state (``_state``) is keyed by device, so several graphs on several GPUs in one process coexist.
+``BUILDS`` / ``GRIDS`` keep the reference's names; one build serves every batch size.  ``GRIDS[B]`` is the launch's CTA
+count for batch B (0: one CTA per SM, or the calling thread's SM budget, ``flashb_set_sm_budget``).  Process state (``_state``) is keyed by device, so several graphs on several GPUs in one process coexist.
 """
 import ctypes
 import json
@@ -93,6 +93,7 @@ class DepthOps:
             layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb = self.args
             d = DepthModelDesc(layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb, B, device)
             self.desc[B] = d
+        d.cfg.grid = GRIDS.get(B, 0)
         return d
 
     def dd2_frame(self, first_cb, bh, tokbuf, outtok, temp, topk, topp, dosample, gs, q, dbg=None, forced=None):
@@ -102,7 +103,8 @@ class DepthOps:
     def dd2_info(self):
         a = self.args
         return json.dumps(dict(NL=len(a[0]) if a else 0, ln12=0, pf_last=0, tab=0, grid=0,
-                               grid_B1=GRIDS[1], grid_B2=GRIDS[2], grid_B4=GRIDS[4], persisting_l2_limit=0))
+                               grid_B1=GRIDS[1], grid_B2=GRIDS[2], grid_B4=GRIDS[4], grid_B8=GRIDS[8],
+                               grid_B16=GRIDS[16], persisting_l2_limit=0))
 
     def dd2_tab_build(self):
         raise RuntimeError('the per-token step table (flash/csrc/depth_frame.cu:714-754) is not built by flashb')
