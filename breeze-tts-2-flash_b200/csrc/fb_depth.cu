@@ -479,39 +479,55 @@ __device__ __noinline__ void dd_attention(const DDArgs& a, int l, int pos, unsig
   }
 }
 
-// Attention of ONE (batch row b, KV head kvh) pair -- its G query heads -- for the distributed mode (used when the
-// whole batch's K/V would not fit one staging round): the CTA stages q, K and V of the pair, computes as
-// dd_attention does, and writes the output over the pair's q slice in a.qb (no other CTA reads that slice before the
-// barrier that follows).
+// Shared-memory bytes of one (batch row, KV head) pair in the distributed attention mode: its G q rows, the layer's
+// K and V of positions 0..P-1, G x 32 scores.
+__host__ __device__ constexpr size_t dd_pair_bytes(int G, int P) {
+  return (size_t)G * 256 + 2 * (size_t)P * 256 + (size_t)G * 32 * 4;
+}
+
+// Distributed attention: this CTA's (batch row, KV head) pairs [p0, p1) (pair i = row i / NKV, KV head i % NKV),
+// all staged in one cp.async round trip.  The same arithmetic and rounding points as dd_attention; the output goes
+// over each pair's q slice in a.qb (no other CTA reads that slice before the barrier that follows).
 template <int G>
-__device__ __noinline__ void dd_attention_pair(const DDArgs& a, int l, int pos, int b, int kvh, unsigned char* att) {
+__device__ __noinline__ void dd_attention_pairs(const DDArgs& a, int l, int pos, int p0, int p1, unsigned char* att) {
   const int tid = threadIdx.x;
-  const int QD = a.NH * 128;
-  const int np = pos + 1;
-  bf16* qs = reinterpret_cast<bf16*>(att);
-  bf16* ks = qs + G * 128;
-  bf16* vs = ks + (size_t)np * 128;
-  float* ps = reinterpret_cast<float*>(vs + (size_t)np * 128);
-  bf16* qg = a.qb + (size_t)b * QD + (size_t)kvh * G * 128;
-  const size_t kvoff = ((((size_t)l * a.B + b) * a.NKV + kvh) * a.P) * 128;
-  const int qch = G * 16, kch = np * 16;
-  for (int i = tid; i < qch + 2 * kch; i += PK_CONSUMERS) {
-    if (i < qch) {
-      cp_async16(qs + (size_t)i * 8, qg + (size_t)i * 8);
+  const int QD = a.NH * 128, NKV = a.NKV;
+  const int np = pos + 1, npair = p1 - p0;
+  if (npair <= 0) return;
+  const size_t pb = dd_pair_bytes(G, np);
+  auto qs_of = [&](int k) { return reinterpret_cast<bf16*>(att + (size_t)k * pb); };
+  auto ks_of = [&](int k) { return qs_of(k) + G * 128; };
+  auto vs_of = [&](int k) { return ks_of(k) + (size_t)np * 128; };
+  auto ps_of = [&](int k) { return reinterpret_cast<float*>(vs_of(k) + (size_t)np * 128); };
+  auto qg_of = [&](int k) {
+    const int pi = p0 + k, b = pi / NKV, kvh = pi - b * NKV;
+    return a.qb + (size_t)b * QD + (size_t)kvh * G * 128;
+  };
+  const int qch = G * 16, kch = np * 16, per = qch + 2 * kch;
+  for (int i = tid; i < npair * per; i += PK_CONSUMERS) {
+    const int k = i / per;
+    int j = i - k * per;
+    if (j < qch) {
+      cp_async16(qs_of(k) + (size_t)j * 8, qg_of(k) + (size_t)j * 8);
     } else {
-      int j = i - qch;
+      j -= qch;
       const bool isv = j >= kch;
       if (isv) j -= kch;
-      cp_async16((isv ? vs : ks) + (size_t)j * 8, (isv ? a.vc : a.kc) + kvoff + (size_t)j * 8);
+      const int pi = p0 + k, b = pi / NKV, kvh = pi - b * NKV;
+      const size_t kvoff = ((((size_t)l * a.B + b) * NKV + kvh) * a.P) * 128;
+      cp_async16((isv ? vs_of(k) : ks_of(k)) + (size_t)j * 8, (isv ? a.vc : a.kc) + kvoff + (size_t)j * 8);
     }
   }
   cp_async_commit();
   cp_async_wait<0>();
   named_sync(1, PK_CONSUMERS);
-  for (int i = tid; i < G * np; i += PK_CONSUMERS) {
-    const int hq = i / np, j = i - hq * np;
-    const uint4* qr = reinterpret_cast<const uint4*>(qs + (size_t)hq * 128);
-    const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)j * 128);
+  const float scaling = a.scaling;
+  for (int i = tid; i < npair * G * np; i += PK_CONSUMERS) {
+    const int k = i / (G * np);
+    const int r = i - k * G * np;
+    const int hq = r / np, j = r - hq * np;
+    const uint4* qr = reinterpret_cast<const uint4*>(qs_of(k) + (size_t)hq * 128);
+    const uint4* kr = reinterpret_cast<const uint4*>(ks_of(k) + (size_t)j * 128);
     float d = 0.f;
 #pragma unroll 4
     for (int cc = 0; cc < 16; ++cc) {
@@ -522,11 +538,12 @@ __device__ __noinline__ void dd_attention_pair(const DDArgs& a, int l, int pos, 
 #pragma unroll
       for (int u = 0; u < 8; ++u) d = fmaf(qf[u], kf[u], d);
     }
-    ps[hq * 32 + j] = rbf(rbf(d) * a.scaling);
+    ps_of(k)[hq * 32 + j] = rbf(rbf(d) * scaling);
   }
   named_sync(1, PK_CONSUMERS);
-  if (tid < G) {
-    float* pr = ps + tid * 32;
+  if (tid < npair * G) {
+    const int k = tid / G, hq = tid - k * G;
+    float* pr = ps_of(k) + hq * 32;
     float mx = -INFINITY;
     for (int j = 0; j < np; ++j) mx = fmaxf(mx, pr[j]);
     float den = 0.f;
@@ -538,9 +555,12 @@ __device__ __noinline__ void dd_attention_pair(const DDArgs& a, int l, int pos, 
     for (int j = 0; j < np; ++j) pr[j] = rbf(pr[j] / den);
   }
   named_sync(1, PK_CONSUMERS);
-  for (int i = tid; i < G * 16; i += PK_CONSUMERS) {
-    const int hq = i >> 4, c = i & 15;
-    const float* pr = ps + hq * 32;
+  for (int i = tid; i < npair * G * 16; i += PK_CONSUMERS) {
+    const int k = i / (G * 16);
+    const int r = i - k * G * 16;
+    const int hq = r >> 4, c = r & 15;
+    const float* pr = ps_of(k) + hq * 32;
+    const bf16* vs = vs_of(k);
     float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < np; ++j) {
       float vf[8];
@@ -554,7 +574,7 @@ __device__ __noinline__ void dd_attention_pair(const DDArgs& a, int l, int pos, 
     ov.y = pack2(o[2], o[3]);
     ov.z = pack2(o[4], o[5]);
     ov.w = pack2(o[6], o[7]);
-    *reinterpret_cast<uint4*>(qg + (size_t)hq * 128 + c * 8) = ov;
+    *reinterpret_cast<uint4*>(qg_of(k) + (size_t)hq * 128 + c * 8) = ov;
   }
   named_sync(1, PK_CONSUMERS);
 }
@@ -772,8 +792,10 @@ __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int p
   const int tb = 3 + 9 * l;
   bf16* const ob = a.ob;
   if (a.att_split) {
-    if ((int)blockIdx.x < a.B * NKV)
-      dd_attention_pair<G>(a, l, pos, (int)blockIdx.x / NKV, (int)blockIdx.x % NKV, m.xs + a.att_off);
+    const int npairs = a.B * NKV;
+    const int p0 = (int)((long long)npairs * blockIdx.x / gridDim.x);
+    const int p1 = (int)((long long)npairs * (blockIdx.x + 1) / gridDim.x);
+    dd_attention_pairs<G>(a, l, pos, p0, p1, m.xs + a.att_off);
     if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) {
       c.ok = 0;
       return c;
@@ -1117,23 +1139,25 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
     a.d_xchunk = 1;
     layout(1, keep_off, base);
   }
-  // attention: the whole batch in one staging round when that still leaves 4 ring stages; otherwise one
-  // (batch row, KV head) pair per CTA (distributed mode: one extra grid barrier per layer, small staging), or, with
-  // fewer CTAs than pairs, the batch in chunks of rows on every CTA
+  // attention: the whole batch in one staging round when that still leaves 4 ring stages; otherwise the
+  // (batch row, KV head) pairs spread over the CTAs (distributed mode: one extra grid barrier per layer, small
+  // staging); if even a CTA's share of pairs leaves fewer than 3 stages, the batch in chunks of rows on every CTA
   const int G = c->heads / c->kv_heads;
   size_t xs = al256d(att_off + dd_attn_bytes(c->batch, c->heads, c->kv_heads, c->n_decode + 1));
   if (xs < base) xs = base;
   int nst = stages_for(xs);
   a.att_bc = c->batch;
   a.att_split = 0;
-  if (nst < 4 && c->batch * c->kv_heads <= grid) {
-    const size_t pair = (size_t)G * 256 + 2 * (size_t)(c->n_decode + 1) * 256 + (size_t)G * 32 * 4;
-    xs = al256d(att_off + pair);
-    if (xs < base) xs = base;
-    nst = stages_for(xs);
-    a.att_split = 1;
+  if (nst < 4) {
+    const int per_cta = (c->batch * c->kv_heads + grid - 1) / grid;
+    size_t xs_split = al256d(att_off + per_cta * dd_pair_bytes(G, c->n_decode + 1));
+    if (xs_split < base) xs_split = base;
+    if (stages_for(xs_split) >= 3) {
+      xs = xs_split;
+      nst = stages_for(xs);
+      a.att_split = 1;
+    }
   }
-  // too few CTAs for one (row, KV head) pair each: every CTA stages the batch's K/V in chunks of rows instead
   while (nst < 4 && !a.att_split && a.att_bc > 1) {
     a.att_bc = (a.att_bc + 1) / 2;
     xs = al256d(att_off + dd_attn_bytes(a.att_bc, c->heads, c->kv_heads, c->n_decode + 1));

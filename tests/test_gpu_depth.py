@@ -129,12 +129,12 @@ def test_depth_free_running_equals_forced_oracle():
     np.testing.assert_array_equal(tok, outtok[:, -1])
 
 
-@pytest.mark.parametrize('B,grid', [(2, 0), (8, 0), (16, 0), (16, 74), (16, 18)])
+@pytest.mark.parametrize('B,grid', [(2, 0), (8, 0), (16, 0), (16, 74), (16, 18), (16, 8)])
 def test_depth_full_size_forced_and_sampler(B, grid):
     """The synthetic full-size depth decoder (4 layers, hidden 1024, 16 codebooks of 2048).  B = 8 (four CFG pairs)
-    runs the distributed attention mode (one (row, KV head) pair per CTA) and one sampler CTA per pair.  A grid of
-    fewer CTAs than SMs (a lane of the GPU) spreads the same tasks over fewer CTAs; with fewer CTAs than (row, KV
-    head) pairs (18 < 16 x 2) every CTA stages the batch's K/V in chunks of rows instead."""
+    runs the distributed attention mode ((row, KV head) pairs spread over the CTAs) and one sampler CTA per pair.  A
+    grid of fewer CTAs than SMs (a lane of the GPU) spreads the same tasks over fewer CTAs; with fewer CTAs than
+    pairs (18 or 8 < 16 x 2) a CTA takes several pairs, staged together."""
     m = _model(small=False, B=B, seed=5)
     m.desc.cfg.grid = grid
     c = m.cfg
