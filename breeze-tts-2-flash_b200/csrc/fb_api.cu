@@ -1,8 +1,13 @@
 // flashb: library-level C ABI (error reporting, device error word, launch helper).
+#include <cudaTypedefs.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "fb_common.cuh"
 
@@ -48,6 +53,49 @@ int num_sms() {
     g_sms[dev] = n > 0 ? n : 148;
   }
   return g_sms[dev];
+}
+
+int tmap_rows(CUtensorMap* out, const void* base, long long rows, int K, int kc) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  static std::map<std::tuple<uintptr_t, long long, int, int>, CUtensorMap> cache;
+  static std::mutex mu;
+  if (!base || rows < 1 || rows > (1ll << 31) || K < 64 || K % 64 || kc < 64 || kc % 64 || kc / 64 > 256 ||
+      (reinterpret_cast<uintptr_t>(base) & 15)) {
+    set_msg("tensor map: bad matrix (rows %lld, K %d, stage columns %d, base %p)", rows, K, kc, base);
+    return FB_ERR_ARG;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), rows, K, kc);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return FB_OK;
+  }
+  if (!enc) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn) {
+      set_msg("tensor map: cuTensorMapEncodeTiled unavailable");
+      return FB_ERR_CUDA;
+    }
+    enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  CUtensorMap m;
+  std::memset(&m, 0, sizeof(m));
+  const cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(K / 64)};
+  const cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};   // bytes: next row, next 64-column block
+  const cuuint32_t box[3] = {64, 8, (cuuint32_t)(kc / 64)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_msg("tensor map: cuTensorMapEncodeTiled failed (%d) for rows %lld, K %d", (int)r, rows, K);
+    return FB_ERR_CUDA;
+  }
+  cache.emplace(key, m);
+  *out = m;
+  return FB_OK;
 }
 
 int grid_sms() {

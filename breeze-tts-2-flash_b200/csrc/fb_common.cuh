@@ -1,6 +1,7 @@
 // flashb: shared device helpers for the sm_100a kernels (bf16 conversion, bulk-copy/mbarrier pipeline, PDL,
 // bounded waits, the device error word).
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -152,7 +153,12 @@ int launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_
                int cluster_x = 0);
 bool pdl_enabled();
 int num_sms();
-int grid_sms();  // num_sms(), or the calling thread's SM budget when one is set (flashb_set_sm_budget)
+int grid_sms();
+// Tensor map of a row-major bf16 matrix [rows, K] (K % 64 == 0, base 16-byte aligned) viewed as
+// [K / 64 column blocks][rows][64 columns], for 8-row boxes of kc columns with the 128-byte swizzle (fb_stream.cuh
+// TMA stages).  Encoded through the driver's cuTensorMapEncodeTiled (fetched once, no link to libcuda) and cached
+// per (base, rows, K, kc).  Returns FB_OK, or FB_ERR_ARG / FB_ERR_CUDA with the message set.
+int tmap_rows(CUtensorMap* out, const void* base, long long rows, int K, int kc);  // num_sms(), or the calling thread's SM budget when one is set (flashb_set_sm_budget)
 }  // namespace fbh
 
 #define FB_CHECK_ARG(cond, ...)          \

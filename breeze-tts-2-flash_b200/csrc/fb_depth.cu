@@ -28,6 +28,7 @@
 //
 // Scratch (residual stream, q, o, act, logits, KV cache, barrier) is one caller-owned buffer, zeroed once.
 #define FB_ST_KC 1024
+#define FB_ST_TMA 1
 #define FB_PK_MAX_STAGES 8
 #include <mutex>
 
@@ -37,12 +38,16 @@ namespace fb {
 
 constexpr int DD_MAXB = 16;     // batch rows (eight CFG pairs)
 constexpr int DD_MAXV = 4096;   // sampler vocabulary bound (composite key packs 12 index bits)
+constexpr int DD_MAXL = 8;      // layers (their tensor maps travel in the argument block)
+enum { DD_WQ, DD_WK, DD_WV, DD_WO, DD_WG, DD_WU, DD_WD, DD_NMAPS };
 
 struct DDLayer {
   const bf16 *ln1, *wq, *wk, *wv, *wo, *ln2, *wg, *wu, *wd;
 };
 
-struct DDArgs {
+struct alignas(64) DDArgs {
+  CUtensorMap tm_proj, tm_head;           // projector [H, AE]; codebook heads [n_decode * V, H]
+  CUtensorMap tm[DD_MAXL][DD_NMAPS];      // per layer: wq, wk, wv, wo, wg, wu, wd
   int L, B, H, AE, NH, NKV, F, V, CB, NCB, P;
   float eps, scaling;
   const DDLayer* layers;
@@ -638,7 +643,8 @@ __device__ __forceinline__ DDSm dd_smem(const DDArgs& a) {
   DDSm m;
   m.xs = smem;
   m.zero16 = smem + a.xs_bytes;
-  unsigned char* ringb = m.zero16 + 128;
+  unsigned char* ringb = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(m.zero16 + 128) + (ST_ALIGN - 1)) & ~uintptr_t(ST_ALIGN - 1));
   m.red = reinterpret_cast<float*>(ringb + (size_t)a.nstages * ST_BYTES);
   m.sums = m.red + ST_CWARPS * 128 * NT;
   uint64_t* full = reinterpret_cast<uint64_t*>(m.sums + 128 * NT);
@@ -653,37 +659,36 @@ struct DDCur {
   int ok;
 };
 
-// Producer warp: every weight slice of the frame, in the consumers' order, through the ring.
+// Producer warp: every weight slice of the frame, in the consumers' order, through the ring (two 8-row TMA tensor
+// copies per stage; the maps travel in the argument block).
 template <int NT>
 __device__ __noinline__ void dd_producer(const DDArgs& a) {
   DDSm m = dd_smem<NT>(a);
   const int H = a.H, AE = a.AE, NH = a.NH, NKV = a.NKV, F = a.F, V = a.V;
   const int QKVU = (NH + 2 * NKV) * 64;  // rotary pair units
   const int L = a.L, NCB = a.NCB;
-  const bf16 *const proj = a.proj, *const head_t = a.head_t;
-  const DDLayer* const layers = a.layers;
   unsigned* const err = a.err;
   int t = 0;
   bool ok = true;
   for (int s = 0; s < NCB && ok; ++s) {
     for (int sub = 0; sub < (s == 0 ? 2 : 1) && ok; ++sub) {
-      ok = ok && produce_task<1>(m.rg, t, H, AE, [&](int n, int) { return proj + (size_t)n * AE; }, err);
+      ok = ok && produce_task_tma<1>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
       for (int l = 0; l < L && ok; ++l) {
-        const DDLayer W = layers[l];   // by value: the row lambdas below then read registers only
-        ok = ok && produce_task<2>(m.rg, t, QKVU, H, [&](int u, int mat) -> const bf16* {
+        const CUtensorMap* W = a.tm[l];
+        // unit u = (head hh, rotary pair d): matrix 0 carries row hh * 128 + d, matrix 1 row hh * 128 + 64 + d
+        ok = ok && produce_task_tma<2>(m.rg, t, QKVU, H, [&](int u, int mat) {
           const int hh = u >> 6, d = (u & 63) + mat * 64;
-          if (hh < NH) return W.wq + (size_t)(hh * 128 + d) * H;
-          if (hh < NH + NKV) return W.wk + (size_t)((hh - NH) * 128 + d) * H;
-          return W.wv + (size_t)((hh - NH - NKV) * 128 + d) * H;
+          if (hh < NH) return TmaRows{&W[DD_WQ], hh * 128 + d};
+          if (hh < NH + NKV) return TmaRows{&W[DD_WK], (hh - NH) * 128 + d};
+          return TmaRows{&W[DD_WV], (hh - NH - NKV) * 128 + d};
         }, err);
-        ok = ok && produce_task<1>(m.rg, t, H, NH * 128,
-                                   [&](int n, int) { return W.wo + (size_t)n * NH * 128; }, err);
-        ok = ok && produce_task<2>(m.rg, t, F, H,
-                                   [&](int n, int mat) { return (mat ? W.wu : W.wg) + (size_t)n * H; }, err);
-        ok = ok && produce_task<1>(m.rg, t, H, F, [&](int n, int) { return W.wd + (size_t)n * F; }, err);
+        ok = ok && produce_task_tma<1>(m.rg, t, H, NH * 128, [&](int n, int) { return TmaRows{&W[DD_WO], n}; }, err);
+        ok = ok && produce_task_tma<2>(m.rg, t, F, H,
+                                       [&](int n, int mat) { return TmaRows{&W[mat ? DD_WU : DD_WG], n}; }, err);
+        ok = ok && produce_task_tma<1>(m.rg, t, H, F, [&](int n, int) { return TmaRows{&W[DD_WD], n}; }, err);
       }
     }
-    ok = ok && produce_task<1>(m.rg, t, V, H, [&](int n, int) { return head_t + ((size_t)s * V + n) * H; }, err);
+    ok = ok && produce_task_tma<1>(m.rg, t, V, H, [&](int n, int) { return TmaRows{&a.tm_head, s * V + n}; }, err);
   }
   // never leave with copies in flight into this CTA's shared memory
   for (int u = max(0, t - m.rg.nst); u < t; ++u)
@@ -1080,8 +1085,10 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   FB_CHECK_ARG(c->vocab >= 1 && c->vocab <= DD_MAXV && c->codebook_size >= 1 && c->codebook_size <= c->vocab,
                "dd_frame: vocab must be <= %d and codebook_size <= vocab", DD_MAXV);
   FB_CHECK_ARG(c->n_decode >= 1 && c->n_decode <= 31, "dd_frame: n_decode must be 1..31");
-  FB_CHECK_ARG(c->hidden % 16 == 0 && c->embed_dim % 16 == 0 && c->ffn % 16 == 0 && c->heads % c->kv_heads == 0,
-               "dd_frame: bad dims");
+  FB_CHECK_ARG(c->hidden % 64 == 0 && c->embed_dim % 64 == 0 && c->ffn % 64 == 0 && c->heads % c->kv_heads == 0,
+               "dd_frame: hidden, embed_dim and ffn must be multiples of 64, heads a multiple of kv_heads");
+  FB_CHECK_ARG(c->layers >= 1 && c->layers <= DD_MAXL && c->layers_host,
+               "dd_frame: 1..%d layers, with the host copy of the layer table (layers_host)", DD_MAXL);
   FB_CHECK_ARG(((uintptr_t)scratch & 255) == 0, "dd_frame: scratch must be 256-byte aligned");
   const DDLayout Lo = dd_layout(c);
   DDArgs a{};
@@ -1089,6 +1096,24 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.F = c->ffn; a.V = c->vocab; a.CB = c->codebook_size; a.NCB = c->n_decode; a.P = c->n_decode + 1;
   a.eps = c->eps; a.scaling = c->scaling;
   a.layers = (const DDLayer*)layers_dev;
+  {
+    // tensor maps of every streamed matrix, built from the host copy of the layer table (cached per matrix)
+    const DDLayer* hl = (const DDLayer*)c->layers_host;
+    const int QD = c->heads * 128, KD = c->kv_heads * 128;
+    int rc = fbh::tmap_rows(&a.tm_proj, c->proj, c->hidden, c->embed_dim, ST_KC);
+    if (!rc) rc = fbh::tmap_rows(&a.tm_head, c->head_t, (long long)c->n_decode * c->vocab, c->hidden, ST_KC);
+    for (int l = 0; l < c->layers && !rc; ++l) {
+      const DDLayer& W = hl[l];
+      rc = fbh::tmap_rows(&a.tm[l][DD_WQ], W.wq, QD, c->hidden, ST_KC);
+      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WK], W.wk, KD, c->hidden, ST_KC);
+      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WV], W.wv, KD, c->hidden, ST_KC);
+      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WO], W.wo, c->hidden, QD, ST_KC);
+      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WG], W.wg, c->ffn, c->hidden, ST_KC);
+      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WU], W.wu, c->ffn, c->hidden, ST_KC);
+      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WD], W.wd, c->hidden, c->ffn, ST_KC);
+    }
+    if (rc) return rc;
+  }
   a.embed = (const bf16*)c->embed; a.proj = (const bf16*)c->proj; a.normf = (const bf16*)c->normf;
   a.head_t = (const bf16*)c->head_t; a.cos_tab = (const bf16*)c->cos_tab; a.sin_tab = (const bf16*)c->sin_tab;
   a.first_cb = (const long long*)first_cb; a.bh = (const bf16*)bh; a.tokbuf = (long long*)tokbuf;
@@ -1121,7 +1146,7 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   const size_t xs_smp = al256d(dd_sampler_bytes(c->vocab));
   const size_t budget = 227 * 1024 - ST_CWARPS * 16 * 4 - 32 * 4 - DD_MAXB * 8 - 2 * 128 * 2 - 256;
   auto stages_for = [&](size_t xsb) {
-    const size_t fixed = xsb + 128 + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * PK_MAX_STAGES * 8;
+    const size_t fixed = xsb + 128 + ST_ALIGN + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * PK_MAX_STAGES * 8;
     int n = fixed < budget ? (int)((budget - fixed) / ST_BYTES) : 0;
     return n > PK_MAX_STAGES ? PK_MAX_STAGES : n;
   };
@@ -1171,7 +1196,7 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.xs_bytes = (int)xs;
   a.att_off = (int)att_off;
   a.keep_off = (int)keep_off;
-  const size_t fixed = xs + 128 + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * PK_MAX_STAGES * 8;
+  const size_t fixed = xs + 128 + ST_ALIGN + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * PK_MAX_STAGES * 8;
   a.nstages = nst;
   const size_t smem = fixed + (size_t)nst * ST_BYTES;
   cudaStream_t st = (cudaStream_t)stream;

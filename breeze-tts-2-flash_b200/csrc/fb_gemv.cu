@@ -14,6 +14,10 @@
 // two CTAs fit on an SM (<= ~112 KB each), letting the next kernel's CTAs co-reside and prefetch.
 #include "fb_gemv_core.cuh"
 
+#ifndef FB_GEMV_NARROW_MIN
+#define FB_GEMV_NARROW_MIN 4
+#endif
+
 namespace fb {
 
 constexpr int GV_CWARPS = 8;
@@ -22,7 +26,8 @@ constexpr int GV_STAGE_BYTES = 32768;
 constexpr int GV_MAX_STAGES = 12;
 constexpr int GV_SMEM_BUDGET = 112 * 1024;
 
-// Fallback for K % 8 == 0 but K % 16 != 0 (no whole mma k-steps): scalar FMA from shared memory.
+// Fallback for K % 8 == 0 but K % 64 != 0 (the tensor path's column blocks are 64 wide): scalar FMA from shared
+// memory.
 // A stage holds RS consecutive output rows (x NMAT matrices) in full (all K columns), copied as contiguous runs:
 // one bulk copy per matrix and segment (<= 3 per stage), each up to 32 KB.  Warps take rows round-robin; when a
 // stage has fewer rows than warps, 2 or 4 warps split each row's K range and combine their partial sums through
@@ -302,13 +307,16 @@ int launch_gemv_t(GemvArgs& a, cudaStream_t st) {
 template <int EPI, bool NORM>
 int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
   a.M = M;
-  if (a.K % 16 == 0) {
-    // x staged whole with 64 KB stages; else whole with 32 KB stages (three or more); else (no norm) x in
-    // double-buffered column chunks, 64 KB stages then 32 KB stages
-    int rc = launch_mma_t<EPI, NORM>(a, st, 0);
-    if (rc == FB_ERR_UNSUPPORTED) rc = gemv_mma_narrow(a, EPI, NORM, st, 0);
-    if (rc == FB_ERR_UNSUPPORTED && !NORM) rc = launch_mma_t<EPI, NORM>(a, st, 1);
-    if (rc == FB_ERR_UNSUPPORTED && !NORM) rc = gemv_mma_narrow(a, EPI, NORM, st, 1);
+  if (a.K % 64 == 0) {
+    // x staged whole: 64 KB stages if three fit, else 32 KB stages if four fit (bytes in flight per SM set the
+    // streaming rate of a small grid), else whichever fits; else (no norm) x in double-buffered column chunks,
+    // 64 KB stages then 32 KB stages
+    int rc = launch_mma_t<EPI, NORM>(a, st, 0, 3);
+    if (rc == FB_ERR_UNSUPPORTED) rc = gemv_mma_narrow(a, EPI, NORM, st, 0, FB_GEMV_NARROW_MIN);
+    if (rc == FB_ERR_UNSUPPORTED) rc = launch_mma_t<EPI, NORM>(a, st, 0, 2);
+    if (rc == FB_ERR_UNSUPPORTED) rc = gemv_mma_narrow(a, EPI, NORM, st, 0, 2);
+    if (rc == FB_ERR_UNSUPPORTED && !NORM) rc = launch_mma_t<EPI, NORM>(a, st, 1, 2);
+    if (rc == FB_ERR_UNSUPPORTED && !NORM) rc = gemv_mma_narrow(a, EPI, NORM, st, 1, 2);
     return rc;
   }
   switch (M) {
@@ -317,7 +325,7 @@ int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
     case 3: return launch_gemv_t<3, EPI, NORM>(a, st);
     case 4: return launch_gemv_t<4, EPI, NORM>(a, st);
     case 8: return launch_gemv_t<8, EPI, NORM>(a, st);
-    default: fbh::set_msg("gemv: M=%d rows not built for K %% 16 != 0 (1, 2, 3, 4, 8)", M); return FB_ERR_UNSUPPORTED;
+    default: fbh::set_msg("gemv: M=%d rows not built for K %% 64 != 0 (1, 2, 3, 4, 8)", M); return FB_ERR_UNSUPPORTED;
   }
 }
 
@@ -332,7 +340,7 @@ int common_checks(const void* x, int64_t ldx, int M, int K, const void* y, int64
 
 int setup_ring(GemvArgs& a, int M, int nmat) {
   a.err = fbh::device_err_ptr();
-  if (a.K % 16 == 0) return FB_OK;  // tensor-core path: its ring is sized at launch
+  if (a.K % 64 == 0) return FB_OK;  // tensor-core path: its ring is sized at launch
   const int row_bytes = nmat * a.K * 2;
   if (row_bytes > GV_STAGE_BYTES) {
     fbh::set_msg("gemv: K=%d too large for one stage (max %d)", a.K, GV_STAGE_BYTES / (2 * nmat));
@@ -364,6 +372,15 @@ extern "C" int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const v
   FB_CHECK_ARG(N1 >= 0 && N2 >= 0 && (N1 == 0 || (W1 && al16(W1))) && (N2 == 0 || (W2 && al16(W2))),
                "gemv_seg: bad W1/W2 segment");
   FB_CHECK_ARG(!nw || al16(nw), "gemv_seg: norm weight misaligned");
+  if (K % 64 == 0 && ((N1 && N0 % 8) || (N2 && (N0 + N1) % 8))) {
+    // the tensor path's 8-row copies need segment boundaries at multiples of 8: one launch per segment instead
+    bf16* yb = (bf16*)y;
+    rc = flashb_gemv_seg(x, ldx, M, K, nw, eps, W0, N0, nullptr, 0, nullptr, 0, yb, ldy, stream);
+    if (!rc && N1) rc = flashb_gemv_seg(x, ldx, M, K, nw, eps, W1, N1, nullptr, 0, nullptr, 0, yb + N0, ldy, stream);
+    if (!rc && N2)
+      rc = flashb_gemv_seg(x, ldx, M, K, nw, eps, W2, N2, nullptr, 0, nullptr, 0, yb + N0 + N1, ldy, stream);
+    return rc;
+  }
   GemvArgs a{};
   a.x = (const bf16*)x; a.ldx = (long)ldx; a.nw = (const bf16*)nw; a.eps = eps;
   a.W0 = (const bf16*)W0; a.W1 = N1 ? (const bf16*)W1 : a.W0; a.W2 = N2 ? (const bf16*)W2 : a.W0;

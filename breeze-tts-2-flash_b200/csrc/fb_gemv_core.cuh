@@ -1,15 +1,18 @@
 // flashb: the tensor-core GEMV kernel (see fb_gemv.cu for the semantics), shared by two translation units that
 // build it for two stage widths: fb_gemv.cu (FB_ST_KC = 2048, 64 KB stages) and fb_gemv_narrow.cu (1024, 32 KB
-// stages, used when the activation rows leave no room for two 64 KB stages).  The kernel and its launcher live in
-// the stage-width inline namespace of fb_stream.cuh; the argument block and the row helpers do not depend on it.
+// stages, used when the activation rows leave no room for two 64 KB stages).  Both use TMA stages (FB_ST_TMA 1):
+// the weight matrices reach the kernel as tensor maps inside the argument block.  The kernel and its launcher live
+// in the stage inline namespace of fb_stream.cuh; the argument block and the row helpers do not depend on it.
 #pragma once
+#define FB_ST_TMA 1
 #include "fb_stream.cuh"
 
 namespace fb {
 
 #ifndef FB_GEMV_ARGS_DEFINED
 #define FB_GEMV_ARGS_DEFINED
-struct GemvArgs {
+struct alignas(64) GemvArgs {
+  CUtensorMap tm[3];   // W0, W1, W2 as [K / 64][rows][64] bf16, 8-row boxes of ST_KC columns (tensor path)
   const bf16* x;
   long ldx;
   const bf16* nw;
@@ -52,21 +55,29 @@ __device__ __forceinline__ int gv_seg_end(const GemvArgs& a, int n) {
 #endif
 
 // Launches the 32 KB-stage build (fb_gemv_narrow.cu); epi / norm select the instantiation, xchunk the staging.
-int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st, int xchunk);
+int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st, int xchunk, int min_nst);
 
-inline namespace FB_ST_NS_CAT(kc, FB_ST_KC) {
+inline namespace FB_ST_NS {
 
-// Tensor-core path (K % 16 == 0): a producer warp streams stages of 16 weight rows x ST_KC columns with 1-D bulk
-// copies into a ring of mbarrier-tracked slots; 8 consumer warps run mma.sync m16n8k16 on them (fb_stream.cuh).
-// NMAT = 2 (gate/up): rows 0..7 of a stage are gate rows of 8 output units, rows 8..15 the matching up rows, so a
-// unit's gate and up sums land in the same reduction slots.
+// Tensor-core path (K % 64 == 0): a producer warp streams stages of 16 weight rows x ST_KC columns, two 8-row TMA
+// tensor copies each, into a ring of mbarrier-tracked slots; 8 consumer warps run mma.sync m16n8k16 on them
+// (fb_stream.cuh).  NMAT = 2 (gate/up): rows 0..7 of a stage are gate rows of 8 output units, rows 8..15 the
+// matching up rows, so a unit's gate and up sums land in the same reduction slots.  A CTA's output rows start at a
+// multiple of 8, so no 8-row copy straddles a segment boundary (the host keeps those multiples of 8).
 constexpr int GM_MAX_STAGES = 6;
 constexpr int GM_THREADS = (ST_CWARPS + 1) * 32;
+
+// Tensor map and first row of output rows n .. n + 7 (n a multiple of 8; segment boundaries are multiples of 8).
+__device__ __forceinline__ TmaRows gv_tma_rows(const GemvArgs& a, int n) {
+  if (n < a.N0) return TmaRows{&a.tm[0], n};
+  if (n < a.N0 + a.N1) return TmaRows{&a.tm[1], n - a.N0};
+  return TmaRows{&a.tm[2], n - a.N0 - a.N1};
+}
 
 // NT tiles of 8 activation rows (M <= 8 NT).  a.xchunk: x does not fit whole, so it is staged per column chunk
 // (ST_KC columns, double-buffered, the next chunk in flight while this one is multiplied); only without NORM.
 template <int EPI, bool NORM, int NT>
-__global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const __grid_constant__ GemvArgs a) {
   constexpr int NMAT = EPI == 2 ? 2 : 1;
   constexpr int UG = ST_ROWS / NMAT;  // output units per row group
   constexpr int MS = 8 * NT;          // activation-row slots per reduced output row
@@ -75,7 +86,8 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
   const int x_pitch = a.xchunk ? ST_KC * 2 + 16 : K * 2 + 16;
   unsigned char* xs = smem;
   unsigned char* zero16 = smem + a.xs_bytes;
-  unsigned char* ring = zero16 + 128;
+  unsigned char* ring = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(zero16 + 128) + (ST_ALIGN - 1)) & ~uintptr_t(ST_ALIGN - 1));
   float* red = reinterpret_cast<float*>(ring + (size_t)NST * ST_BYTES);
   float* sums = red + ST_CWARPS * 128 * NT;
   uint64_t* full = reinterpret_cast<uint64_t*>(sums + 128 * NT);
@@ -84,7 +96,9 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, bid = blockIdx.x;
-  const int u0 = (int)((long long)a.N * bid / G), u1 = (int)((long long)a.N * (bid + 1) / G);
+  const int n8 = (a.N + 7) >> 3;
+  const int u0 = min(a.N, 8 * (int)((long long)n8 * bid / G));
+  const int u1 = min(a.N, 8 * (int)((long long)n8 * (bid + 1) / G));
   const int ngroups = (u1 - u0 + UG - 1) / UG;
   const int nkc = (K + ST_KC - 1) / ST_KC;
   const int T = ngroups * nkc;
@@ -108,15 +122,18 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
       const int g = t / nkc, kc = t % nkc;
       const int n0 = u0 + g * UG;
       const int nu = min(UG, u1 - n0);
-      const int k0 = kc * ST_KC;
-      const int kw = min(ST_KC, K - k0);
-      unsigned char* st = ring + (size_t)s * ST_BYTES;
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], (unsigned)(nu * NMAT * kw * 2));
-      __syncwarp();
-      if (lane < ST_ROWS) {
-        const int i = lane % UG, mat = lane / UG;
-        if (i < nu) bulk_g2s(st + lane * ST_PITCH, gv_row<EPI>(a, n0 + i, mat) + k0, (unsigned)(kw * 2), &full[s]);
+      if (lane == 0) {
+        TmaRows lo, hi;
+        if (EPI == 2) {
+          lo = TmaRows{&a.tm[0], n0};
+          hi = TmaRows{&a.tm[1], n0};
+        } else {
+          lo = gv_tma_rows(a, n0);
+          hi = nu > 8 ? gv_tma_rows(a, n0 + 8) : TmaRows{nullptr, 0};
+        }
+        tma_stage(ring + (size_t)s * ST_BYTES, lo, hi, kc, &full[s]);
       }
+      __syncwarp();
       ++issued;
     }
     for (int t = max(0, issued - NST); t < issued; ++t)
@@ -247,23 +264,32 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const GemvArgs a) 
 // Ring depth and launch for this stage width: x whole (xchunk = 0) or in double-buffered column chunks (1, only
 // without NORM).  Returns FB_ERR_UNSUPPORTED when fewer than two ring stages fit.
 template <int EPI, bool NORM, int NT>
-inline int launch_mma_nt(GemvArgs& a, cudaStream_t st, int xchunk) {
+inline int launch_mma_nt(GemvArgs& a, cudaStream_t st, int xchunk, int min_nst) {
   auto kern = gemv_mma_kernel<EPI, NORM, NT>;
   a.xchunk = xchunk;
   a.xs_bytes = xchunk ? ((2 * a.M * (ST_KC * 2 + 16)) + 127) / 128 * 128 : ((a.M * (a.K * 2 + 16)) + 127) / 128 * 128;
-  const size_t fixed = (size_t)a.xs_bytes + 128 + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * GM_MAX_STAGES * 8;
+  const size_t fixed = (size_t)a.xs_bytes + 128 + ST_ALIGN + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT +
+                       2 * GM_MAX_STAGES * 8;
 #ifndef FB_GM_BUDGET
 #define FB_GM_BUDGET 220000
 #endif
   int nst = fixed < FB_GM_BUDGET ? (int)((FB_GM_BUDGET - fixed) / ST_BYTES) : 0;
   if (nst < 3 && fixed < 210 * 1024) nst = (int)((210 * 1024 - fixed) / ST_BYTES);
   if (nst > GM_MAX_STAGES) nst = GM_MAX_STAGES;
-  if (nst < 2) {
-    fbh::set_msg("gemv: M*K = %d activations do not fit the shared-memory budget", a.M * a.K);
+  if (nst < min_nst) {
+    fbh::set_msg("gemv: M*K = %d activations leave fewer than %d ring stages", a.M * a.K, min_nst);
     return FB_ERR_UNSUPPORTED;
   }
   a.nstages = nst;
   const size_t smem = fixed + (size_t)nst * ST_BYTES;
+  // tensor maps of the weight matrices (EPI 2: gate, up; else the q|k|v-style segments)
+  const int nseg[3] = {EPI == 2 ? a.N : a.N0, EPI == 2 ? a.N : a.N1, EPI == 2 ? 0 : a.N - a.N0 - a.N1};
+  const bf16* wseg[3] = {a.W0, a.W1, a.W2};
+  for (int i = 0; i < 3; ++i) {
+    if (nseg[i] <= 0) continue;
+    const int rc = fbh::tmap_rows(&a.tm[i], wseg[i], nseg[i], a.K, ST_KC);
+    if (rc != FB_OK) return rc;
+  }
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -282,13 +308,13 @@ inline int launch_mma_nt(GemvArgs& a, cudaStream_t st, int xchunk) {
 
 // This build's launch for M <= 16 rows: one or two activation tiles, x whole or chunked.
 template <int EPI, bool NORM>
-inline int launch_mma_t(GemvArgs& a, cudaStream_t st, int xchunk = 0) {
+inline int launch_mma_t(GemvArgs& a, cudaStream_t st, int xchunk = 0, int min_nst = 2) {
   if (xchunk && NORM) {
     fbh::set_msg("gemv: chunked activations need the norm-free kernel");
     return FB_ERR_UNSUPPORTED;
   }
-  if (a.M <= 8) return launch_mma_nt<EPI, NORM, 1>(a, st, xchunk);
-  return launch_mma_nt<EPI, NORM, 2>(a, st, xchunk);
+  if (a.M <= 8) return launch_mma_nt<EPI, NORM, 1>(a, st, xchunk, min_nst);
+  return launch_mma_nt<EPI, NORM, 2>(a, st, xchunk, min_nst);
 }
 
 }  // inline namespace

@@ -14,7 +14,7 @@
 #endif
 
 namespace fb {
-inline namespace FB_ST_NS_CAT(kc, FB_ST_KC) {
+inline namespace FB_ST_NS {
 
 constexpr int PK_MAX_STAGES = FB_PK_MAX_STAGES;
 constexpr int PK_CONSUMERS = ST_CWARPS * 32;        // 256
@@ -103,12 +103,20 @@ struct Ring {
 
 // A streamed GEMV task: `units` output units over K columns; NMAT = 2 pairs each unit with a second weight row
 // (gate/up, or the two rotary halves of a q/k head dimension).  Row pointers come from a functor row(n, mat).
-// CTA c owns units [units * c / G, units * (c + 1) / G).
+// CTA c owns units [units * c / G, units * (c + 1) / G); with TMA stages the split is in blocks of 8 units, so
+// every 8-row tensor copy starts at a multiple of 8 and never straddles a segment or head boundary that is one.
 __device__ __forceinline__ void task_range(int units, int& u0, int& u1) {
+#if FB_ST_TMA
+  const int n8 = (units + 7) >> 3;
+  u0 = min(units, 8 * (int)((long long)n8 * blockIdx.x / gridDim.x));
+  u1 = min(units, 8 * (int)((long long)n8 * (blockIdx.x + 1) / gridDim.x));
+#else
   u0 = (int)((long long)units * blockIdx.x / gridDim.x);
   u1 = (int)((long long)units * (blockIdx.x + 1) / gridDim.x);
+#endif
 }
 
+#if !FB_ST_TMA
 // Producer half of one 16-row group: stream its nkc column chunks; `row` is this lane's weight row (lanes < nrows,
 // others pass nullptr).  Returns the new stage counter, or -1 on timeout.  Not inlined (one copy for every task).
 __device__ __noinline__ int produce_group(Ring rg, int t, const bf16* row, int nrows, int K, unsigned* err) {
@@ -144,6 +152,42 @@ __device__ __forceinline__ bool produce_task(Ring& rg, int& t, int units, int K,
   }
   return true;
 }
+
+#endif
+
+#if FB_ST_TMA
+// Producer half of one 16-row group with TMA stages: rows 0..7 from `lo`, rows 8..15 from `hi` (either may be
+// empty), every ST_KC column chunk.  Lane 0 issues; returns the new stage counter, or -1 on timeout.
+__device__ __noinline__ int produce_group_tma(Ring rg, int t, TmaRows lo, TmaRows hi, int K, unsigned* err) {
+  const int lane = threadIdx.x & 31;
+  const int nkc = (K + ST_KC - 1) / ST_KC;
+  for (int kc = 0; kc < nkc; ++kc, ++t) {
+    const int s = t % rg.nst;
+    if (t >= rg.nst && !mbar_wait_warp(&rg.empty[s], ((t / rg.nst) - 1) & 1, err)) return -1;
+    if (lane == 0) tma_stage(rg.base + (size_t)s * ST_BYTES, lo, hi, kc, &rg.full[s]);
+    __syncwarp();
+  }
+  return t;
+}
+
+// Producer half with TMA stages.  src(n, mat) is the tensor map and first row of the 8 rows of units n .. n + 7 of
+// matrix mat (n a multiple of 8).  NMAT = 1: a group is 16 units, rows 0..7 units n0.., rows 8..15 units n0 + 8..;
+// NMAT = 2: a group is 8 units, rows 0..7 from matrix 0, rows 8..15 the same units of matrix 1.
+template <int NMAT, typename SrcFn>
+__device__ __forceinline__ bool produce_task_tma(Ring& rg, int& t, int units, int K, SrcFn src, unsigned* err) {
+  constexpr int UG = ST_ROWS / NMAT;
+  int u0, u1;
+  task_range(units, u0, u1);
+  for (int n0 = u0; n0 < u1; n0 += UG) {
+    const int nu = min(UG, u1 - n0);
+    const TmaRows lo = src(n0, 0);
+    const TmaRows hi = NMAT == 2 ? src(n0, 1) : (nu > 8 ? src(n0 + 8, 0) : TmaRows{nullptr, 0});
+    t = produce_group_tma(rg, t, lo, hi, K, err);
+    if (t < 0) return false;
+  }
+  return true;
+}
+#endif
 
 // L2 prefetch of this CTA's slice of a task (one bulk prefetch per weight row).  Measured on the backbone step it
 // does not pay off (the critical path is latency, not bandwidth), so the step kernels do not call it; kept as a tool.

@@ -71,7 +71,7 @@ class FbDDConfig(ctypes.Structure):
     _fields_ = [('layers', I), ('batch', I), ('hidden', I), ('embed_dim', I), ('heads', I), ('kv_heads', I),
                 ('head_dim', I), ('ffn', I), ('vocab', I), ('codebook_size', I), ('n_decode', I), ('eps', F),
                 ('scaling', F), ('embed', P), ('proj', P), ('normf', P), ('head_t', P), ('cos_tab', P),
-                ('sin_tab', P), ('trace', P), ('grid', I)]
+                ('sin_tab', P), ('trace', P), ('grid', I), ('layers_host', P)]
 
 
 class FbBBLayer(ctypes.Structure):

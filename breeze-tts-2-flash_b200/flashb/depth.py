@@ -38,6 +38,7 @@ class DepthModelDesc:
             recs[i] = _native.FbDDLayer(*[t.data_ptr() for t in (w['ln1'], w['wq'], w['wk'], w['wv'], w['wo'],
                                                                  w['ln2'], w['wg'], w['wu'], w['wd'])])
         self.table = torch.frombuffer(bytearray(bytes(recs)), dtype=torch.uint8).to(device)
+        self._recs = recs                      # host copy of the layer table (tensor maps are built from it)
         c = _native.FbDDConfig()
         c.layers, c.batch, c.hidden, c.embed_dim = len(layers), batch, L0['wq'].shape[1], embed.shape[1]
         c.heads, c.kv_heads, c.head_dim, c.ffn = L0['wq'].shape[0] // 128, L0['wk'].shape[0] // 128, 128, \
@@ -46,6 +47,7 @@ class DepthModelDesc:
         c.eps, c.scaling = float(eps), float(scaling)
         c.embed, c.proj, c.normf, c.head_t = embed.data_ptr(), proj.data_ptr(), normf.data_ptr(), head_t.data_ptr()
         c.cos_tab, c.sin_tab = cos_tab.data_ptr(), sin_tab.data_ptr()
+        c.layers_host = ctypes.addressof(recs)
         self.cfg = c
         self.keep = (layers, embed, proj, normf, head_t, cos_tab, sin_tab)
         n = int(_native.lib().flashb_dd_scratch_bytes(ctypes.byref(c)))

@@ -203,6 +203,8 @@ typedef struct {
   const void* sin_tab;
   uint64_t* trace;     /* optional: [grid][n_decode][11 + 9 * layers] %globaltimer stamps per CTA (task ends, barriers) */
   int grid;            /* CTAs of the launch, one per SM: 0 = every SM; fewer leave SMs to work on other streams */
+  const void* layers_host; /* fb_dd_layer[layers] in host memory, the same pointers as layers_dev: the weight matrices'
+                            * TMA tensor maps are built from it on the host (cached per matrix) */
 } fb_dd_config;
 int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg);
 int64_t flashb_dd_layer_bytes(void);
