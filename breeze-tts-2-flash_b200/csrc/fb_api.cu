@@ -56,16 +56,29 @@ int num_sms() {
 }
 
 int tmap_rows(CUtensorMap* out, const void* base, long long rows, int K, int kc) {
+  if (kc < 64 || kc % 64) {
+    set_msg("tensor map: stage columns %d not a multiple of 64", kc);
+    return FB_ERR_ARG;
+  }
+  return tmap_box(out, base, rows, K, 64, 8, kc / 64, true);
+}
+
+int tmap_box(CUtensorMap* out, const void* base, long long rows, int K, int inner, int box_rows, int box_blocks,
+             bool swizzle128, long long ld) {
   static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
-  static std::map<std::tuple<uintptr_t, long long, int, int>, CUtensorMap> cache;
+  static std::map<std::tuple<uintptr_t, long long, int, int, int, int, int, long long>, CUtensorMap> cache;
   static std::mutex mu;
-  if (!base || rows < 1 || rows > (1ll << 31) || K < 64 || K % 64 || kc < 64 || kc % 64 || kc / 64 > 256 ||
+  if (ld == 0) ld = K;
+  if (!base || rows < 1 || rows > (1ll << 31) || inner < 8 || inner % 8 || K < inner || K % inner || ld < K ||
+      ld % 8 || box_rows < 1 || box_rows > 256 || box_blocks < 1 || box_blocks > 256 || (swizzle128 && inner != 64) ||
       (reinterpret_cast<uintptr_t>(base) & 15)) {
-    set_msg("tensor map: bad matrix (rows %lld, K %d, stage columns %d, base %p)", rows, K, kc, base);
+    set_msg("tensor map: bad matrix (rows %lld, K %d, ld %lld, block %d, box %d x %d, base %p)", rows, K, ld, inner,
+            box_rows, box_blocks, base);
     return FB_ERR_ARG;
   }
   std::lock_guard<std::mutex> lk(mu);
-  const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), rows, K, kc);
+  const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), rows, K, inner, box_rows, box_blocks,
+                                   swizzle128 ? 1 : 0, ld);
   auto it = cache.find(key);
   if (it != cache.end()) {
     *out = it->second;
@@ -82,15 +95,17 @@ int tmap_rows(CUtensorMap* out, const void* base, long long rows, int K, int kc)
   }
   CUtensorMap m;
   std::memset(&m, 0, sizeof(m));
-  const cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(K / 64)};
-  const cuuint64_t strides[2] = {(cuuint64_t)K * 2, 128};   // bytes: next row, next 64-column block
-  const cuuint32_t box[3] = {64, 8, (cuuint32_t)(kc / 64)};
+  const cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)(K / inner)};
+  const cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)inner * 2};   // bytes: next row, next block
+  const cuuint32_t box[3] = {(cuuint32_t)inner, (cuuint32_t)box_rows, (cuuint32_t)box_blocks};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                         CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    set_msg("tensor map: cuTensorMapEncodeTiled failed (%d) for rows %lld, K %d", (int)r, rows, K);
+    set_msg("tensor map: cuTensorMapEncodeTiled failed (%d) for rows %lld, K %d, box %d x %d x %d", (int)r, rows, K,
+            inner, box_rows, box_blocks);
     return FB_ERR_CUDA;
   }
   cache.emplace(key, m);

@@ -158,7 +158,11 @@ int grid_sms();
 // [K / 64 column blocks][rows][64 columns], for 8-row boxes of kc columns with the 128-byte swizzle (fb_stream.cuh
 // TMA stages).  Encoded through the driver's cuTensorMapEncodeTiled (fetched once, no link to libcuda) and cached
 // per (base, rows, K, kc).  Returns FB_OK, or FB_ERR_ARG / FB_ERR_CUDA with the message set.
-int tmap_rows(CUtensorMap* out, const void* base, long long rows, int K, int kc);  // num_sms(), or the calling thread's SM budget when one is set (flashb_set_sm_budget)
+int tmap_rows(CUtensorMap* out, const void* base, long long rows, int K, int kc);
+// General form: [rows, K] bf16 with row stride ld elements (0: K), viewed as [K / inner][rows][inner]; boxes of
+// box_rows rows x box_blocks blocks of `inner` columns, 128-byte swizzle (inner = 64) or none.
+int tmap_box(CUtensorMap* out, const void* base, long long rows, int K, int inner, int box_rows, int box_blocks,
+             bool swizzle128, long long ld = 0);  // num_sms(), or the calling thread's SM budget when one is set (flashb_set_sm_budget)
 }  // namespace fbh
 
 #define FB_CHECK_ARG(cond, ...)          \

@@ -20,6 +20,9 @@
 
 namespace fb {
 
+// Kernel the calling thread's last GEMV launch used: 0 FMA, 1 mma.sync stream, 2 tcgen05 (flashb_gemv_last_path).
+thread_local int t_gemv_path = -1;
+
 constexpr int GV_CWARPS = 8;
 constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;
 constexpr int GV_STAGE_BYTES = 32768;
@@ -308,6 +311,12 @@ template <int EPI, bool NORM>
 int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
   a.M = M;
   if (a.K % 64 == 0) {
+    int rt = gemv_tc(a, EPI, NORM, st);       // tcgen05 kernel (fb_gemv_tc.cu) when the shape suits it
+    if (rt != FB_ERR_UNSUPPORTED) {
+      t_gemv_path = 2;
+      return rt;
+    }
+    t_gemv_path = 1;
     // x staged whole: 64 KB stages if three fit, else 32 KB stages if four fit (bytes in flight per SM set the
     // streaming rate of a small grid), else whichever fits; else (no norm) x in double-buffered column chunks,
     // 64 KB stages then 32 KB stages
@@ -319,6 +328,7 @@ int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
     if (rc == FB_ERR_UNSUPPORTED && !NORM) rc = gemv_mma_narrow(a, EPI, NORM, st, 1, 2);
     return rc;
   }
+  t_gemv_path = 0;
   switch (M) {
     case 1: return launch_gemv_t<1, EPI, NORM>(a, st);
     case 2: return launch_gemv_t<2, EPI, NORM>(a, st);
@@ -390,6 +400,8 @@ extern "C" int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const v
   cudaStream_t st = (cudaStream_t)stream;
   return nw ? dispatch_m<0, true>(a, M, st) : dispatch_m<0, false>(a, M, st);
 }
+
+extern "C" int flashb_gemv_last_path(void) { return t_gemv_path; }
 
 extern "C" int flashb_gemv_resid(const void* x, int64_t ldx, int M, int K, const void* W, int N, const void* res,
                                  int64_t ldr, void* y, int64_t ldy, void* stream) {

@@ -36,6 +36,10 @@ const char* flashb_version(void);
  * kernel whose bounded wait expired.  Synchronises the device.  No reference counterpart (the reference's spin
  * barriers are unbounded, flash/csrc/depth_common.cuh:52-65). */
 int flashb_device_error(int clear);
+/* Which kernel the calling thread's last GEMV call launched: 0 = the scalar-FMA fallback (K % 64 != 0),
+ * 1 = the mma.sync weight stream, 2 = the tcgen05 kernel (enough 128-row blocks for the grid); -1 before any.
+ * For tests and profiling; no reference counterpart. */
+int flashb_gemv_last_path(void);
 /* Programmatic dependent launch on (1, default) / off (0) for all later launches of this process. */
 void flashb_set_pdl(int enable);
 /* SM budget of the calling host thread (0, the default: every SM).  Launches issued later by this thread -- directly

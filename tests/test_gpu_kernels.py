@@ -235,3 +235,53 @@ def test_lm_head_cfg(ops, B):
     assert_close(logits.cpu().numpy(), lg_ref, tol=1e-5, what='lm_head')
     cfg_ref = dec.cfg_combine(logits.cpu().numpy(), half, 4.0) if B >= 2 else logits.cpu().numpy()[:1]
     assert np.array_equal(cfg.cpu().numpy(), cfg_ref), 'CFG combine is elementwise: bit-exact given the logits'
+
+
+# ------------------------------------------------------------------------------------------------ tcgen05 GEMV
+def _budget(n):
+    from flashb._native import lib
+    lib().flashb_set_sm_budget(n)
+
+
+def _path():
+    from flashb._native import lib
+    return lib().flashb_gemv_last_path()
+
+
+@pytest.mark.parametrize('kind,M,budget', [('gateup', 16, 18), ('gateup', 2, 18), ('gateup', 5, 64),
+                                           ('qkv', 16, 18), ('qkv', 1, 8), ('o', 16, 18), ('o', 7, 4),
+                                           ('down', 16, 18), ('down', 2, 18), ('odd', 3, 2)])
+def test_gemv_tcgen05_matches_oracle(ops, kind, M, budget):
+    """The tcgen05 kernel (weights as the MMA's 128-row M side, fp32 sums in TMEM) runs when the grid has enough
+    128-row blocks; a small SM budget (a lane of the GPU) selects it for the backbone's shapes."""
+    fx, _ = ops
+    K = {'down': 6144, 'odd': 1024}.get(kind, 2048)
+    x = randn((M, K), 41)
+    nw = randn((K,), 42, 0.1, 1.0)
+    try:
+        _budget(budget)
+        if kind == 'gateup':
+            Wg, Wu = randn((6144, K), 43, 0.02), randn((6144, K), 44, 0.02)
+            y = torch.empty(M, 6144, dtype=torch.bfloat16, device='cuda')
+            fx.gemv_gateup(x, nw, 1e-6, Wg, Wu, y)
+            ref = dec.gemv_gateup(np32(x), np32(nw), 1e-6, np32(Wg), np32(Wu))
+        elif kind == 'qkv':
+            Wq, Wk, Wv = randn((2048, K), 45, 0.02), randn((512, K), 46, 0.02), randn((512, K), 47, 0.02)
+            y = torch.empty(M, 3072, dtype=torch.bfloat16, device='cuda')
+            fx.gemv_seg(x, nw, 1e-6, Wq, Wk, Wv, y)
+            ref = dec.gemv_seg(np32(x), np32(nw), 1e-6, [np32(Wq), np32(Wk), np32(Wv)])
+        else:
+            N = 300 if kind == 'odd' else 2048
+            W = randn((N, K), 48, 0.02)
+            res = randn((M, N), 49)
+            y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+            fx.gemv_resid(x, W, res, y)
+            ref = dec.gemv_resid(np32(x), np32(W), np32(res))
+        torch.cuda.synchronize()
+        path = _path()
+    finally:
+        _budget(0)
+    assert path == 2, f'expected the tcgen05 kernel, got path {path}'
+    assert_close(np32(y), ref, what=f'tcgen05 {kind} M={M}')
+    from flashb._native import device_error
+    assert device_error() == 0
