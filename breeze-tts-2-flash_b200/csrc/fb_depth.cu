@@ -33,12 +33,18 @@
 #include <mutex>
 
 #include "fb_persist.cuh"
+#include "fb_tc.cuh"
 
 namespace fb {
 
 constexpr int DD_MAXB = 16;     // batch rows (eight CFG pairs)
 constexpr int DD_MAXV = 4096;   // sampler vocabulary bound (composite key packs 12 index bits)
 constexpr int DD_MAXL = 8;      // layers (their tensor maps travel in the argument block)
+constexpr int DD_TC_KX = 2048;  // tcgen05 build: activation columns staged at once (larger K runs in passes)
+constexpr int DD_TC_SUMS = 4096;  // tcgen05 build: floats of the accumulator dump (16 groups x 16 rows x 16)
+#ifndef DD_TC_MAX_GRID
+#define DD_TC_MAX_GRID 32         // tcgen05 build on grids of at most this many CTAs
+#endif
 enum { DD_WQ, DD_WK, DD_WV, DD_WO, DD_WG, DD_WU, DD_WD, DD_NMAPS };
 
 struct DDLayer {
@@ -478,7 +484,7 @@ __device__ __noinline__ void dd_attention(const DDArgs& a, int l, int pos, unsig
       ov.y = pack2(o[2], o[3]);
       ov.z = pack2(o[4], o[5]);
       ov.w = pack2(o[6], o[7]);
-      *reinterpret_cast<uint4*>(xs + (size_t)(b0 + bb) * x_pitch + (size_t)(qh * 128 + c * 8) * 2) = ov;
+      *reinterpret_cast<uint4*>(xs + xs_off(b0 + bb, qh * 16 + c, x_pitch)) = ov;
     }
     named_sync(1, PK_CONSUMERS);
   }
@@ -592,14 +598,14 @@ __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const D
   const int H = a.H, kv = H >> 3;
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
-    cp_async16(xs + (size_t)m * x_pitch + j * 16, a.xres + (size_t)m * H + (size_t)j * 8);
+    cp_async16(xs + xs_off(m, j, x_pitch), a.xres + (size_t)m * H + (size_t)j * 8);
     cp_async16(keep + (size_t)m * H + (size_t)j * 8, a.ob + (size_t)m * H + (size_t)j * 8);
   }
   cp_async_commit();
   cp_async_wait<0>();
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
-    uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
+    uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
     uint4* pk = reinterpret_cast<uint4*>(keep + (size_t)m * H + (size_t)j * 8);
     float x[8], o[8];
     cvt8(*px, x);
@@ -629,6 +635,8 @@ __shared__ float g_dd_nred[ST_CWARPS * 16];
 __shared__ int g_dd_int[32];
 __shared__ long long g_dd_tok[DD_MAXB];            // tokens fed to the next step (this CTA's copy)
 __shared__ __align__(16) bf16 g_dd_cs[2][128];     // [cos|sin][dim] of the sub-step's position
+__shared__ uint32_t g_dd_tmem;                     // tcgen05 build: TMEM base of the accumulators
+__shared__ __align__(8) uint64_t g_dd_mbar;        // tcgen05 build: "the MMAs issued so far are complete"
 
 struct DDSm {
   unsigned char* xs;
@@ -637,27 +645,202 @@ struct DDSm {
   float* sums;
   Ring rg;
 };
+// NT = 1 or 2: mma.sync build with NT activation tiles of 8 rows; NT = 0: the tcgen05 build (activations staged in
+// the B-operand layout, 1024-aligned; the reduction area becomes the accumulator dump).
 template <int NT>
 __device__ __forceinline__ DDSm dd_smem(const DDArgs& a) {
   extern __shared__ __align__(128) unsigned char smem[];
   DDSm m;
-  m.xs = smem;
-  m.zero16 = smem + a.xs_bytes;
+  m.xs = NT ? smem
+            : reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
+  m.zero16 = m.xs + a.xs_bytes;
   unsigned char* ringb = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(m.zero16 + 128) + (ST_ALIGN - 1)) & ~uintptr_t(ST_ALIGN - 1));
   m.red = reinterpret_cast<float*>(ringb + (size_t)a.nstages * ST_BYTES);
-  m.sums = m.red + ST_CWARPS * 128 * NT;
+  m.sums = m.red + (NT ? ST_CWARPS * 128 * NT : DD_TC_SUMS);
   uint64_t* full = reinterpret_cast<uint64_t*>(m.sums + 128 * NT);
   m.rg = Ring{ringb, full, full + PK_MAX_STAGES, a.nstages};
   return m;
 }
 
-// Consumer cursor: ring stage counter, grid-barrier epoch, ok (0 once a bounded wait gave up).
+// Consumer cursor: ring stage counter, grid-barrier epoch, ok (0 once a bounded wait gave up), tcgen05 build: phase
+// of g_dd_mbar.
 struct DDCur {
   int t;
   unsigned epoch;
   int ok;
+  unsigned tph;
 };
+
+// ------------------------------------------------------------------------------------------------ tcgen05 build
+// A GEMV task on the tensor cores: blocks of 128 weight rows (the MMA's M) against the 16 staged activation rows
+// (N = 16), fp32 sums in TMEM.  KIND 0: 128 consecutive output units per block; KIND 1: 128 units of gate rows and
+// the same units of up rows (two accumulators, 64-column stages); KIND 2: one q / k / v head per block (64 rotary
+// pair units: rows d and d + 64 of the head).  A stage is 32 KB of weights in the canonical K-major 128-byte-swizzle
+// layout, streamed by the producer warp with one (KIND 1: two) TMA tensor copies; CTA c owns blocks
+// [nb c / G, nb (c + 1) / G).
+template <int KIND>
+__device__ __forceinline__ void tc_task_blocks(int units, int& b0, int& b1) {
+  constexpr int UB = KIND == 2 ? 64 : 128;
+  const int nb = (units + UB - 1) / UB;
+  b0 = (int)((long long)nb * blockIdx.x / gridDim.x);
+  b1 = (int)((long long)nb * (blockIdx.x + 1) / gridDim.x);
+}
+
+// Producer half.  src(n0, mat) gives the tensor map and first row of the block starting at unit n0 (mat 1: the up
+// rows of KIND 1).
+template <int KIND, typename SrcFn>
+__device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int K, SrcFn src, unsigned* err) {
+  constexpr int UB = KIND == 2 ? 64 : 128;
+  constexpr int C = KIND == 1 ? 64 : 128;
+  const int lane = threadIdx.x & 31;
+  int b0, b1;
+  tc_task_blocks<KIND>(units, b0, b1);
+  const int nkc = (K + C - 1) / C;
+  for (int bi = b0; bi < b1; ++bi) {
+    const TmaRows w0 = src(bi * UB, 0);
+    const TmaRows w1 = KIND == 1 ? src(bi * UB, 1) : TmaRows{nullptr, 0};
+    for (int kc = 0; kc < nkc; ++kc, ++t) {
+      const int s = t % rg.nst;
+      if (t >= rg.nst && !mbar_wait_warp(&rg.empty[s], ((t / rg.nst) - 1) & 1, err)) return false;
+      if (lane == 0) {
+        unsigned char* st = rg.base + (size_t)s * ST_BYTES;
+        mbar_arrive_expect_tx(&rg.full[s], (unsigned)ST_BYTES);
+        if (KIND == 1) {
+          tma_load_3d(st, w0.map, 0, w0.row, kc, &rg.full[s]);
+          tma_load_3d(st + ST_BYTES / 2, w1.map, 0, w1.row, kc, &rg.full[s]);
+        } else {
+          tma_load_3d(st, w0.map, 0, w0.row, kc * 2, &rg.full[s]);
+        }
+      }
+      __syncwarp();
+    }
+  }
+  return true;
+}
+
+// Consumer half (all 256 consumer threads).  The activations of the first K pass are staged at xs (B-operand
+// layout) by the caller; stage_x(p) restages pass p (K > DD_TC_KX, or a further block).  Consumer warp 0 waits for
+// the stages and its lane 0 issues the MMAs (four independent accumulator chains per matrix, summed in a fixed
+// order) and commits them to the ring's empty barriers and to g_dd_mbar.  Warps 0-3 then copy the accumulators out
+// of TMEM into `dump` as groups of 16 rows x 16 activation rows in the order the mma.sync epilogues read them
+// (KIND 0: 16 units; KIND 1 and 2: rows 0-7 the 8 units' matrix-0 rows, 8-15 their matrix-1 rows), and every thread
+// runs epi(n0, nu, group) per group.  A failed wait in warp 0 still commits (so nobody else waits in vain) and is
+// reported to every thread through shared memory after the next barrier.
+template <int KIND, typename EpiFn, typename StageFn>
+__device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, int K, const unsigned char* xs,
+                                                float* dump, EpiFn epi, StageFn stage_x, unsigned* err) {
+  constexpr int UB = KIND == 2 ? 64 : 128;
+  constexpr int C = KIND == 1 ? 64 : 128;
+  constexpr int NG = KIND == 0 ? 8 : (KIND == 1 ? 16 : 8);    // epilogue groups per block
+  constexpr int GU = KIND == 0 ? 16 : 8;                       // units per group
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int b0, b1;
+  tc_task_blocks<KIND>(units, b0, b1);
+  const int KX = K < DD_TC_KX ? K : DD_TC_KX;
+  const int npass = (K + KX - 1) / KX;
+  const int ncp = KX / C;                                      // stages per pass
+  const uint32_t tmem = g_dd_tmem, xsa = smem_u32(xs);
+  int* abort_flag = &g_dd_int[29];
+  if (threadIdx.x == 0) *abort_flag = 0;
+  fence_proxy_async();                 // the caller's staging writes -> visible to the tensor core
+  named_sync(1, PK_CONSUMERS);
+  for (int bi = b0; bi < b1; ++bi) {
+    for (int p = 0; p < npass; ++p) {
+      if (p > 0 || (bi > b0 && npass > 1)) {
+        stage_x(p);
+        fence_proxy_async();
+        named_sync(1, PK_CONSUMERS);
+      }
+      const int nk = min(ncp, (K - p * KX + C - 1) / C);
+      if (warp == 0) {
+        tc_after();
+        for (int kcp = 0; kcp < nk; ++kcp) {
+          const int t = c.t + kcp, s = t % rg.nst;
+          const bool ok = mbar_wait_warp(&rg.full[s], (t / rg.nst) & 1, err);
+          if (!ok && lane == 0) *abort_flag = 1;
+          if (lane == 0 && ok) {
+            const uint32_t wa = smem_u32(rg.base + (size_t)s * ST_BYTES);
+#pragma unroll
+            for (int j = 0; j < C / 16; ++j) {
+              const int kk = kcp * C + 16 * j;                   // column within the staged pass
+              const uint64_t bd = tc_desc_sw128(xsa + (uint32_t)((kk >> 6) << 11) + (uint32_t)(((kk & 63) >> 4) << 5));
+              if (KIND == 1) {
+                const uint32_t acc = (p > 0 || kcp > 0 || j >= 2) ? 1u : 0u;
+                const uint32_t ch = (uint32_t)((j & 1) * 16);
+                tc_mma16(tmem + ch, tc_desc_sw128(wa + (j & 3) * 32), bd, acc);
+                tc_mma16(tmem + 32 + ch, tc_desc_sw128(wa + ST_BYTES / 2 + (j & 3) * 32), bd, acc);
+              } else {
+                const uint32_t acc = (p > 0 || kcp > 0 || j >= 4) ? 1u : 0u;
+                tc_mma16(tmem + (uint32_t)((j & 3) * 16), tc_desc_sw128(wa + (j >> 2) * (ST_BYTES / 2) + (j & 3) * 32),
+                         bd, acc);
+              }
+            }
+          }
+          if (lane == 0) tc_commit(&rg.empty[s]);
+          __syncwarp();
+        }
+        if (lane == 0) tc_commit(&g_dd_mbar);
+        __syncwarp();
+      }
+      c.t += nk;
+      // the pass's MMAs are complete: the staged activations may be replaced, the accumulators read
+      if (!mbar_wait(&g_dd_mbar, c.tph & 1, err)) *abort_flag = 1;
+      ++c.tph;
+      tc_after();
+    }
+    // accumulators -> dump (warps 0-3, TMEM lane quarter = warp)
+    if (warp < 4) {
+      const int L = warp * 32 + lane;
+      const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
+      float c0[16], c1[16], v[16];
+      tc_ld16(tq, c0);
+      tc_ld16(tq + 16, c1);
+#pragma unroll
+      for (int m = 0; m < 16; ++m) v[m] = c0[m] + c1[m];
+      tc_ld16(tq + 32, c0);
+      tc_ld16(tq + 48, c1);
+      if (KIND == 1) {
+        float* g = dump + (L >> 3) * 256 + (L & 7) * 16;
+        float* u = g + 8 * 16;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+          g[m] = v[m];
+          u[m] = c0[m] + c1[m];
+        }
+      } else {
+        float* d = KIND == 0 ? dump + (L >> 4) * 256 + (L & 15) * 16
+                             : dump + ((L & 63) >> 3) * 256 + ((L >> 6) * 8 + (L & 7)) * 16;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) d[m] = (v[m] + c0[m]) + c1[m];
+      }
+    }
+    tc_before();
+    named_sync(1, PK_CONSUMERS);
+    if (*abort_flag) return false;
+    for (int g = 0; g < NG; ++g) {
+      const int n0 = bi * UB + g * GU;
+      const int nu = min(GU, units - n0);
+      if (nu > 0) epi(n0, nu, dump + g * 256);
+    }
+    named_sync(1, PK_CONSUMERS);       // the dump and the accumulators are reused by the next block
+  }
+  return true;
+}
+
+// One GEMV task of a phase: the mma.sync stream (NT > 0; KIND 1 / 2 -> two matrices per unit) or the tcgen05 path
+// (NT = 0).  x_pitch: the staged activations' row pitch (mma.sync builds).  xg / ldx: activations too large to stage
+// whole (mma.sync, column chunks).  stage_x: restaging of further K passes (tcgen05 build).
+template <int NT, int KIND, typename EpiFn, typename StageFn>
+__device__ __forceinline__ bool dd_gemv(const DDArgs& a, DDSm& m, DDCur& c, int units, int K, int x_pitch, EpiFn epi,
+                                        StageFn stage_x, const bf16* xg = nullptr, long ldx = 0) {
+  if constexpr (NT == 0) {
+    return consume_task_tc<KIND>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err);
+  } else {
+    return consume_task<KIND == 0 ? 1 : 2, NT>(m.rg, c.t, units, K, m.xs, x_pitch, a.B, m.zero16, m.red, m.sums, epi,
+                                                a.err, xg, ldx);
+  }
+}
 
 // Producer warp: every weight slice of the frame, in the consumers' order, through the ring (two 8-row TMA tensor
 // copies per stage; the maps travel in the argument block).
@@ -672,23 +855,45 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
   bool ok = true;
   for (int s = 0; s < NCB && ok; ++s) {
     for (int sub = 0; sub < (s == 0 ? 2 : 1) && ok; ++sub) {
-      ok = ok && produce_task_tma<1>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
+      if constexpr (NT == 0) {
+        ok = ok && produce_task_tc<0>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
+      } else {
+        ok = ok && produce_task_tma<1>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
+      }
       for (int l = 0; l < L && ok; ++l) {
         const CUtensorMap* W = a.tm[l];
-        // unit u = (head hh, rotary pair d): matrix 0 carries row hh * 128 + d, matrix 1 row hh * 128 + 64 + d
-        ok = ok && produce_task_tma<2>(m.rg, t, QKVU, H, [&](int u, int mat) {
-          const int hh = u >> 6, d = (u & 63) + mat * 64;
-          if (hh < NH) return TmaRows{&W[DD_WQ], hh * 128 + d};
-          if (hh < NH + NKV) return TmaRows{&W[DD_WK], (hh - NH) * 128 + d};
-          return TmaRows{&W[DD_WV], (hh - NH - NKV) * 128 + d};
-        }, err);
-        ok = ok && produce_task_tma<1>(m.rg, t, H, NH * 128, [&](int n, int) { return TmaRows{&W[DD_WO], n}; }, err);
-        ok = ok && produce_task_tma<2>(m.rg, t, F, H,
-                                       [&](int n, int mat) { return TmaRows{&W[mat ? DD_WU : DD_WG], n}; }, err);
-        ok = ok && produce_task_tma<1>(m.rg, t, H, F, [&](int n, int) { return TmaRows{&W[DD_WD], n}; }, err);
+        if constexpr (NT == 0) {
+          // one head per block: rows hh * 128 .. + 127 of wq / wk / wv
+          ok = ok && produce_task_tc<2>(m.rg, t, QKVU, H, [&](int u, int) {
+            const int hh = u >> 6;
+            if (hh < NH) return TmaRows{&W[DD_WQ], hh * 128};
+            if (hh < NH + NKV) return TmaRows{&W[DD_WK], (hh - NH) * 128};
+            return TmaRows{&W[DD_WV], (hh - NH - NKV) * 128};
+          }, err);
+          ok = ok && produce_task_tc<0>(m.rg, t, H, NH * 128, [&](int n, int) { return TmaRows{&W[DD_WO], n}; }, err);
+          ok = ok && produce_task_tc<1>(m.rg, t, F, H,
+                                        [&](int n, int mat) { return TmaRows{&W[mat ? DD_WU : DD_WG], n}; }, err);
+          ok = ok && produce_task_tc<0>(m.rg, t, H, F, [&](int n, int) { return TmaRows{&W[DD_WD], n}; }, err);
+        } else {
+          // unit u = (head hh, rotary pair d): matrix 0 carries row hh * 128 + d, matrix 1 row hh * 128 + 64 + d
+          ok = ok && produce_task_tma<2>(m.rg, t, QKVU, H, [&](int u, int mat) {
+            const int hh = u >> 6, d = (u & 63) + mat * 64;
+            if (hh < NH) return TmaRows{&W[DD_WQ], hh * 128 + d};
+            if (hh < NH + NKV) return TmaRows{&W[DD_WK], (hh - NH) * 128 + d};
+            return TmaRows{&W[DD_WV], (hh - NH - NKV) * 128 + d};
+          }, err);
+          ok = ok && produce_task_tma<1>(m.rg, t, H, NH * 128, [&](int n, int) { return TmaRows{&W[DD_WO], n}; }, err);
+          ok = ok && produce_task_tma<2>(m.rg, t, F, H,
+                                         [&](int n, int mat) { return TmaRows{&W[mat ? DD_WU : DD_WG], n}; }, err);
+          ok = ok && produce_task_tma<1>(m.rg, t, H, F, [&](int n, int) { return TmaRows{&W[DD_WD], n}; }, err);
+        }
       }
     }
-    ok = ok && produce_task_tma<1>(m.rg, t, V, H, [&](int n, int) { return TmaRows{&a.tm_head, s * V + n}; }, err);
+    if constexpr (NT == 0) {
+      ok = ok && produce_task_tc<0>(m.rg, t, V, H, [&](int n, int) { return TmaRows{&a.tm_head, s * V + n}; }, err);
+    } else {
+      ok = ok && produce_task_tma<1>(m.rg, t, V, H, [&](int n, int) { return TmaRows{&a.tm_head, s * V + n}; }, err);
+    }
   }
   // never leave with copies in flight into this CTA's shared memory
   for (int u = max(0, t - m.rg.nst); u < t; ++u)
@@ -698,10 +903,10 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
 // E: gather the token embeddings (cp.async, one round trip, with the position's rotary rows) -> projector -> xres
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int sub, int pos) {
-  constexpr int MS = 8 * NT;
+  constexpr int MS = NT ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, AE = a.AE, H = a.H, V = a.V;
-  const int xp_ae = AE * 2 + 16;
+  const int xp_ae = NT ? AE * 2 + 16 : 0;
   bf16* const xres = a.xres;   // locals: stores through them cannot alias the argument block
   DD_STAMP(s, 0);
   const int kv = AE >> 3;
@@ -716,7 +921,7 @@ __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int su
       id = id < 0 ? 0 : (id >= rows ? rows - 1 : id);
       src = a.embed + (size_t)id * AE;
     }
-    cp_async16(m.xs + (size_t)b * xp_ae + j * 16, src + (size_t)j * 8);
+    cp_async16(m.xs + xs_off(b, j, xp_ae), src + (size_t)j * 8);
   }
   if (tid < 32) {    // cos / sin rows of the position, 16 chunks of 16 bytes each
     const int tab = tid >> 4, cc = tid & 15;
@@ -725,13 +930,13 @@ __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int su
   cp_async_commit();
   cp_async_wait<0>();
   named_sync(1, PK_CONSUMERS);
-  if (!consume_task<1, NT>(m.rg, c.t, H, AE, m.xs, xp_ae, M, m.zero16, m.red, m.sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, r = tid - i * M;
-                               xres[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
-                             }
-                           }, a.err)) {
+  if (!dd_gemv<NT, 0>(a, m, c, H, AE, xp_ae,
+                      [&](int n0, int nu, const float* sm) {
+                        if (tid < nu * M) {
+                          const int i = tid / M, r = tid - i * M;
+                          xres[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
+                        }
+                      }, [](int) {})) {
     c.ok = 0;
     return c;
   }
@@ -744,14 +949,15 @@ __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int su
 // S1: RMSNorm + q|k|v (rotary pairs) + RoPE + KV write at `pos`
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_s1(const DDArgs& a, DDCur c, int s, int pos, int l) {
-  constexpr int MS = 8 * NT;
+  constexpr int MS = NT ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, NH = a.NH, NKV = a.NKV, QD = NH * 128;
   const int tb = 3 + 9 * l;
   const int P = a.P;
   bf16 *const qb = a.qb, *const kcache = a.kc, *const vcache = a.vc;
-  load_x(m.xs, H * 2 + 16, a.xres, H, M, H, a.layers[l].ln1, a.eps, g_dd_nred);
-  if (!consume_task<2, NT>(m.rg, c.t, (NH + 2 * NKV) * 64, H, m.xs, H * 2 + 16, M, m.zero16, m.red, m.sums,
+  const int xp = NT ? H * 2 + 16 : 0;
+  load_x(m.xs, xp, a.xres, H, M, H, a.layers[l].ln1, a.eps, g_dd_nred);
+  if (!dd_gemv<NT, 2>(a, m, c, (NH + 2 * NKV) * 64, H, xp,
                            [&](int n0, int nu, const float* sm) {
                              if (tid < nu * M) {
                                const int i = tid / M, b = tid - i * M;
@@ -776,7 +982,7 @@ __device__ __noinline__ DDCur dd_phase_s1(const DDArgs& a, DDCur c, int s, int p
                                  dst[d + 64] = __float2bfloat16_rn(y1);
                                }
                              }
-                           }, a.err)) {
+                           }, [](int) {})) {
     c.ok = 0;
     return c;
   }
@@ -790,10 +996,10 @@ __device__ __noinline__ DDCur dd_phase_s1(const DDArgs& a, DDCur c, int s, int p
 // (batch row, KV head) pair i, writes it over its q slice, and a barrier precedes the o-projection.
 template <int G, int NT>
 __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int pos, int l) {
-  constexpr int MS = 8 * NT;
+  constexpr int MS = NT ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, NKV = a.NKV, QD = a.NH * 128;
-  const int xp_q = QD * 2 + 16;
+  const int xp_q = NT ? QD * 2 + 16 : 0;
   const int tb = 3 + 9 * l;
   bf16* const ob = a.ob;
   if (a.att_split) {
@@ -810,13 +1016,13 @@ __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int p
     dd_attention<G>(a, l, pos, m.xs, xp_q, m.xs + a.att_off);
   }
   DD_STAMP(s, tb + 2);
-  if (!consume_task<1, NT>(m.rg, c.t, H, QD, m.xs, xp_q, M, m.zero16, m.red, m.sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, r = tid - i * M;
-                               ob[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
-                             }
-                           }, a.err)) {
+  if (!dd_gemv<NT, 0>(a, m, c, H, QD, xp_q,
+                      [&](int n0, int nu, const float* sm) {
+                        if (tid < nu * M) {
+                          const int i = tid / M, r = tid - i * M;
+                          ob[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
+                        }
+                      }, [](int) {})) {
     c.ok = 0;
     return c;
   }
@@ -829,22 +1035,23 @@ __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int p
 // S3: RMSNorm(bf16(x + o)) + gate|up + SiLU*up; the un-normalised x_mid rows stay in shared memory for S4
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l) {
-  constexpr int MS = 8 * NT;
+  constexpr int MS = NT ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, F = a.F;
   const int tb = 3 + 9 * l;
   bf16* xkeep = reinterpret_cast<bf16*>(m.xs + a.keep_off);
   bf16* const act = a.act;
-  dd_load_mid(m.xs, H * 2 + 16, a, M, a.layers[l].ln2, g_dd_nred, xkeep);
-  if (!consume_task<2, NT>(m.rg, c.t, F, H, m.xs, H * 2 + 16, M, m.zero16, m.red, m.sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, r = tid - i * M;
-                               const float g = rbf(sm[i * MS + r]);
-                               const float u = rbf(sm[(i + 8) * MS + r]);
-                               act[(size_t)r * F + n0 + i] = __float2bfloat16_rn(rbf(g / (1.0f + expf(-g))) * u);
-                             }
-                           }, a.err)) {
+  const int xp = NT ? H * 2 + 16 : 0;
+  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep);
+  if (!dd_gemv<NT, 1>(a, m, c, F, H, xp,
+                      [&](int n0, int nu, const float* sm) {
+                        if (tid < nu * M) {
+                          const int i = tid / M, r = tid - i * M;
+                          const float g = rbf(sm[i * MS + r]);
+                          const float u = rbf(sm[(i + 8) * MS + r]);
+                          act[(size_t)r * F + n0 + i] = __float2bfloat16_rn(rbf(g / (1.0f + expf(-g))) * u);
+                        }
+                      }, [](int) {})) {
     c.ok = 0;
     return c;
   }
@@ -857,22 +1064,27 @@ __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l
 // S4: down + residual: xres = bf16(x_mid + bf16(d)); act rows too large to stage whole go in column chunks
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l) {
-  constexpr int MS = 8 * NT;
+  constexpr int MS = NT ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, F = a.F;
   const int tb = 3 + 9 * l;
   const bf16* xkeep = reinterpret_cast<const bf16*>(m.xs + a.keep_off);
   bf16* const xres = a.xres;
-  if (!a.d_xchunk) load_x(m.xs, F * 2 + 16, a.act, F, M, F, nullptr, 0.f, g_dd_nred);
-  if (!consume_task<1, NT>(m.rg, c.t, H, F, m.xs, a.d_xchunk ? ST_KC * 2 + 16 : F * 2 + 16, M, m.zero16, m.red,
-                           m.sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, r = tid - i * M, n = n0 + i;
-                               const float xm = b2f(xkeep[(size_t)r * H + n]);
-                               xres[(size_t)r * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * MS + r]));
-                             }
-                           }, a.err, a.d_xchunk ? a.act : nullptr, F)) {
+  // tcgen05 build: act in passes of DD_TC_KX columns; mma.sync: whole, or in column chunks (d_xchunk)
+  auto stage = [&](int p) {
+    const int k0 = p * DD_TC_KX;
+    load_x(m.xs, 0, a.act + k0, F, M, min(DD_TC_KX, F - k0), nullptr, 0.f, g_dd_nred);
+  };
+  if (NT == 0) stage(0);
+  else if (!a.d_xchunk) load_x(m.xs, F * 2 + 16, a.act, F, M, F, nullptr, 0.f, g_dd_nred);
+  if (!dd_gemv<NT, 0>(a, m, c, H, F, a.d_xchunk ? ST_KC * 2 + 16 : F * 2 + 16,
+                      [&](int n0, int nu, const float* sm) {
+                        if (tid < nu * M) {
+                          const int i = tid / M, r = tid - i * M, n = n0 + i;
+                          const float xm = b2f(xkeep[(size_t)r * H + n]);
+                          xres[(size_t)r * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * MS + r]));
+                        }
+                      }, stage, a.d_xchunk ? a.act : nullptr, F)) {
     c.ok = 0;
     return c;
   }
@@ -885,21 +1097,22 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
 // S5: final RMSNorm + codebook head -> fp32 logits
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_s5(const DDArgs& a, DDCur c, int s) {
-  constexpr int MS = 8 * NT;
+  constexpr int MS = NT ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, V = a.V;
   const int te = 3 + 9 * a.L;
   float *const logits = a.logits, *const dbg = a.dbg;
-  load_x(m.xs, H * 2 + 16, a.xres, H, M, H, a.normf, a.eps, g_dd_nred);
-  if (!consume_task<1, NT>(m.rg, c.t, V, H, m.xs, H * 2 + 16, M, m.zero16, m.red, m.sums,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, b = tid - i * M;
-                               const float v = sm[i * MS + b];
-                               logits[(size_t)b * V + n0 + i] = v;
-                               if (dbg) dbg[((size_t)s * M + b) * V + n0 + i] = v;
-                             }
-                           }, a.err)) {
+  const int xp = NT ? H * 2 + 16 : 0;
+  load_x(m.xs, xp, a.xres, H, M, H, a.normf, a.eps, g_dd_nred);
+  if (!dd_gemv<NT, 0>(a, m, c, V, H, xp,
+                      [&](int n0, int nu, const float* sm) {
+                        if (tid < nu * M) {
+                          const int i = tid / M, b = tid - i * M;
+                          const float v = sm[i * MS + b];
+                          logits[(size_t)b * V + n0 + i] = v;
+                          if (dbg) dbg[((size_t)s * M + b) * V + n0 + i] = v;
+                        }
+                      }, [](int) {})) {
     c.ok = 0;
     return c;
   }
@@ -959,42 +1172,47 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
     if (tid == 0) {
       for (int s = 0; s < m.rg.nst; ++s) {
         mbar_init(&m.rg.full[s], 1);
-        mbar_init(&m.rg.empty[s], ST_CWARPS);
+        mbar_init(&m.rg.empty[s], NT ? ST_CWARPS : 1);   // tcgen05 build: released by one tcgen05.commit
       }
+      if (NT == 0) mbar_init(&g_dd_mbar, 1);
       fence_mbar_init();
     }
     if (tid < 32) reinterpret_cast<uint32_t*>(m.zero16)[tid] = 0u;
+    if (NT == 0 && warp == 0) tc_alloc(&g_dd_tmem, 64);   // 4 accumulator chains x 16 columns
   }
+  if (NT == 0) tc_before();
   __syncthreads();
+  if (NT == 0) tc_after();
   if (warp == ST_CWARPS) {
     dd_producer<NT>(a);
     return;
   }
   // Codebook step 0 feeds two tokens (positions 0 and 1); they run as two sub-steps of one token each, which gives
   // the same values (GEMV rows are independent, position 0 does not attend to position 1) with M = B rows always.
-  DDCur c{0, 0u, 1};
-  for (int s = 0; s < a.NCB; ++s) {
-    for (int sub = 0; sub < (s == 0 ? 2 : 1); ++sub) {
+  // A phase that gave up on a bounded wait returns ok = 0 on every consumer thread alike; the loop then ends.
+  DDCur c{0, 0u, 1, 0u};
+  for (int s = 0; s < a.NCB && c.ok; ++s) {
+    for (int sub = 0; sub < (s == 0 ? 2 : 1) && c.ok; ++sub) {
       const int pos = s == 0 ? sub : s + 1;
       c = dd_phase_e<NT>(a, c, s, sub, pos);
-      if (!c.ok) return;
-      for (int l = 0; l < a.L; ++l) {
+      for (int l = 0; l < a.L && c.ok; ++l) {
         c = dd_phase_s1<NT>(a, c, s, pos, l);
-        if (!c.ok) return;
-        c = dd_phase_s2<G, NT>(a, c, s, pos, l);
-        if (!c.ok) return;
-        c = dd_phase_s3<NT>(a, c, s, l);
-        if (!c.ok) return;
-        c = dd_phase_s4<NT>(a, c, s, l);
-        if (!c.ok) return;
+        if (c.ok) c = dd_phase_s2<G, NT>(a, c, s, pos, l);
+        if (c.ok) c = dd_phase_s3<NT>(a, c, s, l);
+        if (c.ok) c = dd_phase_s4<NT>(a, c, s, l);
       }
     }
-    c = dd_phase_s5<NT>(a, c, s);
-    if (!c.ok) return;
-    c = dd_phase_sample(a, c, s);
-    if (!c.ok) return;
+    if (c.ok) c = dd_phase_s5<NT>(a, c, s);
+    if (c.ok) c = dd_phase_sample(a, c, s);
   }
-  grid_exit(a.bar);
+  if (NT == 0) {
+    // every MMA of this CTA has completed (each task waits for its last commit); free the accumulators
+    tc_before();
+    named_sync(1, PK_CONSUMERS);
+    tc_after();
+    if (warp == 0) tc_dealloc(g_dd_tmem, 64);
+  }
+  if (c.ok) grid_exit(a.bar);
 }
 
 }  // namespace fb
@@ -1096,24 +1314,6 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.F = c->ffn; a.V = c->vocab; a.CB = c->codebook_size; a.NCB = c->n_decode; a.P = c->n_decode + 1;
   a.eps = c->eps; a.scaling = c->scaling;
   a.layers = (const DDLayer*)layers_dev;
-  {
-    // tensor maps of every streamed matrix, built from the host copy of the layer table (cached per matrix)
-    const DDLayer* hl = (const DDLayer*)c->layers_host;
-    const int QD = c->heads * 128, KD = c->kv_heads * 128;
-    int rc = fbh::tmap_rows(&a.tm_proj, c->proj, c->hidden, c->embed_dim, ST_KC);
-    if (!rc) rc = fbh::tmap_rows(&a.tm_head, c->head_t, (long long)c->n_decode * c->vocab, c->hidden, ST_KC);
-    for (int l = 0; l < c->layers && !rc; ++l) {
-      const DDLayer& W = hl[l];
-      rc = fbh::tmap_rows(&a.tm[l][DD_WQ], W.wq, QD, c->hidden, ST_KC);
-      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WK], W.wk, KD, c->hidden, ST_KC);
-      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WV], W.wv, KD, c->hidden, ST_KC);
-      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WO], W.wo, c->hidden, QD, ST_KC);
-      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WG], W.wg, c->ffn, c->hidden, ST_KC);
-      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WU], W.wu, c->ffn, c->hidden, ST_KC);
-      if (!rc) rc = fbh::tmap_rows(&a.tm[l][DD_WD], W.wd, c->hidden, c->ffn, ST_KC);
-    }
-    if (rc) return rc;
-  }
   a.embed = (const bf16*)c->embed; a.proj = (const bf16*)c->proj; a.normf = (const bf16*)c->normf;
   a.head_t = (const bf16*)c->head_t; a.cos_tab = (const bf16*)c->cos_tab; a.sin_tab = (const bf16*)c->sin_tab;
   a.first_cb = (const long long*)first_cb; a.bh = (const bf16*)bh; a.tokbuf = (long long*)tokbuf;
@@ -1126,32 +1326,71 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.err = fbh::device_err_ptr();
   a.trace = (unsigned long long*)c->trace;
   const size_t M = (size_t)c->batch;
-  const int NT = c->batch > 8 ? 2 : 1;          // activation tiles of 8 rows
   const int grid = c->grid > 0 ? c->grid : fbh::grid_sms();
   if (grid > fbh::num_sms() || grid < (c->batch >= 2 ? c->batch / 2 : 1)) {
     fbh::set_msg("dd_frame: grid %d outside [%d, %d] (one CTA per SM, one per CFG pair at least)", grid,
                  c->batch >= 2 ? c->batch / 2 : 1, fbh::num_sms());
     return FB_ERR_ARG;
   }
+  // Build: on a small grid (a lane of the GPU) the tcgen05 GEMVs (NT = 0): a CTA streams several 128-row blocks
+  // and the per-CTA rate decides; on a large grid the mma.sync stream with 16-row groups spreads each matrix over
+  // every SM (NT = 1 or 2 activation tiles of 8 rows).
+  const int QD = c->heads * 128, KD = c->kv_heads * 128;
+  const bool tc = grid <= DD_TC_MAX_GRID && c->hidden % 128 == 0 && c->embed_dim % 128 == 0 && c->ffn % 128 == 0;
+  const int NT = tc ? 0 : (c->batch > 8 ? 2 : 1);
+  {
+    // tensor maps of every streamed matrix, built from the host copy of the layer table (cached per matrix):
+    // mma.sync build 8-row boxes of ST_KC columns; tcgen05 build 128-row boxes of 128 columns (gate / up: 64)
+    const DDLayer* hl = (const DDLayer*)c->layers_host;
+    auto map = [&](CUtensorMap* out, const void* base, long long rows, int K, bool half) {
+      return tc ? fbh::tmap_box(out, base, rows, K, 64, 128, half ? 1 : 2, true) : fbh::tmap_rows(out, base, rows, K, ST_KC);
+    };
+    int rc = map(&a.tm_proj, c->proj, c->hidden, c->embed_dim, false);
+    if (!rc) rc = map(&a.tm_head, c->head_t, (long long)c->n_decode * c->vocab, c->hidden, false);
+    for (int l = 0; l < c->layers && !rc; ++l) {
+      const DDLayer& W = hl[l];
+      rc = map(&a.tm[l][DD_WQ], W.wq, QD, c->hidden, false);
+      if (!rc) rc = map(&a.tm[l][DD_WK], W.wk, KD, c->hidden, false);
+      if (!rc) rc = map(&a.tm[l][DD_WV], W.wv, KD, c->hidden, false);
+      if (!rc) rc = map(&a.tm[l][DD_WO], W.wo, c->hidden, QD, false);
+      if (!rc) rc = map(&a.tm[l][DD_WG], W.wg, c->ffn, c->hidden, true);
+      if (!rc) rc = map(&a.tm[l][DD_WU], W.wu, c->ffn, c->hidden, true);
+      if (!rc) rc = map(&a.tm[l][DD_WD], W.wd, c->hidden, c->ffn, false);
+    }
+    if (rc) return rc;
+  }
   // One buffer, several uses, sized for the largest:
   //   GEMV input rows of every phase (E: embed_dim, S1 / S3 / S5: hidden, S2: heads x 128; S4: ffn, whole or as
-  //   two column-chunk buffers when whole rows would leave fewer than 3 ring stages);
+  //   two column-chunk buffers when whole rows would leave fewer than 3 ring stages; the tcgen05 build stages 16
+  //   rows of at most DD_TC_KX columns in the B-operand layout);
   //   x_mid rows kept from S3 to S4 (keep_off, past the S4 input region); attention output rows + staging (att_off);
   //   the sampler's keys.
   const size_t xp_kc = ST_KC * 2 + 16;
-  size_t rows = M * (c->embed_dim * 2 + 16);
-  if (M * (c->hidden * 2 + 16) > rows) rows = M * (c->hidden * 2 + 16);
-  if (M * (c->heads * 128 * 2 + 16) > rows) rows = M * (c->heads * 128 * 2 + 16);
-  const size_t att_off = al256d(M * (c->heads * 128 * 2 + 16));
+  const size_t KXe = (size_t)(c->embed_dim < DD_TC_KX ? c->embed_dim : DD_TC_KX);
+  const size_t KXf = (size_t)(c->ffn < DD_TC_KX ? c->ffn : DD_TC_KX);
+  size_t rows, att_off;
+  if (tc) {
+    rows = 16 * 2 * KXe;
+    if (16 * 2 * (size_t)c->hidden > rows) rows = 16 * 2 * (size_t)c->hidden;
+    if (16 * 2 * (size_t)QD > rows) rows = 16 * 2 * (size_t)QD;
+    att_off = al256d(16 * 2 * (size_t)QD);
+  } else {
+    rows = M * (c->embed_dim * 2 + 16);
+    if (M * (c->hidden * 2 + 16) > rows) rows = M * (c->hidden * 2 + 16);
+    if (M * (QD * 2 + 16) > rows) rows = M * (QD * 2 + 16);
+    att_off = al256d(M * (QD * 2 + 16));
+  }
   const size_t xs_smp = al256d(dd_sampler_bytes(c->vocab));
-  const size_t budget = 227 * 1024 - ST_CWARPS * 16 * 4 - 32 * 4 - DD_MAXB * 8 - 2 * 128 * 2 - 256;
+  const size_t budget = 227 * 1024 - ST_CWARPS * 16 * 4 - 32 * 4 - DD_MAXB * 8 - 2 * 128 * 2 - 256 - 16;
+  const size_t red_bytes = tc ? DD_TC_SUMS * 4 + 1024 : ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT;
+  const size_t slot = ST_BYTES;
   auto stages_for = [&](size_t xsb) {
-    const size_t fixed = xsb + 128 + ST_ALIGN + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * PK_MAX_STAGES * 8;
-    int n = fixed < budget ? (int)((budget - fixed) / ST_BYTES) : 0;
+    const size_t fixed = xsb + 128 + ST_ALIGN + red_bytes + 2 * PK_MAX_STAGES * 8;
+    int n = fixed < budget ? (int)((budget - fixed) / slot) : 0;
     return n > PK_MAX_STAGES ? PK_MAX_STAGES : n;
   };
   auto layout = [&](int d_chunk, size_t& keep_off, size_t& base) {
-    const size_t d_region = d_chunk ? 2 * M * xp_kc : M * (c->ffn * 2 + 16);
+    const size_t d_region = tc ? 16 * 2 * KXf : (d_chunk ? 2 * M * xp_kc : M * (c->ffn * 2 + 16));
     keep_off = al256d(d_region > rows ? d_region : rows);
     base = al256d(keep_off + M * c->hidden * 2);
     if (al256d(rows) > base) base = al256d(rows);
@@ -1160,7 +1399,7 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   size_t keep_off = 0, base = 0;
   a.d_xchunk = 0;
   layout(0, keep_off, base);
-  if (stages_for(base) < 3) {
+  if (!tc && stages_for(base) < 3) {
     a.d_xchunk = 1;
     layout(1, keep_off, base);
   }
@@ -1173,44 +1412,50 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   int nst = stages_for(xs);
   a.att_bc = c->batch;
   a.att_split = 0;
-  if (nst < 4) {
+  // ring depth wanted / acceptable, in slots (tcgen05 slots are half as large)
+  const int want = 4, accept = 3, least = 2;
+  if (nst < want) {
     const int per_cta = (c->batch * c->kv_heads + grid - 1) / grid;
     size_t xs_split = al256d(att_off + per_cta * dd_pair_bytes(G, c->n_decode + 1));
     if (xs_split < base) xs_split = base;
-    if (stages_for(xs_split) >= 3) {
+    if (stages_for(xs_split) >= accept) {
       xs = xs_split;
       nst = stages_for(xs);
       a.att_split = 1;
     }
   }
-  while (nst < 4 && !a.att_split && a.att_bc > 1) {
+  while (nst < want && !a.att_split && a.att_bc > 1) {
     a.att_bc = (a.att_bc + 1) / 2;
     xs = al256d(att_off + dd_attn_bytes(a.att_bc, c->heads, c->kv_heads, c->n_decode + 1));
     if (xs < base) xs = base;
     nst = stages_for(xs);
   }
-  if (nst < 2) {
-    fbh::set_msg("dd_frame: activations too large for two ring stages");
+  if (nst < least) {
+    fbh::set_msg("dd_frame: activations too large for %d ring slots", least);
     return FB_ERR_UNSUPPORTED;
   }
   a.xs_bytes = (int)xs;
   a.att_off = (int)att_off;
   a.keep_off = (int)keep_off;
-  const size_t fixed = xs + 128 + ST_ALIGN + ST_CWARPS * 128 * 4 * NT + 128 * 4 * NT + 2 * PK_MAX_STAGES * 8;
+  const size_t fixed = xs + 128 + ST_ALIGN + red_bytes + 2 * PK_MAX_STAGES * 8;
   a.nstages = nst;
-  const size_t smem = fixed + (size_t)nst * ST_BYTES;
+  const size_t smem = fixed + (size_t)nst * slot;
   cudaStream_t st = (cudaStream_t)stream;
-  const int key = (c->heads / c->kv_heads) * 10 + NT;
+  const int key = G * 10 + NT;
   switch (key) {
+    case 10: return launch_dd<1, 0>(a, smem, grid, st);
     case 11: return launch_dd<1, 1>(a, smem, grid, st);
     case 12: return launch_dd<1, 2>(a, smem, grid, st);
+    case 20: return launch_dd<2, 0>(a, smem, grid, st);
     case 21: return launch_dd<2, 1>(a, smem, grid, st);
     case 22: return launch_dd<2, 2>(a, smem, grid, st);
+    case 40: return launch_dd<4, 0>(a, smem, grid, st);
     case 41: return launch_dd<4, 1>(a, smem, grid, st);
     case 42: return launch_dd<4, 2>(a, smem, grid, st);
+    case 80: return launch_dd<8, 0>(a, smem, grid, st);
     case 81: return launch_dd<8, 1>(a, smem, grid, st);
     case 82: return launch_dd<8, 2>(a, smem, grid, st);
-    default: fbh::set_msg("dd_frame: GQA group %d not built", c->heads / c->kv_heads); return FB_ERR_UNSUPPORTED;
+    default: fbh::set_msg("dd_frame: GQA group %d not built", G); return FB_ERR_UNSUPPORTED;
   }
 }
 

@@ -26,6 +26,7 @@
 // winds down (the producer waits for its own copies, the TMEM is freed).
 #define FB_ST_TMA 1
 #include "fb_gemv_core.cuh"
+#include "fb_tc.cuh"
 
 namespace fb {
 namespace {
@@ -55,41 +56,6 @@ struct alignas(64) TcArgs {
   int nst;
   unsigned* err;
 };
-
-// Shared-memory matrix descriptors (tcgen05): start >> 4 in [0, 14), LBO >> 4 in [16, 30), SBO >> 4 in [32, 46),
-// version 1 in [46, 48), layout type in [61, 64) (0: no swizzle, 2: 128-byte swizzle).
-__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
-}
-// kind::f16 instruction descriptor: D fp32, A and B bf16, both K-major, N = 16, M = 128.
-constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((16u >> 3) << 17) | ((128u >> 4) << 24);
-
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %4, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(TC_IDESC));
-}
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, float (&f)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(r[i]);
-}
 
 // Tensor map and first row of 128 weight rows starting at block row r (EPI 0/1: segments are multiples of 128).
 // Rows past the last row stay with the last segment (an out-of-range box reads zeros), never with an empty one.
@@ -231,17 +197,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           const uint32_t xa = smem_u32(xring + (size_t)s * TC_XBYTES);
 #pragma unroll
           for (int j = 0; j < TC_C / 16; ++j) {
-            const uint64_t bd = tc_desc(xa + (j >> 2) * (16 * 128) + (j & 3) * 32, 16, 1024, 2);
+            const uint64_t bd = tc_desc_sw128(xa + (j >> 2) * (16 * 128) + (j & 3) * 32);
             if (EPI == 2) {
               // gate chains in columns [0, 32), up chains in [32, 64)
               const uint32_t acc = (kc > 0 || j >= 2) ? 1u : 0u;
               const uint32_t ch = (uint32_t)((j & 1) * 16);
-              tc_mma(td + ch, tc_desc(wa + (j & 3) * 32, 16, 1024, 2), bd, acc);
-              tc_mma(td + 32 + ch, tc_desc(wa + TC_BR * 128 + (j & 3) * 32, 16, 1024, 2), bd, acc);
+              tc_mma16(td + ch, tc_desc_sw128(wa + (j & 3) * 32), bd, acc);
+              tc_mma16(td + 32 + ch, tc_desc_sw128(wa + TC_BR * 128 + (j & 3) * 32), bd, acc);
             } else {
               const uint32_t acc = (kc > 0 || j >= NCH) ? 1u : 0u;
-              tc_mma(td + (uint32_t)((j % NCH) * 16),
-                     tc_desc(wa + (j >> 2) * (TC_BR * 128) + (j & 3) * 32, 16, 1024, 2), bd, acc);
+              tc_mma16(td + (uint32_t)((j % NCH) * 16),
+                     tc_desc_sw128(wa + (j >> 2) * (TC_BR * 128) + (j & 3) * 32), bd, acc);
             }
           }
           tc_commit(&empty[s]);

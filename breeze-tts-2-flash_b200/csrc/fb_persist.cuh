@@ -268,6 +268,14 @@ __device__ __forceinline__ bool consume_task(Ring& rg, int& t, int units, int K,
   return true;
 }
 
+// Byte offset of 16-byte unit j (columns 8 j .. 8 j + 7) of staged activation row m.  x_pitch > 0: rows at that
+// pitch.  x_pitch == 0: the tcgen05 B-operand layout (canonical K-major, 128-byte swizzle): 64-column blocks of
+// 16 rows x 128 B, unit j of row m at unit (j % 8) ^ (m % 8) of its 128-byte row.
+__device__ __forceinline__ uint32_t xs_off(int m, int j, int x_pitch) {
+  if (x_pitch) return (uint32_t)(m * x_pitch + j * 16);
+  return (uint32_t)(((j >> 3) << 11) + (m << 7) + (((j & 7) ^ (m & 7)) << 4));
+}
+
 // Per-row RMS factors of M <= 16 staged rows: warp w reduces rows w and w + 8 (each lane's chunks in order, then a
 // butterfly), and rs[m] = 1 / sqrt(mean(x^2) + eps).  Every staged chunk must be visible to every consumer thread.
 __device__ __noinline__ void row_rms(const unsigned char* xs, int x_pitch, int M, int K, float eps, float* rs) {
@@ -277,7 +285,7 @@ __device__ __noinline__ void row_rms(const unsigned char* xs, int x_pitch, int M
     float q = 0.f;
     for (int j = lane; j < kv; j += 32) {
       float f[8];
-      cvt8(*reinterpret_cast<const uint4*>(xs + (size_t)m * x_pitch + j * 16), f);
+      cvt8(*reinterpret_cast<const uint4*>(xs + xs_off(m, j, x_pitch)), f);
 #pragma unroll
       for (int u = 0; u < 8; ++u) q = fmaf(f[u], f[u], q);
     }
@@ -293,7 +301,7 @@ __device__ __forceinline__ void apply_rms(unsigned char* xs, int x_pitch, int M,
   const int kv = K >> 3;
   for (int i = threadIdx.x; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
-    uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
+    uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
     float f[8], w[8];
     cvt8(*px, f);
     cvt8(*reinterpret_cast<const uint4*>(nw + (size_t)j * 8), w);
@@ -315,7 +323,7 @@ __device__ __noinline__ void load_x(unsigned char* xs, int x_pitch, const bf16* 
   const int kv = K >> 3;
   for (int i = threadIdx.x; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
-    cp_async16(xs + (size_t)m * x_pitch + j * 16, x + (size_t)m * ld + (size_t)j * 8);
+    cp_async16(xs + xs_off(m, j, x_pitch), x + (size_t)m * ld + (size_t)j * 8);
   }
   cp_async_commit();
   cp_async_wait<0>();

@@ -89,9 +89,11 @@ def _set(m, p):
     m.guidance_scale.fill_(p['gs'])
 
 
-@pytest.mark.parametrize('B', [1, 2, 4, 8, 16])
-def test_depth_forced_logits_match_oracle(B):
+@pytest.mark.parametrize('B,grid', [(1, 0), (2, 0), (4, 0), (8, 0), (16, 0), (1, 4), (2, 8), (16, 12), (16, 32)])
+def test_depth_forced_logits_match_oracle(B, grid):
+    """grid 0: every SM, the mma.sync build; a grid of at most 32 CTAs (a lane of the GPU) runs the tcgen05 build."""
     m = _model(B=B)
+    m.desc.cfg.grid = grid
     c = m.cfg
     forced = np.random.default_rng(B).integers(0, c.vocab, (c.n_decode, B))
     outtok, logits, _ = _run(m, forced)
@@ -129,7 +131,7 @@ def test_depth_free_running_equals_forced_oracle():
     np.testing.assert_array_equal(tok, outtok[:, -1])
 
 
-@pytest.mark.parametrize('B,grid', [(2, 0), (8, 0), (16, 0), (16, 74), (16, 18), (16, 8)])
+@pytest.mark.parametrize('B,grid', [(2, 0), (8, 0), (16, 0), (16, 74), (16, 18), (16, 8), (2, 18)])
 def test_depth_full_size_forced_and_sampler(B, grid):
     """The synthetic full-size depth decoder (4 layers, hidden 1024, 16 codebooks of 2048).  B = 8 (four CFG pairs)
     runs the distributed attention mode ((row, KV head) pairs spread over the CTAs) and one sampler CTA per pair.  A

@@ -77,7 +77,7 @@ def _oracle_backbone(bb):
                                bb.cfg.eps, bb.cfg.theta)
 
 
-@pytest.mark.parametrize('group,lanes', [(1, 1), (2, 1), (4, 1), (8, 1), (1, 2), (2, 3)])
+@pytest.mark.parametrize('group,lanes', [(1, 1), (2, 1), (4, 1), (8, 1), (1, 2), (2, 3), (2, 6)])
 def test_frame_engine_matches_oracle_and_standalone_depth(group, lanes):
     """group 2: two streams share one slot (rows [c0, c1, u0, u1]); every row must still match the oracle.
     lanes > 1: the slots' frames run on several CUDA streams side by side, each lane sized for part of the SMs."""
