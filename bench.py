@@ -34,9 +34,9 @@ N_STREAMS = 64
 PROMPT = 512
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0)
 # dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch at the bench's default shape (8 streams
-# per launch, B = 16 rows, one lane's grid of 18 CTAs): ncu --set full capture of the full-size depth model, 2,177,250,048
-# B read + 8,066,304 B written (profiles/dd_frame_kernel_depth_frame_8streams_grid18.md).
-DD_TRAFFIC_BYTES = 2185316352
+# per launch, B = 16 rows, one lane's grid of 18 CTAs: the tcgen05 build): ncu --set full capture of the full-size
+# depth model, 2,178,643,968 B read + 8,247,552 B written (profiles/dd_frame_kernel_tcgen05_8streams_grid18.md).
+DD_TRAFFIC_BYTES = 2186891520
 PREFILL_CFG = dict(B=2, NH=16, NKV=4, L=512, D=128, pads=(0, 37))
 
 
@@ -276,7 +276,9 @@ def main():
     if my_streams % a.group:
         raise SystemExit(f'{my_streams} streams per rank do not split into groups of {a.group}')
     LAT_FRAMES = 20
-    lanes = max(1, min(a.lanes, my_streams // a.group)) if a.case in ('frame', 'depth') else 1
+    # frame: at most one lane per slot; the one-part cases keep the requested lanes, so that a single slot can be
+    # timed or profiled at a lane's grid size
+    lanes = max(1, min(a.lanes, my_streams // a.group)) if a.case == 'frame' else max(1, a.lanes)
     eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + LAT_FRAMES + 8, device=dev, seed=0,
                       depth_only=(a.case == 'depth'), group=a.group, single_slot=(a.case == 'frame'),
                       lanes=lanes)
@@ -306,7 +308,7 @@ def main():
         if case != 'backbone':
             eng.step(mark)       # the frame, or the depth part alone (an engine without backbone)
             return
-        # the backbone part alone, on the current stream (one lane)
+        # the backbone part alone, on the current stream (graphs captured with the lane's SM budget)
         for i in range(S):
             mark('bb', i, stream)
             eng.streams[i].graph.replay()

@@ -307,8 +307,8 @@ class FrameEngine:
             raise ValueError('backbone codebooks must be <= 1 + depth codebooks and depth embed_dim == backbone hidden')
         if group not in (1, 2, 4, 8) or n_streams % group:
             raise ValueError('group must be 1, 2, 4 or 8 and divide the number of streams')
-        if lanes < 1 or lanes > max(1, n_streams // group):
-            raise ValueError('lanes must be between 1 and the number of slots')
+        if lanes < 1:
+            raise ValueError('lanes must be at least 1 (more lanes than slots leave some lanes idle)')
         self.bcfg, self.dcfg, self.group = bcfg, dcfg, group
         self.device = dev = torch.device(device)
         self.lanes = lanes
