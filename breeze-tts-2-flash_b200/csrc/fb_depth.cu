@@ -41,7 +41,7 @@ constexpr int DD_MAXB = 16;     // batch rows (eight CFG pairs)
 constexpr int DD_MAXV = 4096;   // sampler vocabulary bound (composite key packs 12 index bits)
 constexpr int DD_MAXL = 8;      // layers (their tensor maps travel in the argument block)
 constexpr int DD_TC_KX = 2048;  // tcgen05 build: activation columns staged at once (larger K runs in passes)
-constexpr int DD_TC_SUMS = 4096;  // tcgen05 build: floats of the accumulator dump (16 groups x 16 rows x 16)
+constexpr int DD_TC_SUMS = 2048;  // tcgen05 build: floats of the accumulator dump (8 groups x 16 rows x 16)
 #ifndef DD_TC_MAX_GRID
 #define DD_TC_MAX_GRID 32         // tcgen05 build on grids of at most this many CTAs
 #endif
@@ -590,36 +590,50 @@ __device__ __noinline__ void dd_attention_pairs(const DDArgs& a, int l, int pos,
   named_sync(1, PK_CONSUMERS);
 }
 
-// x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.  xres and ob arrive with cp.async (one round trip);
-// the un-normalised x_mid rows are also kept in `keep` ([M][H] bf16) for the down projection's residual.
+// x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.  xres arrives with cp.async and ob with L2 loads into
+// registers, all in flight at once (one round trip).  The un-normalised x_mid of columns [k_lo, k_hi) -- the output
+// rows this CTA owns in the down projection -- are kept in `keep` ([M][k_hi - k_lo] bf16) for its residual.
 __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const DDArgs& a, int M, const bf16* nw,
-                                         float* nred, bf16* keep) {
+                                         float* nred, bf16* keep, int k_lo, int k_hi) {
   const int tid = threadIdx.x;
-  const int H = a.H, kv = H >> 3;
+  const int H = a.H, kv = H >> 3, kw = k_hi - k_lo;
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
     cp_async16(xs + xs_off(m, j, x_pitch), a.xres + (size_t)m * H + (size_t)j * 8);
-    cp_async16(keep + (size_t)m * H + (size_t)j * 8, a.ob + (size_t)m * H + (size_t)j * 8);
   }
   cp_async_commit();
-  cp_async_wait<0>();
-  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
-    const int m = i / kv, j = i - m * kv;
-    uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
-    uint4* pk = reinterpret_cast<uint4*>(keep + (size_t)m * H + (size_t)j * 8);
-    float x[8], o[8];
-    cvt8(*px, x);
-    cvt8(*pk, o);
-    float v[8];
+  for (int i0 = tid; i0 < M * kv; i0 += 8 * PK_CONSUMERS) {
+    uint4 ov[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = rbf(x[u] + o[u]);
-    uint4 w;
-    w.x = pack2(v[0], v[1]);
-    w.y = pack2(v[2], v[3]);
-    w.z = pack2(v[4], v[5]);
-    w.w = pack2(v[6], v[7]);
-    *px = w;
-    *pk = w;
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * PK_CONSUMERS;
+      if (i < M * kv) {
+        const int m = i / kv, j = i - m * kv;
+        ov[u] = __ldcg(reinterpret_cast<const uint4*>(a.ob + (size_t)m * H + (size_t)j * 8));
+      }
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * PK_CONSUMERS;
+      if (i < M * kv) {
+        const int m = i / kv, j = i - m * kv;
+        uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
+        float x[8], o[8], v[8];
+        cvt8(*px, x);
+        cvt8(ov[u], o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = rbf(x[q] + o[q]);
+        uint4 w;
+        w.x = pack2(v[0], v[1]);
+        w.y = pack2(v[2], v[3]);
+        w.z = pack2(v[4], v[5]);
+        w.w = pack2(v[6], v[7]);
+        *px = w;
+        const int k = j * 8;
+        if (k >= k_lo && k < k_hi) *reinterpret_cast<uint4*>(keep + (size_t)m * kw + (k - k_lo)) = w;
+      }
+    }
   }
   named_sync(1, PK_CONSUMERS);
   row_rms(xs, x_pitch, M, H, a.eps, nred);
@@ -673,15 +687,20 @@ struct DDCur {
 };
 
 // ------------------------------------------------------------------------------------------------ tcgen05 build
-// A GEMV task on the tensor cores: blocks of 128 weight rows (the MMA's M) against the 16 staged activation rows
-// (N = 16), fp32 sums in TMEM.  KIND 0: 128 consecutive output units per block; KIND 1: 128 units of gate rows and
-// the same units of up rows (two accumulators, 64-column stages); KIND 2: one q / k / v head per block (64 rotary
-// pair units: rows d and d + 64 of the head).  A stage is 32 KB of weights in the canonical K-major 128-byte-swizzle
-// layout, streamed by the producer warp with one (KIND 1: two) TMA tensor copies; CTA c owns blocks
-// [nb c / G, nb (c + 1) / G).
+// A GEMV task on the tensor cores: blocks of weight rows (the MMA's M) against the 16 staged activation rows
+// (N = 16), fp32 sums in TMEM.  KIND 0: 64 consecutive output units per block (M = 64, stages of 64 rows x 256
+// columns); KIND 1: 128 units of gate rows and the same units of up rows (two M = 128 accumulators, stages of
+// 2 x 128 rows x 64 columns); KIND 2: one q / k / v head per block (M = 128, stages of 128 rows x 128 columns: 64
+// rotary pair units, rows d and d + 64 of the head).  64-row blocks spread the 1024-row matrices of the depth
+// model over 16 CTAs instead of 8; the 4096-row gate|up task keeps 128-unit blocks (fewer per-block epilogues).  A stage is 32 KB of weights in the canonical K-major 128-byte-swizzle layout, streamed by
+// the producer warp with one (KIND 1: two) TMA tensor copies; CTA c owns blocks [nb c / G, nb (c + 1) / G).
+template <int KIND>
+constexpr int tc_cols() { return KIND == 0 ? 256 : (KIND == 1 ? 64 : 128); }   // columns per stage
+template <int KIND>
+constexpr int tc_units() { return KIND == 1 ? 128 : 64; }                      // output units per block
 template <int KIND>
 __device__ __forceinline__ void tc_task_blocks(int units, int& b0, int& b1) {
-  constexpr int UB = KIND == 2 ? 64 : 128;
+  constexpr int UB = tc_units<KIND>();
   const int nb = (units + UB - 1) / UB;
   b0 = (int)((long long)nb * blockIdx.x / gridDim.x);
   b1 = (int)((long long)nb * (blockIdx.x + 1) / gridDim.x);
@@ -691,8 +710,8 @@ __device__ __forceinline__ void tc_task_blocks(int units, int& b0, int& b1) {
 // rows of KIND 1).
 template <int KIND, typename SrcFn>
 __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int K, SrcFn src, unsigned* err) {
-  constexpr int UB = KIND == 2 ? 64 : 128;
-  constexpr int C = KIND == 1 ? 64 : 128;
+  constexpr int UB = tc_units<KIND>();
+  constexpr int C = tc_cols<KIND>();
   const int lane = threadIdx.x & 31;
   int b0, b1;
   tc_task_blocks<KIND>(units, b0, b1);
@@ -707,10 +726,12 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
         unsigned char* st = rg.base + (size_t)s * ST_BYTES;
         mbar_arrive_expect_tx(&rg.full[s], (unsigned)ST_BYTES);
         if (KIND == 1) {
-          tma_load_3d(st, w0.map, 0, w0.row, kc, &rg.full[s]);
+          tma_load_3d(st, w0.map, 0, w0.row, kc, &rg.full[s]);                      // [128 rows][128 B]
           tma_load_3d(st + ST_BYTES / 2, w1.map, 0, w1.row, kc, &rg.full[s]);
+        } else if (KIND == 0) {
+          tma_load_3d(st, w0.map, 0, w0.row, kc * 4, &rg.full[s]);                  // [4][64 rows][128 B]
         } else {
-          tma_load_3d(st, w0.map, 0, w0.row, kc * 2, &rg.full[s]);
+          tma_load_3d(st, w0.map, 0, w0.row, kc * 2, &rg.full[s]);                  // [2][128 rows][128 B]
         }
       }
       __syncwarp();
@@ -730,9 +751,8 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
 template <int KIND, typename EpiFn, typename StageFn>
 __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, int K, const unsigned char* xs,
                                                 float* dump, EpiFn epi, StageFn stage_x, unsigned* err) {
-  constexpr int UB = KIND == 2 ? 64 : 128;
-  constexpr int C = KIND == 1 ? 64 : 128;
-  constexpr int NG = KIND == 0 ? 8 : (KIND == 1 ? 16 : 8);    // epilogue groups per block
+  constexpr int UB = tc_units<KIND>();
+  constexpr int C = tc_cols<KIND>();
   constexpr int GU = KIND == 0 ? 16 : 8;                       // units per group
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int b0, b1;
@@ -765,15 +785,19 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
             for (int j = 0; j < C / 16; ++j) {
               const int kk = kcp * C + 16 * j;                   // column within the staged pass
               const uint64_t bd = tc_desc_sw128(xsa + (uint32_t)((kk >> 6) << 11) + (uint32_t)(((kk & 63) >> 4) << 5));
+              const uint32_t ka = (uint32_t)((j >> 2) * (KIND == 2 ? 128 * 128 : 64 * 128) + (j & 3) * 32);
               if (KIND == 1) {
+                // gate: [128 rows][128 B] at 0, up at 16 KB; two chains each
                 const uint32_t acc = (p > 0 || kcp > 0 || j >= 2) ? 1u : 0u;
                 const uint32_t ch = (uint32_t)((j & 1) * 16);
                 tc_mma16(tmem + ch, tc_desc_sw128(wa + (j & 3) * 32), bd, acc);
                 tc_mma16(tmem + 32 + ch, tc_desc_sw128(wa + ST_BYTES / 2 + (j & 3) * 32), bd, acc);
+              } else if (KIND == 0) {
+                const uint32_t acc = (p > 0 || kcp > 0 || j >= 4) ? 1u : 0u;
+                tc_mma16_m64(tmem + (uint32_t)((j & 3) * 16), tc_desc_sw128(wa + ka), bd, acc);
               } else {
                 const uint32_t acc = (p > 0 || kcp > 0 || j >= 4) ? 1u : 0u;
-                tc_mma16(tmem + (uint32_t)((j & 3) * 16), tc_desc_sw128(wa + (j >> 2) * (ST_BYTES / 2) + (j & 3) * 32),
-                         bd, acc);
+                tc_mma16(tmem + (uint32_t)((j & 3) * 16), tc_desc_sw128(wa + ka), bd, acc);
               }
             }
           }
@@ -789,7 +813,10 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
       ++c.tph;
       tc_after();
     }
-    // accumulators -> dump (warps 0-3, TMEM lane quarter = warp)
+    // accumulators -> dump (warps 0-3, TMEM lane quarter = warp) -> epilogues.  KIND 0 (M = 64): block row r sits
+    // in lane (r % 16) of quarter r / 16, so warp q's lanes 0-15 hold rows 16 q ..; KIND 1 and 2 (M = 128): row =
+    // lane of the 128.  KIND 1 goes in two rounds of 64 units (8 groups each) through the 8-group dump.
+    float kg1[16], ku1[16];                                    // KIND 1, warps 2-3: their units for round 2
     if (warp < 4) {
       const int L = warp * 32 + lane;
       const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
@@ -800,32 +827,88 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
       for (int m = 0; m < 16; ++m) v[m] = c0[m] + c1[m];
       tc_ld16(tq + 32, c0);
       tc_ld16(tq + 48, c1);
-      if (KIND == 1) {
-        float* g = dump + (L >> 3) * 256 + (L & 7) * 16;
-        float* u = g + 8 * 16;
-#pragma unroll
-        for (int m = 0; m < 16; ++m) {
-          g[m] = v[m];
-          u[m] = c0[m] + c1[m];
-        }
-      } else {
-        float* d = KIND == 0 ? dump + (L >> 4) * 256 + (L & 15) * 16
-                             : dump + ((L & 63) >> 3) * 256 + ((L >> 6) * 8 + (L & 7)) * 16;
+      if (KIND == 2) {
+        float* d = dump + ((L & 63) >> 3) * 256 + ((L >> 6) * 8 + (L & 7)) * 16;
 #pragma unroll
         for (int m = 0; m < 16; ++m) d[m] = (v[m] + c0[m]) + c1[m];
+      } else if (KIND == 0 && lane < 16) {
+        const int r = warp * 16 + lane;                          // block row (unit)
+        float* d = dump + (r >> 4) * 256 + (r & 15) * 16;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) d[m] = (v[m] + c0[m]) + c1[m];
+      }
+      if (KIND == 1) {
+        // units 0..63 now (warps 0-1), units 64..127 after the first round's epilogues (warps 2-3)
+#pragma unroll
+        for (int m = 0; m < 16; ++m) c0[m] = c0[m] + c1[m];     // up
+        if (warp < 2) {
+          float* g = dump + (L >> 3) * 256 + (L & 7) * 16;
+#pragma unroll
+          for (int m = 0; m < 16; ++m) {
+            g[m] = v[m];
+            g[128 + m] = c0[m];
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < 16; ++m) c1[m] = v[m];                // keep gate for round 2
+        if (warp >= 2) {
+#pragma unroll
+          for (int m = 0; m < 16; ++m) kg1[m] = c1[m], ku1[m] = c0[m];
+        }
       }
     }
     tc_before();
     named_sync(1, PK_CONSUMERS);
     if (*abort_flag) return false;
-    for (int g = 0; g < NG; ++g) {
-      const int n0 = bi * UB + g * GU;
-      const int nu = min(GU, units - n0);
-      if (nu > 0) epi(n0, nu, dump + g * 256);
+    if (KIND == 1) {
+      for (int g = 0; g < 8; ++g) {
+        const int n0 = bi * UB + g * GU;
+        const int nu = min(GU, units - n0);
+        if (nu > 0) epi(n0, nu, dump + g * 256);
+      }
+      named_sync(1, PK_CONSUMERS);
+      if (warp >= 2 && warp < 4) {
+        const int Lr = (warp - 2) * 32 + lane;
+        float* g = dump + (Lr >> 3) * 256 + (Lr & 7) * 16;
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+          g[m] = kg1[m];
+          g[128 + m] = ku1[m];
+        }
+      }
+      named_sync(1, PK_CONSUMERS);
+      for (int g = 0; g < 8; ++g) {
+        const int n0 = bi * UB + 64 + g * GU;
+        const int nu = min(GU, units - n0);
+        if (nu > 0) epi(n0, nu, dump + g * 256);
+      }
+    } else
+    {
+      // KIND 0: 4 groups of 16 units; KIND 1 and 2: 8 groups of 8 units
+      constexpr int NGR = KIND == 0 ? 4 : 8;
+      for (int g = 0; g < NGR; ++g) {
+        const int n0 = bi * UB + g * GU;
+        const int nu = min(GU, units - n0);
+        if (nu > 0) epi(n0, nu, dump + g * 256);
+      }
     }
     named_sync(1, PK_CONSUMERS);       // the dump and the accumulators are reused by the next block
   }
   return true;
+}
+
+// Output rows [k_lo, k_hi) this CTA owns in the down projection (H units): its 128-row blocks (tcgen05 build) or
+// its task range (mma.sync build).  S3 keeps x_mid for exactly these columns; S4 adds them to its outputs.
+template <int NT>
+__device__ __forceinline__ void dd_down_rows(const DDArgs& a, int& k_lo, int& k_hi) {
+  if constexpr (NT == 0) {
+    int b0, b1;
+    tc_task_blocks<0>(a.H, b0, b1);
+    k_lo = min(a.H, b0 * 64);
+    k_hi = min(a.H, b1 * 64);
+  } else {
+    task_range(a.H, k_lo, k_hi);
+  }
 }
 
 // One GEMV task of a phase: the mma.sync stream (NT > 0; KIND 1 / 2 -> two matrices per unit) or the tcgen05 path
@@ -1041,8 +1124,10 @@ __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l
   const int tb = 3 + 9 * l;
   bf16* xkeep = reinterpret_cast<bf16*>(m.xs + a.keep_off);
   bf16* const act = a.act;
+  int k_lo, k_hi;
+  dd_down_rows<NT>(a, k_lo, k_hi);
   const int xp = NT ? H * 2 + 16 : 0;
-  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep);
+  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep, k_lo, k_hi);
   if (!dd_gemv<NT, 1>(a, m, c, F, H, xp,
                       [&](int n0, int nu, const float* sm) {
                         if (tid < nu * M) {
@@ -1070,6 +1155,9 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
   const int tb = 3 + 9 * l;
   const bf16* xkeep = reinterpret_cast<const bf16*>(m.xs + a.keep_off);
   bf16* const xres = a.xres;
+  int k_lo, k_hi;
+  dd_down_rows<NT>(a, k_lo, k_hi);
+  const int kw = k_hi - k_lo;
   // tcgen05 build: act in passes of DD_TC_KX columns; mma.sync: whole, or in column chunks (d_xchunk)
   auto stage = [&](int p) {
     const int k0 = p * DD_TC_KX;
@@ -1081,7 +1169,7 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
                       [&](int n0, int nu, const float* sm) {
                         if (tid < nu * M) {
                           const int i = tid / M, r = tid - i * M, n = n0 + i;
-                          const float xm = b2f(xkeep[(size_t)r * H + n]);
+                          const float xm = b2f(xkeep[(size_t)r * kw + (n - k_lo)]);
                           xres[(size_t)r * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * MS + r]));
                         }
                       }, stage, a.d_xchunk ? a.act : nullptr, F)) {
@@ -1336,26 +1424,29 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   // and the per-CTA rate decides; on a large grid the mma.sync stream with 16-row groups spreads each matrix over
   // every SM (NT = 1 or 2 activation tiles of 8 rows).
   const int QD = c->heads * 128, KD = c->kv_heads * 128;
-  const bool tc = grid <= DD_TC_MAX_GRID && c->hidden % 128 == 0 && c->embed_dim % 128 == 0 && c->ffn % 128 == 0;
+  const bool tc = grid <= DD_TC_MAX_GRID && c->hidden % 256 == 0 && c->embed_dim % 256 == 0 && c->ffn % 256 == 0 &&
+                  QD % 256 == 0;
   const int NT = tc ? 0 : (c->batch > 8 ? 2 : 1);
   {
     // tensor maps of every streamed matrix, built from the host copy of the layer table (cached per matrix):
-    // mma.sync build 8-row boxes of ST_KC columns; tcgen05 build 128-row boxes of 128 columns (gate / up: 64)
+    // mma.sync build: 8-row boxes of ST_KC columns.  tcgen05 build: the stage of the task's kind, 64 rows x 256
+    // columns (plain), 128 x 64 (gate, up), 128 x 128 (q, k, v heads)
     const DDLayer* hl = (const DDLayer*)c->layers_host;
-    auto map = [&](CUtensorMap* out, const void* base, long long rows, int K, bool half) {
-      return tc ? fbh::tmap_box(out, base, rows, K, 64, 128, half ? 1 : 2, true) : fbh::tmap_rows(out, base, rows, K, ST_KC);
+    auto map = [&](CUtensorMap* out, const void* base, long long rows, int K, int kind) {
+      if (!tc) return fbh::tmap_rows(out, base, rows, K, ST_KC);
+      return fbh::tmap_box(out, base, rows, K, 64, kind == 0 ? 64 : 128, kind == 0 ? 4 : (kind == 1 ? 1 : 2), true);
     };
-    int rc = map(&a.tm_proj, c->proj, c->hidden, c->embed_dim, false);
-    if (!rc) rc = map(&a.tm_head, c->head_t, (long long)c->n_decode * c->vocab, c->hidden, false);
+    int rc = map(&a.tm_proj, c->proj, c->hidden, c->embed_dim, 0);
+    if (!rc) rc = map(&a.tm_head, c->head_t, (long long)c->n_decode * c->vocab, c->hidden, 0);
     for (int l = 0; l < c->layers && !rc; ++l) {
       const DDLayer& W = hl[l];
-      rc = map(&a.tm[l][DD_WQ], W.wq, QD, c->hidden, false);
-      if (!rc) rc = map(&a.tm[l][DD_WK], W.wk, KD, c->hidden, false);
-      if (!rc) rc = map(&a.tm[l][DD_WV], W.wv, KD, c->hidden, false);
-      if (!rc) rc = map(&a.tm[l][DD_WO], W.wo, c->hidden, QD, false);
-      if (!rc) rc = map(&a.tm[l][DD_WG], W.wg, c->ffn, c->hidden, true);
-      if (!rc) rc = map(&a.tm[l][DD_WU], W.wu, c->ffn, c->hidden, true);
-      if (!rc) rc = map(&a.tm[l][DD_WD], W.wd, c->hidden, c->ffn, false);
+      rc = map(&a.tm[l][DD_WQ], W.wq, QD, c->hidden, 2);
+      if (!rc) rc = map(&a.tm[l][DD_WK], W.wk, KD, c->hidden, 2);
+      if (!rc) rc = map(&a.tm[l][DD_WV], W.wv, KD, c->hidden, 2);
+      if (!rc) rc = map(&a.tm[l][DD_WO], W.wo, c->hidden, QD, 0);
+      if (!rc) rc = map(&a.tm[l][DD_WG], W.wg, c->ffn, c->hidden, 1);
+      if (!rc) rc = map(&a.tm[l][DD_WU], W.wu, c->ffn, c->hidden, 1);
+      if (!rc) rc = map(&a.tm[l][DD_WD], W.wd, c->hidden, c->ffn, 0);
     }
     if (rc) return rc;
   }
@@ -1389,10 +1480,20 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
     int n = fixed < budget ? (int)((budget - fixed) / slot) : 0;
     return n > PK_MAX_STAGES ? PK_MAX_STAGES : n;
   };
+  // x_mid kept from S3 to S4: only the down projection's output rows this CTA owns
+  size_t keep_rows;
+  if (tc) {
+    const int nb = (c->hidden + 63) / 64;
+    keep_rows = (size_t)((nb + grid - 1) / grid) * 64;
+  } else {
+    const int n8 = (c->hidden + 7) / 8;
+    keep_rows = (size_t)((n8 + grid - 1) / grid) * 8;
+  }
+  if (keep_rows > (size_t)c->hidden) keep_rows = (size_t)c->hidden;
   auto layout = [&](int d_chunk, size_t& keep_off, size_t& base) {
     const size_t d_region = tc ? 16 * 2 * KXf : (d_chunk ? 2 * M * xp_kc : M * (c->ffn * 2 + 16));
     keep_off = al256d(d_region > rows ? d_region : rows);
-    base = al256d(keep_off + M * c->hidden * 2);
+    base = al256d(keep_off + M * keep_rows * 2);
     if (al256d(rows) > base) base = al256d(rows);
     if (xs_smp > base) base = xs_smp;
   };

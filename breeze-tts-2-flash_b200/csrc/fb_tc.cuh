@@ -15,17 +15,24 @@ __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
 __device__ __forceinline__ uint64_t tc_desc_sw128(uint32_t saddr) { return tc_desc(saddr, 16, 1024, 2); }
-// kind::f16 instruction descriptor: D fp32, A and B bf16, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t tc_idesc(uint32_t n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((128u >> 4) << 24);
+// kind::f16 instruction descriptor: D fp32, A and B bf16, both K-major, M = m (64 or 128), N = n.
+__host__ __device__ constexpr uint32_t tc_idesc(uint32_t n, uint32_t m = 128) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
-// D[tmem] (+)= A . B^T, M = 128, N = 16, K = 16 (accumulate != 0 adds to D).
+// D[tmem] (+)= A . B^T, M = 128 (or M = 64 with tc_mma16_m64), N = 16, K = 16 (accumulate != 0 adds to D).
+// M = 64 puts D row r in TMEM lane (r % 16) + 32 (r / 16): the first 16 lanes of each warp's quarter.
 __device__ __forceinline__ void tc_mma16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %4, p;\n\t}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(tc_idesc(16)));
+}
+__device__ __forceinline__ void tc_mma16_m64(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %4, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(tc_idesc(16, 64)));
 }
 // The mbarrier receives one arrival once every MMA issued so far by this thread has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
