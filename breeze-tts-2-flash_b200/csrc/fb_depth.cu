@@ -590,50 +590,36 @@ __device__ __noinline__ void dd_attention_pairs(const DDArgs& a, int l, int pos,
   named_sync(1, PK_CONSUMERS);
 }
 
-// x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.  xres arrives with cp.async and ob with L2 loads into
-// registers, all in flight at once (one round trip).  The un-normalised x_mid of columns [k_lo, k_hi) -- the output
-// rows this CTA owns in the down projection -- are kept in `keep` ([M][k_hi - k_lo] bf16) for its residual.
+// x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.  xres and ob arrive with cp.async (one round trip);
+// the un-normalised x_mid rows are also kept in `keep` ([M][H] bf16) for the down projection's residual.
 __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const DDArgs& a, int M, const bf16* nw,
-                                         float* nred, bf16* keep, int k_lo, int k_hi) {
+                                         float* nred, bf16* keep) {
   const int tid = threadIdx.x;
-  const int H = a.H, kv = H >> 3, kw = k_hi - k_lo;
+  const int H = a.H, kv = H >> 3;
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
     cp_async16(xs + xs_off(m, j, x_pitch), a.xres + (size_t)m * H + (size_t)j * 8);
+    cp_async16(keep + (size_t)m * H + (size_t)j * 8, a.ob + (size_t)m * H + (size_t)j * 8);
   }
   cp_async_commit();
-  for (int i0 = tid; i0 < M * kv; i0 += 8 * PK_CONSUMERS) {
-    uint4 ov[8];
+  cp_async_wait<0>();
+  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
+    const int m = i / kv, j = i - m * kv;
+    uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
+    uint4* pk = reinterpret_cast<uint4*>(keep + (size_t)m * H + (size_t)j * 8);
+    float x[8], o[8];
+    cvt8(*px, x);
+    cvt8(*pk, o);
+    float v[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * PK_CONSUMERS;
-      if (i < M * kv) {
-        const int m = i / kv, j = i - m * kv;
-        ov[u] = __ldcg(reinterpret_cast<const uint4*>(a.ob + (size_t)m * H + (size_t)j * 8));
-      }
-    }
-    cp_async_wait<0>();
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int i = i0 + u * PK_CONSUMERS;
-      if (i < M * kv) {
-        const int m = i / kv, j = i - m * kv;
-        uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
-        float x[8], o[8], v[8];
-        cvt8(*px, x);
-        cvt8(ov[u], o);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) v[q] = rbf(x[q] + o[q]);
-        uint4 w;
-        w.x = pack2(v[0], v[1]);
-        w.y = pack2(v[2], v[3]);
-        w.z = pack2(v[4], v[5]);
-        w.w = pack2(v[6], v[7]);
-        *px = w;
-        const int k = j * 8;
-        if (k >= k_lo && k < k_hi) *reinterpret_cast<uint4*>(keep + (size_t)m * kw + (k - k_lo)) = w;
-      }
-    }
+    for (int u = 0; u < 8; ++u) v[u] = rbf(x[u] + o[u]);
+    uint4 w;
+    w.x = pack2(v[0], v[1]);
+    w.y = pack2(v[2], v[3]);
+    w.z = pack2(v[4], v[5]);
+    w.w = pack2(v[6], v[7]);
+    *px = w;
+    *pk = w;
   }
   named_sync(1, PK_CONSUMERS);
   row_rms(xs, x_pitch, M, H, a.eps, nred);
@@ -897,20 +883,6 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
   return true;
 }
 
-// Output rows [k_lo, k_hi) this CTA owns in the down projection (H units): its 128-row blocks (tcgen05 build) or
-// its task range (mma.sync build).  S3 keeps x_mid for exactly these columns; S4 adds them to its outputs.
-template <int NT>
-__device__ __forceinline__ void dd_down_rows(const DDArgs& a, int& k_lo, int& k_hi) {
-  if constexpr (NT == 0) {
-    int b0, b1;
-    tc_task_blocks<0>(a.H, b0, b1);
-    k_lo = min(a.H, b0 * 64);
-    k_hi = min(a.H, b1 * 64);
-  } else {
-    task_range(a.H, k_lo, k_hi);
-  }
-}
-
 // One GEMV task of a phase: the mma.sync stream (NT > 0; KIND 1 / 2 -> two matrices per unit) or the tcgen05 path
 // (NT = 0).  x_pitch: the staged activations' row pitch (mma.sync builds).  xg / ldx: activations too large to stage
 // whole (mma.sync, column chunks).  stage_x: restaging of further K passes (tcgen05 build).
@@ -934,6 +906,12 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
   const int QKVU = (NH + 2 * NKV) * 64;  // rotary pair units
   const int L = a.L, NCB = a.NCB;
   unsigned* const err = a.err;
+  {
+    // every tensor map of the frame into the descriptor cache first (a miss would stall the first copy of a phase)
+    const int lane = threadIdx.x & 31;
+    for (int i = lane; i < 2 + DD_NMAPS * L; i += 32)
+      tma_prefetch_map(i == 0 ? &a.tm_proj : (i == 1 ? &a.tm_head : &a.tm[(i - 2) / DD_NMAPS][(i - 2) % DD_NMAPS]));
+  }
   int t = 0;
   bool ok = true;
   for (int s = 0; s < NCB && ok; ++s) {
@@ -1124,10 +1102,8 @@ __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l
   const int tb = 3 + 9 * l;
   bf16* xkeep = reinterpret_cast<bf16*>(m.xs + a.keep_off);
   bf16* const act = a.act;
-  int k_lo, k_hi;
-  dd_down_rows<NT>(a, k_lo, k_hi);
   const int xp = NT ? H * 2 + 16 : 0;
-  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep, k_lo, k_hi);
+  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep);
   if (!dd_gemv<NT, 1>(a, m, c, F, H, xp,
                       [&](int n0, int nu, const float* sm) {
                         if (tid < nu * M) {
@@ -1155,9 +1131,6 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
   const int tb = 3 + 9 * l;
   const bf16* xkeep = reinterpret_cast<const bf16*>(m.xs + a.keep_off);
   bf16* const xres = a.xres;
-  int k_lo, k_hi;
-  dd_down_rows<NT>(a, k_lo, k_hi);
-  const int kw = k_hi - k_lo;
   // tcgen05 build: act in passes of DD_TC_KX columns; mma.sync: whole, or in column chunks (d_xchunk)
   auto stage = [&](int p) {
     const int k0 = p * DD_TC_KX;
@@ -1169,7 +1142,7 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
                       [&](int n0, int nu, const float* sm) {
                         if (tid < nu * M) {
                           const int i = tid / M, r = tid - i * M, n = n0 + i;
-                          const float xm = b2f(xkeep[(size_t)r * kw + (n - k_lo)]);
+                          const float xm = b2f(xkeep[(size_t)r * H + n]);
                           xres[(size_t)r * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * MS + r]));
                         }
                       }, stage, a.d_xchunk ? a.act : nullptr, F)) {
@@ -1480,16 +1453,8 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
     int n = fixed < budget ? (int)((budget - fixed) / slot) : 0;
     return n > PK_MAX_STAGES ? PK_MAX_STAGES : n;
   };
-  // x_mid kept from S3 to S4: only the down projection's output rows this CTA owns
-  size_t keep_rows;
-  if (tc) {
-    const int nb = (c->hidden + 63) / 64;
-    keep_rows = (size_t)((nb + grid - 1) / grid) * 64;
-  } else {
-    const int n8 = (c->hidden + 7) / 8;
-    keep_rows = (size_t)((n8 + grid - 1) / grid) * 8;
-  }
-  if (keep_rows > (size_t)c->hidden) keep_rows = (size_t)c->hidden;
+  // x_mid kept from S3 to S4 (its rows also stage ob in S3)
+  const size_t keep_rows = (size_t)c->hidden;
   auto layout = [&](int d_chunk, size_t& keep_off, size_t& base) {
     const size_t d_region = tc ? 16 * 2 * KXf : (d_chunk ? 2 * M * xp_kc : M * (c->ffn * 2 + 16));
     keep_off = al256d(d_region > rows ? d_region : rows);

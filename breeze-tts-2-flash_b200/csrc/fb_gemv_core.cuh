@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const __grid_const
 
   if (warp == ST_CWARPS) {
     // ------------------------------------------------------------ producer: weights only, runs before pdl_wait
+    if (lane < 3) tma_prefetch_map(&a.tm[lane]);
     int issued = 0;
     for (int t = 0; t < T; ++t) {
       const int s = t % NST;

@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       tma_load_3d(xring + (size_t)s * TC_XBYTES, &a.tx, 0, 0, kc * (TC_C / 64), &full[s]);
     };
     constexpr unsigned STAGE_TX = (unsigned)(TC_WBYTES + 16 * TC_C * 2);
+    if (lane < 4) tma_prefetch_map(lane < 3 ? (const void*)&a.tw[lane] : (const void*)&a.tx);
     bool ok = true;
     const int pre = min(T, NST);
     if (lane == 0) {

@@ -289,6 +289,10 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0,
       "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
 }
+// Pull a tensor map into the TMA unit's descriptor cache ahead of its first copy.
+__device__ __forceinline__ void tma_prefetch_map(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
 // Source of 8 stage rows: rows row .. row + 7 of the matrix behind tensor map `map` (nullptr: nothing to load).
 struct TmaRows {
   const void* map;
