@@ -326,8 +326,8 @@ def main():
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
-    for _ in range(a.steps):
-        one_step(evs)
+    for t in range(a.steps):
+        one_step(evs)   # the lanes join at the end of every step (measured faster than lanes running free)
     t_end.record(stream)
     barrier()
     clk = clocks.stop() if clocks else None
@@ -374,29 +374,36 @@ def main():
         G = a.group
         qh = torch.empty(R, dcfg.n_decode, G, dcfg.vocab).exponential_(1, generator=torch.Generator().manual_seed(5))
         qh = qh.pin_memory()
-        toks_h = torch.zeros(S, 2 * G + 2 * G * dcfg.n_decode, dtype=torch.long).pin_memory()
-        done = torch.cuda.Event()
+        toks_h = torch.zeros(2, S, 2 * G + 2 * G * dcfg.n_decode, dtype=torch.long).pin_memory()
         h2d = S * qh[0].numel() * 4
-        d2h = S * toks_h[0].numel() * 8
+        d2h = S * toks_h[0, 0].numel() * 8
+        got = [None] * S            # per slot: the event after its previous frame's token copies
 
         def e2e_step(t):
-            # every slot: its Exp(1) draws in from pinned host memory before the frame, its tokens out after it (on
-            # the slot's lane stream); the host holds every stream's tokens of this step before the next step
+            # every slot: before its frame the host has that slot's previous tokens (its event), then its Exp(1)
+            # draws go in from pinned host memory; after the frame its tokens come out into the other half of a
+            # double-buffered pinned array.  Slots are waited for one by one, so the host issues the next frames
+            # while the GPU still runs this step; the lanes still join on the device at the end of every step.
             def h2d_q(kind, i, s):
                 if kind == 'bb':
+                    if got[i] is not None:
+                        got[i].synchronize()
                     eng.streams[i].q.copy_(qh[(i + t) % R], non_blocking=True)
 
             def d2h_tokens(kind, i, s):
                 st = eng.streams[i]
-                toks_h[i, :2 * G].copy_(st.first_cb, non_blocking=True)
-                toks_h[i, 2 * G:].copy_(st.outtok.view(-1), non_blocking=True)
+                toks_h[t & 1, i, :2 * G].copy_(st.first_cb, non_blocking=True)
+                toks_h[t & 1, i, 2 * G:].copy_(st.outtok.view(-1), non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(s)
+                got[i] = ev
 
             eng.step(h2d_q, d2h_tokens)
-            done.record(stream)
-            done.synchronize()
 
         for t in range(a.warmup):
             e2e_step(t)
+        torch.cuda.synchronize(dev)
+        got = [None] * S
         barrier()
         w0 = torch.cuda.Event(enable_timing=True)
         w1 = torch.cuda.Event(enable_timing=True)
@@ -404,6 +411,9 @@ def main():
         for t in range(a.steps):
             e2e_step(t)
         w1.record(stream)
+        for e in got:
+            if e is not None:
+                e.synchronize()     # the last step's tokens are on the host
         barrier()
         e_ms = maxred(w0.elapsed_time(w1))
         e2e = dict(value=round(frames / (e_ms / 1e3), 3), unit='frames/s', h2d_bytes_per_step=h2d,

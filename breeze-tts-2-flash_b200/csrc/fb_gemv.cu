@@ -310,6 +310,26 @@ int launch_gemv_t(GemvArgs& a, cudaStream_t st) {
 template <int EPI, bool NORM>
 int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
   a.M = M;
+  if (M > 16) {
+    // up to 128 rows: the tcgen05 kernel (MMA N = the rows); else row blocks of 16 through the paths below, each
+    // block streaming the weights again
+    if (a.K % 64 == 0) {
+      const int rt = gemv_tc(a, EPI, NORM, st);
+      if (rt != FB_ERR_UNSUPPORTED) {
+        t_gemv_path = 2;
+        return rt;
+      }
+    }
+    for (int r0 = 0; r0 < M; r0 += 16) {
+      GemvArgs b = a;
+      b.x += (size_t)r0 * a.ldx;
+      b.y += (size_t)r0 * a.ldy;
+      if (b.res) b.res += (size_t)r0 * a.ldr;
+      const int rc = dispatch_m<EPI, NORM>(b, M - r0 < 16 ? M - r0 : 16, st);
+      if (rc) return rc;
+    }
+    return FB_OK;
+  }
   if (a.K % 64 == 0) {
     int rt = gemv_tc(a, EPI, NORM, st);       // tcgen05 kernel (fb_gemv_tc.cu) when the shape suits it
     if (rt != FB_ERR_UNSUPPORTED) {
@@ -341,7 +361,7 @@ int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
 
 int common_checks(const void* x, int64_t ldx, int M, int K, const void* y, int64_t ldy) {
   FB_CHECK_ARG(x && y, "gemv: null x or y");
-  FB_CHECK_ARG(M >= 1 && M <= 16, "gemv: M=%d out of range 1..16", M);
+  FB_CHECK_ARG(M >= 1 && M <= 128, "gemv: M=%d out of range 1..128", M);
   FB_CHECK_ARG(K > 0 && K % 8 == 0, "gemv: K=%d must be a positive multiple of 8", K);
   FB_CHECK_ARG(ldx % 8 == 0 && ldy >= 1 && al16(x), "gemv: x row stride %lld must be a multiple of 8 and x 16B aligned",
                (long long)ldx);
@@ -358,6 +378,7 @@ int setup_ring(GemvArgs& a, int M, int nmat) {
   }
   a.RS = GV_STAGE_BYTES / row_bytes;
   if (a.RS > 16) a.RS = 16;
+  if (M > 16) M = 16;   // more rows go through the tcgen05 kernel or in row blocks of 16
   a.xs_bytes = ((M * a.K * 2) + 127) / 128 * 128;
   int nst = (GV_SMEM_BUDGET - a.xs_bytes) / GV_STAGE_BYTES;
   if (nst < 2) nst = (200 * 1024 - a.xs_bytes) / GV_STAGE_BYTES;
@@ -402,6 +423,10 @@ extern "C" int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const v
 }
 
 extern "C" int flashb_gemv_last_path(void) { return t_gemv_path; }
+
+extern "C" int flashb_gemv_last_split(void) { return t_gemv_path == 2 ? fb::gemv_tc_last_split() : 1; }
+
+extern "C" void flashb_set_gemv_split(int enable) { fb::gemv_tc_set_split_small(enable); }
 
 extern "C" int flashb_gemv_resid(const void* x, int64_t ldx, int M, int K, const void* W, int N, const void* res,
                                  int64_t ldr, void* y, int64_t ldy, void* stream) {

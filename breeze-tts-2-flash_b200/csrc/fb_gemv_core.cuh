@@ -54,8 +54,11 @@ __device__ __forceinline__ int gv_seg_end(const GemvArgs& a, int n) {
 
 #endif
 
-// The tcgen05 GEMV (fb_gemv_tc.cu); FB_ERR_UNSUPPORTED when the shape does not suit it.
+// The tcgen05 GEMV (fb_gemv_tc.cu); FB_ERR_UNSUPPORTED when the shape does not suit it.  gemv_tc_last_split: the
+// CTAs per block (split K) of this thread's last tcgen05 launch.
 int gemv_tc(GemvArgs& a, int epi, bool norm, cudaStream_t st);
+int gemv_tc_last_split();
+void gemv_tc_set_split_small(int on);
 
 // Launches the 32 KB-stage build (fb_gemv_narrow.cu); epi / norm select the instantiation, xchunk the staging.
 int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st, int xchunk, int min_nst);

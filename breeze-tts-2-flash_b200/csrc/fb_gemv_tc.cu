@@ -1,14 +1,15 @@
-// flashb: skinny GEMV on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), for M <= 16 activation
-// rows and K % 64 == 0.  Same semantics as the mma.sync kernel of fb_gemv_core.cuh (see fb_gemv.cu):
+// flashb: skinny GEMV / small GEMM on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), for up to
+// 128 activation rows and K % 64 == 0.  Same semantics as the mma.sync kernel of fb_gemv_core.cuh (see fb_gemv.cu):
 //   y[m, n] = sum_k xin[m, k] W[n, k] (fp32), NORM: xin = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))),
 //   EPI 0: bf16(acc)   EPI 1: bf16(res + bf16(acc))   EPI 2: bf16(bf16(silu(bf16(acc_gate))) * bf16(acc_up)).
 //
-// B200 design.  The GEMV is turned around so that the weights are the MMA's M side: D[128 weight rows x 16] +=
-// W[128 x 16 k] . x^T[16 k x 16 activation rows] (tcgen05.mma.cta_group::1.kind::f16, M = 128, N = 16, K = 16),
-// activation rows >= M being zeros.  A CTA owns whole blocks of 128 output units and walks K in stages:
+// B200 design.  The GEMV is turned around so that the weights are the MMA's M side: D[128 weight rows x MT] +=
+// W[128 x 16 k] . x^T[16 k x MT activation rows] (tcgen05.mma.cta_group::1.kind::f16, M = 128, N = MT, K = 16), MT
+// = the activation rows rounded up to 16, 32, 64 or 128, rows >= M being zeros.  A CTA owns whole blocks of 128
+// output units and walks K in stages:
 //   * warp 0 (one lane) streams each stage with TMA tensor copies in the canonical K-major 128-byte-swizzle operand
 //     layout (8-row groups 1024 B apart): EPI 0/1 one 128-row x 128-column box of W; EPI 2 one 128-row x 64-column
-//     box of the gate rows and one of the up rows; plus the activation tile x[16 rows x the stage's columns] in the
+//     box of the gate rows and one of the up rows; plus the activation tile x[MT rows x the stage's columns] in the
 //     same layout.  One large box per matrix and stage matters: measured on B200, one SM streams 93 GB/s with a
 //     128 x 128 box per 32 KB stage, 67 GB/s with four 64 x 64 boxes, 35 GB/s with 8-row boxes.  Weights are
 //     independent of the previous kernel, so the first ring's worth of weight copies is issued before
@@ -16,34 +17,61 @@
 //   * warp 1 (one lane) issues the stage's MMAs (EPI 2: gate and up into two accumulators, so that a unit's gate
 //     and up sums land in the same TMEM lane) and commits them to the stage's "empty" barrier (the ring slot is
 //     free once the tensor core has read it) and, after a block's last stage, to the block's accumulator barrier.
-//     The accumulators are double-buffered in TMEM, so block i + 1 accumulates while the epilogue of block i runs;
+//     The accumulators are double-buffered in TMEM, so block i + 1 accumulates while the epilogue of block i runs.
+//     With few activation rows (N = 16 or 32) consecutive k-steps go to independent accumulator chains, summed in a
+//     fixed order in the epilogue: a single chain of small dependent MMAs kept every ring slot busy about twice as
+//     long (measured);
 //   * warps 2-5 (one TMEM lane quarter each) read a block's accumulators (tcgen05.ld 32x32b.x16: row = lane,
-//     16 activation columns), release them, and write the outputs.  With NORM they first rescale every activation
-//     tile in shared memory (the RMS factors of the M rows are computed once per CTA) and hand it to the MMA warp
-//     through a second barrier.
+//     16 activation columns at a time), release them, and write the outputs.  With NORM they first rescale every
+//     activation tile in shared memory (the RMS factors of the M rows are computed once per CTA) and hand it to the
+//     MMA warp through a second barrier.
+// Split K (a matrix with too few 128-row blocks to fill the grid, e.g. 16 blocks on 148 SMs): the grid becomes one
+// thread-block cluster of S <= 8 CTAs per block, CTA r of a cluster takes the r-th of S column ranges, and the S
+// partial sums meet through distributed shared memory: every CTA copies its fp32 accumulators into its own (now
+// idle) ring, a cluster barrier, then CTA r sums units [128 r / S, 128 (r + 1) / S) of the block over the S CTAs in
+// rank order (deterministic) and writes them, and a second cluster barrier keeps every CTA's shared memory alive
+// until its peers have read it.  No global workspace, no atomics, no second launch.
 // There is no cross-warp reduction and no mma.sync: one thread drives the tensor core, the fp32 sums stay in TMEM
 // across the whole K loop.  Every wait is bounded (fb_common.cuh); on expiry the error word is set and the CTA
-// winds down (the producer waits for its own copies, the TMEM is freed).
+// winds down (the producer waits for its own copies, the cluster barriers are still reached, the TMEM is freed).
 #define FB_ST_TMA 1
+#include <cooperative_groups.h>
+
+#include <cstdlib>
+
 #include "fb_gemv_core.cuh"
 #include "fb_tc.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace fb {
 namespace {
 
 constexpr int TC_BR = 128;                      // output units per block (the MMA's M)
 constexpr int TC_WBYTES = 32768;                // weight tile per stage: 128 rows x 128 columns (EPI 2: x 2 x 64)
-constexpr int TC_XBYTES = 16 * 128 * 2;         // activation tile (16 rows x up to 128 columns)
 // columns per stage: 128, or 64 for EPI 2 (gate and up tiles share the stage)
 template <int EPI>
 constexpr int tc_cols() { return EPI == 2 ? 64 : 128; }
+template <int EPI, int MT>
+constexpr int tc_xbytes() { return MT * tc_cols<EPI>() * 2; }    // activation tile per stage
+// independent accumulator chains per matrix
+template <int EPI, int MT>
+constexpr int tc_nch() { return EPI == 2 ? (MT == 16 ? 2 : 1) : (MT == 16 ? 4 : (MT == 32 ? 2 : 1)); }
+// TMEM columns of one accumulator buffer (x 2 buffers; at most 256)
+template <int EPI, int MT>
+constexpr int tc_dcols() { return (EPI == 2 ? 2 : 1) * tc_nch<EPI, MT>() * MT; }
+// split K: row pitch (floats) of the partial sums [unit][MT (+ MT up)], odd so that column writes and row reads
+// are free of bank conflicts
+template <int EPI, int MT>
+constexpr int tc_rp() { return (EPI == 2 ? 2 : 1) * MT + 1; }
 constexpr int TC_MAX_STAGES = 6;
+constexpr int TC_MAX_SPLIT = 8;                 // CTAs per cluster (portable cluster size)
 constexpr int TC_THREADS = 6 * 32;
 constexpr int TC_EPI_THREADS = 4 * 32;
 
 struct alignas(64) TcArgs {
   CUtensorMap tw[3];   // weight segments (EPI 2: gate, up) as [K / 64][rows][64], boxes of 128 rows x the stage
-  CUtensorMap tx;      // x [M, K] as [K / 64][M][64], one box = 16 rows x the stage (both 128-byte swizzle)
+  CUtensorMap tx;      // x [M, K] as [K / 64][M][64], one box = MT rows x the stage (both 128-byte swizzle)
   const bf16* x;
   long ldx;
   const bf16* nw;
@@ -54,6 +82,7 @@ struct alignas(64) TcArgs {
   const bf16* res;
   long ldr;
   int nst;
+  int split;           // CTAs per cluster sharing one block's K range (1: no split)
   unsigned* err;
 };
 
@@ -66,36 +95,55 @@ __device__ __forceinline__ TmaRows tc_rows(const TcArgs& a, int r) {
   return TmaRows{&a.tw[2], r - a.N0 - a.N1};
 }
 
-template <int EPI, bool NORM>
+// The epilogue of one output: fp32 sum(s) -> the output value of unit n, row m (before the bf16 store).
+template <int EPI>
+__device__ __forceinline__ float tc_out(const TcArgs& a, float v, float u, int m, int n) {
+  if (EPI == 2) {
+    const float gg = rbf(v);
+    return rbf(gg / (1.0f + expf(-gg))) * rbf(u);
+  }
+  if (EPI == 1) return b2f(a.res[(size_t)m * a.ldr + n]) + rbf(v);
+  return v;
+}
+
+template <int EPI, bool NORM, int MT>
 __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_constant__ TcArgs a) {
   constexpr int TC_C = tc_cols<EPI>();
+  constexpr int XB = tc_xbytes<EPI, MT>();
   constexpr int UB = TC_BR;                           // output units per block
-  // Accumulator chains: consecutive k-steps of a stage go to NCH independent accumulators (EPI 2: gate and up get
-  // two each), summed in a fixed order in the epilogue.  The tensor core then overlaps them instead of running one
-  // dependent chain of 8 small MMAs per stage, which kept every ring slot busy about twice as long (measured).
-  constexpr int NCH = 4;
-  constexpr int DCOLS = NCH * 16;                     // TMEM columns per accumulator buffer (x 2 buffers)
+  constexpr int NCH = tc_nch<EPI, MT>();
+  constexpr int DCOLS = tc_dcols<EPI, MT>();          // TMEM columns per accumulator buffer (x 2 buffers)
+  constexpr int RP = tc_rp<EPI, MT>();
+  constexpr uint32_t IDESC = tc_idesc(MT);
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = a.nst;
   unsigned char* wring = smem;                                   // [NST][TC_WBYTES], 1024-aligned
-  unsigned char* xring = smem + (size_t)NST * TC_WBYTES;         // [NST][TC_XBYTES]
-  uint64_t* full = reinterpret_cast<uint64_t*>(xring + (size_t)NST * TC_XBYTES);
+  unsigned char* xring = smem + (size_t)NST * TC_WBYTES;         // [NST][XB]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xring + (size_t)NST * XB);
   uint64_t* empty = full + TC_MAX_STAGES;
   uint64_t* xok = empty + TC_MAX_STAGES;
   uint64_t* dfull = xok + TC_MAX_STAGES;                          // [2]
   uint64_t* dempty = dfull + 2;                                   // [2]
   uint32_t* tslot = reinterpret_cast<uint32_t*>(dempty + 2);
-  float* rs = reinterpret_cast<float*>(tslot + 4);                // [16] RMS factors
+  float* rs = reinterpret_cast<float*>(tslot + 4);                // [MT] RMS factors
+  float* red = reinterpret_cast<float*>(smem);                    // split K: partial sums, over the idle ring
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = a.K, M = a.M;
-  const int nkc = (K + TC_C - 1) / TC_C;
+  const int nkc_all = (K + TC_C - 1) / TC_C;
   const int units = a.N;
   const int nb_all = (units + UB - 1) / UB;
-  const int b0 = (int)((long long)nb_all * blockIdx.x / gridDim.x);
-  const int b1 = (int)((long long)nb_all * (blockIdx.x + 1) / gridDim.x);
+  // split K: cluster c takes block c and its rank r the r-th column range; else CTA c takes blocks [b0, b1)
+  const int S = a.split;
+  const int rank = (int)(blockIdx.x % S);
+  const int nclu = gridDim.x / S;
+  const int cid = blockIdx.x / S;
+  const int b0 = (int)((long long)nb_all * cid / nclu);
+  const int b1 = (int)((long long)nb_all * (cid + 1) / nclu);
+  const int kc0 = (int)((long long)nkc_all * rank / S);
+  const int nkc = (int)((long long)nkc_all * (rank + 1) / S) - kc0;
   const int nblk = b1 - b0;
   const int T = nblk * nkc;
 
@@ -111,12 +159,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     }
     fence_mbar_init();
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
-                 "r"(2 * DCOLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
+  if (warp == 1) tc_alloc(tslot, 2 * DCOLS);
   tc_before();
   __syncthreads();
   tc_after();
@@ -126,7 +169,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     // ------------------------------------------------------------------ producer
     int issued = 0;
     auto issue_w = [&](int t) {
-      const int s = t % NST, kc = t % nkc, blk = b0 + t / nkc;
+      const int s = t % NST, kc = kc0 + t % nkc, blk = b0 + t / nkc;
       unsigned char* wt = wring + (size_t)s * TC_WBYTES;
       if (EPI == 2) {
         // [gate 128 rows x 128 B][up 128 rows x 128 B]
@@ -139,10 +182,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       }
     };
     auto issue_x = [&](int t) {
-      const int s = t % NST, kc = t % nkc;
-      tma_load_3d(xring + (size_t)s * TC_XBYTES, &a.tx, 0, 0, kc * (TC_C / 64), &full[s]);
+      const int s = t % NST, kc = kc0 + t % nkc;
+      tma_load_3d(xring + (size_t)s * XB, &a.tx, 0, 0, kc * (TC_C / 64), &full[s]);
     };
-    constexpr unsigned STAGE_TX = (unsigned)(TC_WBYTES + 16 * TC_C * 2);
+    constexpr unsigned STAGE_TX = (unsigned)(TC_WBYTES + XB);
     if (lane < 4) tma_prefetch_map(lane < 3 ? (const void*)&a.tw[lane] : (const void*)&a.tx);
     bool ok = true;
     const int pre = min(T, NST);
@@ -195,20 +238,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         tc_after();
         if (lane == 0) {
           const uint32_t wa = smem_u32(wring + (size_t)s * TC_WBYTES);
-          const uint32_t xa = smem_u32(xring + (size_t)s * TC_XBYTES);
+          const uint32_t xa = smem_u32(xring + (size_t)s * XB);
 #pragma unroll
           for (int j = 0; j < TC_C / 16; ++j) {
-            const uint64_t bd = tc_desc_sw128(xa + (j >> 2) * (16 * 128) + (j & 3) * 32);
+            const uint64_t bd = tc_desc_sw128(xa + (j >> 2) * (MT * 128) + (j & 3) * 32);
+            const uint32_t acc = (kc > 0 || j >= NCH) ? 1u : 0u;
+            const uint32_t ch = (uint32_t)((j % NCH) * MT);
             if (EPI == 2) {
-              // gate chains in columns [0, 32), up chains in [32, 64)
-              const uint32_t acc = (kc > 0 || j >= 2) ? 1u : 0u;
-              const uint32_t ch = (uint32_t)((j & 1) * 16);
-              tc_mma16(td + ch, tc_desc_sw128(wa + (j & 3) * 32), bd, acc);
-              tc_mma16(td + 32 + ch, tc_desc_sw128(wa + TC_BR * 128 + (j & 3) * 32), bd, acc);
+              // gate chains in columns [0, NCH MT), up chains in [NCH MT, 2 NCH MT)
+              tc_mma(td + ch, tc_desc_sw128(wa + (j & 3) * 32), bd, acc, IDESC);
+              tc_mma(td + NCH * MT + ch, tc_desc_sw128(wa + TC_BR * 128 + (j & 3) * 32), bd, acc, IDESC);
             } else {
-              const uint32_t acc = (kc > 0 || j >= NCH) ? 1u : 0u;
-              tc_mma16(td + (uint32_t)((j % NCH) * 16),
-                     tc_desc_sw128(wa + (j >> 2) * (TC_BR * 128) + (j & 3) * 32), bd, acc);
+              tc_mma(td + ch, tc_desc_sw128(wa + (j >> 2) * (TC_BR * 128) + (j & 3) * 32), bd, acc, IDESC);
             }
           }
           tc_commit(&empty[s]);
@@ -230,7 +271,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     bool ok = true;
     if (NORM) {
       // RMS factor of each activation row: warp q reduces rows q, q + 4, ...
-      for (int m = q; m < 16; m += 4) {
+      for (int m = q; m < MT; m += 4) {
         float ss = 0.f;
         if (m < M)
           for (int j = lane; j < (K >> 3); j += 32) {
@@ -245,12 +286,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       named_sync(1, TC_EPI_THREADS);
     }
     auto fix = [&](int t) -> bool {       // rescale stage t's activation tile in place
-      const int s = t % NST, kc = t % nkc;
+      const int s = t % NST, kc = kc0 + t % nkc;
       if (!mbar_wait_warp(&full[s], (t / NST) & 1, a.err)) return false;
-      unsigned char* xt = xring + (size_t)s * TC_XBYTES;
-      for (int i = etid; i < 16 * TC_C * 2 / 16; i += TC_EPI_THREADS) {
+      unsigned char* xt = xring + (size_t)s * XB;
+      for (int i = etid; i < XB / 16; i += TC_EPI_THREADS) {
         // [64-column block c][row m][16-byte unit jp], unit jp holding columns 8 (jp ^ (m % 8)) .. of the block
-        const int c = i >> 7, m = (i >> 3) & 15, jp = i & 7;
+        const int c = i / (MT * 8), m = (i >> 3) % MT, jp = i & 7;
         const int k = kc * TC_C + c * 64 + ((jp ^ (m & 7)) << 3);
         if (m >= M || k >= K) continue;
         uint4* p = reinterpret_cast<uint4*>(xt + (size_t)i * 16);
@@ -270,51 +311,67 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       if (lane == 0) mbar_arrive(&xok[s]);
       return true;
     };
+    // activation columns c16 .. c16 + 15 of this thread's row: the chains of matrix mat summed in a fixed order
+    auto load16 = [&](uint32_t tq, int mat, int c16, float (&v)[16]) {
+      tc_ld16(tq + (uint32_t)(mat * NCH * MT + c16), v);
+#pragma unroll
+      for (int ch = 1; ch < NCH; ++ch) {
+        float c[16];
+        tc_ld16(tq + (uint32_t)(mat * NCH * MT + ch * MT + c16), c);
+#pragma unroll
+        for (int m = 0; m < 16; ++m) v[m] += c[m];
+      }
+    };
     auto epilogue = [&](int i) -> bool {
       if (!mbar_wait(&dfull[i & 1], (i >> 1) & 1, a.err)) return false;
       tc_after();
       const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((i & 1) * DCOLS);
-      float v[16], u[16];
-      {
-        float c0[16], c1[16];
-        tc_ld16(tq, c0);
-        tc_ld16(tq + 16, c1);
+      const int n = (b0 + i) * UB + row;
+#pragma unroll 1
+      for (int c16 = 0; c16 < MT; c16 += 16) {
+        float v[16], u[16];
+        load16(tq, 0, c16, v);
+        if (EPI == 2) load16(tq, 1, c16, u);
+        if (n < units) {
 #pragma unroll
-        for (int m = 0; m < 16; ++m) v[m] = c0[m] + c1[m];
-        tc_ld16(tq + 32, c0);
-        tc_ld16(tq + 48, c1);
-        if (EPI == 2) {
-#pragma unroll
-          for (int m = 0; m < 16; ++m) u[m] = c0[m] + c1[m];
-        } else {
-#pragma unroll
-          for (int m = 0; m < 16; ++m) v[m] = (v[m] + c0[m]) + c1[m];
+          for (int m = 0; m < 16; ++m)
+            if (c16 + m < M)
+              a.y[(size_t)(c16 + m) * a.ldy + n] =
+                  __float2bfloat16_rn(tc_out<EPI>(a, v[m], EPI == 2 ? u[m] : 0.f, c16 + m, n));
         }
       }
       tc_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dempty[i & 1]);
-      const int n = (b0 + i) * UB + row;
-      if (n < units) {
-#pragma unroll
-        for (int m = 0; m < 16; ++m) {
-          if (m < M) {
-            float o;
-            if (EPI == 2) {
-              const float gg = rbf(v[m]);
-              o = rbf(gg / (1.0f + expf(-gg))) * rbf(u[m]);
-            } else if (EPI == 1) {
-              o = b2f(a.res[(size_t)m * a.ldr + n]) + rbf(v[m]);
-            } else {
-              o = v[m];
-            }
-            a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(o);
-          }
-        }
-      }
       return true;
     };
-    if (NORM) {
+    // split K: this CTA's partial sums of its one block -> red[unit][MT (+ MT up)]
+    auto dump = [&]() -> bool {
+      if (!mbar_wait(&dfull[0], 0, a.err)) return false;
+      tc_after();
+      const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c16 = 0; c16 < MT; c16 += 16) {
+        float v[16];
+        load16(tq, 0, c16, v);
+#pragma unroll
+        for (int m = 0; m < 16; ++m) red[row * RP + c16 + m] = v[m];
+        if (EPI == 2) {
+          load16(tq, 1, c16, v);
+#pragma unroll
+          for (int m = 0; m < 16; ++m) red[row * RP + MT + c16 + m] = v[m];
+        }
+      }
+      tc_before();
+      return true;
+    };
+    if (S > 1) {
+      if (nblk == 1) {
+        if (NORM)
+          for (int kc = 0; kc < nkc && ok; ++kc) ok = fix(kc);
+        if (ok) ok = dump();
+      }
+    } else if (NORM) {
       // rescale block i's tiles, then write block i - 1 (its accumulator fills while block i is rescaled)
       for (int i = 0; i < nblk && ok; ++i) {
         for (int kc = 0; kc < nkc && ok; ++kc) ok = fix(i * nkc + kc);
@@ -325,19 +382,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       for (int i = 0; i < nblk && ok; ++i) ok = epilogue(i);
     }
   }
+  __syncwarp();
+  if (S > 1) {
+    // every thread of every CTA of the cluster reaches both barriers, whatever happened above
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (warp >= 2 && nblk == 1) {
+      const int u0 = UB * rank / S, nu = UB * (rank + 1) / S - u0;
+      for (int idx = tid - 64; idx < nu * M; idx += TC_EPI_THREADS) {
+        const int m = idx / nu, uu = u0 + idx % nu;
+        const int n = b0 * UB + uu;
+        float v = 0.f, u = 0.f;
+        for (int p = 0; p < S; ++p) {
+          const float* rp = cluster.map_shared_rank(red, p) + uu * RP + m;
+          v += rp[0];
+          if (EPI == 2) u += rp[MT];
+        }
+        if (n < units) a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(tc_out<EPI>(a, v, u, m, n));
+      }
+    }
+    cluster.sync();
+  }
   tc_before();
   __syncthreads();
   tc_after();
-  if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * DCOLS) : "memory");
+  if (warp == 1) tc_dealloc(tmem, 2 * DCOLS);
 }
 
-template <int EPI, bool NORM>
-int launch_tc(const GemvArgs& g, cudaStream_t st) {
+thread_local int t_split = 1;
+// split K also for M <= 16 (FLASHB_TC_SPLIT=1 or flashb_set_gemv_split(1)).  Off by default: measured on B200 at 148 SMs and M = 2, the
+// mma.sync kernel's 8-row split takes 3.6 / 7.8 / 7.9 / 14.7 us for the backbone's o / q|k|v / down / gate|up
+// matrices, the cluster split 9.2 / 17.2 / 14.6 / 27.4 us (a cluster of 8 large-smem CTAs waits for whole free SMs
+// of one GPC, so it cannot start while the previous kernel drains).
+int g_split_small = -1;
+
+template <int EPI, bool NORM, int MT>
+int launch_tc(const GemvArgs& g, int split, cudaStream_t st) {
   TcArgs a{};
   a.x = g.x; a.ldx = g.ldx; a.nw = g.nw; a.eps = g.eps;
   a.N0 = g.N0; a.N1 = g.N1; a.N = g.N; a.K = g.K; a.M = g.M;
   a.y = g.y; a.ldy = g.ldy; a.res = g.res; a.ldr = g.ldr; a.err = g.err;
+  a.split = split;
   const int nseg[3] = {EPI == 2 ? g.N : g.N0, EPI == 2 ? g.N : g.N1, EPI == 2 ? 0 : g.N - g.N0 - g.N1};
   const bf16* wseg[3] = {g.W0, g.W1, g.W2};
   for (int i = 0; i < 3; ++i) {
@@ -345,15 +430,18 @@ int launch_tc(const GemvArgs& g, cudaStream_t st) {
     if (fbh::tmap_box(&a.tw[i], wseg[i], nseg[i], g.K, 64, TC_BR, tc_cols<EPI>() / 64, true) != FB_OK)
       return FB_ERR_UNSUPPORTED;
   }
-  // x [M rows, K] viewed as [K / 64 blocks][M rows][64]: one box = 16 rows x the stage (rows >= M read zeros)
-  if (fbh::tmap_box(&a.tx, g.x, g.M, g.K, 64, 16, tc_cols<EPI>() / 64, true, (long long)g.ldx) != FB_OK)
+  // x [M rows, K] viewed as [K / 64 blocks][M rows][64]: one box = MT rows x the stage (rows >= M read zeros)
+  if (fbh::tmap_box(&a.tx, g.x, g.M, g.K, 64, MT, tc_cols<EPI>() / 64, true, (long long)g.ldx) != FB_OK)
     return FB_ERR_UNSUPPORTED;
-  const size_t fixed = 1024 + (size_t)TC_MAX_STAGES * 3 * 8 + 4 * 8 + 16 + 16 * 4;
-  int nst = (int)((227 * 1024 - fixed) / (TC_WBYTES + TC_XBYTES));
+  constexpr int XB = tc_xbytes<EPI, MT>();
+  const size_t fixed = 1024 + (size_t)TC_MAX_STAGES * 3 * 8 + 4 * 8 + 16 + MT * 4;
+  int nst = (int)((227 * 1024 - fixed) / (TC_WBYTES + XB));
   if (nst > TC_MAX_STAGES) nst = TC_MAX_STAGES;
   a.nst = nst;
-  const size_t smem = fixed + (size_t)nst * (TC_WBYTES + TC_XBYTES);
-  auto kern = gemv_tc_kernel<EPI, NORM>;
+  // split K: the partial sums [128][RP] fp32 must fit over the ring
+  if (split > 1 && (size_t)TC_BR * tc_rp<EPI, MT>() * 4 > (size_t)nst * (TC_WBYTES + XB)) return FB_ERR_UNSUPPORTED;
+  const size_t smem = fixed + (size_t)nst * (TC_WBYTES + XB);
+  auto kern = gemv_tc_kernel<EPI, NORM, MT>;
   static int attr_done[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -366,28 +454,56 @@ int launch_tc(const GemvArgs& g, cudaStream_t st) {
     attr_done[dev] = (int)smem;
   }
   const int nb = (g.N + TC_BR - 1) / TC_BR;
-  const int grid = nb < fbh::grid_sms() ? nb : fbh::grid_sms();
+  const int grid = split > 1 ? nb * split : (nb < fbh::grid_sms() ? nb : fbh::grid_sms());
   void* args[] = {(void*)&a};
-  return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(TC_THREADS), smem, st, args, true);
+  t_split = split;
+  return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(TC_THREADS), smem, st, args, true,
+                         split > 1 ? split : 0);
+}
+
+template <int EPI, bool NORM>
+int launch_mt(const GemvArgs& g, int split, cudaStream_t st) {
+  if (g.M <= 16) return launch_tc<EPI, NORM, 16>(g, split, st);
+  if (g.M <= 32) return launch_tc<EPI, NORM, 32>(g, split, st);
+  if (g.M <= 64) return launch_tc<EPI, NORM, 64>(g, split, st);
+  return launch_tc<EPI, NORM, 128>(g, split, st);
 }
 
 }  // namespace
 
-// The tensor-core (tcgen05) GEMV when it applies: M <= 16, K % 64 == 0, segment boundaries at multiples of 128,
-// and enough 128-unit blocks to keep at least a third of the grid busy (fewer, and the mma.sync kernel's finer
-// split over every SM is faster).  Returns FB_ERR_UNSUPPORTED when it does not apply.
+// The tensor-core (tcgen05) GEMV when it applies: 1 <= M <= 128, K % 64 == 0, segment boundaries at multiples of
+// 128.  With at least a third of the grid's CTAs in 128-row blocks, each CTA takes whole blocks; with fewer blocks
+// the K range of each block is split over a cluster of S = min(8, grid / blocks, column stages) CTAs.  For M <= 16
+// it then returns FB_ERR_UNSUPPORTED (the mma.sync kernel's 8-row split over every SM is faster) unless
+// FLASHB_TC_SPLIT=1.
 int gemv_tc(GemvArgs& g, int epi, bool norm, cudaStream_t st) {
-  if (g.M < 1 || g.M > 16 || g.K % 64 != 0) return FB_ERR_UNSUPPORTED;
+  if (g.M < 1 || g.M > 128 || g.K % 64 != 0) return FB_ERR_UNSUPPORTED;
   const int n2 = g.N - g.N0 - g.N1;
   if (epi != 2 && (((g.N1 || n2) && g.N0 % TC_BR) || (n2 && (g.N0 + g.N1) % TC_BR))) return FB_ERR_UNSUPPORTED;
+  if (g_split_small < 0) {
+    const char* e = getenv("FLASHB_TC_SPLIT");
+    g_split_small = (e && e[0] == '1') ? 1 : 0;
+  }
   const int nb = (g.N + TC_BR - 1) / TC_BR;
-  if (nb * 3 < fbh::grid_sms()) return FB_ERR_UNSUPPORTED;
-  if (epi == 0 && norm) return launch_tc<0, true>(g, st);
-  if (epi == 0) return launch_tc<0, false>(g, st);
-  if (epi == 1) return launch_tc<1, false>(g, st);
-  if (epi == 2 && norm) return launch_tc<2, true>(g, st);
-  if (epi == 2) return launch_tc<2, false>(g, st);
+  const int G = fbh::grid_sms();
+  int split = 1;
+  if (nb * 3 < G) {
+    const int nkc = g.K / (epi == 2 ? 64 : 128);
+    split = G / nb;
+    if (split > TC_MAX_SPLIT) split = TC_MAX_SPLIT;
+    if (split > nkc) split = nkc;
+    if (split < 2) split = 1;
+    if (g.M <= 16 && (split == 1 || !g_split_small)) return FB_ERR_UNSUPPORTED;
+  }
+  if (epi == 0 && norm) return launch_mt<0, true>(g, split, st);
+  if (epi == 0) return launch_mt<0, false>(g, split, st);
+  if (epi == 1) return launch_mt<1, false>(g, split, st);
+  if (epi == 2 && norm) return launch_mt<2, true>(g, split, st);
+  if (epi == 2) return launch_mt<2, false>(g, split, st);
   return FB_ERR_UNSUPPORTED;
 }
+
+int gemv_tc_last_split() { return t_split; }
+void gemv_tc_set_split_small(int on) { g_split_small = on ? 1 : 0; }
 
 }  // namespace fb

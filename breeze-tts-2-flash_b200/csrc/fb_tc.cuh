@@ -34,6 +34,14 @@ __device__ __forceinline__ void tc_mma16_m64(uint32_t tmem_d, uint64_t adesc, ui
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %4, p;\n\t}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(tc_idesc(16, 64)));
 }
+// Any N (a multiple of 16 up to 256 for M = 128): idesc = tc_idesc(n, m).
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate,
+                                       uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %3, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %4, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(accumulate), "r"(idesc));
+}
 // The mbarrier receives one arrival once every MMA issued so far by this thread has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -423,12 +423,13 @@ class FrameEngine:
     def _budget(self, st):
         return 0 if st.lane is None else self.lane_sms
 
-    def step(self, before_part=None, after_part=None):
-        """One frame of every slot (not the single-stream slot), lanes side by side, ordered after the work already
-        on the current stream; the current stream waits for every lane at the end.  ``before_part(kind, i, stream)``,
-        if given, is called before each part ('bb' or 'dd') of slot i with the CUDA stream it is issued on, and with
-        ('end', None, stream) once per lane stream after its last part; ``after_part('dd', i, stream)`` after the depth
-        part of slot i."""
+    def step(self, before_part=None, after_part=None, fork=True, join=True):
+        """One frame of every slot (not the single-stream slot), lanes side by side.  fork: the lanes first wait for
+        the work already on the current stream; join: the current stream waits for every lane at the end.  Steps in
+        a row need the fork only on the first and the join only on the last, so that a lane never waits for the
+        others between steps.  ``before_part(kind, i, stream)``, if given, is called before each part ('bb' or
+        'dd') of slot i with the CUDA stream it is issued on, and with ('end', None, stream) once per lane stream
+        after its last part; ``after_part('dd', i, stream)`` after the depth part of slot i."""
         cur = torch.cuda.current_stream(self.device)
         if self.lanes == 1:
             for i in range(len(self.streams)):
@@ -436,15 +437,17 @@ class FrameEngine:
             if before_part is not None:
                 before_part('end', None, cur)
             return
-        for ls in self.lane_stream:
-            ls.wait_stream(cur)
+        if fork:
+            for ls in self.lane_stream:
+                ls.wait_stream(cur)
         for i, st in enumerate(self.streams):
             with torch.cuda.stream(self.lane_stream[st.lane]):
                 self.frame(i, before_part, after_part)
         for ls in self.lane_stream:
             if before_part is not None:
                 before_part('end', None, ls)
-            cur.wait_stream(ls)
+            if join:
+                cur.wait_stream(ls)
 
     def frame(self, i, before_part=None, after_part=None):
         st = self._get(i)

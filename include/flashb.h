@@ -40,6 +40,13 @@ int flashb_device_error(int clear);
  * 1 = the mma.sync weight stream, 2 = the tcgen05 kernel (enough 128-row blocks for the grid); -1 before any.
  * For tests and profiling; no reference counterpart. */
 int flashb_gemv_last_path(void);
+/* CTAs per 128-row block of the calling thread's last tcgen05 GEMV launch: 1, or S >= 2 when the block's K range
+ * was split over a thread-block cluster of S CTAs (too few blocks for the grid).  For tests; no reference
+ * counterpart. */
+int flashb_gemv_last_split(void);
+/* Split K over a cluster also for M <= 16 rows (1) or not (0, the default: the mma.sync kernel is faster there on
+ * a whole B200).  Process-wide; no reference counterpart. */
+void flashb_set_gemv_split(int enable);
 /* Programmatic dependent launch on (1, default) / off (0) for all later launches of this process. */
 void flashb_set_pdl(int enable);
 /* SM budget of the calling host thread (0, the default: every SM).  Launches issued later by this thread -- directly
@@ -78,8 +85,9 @@ int flashb_attn_decode_fused(const void* qkv, int64_t qkv_sb, const void* qn_w, 
 
 /* ---------------------------------------------------------------------------------------------- fused GEMVs
  * y[m, n] = sum_k xin[m, k] * W[n, k], nn.Linear layout (W [N, K] bf16 row-major contiguous), fp32 accumulation,
- * M = 1..8 rows (x row stride ldx, y row stride ldy, both multiples of 8 elements), K % 8 == 0.  All pointers
- * 16-byte aligned. */
+ * M = 1..128 rows (the reference: 1..8; x row stride ldx, y row stride ldy, both multiples of 8 elements),
+ * K % 8 == 0.  All pointers 16-byte aligned.  More than 16 rows run on the tcgen05 kernel (K % 64 == 0), which then
+ * streams the weights once for all rows; otherwise in row blocks of 16. */
 /* Replaces gemv_seg (flash/csrc/bb_fused.cu:293-316): y[:, 0:N0+N1+N2] = norm?(x) @ [W0; W1; W2]^T, where norm is
  * the eager Qwen3 RMSNorm with weight nw [K] when nw != NULL.  W1/W2 may be NULL with N1/N2 = 0. */
 int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const void* nw, float eps, const void* W0, int N0,

@@ -136,6 +136,22 @@ def test_frame_engine_matches_oracle_and_standalone_depth(group, lanes):
     assert device_error() == 0
 
 
+def test_frame_engine_free_running_lanes_equal_joined_steps():
+    """Steps issued with the lanes joined only after the last one give the same tokens as steps joined one by one:
+    each slot's frames stay in order on its lane stream, and no lane reads another's buffers."""
+    ea = _small_engine(streams=8, group=2, lanes=2)
+    eb = _small_engine(streams=8, group=2, lanes=2)
+    ea.capture()
+    eb.capture()
+    for t in range(4):
+        ea.step()
+        eb.step(fork=(t == 0), join=(t == 3))
+    torch.cuda.synchronize()
+    for sa, sb in zip(ea.streams, eb.streams):
+        assert torch.equal(sa.outtok, sb.outtok) and torch.equal(sa.first_cb, sb.first_cb)
+        assert torch.equal(sa.bb.cfg_logits_buf, sb.bb.cfg_logits_buf)
+
+
 def test_frame_engine_graph_equals_eager():
     ea = _small_engine(streams=1)
     eb = _small_engine(streams=1)

@@ -285,3 +285,69 @@ def test_gemv_tcgen05_matches_oracle(ops, kind, M, budget):
     assert_close(np32(y), ref, what=f'tcgen05 {kind} M={M}')
     from flashb._native import device_error
     assert device_error() == 0
+
+
+def _split():
+    from flashb._native import lib
+    return lib().flashb_gemv_last_split()
+
+
+@pytest.mark.parametrize('kind,M,budget,split', [
+    # many activation rows (MMA N = 32, 64, 128), whole blocks per CTA
+    ('gateup', 128, 18, 1), ('gateup', 40, 32, 1), ('qkv', 128, 8, 1), ('qkv', 17, 8, 1), ('o', 64, 4, 1),
+    ('down', 100, 4, 1),
+    # too few 128-row blocks for the grid: each block's K range split over a cluster
+    ('qkv', 128, 0, 6), ('o', 128, 0, 8), ('down', 128, 0, 8), ('gateup', 128, 0, 3), ('o', 2, 0, 8),
+    ('qkv', 16, 0, 6), ('down', 33, 0, 8), ('gateup', 2, 0, 3), ('odd', 70, 0, 8), ('o', 128, 64, 4)])
+def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, split):
+    """Up to 128 activation rows on the tcgen05 kernel (the weights streamed once for every row), and split K over
+    a thread-block cluster with the partial sums reduced through distributed shared memory (budget 0 = all SMs,
+    e.g. 148 on B200: 16 blocks of a 2048-row matrix become 16 clusters of 8; for M <= 16 only when switched on)."""
+    fx, _ = ops
+    K = {'down': 6144, 'odd': 1024}.get(kind, 2048)
+    x = randn((M, K), 51)
+    nw = randn((K,), 52, 0.1, 1.0)
+    nsm = torch.cuda.get_device_properties(0).multi_processor_count
+    if budget == 0 and nsm < 148:
+        pytest.skip('split counts are for a 148-SM B200')
+    from flashb._native import lib
+    try:
+        _budget(budget)
+        lib().flashb_set_gemv_split(1 if M <= 16 and split > 1 else 0)
+        if kind == 'gateup':
+            Wg, Wu = randn((6144, K), 53, 0.02), randn((6144, K), 54, 0.02)
+            y = torch.empty(M, 6144, dtype=torch.bfloat16, device='cuda')
+            fx.gemv_gateup(x, nw, 1e-6, Wg, Wu, y)
+            ref = dec.gemv_gateup(np32(x), np32(nw), 1e-6, np32(Wg), np32(Wu))
+        elif kind == 'qkv':
+            Wq, Wk, Wv = randn((2048, K), 55, 0.02), randn((512, K), 56, 0.02), randn((512, K), 57, 0.02)
+            y = torch.empty(M, 3072, dtype=torch.bfloat16, device='cuda')
+            fx.gemv_seg(x, nw, 1e-6, Wq, Wk, Wv, y)
+            ref = dec.gemv_seg(np32(x), np32(nw), 1e-6, [np32(Wq), np32(Wk), np32(Wv)])
+        else:
+            N = 300 if kind == 'odd' else 2048
+            W = randn((N, K), 58, 0.02)
+            res = randn((M, N), 59)
+            y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+            fx.gemv_resid(x, W, res, y)
+            ref = dec.gemv_resid(np32(x), np32(W), np32(res))
+        torch.cuda.synchronize()
+        path, got_split = _path(), _split()
+        # the same call again gives the same bits (the split's reduction order is fixed)
+        y2 = torch.empty_like(y)
+        if kind == 'gateup':
+            fx.gemv_gateup(x, nw, 1e-6, Wg, Wu, y2)
+        elif kind == 'qkv':
+            fx.gemv_seg(x, nw, 1e-6, Wq, Wk, Wv, y2)
+        else:
+            fx.gemv_resid(x, W, res, y2)
+        torch.cuda.synchronize()
+    finally:
+        _budget(0)
+        lib().flashb_set_gemv_split(0)
+    assert path == 2, f'expected the tcgen05 kernel, got path {path}'
+    assert got_split == split, f'expected split {split}, got {got_split}'
+    assert_close(np32(y), ref, what=f'tcgen05 {kind} M={M} split={split}')
+    assert torch.equal(y, y2)
+    from flashb._native import device_error
+    assert device_error() == 0
