@@ -54,6 +54,9 @@ def args_():
                    help='streams decoded together per launch (their GEMV rows share every weight read)')
     p.add_argument('--lanes', type=int, default=8,
                    help='GPU lanes: slots run on this many CUDA streams side by side, each sized for 1/lanes of the SMs')
+    p.add_argument('--backbone', default='shared', choices=['shared', 'lanes'],
+                   help='shared: one backbone graph for every slot on the whole GPU (row groups of 16 per GEMV '
+                        'launch); lanes: a backbone graph per slot on its lane')
     p.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample length')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
@@ -279,9 +282,10 @@ def main():
     # frame: at most one lane per slot; the one-part cases keep the requested lanes, so that a single slot can be
     # timed or profiled at a lane's grid size
     lanes = max(1, min(a.lanes, my_streams // a.group)) if a.case == 'frame' else max(1, a.lanes)
+    shared = a.backbone == 'shared' and a.case in ('frame', 'backbone')
     eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + LAT_FRAMES + 8, device=dev, seed=0,
                       depth_only=(a.case == 'depth'), group=a.group, single_slot=(a.case == 'frame'),
-                      lanes=lanes)
+                      lanes=lanes, shared_backbone=shared)
     eng.capture()
     stream = torch.cuda.current_stream(dev)
 
@@ -308,10 +312,15 @@ def main():
         if case != 'backbone':
             eng.step(mark)       # the frame, or the depth part alone (an engine without backbone)
             return
-        # the backbone part alone, on the current stream (graphs captured with the lane's SM budget)
-        for i in range(S):
-            mark('bb', i, stream)
-            eng.streams[i].graph.replay()
+        # the backbone part alone, on the current stream (graphs captured with the lane's SM budget, or the shared
+        # graph of every slot)
+        if eng.shared:
+            mark('bb', -1, stream)
+            eng.bb_graph.replay()
+        else:
+            for i in range(S):
+                mark('bb', i, stream)
+                eng.streams[i].graph.replay()
         mark('end', None, stream)
 
     # ---- device-resident run
@@ -342,11 +351,12 @@ def main():
         prev = last.get(s_.cuda_stream)
         if prev is not None:
             (bb_ms if prev[0] == 'bb' else dd_ms).append(prev[1].elapsed_time(e))
-        last[s_.cuda_stream] = None if kind == 'end' else (kind, e)
+        last[s_.cuda_stream] = None if kind in ('end', 'bbend') else (kind, e)
     kv1 = int(eng.streams[0].bb.cache_position.item()) + 1 if eng.streams[0].bb is not None else 0
     pk = peaks()
     dd_bytes = dcfg.n_decode * dcfg.step_weight_bytes()
-    bb_bytes = backbone_step_bytes(bcfg, 2 * a.group, (kv0 + kv1) // 2)
+    bb_rows = 2 * a.group * (S if eng.shared else 1)      # rows of one backbone graph
+    bb_bytes = backbone_step_bytes(bcfg, bb_rows, (kv0 + kv1) // 2)
     roof = None
     if dd_ms:
         dd_avg = sum(dd_ms) / len(dd_ms)
@@ -361,11 +371,14 @@ def main():
     if bb_ms:
         bb_avg = sum(bb_ms) / len(bb_ms)
         ach = bb_bytes / (bb_avg / 1e3) / 1e9
-        roof_bb = dict(kernels='backbone step (GQA decode attention + fused GEMVs + ends, 146 launches as a graph)',
+        nconc = 1 if eng.shared else lanes
+        roof_bb = dict(kernels=('backbone step of every slot (GQA decode attention + fused GEMVs + ends, one graph, '
+                                f'{bb_rows} rows)' if eng.shared else
+                                'backbone step (GQA decode attention + fused GEMVs + ends, 146 launches as a graph)'),
                        bound='hbm', achieved=round(ach, 1), peak=pk['hbm_gbs'], unit='GB/s',
                        frac=round(ach / pk['hbm_gbs'], 4), algorithmic_bytes=bb_bytes, step_ms=round(bb_avg, 4),
-                       peak_source=pk['source'], concurrent_steps=lanes, achieved_all_lanes=round(ach * lanes, 1),
-                       frac_all_lanes=round(ach * lanes / pk['hbm_gbs'], 4))
+                       peak_source=pk['source'], concurrent_steps=nconc, achieved_all_lanes=round(ach * nconc, 1),
+                       frac_all_lanes=round(ach * nconc / pk['hbm_gbs'], 4))
 
     # ---- end-to-end run through the engine API with host buffers
     e2e = None
@@ -385,10 +398,11 @@ def main():
             # double-buffered pinned array.  Slots are waited for one by one, so the host issues the next frames
             # while the GPU still runs this step; the lanes still join on the device at the end of every step.
             def h2d_q(kind, i, s):
-                if kind == 'bb':
-                    if got[i] is not None:
-                        got[i].synchronize()
-                    eng.streams[i].q.copy_(qh[(i + t) % R], non_blocking=True)
+                if kind == 'bb':    # i = -1: the shared backbone of every slot
+                    for j in (range(S) if i < 0 else (i,)):
+                        if got[j] is not None:
+                            got[j].synchronize()
+                        eng.streams[j].q.copy_(qh[(j + t) % R], non_blocking=True)
 
             def d2h_tokens(kind, i, s):
                 st = eng.streams[i]
@@ -446,8 +460,10 @@ def main():
     if rank == 0:
         wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + greedy '
                        f'codebook-0 + 16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9); '
-                       f'{a.group} stream(s) per launch share the weight reads; {lanes} lane(s) of the GPU side by '
-                       f'side',
+                       f'{a.group} stream(s) per depth launch share the weight reads; {lanes} lane(s) of the GPU side '
+                       f'by side; ' + (f'one backbone graph for all {my_streams} streams ({2 * my_streams} rows, GEMVs '
+                                       f'as row groups of 16)' if eng.shared else
+                                       f'a backbone graph per {a.group} streams on its lane'),
               'depth': 'depth frame only (4 layers, hidden 1024, 16 codebooks of 2048, CFG + top-k 50 sampling)',
               'backbone': 'backbone decode step only (28 layers, hidden 2048, B=2, KV 512+t) + frame link'}[case]
         line = dict(
@@ -456,7 +472,7 @@ def main():
             vs_baseline=None, dtype='bf16', data='synthetic (seeded random bf16 weights, random prompt KV)',
             config=dict(workload=wl, streams=total_streams, streams_per_gpu=my_streams, step='one frame of every stream '
                         'on the rank', streams_per_launch=a.group, prompt_len=a.prompt, kv_len=[kv0, kv1],
-                        parallelism=f'replica x{world}', lanes=lanes,
+                        parallelism=f'replica x{world}', lanes=lanes, backbone=a.backbone if shared else 'lanes',
                         lane_sms=eng.lane_sms or torch.cuda.get_device_properties(dev).multi_processor_count,
                         l2='inputs larger than L2: 2.70 GB backbone weights per step, 130 MB depth weights per '
                            'codebook step; no flush', cb0='greedy (backbone sampler do_sample=False)',
@@ -469,6 +485,7 @@ def main():
     if world > 1:
         for st in eng.streams + ([eng.single] if eng.single is not None else []):
             st.graph = None
+        eng.bb_graph = None
         barrier()
         dist.destroy_process_group()
 

@@ -21,11 +21,20 @@
 // distributed shared memory (in split order, so the result is deterministic) -- no global workspace, no atomics.
 #include <cooperative_groups.h>
 
+#include <cstdlib>
+
 #include "fb_common.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace fb {
+
+// fb_attn_mma.cu: the tensor-core kernel for the fused variant when the rows alone fill the grid
+int attn_mma_fused(const bf16* qkv, long qkv_sb, const bf16* qn_w, const bf16* kn_w, float eps, const bf16* cos,
+                   const bf16* sin, long cs_sb, bf16* kc, bf16* vc, long c_sb, long c_sh, int B, int NH, int NKV,
+                   int S, const void* mask, int mask_bf16, long m_sb, const long long* cache_pos, float scaling,
+                   bf16* out, cudaStream_t st);
+thread_local int t_attn_path = -1;
 
 constexpr int AT_D = 128;
 constexpr int AT_THREADS = 128;
@@ -324,12 +333,30 @@ using namespace fb;
 
 constexpr size_t AT_SMEM = 4 * (size_t)AT_CHUNK * AT_D * 2;  // K and V, two stages
 
+// Splits per (b, kv-head): about two CTAs per SM in all, at least 16 keys each, at most g_max_split (the cluster
+// size; FLASHB_ATTN_SPLITS sets it, default AT_MAXCLUSTER).
+int g_max_split = -1;
+int g_mma = -1;   // the tensor-core kernel for the fused variant (FLASHB_ATTN_MMA=0 turns it off)
+
+bool mma_enabled() {
+  if (g_mma < 0) {
+    const char* e = getenv("FLASHB_ATTN_MMA");
+    g_mma = (e && e[0] == '0') ? 0 : 1;
+  }
+  return g_mma == 1;
+}
+
 int pick_nsplit(int B, int NKV, int S) {
+  if (g_max_split < 0) {
+    const char* e = getenv("FLASHB_ATTN_SPLITS");
+    const int v = e ? atoi(e) : 0;
+    g_max_split = (v >= 1 && v <= AT_MAXCLUSTER) ? v : AT_MAXCLUSTER;
+  }
   const int target = 2 * fbh::grid_sms();
   int ns = (target + B * NKV - 1) / (B * NKV);
   const int cap_len = (S + 15) / 16;
   if (ns > cap_len) ns = cap_len;
-  if (ns > AT_MAXCLUSTER) ns = AT_MAXCLUSTER;
+  if (ns > g_max_split) ns = g_max_split;
   return ns < 1 ? 1 : ns;
 }
 
@@ -392,6 +419,8 @@ int fill_common(AttnArgs& a, const void* kc, const void* vc, int64_t c_sb, int64
 
 }  // namespace
 
+extern "C" int flashb_attn_last_path(void) { return fb::t_attn_path; }
+
 extern "C" int64_t flashb_attn_ws_floats(int B, int NH, int NKV, int S, int D) {
   (void)B; (void)NH; (void)NKV; (void)S; (void)D;
   return 0;  // split partials are merged in distributed shared memory; no global workspace is needed
@@ -427,5 +456,15 @@ extern "C" int flashb_attn_decode_fused(const void* qkv, int64_t qkv_sb, const v
   a.qn_w = (const bf16*)qn_w; a.kn_w = (const bf16*)kn_w; a.eps = eps;
   a.cos = (const bf16*)cos; a.sin = (const bf16*)sin; a.cs_sb = (long)cs_sb;
   a.cache_pos = (const long long*)cache_pos;
+  if (a.nsplit == 1 && mma_enabled()) {
+    // the rows alone fill the grid: the tensor-core kernel (one CTA per row and KV head)
+    rc = attn_mma_fused(a.qkv, a.qkv_sb, a.qn_w, a.kn_w, eps, a.cos, a.sin, a.cs_sb, a.kc, a.vc, a.c_sb, a.c_sh, B,
+                        NH, NKV, S, mask, a.mask_bf16, a.m_sb, a.cache_pos, scaling, a.out, (cudaStream_t)stream);
+    if (rc != FB_ERR_UNSUPPORTED) {
+      t_attn_path = 1;
+      return rc;
+    }
+  }
+  t_attn_path = 0;
   return dispatch_g<true>(a, B, NH / NKV, (cudaStream_t)stream);
 }

@@ -428,6 +428,11 @@ extern "C" int flashb_gemv_last_split(void) { return t_gemv_path == 2 ? fb::gemv
 
 extern "C" void flashb_set_gemv_split(int enable) { fb::gemv_tc_set_split_small(enable); }
 
+extern "C" int flashb_set_gemv_group_rows(int rows) {
+  FB_CHECK_ARG(rows == 16 || rows == 32 || rows == 64 || rows == 128, "gemv: group rows %d not 16, 32, 64 or 128", rows);
+  return fb::gemv_tc_set_group_rows(rows);
+}
+
 extern "C" int flashb_gemv_resid(const void* x, int64_t ldx, int M, int K, const void* W, int N, const void* res,
                                  int64_t ldr, void* y, int64_t ldy, void* stream) {
   int rc = common_checks(x, ldx, M, K, y, ldy);

@@ -59,6 +59,7 @@ __device__ __forceinline__ int gv_seg_end(const GemvArgs& a, int n) {
 int gemv_tc(GemvArgs& a, int epi, bool norm, cudaStream_t st);
 int gemv_tc_last_split();
 void gemv_tc_set_split_small(int on);
+int gemv_tc_set_group_rows(int rows);
 
 // Launches the 32 KB-stage build (fb_gemv_narrow.cu); epi / norm select the instantiation, xchunk the staging.
 int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st, int xchunk, int min_nst);

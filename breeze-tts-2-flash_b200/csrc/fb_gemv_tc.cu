@@ -5,8 +5,10 @@
 //
 // B200 design.  The GEMV is turned around so that the weights are the MMA's M side: D[128 weight rows x MT] +=
 // W[128 x 16 k] . x^T[16 k x MT activation rows] (tcgen05.mma.cta_group::1.kind::f16, M = 128, N = MT, K = 16), MT
-// = the activation rows rounded up to 16, 32, 64 or 128, rows >= M being zeros.  A CTA owns whole blocks of 128
-// output units and walks K in stages:
+// = the activation rows rounded up to 16, 32, 64 or 128, rows >= M being zeros.  More rows than MT form row groups
+// (blockIdx.y): each group is the same GEMV over MT rows on its share of the grid, and the groups, launched together,
+// stream each weight tile from HBM about once and from L2 for the others.  A CTA owns whole blocks of 128 output
+// units and walks K in stages:
 //   * warp 0 (one lane) streams each stage with TMA tensor copies in the canonical K-major 128-byte-swizzle operand
 //     layout (8-row groups 1024 B apart): EPI 0/1 one 128-row x 128-column box of W; EPI 2 one 128-row x 64-column
 //     box of the gate rows and one of the up rows; plus the activation tile x[MT rows x the stage's columns] in the
@@ -60,14 +62,18 @@ constexpr int tc_nch() { return EPI == 2 ? (MT == 16 ? 2 : 1) : (MT == 16 ? 4 : 
 // TMEM columns of one accumulator buffer (x 2 buffers; at most 256)
 template <int EPI, int MT>
 constexpr int tc_dcols() { return (EPI == 2 ? 2 : 1) * tc_nch<EPI, MT>() * MT; }
-// split K: row pitch (floats) of the partial sums [unit][MT (+ MT up)], odd so that column writes and row reads
-// are free of bank conflicts
+// split K: row pitch (floats) of the partial sums [unit][MT (+ MT up)]: 16-byte rows, and 4 banks apart so that
+// a warp's float4 writes of 32 rows are conflict-free
 template <int EPI, int MT>
-constexpr int tc_rp() { return (EPI == 2 ? 2 : 1) * MT + 1; }
+constexpr int tc_rp() { return (EPI == 2 ? 2 : 1) * MT + 4; }
 constexpr int TC_MAX_STAGES = 6;
 constexpr int TC_MAX_SPLIT = 8;                 // CTAs per cluster (portable cluster size)
 constexpr int TC_THREADS = 6 * 32;
 constexpr int TC_EPI_THREADS = 4 * 32;
+
+// Split phases of a cluster barrier (every thread of every CTA of the cluster arrives once per phase, then waits).
+__device__ __forceinline__ void cl_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cl_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 struct alignas(64) TcArgs {
   CUtensorMap tw[3];   // weight segments (EPI 2: gate, up) as [K / 64][rows][64], boxes of 128 rows x the stage
@@ -128,10 +134,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   uint64_t* dempty = dfull + 2;                                   // [2]
   uint32_t* tslot = reinterpret_cast<uint32_t*>(dempty + 2);
   float* rs = reinterpret_cast<float*>(tslot + 4);                // [MT] RMS factors
+  float* psum = rs + MT;                                          // [MT] sums of squares (split K: this CTA's)
   float* red = reinterpret_cast<float*>(smem);                    // split K: partial sums, over the idle ring
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = a.K, M = a.M;
+  // row group blockIdx.y: activation rows [r0, r0 + M) of the launch's a.M
+  const int r0 = blockIdx.y * MT;
+  const int K = a.K, M = min(MT, a.M - r0);
   const int nkc_all = (K + TC_C - 1) / TC_C;
   const int units = a.N;
   const int nb_all = (units + UB - 1) / UB;
@@ -164,6 +173,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   __syncthreads();
   tc_after();
   const uint32_t tmem = *tslot;
+  // split K, phase 0 of the cluster barrier: with NORM the epilogue warps exchange the RMS partial sums of their K
+  // ranges; every other thread arrives now and waits at the end
+  const bool early = S > 1 && !(NORM && warp >= 2);
+  if (early) cl_arrive();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
@@ -183,7 +196,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     };
     auto issue_x = [&](int t) {
       const int s = t % NST, kc = kc0 + t % nkc;
-      tma_load_3d(xring + (size_t)s * XB, &a.tx, 0, 0, kc * (TC_C / 64), &full[s]);
+      tma_load_3d(xring + (size_t)s * XB, &a.tx, 0, r0, kc * (TC_C / 64), &full[s]);
     };
     constexpr unsigned STAGE_TX = (unsigned)(TC_WBYTES + XB);
     if (lane < 4) tma_prefetch_map(lane < 3 ? (const void*)&a.tw[lane] : (const void*)&a.tx);
@@ -270,18 +283,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     pdl_trigger();
     bool ok = true;
     if (NORM) {
-      // RMS factor of each activation row: warp q reduces rows q, q + 4, ...
-      for (int m = q; m < MT; m += 4) {
-        float ss = 0.f;
-        if (m < M)
-          for (int j = lane; j < (K >> 3); j += 32) {
-            float f[8];
-            cvt8(*reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + j * 8), f);
+      // sums of squares of the rows over their 16-byte chunks [jb, je) -> psum[m]: warp q takes rows q, q + 4, ...,
+      // RB of them at a time (RB loads in flight per lane), each lane its chunks in order, then a butterfly
+      constexpr int RB = MT / 4 < 8 ? MT / 4 : 8;
+      const int jb = S > 1 ? kc0 * TC_C / 8 : 0;
+      const int je = S > 1 ? min(K, (kc0 + nkc) * TC_C) / 8 : K / 8;
+      for (int i0 = 0; i0 < MT / 4; i0 += RB) {
+        float ss[RB];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) ss = fmaf(f[u], f[u], ss);
+        for (int r = 0; r < RB; ++r) ss[r] = 0.f;
+        for (int j = jb + lane; j < je; j += 32) {
+          uint4 v[RB];
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            const int m = q + 4 * (i0 + r);
+            v[r] = m < M ? *reinterpret_cast<const uint4*>(a.x + (size_t)(r0 + m) * a.ldx + (size_t)j * 8)
+                         : make_uint4(0u, 0u, 0u, 0u);
           }
-        ss = warp_sum(ss);
-        if (lane == 0) rs[m] = 1.0f / sqrtf(ss / (float)K + a.eps);
+#pragma unroll
+          for (int r = 0; r < RB; ++r) {
+            float f[8];
+            cvt8(v[r], f);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) ss[r] = fmaf(f[u], f[u], ss[r]);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          const float t = warp_sum(ss[r]);
+          if (lane == 0) psum[q + 4 * (i0 + r)] = t;
+        }
+      }
+      if (S > 1) {
+        // the cluster's partial sums, added in rank order
+        cl_arrive();
+        cl_wait();
+        cg::cluster_group cluster = cg::this_cluster();
+        for (int m = etid; m < MT; m += TC_EPI_THREADS) {
+          float t = 0.f;
+          for (int p = 0; p < S; ++p) t += *cluster.map_shared_rank(psum + m, p);
+          rs[m] = 1.0f / sqrtf(t / (float)K + a.eps);
+        }
+      } else {
+        __syncwarp();
+        for (int m = lane; m < MT; m += 32)
+          if ((m & 3) == q) rs[m] = 1.0f / sqrtf(psum[m] / (float)K + a.eps);
       }
       named_sync(1, TC_EPI_THREADS);
     }
@@ -336,8 +382,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
 #pragma unroll
           for (int m = 0; m < 16; ++m)
             if (c16 + m < M)
-              a.y[(size_t)(c16 + m) * a.ldy + n] =
-                  __float2bfloat16_rn(tc_out<EPI>(a, v[m], EPI == 2 ? u[m] : 0.f, c16 + m, n));
+              a.y[(size_t)(r0 + c16 + m) * a.ldy + n] =
+                  __float2bfloat16_rn(tc_out<EPI>(a, v[m], EPI == 2 ? u[m] : 0.f, r0 + c16 + m, n));
         }
       }
       tc_before();
@@ -354,12 +400,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
       for (int c16 = 0; c16 < MT; c16 += 16) {
         float v[16];
         load16(tq, 0, c16, v);
+        float4* d = reinterpret_cast<float4*>(red + row * RP + c16);
 #pragma unroll
-        for (int m = 0; m < 16; ++m) red[row * RP + c16 + m] = v[m];
+        for (int m = 0; m < 4; ++m) d[m] = make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3]);
         if (EPI == 2) {
           load16(tq, 1, c16, v);
+          d = reinterpret_cast<float4*>(red + row * RP + MT + c16);
 #pragma unroll
-          for (int m = 0; m < 16; ++m) red[row * RP + MT + c16 + m] = v[m];
+          for (int m = 0; m < 4; ++m) d[m] = make_float4(v[4 * m], v[4 * m + 1], v[4 * m + 2], v[4 * m + 3]);
         }
       }
       tc_before();
@@ -383,22 +431,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     }
   }
   __syncwarp();
+  if (early) cl_wait();
   if (S > 1) {
     // every thread of every CTA of the cluster reaches both barriers, whatever happened above
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     if (warp >= 2 && nblk == 1) {
+      // unit uu, rows 4 mq .. 4 mq + 3: the S partial sums (all requested together), added in rank order
       const int u0 = UB * rank / S, nu = UB * (rank + 1) / S - u0;
-      for (int idx = tid - 64; idx < nu * M; idx += TC_EPI_THREADS) {
-        const int m = idx / nu, uu = u0 + idx % nu;
+      const int nq = (M + 3) / 4;
+      for (int idx = tid - 64; idx < nu * nq; idx += TC_EPI_THREADS) {
+        const int mq = idx / nu, uu = u0 + idx % nu;
         const int n = b0 * UB + uu;
-        float v = 0.f, u = 0.f;
-        for (int p = 0; p < S; ++p) {
-          const float* rp = cluster.map_shared_rank(red, p) + uu * RP + m;
-          v += rp[0];
-          if (EPI == 2) u += rp[MT];
+        float4 pv[TC_MAX_SPLIT], pu[TC_MAX_SPLIT];
+#pragma unroll
+        for (int p = 0; p < TC_MAX_SPLIT; ++p)
+          if (p < S) {
+            const float* rp = cluster.map_shared_rank(red, p) + uu * RP + mq * 4;
+            pv[p] = *reinterpret_cast<const float4*>(rp);
+            if (EPI == 2) pu[p] = *reinterpret_cast<const float4*>(rp + MT);
+          }
+        float v[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p = 0; p < TC_MAX_SPLIT; ++p)
+          if (p < S) {
+            v[0] += pv[p].x; v[1] += pv[p].y; v[2] += pv[p].z; v[3] += pv[p].w;
+            if (EPI == 2) {
+              u[0] += pu[p].x; u[1] += pu[p].y; u[2] += pu[p].z; u[3] += pu[p].w;
+            }
+          }
+        if (n < units) {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int m = mq * 4 + r;
+            if (m < M) a.y[(size_t)(r0 + m) * a.ldy + n] = __float2bfloat16_rn(tc_out<EPI>(a, v[r], u[r], r0 + m, n));
+          }
         }
-        if (n < units) a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(tc_out<EPI>(a, v, u, m, n));
       }
     }
     cluster.sync();
@@ -415,6 +483,9 @@ thread_local int t_split = 1;
 // matrices, the cluster split 9.2 / 17.2 / 14.6 / 27.4 us (a cluster of 8 large-smem CTAs waits for whole free SMs
 // of one GPC, so it cannot start while the previous kernel drains).
 int g_split_small = -1;
+// rows per row group for M > 16: 16 (default; groups of 16 rows side by side), or 32 / 64 / 128 (wide MMA tiles,
+// fewer groups)
+int g_group_rows = 16;
 
 template <int EPI, bool NORM, int MT>
 int launch_tc(const GemvArgs& g, int split, cudaStream_t st) {
@@ -434,7 +505,7 @@ int launch_tc(const GemvArgs& g, int split, cudaStream_t st) {
   if (fbh::tmap_box(&a.tx, g.x, g.M, g.K, 64, MT, tc_cols<EPI>() / 64, true, (long long)g.ldx) != FB_OK)
     return FB_ERR_UNSUPPORTED;
   constexpr int XB = tc_xbytes<EPI, MT>();
-  const size_t fixed = 1024 + (size_t)TC_MAX_STAGES * 3 * 8 + 4 * 8 + 16 + MT * 4;
+  const size_t fixed = 1024 + (size_t)TC_MAX_STAGES * 3 * 8 + 4 * 8 + 16 + 2 * MT * 4;
   int nst = (int)((227 * 1024 - fixed) / (TC_WBYTES + XB));
   if (nst > TC_MAX_STAGES) nst = TC_MAX_STAGES;
   a.nst = nst;
@@ -454,26 +525,30 @@ int launch_tc(const GemvArgs& g, int split, cudaStream_t st) {
     attr_done[dev] = (int)smem;
   }
   const int nb = (g.N + TC_BR - 1) / TC_BR;
-  const int grid = split > 1 ? nb * split : (nb < fbh::grid_sms() ? nb : fbh::grid_sms());
+  const int groups = (g.M + MT - 1) / MT;
+  int gsm = fbh::grid_sms() / groups;
+  if (gsm < 1) gsm = 1;
+  const int grid = split > 1 ? nb * split : (nb < gsm ? nb : gsm);
   void* args[] = {(void*)&a};
   t_split = split;
-  return fbh::launch_pdl((const void*)kern, dim3(grid), dim3(TC_THREADS), smem, st, args, true,
+  return fbh::launch_pdl((const void*)kern, dim3(grid, groups), dim3(TC_THREADS), smem, st, args, true,
                          split > 1 ? split : 0);
 }
 
 template <int EPI, bool NORM>
-int launch_mt(const GemvArgs& g, int split, cudaStream_t st) {
-  if (g.M <= 16) return launch_tc<EPI, NORM, 16>(g, split, st);
-  if (g.M <= 32) return launch_tc<EPI, NORM, 32>(g, split, st);
-  if (g.M <= 64) return launch_tc<EPI, NORM, 64>(g, split, st);
+int launch_mt(const GemvArgs& g, int mt, int split, cudaStream_t st) {
+  if (mt == 16) return launch_tc<EPI, NORM, 16>(g, split, st);
+  if (mt == 32) return launch_tc<EPI, NORM, 32>(g, split, st);
+  if (mt == 64) return launch_tc<EPI, NORM, 64>(g, split, st);
   return launch_tc<EPI, NORM, 128>(g, split, st);
 }
 
 }  // namespace
 
 // The tensor-core (tcgen05) GEMV when it applies: 1 <= M <= 128, K % 64 == 0, segment boundaries at multiples of
-// 128.  With at least a third of the grid's CTAs in 128-row blocks, each CTA takes whole blocks; with fewer blocks
-// the K range of each block is split over a cluster of S = min(8, grid / blocks, column stages) CTAs.  For M <= 16
+// 128.  M > 16 rows run as row groups of 16 (or of the wide tile set by gemv_tc_set_group_rows), each on an equal
+// share of the grid.  With at least a third of a group's CTAs in 128-row blocks, each CTA takes whole blocks; with
+// fewer blocks the K range of each block is split over a cluster of S = min(8, CTAs / blocks, column stages) CTAs.  For M <= 16
 // it then returns FB_ERR_UNSUPPORTED (the mma.sync kernel's 8-row split over every SM is faster) unless
 // FLASHB_TC_SPLIT=1.
 int gemv_tc(GemvArgs& g, int epi, bool norm, cudaStream_t st) {
@@ -484,8 +559,16 @@ int gemv_tc(GemvArgs& g, int epi, bool norm, cudaStream_t st) {
     const char* e = getenv("FLASHB_TC_SPLIT");
     g_split_small = (e && e[0] == '1') ? 1 : 0;
   }
+  int mt = 16;                             // rows per group
+  if (g.M > 16) {
+    mt = g_group_rows;
+    while (mt > 16 && mt / 2 >= g.M) mt /= 2;    // no wider than the rows need
+  }
+  const int groups = (g.M + mt - 1) / mt;
   const int nb = (g.N + TC_BR - 1) / TC_BR;
-  const int G = fbh::grid_sms();
+  int G = fbh::grid_sms() / groups;        // SMs per row group
+  if (G < 1) G = 1;
+  const int mrows = g.M < mt ? g.M : mt;   // rows of a group
   int split = 1;
   if (nb * 3 < G) {
     const int nkc = g.K / (epi == 2 ? 64 : 128);
@@ -493,17 +576,22 @@ int gemv_tc(GemvArgs& g, int epi, bool norm, cudaStream_t st) {
     if (split > TC_MAX_SPLIT) split = TC_MAX_SPLIT;
     if (split > nkc) split = nkc;
     if (split < 2) split = 1;
-    if (g.M <= 16 && (split == 1 || !g_split_small)) return FB_ERR_UNSUPPORTED;
+    if (mrows <= 16 && (split == 1 || !g_split_small)) return FB_ERR_UNSUPPORTED;
   }
-  if (epi == 0 && norm) return launch_mt<0, true>(g, split, st);
-  if (epi == 0) return launch_mt<0, false>(g, split, st);
-  if (epi == 1) return launch_mt<1, false>(g, split, st);
-  if (epi == 2 && norm) return launch_mt<2, true>(g, split, st);
-  if (epi == 2) return launch_mt<2, false>(g, split, st);
+  if (epi == 0 && norm) return launch_mt<0, true>(g, mt, split, st);
+  if (epi == 0) return launch_mt<0, false>(g, mt, split, st);
+  if (epi == 1) return launch_mt<1, false>(g, mt, split, st);
+  if (epi == 2 && norm) return launch_mt<2, true>(g, mt, split, st);
+  if (epi == 2) return launch_mt<2, false>(g, mt, split, st);
   return FB_ERR_UNSUPPORTED;
 }
 
 int gemv_tc_last_split() { return t_split; }
 void gemv_tc_set_split_small(int on) { g_split_small = on ? 1 : 0; }
+int gemv_tc_set_group_rows(int rows) {
+  if (rows != 16 && rows != 32 && rows != 64 && rows != 128) return FB_ERR_ARG;
+  g_group_rows = rows;
+  return FB_OK;
+}
 
 }  // namespace fb

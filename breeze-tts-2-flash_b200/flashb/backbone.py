@@ -227,8 +227,14 @@ def fused_decode_step(graph, advance=False):
                   st['cos_tab'], st['sin_tab'], st['x0'], st['cos'], st['sin'])
     layers = graph.static_cache.layers
     x = run_layers(st, st['x0'], [(L.keys, L.values) for L in layers], graph.attn_mask, graph.cache_position)
-    fx.lm_head_cfg(x, st['norm_w'], st['norm_eps'], st['lm_head32'], graph.guidance_scale,
-                   graph.hidden_buf.view(B, -1), graph.logits_buf, graph.cfg_logits_buf)
+    # flashb extension: ``graph.cfg_block`` rows per CFG block (several independent groups of streams in one graph,
+    # each laid out [cond..., uncond...]); the official graph is one block
+    blk = getattr(graph, 'cfg_block', B)
+    hb = graph.hidden_buf.view(B, -1)
+    for j in range(0, B, blk):
+        fx.lm_head_cfg(x[j:j + blk], st['norm_w'], st['norm_eps'], st['lm_head32'], graph.guidance_scale,
+                       hb[j:j + blk], graph.logits_buf[j:j + blk],
+                       graph.cfg_logits_buf[j // 2:(j + blk) // 2] if blk >= 2 else graph.cfg_logits_buf[j:j + 1])
 
 
 def install(api=None):

@@ -256,7 +256,7 @@ class _Slot:
     """``g`` streams decoded together: one backbone graph and one depth launch over 2 g rows laid out
     [cond_0 .. cond_{g-1}, uncond_0 .. uncond_{g-1}] (the CFG pair of stream k is rows k and k + g), which is the row
     order every kernel on the path already uses for B = 2 g."""
-    __slots__ = ('g', 'bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph', 'desc', 'lane')
+    __slots__ = ('g', 'bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph', 'desc', 'lane', 'r0')
 
 
 class sm_budget:
@@ -297,10 +297,16 @@ class FrameEngine:
     ``lanes`` > 1 splits the GPU: slot i belongs to lane i % lanes, every lane has its own CUDA stream, depth scratch
     and an SM budget of num_sms // lanes (grids of its persistent kernels, split counts of its attention), and
     ``step()`` runs the lanes side by side.  Every kernel here is latency-bound at decode sizes, so two half-GPU
-    lanes finish two slots sooner than one whole-GPU lane finishes them one after the other."""
+    lanes finish two slots sooner than one whole-GPU lane finishes them one after the other.
+
+    ``shared_backbone``: one backbone graph for the rows of every slot (slot i = rows [2 g i, 2 g (i + 1)), each
+    laid out [cond, uncond] with its own CFG block), captured on the whole GPU: its GEMVs run as row groups of 16
+    side by side in one launch each, which read every weight tile at about the same time (L2 serves all but the
+    first read), and its attention covers every row in one launch.  The depth launches stay per slot, on the
+    lanes.  ``step()`` then replays the one backbone graph and forks the lanes for the depth frames."""
 
     def __init__(self, bcfg: BackboneConfig, dcfg: DepthConfig, n_streams, prompt_len, max_frames, device='cuda',
-                 seed=0, depth_only=False, group=1, single_slot=False, lanes=1):
+                 seed=0, depth_only=False, group=1, single_slot=False, lanes=1, shared_backbone=False):
         """``depth_only``: no backbone (a random hidden state per stream feeds the depth frame) -- for timing or
         profiling the depth frame alone on a small device footprint."""
         if bcfg.codebooks - 1 > dcfg.n_decode or dcfg.embed_dim != bcfg.hidden:
@@ -333,7 +339,26 @@ class FrameEngine:
         self._gen = torch.Generator(device='cpu').manual_seed(seed + 17)
         self._first_bb = None
         self._seed = seed
-        self.streams = [self._slot(group, 1000 + seed + i) for i in range(n_streams // group)]
+        self.shared = bool(shared_backbone) and not depth_only
+        self.bb = None
+        self.bb_graph = None
+        n_slots = n_streams // group
+        if self.shared:
+            R = 2 * group * n_slots
+            if R > 128:
+                raise ValueError('shared_backbone: at most 128 backbone rows (64 streams) per graph')
+            self.bb = SyntheticBackboneGraph(bcfg, R, self.max_seq_len, dev, seed=seed + 2)
+            self.bb.cfg_block = 2 * group
+            self._first_bb = self.bb
+            self.bb.fill_kv(prompt_len, seed=1000 + seed)
+            self.bb.set_position(prompt_len - 1)
+            gen = self._gen
+            self.first_cb = torch.cat([torch.randint(0, self.n_valid, (group,), generator=gen).repeat(2)
+                                       for _ in range(n_slots)]).to(dev)
+            self.outtok = torch.cat([torch.randint(0, dcfg.codebook_size, (group, dcfg.n_decode),
+                                                   generator=gen).repeat(2, 1) for _ in range(n_slots)]).to(dev)
+        self.streams = [self._slot(group, 1000 + seed + i, row0=2 * group * i if self.shared else None)
+                        for i in range(n_slots)]
         for i, st in enumerate(self.streams):
             st.lane = i % lanes
             st.desc = self.lane_desc[st.lane]
@@ -347,10 +372,23 @@ class FrameEngine:
                 d.layers, d.embed, d.proj, d.normf, d.head_t, d.cos_tab, d.sin_tab, dcfg.eps, 128 ** -0.5,
                 dcfg.codebook_size, 2, dev)
 
-    def _slot(self, g, kv_seed):
+    def _slot(self, g, kv_seed, row0=None):
+        """A slot of g streams; row0: its first row in the shared backbone graph (None: a backbone of its own)."""
         dcfg, dev, gen = self.dcfg, self.device, self._gen
         st = _Slot()
         st.g = g
+        st.r0 = row0
+        if row0 is not None:
+            st.bb = self.bb
+            st.bh = self.bb.hidden_buf.view(self.bb.batch_size, -1)[row0:row0 + 2 * g]
+            st.first_cb = self.first_cb[row0:row0 + 2 * g]
+            st.outtok = self.outtok[row0:row0 + 2 * g]
+            st.tokbuf = torch.zeros(2 * g, dtype=torch.long, device=dev)
+            st.q = torch.empty(dcfg.n_decode, g, dcfg.vocab).exponential_(1, generator=gen).to(dev)
+            st.graph = None
+            st.desc = self.depth.desc
+            st.lane = 0
+            return st
         if self.depth_only:
             st.bb = None
             st.bh = torch.randn(2 * g, dcfg.embed_dim, generator=gen).to(torch.bfloat16).to(dev)
@@ -373,9 +411,23 @@ class FrameEngine:
     def _get(self, i):
         return self.single if i == 'single' else self.streams[i]
 
+    def shared_backbone_part(self):
+        """The shared backbone graph's body: frame ids of every row, one backbone step, codebook 0 per slot."""
+        bb, g = self.bb, self.group
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        check(lib().flashb_frame_ids(self.first_cb.data_ptr(), self.outtok.data_ptr(), self.dcfg.n_decode,
+                                     bb.batch_size, self.bcfg.codebooks, bb.input_ids_buf.data_ptr(), stream))
+        bb.decode_step(advance=True)
+        cl = bb.cfg_logits_buf
+        for st in self.streams:
+            check(lib().flashb_cb0_greedy(cl[st.r0 // 2:].data_ptr(), cl.stride(0), g, self.n_valid, 2 * g,
+                                          st.first_cb.data_ptr(), stream))
+
     # one frame, split into its backbone part (graph-capturable) and the depth launch
     def backbone_part(self, i):
         st = self._get(i)
+        if st.r0 is not None:
+            raise ValueError('slots of a shared backbone have no backbone part of their own (shared_backbone_part)')
         g = st.g
         stream = torch.cuda.current_stream(self.device).cuda_stream
         C = self.bcfg.codebooks
@@ -403,7 +455,24 @@ class FrameEngine:
                 self.depth_part(i)
             torch.cuda.synchronize(self.device)
             return
-        for i, st in self._slots()[:1] + ([self._slots()[-1]] if self.single is not None else []):
+        if self.shared:
+            self.shared_backbone_part()
+            for i in range(len(self.streams)):
+                with sm_budget(self.lane_sms):
+                    self.depth_part(i)
+            torch.cuda.synchronize(self.device)
+            self.bb.set_position(self.prompt_len - 1)
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    self.shared_backbone_part()
+                self.bb_graph = graph
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            torch.cuda.synchronize(self.device)
+        for i, st in ([] if self.shared else self._slots()[:1]) + (
+                [self._slots()[-1]] if self.single is not None else []):
             with sm_budget(self._budget(st)):
                 self.backbone_part(i)
                 self.depth_part(i)
@@ -413,6 +482,8 @@ class FrameEngine:
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
             for i, st in self._slots():
+                if st.r0 is not None:
+                    continue
                 graph = torch.cuda.CUDAGraph()
                 with sm_budget(self._budget(st)), torch.cuda.graph(graph, stream=side):
                     self.backbone_part(i)
@@ -431,6 +502,34 @@ class FrameEngine:
         'dd') of slot i with the CUDA stream it is issued on, and with ('end', None, stream) once per lane stream
         after its last part; ``after_part('dd', i, stream)`` after the depth part of slot i."""
         cur = torch.cuda.current_stream(self.device)
+        if self.shared:
+            # the backbone of every slot (one graph on the whole GPU), then the depth frames on the lanes
+            if before_part is not None:
+                before_part('bb', -1, cur)
+            if self.bb_graph is not None:
+                self.bb_graph.replay()
+            else:
+                self.shared_backbone_part()
+            if before_part is not None:
+                before_part('bbend', -1, cur)
+            lanes = self.lane_stream if self.lanes > 1 else [cur]
+            if self.lanes > 1 and fork:
+                for ls in lanes:
+                    ls.wait_stream(cur)
+            for i, st in enumerate(self.streams):
+                s = lanes[st.lane]
+                with torch.cuda.stream(s):
+                    if before_part is not None:
+                        before_part('dd', i, s)
+                    self.depth_part(i)
+                    if after_part is not None:
+                        after_part('dd', i, s)
+            for ls in lanes:
+                if before_part is not None:
+                    before_part('end', None, ls)
+                if self.lanes > 1 and join:
+                    cur.wait_stream(ls)
+            return
         if self.lanes == 1:
             for i in range(len(self.streams)):
                 self.frame(i, before_part, after_part)
@@ -451,6 +550,8 @@ class FrameEngine:
 
     def frame(self, i, before_part=None, after_part=None):
         st = self._get(i)
+        if st.r0 is not None:
+            raise ValueError('slots of a shared backbone run their frames through step()')
         stream = torch.cuda.current_stream(self.device)
         if before_part is not None and st.bb is not None:
             before_part('bb', i, stream)
@@ -467,7 +568,12 @@ class FrameEngine:
             after_part('dd', i, stream)
 
     def launches_per_frame(self):
-        """Kernel launches per slot frame (the same for any group size)."""
+        """Kernel launches per slot frame (the same for any group size); with a shared backbone, its launches shared
+        out over the slots (the graph's 2 + 5 x layers + 2 launches once, an LM head and a codebook-0 pick per
+        slot)."""
+        if self.shared:
+            n = len(self.streams)
+            return (launches_per_backbone_step(self.bcfg) - 1 + 2) / n + 2 + 1
         return launches_per_backbone_step(self.bcfg) + 1 + 3
 
     def frame_bytes(self):
@@ -475,6 +581,10 @@ class FrameEngine:
         if self.depth_only:
             return self.dcfg.n_decode * self.dcfg.step_weight_bytes()
         kv = int(self.streams[0].bb.cache_position.item()) + 1
+        if self.shared:
+            n = len(self.streams)
+            return backbone_step_bytes(self.bcfg, 2 * self.group * n, kv) / n + \
+                self.dcfg.n_decode * self.dcfg.step_weight_bytes()
         return backbone_step_bytes(self.bcfg, 2 * self.group, kv) + self.dcfg.n_decode * self.dcfg.step_weight_bytes()
 
 

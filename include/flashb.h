@@ -40,6 +40,10 @@ int flashb_device_error(int clear);
  * 1 = the mma.sync weight stream, 2 = the tcgen05 kernel (enough 128-row blocks for the grid); -1 before any.
  * For tests and profiling; no reference counterpart. */
 int flashb_gemv_last_path(void);
+/* Which kernel the calling thread's last fused decode attention launched: 0 = the split-KV scalar kernel, 1 = the
+ * tensor-core kernel (one CTA per row and KV head, when the rows alone fill the grid); -1 before any.  For tests;
+ * no reference counterpart. */
+int flashb_attn_last_path(void);
 /* CTAs per 128-row block of the calling thread's last tcgen05 GEMV launch: 1, or S >= 2 when the block's K range
  * was split over a thread-block cluster of S CTAs (too few blocks for the grid).  For tests; no reference
  * counterpart. */
@@ -47,6 +51,11 @@ int flashb_gemv_last_split(void);
 /* Split K over a cluster also for M <= 16 rows (1) or not (0, the default: the mma.sync kernel is faster there on
  * a whole B200).  Process-wide; no reference counterpart. */
 void flashb_set_gemv_split(int enable);
+/* Activation rows per row group of the tcgen05 GEMV when M > 16: 16 (the default: groups of 16 rows launched
+ * side by side, each on an equal share of the SMs, reading the same weight tiles at about the same time so that
+ * L2 serves all but the first), or 32 / 64 / 128 (wider MMA tiles, fewer groups).  Process-wide; no reference
+ * counterpart. */
+int flashb_set_gemv_group_rows(int rows);
 /* Programmatic dependent launch on (1, default) / off (0) for all later launches of this process. */
 void flashb_set_pdl(int enable);
 /* SM budget of the calling host thread (0, the default: every SM).  Launches issued later by this thread -- directly

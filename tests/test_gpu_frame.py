@@ -136,6 +136,61 @@ def test_frame_engine_matches_oracle_and_standalone_depth(group, lanes):
     assert device_error() == 0
 
 
+@pytest.mark.parametrize('group,slots,lanes', [(2, 3, 3), (1, 2, 1), (4, 2, 2), (8, 2, 2)])
+def test_frame_engine_shared_backbone_matches_oracle(group, slots, lanes):
+    """One backbone graph for every slot's rows (slot i = rows [2 g i, 2 g (i + 1)), its own CFG block; the GEMVs
+    as row groups of 16), the depth frames per slot on the lanes: every slot's block matches the oracle's step on
+    that block, and the depth launch consumed the block's hidden state and codebook 0."""
+    from flashb.engine import BackboneConfig, DepthConfig, FrameEngine
+    bcfg = BackboneConfig(hidden=512, layers=2, heads=8, kv_heads=2, ffn=1024, vocab=65, codebooks=7)
+    dcfg = DepthConfig(hidden=256, embed_dim=512, layers=2, heads=2, kv_heads=1, ffn=512, vocab=64,
+                       codebook_size=60, n_decode=6)
+    eng = FrameEngine(bcfg, dcfg, group * slots, 40, 4, seed=4, group=group, lanes=lanes, shared_backbone=True)
+    eng.capture()
+    bb = eng.bb
+    R, G2 = bb.batch_size, 2 * group
+    assert R == G2 * slots
+    W = _oracle_backbone(bb)
+    C = bcfg.codebooks
+    mask = np32(bb.attn_mask).copy()
+    pos = int(bb.cache_position.item())
+    pids = bb.position_ids.view(-1).cpu().numpy().copy()
+    for f in range(3):
+        kcs = [np32(L.keys).copy() for L in bb.static_cache.layers]
+        vcs = [np32(L.values).copy() for L in bb.static_cache.layers]
+        ids = np.concatenate([eng.first_cb.cpu().numpy()[:, None], eng.outtok.cpu().numpy()[:, :C - 1]], 1)
+        eng.step()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(bb.input_ids_buf.view(R, -1).cpu().numpy(), ids)
+        pos += 1
+        pids += 1
+        mask[..., pos] = 0.0
+        assert int(bb.cache_position.item()) == pos
+        gs = float(bb.guidance_scale.item())
+        g_h = np32(bb.hidden_buf).reshape(R, -1)
+        g_lg = bb.logits_buf.cpu().numpy()
+        g_cfg = bb.cfg_logits_buf.cpu().numpy()
+        for i, st in enumerate(eng.streams):
+            r = slice(st.r0, st.r0 + G2)
+            h, lg, _ = dec.backbone_step(W, ids[r], [k[r] for k in kcs], [v[r] for v in vcs], mask[r], pos, pids[r],
+                                         gs)
+            assert_close(g_h[r], h, tol=3e-2, what=f'slot {i} frame {f} hidden')
+            assert_close(g_lg[r], lg, what=f'slot {i} frame {f} logits')
+            cfg_blk = g_cfg[st.r0 // 2:st.r0 // 2 + group]
+            np.testing.assert_array_equal(cfg_blk, dec.cfg_combine(g_lg[r], group, gs))
+            cb0 = [ofr.greedy_cb0(cfg_blk[k], eng.n_valid) for k in range(group)]
+            np.testing.assert_array_equal(st.first_cb.cpu().numpy(), cb0 + cb0)
+            d = eng.depth
+            out = torch.zeros_like(st.outtok)
+            tb = torch.zeros_like(st.tokbuf)
+            st.desc.frame(st.first_cb, st.bh, tb, out, d.temperature[:group], d.top_k[:group], d.top_p[:group],
+                          d.do_sample[:group], d.guidance_scale[:group], st.q)
+            torch.cuda.synchronize()
+            assert torch.equal(out, st.outtok)
+    from flashb._native import device_error
+    assert device_error() == 0
+
+
 def test_frame_engine_free_running_lanes_equal_joined_steps():
     """Steps issued with the lanes joined only after the last one give the same tokens as steps joined one by one:
     each slot's frames stay in order on its lane stream, and no lane reads another's buffers."""

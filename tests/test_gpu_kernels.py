@@ -183,6 +183,45 @@ def test_attn_decode_fused(ops, NKV, S, pos):
     assert np.mean(np32(kc)[:, :, pos] == kc_ref[:, :, pos]) > 0.95
 
 
+@pytest.mark.parametrize('B,NKV,S,pos,budget', [(16, 4, 600, 515, 18), (128, 4, 576, 515, 0), (40, 8, 300, 63, 0),
+                                                 (24, 2, 200, 64, 8), (64, 4, 130, 0, 64), (128, 16, 96, 95, 0)])
+def test_attn_decode_fused_tensor_cores(ops, B, NKV, S, pos, budget):
+    """Many rows: one CTA per (row, KV head) with the two products of each 64-key chunk on mma.sync (the
+    tensor-core kernel) -- ragged last chunks, chunk-aligned positions, GQA groups 4, 2 and 1, left padding."""
+    _, ax = ops
+    NH = 16
+    qkv = randn((B, (NH + 2 * NKV) * 128), 80, 2.0)
+    qn, kn = randn((128,), 81, 0.1, 1.0), randn((128,), 82, 0.1, 1.0)
+    kc, vc = randn((B, NKV, S, 128), 83), randn((B, NKV, S, 128), 84)
+    kc[:, :, pos:] = 0
+    vc[:, :, pos:] = 0
+    from flashb.engine import rope_table
+    cos_t, sin_t = rope_table(1e6, 128, S, 'cuda')
+    pids = torch.tensor([max(0, pos - (b % 5)) for b in range(B)])
+    cos, sin = cos_t[pids].view(B, 1, 128).contiguous(), sin_t[pids].view(B, 1, 128).contiguous()
+    mask = _mask(B, S, tuple((min(b % 5, pos), pos + 1) for b in range(B)))
+    cp = torch.tensor([pos], dtype=torch.long, device='cuda')
+    out = torch.empty(B, 1, NH, 128, dtype=torch.bfloat16, device='cuda')
+    sc, cm, part, cnt = _attn_ws(B, NH, NKV, S)
+    kc_ref, vc_ref = np32(kc).copy(), np32(vc).copy()
+    from flashb._native import lib
+    try:
+        _budget(budget)
+        ax.attn_decode_fused(qkv, qn, kn, 1e-6, cos, sin, kc, vc, mask, cp, 128 ** -0.5, sc, cm, part, cnt, out)
+        torch.cuda.synchronize()
+        path = lib().flashb_attn_last_path()
+    finally:
+        _budget(0)
+    assert path == 1, f'expected the tensor-core kernel, got path {path}'
+    ref = dec.attn_decode_fused(np32(qkv), np32(qn), np32(kn), 1e-6, np32(cos), np32(sin), kc_ref, vc_ref,
+                                np32(mask), pos, 128 ** -0.5)
+    assert_close(np32(out), ref, what=f'tensor-core fused attn B={B}')
+    assert np.array_equal(np32(vc), vc_ref)
+    assert_close(np32(kc)[:, :, pos], kc_ref[:, :, pos], tol=1e-2, what='k write')
+    from flashb._native import device_error
+    assert device_error() == 0
+
+
 def test_attn_determinism(ops):
     _, ax = ops
     B, NH, NKV, S = 2, 16, 4, 2048
@@ -292,17 +331,22 @@ def _split():
     return lib().flashb_gemv_last_split()
 
 
-@pytest.mark.parametrize('kind,M,budget,split', [
-    # many activation rows (MMA N = 32, 64, 128), whole blocks per CTA
-    ('gateup', 128, 18, 1), ('gateup', 40, 32, 1), ('qkv', 128, 8, 1), ('qkv', 17, 8, 1), ('o', 64, 4, 1),
-    ('down', 100, 4, 1),
+@pytest.mark.parametrize('kind,M,budget,rows,split', [
+    # row groups of 16 side by side (blockIdx.y), each on its share of the SMs
+    ('gateup', 128, 18, 16, 1), ('gateup', 40, 32, 16, 1), ('qkv', 128, 8, 16, 1), ('qkv', 17, 8, 16, 1),
+    ('o', 64, 4, 16, 1), ('down', 100, 4, 16, 1), ('qkv', 128, 0, 16, 1), ('gateup', 128, 0, 16, 1),
+    ('o', 128, 0, 16, 1), ('down', 128, 0, 16, 1), ('down', 33, 0, 16, 3),
+    # wide tiles (MMA N = 32, 64, 128), whole blocks per CTA
+    ('gateup', 40, 32, 32, 1), ('down', 100, 8, 128, 1), ('qkv', 60, 8, 64, 1),
     # too few 128-row blocks for the grid: each block's K range split over a cluster
-    ('qkv', 128, 0, 6), ('o', 128, 0, 8), ('down', 128, 0, 8), ('gateup', 128, 0, 3), ('o', 2, 0, 8),
-    ('qkv', 16, 0, 6), ('down', 33, 0, 8), ('gateup', 2, 0, 3), ('odd', 70, 0, 8), ('o', 128, 64, 4)])
-def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, split):
-    """Up to 128 activation rows on the tcgen05 kernel (the weights streamed once for every row), and split K over
-    a thread-block cluster with the partial sums reduced through distributed shared memory (budget 0 = all SMs,
-    e.g. 148 on B200: 16 blocks of a 2048-row matrix become 16 clusters of 8; for M <= 16 only when switched on)."""
+    ('qkv', 128, 0, 128, 6), ('o', 128, 0, 128, 8), ('down', 128, 0, 128, 8), ('gateup', 128, 0, 128, 3),
+    ('o', 2, 0, 16, 8), ('qkv', 16, 0, 16, 6), ('down', 33, 0, 64, 8), ('gateup', 2, 0, 16, 3),
+    ('odd', 70, 0, 128, 8), ('o', 128, 64, 128, 4)])
+def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, rows, split):
+    """More than 16 activation rows on the tcgen05 kernel: row groups of 16 side by side (the default) or wide MMA
+    tiles of 32 / 64 / 128 rows, and split K over a thread-block cluster with the partial sums reduced through
+    distributed shared memory (budget 0 = all SMs, e.g. 148 on B200: 16 blocks of a 2048-row matrix become 16
+    clusters of 8; for groups of at most 16 rows only when switched on)."""
     fx, _ = ops
     K = {'down': 6144, 'odd': 1024}.get(kind, 2048)
     x = randn((M, K), 51)
@@ -313,7 +357,8 @@ def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, split):
     from flashb._native import lib
     try:
         _budget(budget)
-        lib().flashb_set_gemv_split(1 if M <= 16 and split > 1 else 0)
+        lib().flashb_set_gemv_split(1 if rows == 16 and split > 1 else 0)
+        assert lib().flashb_set_gemv_group_rows(rows) == 0
         if kind == 'gateup':
             Wg, Wu = randn((6144, K), 53, 0.02), randn((6144, K), 54, 0.02)
             y = torch.empty(M, 6144, dtype=torch.bfloat16, device='cuda')
@@ -345,9 +390,10 @@ def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, split):
     finally:
         _budget(0)
         lib().flashb_set_gemv_split(0)
+        lib().flashb_set_gemv_group_rows(16)
     assert path == 2, f'expected the tcgen05 kernel, got path {path}'
     assert got_split == split, f'expected split {split}, got {got_split}'
-    assert_close(np32(y), ref, what=f'tcgen05 {kind} M={M} split={split}')
+    assert_close(np32(y), ref, what=f'tcgen05 {kind} M={M} rows={rows} split={split}')
     assert torch.equal(y, y2)
     from flashb._native import device_error
     assert device_error() == 0
