@@ -67,9 +67,17 @@ struct AttnArgs {
   unsigned* err;
 };
 
-// RMSNorm over 128 dims + RoPE for one head; lane owns dims [4*lane, 4*lane + 4).
-__device__ __forceinline__ void norm_rope_head(const bf16* x, const bf16* w, float eps, const bf16* cs,
-                                               const bf16* sn, int lane, float out[4]) {
+// This lane's 4 dims [4 lane, 4 lane + 4) of a bf16 vector, as floats.
+__device__ __forceinline__ void load4(const bf16* p, int lane, float out[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p + lane * 4);
+  out[0] = lo_f(u.x);
+  out[1] = hi_f(u.x);
+  out[2] = lo_f(u.y);
+  out[3] = hi_f(u.y);
+}
+// RMSNorm over 128 dims + RoPE for one head with the lane's norm weights w, cos cs and sin sn already loaded.
+__device__ __forceinline__ void norm_rope_pre(const bf16* x, const float w[4], float eps, const float cs[4],
+                                              const float sn[4], int lane, float out[4]) {
   const int d0 = lane * 4;
   const uint2 xv = *reinterpret_cast<const uint2*>(x + d0);
   float v[4] = {lo_f(xv.x), hi_f(xv.x), lo_f(xv.y), hi_f(xv.y)};
@@ -78,12 +86,12 @@ __device__ __forceinline__ void norm_rope_head(const bf16* x, const bf16* w, flo
   const float r = 1.0f / sqrtf(ss / (float)AT_D + eps);
   float y[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) y[j] = rbf(b2f(w[d0 + j]) * rbf(v[j] * r));
+  for (int j = 0; j < 4; ++j) y[j] = rbf(w[j] * rbf(v[j] * r));
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const float partner = __shfl_xor_sync(FULL, y[j], 16);
     const float rot = lane < 16 ? -partner : partner;
-    out[j] = rbf(rbf(y[j] * b2f(cs[d0 + j])) + rbf(rot * b2f(sn[d0 + j])));
+    out[j] = rbf(rbf(y[j] * cs[j]) + rbf(rot * sn[j]));
   }
 }
 
@@ -138,6 +146,23 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
   if (FUSED && tid == 0) {
     for (int c = 0; c < min(2, nchunks); ++c) issue(c);
   }
+  // Fused: the norm weights, this row's cos / sin and the first chunk's mask values are read before
+  // griddepcontrol.wait.  In the decode step they are written by the host or by launches at least two back
+  // (embed_rope, step_advance), which have completed before this kernel can start (its predecessor, the q|k|v GEMV,
+  // lets it start only after its own griddepcontrol.wait); only q|k|v comes from the predecessor.
+  float wq4[4], wk4[4], cs4[4], sn4[4];
+  float m_first = -INFINITY;
+  if (FUSED) {
+    load4(a.qn_w, lane, wq4);
+    load4(a.kn_w, lane, wk4);
+    load4(a.cos + (size_t)b * a.cs_sb, lane, cs4);
+    load4(a.sin + (size_t)b * a.cs_sb, lane, sn4);
+    if (tid < AT_CHUNK && nchunks > 0 && tid < min(AT_CHUNK, p_end - p_begin)) {
+      const size_t mi = (size_t)b * a.m_sb + p_begin + tid;
+      m_first = a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi])
+                            : reinterpret_cast<const float*>(a.mask)[mi];
+    }
+  }
   pdl_wait();
   pdl_trigger();
   if (!FUSED && tid == 0) {
@@ -149,8 +174,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     const int hq = h * G + g;
     if (FUSED) {
       float qv[4];
-      norm_rope_head(a.qkv + (size_t)b * a.qkv_sb + (size_t)hq * AT_D, a.qn_w, a.eps, a.cos + (size_t)b * a.cs_sb,
-                     a.sin + (size_t)b * a.cs_sb, lane, qv);
+      norm_rope_pre(a.qkv + (size_t)b * a.qkv_sb + (size_t)hq * AT_D, wq4, a.eps, cs4, sn4, lane, qv);
 #pragma unroll
       for (int j = 0; j < 4; ++j) q_s[g][lane * 4 + j] = qv[j];
     } else {
@@ -163,8 +187,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
   if (owner) {
     if (warp == 0) {
       float kv[4];
-      norm_rope_head(a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AT_D, a.kn_w, a.eps,
-                     a.cos + (size_t)b * a.cs_sb, a.sin + (size_t)b * a.cs_sb, lane, kv);
+      norm_rope_pre(a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AT_D, wk4, a.eps, cs4, sn4, lane, kv);
 #pragma unroll
       for (int j = 0; j < 4; ++j) newk[lane * 4 + j] = __float2bfloat16_rn(kv[j]);
     } else if (warp == 1) {
@@ -209,7 +232,9 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     }
     if (tid < AT_CHUNK) {
       float m = -INFINITY;
-      if (tid < n) {
+      if (FUSED && c == 0) {
+        m = m_first;
+      } else if (tid < n) {
         const size_t mi = (size_t)b * a.m_sb + p0 + tid;
         m = a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi]) : reinterpret_cast<const float*>(a.mask)[mi];
       }

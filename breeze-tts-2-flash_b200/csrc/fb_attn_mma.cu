@@ -14,11 +14,14 @@
 //                                                          of the group padded to 8 columns)
 //   O^T[128 dims x 8 heads] += V^T[128 x 64] . P^T[64 x 8] (warp w: dims 32 w .. 32 w + 31)
 // K and V chunks arrive by TMA tensor copies in the 128-byte-swizzle layout (two 64-dimension blocks of 64 rows),
-// double-buffered on mbarriers, so that ldmatrix (plain for K, transposed for V) reads them without bank conflicts.
+// AM_STAGES chunks in flight on mbarriers, so that ldmatrix (plain for K, transposed for V) reads them without bank
+// conflicts (one contiguous 1-D bulk copy per chunk, read by ldmatrix with 8-way conflicts, measured 73 vs 44 us
+// at 128 rows).
 // The online softmax runs on the S fragments: per-head chunk maxima and sums through warp shuffles and a 4-warp
-// exchange in shared memory; P^T goes to shared memory as bf16 for the second product.  The first two chunks are
-// requested before griddepcontrol.wait (old cache rows are not written by the preceding kernel); the row written
-// at cache_pos is patched into the staged chunk.  Every wait is bounded.
+// exchange in shared memory; P^T goes to shared memory as bf16 for the second product.  The mask values of a
+// chunk are fetched by cp.async as far ahead as its K and V.  The first chunks are requested before
+// griddepcontrol.wait (old cache rows are not written by the preceding kernel); the row written at cache_pos is
+// patched into the staged chunk.  Every wait is bounded.
 #include "fb_common.cuh"
 
 namespace fb {
@@ -29,6 +32,12 @@ constexpr int AM_D = 128;
 constexpr int AM_THREADS = 128;
 constexpr int AM_CHUNK = 64;
 constexpr int AM_TILE = AM_CHUNK * AM_D * 2;      // bytes of one staged K or V chunk (16 KB)
+// chunks in flight per CTA: measured on B200 at 128 rows x 4 KV heads, two stages (three CTAs per SM) left every
+// chunk waiting ~2 us for its copy; three stages (two CTAs per SM) cover that latency
+#ifndef AM_STAGES
+#define AM_STAGES 3
+#endif
+
 
 struct alignas(64) AttnMmaArgs {
   CUtensorMap tk, tv;      // the caches as [2 blocks of 64 dims][B * NKV * S rows][64], boxes of 64 rows x 2 blocks
@@ -62,6 +71,13 @@ __device__ __forceinline__ void am_tma(void* dst, const CUtensorMap* map, int ro
 __device__ __forceinline__ void fence_proxy_async_cta() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// 4-byte asynchronous copy global -> shared of `bytes` (0, 2 or 4) source bytes, the rest zero-filled.
+__device__ __forceinline__ void am_cp4(void* dst, const void* src, int bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void am_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void am_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 __device__ __forceinline__ void am_ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -85,9 +101,18 @@ __device__ __forceinline__ uint32_t am_off(int r, int u) {
   return (uint32_t)(((u >> 3) << 13) + (r << 7) + ((((u & 7) ^ (r & 7))) << 4));
 }
 
-// RMSNorm over 128 dims + RoPE for one head; lane owns dims [4 lane, 4 lane + 4) (the scalar kernel's helper).
-__device__ __forceinline__ void am_norm_rope(const bf16* x, const bf16* w, float eps, const bf16* cs, const bf16* sn,
-                                             int lane, float out[4]) {
+// This lane's 4 dims [4 lane, 4 lane + 4) of a bf16 vector, as floats.
+__device__ __forceinline__ void am_load4(const bf16* p, int lane, float out[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p + lane * 4);
+  out[0] = lo_f(u.x);
+  out[1] = hi_f(u.x);
+  out[2] = lo_f(u.y);
+  out[3] = hi_f(u.y);
+}
+// RMSNorm over 128 dims + RoPE for one head with the lane's norm weights, cos and sin already loaded (the scalar
+// kernel's operation order).
+__device__ __forceinline__ void am_norm_rope(const bf16* x, const float w[4], float eps, const float cs[4],
+                                             const float sn[4], int lane, float out[4]) {
   const int d0 = lane * 4;
   const uint2 xv = *reinterpret_cast<const uint2*>(x + d0);
   float v[4] = {lo_f(xv.x), hi_f(xv.x), lo_f(xv.y), hi_f(xv.y)};
@@ -96,12 +121,12 @@ __device__ __forceinline__ void am_norm_rope(const bf16* x, const bf16* w, float
   const float r = 1.0f / sqrtf(ss / (float)AM_D + eps);
   float y[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) y[j] = rbf(b2f(w[d0 + j]) * rbf(v[j] * r));
+  for (int j = 0; j < 4; ++j) y[j] = rbf(w[j] * rbf(v[j] * r));
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const float partner = __shfl_xor_sync(FULL, y[j], 16);
     const float rot = lane < 16 ? -partner : partner;
-    out[j] = rbf(rbf(y[j] * b2f(cs[d0 + j])) + rbf(rot * b2f(sn[d0 + j])));
+    out[j] = rbf(rbf(y[j] * cs[j]) + rbf(rot * sn[j]));
   }
 }
 
@@ -110,13 +135,13 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
   extern __shared__ __align__(1024) unsigned char am_smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(am_smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sK = sm;                       // [2][16 KB]
-  unsigned char* sV = sm + 2 * AM_TILE;         // [2][16 KB]
-  __shared__ __align__(8) uint64_t full[2];
+  unsigned char* sK = sm;                       // [AM_STAGES][16 KB]
+  unsigned char* sV = sm + AM_STAGES * AM_TILE; // [AM_STAGES][16 KB]
+  __shared__ __align__(8) uint64_t full[AM_STAGES];
   __shared__ __align__(16) bf16 qs[8][AM_D];    // query heads of the group (rows >= G zero)
   __shared__ __align__(16) bf16 ps[8][AM_CHUNK + 8];   // P^T of the chunk: [head][key], bf16
   __shared__ float red_m[4][8], red_l[4][8];
-  __shared__ float mrow[AM_CHUNK];
+  __shared__ __align__(16) unsigned char mring[AM_STAGES][AM_CHUNK * 4];   // the chunks' mask values (bf16 or fp32)
   __shared__ __align__(16) bf16 newk[AM_D];
   __shared__ __align__(16) bf16 newv[AM_D];
 
@@ -130,21 +155,49 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
   const int row0 = (b * NKV + h) * S;           // first cache row of (b, h) in the tensor maps' row space
 
   if (tid == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
+    for (int i = 0; i < AM_STAGES; ++i) mbar_init(&full[i], 1);
     fence_mbar_init();
     asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tk) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tv) : "memory");
   }
   __syncthreads();
   auto issue = [&](int c) {
-    const int s = c & 1;
+    const int s = c % AM_STAGES;
     mbar_arrive_expect_tx(&full[s], 2u * AM_TILE);
     am_tma(sK + s * AM_TILE, &a.tk, row0 + c * AM_CHUNK, &full[s]);
     am_tma(sV + s * AM_TILE, &a.tv, row0 + c * AM_CHUNK, &full[s]);
   };
+  // mask values of chunk c into mring[c % AM_STAGES] by cp.async, one commit group per chunk (empty past the end),
+  // requested as far ahead as the K / V copies
+  const unsigned char* mrow_g = reinterpret_cast<const unsigned char*>(a.mask) +
+                                (size_t)b * a.m_sb * (a.mask_bf16 ? 2 : 4);
+  auto issue_mask = [&](int c) {
+    const int s = c % AM_STAGES, p0 = c * AM_CHUNK;
+    if (c < nchunks) {
+      if (a.mask_bf16) {
+        if (tid < AM_CHUNK / 2) {
+          const int e = p0 + 2 * tid;
+          const int bytes = e < len ? (e + 1 < len ? 4 : 2) : 0;
+          am_cp4(&mring[s][4 * tid], mrow_g + (size_t)(e < len ? e : 0) * 2, bytes);
+        }
+      } else if (tid < AM_CHUNK) {
+        const int e = p0 + tid;
+        am_cp4(&mring[s][4 * tid], mrow_g + (size_t)(e < len ? e : 0) * 4, e < len ? 4 : 0);
+      }
+    }
+    am_cp_commit();
+  };
   if (tid == 0)
-    for (int c = 0; c < min(2, nchunks); ++c) issue(c);
+    for (int c = 0; c < min(AM_STAGES, nchunks); ++c) issue(c);
+  // the norm weights, this row's cos / sin and the mask are read before griddepcontrol.wait: in the decode step
+  // they are written by the host or by launches at least two back (embed_rope, step_advance), complete before this
+  // kernel can start; only q|k|v comes from the predecessor
+  for (int c = 0; c < AM_STAGES; ++c) issue_mask(c);
+  float wq4[4], wk4[4], cs4[4], sn4[4];
+  am_load4(a.qn_w, lane, wq4);
+  am_load4(a.kn_w, lane, wk4);
+  am_load4(a.cos + (size_t)b * a.cs_sb, lane, cs4);
+  am_load4(a.sin + (size_t)b * a.cs_sb, lane, sn4);
   pdl_wait();
   pdl_trigger();
 
@@ -152,8 +205,7 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
   for (int g = warp; g < 8; g += AM_THREADS / 32) {
     if (g < G) {
       float qv[4];
-      am_norm_rope(a.qkv + (size_t)b * a.qkv_sb + (size_t)(h * G + g) * AM_D, a.qn_w, a.eps,
-                   a.cos + (size_t)b * a.cs_sb, a.sin + (size_t)b * a.cs_sb, lane, qv);
+      am_norm_rope(a.qkv + (size_t)b * a.qkv_sb + (size_t)(h * G + g) * AM_D, wq4, a.eps, cs4, sn4, lane, qv);
 #pragma unroll
       for (int j = 0; j < 4; ++j) qs[g][lane * 4 + j] = __float2bfloat16_rn(qv[j]);
     } else {
@@ -164,20 +216,13 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
   if (write) {
     if (warp == 0) {
       float kv[4];
-      am_norm_rope(a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AM_D, a.kn_w, a.eps,
-                   a.cos + (size_t)b * a.cs_sb, a.sin + (size_t)b * a.cs_sb, lane, kv);
+      am_norm_rope(a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AM_D, wk4, a.eps, cs4, sn4, lane, kv);
 #pragma unroll
       for (int j = 0; j < 4; ++j) newk[lane * 4 + j] = __float2bfloat16_rn(kv[j]);
     } else if (warp == 1) {
       const bf16* vp = a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + NKV + h) * AM_D;
       *reinterpret_cast<uint2*>(&newv[lane * 4]) = *reinterpret_cast<const uint2*>(vp + lane * 4);
     }
-  }
-  // the first chunk's mask values
-  float mnext = -INFINITY;
-  if (tid < AM_CHUNK && tid < len) {
-    const size_t mi = (size_t)b * a.m_sb + tid;
-    mnext = a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi]) : reinterpret_cast<const float*>(a.mask)[mi];
   }
   __syncthreads();
   if (write) {
@@ -202,18 +247,11 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
   bool ok = true;
   int cfail = 0;
   for (int c = 0; c < nchunks; ++c) {
-    const int s = c & 1;
+    const int s = c % AM_STAGES;
     const int p0 = c * AM_CHUNK;
     const int n = min(AM_CHUNK, len - p0);
-    if (tid < AM_CHUNK) mrow[tid] = mnext;
-    // next chunk's mask values, in flight while this chunk is processed
-    mnext = -INFINITY;
-    if (tid < AM_CHUNK && p0 + AM_CHUNK + tid < len) {
-      const size_t mi = (size_t)b * a.m_sb + p0 + AM_CHUNK + tid;
-      mnext = a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi])
-                          : reinterpret_cast<const float*>(a.mask)[mi];
-    }
-    ok = __syncthreads_and(mbar_wait(&full[s], (c >> 1) & 1, a.err));
+    am_cp_wait<AM_STAGES - 1>();     // this thread's mask copies of chunk c have landed
+    ok = __syncthreads_and(mbar_wait(&full[s], (c / AM_STAGES) & 1, a.err));
     if (!ok) {
       cfail = c;
       break;
@@ -250,7 +288,9 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int key = k0 + (i >> 1) * 8, hh = h0 + (i & 1);
-      const float m = key < n ? mrow[key] : -INFINITY;
+      const float m = key >= n ? -INFINITY
+                               : (a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(mring[s])[key])
+                                              : reinterpret_cast<const float*>(mring[s])[key]);
       float v = -INFINITY;
       if (key < n && hh < G && m > -1e30f) {
         v = rbf(rbf(sc[i]) * a.scaling);
@@ -328,15 +368,18 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
       }
     }
     __syncthreads();   // the stage, ps and red_* are reused
-    if (tid == 0 && c + 2 < nchunks) {
+    if (tid == 0 && c + AM_STAGES < nchunks) {
       fence_proxy_async_cta();   // this stage's generic writes (patch, zeroed rows) before the copy overwrites it
-      issue(c + 2);
+      issue(c + AM_STAGES);
     }
+    issue_mask(c + AM_STAGES);
   }
   if (!ok) {
     // a wait gave up: the error word is set; never leave with copies in flight into this CTA's shared memory
+    am_cp_wait<0>();
     if (tid == 0)
-      for (int c = cfail; c < min(cfail + 2, nchunks); ++c) mbar_wait(&full[c & 1], (c >> 1) & 1, a.err);
+      for (int c = cfail; c < min(cfail + AM_STAGES, nchunks); ++c)
+        mbar_wait(&full[c % AM_STAGES], (c / AM_STAGES) & 1, a.err);
     return;
   }
   // ---- out[b, h G + head, dim] = O / l
@@ -363,6 +406,8 @@ int attn_mma_fused(const bf16* qkv, long qkv_sb, const bf16* qn_w, const bf16* k
                    bf16* out, cudaStream_t st) {
   const int G = NH / NKV;
   if (G > 8 || (G & (G - 1)) || c_sh != (long)S * AM_D || c_sb != c_sh * NKV) return FB_ERR_UNSUPPORTED;
+  // the mask rows are copied 4 bytes at a time
+  if ((reinterpret_cast<uintptr_t>(mask) & 3) || (mask_bf16 && (m_sb & 1))) return FB_ERR_UNSUPPORTED;
   AttnMmaArgs a{};
   const long long rows = (long long)B * NKV * S;
   if (fbh::tmap_box(&a.tk, kc, rows, AM_D, 64, AM_CHUNK, 2, true) != FB_OK ||
@@ -373,7 +418,7 @@ int attn_mma_fused(const bf16* qkv, long qkv_sb, const bf16* qn_w, const bf16* k
   a.mask = mask; a.m_sb = m_sb; a.mask_bf16 = mask_bf16; a.cache_pos = cache_pos; a.scaling = scaling;
   a.out = out; a.S = S; a.NH = NH; a.NKV = NKV;
   a.err = fbh::device_err_ptr();
-  const size_t smem = 4 * (size_t)AM_TILE + 1024;
+  const size_t smem = 2 * AM_STAGES * (size_t)AM_TILE + 1024;
   const void* kern = nullptr;
   switch (G) {
     case 1: kern = (const void*)attn_mma_kernel<1>; break;
