@@ -54,6 +54,7 @@ struct alignas(64) AttnMmaArgs {
   const void* mask;
   long m_sb;
   int mask_bf16;
+  int mask_async;          // 1: mask rows 4-byte aligned, copied by cp.async; 0: plain loads
   const long long* cache_pos;
   float scaling;
   bf16* out;
@@ -173,7 +174,17 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
                                 (size_t)b * a.m_sb * (a.mask_bf16 ? 2 : 4);
   auto issue_mask = [&](int c) {
     const int s = c % AM_STAGES, p0 = c * AM_CHUNK;
-    if (c < nchunks) {
+    if (c < nchunks && !a.mask_async) {
+      // rows not 4-byte aligned (odd stride of a bf16 mask): plain loads, this thread waits for its value
+      if (tid < AM_CHUNK) {
+        const int e = p0 + tid;
+        if (a.mask_bf16)
+          reinterpret_cast<bf16*>(mring[s])[tid] =
+              e < len ? reinterpret_cast<const bf16*>(mrow_g)[e] : __float2bfloat16_rn(0.f);
+        else
+          reinterpret_cast<float*>(mring[s])[tid] = e < len ? reinterpret_cast<const float*>(mrow_g)[e] : 0.f;
+      }
+    } else if (c < nchunks) {
       if (a.mask_bf16) {
         if (tid < AM_CHUNK / 2) {
           const int e = p0 + 2 * tid;
@@ -406,8 +417,8 @@ int attn_mma_fused(const bf16* qkv, long qkv_sb, const bf16* qn_w, const bf16* k
                    bf16* out, cudaStream_t st) {
   const int G = NH / NKV;
   if (G > 8 || (G & (G - 1)) || c_sh != (long)S * AM_D || c_sb != c_sh * NKV) return FB_ERR_UNSUPPORTED;
-  // the mask rows are copied 4 bytes at a time
-  if ((reinterpret_cast<uintptr_t>(mask) & 3) || (mask_bf16 && (m_sb & 1))) return FB_ERR_UNSUPPORTED;
+  // the mask rows are copied 4 bytes at a time when 4-byte aligned
+  const int mask_async = !((reinterpret_cast<uintptr_t>(mask) & 3) || (mask_bf16 && (m_sb & 1)));
   AttnMmaArgs a{};
   const long long rows = (long long)B * NKV * S;
   if (fbh::tmap_box(&a.tk, kc, rows, AM_D, 64, AM_CHUNK, 2, true) != FB_OK ||
@@ -415,7 +426,8 @@ int attn_mma_fused(const bf16* qkv, long qkv_sb, const bf16* qn_w, const bf16* k
     return FB_ERR_UNSUPPORTED;
   a.qkv = qkv; a.qkv_sb = qkv_sb; a.qn_w = qn_w; a.kn_w = kn_w; a.eps = eps;
   a.cos = cos; a.sin = sin; a.cs_sb = cs_sb; a.kc = kc; a.vc = vc;
-  a.mask = mask; a.m_sb = m_sb; a.mask_bf16 = mask_bf16; a.cache_pos = cache_pos; a.scaling = scaling;
+  a.mask = mask; a.m_sb = m_sb; a.mask_bf16 = mask_bf16; a.mask_async = mask_async;
+  a.cache_pos = cache_pos; a.scaling = scaling;
   a.out = out; a.S = S; a.NH = NH; a.NKV = NKV;
   a.err = fbh::device_err_ptr();
   const size_t smem = 2 * AM_STAGES * (size_t)AM_TILE + 1024;

@@ -321,7 +321,8 @@ class FrameEngine:
         nsm = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == 'cuda' else 0
         self.lane_sms = 0 if lanes == 1 else nsm // lanes
         self.prompt_len = prompt_len
-        self.max_seq_len = prompt_len + max_frames + 2
+        # a multiple of 8 positions: the mask rows (bf16, one per position) start 16-byte aligned
+        self.max_seq_len = (prompt_len + max_frames + 2 + 7) // 8 * 8
         self.n_valid = min(dcfg.codebook_size, bcfg.vocab)
         self.depth_only = depth_only
         self.depth = SyntheticDepth(dcfg, batch=2 * group, device=dev, seed=seed + 3)

@@ -184,10 +184,12 @@ def test_attn_decode_fused(ops, NKV, S, pos):
 
 
 @pytest.mark.parametrize('B,NKV,S,pos,budget', [(16, 4, 600, 515, 18), (128, 4, 576, 515, 0), (40, 8, 300, 63, 0),
-                                                 (24, 2, 200, 64, 8), (64, 4, 130, 0, 64), (128, 16, 96, 95, 0)])
+                                                 (24, 2, 200, 64, 8), (64, 4, 130, 0, 64), (128, 16, 96, 95, 0),
+                                                 (32, 4, 301, 150, 16)])
 def test_attn_decode_fused_tensor_cores(ops, B, NKV, S, pos, budget):
     """Many rows: one CTA per (row, KV head) with the two products of each 64-key chunk on mma.sync (the
-    tensor-core kernel) -- ragged last chunks, chunk-aligned positions, GQA groups 4, 2 and 1, left padding."""
+    tensor-core kernel) -- ragged last chunks, chunk-aligned positions, GQA groups 4, 2 and 1, left padding, and an
+    odd mask row stride (S = 301: mask rows not 4-byte aligned, read with plain loads)."""
     _, ax = ops
     NH = 16
     qkv = randn((B, (NH + 2 * NKV) * 128), 80, 2.0)
