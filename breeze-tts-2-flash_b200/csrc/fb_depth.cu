@@ -397,7 +397,7 @@ __host__ __device__ constexpr size_t dd_attn_bytes(int bc, int NH, int NKV, int 
 // The step's token at position `pos` of every batch row, all NH query heads, over the layer's cached positions
 // 0..pos, computed by every CTA (the o-projection that follows needs every row).  Batch rows go in chunks of
 // a.att_bc; per chunk one round trip stages q, K and V in shared memory with cp.async, then scores (one thread per
-// (row, key)), softmax (one thread per row) and p.V (one thread per (row, 8 dims)).  Eager rounding:
+// (row, key)), softmax (a warp per row) and p.V (one thread per (row, 8 dims)).  Eager rounding:
 // s = bf16(bf16(q.k) * scaling), p = bf16(softmax_fp32(s)), out = bf16(sum p v).  Output rows go to xs (the
 // o-projection input); `att` is the staging area.
 template <int G>
@@ -453,17 +453,15 @@ __device__ __noinline__ void dd_attention(const DDArgs& a, int l, int pos, unsig
       ps[row * 32 + j] = rbf(rbf(d) * a.scaling);
     }
     named_sync(1, PK_CONSUMERS);
-    if (tid < nrow) {
-      float* pr = ps + tid * 32;
-      float mx = -INFINITY;
-      for (int j = 0; j < np; ++j) mx = fmaxf(mx, pr[j]);
-      float den = 0.f;
-      for (int j = 0; j < np; ++j) {
-        const float e = expf(pr[j] - mx);
-        pr[j] = e;
-        den += e;
-      }
-      for (int j = 0; j < np; ++j) pr[j] = rbf(pr[j] / den);
+    // softmax per row: a warp per row, a lane per key (np <= 32)
+    for (int row = tid >> 5; row < nrow; row += PK_CONSUMERS / 32) {
+      float* pr = ps + row * 32;
+      const int lane = tid & 31;
+      const float v = lane < np ? pr[lane] : -INFINITY;
+      const float mx = warp_max(v);
+      const float e = lane < np ? expf(v - mx) : 0.f;
+      const float den = warp_sum(e);
+      if (lane < np) pr[lane] = rbf(e / den);
     }
     named_sync(1, PK_CONSUMERS);
     for (int i = tid; i < nrow * 16; i += PK_CONSUMERS) {
@@ -552,18 +550,16 @@ __device__ __noinline__ void dd_attention_pairs(const DDArgs& a, int l, int pos,
     ps_of(k)[hq * 32 + j] = rbf(rbf(d) * scaling);
   }
   named_sync(1, PK_CONSUMERS);
-  if (tid < npair * G) {
-    const int k = tid / G, hq = tid - k * G;
+  // softmax per (pair, q head) row: a warp per row, a lane per key (np <= 32)
+  for (int row = tid >> 5; row < npair * G; row += PK_CONSUMERS / 32) {
+    const int k = row / G, hq = row - k * G;
     float* pr = ps_of(k) + hq * 32;
-    float mx = -INFINITY;
-    for (int j = 0; j < np; ++j) mx = fmaxf(mx, pr[j]);
-    float den = 0.f;
-    for (int j = 0; j < np; ++j) {
-      const float e = expf(pr[j] - mx);
-      pr[j] = e;
-      den += e;
-    }
-    for (int j = 0; j < np; ++j) pr[j] = rbf(pr[j] / den);
+    const int lane = tid & 31;
+    const float v = lane < np ? pr[lane] : -INFINITY;
+    const float mx = warp_max(v);
+    const float e = lane < np ? expf(v - mx) : 0.f;
+    const float den = warp_sum(e);
+    if (lane < np) pr[lane] = rbf(e / den);
   }
   named_sync(1, PK_CONSUMERS);
   for (int i = tid; i < npair * G * 16; i += PK_CONSUMERS) {
