@@ -74,7 +74,8 @@ def peaks():
 
 # ------------------------------------------------------------------------------------------------ clocks
 class Clocks:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    """nvidia-smi sampled every 100 ms while the timed region runs: started ahead (it takes a few hundred ms to print
+    its first sample), and only the samples after mark() -- the start of the timed region -- are kept."""
     FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
@@ -88,9 +89,29 @@ class Clocks:
             self.out = open(self.path, 'w')
             self.proc = subprocess.Popen(['nvidia-smi', '-i', ','.join(str(i) for i in gpu_ids),
                                           f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                                          '-lms', '200'], stdout=self.out, stderr=subprocess.DEVNULL)
+                                          '-lms', '100'], stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+        self.skip = 0
+
+    def _lines(self):
+        try:
+            with open(self.path) as f:
+                return sum(1 for _ in f)
+        except Exception:
+            return 0
+
+    def wait_started(self, timeout=3.0):
+        """Returns once nvidia-smi has printed a sample (or after `timeout` seconds)."""
+        t0 = time.time()
+        while self.proc is not None and self._lines() == 0 and time.time() - t0 < timeout:
+            time.sleep(0.02)
+
+    def mark(self):
+        """The timed region starts now: earlier samples are dropped."""
+        if self.proc is not None:
+            self.out.flush()
+            self.skip = self._lines()
 
     def stop(self):
         if self.proc is None:
@@ -110,7 +131,7 @@ class Clocks:
         os.unlink(self.path)
         if not rows:
             return None
-        rows = rows[1:] or rows          # the first sample may predate the load
+        rows = rows[self.skip:] or rows[-1:]   # samples from the timed region (else the last one)
         sm = sorted(float(r[1]) for r in rows if r[1].replace('.', '').isdigit())
         names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == 'active'})
@@ -330,8 +351,12 @@ def main():
     gpu_ids = [int(x) for x in os.environ['CUDA_VISIBLE_DEVICES'].split(',')] \
         if os.environ.get('CUDA_VISIBLE_DEVICES', '').replace(',', '').isdigit() else list(range(world))
     clocks = Clocks(gpu_ids[:world]) if rank == 0 else None
+    if clocks:
+        clocks.wait_started()
     evs = []
     barrier()
+    if clocks:
+        clocks.mark()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
