@@ -85,7 +85,11 @@ int flashb_attn_decode(const void* q, int64_t q_sb, int64_t q_sh, const void* kc
 /* Replaces attn_decode_fused (flash/csrc/bb_attn.cu:433-460): qkv [B, (NH + 2 NKV) * D] raw q|k|v projections
  * (row stride qkv_sb); Qwen3 q_norm/k_norm (weights qn_w/kn_w [D], eps) + RoPE with cos/sin [B, 1, D] bf16 (row
  * stride cs_sb); writes the new k (normed, roped) and v at slot cache_pos[0] (device int64) of kc/vc, then attends
- * over slots [0, min(S, cache_pos + 1)) under the mask. */
+ * over slots [0, min(S, cache_pos + 1)) under the mask.  Launched with programmatic dependent launch, the kernel
+ * reads cache_pos, the norm weights, cos/sin and the mask before the previous kernel in the stream has finished;
+ * only qkv may come from that previous kernel.  The others must be written at least two launches earlier (as
+ * embed_rope and step_advance are in the decode step), on the host, or by a kernel that does not allow dependent
+ * launch (flashb_set_pdl(0) turns dependent launch off). */
 int flashb_attn_decode_fused(const void* qkv, int64_t qkv_sb, const void* qn_w, const void* kn_w, float eps,
                              const void* cos, const void* sin, int64_t cs_sb, void* kc, void* vc, int64_t c_sb,
                              int64_t c_sh, int B, int NH, int NKV, int S, int D, const void* mask, int mask_is_bf16,
