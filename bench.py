@@ -55,7 +55,7 @@ def args_():
     p.add_argument('--lanes', type=int, default=8,
                    help='GPU lanes: slots run on this many CUDA streams side by side, each sized for 1/lanes of the SMs')
     p.add_argument('--backbone', default='shared', choices=['shared', 'lanes'],
-                   help='shared: one backbone graph for every slot on the whole GPU (row groups of 16 per GEMV '
+                   help='shared: one backbone graph for every slot on the whole GPU (row groups of 64 per GEMV '
                         'launch); lanes: a backbone graph per slot on its lane')
     p.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample length')
     p.add_argument('--no-cpu-baseline', action='store_true')
@@ -487,7 +487,7 @@ def main():
                        f'codebook-0 + 16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9); '
                        f'{a.group} stream(s) per depth launch share the weight reads; {lanes} lane(s) of the GPU side '
                        f'by side; ' + (f'one backbone graph for all {my_streams} streams ({2 * my_streams} rows, GEMVs '
-                                       f'as row groups of 16)' if eng.shared else
+                                       f'as row groups of 64)' if eng.shared else
                                        f'a backbone graph per {a.group} streams on its lane'),
               'depth': 'depth frame only (4 layers, hidden 1024, 16 codebooks of 2048, CFG + top-k 50 sampling)',
               'backbone': 'backbone decode step only (28 layers, hidden 2048, B=2, KV 512+t) + frame link'}[case]

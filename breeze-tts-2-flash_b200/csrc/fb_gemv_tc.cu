@@ -483,9 +483,9 @@ thread_local int t_split = 1;
 // matrices, the cluster split 9.2 / 17.2 / 14.6 / 27.4 us (a cluster of 8 large-smem CTAs waits for whole free SMs
 // of one GPC, so it cannot start while the previous kernel drains).
 int g_split_small = -1;
-// rows per row group for M > 16: 16 (default; groups of 16 rows side by side), or 32 / 64 / 128 (wide MMA tiles,
-// fewer groups)
-int g_group_rows = 16;
+// rows per row group for M > 16: 64 (default), or 16 / 32 / 128.  Measured on B200 in the shared backbone step
+// (128 rows, 148 SMs): 16 -> 5.92 ms, 32 -> 5.71, 64 -> 5.32, 128 -> 7.04 ms per step.
+int g_group_rows = 64;
 
 template <int EPI, bool NORM, int MT>
 int launch_tc(const GemvArgs& g, int split, cudaStream_t st) {
@@ -546,7 +546,7 @@ int launch_mt(const GemvArgs& g, int mt, int split, cudaStream_t st) {
 }  // namespace
 
 // The tensor-core (tcgen05) GEMV when it applies: 1 <= M <= 128, K % 64 == 0, segment boundaries at multiples of
-// 128.  M > 16 rows run as row groups of 16 (or of the wide tile set by gemv_tc_set_group_rows), each on an equal
+// 128.  M > 16 rows run as row groups of 64 rows (or of the width set by gemv_tc_set_group_rows), each on an equal
 // share of the grid.  With at least a third of a group's CTAs in 128-row blocks, each CTA takes whole blocks; with
 // fewer blocks the K range of each block is split over a cluster of S = min(8, CTAs / blocks, column stages) CTAs.  For M <= 16
 // it then returns FB_ERR_UNSUPPORTED (the mma.sync kernel's 8-row split over every SM is faster) unless

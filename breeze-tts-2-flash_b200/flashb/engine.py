@@ -300,7 +300,7 @@ class FrameEngine:
     lanes finish two slots sooner than one whole-GPU lane finishes them one after the other.
 
     ``shared_backbone``: one backbone graph for the rows of every slot (slot i = rows [2 g i, 2 g (i + 1)), each
-    laid out [cond, uncond] with its own CFG block), captured on the whole GPU: its GEMVs run as row groups of 16
+    laid out [cond, uncond] with its own CFG block), captured on the whole GPU: its GEMVs run as row groups of 64 rows
     side by side in one launch each, which read every weight tile at about the same time (L2 serves all but the
     first read), and its attention covers every row in one launch.  The depth launches stay per slot, on the
     lanes.  ``step()`` then replays the one backbone graph and forks the lanes for the depth frames."""

@@ -51,10 +51,10 @@ int flashb_gemv_last_split(void);
 /* Split K over a cluster also for M <= 16 rows (1) or not (0, the default: the mma.sync kernel is faster there on
  * a whole B200).  Process-wide; no reference counterpart. */
 void flashb_set_gemv_split(int enable);
-/* Activation rows per row group of the tcgen05 GEMV when M > 16: 16 (the default: groups of 16 rows launched
- * side by side, each on an equal share of the SMs, reading the same weight tiles at about the same time so that
- * L2 serves all but the first), or 32 / 64 / 128 (wider MMA tiles, fewer groups).  Process-wide; no reference
- * counterpart. */
+/* Activation rows per row group of the tcgen05 GEMV when M > 16: 16, 32, 64 (the default) or 128.  The groups
+ * run side by side, each on an equal share of the SMs, and read the same weight tiles at about the same time, so
+ * that L2 serves all but the first read; wider groups read each tile for more rows (the MMA's N).  Process-wide;
+ * no reference counterpart. */
 int flashb_set_gemv_group_rows(int rows);
 /* Programmatic dependent launch on (1, default) / off (0) for all later launches of this process. */
 void flashb_set_pdl(int enable);

@@ -392,7 +392,7 @@ def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, rows, split):
     finally:
         _budget(0)
         lib().flashb_set_gemv_split(0)
-        lib().flashb_set_gemv_group_rows(16)
+        lib().flashb_set_gemv_group_rows(64)   # the library's default
     assert path == 2, f'expected the tcgen05 kernel, got path {path}'
     assert got_split == split, f'expected split {split}, got {got_split}'
     assert_close(np32(y), ref, what=f'tcgen05 {kind} M={M} rows={rows} split={split}')
