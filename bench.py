@@ -303,7 +303,8 @@ def main():
     # frame: at most one lane per slot; the one-part cases keep the requested lanes, so that a single slot can be
     # timed or profiled at a lane's grid size
     lanes = max(1, min(a.lanes, my_streams // a.group)) if a.case == 'frame' else max(1, a.lanes)
-    shared = a.backbone == 'shared' and a.case in ('frame', 'backbone')
+    # one shared backbone graph holds at most 128 rows (64 streams); more streams per GPU run per-lane graphs
+    shared = a.backbone == 'shared' and a.case in ('frame', 'backbone') and 2 * my_streams <= 128
     eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + LAT_FRAMES + 8, device=dev, seed=0,
                       depth_only=(a.case == 'depth'), group=a.group, single_slot=(a.case == 'frame'),
                       lanes=lanes, shared_backbone=shared)
