@@ -311,8 +311,8 @@ template <int EPI, bool NORM>
 int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
   a.M = M;
   if (M > 16) {
-    // up to 128 rows: the tcgen05 kernel (MMA N = the rows); else row blocks of 16 through the paths below, each
-    // block streaming the weights again
+    // up to 128 rows: the tcgen05 kernel (MMA N = the rows); else row blocks through the paths below (16 rows, or
+    // 8 / 4 / 2 / 1 for K % 64 != 0), each block streaming the weights again
     if (a.K % 64 == 0) {
       const int rt = gemv_tc(a, EPI, NORM, st);
       if (rt != FB_ERR_UNSUPPORTED) {
@@ -320,13 +320,19 @@ int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
         return rt;
       }
     }
-    for (int r0 = 0; r0 < M; r0 += 16) {
+    for (int r0 = 0; r0 < M;) {
+      int m = M - r0 < 16 ? M - r0 : 16;
+      if (a.K % 64 != 0) {   // the scalar kernel's row counts: 8, 4, 2, 1
+        m = 8;
+        while (m > M - r0) m >>= 1;
+      }
       GemvArgs b = a;
       b.x += (size_t)r0 * a.ldx;
       b.y += (size_t)r0 * a.ldy;
       if (b.res) b.res += (size_t)r0 * a.ldr;
-      const int rc = dispatch_m<EPI, NORM>(b, M - r0 < 16 ? M - r0 : 16, st);
+      const int rc = dispatch_m<EPI, NORM>(b, m, st);
       if (rc) return rc;
+      r0 += m;
     }
     return FB_OK;
   }

@@ -100,7 +100,7 @@ int flashb_attn_decode_fused(const void* qkv, int64_t qkv_sb, const void* qn_w, 
  * y[m, n] = sum_k xin[m, k] * W[n, k], nn.Linear layout (W [N, K] bf16 row-major contiguous), fp32 accumulation,
  * M = 1..128 rows (the reference: 1..8; x row stride ldx, y row stride ldy, both multiples of 8 elements),
  * K % 8 == 0.  All pointers 16-byte aligned.  More than 16 rows run on the tcgen05 kernel (K % 64 == 0), which then
- * streams the weights once for all rows; otherwise in row blocks of 16. */
+ * streams the weights once for all rows; otherwise in row blocks (16 rows, or 8 / 4 / 2 / 1 when K % 64 != 0). */
 /* Replaces gemv_seg (flash/csrc/bb_fused.cu:293-316): y[:, 0:N0+N1+N2] = norm?(x) @ [W0; W1; W2]^T, where norm is
  * the eager Qwen3 RMSNorm with weight nw [K] when nw != NULL.  W1/W2 may be NULL with N1/N2 = 0. */
 int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const void* nw, float eps, const void* W0, int N0,

@@ -328,6 +328,22 @@ def test_gemv_tcgen05_matches_oracle(ops, kind, M, budget):
     assert device_error() == 0
 
 
+def test_gemv_more_rows_without_tensor_cores(ops):
+    """More than 16 rows with K % 64 != 0 (no tcgen05 kernel): row blocks of 16 through the M <= 16 paths."""
+    fx, _ = ops
+    M, K, N = 40, 1000, 300
+    x = randn((M, K), 71)
+    W = randn((N, K), 72, 0.02)
+    res = randn((M, N), 73)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+    fx.gemv_resid(x, W, res, y)
+    assert_close(np32(y), dec.gemv_resid(np32(x), np32(W), np32(res)), what='gemv_resid M=40 K=1000')
+    nw = randn((K,), 74, 0.1, 1.0)
+    y2 = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+    fx.gemv_seg(x, nw, 1e-6, W, None, None, y2)
+    assert_close(np32(y2), dec.gemv_seg(np32(x), np32(nw), 1e-6, [np32(W)]), what='gemv_seg M=40 K=1000')
+
+
 def _split():
     from flashb._native import lib
     return lib().flashb_gemv_last_split()
@@ -343,7 +359,9 @@ def _split():
     # too few 128-row blocks for the grid: each block's K range split over a cluster
     ('qkv', 128, 0, 128, 6), ('o', 128, 0, 128, 8), ('down', 128, 0, 128, 8), ('gateup', 128, 0, 128, 3),
     ('o', 2, 0, 16, 8), ('qkv', 16, 0, 16, 6), ('down', 33, 0, 64, 8), ('gateup', 2, 0, 16, 3),
-    ('odd', 70, 0, 128, 8), ('o', 128, 64, 128, 4)])
+    ('odd', 70, 0, 128, 8), ('o', 128, 64, 128, 4),
+    # the default: two groups of 64 rows on 74 SMs each (the shared backbone's 128 rows)
+    ('qkv', 128, 0, 64, 3), ('o', 128, 0, 64, 4), ('down', 128, 0, 64, 4), ('gateup', 128, 0, 64, 1)])
 def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, rows, split):
     """More than 16 activation rows on the tcgen05 kernel: row groups of 16 side by side (the default) or wide MMA
     tiles of 32 / 64 / 128 rows, and split K over a thread-block cluster with the partial sums reduced through
