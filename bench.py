@@ -171,6 +171,25 @@ def cpu_frames(seconds, max_frames=None, warmup=1, prompt=PROMPT, seed=0):
     return n / el, n, el, threads
 
 
+def frame_config(a, world, my_streams, lanes, shared, lane_sms, kv_len, case='frame'):
+    """The `config` of a bench line: the workload both arms (flashb and --impl reference) report."""
+    wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + greedy '
+                   f'codebook-0 + 16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9); '
+                   f'{a.group} stream(s) per depth launch share the weight reads; {lanes} lane(s) of the GPU side '
+                   f'by side; ' + (f'one backbone graph for all {my_streams} streams ({2 * my_streams} rows, GEMVs '
+                                   f'as row groups of 64)' if shared else
+                                   f'a backbone graph per {a.group} streams on its lane'),
+          'depth': 'depth frame only (4 layers, hidden 1024, 16 codebooks of 2048, CFG + top-k 50 sampling)',
+          'backbone': 'backbone decode step only (28 layers, hidden 2048, B=2, KV 512+t) + frame link'}[case]
+    return dict(workload=wl, streams=my_streams * world, streams_per_gpu=my_streams,
+                step='one frame of every stream on the rank', streams_per_launch=a.group, prompt_len=a.prompt,
+                kv_len=kv_len, parallelism=f'replica x{world}', lanes=lanes, backbone='shared' if shared else 'lanes',
+                lane_sms=lane_sms,
+                l2='inputs larger than L2: 2.70 GB backbone weights per step, 130 MB depth weights per codebook '
+                   'step; no flush', cb0='greedy (backbone sampler do_sample=False)',
+                prefill='not timed (random prompt KV)')
+
+
 def run_reference(a):
     """--impl reference: the CPU oracle port of the frame, one frame per step (rank 0 only)."""
     rank = int(os.environ.get('RANK', '0'))
@@ -199,12 +218,15 @@ def run_reference(a):
     v = a.steps / el
     sample = (f'{a.steps} frames of one stream (backbone step at KV {a.prompt}+t + 16-codebook depth frame), '
               f'numpy oracle port, {threads} BLAS threads')
+    # the flashb arm's workload (every stream's frame counts the same), timed on a bounded sample of it
+    world = max(1, a.gpus)
+    lanes = max(1, min(a.lanes, a.streams // a.group))
+    shared = a.backbone == 'shared' and 2 * a.streams <= 128
+    cfg = frame_config(a, world, a.streams, lanes, shared, None, [a.prompt + 1, a.prompt + a.warmup + a.steps])
     print(json.dumps(dict(
         impl='reference', metric='frames/s', value=round(v, 4), unit='frames/s', n_gpus=a.gpus, steps=a.steps,
-        warmup=a.warmup, ms_per_step=round(el / a.steps * 1e3, 3), higher_is_better=True, scaling='strong',
-        vs_baseline=None, dtype='bf16', data='synthetic',
-        config=dict(workload='streaming frame: 28-layer backbone decode step + 16-codebook depth frame (CPU port)',
-                    prompt_len=a.prompt, streams=1),
+        warmup=a.warmup, ms_per_step=round(el / a.steps * 1e3, 3), higher_is_better=True, scaling='weak',
+        vs_baseline=None, dtype='bf16', data='synthetic', config=cfg,
         cpu_baseline=dict(value=round(v, 4), unit='frames/s', cores=threads, kind='port', sample=sample),
         e2e=dict(value=round(v, 4), unit='frames/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))), flush=True)
 
@@ -484,25 +506,13 @@ def main():
     launches = eng.launches_per_frame() if case == 'frame' else (
         1 if case == 'depth' else eng.launches_per_frame() - 1)
     if rank == 0:
-        wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + greedy '
-                       f'codebook-0 + 16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9); '
-                       f'{a.group} stream(s) per depth launch share the weight reads; {lanes} lane(s) of the GPU side '
-                       f'by side; ' + (f'one backbone graph for all {my_streams} streams ({2 * my_streams} rows, GEMVs '
-                                       f'as row groups of 64)' if eng.shared else
-                                       f'a backbone graph per {a.group} streams on its lane'),
-              'depth': 'depth frame only (4 layers, hidden 1024, 16 codebooks of 2048, CFG + top-k 50 sampling)',
-              'backbone': 'backbone decode step only (28 layers, hidden 2048, B=2, KV 512+t) + frame link'}[case]
         line = dict(
             metric='frames/s', value=round(value, 3), unit='frames/s', n_gpus=world, steps=a.steps,
             warmup=a.warmup, ms_per_step=round(ms_max / a.steps, 3), higher_is_better=True, scaling='weak',
             vs_baseline=None, dtype='bf16', data='synthetic (seeded random bf16 weights, random prompt KV)',
-            config=dict(workload=wl, streams=total_streams, streams_per_gpu=my_streams, step='one frame of every stream '
-                        'on the rank', streams_per_launch=a.group, prompt_len=a.prompt, kv_len=[kv0, kv1],
-                        parallelism=f'replica x{world}', lanes=lanes, backbone=a.backbone if shared else 'lanes',
-                        lane_sms=eng.lane_sms or torch.cuda.get_device_properties(dev).multi_processor_count,
-                        l2='inputs larger than L2: 2.70 GB backbone weights per step, 130 MB depth weights per '
-                           'codebook step; no flush', cb0='greedy (backbone sampler do_sample=False)',
-                        prefill='not timed (random prompt KV)'),
+            config=frame_config(a, world, my_streams, lanes, eng.shared,
+                                eng.lane_sms or torch.cuda.get_device_properties(dev).multi_processor_count,
+                                [kv0, kv1], case),
             frames_per_s_per_gpu=round(value / world, 3), tokens_per_s=round(value * 17, 1),
             frame_ms_single_stream=lat,
             roofline=roof, roofline_backbone=roof_bb, prefill=prefill, cpu_baseline=cpu, e2e=e2e,
