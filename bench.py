@@ -3,8 +3,9 @@
 
 Workload (BASELINE config 5 with configs 3 and 4): 64 independent streams per GPU (64 N for the job: weak scaling,
 streams assigned round-robin, one replica per GPU), each after a 512-token prompt (random KV, the prefill stand-in).
-Streams are decoded 8 per launch (--group) and the GPU runs 8 lanes of slots side by side (--lanes), each lane on
-its own CUDA stream with its kernels sized for 1/8 of the SMs.  A STEP is one frame of every stream on this rank:
+One backbone graph decodes every stream's rows on the whole GPU (--backbone shared: 128 rows, GEMVs in row groups
+of 64); the depth frames run 8 streams per launch (--group) on 8 lanes side by side (--lanes), each lane on its own
+CUDA stream with its kernels sized for 1/8 of the SMs.  A STEP is one frame of every stream on this rank:
 
     frame = next backbone ids from the previous frame -> 28-layer backbone decode step (B = 2 CFG rows, KV length
             512 + t, hidden 2048, 16 q / 4 kv heads, FFN 6144, fp32 lm_head + CFG) -> codebook-0 token (greedy
@@ -14,8 +15,9 @@ its own CUDA stream with its kernels sized for 1/8 of the SMs.  A STEP is one fr
 Outputs one JSON line (rank 0): ``value`` = frames/s of the whole job with every input resident in HBM (max over
 ranks of the device time), ``e2e`` = the same through the engine API with the per-frame Exp(1) draws copied from
 pinned host memory before each frame and the frame's tokens read back to the host after it, every step (as the
-reference's loop reads its tokens), ``roofline`` for the dominant kernel (the depth frame kernel) and ``roofline_backbone`` for the backbone
-step's attention + GEMV kernels, ``cpu_baseline`` = the CPU oracle port of the same frame on this host's cores.
+reference's loop reads its tokens), ``roofline`` for the dominant kernel (the depth frame kernel) and
+``roofline_backbone`` for the backbone step's attention + GEMV kernels, ``cpu_baseline`` = the CPU oracle port of
+the same frame on this host's cores.
 
 ``--impl reference`` times that CPU port alone (rank 0; other ranks exit 0), one frame per step.
 ``--case depth`` / ``--case backbone`` time one part alone (profiling entry points; same JSON shape, no baselines).
