@@ -52,9 +52,6 @@ _PROTOS = {
     'flashb_embed_rope': (I, [P, I, I, I, P, I, P, P, P, I, I, P, P, P, P]),
     'flashb_lm_head_cfg': (I, [P, I, I, P, F, P, I, P, P, P, P, P]),
     'flashb_step_advance': (I, [P, P, I, P, I, L, I, P]),
-    'flashb_bb_scratch_bytes': (L, [P]),
-    'flashb_bb_layer_bytes': (L, []),
-    'flashb_bb_step': (I, [P, P, P, P, P, P, P, I, L, P, I, P, P, P, P]),
     'flashb_cb0_greedy': (I, [P, L, I, I, I, P, P]),
     'flashb_frame_ids': (I, [P, P, I, I, I, P, P]),
     'flashb_prefill_attn': (I, [P, L, L, L, P, L, L, L, P, L, L, L, P, I, L, L, I, I, I, I, I, I, F, I, I, I, P, L, L,
@@ -77,20 +74,6 @@ class FbDDConfig(ctypes.Structure):
                 ('head_dim', I), ('ffn', I), ('vocab', I), ('codebook_size', I), ('n_decode', I), ('eps', F),
                 ('scaling', F), ('embed', P), ('proj', P), ('normf', P), ('head_t', P), ('cos_tab', P),
                 ('sin_tab', P), ('trace', P), ('grid', I), ('layers_host', P)]
-
-
-class FbBBLayer(ctypes.Structure):
-    """fb_bb_layer of include/flashb.h."""
-    _fields_ = [(n, ctypes.c_void_p) for n in ('ln1', 'wq', 'wk', 'wv', 'q_norm', 'k_norm', 'wo', 'ln2', 'wg', 'wu',
-                                               'wd', 'k_cache', 'v_cache')]
-
-
-class FbBBConfig(ctypes.Structure):
-    """fb_bb_config of include/flashb.h."""
-    _fields_ = [('layers', I), ('batch', I), ('hidden', I), ('heads', I), ('kv_heads', I), ('head_dim', I),
-                ('ffn', I), ('lm_rows', I), ('codebooks', I), ('vocab', I), ('cache_len', I), ('max_pos', I),
-                ('eps', F), ('qk_eps', F), ('scaling', F), ('cache_stride_b', L), ('cache_stride_h', L),
-                ('embed', P), ('norm_w', P), ('lm_head32', P), ('cos_tab', P), ('sin_tab', P), ('trace', P)]
 
 
 def lib_path():

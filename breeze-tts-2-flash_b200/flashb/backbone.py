@@ -8,25 +8,16 @@
                -> gemv_resid (o_proj + residual) -> gemv_gateup (RMSNorm + SwiGLU) -> gemv_resid (down + residual)
     lm_head_cfg                        final RMSNorm + fp32 lm_head + CFG                       (1 launch)
 
-Unlike the reference, the embedding, rotary gather, lm_head and CFG also run as library kernels.  By default
-(``STEP_MODE = 'kernels'``) the step is the 2 + 5 x layers separate launches above, chained with programmatic dependent
-launch; ``STEP_MODE = 'persistent'`` (or ``FLASHB_STEP=persistent``) runs it as ONE cooperative launch
-(``flashb_bb_step``: a producer warp per SM streams every layer's weights through a shared-memory ring while the
-consumer warps run the step's tasks between grid barriers).  Measured on B200 the separate launches are faster
-today (1.24 vs 1.98 ms at KV length 1024): inside one launch the attention's chain of dependent global round trips
-sits on the critical path of every layer while HBM is saturated.  Unsupported graphs (head_dim != 128, GQA group outside {1, 2, 4, 8}, biases, non-SiLU MLP, more
+Unlike the reference, the embedding, rotary gather, lm_head and CFG also run as library kernels.  The step is the
+2 + 5 x layers launches above, chained with programmatic dependent launch and captured by the caller's CUDA graph.
+Unsupported graphs (head_dim != 128, GQA group outside {1, 2, 4, 8}, biases, non-SiLU MLP, more
 than 8 batch rows, an audio-embedding projector) route to the original method, as the reference does
 (``flash/backbone.py:49-103``).
 """
-import ctypes
-import os
-
 import torch
 
 from . import _native, kernels
 from ._native import check
-
-STEP_MODE = os.environ.get('FLASHB_STEP', 'kernels')
 
 # The reference's per-GPU launch-shape table (R rows/warp, U unroll, warps), kept for import compatibility; the
 # B200 kernels choose their launch shape themselves.
@@ -154,55 +145,6 @@ def run_layers(st, x, kv_layers, mask, cache_position):
     return x
 
 
-class PersistentStep:
-    """Device-side descriptors and scratch of the one-launch backbone step for one graph."""
-
-    def __init__(self, st, kv_layers, cache_len, device):
-        L0 = st['layers'][0]
-        B = st['B']
-        H = L0.wq.shape[1]
-        self.kv = kv_layers
-        recs = (_native.FbBBLayer * len(st['layers']))()
-        for i, (L, (kc, vc)) in enumerate(zip(st['layers'], kv_layers)):
-            recs[i] = _native.FbBBLayer(L.ln1_w.data_ptr(), L.wq.data_ptr(), L.wk.data_ptr(), L.wv.data_ptr(),
-                                        L.qn_w.data_ptr(), L.kn_w.data_ptr(), L.wo.data_ptr(), L.ln2_w.data_ptr(),
-                                        L.wg.data_ptr(), L.wu.data_ptr(), L.wd.data_ptr(), kc.data_ptr(),
-                                        vc.data_ptr())
-        self.table = torch.frombuffer(bytearray(bytes(recs)), dtype=torch.uint8).to(device)
-        kc0 = kv_layers[0][0]
-        cfg = _native.FbBBConfig()
-        cfg.layers, cfg.batch, cfg.hidden = len(st['layers']), B, H
-        cfg.heads, cfg.kv_heads, cfg.head_dim = L0.wq.shape[0] // 128, L0.wk.shape[0] // 128, 128
-        cfg.ffn, cfg.lm_rows = L0.wg.shape[0], st['lm_head32'].shape[0]
-        cfg.codebooks = st['embed'].shape[0] // st['vocab']
-        cfg.vocab, cfg.cache_len, cfg.max_pos = st['vocab'], cache_len, st['cos_tab'].shape[0]
-        cfg.eps, cfg.qk_eps, cfg.scaling = float(L0.ln1_eps), float(L0.qk_eps), float(L0.scaling)
-        cfg.cache_stride_b, cfg.cache_stride_h = kc0.stride(0), kc0.stride(1)
-        cfg.embed, cfg.norm_w, cfg.lm_head32 = st['embed'].data_ptr(), st['norm_w'].data_ptr(), \
-            st['lm_head32'].data_ptr()
-        cfg.cos_tab, cfg.sin_tab = st['cos_tab'].data_ptr(), st['sin_tab'].data_ptr()
-        self.cfg = cfg
-        n = int(_native.lib().flashb_bb_scratch_bytes(ctypes.byref(cfg)))
-        self.scratch = torch.zeros(n, dtype=torch.uint8, device=device)
-
-    def run(self, ids, position_ids, cache_position, mask, gs, hidden_out, logits, cfg_out, advance=False):
-        m_sb = 0 if mask.shape[0] == 1 else mask.stride(0)
-        check(_native.lib().flashb_bb_step(
-            ctypes.byref(self.cfg), self.table.data_ptr(), self.scratch.data_ptr(), ids.data_ptr(),
-            position_ids.data_ptr(), cache_position.data_ptr(), mask.data_ptr(), int(mask.dtype == torch.bfloat16),
-            m_sb, None if gs is None else gs.data_ptr(), 1 if advance else 0, hidden_out.data_ptr(),
-            logits.data_ptr(), cfg_out.data_ptr(), torch.cuda.current_stream(ids.device).cuda_stream))
-
-
-def _persistent(graph, st):
-    ps = st.get('persist')
-    kv = [(L.keys, L.values) for L in graph.static_cache.layers]
-    if ps is None or any(a[0].data_ptr() != b[0].data_ptr() for a, b in zip(ps.kv, kv)):
-        ps = PersistentStep(st, kv, graph.max_seq_len, graph.hidden_buf.device)
-        st['persist'] = ps
-    return ps
-
-
 def fused_decode_step(graph, advance=False):
     """One backbone decode step on the official graph's buffers (``BackboneGraph._decode_step``).  ``advance``
     (flashb extension, off for the official graph) first moves cache_position / position_ids / mask by one slot on
@@ -211,11 +153,6 @@ def fused_decode_step(graph, advance=False):
     if st is None:
         return ORIG['_decode_step'](graph)
     B = graph.batch_size
-    if STEP_MODE == 'persistent':
-        ps = _persistent(graph, st)
-        ps.run(graph.input_ids_buf, graph.position_ids, graph.cache_position, graph.attn_mask, graph.guidance_scale,
-               graph.hidden_buf, graph.logits_buf, graph.cfg_logits_buf, advance=advance)
-        return
     fx = kernels.fused()
     if advance:
         check(_native.lib().flashb_step_advance(graph.cache_position.data_ptr(), graph.position_ids.data_ptr(), B,
