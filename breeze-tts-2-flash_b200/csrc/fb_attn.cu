@@ -23,7 +23,7 @@
 
 #include <cstdlib>
 
-#include "fb_common.cuh"
+#include "fb_norm.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -66,34 +66,6 @@ struct AttnArgs {
   int S, NH, NKV, nsplit;
   unsigned* err;
 };
-
-// This lane's 4 dims [4 lane, 4 lane + 4) of a bf16 vector, as floats.
-__device__ __forceinline__ void load4(const bf16* p, int lane, float out[4]) {
-  const uint2 u = *reinterpret_cast<const uint2*>(p + lane * 4);
-  out[0] = lo_f(u.x);
-  out[1] = hi_f(u.x);
-  out[2] = lo_f(u.y);
-  out[3] = hi_f(u.y);
-}
-// RMSNorm over 128 dims + RoPE for one head with the lane's norm weights w, cos cs and sin sn already loaded.
-__device__ __forceinline__ void norm_rope_pre(const bf16* x, const float w[4], float eps, const float cs[4],
-                                              const float sn[4], int lane, float out[4]) {
-  const int d0 = lane * 4;
-  const uint2 xv = *reinterpret_cast<const uint2*>(x + d0);
-  float v[4] = {lo_f(xv.x), hi_f(xv.x), lo_f(xv.y), hi_f(xv.y)};
-  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-  ss = warp_sum(ss);
-  const float r = 1.0f / sqrtf(ss / (float)AT_D + eps);
-  float y[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) y[j] = rbf(w[j] * rbf(v[j] * r));
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float partner = __shfl_xor_sync(FULL, y[j], 16);
-    const float rot = lane < 16 ? -partner : partner;
-    out[j] = rbf(rbf(y[j] * cs[j]) + rbf(rot * sn[j]));
-  }
-}
 
 template <int G, bool FUSED>
 __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a) {
@@ -150,13 +122,13 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
   // griddepcontrol.wait.  In the decode step they are written by the host or by launches at least two back
   // (embed_rope, step_advance), which have completed before this kernel can start (its predecessor, the q|k|v GEMV,
   // lets it start only after its own griddepcontrol.wait); only q|k|v comes from the predecessor.
-  float wq4[4], wk4[4], cs4[4], sn4[4];
+  HeadPair wq, wk, cs, sn;
   float m_first = -INFINITY;
   if (FUSED) {
-    load4(a.qn_w, lane, wq4);
-    load4(a.kn_w, lane, wk4);
-    load4(a.cos + (size_t)b * a.cs_sb, lane, cs4);
-    load4(a.sin + (size_t)b * a.cs_sb, lane, sn4);
+    wq = head_load(a.qn_w, lane);
+    wk = head_load(a.kn_w, lane);
+    cs = head_load(a.cos + (size_t)b * a.cs_sb, lane);
+    sn = head_load(a.sin + (size_t)b * a.cs_sb, lane);
     if (tid < AT_CHUNK && nchunks > 0 && tid < min(AT_CHUNK, p_end - p_begin)) {
       const size_t mi = (size_t)b * a.m_sb + p_begin + tid;
       m_first = a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi])
@@ -173,10 +145,12 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
   for (int g = warp; g < G; g += AT_THREADS / 32) {
     const int hq = h * G + g;
     if (FUSED) {
-      float qv[4];
-      norm_rope_pre(a.qkv + (size_t)b * a.qkv_sb + (size_t)hq * AT_D, wq4, a.eps, cs4, sn4, lane, qv);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) q_s[g][lane * 4 + j] = qv[j];
+      const bf16* qr = a.qkv + (size_t)b * a.qkv_sb + (size_t)hq * AT_D;
+      const HeadPair qv = head_norm_rope(qr, wq, cs, sn, a.eps, lane);
+      q_s[g][2 * lane] = qv.lo[0];
+      q_s[g][2 * lane + 1] = qv.lo[1];
+      q_s[g][64 + 2 * lane] = qv.hi[0];
+      q_s[g][64 + 2 * lane + 1] = qv.hi[1];
     } else {
       const bf16* qp = a.q + (size_t)b * a.q_sb + (size_t)hq * a.q_sh;
 #pragma unroll
@@ -186,10 +160,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
   const bool owner = FUSED && pos >= p_begin && pos < p_end;
   if (owner) {
     if (warp == 0) {
-      float kv[4];
-      norm_rope_pre(a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AT_D, wk4, a.eps, cs4, sn4, lane, kv);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) newk[lane * 4 + j] = __float2bfloat16_rn(kv[j]);
+      const bf16* kr = a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AT_D;
+      head_store(newk, head_norm_rope(kr, wk, cs, sn, a.eps, lane), lane);
     } else if (warp == 1) {
       const bf16* vp = a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + a.NKV + h) * AT_D;
       *reinterpret_cast<uint2*>(&newv[lane * 4]) = *reinterpret_cast<const uint2*>(vp + lane * 4);

@@ -22,7 +22,7 @@
 // chunk are fetched by cp.async as far ahead as its K and V.  The first chunks are requested before
 // griddepcontrol.wait (old cache rows are not written by the preceding kernel); the row written at cache_pos is
 // patched into the staged chunk.  Every wait is bounded.
-#include "fb_common.cuh"
+#include "fb_norm.cuh"
 
 namespace fb {
 
@@ -102,35 +102,6 @@ __device__ __forceinline__ uint32_t am_off(int r, int u) {
   return (uint32_t)(((u >> 3) << 13) + (r << 7) + ((((u & 7) ^ (r & 7))) << 4));
 }
 
-// This lane's 4 dims [4 lane, 4 lane + 4) of a bf16 vector, as floats.
-__device__ __forceinline__ void am_load4(const bf16* p, int lane, float out[4]) {
-  const uint2 u = *reinterpret_cast<const uint2*>(p + lane * 4);
-  out[0] = lo_f(u.x);
-  out[1] = hi_f(u.x);
-  out[2] = lo_f(u.y);
-  out[3] = hi_f(u.y);
-}
-// RMSNorm over 128 dims + RoPE for one head with the lane's norm weights, cos and sin already loaded (the scalar
-// kernel's operation order).
-__device__ __forceinline__ void am_norm_rope(const bf16* x, const float w[4], float eps, const float cs[4],
-                                             const float sn[4], int lane, float out[4]) {
-  const int d0 = lane * 4;
-  const uint2 xv = *reinterpret_cast<const uint2*>(x + d0);
-  float v[4] = {lo_f(xv.x), hi_f(xv.x), lo_f(xv.y), hi_f(xv.y)};
-  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-  ss = warp_sum(ss);
-  const float r = 1.0f / sqrtf(ss / (float)AM_D + eps);
-  float y[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) y[j] = rbf(w[j] * rbf(v[j] * r));
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float partner = __shfl_xor_sync(FULL, y[j], 16);
-    const float rot = lane < 16 ? -partner : partner;
-    out[j] = rbf(rbf(y[j] * cs[j]) + rbf(rot * sn[j]));
-  }
-}
-
 template <int G>
 __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_constant__ AttnMmaArgs a) {
   extern __shared__ __align__(1024) unsigned char am_smem_raw[];
@@ -204,21 +175,16 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
   // they are written by the host or by launches at least two back (embed_rope, step_advance), complete before this
   // kernel can start; only q|k|v comes from the predecessor
   for (int c = 0; c < AM_STAGES; ++c) issue_mask(c);
-  float wq4[4], wk4[4], cs4[4], sn4[4];
-  am_load4(a.qn_w, lane, wq4);
-  am_load4(a.kn_w, lane, wk4);
-  am_load4(a.cos + (size_t)b * a.cs_sb, lane, cs4);
-  am_load4(a.sin + (size_t)b * a.cs_sb, lane, sn4);
+  const HeadPair wq = head_load(a.qn_w, lane), wk = head_load(a.kn_w, lane);
+  const HeadPair cs = head_load(a.cos + (size_t)b * a.cs_sb, lane), sn = head_load(a.sin + (size_t)b * a.cs_sb, lane);
   pdl_wait();
   pdl_trigger();
 
   // ---- queries of the group, and in every CTA the new key / value row (written to the cache by this CTA)
   for (int g = warp; g < 8; g += AM_THREADS / 32) {
     if (g < G) {
-      float qv[4];
-      am_norm_rope(a.qkv + (size_t)b * a.qkv_sb + (size_t)(h * G + g) * AM_D, wq4, a.eps, cs4, sn4, lane, qv);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) qs[g][lane * 4 + j] = __float2bfloat16_rn(qv[j]);
+      const bf16* qr = a.qkv + (size_t)b * a.qkv_sb + (size_t)(h * G + g) * AM_D;
+      head_store(qs[g], head_norm_rope(qr, wq, cs, sn, a.eps, lane), lane);
     } else {
       *reinterpret_cast<uint2*>(&qs[g][lane * 4]) = make_uint2(0u, 0u);
     }
@@ -226,10 +192,8 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
   const bool write = pos >= 0 && pos < S;
   if (write) {
     if (warp == 0) {
-      float kv[4];
-      am_norm_rope(a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AM_D, wk4, a.eps, cs4, sn4, lane, kv);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) newk[lane * 4 + j] = __float2bfloat16_rn(kv[j]);
+      const bf16* kr = a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + h) * AM_D;
+      head_store(newk, head_norm_rope(kr, wk, cs, sn, a.eps, lane), lane);
     } else if (warp == 1) {
       const bf16* vp = a.qkv + (size_t)b * a.qkv_sb + (size_t)(NH + NKV + h) * AM_D;
       *reinterpret_cast<uint2*>(&newv[lane * 4]) = *reinterpret_cast<const uint2*>(vp + lane * 4);

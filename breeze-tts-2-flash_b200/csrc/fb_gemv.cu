@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_fma_kernel(const GemvArgs a) 
   unsigned char* ring = smem + a.xs_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)a.nstages * GV_STAGE_BYTES);
   uint64_t* empty = full + GV_MAX_STAGES;
-  __shared__ float red[GV_CWARPS][M];
+  __shared__ float rfac[M];
   __shared__ float part[GV_CWARPS][NMAT][M];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -101,59 +101,21 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_fma_kernel(const GemvArgs a) 
   pdl_wait();
   pdl_trigger();
   const int ctid = threadIdx.x;  // 0..255
-  const int kv = K >> 3;
   {
-    float ss[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m) ss[m] = 0.f;
-    for (int i = ctid; i < M * kv; i += GV_CWARPS * 32) {
-      const int m = i / kv, j = i - m * kv;
-      const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + (size_t)j * 8);
-      reinterpret_cast<uint4*>(xs)[i] = v;
-      if (NORM) {
-        float f[8];
-        cvt8(v, f);
-        float s = 0.f;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) s = fmaf(f[t], f[t], s);
-#pragma unroll
-        for (int mm = 0; mm < M; ++mm)
-          if (mm == m) ss[mm] += s;
-      }
-    }
-    if (NORM) {
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        const float s = warp_sum(ss[m]);
-        if (lane == 0) red[warp][m] = s;
-      }
-      named_sync(1, GV_CWARPS * 32);
-      float rs[M];
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        float s = 0.f;
-#pragma unroll
-        for (int w = 0; w < GV_CWARPS; ++w) s += red[w][m];
-        rs[m] = 1.0f / sqrtf(s / (float)K + a.eps);
-      }
-      for (int i = ctid; i < M * kv; i += GV_CWARPS * 32) {
-        const int m = i / kv, j = i - m * kv;
-        float f[8], w[8];
-        cvt8(reinterpret_cast<const uint4*>(xs)[i], f);
-        cvt8(*reinterpret_cast<const uint4*>(a.nw + (size_t)j * 8), w);
-        float r = 0.f;
-#pragma unroll
-        for (int mm = 0; mm < M; ++mm)
-          if (mm == m) r = rs[mm];
-        uint4 o;
-        o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
-        o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
-        o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
-        o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
-        reinterpret_cast<uint4*>(xs)[i] = o;
-      }
+    // stage x (rows at a pitch of K elements), then the row factors and the norm in place
+    const int nu = K >> 3;
+    for (int i = ctid; i < M * nu; i += GV_CWARPS * 32) {
+      const int m = i / nu, u = i - m * nu;
+      reinterpret_cast<uint4*>(xs)[i] = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + (size_t)u * 8);
     }
     named_sync(1, GV_CWARPS * 32);
+    if (NORM) {
+      const PitchOff off{K * 2};
+      rms_row_factors(smem, off, M, K, a.eps, rfac, warp, GV_CWARPS);
+      named_sync(1, GV_CWARPS * 32);
+      rms_rows_apply(smem, off, M, K, a.nw, rfac, ctid, GV_CWARPS * 32);
+      named_sync(1, GV_CWARPS * 32);
+    }
   }
 
   for (int t = 0; t < T; ++t) {
@@ -245,38 +207,36 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_fma_kernel(const GemvArgs a) 
 }
 
 
-// Standalone Qwen3RMSNorm over rows (one CTA per row).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16* __restrict__ x, long ldx,
-                                                      const bf16* __restrict__ w, float eps, bf16* __restrict__ y,
-                                                      long ldy, int K) {
+// Standalone Qwen3 RMSNorm: one warp per row, 4 rows per CTA.  A lane keeps its units of the row in registers
+// (RN_UNITS per lane covers K <= 32 * 8 * RN_UNITS columns) so the row is read from global memory once.
+constexpr int RN_WARPS = 4, RN_UNITS = 16;
+__global__ void __launch_bounds__(RN_WARPS * 32) rmsnorm_rows_kernel(const bf16* __restrict__ x, long ldx,
+                                                                     const bf16* __restrict__ w, float eps,
+                                                                     bf16* __restrict__ y, long ldy, int M, int K) {
   pdl_wait();
   pdl_trigger();
-  const int m = blockIdx.x;
-  __shared__ float red[8];
-  const bf16* xr = x + (size_t)m * ldx;
-  float s = 0.f;
-  for (int j = threadIdx.x * 8; j < K; j += blockDim.x * 8) {
-    float f[8];
-    cvt8(*reinterpret_cast<const uint4*>(xr + j), f);
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.x * RN_WARPS + (threadIdx.x >> 5);
+  if (m >= M) return;
+  const int nu = K >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)m * ldx);
+  uint4 v[RN_UNITS];
+  float acc = 0.f;
 #pragma unroll
-    for (int t = 0; t < 8; ++t) s = fmaf(f[t], f[t], s);
+  for (int i = 0; i < RN_UNITS; ++i) {
+    const int u = lane + 32 * i;
+    if (u < nu) {
+      v[i] = xr[u];
+      acc = sumsq8(v[i], acc);
+    }
   }
-  s = warp_sum(s);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-  __syncthreads();
-  float tot = 0.f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
-  const float r = 1.0f / sqrtf(tot / (float)K + eps);
-  for (int j = threadIdx.x * 8; j < K; j += blockDim.x * 8) {
-    float f[8], ww[8];
-    cvt8(*reinterpret_cast<const uint4*>(xr + j), f);
-    cvt8(*reinterpret_cast<const uint4*>(w + j), ww);
-    uint4 o;
-    o.x = pack2(ww[0] * rbf(f[0] * r), ww[1] * rbf(f[1] * r));
-    o.y = pack2(ww[2] * rbf(f[2] * r), ww[3] * rbf(f[3] * r));
-    o.z = pack2(ww[4] * rbf(f[4] * r), ww[5] * rbf(f[5] * r));
-    o.w = pack2(ww[6] * rbf(f[6] * r), ww[7] * rbf(f[7] * r));
-    *reinterpret_cast<uint4*>(y + (size_t)m * ldy + j) = o;
+  const float r = rms_factor(warp_sum(acc), K, eps);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)m * ldy);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+  for (int i = 0; i < RN_UNITS; ++i) {
+    const int u = lane + 32 * i;
+    if (u < nu) yr[u] = rms_unit(v[i], wr[u], r);
   }
 }
 
@@ -471,10 +431,12 @@ extern "C" int flashb_rmsnorm(const void* x, int64_t ldx, int M, int K, const vo
   int rc = common_checks(x, ldx, M, K, y, ldy);
   if (rc) return rc;
   FB_CHECK_ARG(w && al16(w) && ldy % 8 == 0 && al16(y), "rmsnorm: bad weight or output stride");
+  FB_CHECK_ARG(K <= 32 * 8 * RN_UNITS, "rmsnorm: K %d above %d", K, 32 * 8 * RN_UNITS);
   const bf16* xp = (const bf16*)x;
   const bf16* wp = (const bf16*)w;
   bf16* yp = (bf16*)y;
   long lx = (long)ldx, ly = (long)ldy;
-  void* args[] = {(void*)&xp, (void*)&lx, (void*)&wp, (void*)&eps, (void*)&yp, (void*)&ly, (void*)&K};
-  return fbh::launch_pdl((const void*)rmsnorm_kernel, dim3(M), dim3(256), 0, (cudaStream_t)stream, args, true);
+  void* args[] = {(void*)&xp, (void*)&lx, (void*)&wp, (void*)&eps, (void*)&yp, (void*)&ly, (void*)&M, (void*)&K};
+  return fbh::launch_pdl((const void*)rmsnorm_rows_kernel, dim3((M + RN_WARPS - 1) / RN_WARPS), dim3(RN_WARPS * 32),
+                         0, (cudaStream_t)stream, args, true);
 }

@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const __grid_const
   float* sums = red + ST_CWARPS * 128 * NT;
   uint64_t* full = reinterpret_cast<uint64_t*>(sums + 128 * NT);
   uint64_t* empty = full + GM_MAX_STAGES;
-  __shared__ float nred[ST_CWARPS][MS];
+  __shared__ float rfac[MS];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = gridDim.x, bid = blockIdx.x;
@@ -153,60 +153,22 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const __grid_const
   pdl_wait();
   pdl_trigger();
   const int ctid = tid;
-  const int kv = K >> 3;
   if (!a.xchunk) {
-    float ss[MS];
-#pragma unroll
-    for (int m = 0; m < MS; ++m) ss[m] = 0.f;
-    for (int i = ctid; i < M * kv; i += ST_CWARPS * 32) {
-      const int m = i / kv, j = i - m * kv;
-      const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + (size_t)j * 8);
-      *reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16) = v;
-      if (NORM) {
-        float f[8];
-        cvt8(v, f);
-        float q = 0.f;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) q = fmaf(f[t], f[t], q);
-#pragma unroll
-        for (int mm = 0; mm < MS; ++mm)
-          if (mm == m) ss[mm] += q;
-      }
-    }
-    if (NORM) {
-#pragma unroll
-      for (int m = 0; m < MS; ++m) {
-        const float q = warp_sum(ss[m]);
-        if (lane == 0) nred[warp][m] = q;
-      }
-      named_sync(1, ST_CWARPS * 32);
-      float rs[MS];
-#pragma unroll
-      for (int m = 0; m < MS; ++m) {
-        float q = 0.f;
-#pragma unroll
-        for (int w = 0; w < ST_CWARPS; ++w) q += nred[w][m];
-        rs[m] = 1.0f / sqrtf(q / (float)K + a.eps);
-      }
-      for (int i = ctid; i < M * kv; i += ST_CWARPS * 32) {
-        const int m = i / kv, j = i - m * kv;
-        uint4* px = reinterpret_cast<uint4*>(xs + (size_t)m * x_pitch + j * 16);
-        float f[8], w[8];
-        cvt8(*px, f);
-        cvt8(*reinterpret_cast<const uint4*>(a.nw + (size_t)j * 8), w);
-        float r = 0.f;
-#pragma unroll
-        for (int mm = 0; mm < MS; ++mm)
-          if (mm == m) r = rs[mm];
-        uint4 o;
-        o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
-        o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
-        o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
-        o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
-        *px = o;
-      }
+    // stage every x row, then the row factors and the norm in place
+    const int nu = K >> 3;
+    const PitchOff off{x_pitch};
+    for (int i = ctid; i < M * nu; i += ST_CWARPS * 32) {
+      const int m = i / nu, u = i - m * nu;
+      *reinterpret_cast<uint4*>(xs + off(m, u)) =
+          *reinterpret_cast<const uint4*>(a.x + (size_t)m * a.ldx + (size_t)u * 8);
     }
     named_sync(1, ST_CWARPS * 32);
+    if (NORM) {
+      rms_row_factors(xs, off, M, K, a.eps, rfac, warp, ST_CWARPS);
+      named_sync(1, ST_CWARPS * 32);
+      rms_rows_apply(xs, off, M, K, a.nw, rfac, ctid, ST_CWARPS * 32);
+      named_sync(1, ST_CWARPS * 32);
+    }
   }
 
   int t = 0;

@@ -322,12 +322,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         for (int m = etid; m < MT; m += TC_EPI_THREADS) {
           float t = 0.f;
           for (int p = 0; p < S; ++p) t += *cluster.map_shared_rank(psum + m, p);
-          rs[m] = 1.0f / sqrtf(t / (float)K + a.eps);
+          rs[m] = rms_factor(t, K, a.eps);
         }
       } else {
         __syncwarp();
         for (int m = lane; m < MT; m += 32)
-          if ((m & 3) == q) rs[m] = 1.0f / sqrtf(psum[m] / (float)K + a.eps);
+          if ((m & 3) == q) rs[m] = rms_factor(psum[m], K, a.eps);
       }
       named_sync(1, TC_EPI_THREADS);
     }
@@ -341,16 +341,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         const int k = kc * TC_C + c * 64 + ((jp ^ (m & 7)) << 3);
         if (m >= M || k >= K) continue;
         uint4* p = reinterpret_cast<uint4*>(xt + (size_t)i * 16);
-        float f[8], w[8];
-        cvt8(*p, f);
-        cvt8(*reinterpret_cast<const uint4*>(a.nw + k), w);
-        const float r = rs[m];
-        uint4 o;
-        o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
-        o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
-        o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
-        o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
-        *p = o;
+        *p = rms_unit(*p, *reinterpret_cast<const uint4*>(a.nw + k), rs[m]);
       }
       fence_proxy_async();                 // generic-proxy writes -> visible to the tensor core's reads
       __syncwarp();

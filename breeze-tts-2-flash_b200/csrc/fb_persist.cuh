@@ -276,43 +276,22 @@ __device__ __forceinline__ uint32_t xs_off(int m, int j, int x_pitch) {
   return (uint32_t)(((j >> 3) << 11) + (m << 7) + (((j & 7) ^ (m & 7)) << 4));
 }
 
-// Per-row RMS factors of M <= 16 staged rows: warp w reduces rows w and w + 8 (each lane's chunks in order, then a
-// butterfly), and rs[m] = 1 / sqrt(mean(x^2) + eps).  Every staged chunk must be visible to every consumer thread.
+// Offset functor for xs_off (either staged layout).
+struct StagedOff {
+  int pitch;
+  __device__ __forceinline__ uint32_t operator()(int m, int u) const { return xs_off(m, u, pitch); }
+};
+
+// Per-row RMS factors of M <= 16 staged rows (one warp per row over the consumer warps), then a consumer barrier.
 __device__ __noinline__ void row_rms(const unsigned char* xs, int x_pitch, int M, int K, float eps, float* rs) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kv = K >> 3;
-  for (int m = warp; m < M; m += ST_CWARPS) {
-    float q = 0.f;
-    for (int j = lane; j < kv; j += 32) {
-      float f[8];
-      cvt8(*reinterpret_cast<const uint4*>(xs + xs_off(m, j, x_pitch)), f);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) q = fmaf(f[u], f[u], q);
-    }
-    q = warp_sum(q);
-    if (lane == 0) rs[m] = 1.0f / sqrtf(q / (float)K + eps);
-  }
+  rms_row_factors(xs, StagedOff{x_pitch}, M, K, eps, rs, threadIdx.x >> 5, ST_CWARPS);
   named_sync(1, PK_CONSUMERS);
 }
 
-// Eager Qwen3 RMSNorm in place on staged rows (double rounding: bf16(w * bf16(x * r))), r from row_rms.
+// The eager Qwen3 RMSNorm in place on staged rows, factors from row_rms.
 __device__ __forceinline__ void apply_rms(unsigned char* xs, int x_pitch, int M, int K, const bf16* nw,
                                           const float* rs) {
-  const int kv = K >> 3;
-  for (int i = threadIdx.x; i < M * kv; i += PK_CONSUMERS) {
-    const int m = i / kv, j = i - m * kv;
-    uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
-    float f[8], w[8];
-    cvt8(*px, f);
-    cvt8(*reinterpret_cast<const uint4*>(nw + (size_t)j * 8), w);
-    const float r = rs[m];
-    uint4 o;
-    o.x = pack2(w[0] * rbf(f[0] * r), w[1] * rbf(f[1] * r));
-    o.y = pack2(w[2] * rbf(f[2] * r), w[3] * rbf(f[3] * r));
-    o.z = pack2(w[4] * rbf(f[4] * r), w[5] * rbf(f[5] * r));
-    o.w = pack2(w[6] * rbf(f[6] * r), w[7] * rbf(f[7] * r));
-    *px = o;
-  }
+  rms_rows_apply(xs, StagedOff{x_pitch}, M, K, nw, rs, threadIdx.x, PK_CONSUMERS);
 }
 
 // Stage rows [0, M) (M <= 16) of a global bf16 activation matrix (row stride ld) into xs, optionally applying the

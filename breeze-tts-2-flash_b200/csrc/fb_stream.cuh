@@ -16,7 +16,7 @@
 // Both sides walk the same static stage sequence, so the producer runs ahead of the consumers by the ring depth,
 // across task boundaries and grid barriers (weights never depend on activations).
 #pragma once
-#include "fb_common.cuh"
+#include "fb_norm.cuh"
 
 // The stage width (FB_ST_KC, default 2048 columns) and the stage layout (FB_ST_TMA) are per-translation-unit
 // choices; everything that depends on them lives in an inline namespace named after them, so units built
