@@ -1300,6 +1300,24 @@ DDLayout dd_layout(const fb_dd_config* c) {
   return s;
 }
 
+// Checks of the configuration's fields, made before anything is sized or enqueued from them.
+int dd_validate(const fb_dd_config* c) {
+  FB_CHECK_ARG(c->head_dim == 128 && c->batch >= 1 && c->batch <= DD_MAXB && (c->batch == 1 || c->batch % 2 == 0),
+               "dd_frame: head_dim must be 128, batch 1 or an even number up to %d", DD_MAXB);
+  FB_CHECK_ARG(c->vocab >= 1 && c->vocab <= DD_MAXV && c->codebook_size >= 1 && c->codebook_size <= c->vocab,
+               "dd_frame: vocab must be <= %d and codebook_size <= vocab", DD_MAXV);
+  FB_CHECK_ARG(c->n_decode >= 1 && c->n_decode <= 31, "dd_frame: n_decode must be 1..31");
+  FB_CHECK_ARG(c->heads >= 1 && c->kv_heads >= 1 && c->heads <= 64 && c->heads % c->kv_heads == 0,
+               "dd_frame: heads must be 1..64 and a multiple of kv_heads >= 1");
+  FB_CHECK_ARG(c->hidden >= 64 && c->embed_dim >= 64 && c->ffn >= 64 && c->hidden <= 65536 &&
+                   c->embed_dim <= 65536 && c->ffn <= 65536 && c->hidden % 64 == 0 && c->embed_dim % 64 == 0 &&
+                   c->ffn % 64 == 0,
+               "dd_frame: hidden, embed_dim and ffn must be positive multiples of 64 up to 65536");
+  FB_CHECK_ARG(c->layers >= 1 && c->layers <= DD_MAXL && c->layers_host,
+               "dd_frame: 1..%d layers, with the host copy of the layer table (layers_host)", DD_MAXL);
+  return FB_OK;
+}
+
 template <int G, int NT>
 int launch_dd(DDArgs& a, size_t smem, int grid, cudaStream_t st) {
   auto kern = dd_frame_kernel<G, NT>;
@@ -1355,15 +1373,7 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   static_assert(sizeof(fb_dd_layer) == sizeof(DDLayer), "fb_dd_layer layout");
   FB_CHECK_ARG(c && layers_dev && scratch && first_cb && bh && tokbuf && outtok && temp && topk && topp && dosample &&
                    gs && q, "dd_frame: null pointer argument");
-  FB_CHECK_ARG(c->head_dim == 128 && c->batch >= 1 && c->batch <= DD_MAXB && (c->batch == 1 || c->batch % 2 == 0),
-               "dd_frame: head_dim must be 128, batch 1 or an even number up to %d", DD_MAXB);
-  FB_CHECK_ARG(c->vocab >= 1 && c->vocab <= DD_MAXV && c->codebook_size >= 1 && c->codebook_size <= c->vocab,
-               "dd_frame: vocab must be <= %d and codebook_size <= vocab", DD_MAXV);
-  FB_CHECK_ARG(c->n_decode >= 1 && c->n_decode <= 31, "dd_frame: n_decode must be 1..31");
-  FB_CHECK_ARG(c->hidden % 64 == 0 && c->embed_dim % 64 == 0 && c->ffn % 64 == 0 && c->heads % c->kv_heads == 0,
-               "dd_frame: hidden, embed_dim and ffn must be multiples of 64, heads a multiple of kv_heads");
-  FB_CHECK_ARG(c->layers >= 1 && c->layers <= DD_MAXL && c->layers_host,
-               "dd_frame: 1..%d layers, with the host copy of the layer table (layers_host)", DD_MAXL);
+  if (int rc = dd_validate(c)) return rc;
   FB_CHECK_ARG(((uintptr_t)scratch & 255) == 0, "dd_frame: scratch must be 256-byte aligned");
   const DDLayout Lo = dd_layout(c);
   DDArgs a{};
@@ -1538,8 +1548,10 @@ extern "C" int flashb_dd_frame_noalloc(const fb_dd_config* c, const void* layers
                                        const float* gs, const float* q, float* dbg, const int64_t* forced,
                                        void* stream) {
   FB_CHECK_ARG(c, "dd_frame_noalloc: null config");
+  // every field is checked before the layout is computed from it, so no size below can wrap
+  if (int rc = dd_validate(c)) return rc;
   const DDLayout Lo = dd_layout(c);
-  FB_CHECK_ARG(Lo.total <= (size_t)FB_DD_NOALLOC_SCRATCH_BYTES,
+  FB_CHECK_ARG(Lo.total <= (size_t)FB_DD_NOALLOC_SCRATCH_BYTES && Lo.bar + sizeof(GridBar) <= Lo.total,
                "dd_frame_noalloc: this configuration needs %zu bytes of scratch; the built-in area holds %u "
                "(use flashb_dd_frame with a caller-owned buffer)", Lo.total, (unsigned)FB_DD_NOALLOC_SCRATCH_BYTES);
   int dev = 0;

@@ -165,42 +165,6 @@ int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl,
                         int S, int D, float scaling, int causal, int h0, int h1, void* out, int64_t o_sb,
                         int64_t o_sl, int64_t o_sh, void* stream);
 
-/* ---------------------------------------------------------------------------------------------- whole backbone step
- * One cooperative launch per decode step (one CTA per SM) replaces the reference's per-step sequence of 28 x 5 kernels
- * plus eager ops (flash/backbone.py:106-138 fused_decode_step inside UP/models/cudagraph/backbone_graph.py:254-285
- * _decode_step): embedding gather-sum, per layer RMSNorm + q|k|v GEMV, q/k norm + RoPE + KV write + GQA attention,
- * o_proj + residual, RMSNorm + gate|up + SiLU*up, down + residual, then final RMSNorm + fp32 lm_head + CFG.  Same
- * arithmetic as the separate entry points above.  Layer descriptors (fb_bb_layer[layers]) must be in device memory;
- * `scratch` is a device buffer of flashb_bb_scratch_bytes() bytes, 256-byte aligned, zeroed once before first use
- * (and after a reported device error).  With advance != 0 the step first does flashb_step_advance() on the device.
- * ids [batch, codebooks] int64; position_ids [batch] int64; cache_pos [1] int64 (device); mask [batch, 1, 1, S];
- * gs: device fp32 guidance scale; outputs hidden [batch, hidden] bf16, logits [batch, lm_rows] fp32,
- * cfg [batch/2 | 1, lm_rows] fp32. */
-typedef struct {
-  const void *ln1, *wq, *wk, *wv, *q_norm, *k_norm, *wo, *ln2, *wg, *wu, *wd; /* bf16, nn.Linear layouts */
-  void *k_cache, *v_cache;                                                    /* bf16 [batch, kv_heads, S, 128] */
-} fb_bb_layer;
-typedef struct {
-  int layers, batch, hidden, heads, kv_heads, head_dim, ffn;
-  int lm_rows;         /* lm_head output rows */
-  int codebooks, vocab; /* embedding table [codebooks * vocab, hidden] */
-  int cache_len;       /* static KV cache slots S */
-  int max_pos;         /* rows of the cos/sin tables */
-  float eps, qk_eps, scaling;
-  int64_t cache_stride_b, cache_stride_h; /* elements */
-  const void* embed;
-  const void* norm_w;
-  const float* lm_head32; /* [lm_rows, hidden] fp32 */
-  const void* cos_tab;    /* [max_pos, 128] bf16 */
-  const void* sin_tab;
-  uint64_t* trace;        /* optional: [grid][2 + 10 * layers] %globaltimer stamps per CTA (task ends, barrier exits) */
-} fb_bb_config;
-int64_t flashb_bb_scratch_bytes(const fb_bb_config* cfg);
-int64_t flashb_bb_layer_bytes(void);
-int flashb_bb_step(const fb_bb_config* cfg, const void* layers_dev, void* scratch, const int64_t* ids,
-                   int64_t* position_ids, int64_t* cache_pos, void* mask, int mask_is_bf16, int64_t m_sb,
-                   const float* gs, int advance, void* hidden_out, float* logits, float* cfg_out, void* stream);
-
 /* ---------------------------------------------------------------------------------------------- depth frame
  * Replaces the reference's depth frame megakernel dd2_init / dd2_frame (flash/csrc/depth_frame.cu:758-853, 923-934),
  * itself the kernel form of the official DepthDecoderGraph._full_loop (UP/models/cudagraph/depth_decoder_graph.py:
@@ -244,8 +208,10 @@ int flashb_dd_frame(const fb_dd_config* cfg, const void* layers_dev, void* scrat
  * instead a fixed area of FB_DD_NOALLOC_SCRATCH_BYTES (1 MiB) inside the library, reserved on every GPU that loads
  * it until the process exits; configurations whose flashb_dd_scratch_bytes() exceeds it are rejected with
  * FB_ERR_ARG.  Everything else is as for flashb_dd_frame; nothing is allocated and no allocating routine is called.
- * The first call on a device looks up the area's device address (with that device current); make that first call
- * before any stream capture.  Each call clears the area's barrier words on `stream` first; the rest of the area
+ * The first call on a device looks up the area's device address (with that device current) and keeps it until the
+ * process exits; make that first call before any stream capture, and make no call on a device after resetting it
+ * (cudaDeviceReset gives the area a new address, and the kept one would be stale).  The configuration is checked
+ * field by field before anything is sized or enqueued from it.  Each call clears the area's barrier words on `stream` first; the rest of the area
  * keeps the previous call's contents and needs no clearing.  All calls on a device share the one area: calls that
  * can overlap on the GPU (different streams, no ordering between them) race and corrupt each other. */
 #define FB_DD_NOALLOC_SCRATCH_BYTES (1u << 20)
