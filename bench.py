@@ -36,8 +36,8 @@ N_STREAMS = 64
 PROMPT = 512
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0)
 # dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch at the bench's default shape (8 streams
-# per launch, B = 16 rows, one lane's grid of 18 CTAs: the tcgen05 build): ncu --set full capture of the full-size
-# depth model, 2,174,940,416 B read + 7,735,296 B written (profiles/dd_frame_kernel_tcgen05_8streams_grid18.md).
+# per launch, B = 16 rows, one lane's grid of 18 CTAs: the tcgen05 build), from one ncu --set full capture of the
+# full-size depth model: 2,174,940,416 B read + 7,735,296 B written.
 DD_TRAFFIC_BYTES = 2182675712
 PREFILL_CFG = dict(B=2, NH=16, NKV=4, L=512, D=128, pads=(0, 37))
 

@@ -278,8 +278,11 @@ def gold_prefill(out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument('--ref', default=os.environ.get('BREEZE_REF', '/root/reference'))
+    ap.add_argument('--ref', default=os.environ.get('BREEZE_REF'),
+                    help='root of the reference checkout (or set BREEZE_REF)')
     args = ap.parse_args()
+    if not args.ref:
+        ap.error('the reference checkout is required: pass --ref or set BREEZE_REF')
     ref_env(args.ref)
     torch.manual_seed(0)
     out = {}
