@@ -81,16 +81,41 @@ def gold_attention(out):
     out['attn']['out_fp32'] = o32.numpy()
 
 
-def gold_gemv(out):
+def gold_attention1(out):
+    """Config 1 at its exact shapes: the bf16 eager attention and its fp32-upcast form, no mask (every key valid)."""
+    from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
+    c = synth.ATTN1
+    q, k, v = synth.attn1_inputs()
+    mod = _Mod(c['NH'] // c['NKV'])
+    o, _ = eager_attention_forward(mod, q, k, v, None, scaling=c['D'] ** -0.5)
+    o32, _ = eager_attention_forward(mod, q.float(), k.float(), v.float(), None, scaling=c['D'] ** -0.5)
+    out['attn1'] = dict(out=synth.np_bits(o), out_fp32=o32.numpy(), digest=synth.digest(q, k, v))
+
+
+def _swiglu_ref(c, x, gamma, wg, wu, wd):
     import models.breeze as mb
-    c = synth.GEMV
-    x, gamma, wg, wu, wd = synth.gemv_inputs()
     norm = mb.BreezeRMSNorm(c['K'], eps=c['eps']).to(torch.bfloat16)
     norm.weight.data.copy_(gamma)
     with torch.no_grad():
         h = norm(x)
         act = torch.nn.functional.silu(torch.nn.functional.linear(h, wg)) * torch.nn.functional.linear(h, wu)
         y = x + torch.nn.functional.linear(act, wd)
+    return h, act, y
+
+
+def gold_gemv2(out):
+    """Config 2 at its exact shapes through BreezeRMSNorm, F.linear and silu (UP/models/breeze.py:120-208)."""
+    c = synth.GEMV2
+    x, gamma, wg, wu, wd = synth.gemv2_inputs()
+    h, act, y = _swiglu_ref(c, x, gamma, wg, wu, wd)
+    out['gemv2'] = dict(norm=synth.np_bits(h), act=synth.np_bits(act), y=synth.np_bits(y),
+                        digest=synth.digest(x, gamma, wg, wu, wd))
+
+
+def gold_gemv(out):
+    c = synth.GEMV
+    x, gamma, wg, wu, wd = synth.gemv_inputs()
+    h, act, y = _swiglu_ref(c, x, gamma, wg, wu, wd)
     out['gemv'] = dict(norm=synth.np_bits(h), act=synth.np_bits(act), y=synth.np_bits(y),
                        digest=synth.digest(x, gamma, wg, wu, wd))
 
@@ -107,16 +132,16 @@ def _qwen3_config(c):
     return cfg
 
 
-def gold_backbone(out):
+def _official_backbone(c, w, dtype):
+    """The official BackboneGraph over transformers Qwen3 layers (the reference's backbone), weights from w, run in
+    ``dtype``, with the prefill KV of w written into its StaticCache and the generation state set."""
     from models.breeze_backbone_factory import BreezeBackboneAdapter
     from models.cudagraph.backbone_graph import BackboneGraph
-    c = synth.BACKBONE
-    w = synth.backbone_weights()
     cfg = _qwen3_config(c)
     layers, norm, rot = BreezeBackboneAdapter._create_qwen3_layers(cfg)
     model = BreezeBackboneAdapter(cfg, layers, norm, rot)
     inv = model.rotary_emb.inv_freq.clone()
-    model = model.to(torch.bfloat16)
+    model = model.to(dtype)
     model.rotary_emb.inv_freq = inv
     with torch.no_grad():
         for L, lw in zip(model.layers, w['layers']):
@@ -137,18 +162,26 @@ def gold_backbone(out):
     lm_head = torch.nn.Linear(c['H'], c['vocab'], bias=False)
     with torch.no_grad():
         lm_head.weight.copy_(w['lm_head'])
-    g = BackboneGraph(model, lm_head, model.embed_tokens, cfg, device='cpu', dtype=torch.bfloat16,
+    g = BackboneGraph(model, lm_head, model.embed_tokens, cfg, device='cpu', dtype=dtype,
                       max_seq_len=c['S'], guidance_scale=c['gs'], batch_size=c['B'])
     g.prepare_eager()
     P = c['prefill']
     with torch.inference_mode():
         for li, (k, v) in enumerate(w['kv']):
-            g.static_cache.layers[li].update(k, v)
+            g.static_cache.layers[li].update(k.to(dtype), v.to(dtype))
     am = torch.ones(c['B'], P, dtype=torch.long)
     for b, p in enumerate(c['pad']):
         am[b, :p] = 0
     g.set_generation_state(am)
     g._prefill_len = P
+    return g
+
+
+def gold_backbone(out):
+    c = synth.BACKBONE
+    w = synth.backbone_weights()
+    g = _official_backbone(c, w, torch.bfloat16)
+    P = c['prefill']
     hidden, cfg_logits = g.run(w['ids'], 0)
     kv_new = []
     for li in range(c['L']):
@@ -165,6 +198,52 @@ def gold_backbone(out):
                            digest=synth.digest(w['embed'], w['lm_head'], *[t for kv in w['kv'] for t in kv]))
 
 
+def gold_drift(out):
+    """End-to-end drift of the 28-layer config 3 step (KV 1023 + the new token), from the reference's own modules:
+
+    * ``bf16``: the official eager step in bf16 (the reference's arithmetic);
+    * ``fp32``: the same modules and weights run in fp32 (the exact model the bf16 run approximates);
+    * ``oracle``: the numpy restatement (tests' oracle): the bf16 eager rounding points of the official step, with
+      numpy's fp32 summation order instead of torch's.
+    The oracle is bit-exact to the official modules at reduced shapes; over 28 chained layers a different summation
+    order alone makes rare 1-ulp bf16 rounding flips that compound.  ``oracle_vs_bf16`` measures that compounding
+    between two implementations of the reference's own arithmetic, ``bf16_vs_fp32`` the reference's own error."""
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle import decode as dec
+    from oracle.bf16 import from_torch as ft
+    c = synth.BACKBONE28
+    w = synth.backbone_weights(c)
+    g = _official_backbone(c, w, torch.bfloat16)
+    g.run(w['ids'], 0)
+    lg16 = g.logits_buf.numpy().copy()
+    pids, mask = g.position_ids.numpy().copy(), g.attn_mask.float().numpy().copy()
+    del g
+    g = _official_backbone(c, w, torch.float32)
+    g.run(w['ids'], 0)
+    lg32 = g.logits_buf.numpy().copy()
+    del g
+    layers = [{k: ft(v) for k, v in L.items()} for L in w['layers']]
+    W = dec.BackboneWeights(layers, ft(w['norm']), ft(w['embed']), w['lm_head'].numpy(), c['vocab'], c['eps'],
+                            c['theta'])
+    P = c['prefill']
+    kcs = [np.zeros((c['B'], c['NKV'], c['S'], c['D']), np.float32) for _ in range(c['L'])]
+    vcs = [np.zeros_like(x) for x in kcs]
+    for li, (k, v) in enumerate(w['kv']):
+        kcs[li][:, :, :P] = ft(k)
+        vcs[li][:, :, :P] = ft(v)
+    _, lgo, _ = dec.backbone_step(W, w['ids'].numpy()[:, 0, :], kcs, vcs, mask, P, pids.reshape(-1), c['gs'])
+
+    def rel(a, b):
+        return float(np.max(np.abs(a - b)) / np.max(np.abs(b)))
+
+    d = dict(logits_bf16=lg16, logits_fp32=lg32, logits_oracle=lgo, bf16_vs_fp32=rel(lg16, lg32),
+             oracle_vs_bf16=rel(lgo, lg16), oracle_vs_fp32=rel(lgo, lg32),
+             argmax_bf16_fp32=float(np.mean(lg16.argmax(-1) == lg32.argmax(-1))),
+             digest=synth.digest(w['embed'], w['lm_head'], w['ids']))
+    print('drift:', {k: v for k, v in d.items() if not k.startswith('logits')}, flush=True)
+    out['drift'] = d
+
+
 def _patched_multinomial(qsrc):
     """torch.multinomial(probs, 1) -> argmax(probs / q[step]) for the official sampler (one q row set per call)."""
     state = {'i': 0}
@@ -177,12 +256,11 @@ def _patched_multinomial(qsrc):
     return mult, state
 
 
-def gold_depth(out):
+def _official_depth(c, w, dtype):
+    """The official DepthDecoderGraph (eager, on the CPU) in ``dtype`` with the weights of w."""
     import models.breeze as mb
     import models.breeze_base_config as bc
     import models.cudagraph.depth_decoder_graph as ddg
-    c = synth.DEPTH
-    w = synth.depth_weights()
     cfg = bc.BreezeDepthDecoderConfig(num_codebooks=c['ncb'], backbone_hidden_size=c['AE'], vocab_size=c['vocab'],
                                       hidden_size=c['H'], intermediate_size=c['F'], num_hidden_layers=c['L'],
                                       num_attention_heads=c['NH'], num_key_value_heads=c['NKV'], head_dim=c['D'],
@@ -190,7 +268,7 @@ def gold_depth(out):
     cfg._attn_implementation = 'eager'
     model = mb.BreezeDepthDecoderForCausalLM(cfg)
     inv = model.model.rotary_emb.inv_freq.clone()
-    model = model.to(torch.bfloat16)
+    model = model.to(dtype)
     model.model.rotary_emb.inv_freq = inv
     dm = model.model
     assert dm.backbone_hidden_state_projector is None
@@ -209,12 +287,19 @@ def gold_depth(out):
         dm.embed_tokens.weight.copy_(w['embed'])
         dm.inputs_embeds_projector.weight.copy_(w['proj'])
         dm.norm.weight.copy_(w['normf'])
-        model.codebooks_head.weight.data = w['head'].clone()
-    g = ddg.DepthDecoderGraph(model, cfg, device='cpu', dtype=torch.bfloat16, do_sample=True, top_k=c['topk'],
+        model.codebooks_head.weight.data = w['head'].clone().to(dtype)
+    g = ddg.DepthDecoderGraph(model, cfg, device='cpu', dtype=dtype, do_sample=True, top_k=c['topk'],
                               top_p=c['topp'], temperature=c['temp'], guidance_scale=c['gs'],
                               codec_codebook_size=c['codebook_size'], fast=False, debug=True, batch_size=c['B'])
     g.prepare_eager()
     _fix_depth_masks(g)
+    return g, ddg
+
+
+def gold_depth(out):
+    c = synth.DEPTH
+    w = synth.depth_weights()
+    g, ddg = _official_depth(c, w, torch.bfloat16)
     mult, st = _patched_multinomial([w['q'][s] for s in range(c['ncb'] - 1)])
     orig = ddg.torch.multinomial
     ddg.torch.multinomial = mult
@@ -225,6 +310,63 @@ def gold_depth(out):
     assert st['i'] == c['ncb'] - 1
     out['depth'] = dict(tokens=g.output_tokens.numpy().copy(), logits=g.debug_logits.numpy().copy(),
                         ret=toks.numpy().copy(), digest=synth.digest(w['embed'], w['proj'], w['head'], w['bh'], w['q']))
+
+
+def gold_depth_drift(out):
+    """Argmax agreement of the full config 4 depth logits (8 CFG pairs, 16 codebooks, teacher-forced on fixed random
+    tokens so every implementation sees the same inputs at every step), from the reference's own modules:
+    the official eager step in bf16, the same in fp32, and the oracle (the bf16 rounding points with numpy's
+    summation order).  Random-weight logits over 2048 ids have top-2 gaps down to ~1e-4 of their scale, so two
+    implementations of the same bf16 arithmetic that differ only in fp32 summation order disagree on a few rows."""
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle import depth as odepth
+    from oracle.bf16 import from_torch as ft
+    c = synth.DEPTH4
+    w = synth.depth_weights(c)
+    nd, B = c['ncb'] - 1, c['B']
+    forced = torch.randint(0, c['codebook_size'], (nd, B // 2), generator=torch.Generator().manual_seed(77))
+    logits = {}
+    for name, dt in (('bf16', torch.bfloat16), ('fp32', torch.float32)):
+        g, ddg = _official_depth(c, w, dt)
+        state = {'i': 0}
+
+        def mult(probs, n, *a, **kw):
+            t = forced[state['i']].view(-1, 1)
+            state['i'] += 1
+            return t
+
+        orig = ddg.torch.multinomial
+        ddg.torch.multinomial = mult
+        try:
+            g.run(w['bh'].to(dt), w['first'])
+        finally:
+            ddg.torch.multinomial = orig
+        assert state['i'] == nd
+        logits[name] = g.debug_logits.float().numpy().copy()
+        del g
+    layers = [{k: ft(v) for k, v in L.items()} for L in w['layers']]
+    W = odepth.DepthWeights(layers, ft(w['embed']), ft(w['proj']), ft(w['normf']), w['head'].numpy(), c['vocab'],
+                            c['codebook_size'], nd, c['eps'], c['theta'], c['NH'], c['NKV'])
+    half = B // 2
+    par = (np.full(half, c['temp'], np.float32), np.full(half, c['topk']), np.full(half, c['topp'], np.float32),
+           np.ones(half, np.int64), np.full(half, c['gs'], np.float32))
+    fo = np.concatenate([forced.numpy(), forced.numpy()], 1)
+    _, lgo, _ = odepth.depth_frame(W, ft(w['bh']), w['first'].numpy(), w['q'].numpy(), *par, forced=fo)
+    lg16, lg32 = logits['bf16'], logits['fp32']
+    lgo = np.asarray(lgo, np.float32).reshape(lg16.shape)
+
+    def agree(a, b):
+        return float(np.mean(a.argmax(-1) == b.argmax(-1)))
+
+    def rel(a, b):
+        return float(np.max(np.abs(a - b)) / np.max(np.abs(b)))
+
+    d = dict(logits_bf16=lg16, logits_fp32=lg32, logits_oracle=lgo, forced=forced.numpy(),
+             argmax_bf16_fp32=agree(lg16, lg32), argmax_oracle_bf16=agree(lgo, lg16), rel_bf16_fp32=rel(lg16, lg32),
+             rel_oracle_bf16=rel(lgo, lg16), rows=int(np.prod(lg16.shape[:-1])),
+             digest=synth.digest(w['embed'], w['proj'], w['head'], w['bh'], w['q']))
+    print('depth drift:', {k: v for k, v in d.items() if not k.startswith(('logits', 'forced'))}, flush=True)
+    out['depth_drift'] = d
 
 
 def _fix_depth_masks(g):
@@ -280,13 +422,18 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--ref', default=os.environ.get('BREEZE_REF'),
                     help='root of the reference checkout (or set BREEZE_REF)')
+    ap.add_argument('--only', default='', help='comma-separated fixture names to regenerate (default: all)')
     args = ap.parse_args()
     if not args.ref:
         ap.error('the reference checkout is required: pass --ref or set BREEZE_REF')
     ref_env(args.ref)
     torch.manual_seed(0)
     out = {}
-    for fn in (gold_attention, gold_gemv, gold_backbone, gold_depth, gold_sampler, gold_prefill):
+    only = set(args.only.split(',')) if args.only else None
+    for fn in (gold_attention, gold_attention1, gold_gemv, gold_gemv2, gold_backbone, gold_depth, gold_sampler,
+               gold_prefill, gold_drift, gold_depth_drift):
+        if only and fn.__name__[len('gold_'):] not in only:
+            continue
         fn(out)
         print('ok', fn.__name__, flush=True)
     for name, d in out.items():

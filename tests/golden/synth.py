@@ -44,6 +44,19 @@ def attn_inputs(c=ATTN):
     return q, k, v, mask
 
 
+# ---------------------------------------------------------------- decode attention at config 1's exact shapes
+# B 2 (CFG pair), 16 q / 4 KV heads, head_dim 128, KV length 1024, every key valid, q/k/v ~ N(0, 1), seed 0
+ATTN1 = dict(seed=0, B=2, NH=16, NKV=4, D=128, S=1024)
+
+
+def attn1_inputs(c=ATTN1):
+    g = gen(c['seed'])
+    q = randn_bf16(g, (c['B'], c['NH'], 1, c['D']))
+    k = randn_bf16(g, (c['B'], c['NKV'], c['S'], c['D']))
+    v = randn_bf16(g, (c['B'], c['NKV'], c['S'], c['D']))
+    return q, k, v
+
+
 # ---------------------------------------------------------------- RMSNorm + gate/up + SiLU + down (config 2, small)
 GEMV = dict(seed=101, M=2, K=512, F=384, eps=1e-6)
 
@@ -58,9 +71,30 @@ def gemv_inputs(c=GEMV):
     return x, gamma, wg, wu, wd
 
 
+# ---------------------------------------------------------------- config 2 at its exact shapes
+# x [2, 2048] ~ N(0, 1), gamma = 1 + 0.1 N(0, 1), eps 1e-6, W1 [6144, 2048] ~ N(0, 0.02) (rows 0..3071 gate,
+# 3072..6143 up), then the SwiGLU down projection W2 [2048, 3072] ~ N(0, 0.02) with the residual x; seed 1
+GEMV2 = dict(seed=1, M=2, K=2048, F=3072, eps=1e-6)
+
+
+def gemv2_inputs(c=GEMV2):
+    g = gen(c['seed'])
+    x = randn_bf16(g, (c['M'], c['K']))
+    gamma = randn_bf16(g, (c['K'],), std=0.1, mean=1.0)
+    w1 = randn_bf16(g, (2 * c['F'], c['K']), std=0.02)
+    w2 = randn_bf16(g, (c['K'], c['F']), std=0.02)
+    return x, gamma, w1[:c['F']], w1[c['F']:], w2
+
+
 # ---------------------------------------------------------------- backbone decode step (config 3, reduced)
 BACKBONE = dict(seed=102, B=2, H=512, NH=8, NKV=2, D=128, F=1024, L=2, vocab=65, ncb=16, theta=1e6, eps=1e-6,
                 S=96, prefill=60, pad=(0, 3), gs=4.0)
+
+
+# the full config 3 model (28 layers, hidden 2048, FFN 6144, 16 q / 4 KV heads), KV length 1023 + the new token: the
+# end-to-end drift study of make_golden.py (bf16 eager vs fp32, and the oracle's summation order vs torch's)
+BACKBONE28 = dict(seed=106, B=2, H=2048, NH=16, NKV=4, D=128, F=6144, L=28, vocab=2049, ncb=16, theta=1e6, eps=1e-6,
+                  S=1024, prefill=1023, pad=(0, 3), gs=4.0)
 
 
 def backbone_weights(c=BACKBONE):
@@ -86,6 +120,11 @@ def backbone_weights(c=BACKBONE):
 # ---------------------------------------------------------------- depth frame (config 4, reduced)
 DEPTH = dict(seed=103, B=2, H=256, AE=384, NH=2, NKV=1, D=128, F=512, L=2, vocab=64, codebook_size=60, ncb=6,
              theta=500000.0, eps=1e-5, gs=4.0, temp=0.9, topk=50, topp=1.0, q_seed=42)
+
+
+# the full config 4 depth decoder with 8 CFG pairs (16 rows): the argmax-agreement study of make_golden.py
+DEPTH4 = dict(seed=107, B=16, H=1024, AE=2048, NH=8, NKV=2, D=128, F=4096, L=4, vocab=2048, codebook_size=2048,
+              ncb=17, theta=500000.0, eps=1e-5, gs=4.0, temp=0.9, topk=50, topp=1.0, q_seed=42)
 
 
 def depth_weights(c=DEPTH):

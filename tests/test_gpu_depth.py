@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import assert_argmax_agree, assert_close, np32
+from gpu_util import DEPTH_ARGMAX_MIN, assert_argmax_agree, assert_close, np32
 from oracle import depth as odepth
 from oracle import sampler as osmp
 
@@ -103,7 +103,7 @@ def test_depth_forced_logits_match_oracle(B, grid):
                                             m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
     for s in range(c.n_decode):
         assert_close(logits[s], lg_ref[s], what=f'step {s} logits')
-    assert_argmax_agree(logits, lg_ref, what='depth logits')
+    assert_argmax_agree(logits, lg_ref, min_frac=DEPTH_ARGMAX_MIN, what='depth logits')
     np.testing.assert_array_equal(m.tok_buf.cpu().numpy(), np.clip(forced[-1], 0, c.vocab - 1))
     _check_sampler(m, logits, outtok)
 
@@ -148,7 +148,7 @@ def test_depth_full_size_forced_and_sampler(B, grid):
                                       m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
     for s in range(c.n_decode):
         assert_close(logits[s], lg_ref[s], what=f'step {s} logits')
-    assert_argmax_agree(logits, lg_ref, what='depth logits')
+    assert_argmax_agree(logits, lg_ref, min_frac=DEPTH_ARGMAX_MIN, what='depth logits')
     _check_sampler(m, logits, outtok)
 
 

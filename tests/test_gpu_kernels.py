@@ -78,6 +78,24 @@ def test_config2_gateup_then_down(ops, M):
     assert np.mean(np32(act) == ref_act) > 0.9
 
 
+def test_config2_against_reference_golden(ops):
+    """BASELINE config 2 exactly (seed 1, M 2), checked directly against the reference's own BreezeRMSNorm /
+    F.linear / silu output (tests/golden/gemv2.npz)."""
+    import synth
+    from oracle.bf16 import bits_to_f32
+    fx, _ = ops
+    z = np.load(synth.__file__.rsplit('/', 1)[0] + '/gemv2.npz')
+    x, gamma, wg, wu, wd = [t.cuda() for t in synth.gemv2_inputs()]
+    M, F, K = x.shape[0], wg.shape[0], x.shape[1]
+    act = torch.empty(M, F, dtype=torch.bfloat16, device='cuda')
+    y = torch.empty(M, K, dtype=torch.bfloat16, device='cuda')
+    fx.gemv_gateup(x, gamma, synth.GEMV2['eps'], wg, wu, act)
+    fx.gemv_resid(act, wd, x, y)
+    torch.cuda.synchronize()
+    assert_close(np32(act), bits_to_f32(z['act']), what='config 2 act vs reference')
+    assert_close(np32(y), bits_to_f32(z['y']), what='config 2 y vs reference')
+
+
 def test_rmsnorm(ops):
     fx, _ = ops
     x = randn((4, 2048), 31, 3.0)
@@ -138,6 +156,25 @@ def test_attn_decode(ops, NH, NKV, S, valid):
 
 
 
+def test_attn_decode_config1_against_reference_golden(ops):
+    """BASELINE config 1 exactly (seed 0, B 2, 16 q / 4 KV, KV 1024, every key valid), checked directly against the
+    reference's own eager attention output (tests/golden/attn1.npz), bf16 and fp32-upcast forms."""
+    import synth
+    from oracle.bf16 import bits_to_f32
+    _, ax = ops
+    z = np.load(synth.__file__.rsplit('/', 1)[0] + '/attn1.npz')
+    q, k, v = synth.attn1_inputs()
+    c = synth.ATTN1
+    B, NH, NKV, S = c['B'], c['NH'], c['NKV'], c['S']
+    mask = torch.zeros(B, 1, 1, S, dtype=torch.bfloat16, device='cuda')
+    out = torch.empty(B, 1, NH, 128, dtype=torch.bfloat16, device='cuda')
+    sc, cm, part, cnt = _attn_ws(B, NH, NKV, S)
+    ax.attn_decode(q.cuda(), k.cuda(), v.cuda(), mask, 128 ** -0.5, sc, cm, part, cnt, out)
+    torch.cuda.synchronize()
+    assert_close(np32(out), bits_to_f32(z['out']), what='config 1 vs reference bf16')
+    assert_close(np32(out), z['out_fp32'], what='config 1 vs reference fp32 upcast')
+
+
 def test_attn_decode_fp32_mask_and_dead_row(ops):
     _, ax = ops
     B, NH, NKV, S = 2, 16, 4, 300
@@ -184,6 +221,7 @@ def test_attn_decode_fused(ops, NKV, S, pos):
 
 
 @pytest.mark.parametrize('B,NKV,S,pos,budget', [(16, 4, 600, 515, 18), (128, 4, 576, 515, 0), (40, 8, 300, 63, 0),
+                                                 (128, 4, 4096, 4095, 0),     # config 3's longest cache, 128 rows
                                                  (24, 2, 200, 64, 8), (64, 4, 130, 0, 64), (128, 16, 96, 95, 0),
                                                  (32, 4, 301, 150, 16)])
 def test_attn_decode_fused_tensor_cores(ops, B, NKV, S, pos, budget):
