@@ -55,13 +55,15 @@ def args_():
     p.add_argument('--group', type=int, default=8, choices=[1, 2, 4, 8],
                    help='streams decoded together per launch (their GEMV rows share every weight read)')
     p.add_argument('--lanes', type=int, default=8,
-                   help='GPU lanes: slots run on this many CUDA streams side by side, each sized for 1/lanes of the SMs')
+                   help='GPU lanes: slots run on this many CUDA streams side by side, each sized for 1/lanes of the '
+                        'SMs')
     p.add_argument('--backbone', default='shared', choices=['shared', 'lanes'],
                    help='shared: one backbone graph for every slot on the whole GPU (row groups of 64 per GEMV '
                         'launch); lanes: a backbone graph per slot on its lane')
     p.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample length')
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
+    p.add_argument('--no-per-config', action='store_true', help='skip the per-config kernel figures (configs 1-3)')
     return p.parse_args()
 
 
@@ -281,6 +283,124 @@ def measure_prefill(dev, world, rank, iters=50, warmup=5):
                 f'{list(c["pads"])}', parallel='KV-head groups + NCCL all-gather' if sharded else 'whole call per rank',
                 ms=round(ms, 4), algorithmic_flops=fl, achieved=round(ach, 2), unit='TFLOP/s', bound='tensor',
                 peak=peak, frac=round(ach / peak, 4), launches_per_call=1 + (1 if sharded else 0))
+
+
+# ------------------------------------------------------------------------------------------------ per-config kernels
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _time_calls(fn, n, dev, warmup=5):
+    """Average device time (ms) of fn(i) over n calls, i = 0..n-1, CUDA events on the current stream."""
+    import torch
+    for i in range(warmup):
+        fn(i)
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(st)
+    for i in range(n):
+        fn(i)
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / n
+
+
+def _roof(nbytes, ms, pk, **kw):
+    ach = nbytes / (ms / 1e3) / 1e9
+    return dict(us=round(ms * 1e3, 2), algorithmic_bytes=int(nbytes), achieved=round(ach, 1), unit='GB/s',
+                peak=pk['hbm_gbs'], frac=round(ach / pk['hbm_gbs'], 4), **kw)
+
+
+def measure_per_config(dev, iters=200):
+    """BASELINE configs 1-3 at their own shapes, each on the kernels behind its reference entry point, inputs
+    resident and larger than L2 between calls (distinct buffer sets are rotated, their total above L2):
+
+    * config 1 -- attn_decode: B 2, 16 q / 4 KV heads, KV 1024, every key valid;
+    * config 2 -- gemv_gateup [6144 x 2048] (RMSNorm + SiLU*up) then gemv_resid [2048 x 3072], M = 2;
+    * config 3 -- the whole 28-layer backbone decode step (B 2, CUDA graph of its 142 launches) at KV 256 / 1024 /
+      4096 (weights 2.70 GB > L2 on their own).
+    Returns the bench line's ``per_config`` object."""
+    import torch
+    from flashb import kernels
+    from flashb.engine import BackboneConfig, SyntheticBackboneGraph, backbone_step_bytes
+    pk = peaks()
+    ax, fx = kernels.attn(), kernels.fused()
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+
+    def rn(shape, std=1.0, mean=0.0):
+        return (torch.randn(shape, generator=g, device=dev) * std + mean).to(torch.bfloat16)
+
+    out = {}
+    # ---- config 1
+    B, NH, NKV, S, D = 2, 16, 4, 1024, 128
+    kvb = 2 * B * NKV * S * D * 2
+    nset = 2 * L2_BYTES // kvb + 1
+    qs = [rn((B, NH, 1, D)) for _ in range(nset)]
+    ks = [rn((B, NKV, S, D)) for _ in range(nset)]
+    vs = [rn((B, NKV, S, D)) for _ in range(nset)]
+    mask = torch.zeros(B, 1, 1, S, dtype=torch.bfloat16, device=dev)
+    o = torch.empty(B, 1, NH, D, dtype=torch.bfloat16, device=dev)
+    nws = kernels.attn_ws_floats(B, NH, NKV, S)
+    ws = (torch.empty(1, device=dev), torch.empty(1, device=dev), torch.empty(max(1, nws), device=dev),
+          torch.zeros(B * NKV, dtype=torch.int32, device=dev))
+    ms = _time_calls(lambda i: ax.attn_decode(qs[i % nset], ks[i % nset], vs[i % nset], mask, D ** -0.5, *ws, o),
+                     iters, dev)
+    ms_warm = _time_calls(lambda i: ax.attn_decode(qs[0], ks[0], vs[0], mask, D ** -0.5, *ws, o), iters, dev)
+    nbytes = kvb + 2 * B * NH * D * 2
+    out['config1_attn_decode'] = _roof(nbytes, ms, pk, shape='B 2, 16 q / 4 KV heads, head_dim 128, KV 1024',
+                                       us_l2_resident=round(ms_warm * 1e3, 2),
+                                       rotation=f'{nset} buffer sets ({nset * kvb / 2 ** 20:.0f} MiB)')
+    del qs, ks, vs
+    # ---- config 2
+    M, K, F = 2, 2048, 3072
+    wbytes = (2 * F * K + K * F) * 2
+    nset = 2 * L2_BYTES // wbytes + 1
+    w1 = [rn((2 * F, K), 0.02) for _ in range(nset)]
+    w2 = [rn((K, F), 0.02) for _ in range(nset)]
+    x, gamma = rn((M, K)), rn((K,), 0.1, 1.0)
+    act = torch.empty(M, F, dtype=torch.bfloat16, device=dev)
+    y = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+
+    def pair(i):
+        W = w1[i % nset]
+        fx.gemv_gateup(x, gamma, 1e-6, W[:F], W[F:], act)
+        fx.gemv_resid(act, w2[i % nset], x, y)
+
+    ms = _time_calls(pair, iters, dev)
+    ms_gu = _time_calls(lambda i: fx.gemv_gateup(x, gamma, 1e-6, w1[i % nset][:F], w1[i % nset][F:], act), iters, dev)
+    ms_dn = _time_calls(lambda i: fx.gemv_resid(act, w2[i % nset], x, y), iters, dev)
+    io = (M * K * 2 + K * 2 + M * F * 2) + (M * F * 2 + 2 * M * K * 2)
+    out['config2_gemv_pair'] = _roof(wbytes + io, ms, pk, shape='RMSNorm + gate|up [6144 x 2048] + SiLU*up, then '
+                                     'down [2048 x 3072] + residual, M 2', rotation=f'{nset} weight sets',
+                                     gateup=_roof(2 * F * K * 2 + M * K * 2 + M * F * 2, ms_gu, pk),
+                                     down=_roof(K * F * 2 + M * F * 2 + 2 * M * K * 2, ms_dn, pk))
+    del w1, w2
+    # ---- config 3
+    bcfg = BackboneConfig()
+    Smax = 4096
+    bb = SyntheticBackboneGraph(bcfg, batch_size=2, max_seq_len=Smax, device=dev, seed=2)
+    bb.fill_kv(Smax - 1)
+    bb.input_ids_buf.copy_(torch.randint(0, bcfg.vocab, (2, 1, bcfg.codebooks), generator=torch.Generator()
+                                         .manual_seed(3)).to(dev))
+    sweep = {}
+    graph = None
+    for L in (256, 1024, 4096):
+        bb.set_position(L - 1)
+        if graph is None:
+            for _ in range(3):
+                bb.decode_step()
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                bb.decode_step()
+        ms = _time_calls(lambda i: graph.replay(), 20, dev, warmup=3)
+        sweep[f'kv{L}'] = _roof(backbone_step_bytes(bcfg, 2, L), ms, pk)
+    out['config3_backbone_step'] = dict(shape='28 layers, hidden 2048, 16 q / 4 KV heads, FFN 6144, B 2; weights '
+                                        '+ valid KV + fp32 lm_head per step', launches=2 + 5 * bcfg.layers, **sweep)
+    del graph, bb
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------------------------------------------------------ GPU
@@ -505,6 +625,7 @@ def main():
         barrier()
         lat = round(maxred(l0.elapsed_time(l1) / LAT_FRAMES), 4)
     prefill = measure_prefill(dev, world, rank) if case == 'frame' else None
+    per_config = measure_per_config(dev) if case == 'frame' and not a.no_per_config else None
     launches = eng.launches_per_frame() if case == 'frame' else (
         1 if case == 'depth' else eng.launches_per_frame() - 1)
     if rank == 0:
@@ -517,7 +638,8 @@ def main():
                                 [kv0, kv1], case),
             frames_per_s_per_gpu=round(value / world, 3), tokens_per_s=round(value * 17, 1),
             frame_ms_single_stream=lat,
-            roofline=roof, roofline_backbone=roof_bb, prefill=prefill, cpu_baseline=cpu, e2e=e2e,
+            roofline=roof, roofline_backbone=roof_bb, prefill=prefill, per_config=per_config, cpu_baseline=cpu,
+            e2e=e2e,
             gpu_launches=int(launches * frames / a.group), clocks=clk)
         print(json.dumps(line), flush=True)
     if world > 1:
