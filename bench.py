@@ -51,7 +51,8 @@ def args_():
     p.add_argument('--streams', type=int, default=N_STREAMS,
                    help='streams per GPU (the job serves streams x N: weak scaling, one replica per GPU)')
     p.add_argument('--prompt', type=int, default=PROMPT)
-    p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone', 'prefill'])
+    p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone', 'prefill', 'config1', 'config2',
+                                                      'config3'])
     p.add_argument('--group', type=int, default=8, choices=[1, 2, 4, 8],
                    help='streams decoded together per launch (their GEMV rows share every weight read)')
     p.add_argument('--lanes', type=int, default=8,
@@ -145,38 +146,67 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------------ CPU port
-def cpu_frames(seconds, max_frames=None, warmup=1, prompt=PROMPT, seed=0):
-    """The oracle port of one frame (oracle/frame.py) on this host: returns (frames/s, frames timed, threads)."""
-    import numpy as np
-    from oracle import frame as ofr
-    rng = np.random.default_rng(seed)
-    BW = ofr.synthetic_backbone(rng, 28, 2048, 16, 4, 6144, 2049, 17)
-    DW = ofr.synthetic_depth(rng, 4, 1024, 2048, 8, 2, 4096, 2048, 2048, 16)
-    n_total = warmup + (max_frames if max_frames else 10 ** 6)
-    st = ofr.FrameStream(BW, 16, prompt, prompt + min(n_total, 4096) + 2, rng, 2048)
-    q = rng.exponential(size=(16, 1, 2048)).astype(np.float32)
-    params = (np.array([0.9], np.float32), np.array([50]), np.array([1.0], np.float32), np.array([1]),
-              np.array([4.0], np.float32))
-    for _ in range(warmup):
-        ofr.frame(BW, DW, st, 2048, 4.0, params, q)
-    n = 0
-    t0 = time.perf_counter()
-    while True:
-        ofr.frame(BW, DW, st, 2048, 4.0, params, q)
-        n += 1
-        el = time.perf_counter() - t0
-        if (max_frames and n >= max_frames) or (not max_frames and el >= seconds and n >= 2):
-            break
+# Slots of the CPU port's KV cache: the capacity of the reference server's StaticCache (max_seq_len 2048 in
+# UP/breeze_infer/api.py).  The eager attention of the reference attends over every slot of its static cache (the
+# invalid ones masked), so the port does the same whatever the prompt length.
+CPU_CACHE_LEN = 2048
+
+
+def cpu_threads():
+    """Host cores this process may run on (its CPU affinity), the BLAS thread count of both CPU legs."""
     try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get('num_threads', 1) for i in threadpool_info()] or [1])
+        return len(os.sched_getaffinity(0))
     except Exception:
-        threads = os.cpu_count()
-    return n / el, n, el, threads
+        return os.cpu_count() or 1
+
+
+def cpu_frames(seconds=None, frames=None, warmup=1, prompt=PROMPT, seed=0, cache_len=CPU_CACHE_LEN, layers=28):
+    """The oracle port of one stream's frame (oracle/frame.py: 28-layer backbone step + greedy codebook 0 + 16-codebook
+    depth frame, numpy + the C sampler) on this host, its BLAS set to cpu_threads() threads whatever OMP_NUM_THREADS
+    a launcher exported.  Times `frames` frames, or frames until `seconds` have passed (at least 2), after `warmup`
+    untimed ones.  Returns dict(value frames/s, frames, seconds, threads, cache_len)."""
+    import numpy as np
+    from threadpoolctl import threadpool_limits
+    from oracle import frame as ofr
+    threads = cpu_threads()
+    with threadpool_limits(limits=threads):
+        rng = np.random.default_rng(seed)
+        BW = ofr.synthetic_backbone(rng, layers, 2048, 16, 4, 6144, 2049, 17)
+        DW = ofr.synthetic_depth(rng, 4, 1024, 2048, 8, 2, 4096, 2048, 2048, 16)
+        st = ofr.FrameStream(BW, 16, prompt, cache_len, rng, 2048)
+        q = rng.exponential(size=(16, 1, 2048)).astype(np.float32)
+        params = (np.array([0.9], np.float32), np.array([50]), np.array([1.0], np.float32), np.array([1]),
+                  np.array([4.0], np.float32))
+        room = cache_len - prompt - 1               # frames the cache can still take
+        for _ in range(min(warmup, room)):
+            ofr.frame(BW, DW, st, 2048, 4.0, params, q)
+        n = 0
+        t0 = time.perf_counter()
+        while n < room - warmup:
+            ofr.frame(BW, DW, st, 2048, 4.0, params, q)
+            n += 1
+            el = time.perf_counter() - t0
+            if (frames and n >= frames) or (not frames and el >= seconds and n >= 2):
+                break
+    return dict(value=n / el, frames=n, seconds=el, threads=threads, cache_len=cache_len)
+
+
+def cpu_sample(r, prompt):
+    return (f"{r['frames']} frames of one stream ({r['seconds']:.1f} s after 1 warm-up frame): numpy/C oracle port of "
+            f"the 28-layer backbone step (KV cache of {r['cache_len']} slots, {prompt} prompt slots valid + one per "
+            f"frame) + greedy codebook 0 + 16-codebook depth frame, {r['threads']} BLAS threads")
+
+
+def reference_config(a, threads):
+    """The `config` of the --impl reference line: what that arm runs (one stream on the host CPU)."""
+    return dict(workload='one stream\'s streaming frame on the host CPU: the oracle port of the reference path '
+                         '(numpy + C sampler): 28-layer backbone decode step, greedy codebook 0, 16-codebook depth '
+                         'frame with CFG top-k sampling', streams=1, prompt_len=a.prompt, cache_len=CPU_CACHE_LEN,
+                threads=threads, device='cpu', step='one frame of the stream')
 
 
 def frame_config(a, world, my_streams, lanes, shared, lane_sms, kv_len, case='frame'):
-    """The `config` of a bench line: the workload both arms (flashb and --impl reference) report."""
+    """The `config` of the flashb arm's bench line."""
     wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + greedy '
                    f'codebook-0 + 16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9); '
                    f'{a.group} stream(s) per depth launch share the weight reads; {lanes} lane(s) of the GPU side '
@@ -195,43 +225,19 @@ def frame_config(a, world, my_streams, lanes, shared, lane_sms, kv_len, case='fr
 
 
 def run_reference(a):
-    """--impl reference: the CPU oracle port of the frame, one frame per step (rank 0 only)."""
+    """--impl reference: the CPU oracle port of one stream's frame, one frame per step (rank 0 only; other ranks exit
+    0 without work), the same function and cache capacity as the flashb arm's cpu_baseline."""
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return
-    import numpy as np
-    from oracle import frame as ofr
-    rng = np.random.default_rng(0)
-    BW = ofr.synthetic_backbone(rng, 28, 2048, 16, 4, 6144, 2049, 17)
-    DW = ofr.synthetic_depth(rng, 4, 1024, 2048, 8, 2, 4096, 2048, 2048, 16)
-    st = ofr.FrameStream(BW, 16, a.prompt, a.prompt + a.warmup + a.steps + 2, rng, 2048)
-    q = rng.exponential(size=(16, 1, 2048)).astype(np.float32)
-    params = (np.array([0.9], np.float32), np.array([50]), np.array([1.0], np.float32), np.array([1]),
-              np.array([4.0], np.float32))
-    for _ in range(a.warmup):
-        ofr.frame(BW, DW, st, 2048, 4.0, params, q)
-    t0 = time.perf_counter()
-    for _ in range(a.steps):
-        ofr.frame(BW, DW, st, 2048, 4.0, params, q)
-    el = time.perf_counter() - t0
-    try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get('num_threads', 1) for i in threadpool_info()] or [1])
-    except Exception:
-        threads = os.cpu_count()
-    v = a.steps / el
-    sample = (f'{a.steps} frames of one stream (backbone step at KV {a.prompt}+t + 16-codebook depth frame), '
-              f'numpy oracle port, {threads} BLAS threads')
-    # the flashb arm's workload (every stream's frame counts the same), timed on a bounded sample of it
-    world = max(1, a.gpus)
-    lanes = max(1, min(a.lanes, a.streams // a.group))
-    shared = a.backbone == 'shared' and 2 * a.streams <= 128
-    cfg = frame_config(a, world, a.streams, lanes, shared, None, [a.prompt + 1, a.prompt + a.warmup + a.steps])
+    r = cpu_frames(frames=a.steps, warmup=a.warmup, prompt=a.prompt)
+    v = r['value']
     print(json.dumps(dict(
-        impl='reference', metric='frames/s', value=round(v, 4), unit='frames/s', n_gpus=a.gpus, steps=a.steps,
-        warmup=a.warmup, ms_per_step=round(el / a.steps * 1e3, 3), higher_is_better=True, scaling='weak',
-        vs_baseline=None, dtype='bf16', data='synthetic', config=cfg,
-        cpu_baseline=dict(value=round(v, 4), unit='frames/s', cores=threads, kind='port', sample=sample),
+        impl='reference', metric='frames/s', value=round(v, 4), unit='frames/s', n_gpus=a.gpus, steps=r['frames'],
+        warmup=a.warmup, ms_per_step=round(r['seconds'] / r['frames'] * 1e3, 3), higher_is_better=True,
+        scaling='weak', vs_baseline=None, dtype='bf16', data='synthetic', config=reference_config(a, r['threads']),
+        cpu_baseline=dict(value=round(v, 4), unit='frames/s', cores=r['threads'], kind='port',
+                          sample=cpu_sample(r, a.prompt)),
         e2e=dict(value=round(v, 4), unit='frames/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))), flush=True)
 
 
@@ -305,34 +311,53 @@ def _time_calls(fn, n, dev, warmup=5):
     return e0.elapsed_time(e1) / n
 
 
+def _time_graph(fn, n, dev, reps=5):
+    """Average device time (ms) per call of fn(i), i = 0..n-1, captured back to back in one CUDA graph (as the decode
+    step runs them: no host work between calls, consecutive launches chained by programmatic dependent launch) and
+    replayed ``reps`` times after one untimed replay."""
+    import torch
+    for i in range(3):
+        fn(i)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n):
+            fn(i)
+    g.replay()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(st)
+    for _ in range(reps):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    del g
+    return e0.elapsed_time(e1) / (reps * n)
+
+
 def _roof(nbytes, ms, pk, **kw):
     ach = nbytes / (ms / 1e3) / 1e9
     return dict(us=round(ms * 1e3, 2), algorithmic_bytes=int(nbytes), achieved=round(ach, 1), unit='GB/s',
                 peak=pk['hbm_gbs'], frac=round(ach / pk['hbm_gbs'], 4), **kw)
 
 
-def measure_per_config(dev, iters=200):
-    """BASELINE configs 1-3 at their own shapes, each on the kernels behind its reference entry point, inputs
-    resident and larger than L2 between calls (distinct buffer sets are rotated, their total above L2):
-
-    * config 1 -- attn_decode: B 2, 16 q / 4 KV heads, KV 1024, every key valid;
-    * config 2 -- gemv_gateup [6144 x 2048] (RMSNorm + SiLU*up) then gemv_resid [2048 x 3072], M = 2;
-    * config 3 -- the whole 28-layer backbone decode step (B 2, CUDA graph of its 142 launches) at KV 256 / 1024 /
-      4096 (weights 2.70 GB > L2 on their own).
-    Returns the bench line's ``per_config`` object."""
+def _rn(dev, seed):
     import torch
-    from flashb import kernels
-    from flashb.engine import BackboneConfig, SyntheticBackboneGraph, backbone_step_bytes
-    pk = peaks()
-    ax, fx = kernels.attn(), kernels.fused()
     g = torch.Generator(device=dev)
-    g.manual_seed(0)
+    g.manual_seed(seed)
 
     def rn(shape, std=1.0, mean=0.0):
         return (torch.randn(shape, generator=g, device=dev) * std + mean).to(torch.bfloat16)
+    return rn
 
-    out = {}
-    # ---- config 1
+
+def measure_config1(dev, iters=128):
+    """Config 1: attn_decode at B 2, 16 q / 4 KV heads, head_dim 128, KV 1024, every key valid.  Distinct q/K/V sets
+    are rotated (their total above L2), so every call reads its K/V from HBM."""
+    import torch
+    from flashb import kernels
+    pk, ax, rn = peaks(), kernels.attn(), _rn(dev, 0)
     B, NH, NKV, S, D = 2, 16, 4, 1024, 128
     kvb = 2 * B * NKV * S * D * 2
     nset = 2 * L2_BYTES // kvb + 1
@@ -344,15 +369,26 @@ def measure_per_config(dev, iters=200):
     nws = kernels.attn_ws_floats(B, NH, NKV, S)
     ws = (torch.empty(1, device=dev), torch.empty(1, device=dev), torch.empty(max(1, nws), device=dev),
           torch.zeros(B * NKV, dtype=torch.int32, device=dev))
-    ms = _time_calls(lambda i: ax.attn_decode(qs[i % nset], ks[i % nset], vs[i % nset], mask, D ** -0.5, *ws, o),
-                     iters, dev)
-    ms_warm = _time_calls(lambda i: ax.attn_decode(qs[0], ks[0], vs[0], mask, D ** -0.5, *ws, o), iters, dev)
+    def call(i):
+        j = i % nset
+        ax.attn_decode(qs[j], ks[j], vs[j], mask, D ** -0.5, *ws, o)
+
+    ms = _time_graph(call, iters, dev)
+    ms_warm = _time_graph(lambda i: ax.attn_decode(qs[0], ks[0], vs[0], mask, D ** -0.5, *ws, o), iters, dev)
+    ms_one = _time_calls(call, iters, dev)
     nbytes = kvb + 2 * B * NH * D * 2
-    out['config1_attn_decode'] = _roof(nbytes, ms, pk, shape='B 2, 16 q / 4 KV heads, head_dim 128, KV 1024',
-                                       us_l2_resident=round(ms_warm * 1e3, 2),
-                                       rotation=f'{nset} buffer sets ({nset * kvb / 2 ** 20:.0f} MiB)')
-    del qs, ks, vs
-    # ---- config 2
+    return _roof(nbytes, ms, pk, shape='B 2, 16 q / 4 KV heads, head_dim 128, KV 1024',
+                 timing=f'{iters} calls back to back in a CUDA graph', us_l2_resident=round(ms_warm * 1e3, 2),
+                 us_eager_calls=round(ms_one * 1e3, 2),
+                 rotation=f'{nset} buffer sets ({nset * kvb / 2 ** 20:.0f} MiB)')
+
+
+def measure_config2(dev, iters=64):
+    """Config 2: gemv_gateup [6144 x 2048] (RMSNorm + SiLU*up) then gemv_resid [2048 x 3072], M = 2; weight sets
+    rotated above L2."""
+    import torch
+    from flashb import kernels
+    pk, fx, rn = peaks(), kernels.fused(), _rn(dev, 1)
     M, K, F = 2, 2048, 3072
     wbytes = (2 * F * K + K * F) * 2
     nset = 2 * L2_BYTES // wbytes + 1
@@ -367,25 +403,34 @@ def measure_per_config(dev, iters=200):
         fx.gemv_gateup(x, gamma, 1e-6, W[:F], W[F:], act)
         fx.gemv_resid(act, w2[i % nset], x, y)
 
-    ms = _time_calls(pair, iters, dev)
-    ms_gu = _time_calls(lambda i: fx.gemv_gateup(x, gamma, 1e-6, w1[i % nset][:F], w1[i % nset][F:], act), iters, dev)
-    ms_dn = _time_calls(lambda i: fx.gemv_resid(act, w2[i % nset], x, y), iters, dev)
+    ms = _time_graph(pair, iters, dev)
+    ms_gu = _time_graph(lambda i: fx.gemv_gateup(x, gamma, 1e-6, w1[i % nset][:F], w1[i % nset][F:], act), iters,
+                        dev)
+    ms_dn = _time_graph(lambda i: fx.gemv_resid(act, w2[i % nset], x, y), iters, dev)
+    ms_one = _time_calls(pair, iters, dev)
     io = (M * K * 2 + K * 2 + M * F * 2) + (M * F * 2 + 2 * M * K * 2)
-    out['config2_gemv_pair'] = _roof(wbytes + io, ms, pk, shape='RMSNorm + gate|up [6144 x 2048] + SiLU*up, then '
-                                     'down [2048 x 3072] + residual, M 2', rotation=f'{nset} weight sets',
-                                     gateup=_roof(2 * F * K * 2 + M * K * 2 + M * F * 2, ms_gu, pk),
-                                     down=_roof(K * F * 2 + M * F * 2 + 2 * M * K * 2, ms_dn, pk))
-    del w1, w2
-    # ---- config 3
+    return _roof(wbytes + io, ms, pk, shape='RMSNorm + gate|up [6144 x 2048] + SiLU*up, then down [2048 x 3072] + '
+                 'residual, M 2', timing=f'{iters} call pairs back to back in a CUDA graph',
+                 us_eager_calls=round(ms_one * 1e3, 2), rotation=f'{nset} weight sets',
+                 gateup=_roof(2 * F * K * 2 + M * K * 2 + M * F * 2, ms_gu, pk),
+                 down=_roof(K * F * 2 + M * F * 2 + 2 * M * K * 2, ms_dn, pk))
+
+
+def measure_config3(dev, iters=20, kvs=(256, 1024, 4096)):
+    """Config 3: the whole 28-layer backbone decode step (B 2, one CUDA graph of its 142 launches) at each KV length
+    (weights 2.70 GB, above L2 on their own)."""
+    import torch
+    from flashb.engine import BackboneConfig, SyntheticBackboneGraph, backbone_step_bytes
+    pk = peaks()
     bcfg = BackboneConfig()
-    Smax = 4096
+    Smax = max(kvs)
     bb = SyntheticBackboneGraph(bcfg, batch_size=2, max_seq_len=Smax, device=dev, seed=2)
     bb.fill_kv(Smax - 1)
     bb.input_ids_buf.copy_(torch.randint(0, bcfg.vocab, (2, 1, bcfg.codebooks), generator=torch.Generator()
                                          .manual_seed(3)).to(dev))
     sweep = {}
     graph = None
-    for L in (256, 1024, 4096):
+    for L in kvs:
         bb.set_position(L - 1)
         if graph is None:
             for _ in range(3):
@@ -394,13 +439,19 @@ def measure_per_config(dev, iters=200):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 bb.decode_step()
-        ms = _time_calls(lambda i: graph.replay(), 20, dev, warmup=3)
+        ms = _time_calls(lambda i: graph.replay(), iters, dev, warmup=3)
         sweep[f'kv{L}'] = _roof(backbone_step_bytes(bcfg, 2, L), ms, pk)
-    out['config3_backbone_step'] = dict(shape='28 layers, hidden 2048, 16 q / 4 KV heads, FFN 6144, B 2; weights '
-                                        '+ valid KV + fp32 lm_head per step', launches=2 + 5 * bcfg.layers, **sweep)
     del graph, bb
     torch.cuda.empty_cache()
-    return out
+    return dict(shape='28 layers, hidden 2048, 16 q / 4 KV heads, FFN 6144, B 2; weights + valid KV + fp32 lm_head '
+                'per step', launches=2 + 5 * bcfg.layers, **sweep)
+
+
+def measure_per_config(dev):
+    """BASELINE configs 1-3 at their own shapes, each on the kernels behind its reference entry point, inputs
+    resident and larger than L2 between calls.  Returns the bench line's ``per_config`` object."""
+    return dict(config1_attn_decode=measure_config1(dev), config2_gemv_pair=measure_config2(dev),
+                config3_backbone_step=measure_config3(dev))
 
 
 # ------------------------------------------------------------------------------------------------ GPU
@@ -421,6 +472,18 @@ def main():
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
     from flashb import replicas
     from flashb.engine import BackboneConfig, DepthConfig, FrameEngine, backbone_step_bytes
+    if a.case in ('config1', 'config2', 'config3'):
+        # one BASELINE config alone (a profiling entry point): a.steps calls after a.warmup
+        fn = dict(config1=measure_config1, config2=measure_config2, config3=measure_config3)[a.case]
+        r = fn(dev, iters=a.steps)
+        head = r if a.case != 'config3' else r['kv1024']
+        if rank == 0:
+            print(json.dumps(dict(metric='HBM GB/s', value=head['achieved'], unit='GB/s', n_gpus=world,
+                                  steps=a.steps, warmup=a.warmup, ms_per_step=head['us'] / 1e3, higher_is_better=True,
+                                  scaling='weak', vs_baseline=None, dtype='bf16', data='synthetic',
+                                  config=dict(workload=a.case), roofline=dict(bound='hbm', **head), detail=r)),
+                  flush=True)
+        return
     if a.case == 'prefill':
         pf = measure_prefill(dev, world, rank, iters=a.steps, warmup=max(3, a.warmup))
         if rank == 0:
@@ -606,10 +669,9 @@ def main():
     # ---- CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline and case == 'frame':
-        v, n, el, threads = cpu_frames(a.cpu_seconds, prompt=a.prompt)
-        cpu = dict(value=round(v, 4), unit='frames/s', cores=threads, kind='port',
-                   sample=f'{n} frames of one stream ({el:.1f} s after 1 warm-up frame): numpy/C oracle port of '
-                          f'backbone step (KV {a.prompt}+t) + 16-codebook depth frame, {threads} BLAS threads')
+        r = cpu_frames(seconds=a.cpu_seconds, prompt=a.prompt)
+        cpu = dict(value=round(r['value'], 4), unit='frames/s', cores=r['threads'], kind='port',
+                   sample=cpu_sample(r, a.prompt))
 
     # frame latency of ONE stream (its own single-stream slot on the same weights), graph-replayed back to back
     lat = None

@@ -49,7 +49,7 @@ class Layer:
 
 
 def _bf16_2d(t):
-    return t is not None and t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous()
+    return t is not None and t.dtype == torch.bfloat16 and t.is_contiguous()
 
 
 def make_state(B, layers, norm_w, norm_eps, embed_table, vocab, lm_head32, cos_tab, sin_tab, max_seq_len, device):
@@ -66,57 +66,70 @@ def make_state(B, layers, norm_w, norm_eps, embed_table, vocab, lm_head32, cos_t
                 ws=workspace(device, B, nq // 128, nk // 128, max_seq_len))
 
 
+def weights_of(graph):
+    """The official graph's weights as ``Layer`` records plus (norm, embedding table, lm_head): attribute reads and
+    the checks of what the kernels cover, on any device.  None when the graph is outside it (``flash/backbone.py:
+    49-103``: the reference's hook makes the same checks)."""
+    model = graph.model
+    if graph.batch_size not in GEMV_CFG or len(model.layers) == 0:
+        return None
+    Ls = []
+    for layer in model.layers:
+        at, mlp = layer.self_attn, layer.mlp
+        L = Layer()
+        L.ln1_w, L.ln1_eps = layer.input_layernorm.weight, float(layer.input_layernorm.variance_epsilon)
+        L.ln2_w, L.ln2_eps = layer.post_attention_layernorm.weight, float(
+            layer.post_attention_layernorm.variance_epsilon)
+        L.wq, L.wk, L.wv, L.wo = at.q_proj.weight, at.k_proj.weight, at.v_proj.weight, at.o_proj.weight
+        L.qn_w, L.kn_w = at.q_norm.weight, at.k_norm.weight
+        L.qk_eps = float(at.q_norm.variance_epsilon)
+        if float(at.k_norm.variance_epsilon) != L.qk_eps:
+            return None
+        L.scaling = float(at.scaling)
+        L.wg, L.wu, L.wd = mlp.gate_proj.weight, mlp.up_proj.weight, mlp.down_proj.weight
+        for m in (at.q_proj, at.k_proj, at.v_proj, at.o_proj, mlp.gate_proj, mlp.up_proj, mlp.down_proj):
+            if getattr(m, 'bias', None) is not None:
+                return None
+        if not all(_bf16_2d(t) for t in (L.ln1_w, L.ln2_w, L.wq, L.wk, L.wv, L.wo, L.qn_w, L.kn_w, L.wg, L.wu, L.wd)):
+            return None
+        if getattr(mlp, 'act_fn', None).__class__.__name__ not in ('SiLU', 'SiLUActivation'):
+            return None
+        if at.head_dim != 128 or at.num_key_value_groups not in (1, 2, 4, 8) or getattr(at, 'sliding_window', None):
+            return None
+        Ls.append(L)
+    emb = graph.embed_tokens
+    if getattr(emb, 'audio_embeds_projector', None) is not None or not _bf16_2d(emb.embed_audio_tokens.weight):
+        return None
+    lm = graph.lm_head
+    if getattr(lm, 'bias', None) is not None or lm.weight.dtype != torch.float32 or not _bf16_2d(model.norm.weight):
+        return None
+    return Ls, model.norm, emb.embed_audio_tokens.weight, lm.weight
+
+
 def _prep(graph):
-    """Weight handles + buffers for an official BackboneGraph; None -> unsupported, use the original step."""
+    """Weight handles + buffers for an official BackboneGraph on a GPU; None -> unsupported, use the original step."""
     st = getattr(graph, '_bb_state', None)
     if st is not None and st['B'] == graph.batch_size:
         return st
     try:
-        model = graph.model
-        B = graph.batch_size
-        if B not in GEMV_CFG or len(model.layers) == 0:
+        if not torch.device(graph.device).type == 'cuda':
             return None
-        Ls = []
-        for layer in model.layers:
-            at, mlp = layer.self_attn, layer.mlp
-            L = Layer()
-            L.ln1_w, L.ln1_eps = layer.input_layernorm.weight, float(layer.input_layernorm.variance_epsilon)
-            L.ln2_w, L.ln2_eps = layer.post_attention_layernorm.weight, float(
-                layer.post_attention_layernorm.variance_epsilon)
-            L.wq, L.wk, L.wv, L.wo = at.q_proj.weight, at.k_proj.weight, at.v_proj.weight, at.o_proj.weight
-            L.qn_w, L.kn_w = at.q_norm.weight, at.k_norm.weight
-            L.qk_eps = float(at.q_norm.variance_epsilon)
-            if float(at.k_norm.variance_epsilon) != L.qk_eps:
-                return None
-            L.scaling = float(at.scaling)
-            L.wg, L.wu, L.wd = mlp.gate_proj.weight, mlp.up_proj.weight, mlp.down_proj.weight
-            for m in (at.q_proj, at.k_proj, at.v_proj, at.o_proj, mlp.gate_proj, mlp.up_proj, mlp.down_proj):
-                if getattr(m, 'bias', None) is not None:
-                    return None
-            if not all(_bf16_2d(t) for t in (L.ln1_w, L.ln2_w, L.wq, L.wk, L.wv, L.wo, L.qn_w, L.kn_w, L.wg, L.wu,
-                                                L.wd)):
-                return None
-            if getattr(mlp, 'act_fn', None).__class__.__name__ not in ('SiLU', 'SiLUActivation'):
-                return None
-            if at.head_dim != 128 or at.num_key_value_groups not in (1, 2, 4, 8) or getattr(at, 'sliding_window',
-                                                                                              None):
-                return None
-            Ls.append(L)
-        emb = graph.embed_tokens
-        if getattr(emb, 'audio_embeds_projector', None) is not None or not _bf16_2d(emb.embed_audio_tokens.weight):
+        got = weights_of(graph)
+        if got is None:
             return None
-        lm = graph.lm_head
-        if getattr(lm, 'bias', None) is not None or lm.weight.dtype != torch.float32 or not _bf16_2d(model.norm.weight):
+        Ls, norm, table, lm_w = got
+        if not all(t.is_cuda for L in Ls for t in (L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd)):
             return None
+        model, B = graph.model, graph.batch_size
         dev = graph.device
         S = graph.max_seq_len
         with torch.no_grad():
             pos = torch.arange(S + 1, device=dev)[None]
             dummy = torch.zeros(1, S + 1, 128, dtype=torch.bfloat16, device=dev)
             cos, sin = model.rotary_emb(dummy, pos)
-        st = make_state(B, Ls, model.norm.weight, model.norm.variance_epsilon, emb.embed_audio_tokens.weight,
-                        emb.embed_audio_tokens.weight.shape[0] // graph.num_codebooks, lm.weight.contiguous(),
-                        cos[0].contiguous().to(torch.bfloat16), sin[0].contiguous().to(torch.bfloat16), S, dev)
+        st = make_state(B, Ls, norm.weight, norm.variance_epsilon, table, table.shape[0] // graph.num_codebooks,
+                        lm_w.contiguous(), cos[0].contiguous().to(torch.bfloat16),
+                        sin[0].contiguous().to(torch.bfloat16), S, dev)
         kernels.attn()
         kernels.fused()
         graph._bb_state = st

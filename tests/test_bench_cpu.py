@@ -23,12 +23,24 @@ def test_frame_config_keys_and_backbone_mode():
     assert c2['backbone'] == 'lanes' and 'a backbone graph per 8 streams' in c2['workload']
 
 
-def test_reference_and_flashb_arms_share_the_workload():
-    """The reference arm derives its config from the same arguments as the flashb arm (kv_len and lane_sms aside,
-    which describe the run)."""
+def test_reference_arm_describes_its_own_work():
+    """The reference arm's config says what it runs: one stream of the CPU port with the reference server's cache
+    capacity and the host's thread count -- not the GPU arm's multi-stream workload."""
     a = _args()
-    flashb = bench.frame_config(a, 1, 64, 8, True, 18, [513, 546])
-    ref = bench.frame_config(a, 1, a.streams, 8, a.backbone == 'shared' and 2 * a.streams <= 128, None, [513, 515])
-    for k in flashb:
-        if k not in ('kv_len', 'lane_sms'):
-            assert flashb[k] == ref[k], k
+    c = bench.reference_config(a, 7)
+    assert c['streams'] == 1 and c['device'] == 'cpu' and c['threads'] == 7
+    assert c['cache_len'] == bench.CPU_CACHE_LEN == 2048 and c['prompt_len'] == 512
+    assert 'lanes' not in c and 'streams_per_gpu' not in c
+
+
+def test_cpu_threads_ignore_omp_num_threads(monkeypatch):
+    """Both CPU legs size their BLAS pool from the process's CPU affinity, not from OMP_NUM_THREADS (torchrun sets
+    it to 1)."""
+    monkeypatch.setenv('OMP_NUM_THREADS', '1')
+    assert bench.cpu_threads() == len(os.sched_getaffinity(0))
+
+
+def test_cpu_frames_one_frame_small_cache():
+    """The shared CPU leg runs and reports its sample (one frame, after one warm-up frame)."""
+    r = bench.cpu_frames(frames=1, warmup=1, prompt=16, cache_len=20, layers=1)
+    assert r['frames'] == 1 and r['value'] > 0 and r['cache_len'] == 20 and r['threads'] == bench.cpu_threads()
