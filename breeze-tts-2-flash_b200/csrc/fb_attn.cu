@@ -15,8 +15,11 @@
 // (b, kv-head).  Each CTA streams its key range in 64-position chunks (K and V rows are contiguous per (b, kv-head):
 // one 16 KB bulk copy each, double-buffered in shared memory).  In the fused variant the first chunks are requested
 // BEFORE griddepcontrol.wait (old cache slots are not written by the preceding kernel), so the KV stream overlaps the
-// QKV GEMV's tail under PDL.  Scores use half-warp dot products from shared memory, an online softmax per q head of
-// the GQA group, and P.V with one thread per head dimension.  The split partials (m, l, o[128]) stay in each CTA's
+// QKV GEMV's tail under PDL.  Per chunk, 256 threads run three short parallel steps: scores with a quad of threads
+// per key (a 32-dim quarter each, 16-byte units read in a key-rotated order so the quads spread over the banks, two
+// shuffles to combine), an online softmax with one warp per q head of the GQA group, and P.V with each thread
+// owning two head dims over a quarter of the chunk's keys (the quarters added in order at the end).  The next
+// chunk's mask values are loaded during the current chunk.  The split partials (m, l, o[128]) stay in each CTA's
 // shared memory; after a cluster barrier, CTA g of the cluster merges head g by reading its peers' partials through
 // distributed shared memory (in split order, so the result is deterministic) -- no global workspace, no atomics.
 #include <cooperative_groups.h>
@@ -37,7 +40,7 @@ int attn_mma_fused(const bf16* qkv, long qkv_sb, const bf16* qn_w, const bf16* k
 thread_local int t_attn_path = -1;
 
 constexpr int AT_D = 128;
-constexpr int AT_THREADS = 128;
+constexpr int AT_THREADS = 256;
 constexpr int AT_CHUNK = 64;
 constexpr int AT_MAXCLUSTER = 16;   // splits per (b, kv-head) = CTAs per cluster (non-portable size 16)
 
@@ -67,15 +70,20 @@ struct AttnArgs {
   unsigned* err;
 };
 
+// q of the group in shared memory as fp32, each 32-dim quarter padded to 36 floats (spreads the quarter reads of the
+// score step over the banks)
+__device__ __forceinline__ int at_qidx(int g, int d) { return g * 144 + (d >> 5) * 36 + (d & 31); }
+
 template <int G, bool FUSED>
 __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   bf16* sK = reinterpret_cast<bf16*>(smem);                       // [2][CHUNK][D]
   bf16* sV = sK + 2 * AT_CHUNK * AT_D;                            // [2][CHUNK][D]
+  float* red = reinterpret_cast<float*>(sV + 2 * AT_CHUNK * AT_D); // [4 key quarters][G][D] P.V partial sums
   __shared__ __align__(8) uint64_t full[2];
-  __shared__ float q_s[G][AT_D];
-  __shared__ float p_s[G][AT_CHUNK];
-  __shared__ float mrow[AT_CHUNK];
+  __shared__ __align__(16) float q_s[G * 144];
+  __shared__ float s_s[G][AT_CHUNK];                              // scores, then unnormalised probabilities
+  __shared__ float mrow[2][AT_CHUNK];                             // mask values of the chunk (by chunk parity)
   __shared__ float st_m[G], st_l[G], st_scale[G];
   __shared__ __align__(8) bf16 newk[AT_D];
   __shared__ __align__(8) bf16 newv[AT_D];
@@ -115,6 +123,13 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     bulk_g2s(sK + (size_t)s * AT_CHUNK * AT_D, kbase + (size_t)p0 * AT_D, bytes, &full[s]);
     bulk_g2s(sV + (size_t)s * AT_CHUNK * AT_D, vbase + (size_t)p0 * AT_D, bytes, &full[s]);
   };
+  // mask value of key tid of chunk c (threads < AT_CHUNK), -inf past the CTA's range
+  auto mask_of = [&](int c) -> float {
+    const int p = p_begin + c * AT_CHUNK + tid;
+    if (tid >= AT_CHUNK || c >= nchunks || p >= p_end) return -INFINITY;
+    const size_t mi = (size_t)b * a.m_sb + p;
+    return a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi]) : reinterpret_cast<const float*>(a.mask)[mi];
+  };
   if (FUSED && tid == 0) {
     for (int c = 0; c < min(2, nchunks); ++c) issue(c);
   }
@@ -123,22 +138,20 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
   // (embed_rope, step_advance), which have completed before this kernel can start (its predecessor, the q|k|v GEMV,
   // lets it start only after its own griddepcontrol.wait); only q|k|v comes from the predecessor.
   HeadPair wq, wk, cs, sn;
-  float m_first = -INFINITY;
+  float mcur = -INFINITY;
   if (FUSED) {
     wq = head_load(a.qn_w, lane);
     wk = head_load(a.kn_w, lane);
     cs = head_load(a.cos + (size_t)b * a.cs_sb, lane);
     sn = head_load(a.sin + (size_t)b * a.cs_sb, lane);
-    if (tid < AT_CHUNK && nchunks > 0 && tid < min(AT_CHUNK, p_end - p_begin)) {
-      const size_t mi = (size_t)b * a.m_sb + p_begin + tid;
-      m_first = a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi])
-                            : reinterpret_cast<const float*>(a.mask)[mi];
-    }
+    mcur = mask_of(0);
   }
   pdl_wait();
   pdl_trigger();
-  if (!FUSED && tid == 0) {
-    for (int c = 0; c < min(2, nchunks); ++c) issue(c);
+  if (!FUSED) {
+    if (tid == 0)
+      for (int c = 0; c < min(2, nchunks); ++c) issue(c);
+    mcur = mask_of(0);
   }
 
   // ---- queries of this GQA group (and, in the owner CTA, the new key / value)
@@ -147,14 +160,14 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     if (FUSED) {
       const bf16* qr = a.qkv + (size_t)b * a.qkv_sb + (size_t)hq * AT_D;
       const HeadPair qv = head_norm_rope(qr, wq, cs, sn, a.eps, lane);
-      q_s[g][2 * lane] = qv.lo[0];
-      q_s[g][2 * lane + 1] = qv.lo[1];
-      q_s[g][64 + 2 * lane] = qv.hi[0];
-      q_s[g][64 + 2 * lane + 1] = qv.hi[1];
+      q_s[at_qidx(g, 2 * lane)] = qv.lo[0];
+      q_s[at_qidx(g, 2 * lane + 1)] = qv.lo[1];
+      q_s[at_qidx(g, 64 + 2 * lane)] = qv.hi[0];
+      q_s[at_qidx(g, 64 + 2 * lane + 1)] = qv.hi[1];
     } else {
       const bf16* qp = a.q + (size_t)b * a.q_sb + (size_t)hq * a.q_sh;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) q_s[g][lane * 4 + j] = b2f(qp[lane * 4 + j]);
+      for (int j = 0; j < 4; ++j) q_s[at_qidx(g, lane * 4 + j)] = b2f(qp[lane * 4 + j]);
     }
   }
   const bool owner = FUSED && pos >= p_begin && pos < p_end;
@@ -172,93 +185,98 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     st_l[tid] = 0.f;
   }
   __syncthreads();
-  if (owner) {
+  if (owner && tid < AT_D) {
     bf16* kd = a.kc + (size_t)b * a.c_sb + (size_t)h * a.c_sh + (size_t)pos * AT_D;
     bf16* vd = a.vc + (size_t)b * a.c_sb + (size_t)h * a.c_sh + (size_t)pos * AT_D;
     kd[tid] = newk[tid];
     vd[tid] = newv[tid];
   }
 
-  float qf[G][8];
-  const int l16 = lane & 15, hw = lane >> 4;
+  // score step: thread = (key j of the chunk, 32-dim quarter e); P.V step: thread = (dims 2 dp, 2 dp + 1, keys
+  // [16 kq, 16 kq + 16) of the chunk)
+  const int sj = tid >> 2, se = tid & 3;
+  const int dp = tid & 63, kq = tid >> 6;
+  float o[G][2];
 #pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) qf[g][j] = q_s[g][l16 * 8 + j];
-  float o[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) o[g] = 0.f;
+  for (int g = 0; g < G; ++g) o[g][0] = o[g][1] = 0.f;
 
   bool ok = true;
   for (int c = 0; c < nchunks; ++c) {
     const int s = c & 1;
     const int p0 = p_begin + c * AT_CHUNK;
     const int n = min(AT_CHUNK, p_end - p0);
+    if (tid < AT_CHUNK) {
+      mrow[s][tid] = mcur;
+      mcur = mask_of(c + 1);              // the next chunk's mask values, in flight during this chunk
+    }
     ok = __syncthreads_and(mbar_wait(&full[s], (c >> 1) & 1, a.err));
     if (!ok) break;
     bf16* ks = sK + (size_t)s * AT_CHUNK * AT_D;
     bf16* vs = sV + (size_t)s * AT_CHUNK * AT_D;
-    if (owner && pos >= p0 && pos < p0 + n) {
-      ks[(size_t)(pos - p0) * AT_D + tid] = newk[tid];
-      vs[(size_t)(pos - p0) * AT_D + tid] = newv[tid];
-    }
-    if (tid < AT_CHUNK) {
-      float m = -INFINITY;
-      if (FUSED && c == 0) {
-        m = m_first;
-      } else if (tid < n) {
-        const size_t mi = (size_t)b * a.m_sb + p0 + tid;
-        m = a.mask_bf16 ? b2f(reinterpret_cast<const bf16*>(a.mask)[mi]) : reinterpret_cast<const float*>(a.mask)[mi];
+    if (owner && pos >= p0 && pos < p0 + n) {   // the new key / value replace the slot's old contents
+      if (tid < AT_D) {
+        ks[(size_t)(pos - p0) * AT_D + tid] = newk[tid];
+        vs[(size_t)(pos - p0) * AT_D + tid] = newv[tid];
       }
-      mrow[tid] = m;
+      __syncthreads();
     }
-    __syncthreads();
-    // scores: half-warp per key, 8 keys per pass over the 4 warps
-    for (int j0 = 0; j0 < n; j0 += 8) {
-      const int j = j0 + warp * 2 + hw;
-      float kf[8];
-      if (j < n) {
-        cvt8(*reinterpret_cast<const uint4*>(ks + (size_t)j * AT_D + l16 * 8), kf);
-      } else {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) kf[t] = 0.f;
-      }
+    // ---- scores: a quad of threads per key, each a quarter of the dims (16-byte units in a rotated order)
+    {
       float d[G];
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float acc = 0.f;
+      for (int g = 0; g < G; ++g) d[g] = 0.f;
+      if (sj < n) {
+        const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)sj * AT_D + 32 * se);
 #pragma unroll
-        for (int t = 0; t < 8; ++t) acc = fmaf(qf[g][t], kf[t], acc);
-        d[g] = acc;
+        for (int i = 0; i < 4; ++i) {
+          const int ii = (i + sj) & 3;
+          float kf[8];
+          cvt8(kr[ii], kf);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float4* qp = reinterpret_cast<const float4*>(q_s + g * 144 + se * 36 + ii * 8);
+            const float4 qa = qp[0], qb = qp[1];
+            float acc = d[g];
+            acc = fmaf(qa.x, kf[0], acc);
+            acc = fmaf(qa.y, kf[1], acc);
+            acc = fmaf(qa.z, kf[2], acc);
+            acc = fmaf(qa.w, kf[3], acc);
+            acc = fmaf(qb.x, kf[4], acc);
+            acc = fmaf(qb.y, kf[5], acc);
+            acc = fmaf(qb.z, kf[6], acc);
+            acc = fmaf(qb.w, kf[7], acc);
+            d[g] = acc;
+          }
+        }
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g)
+      for (int g = 0; g < G; ++g) {
+        d[g] += __shfl_xor_sync(FULL, d[g], 1);
+        d[g] += __shfl_xor_sync(FULL, d[g], 2);
+      }
+      const float m = mrow[s][sj];
+      const bool valid = sj < n && m > -1e30f;
 #pragma unroll
-        for (int off = 8; off > 0; off >>= 1) d[g] += __shfl_xor_sync(FULL, d[g], off);
-      if (l16 == 0 && j < n) {
-        const float m = mrow[j];
-        const bool valid = m > -1e30f;
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
+      for (int g = 0; g < G; ++g) {
+        if ((g & 3) == se) {
           float sc = rbf(rbf(d[g]) * a.scaling);
           sc = a.mask_bf16 ? rbf(sc + m) : sc + m;
-          p_s[g][j] = valid ? sc : -INFINITY;
+          s_s[g][sj] = valid ? sc : -INFINITY;
         }
       }
     }
     __syncthreads();
-    // online softmax statistics, one warp per head
+    // ---- online softmax statistics, one warp per head
     for (int g = warp; g < G; g += AT_THREADS / 32) {
-      const float s0 = lane < n ? p_s[g][lane] : -INFINITY;
-      const float s1 = lane + 32 < n ? p_s[g][lane + 32] : -INFINITY;
+      const float s0 = s_s[g][lane], s1 = s_s[g][lane + 32];
       const float cm = warp_max(fmaxf(s0, s1));
       const float mold = st_m[g];
       const float mnew = fmaxf(mold, cm);
       const bool any = mnew > -INFINITY;
       const float e0 = (any && s0 > -INFINITY) ? expf(s0 - mnew) : 0.f;
       const float e1 = (any && s1 > -INFINITY) ? expf(s1 - mnew) : 0.f;
-      if (lane < n) p_s[g][lane] = e0;
-      if (lane + 32 < n) p_s[g][lane + 32] = e1;
+      s_s[g][lane] = e0;
+      s_s[g][lane + 32] = e1;
       const float es = warp_sum(e0 + e1);
       if (lane == 0) {
         const float scale = (mold > -INFINITY) ? expf(mold - mnew) : 0.f;
@@ -268,57 +286,82 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
       }
     }
     __syncthreads();
-    // P . V, thread = head dimension
+    // ---- P . V: this thread's two dims over its quarter of the keys
 #pragma unroll
-    for (int g = 0; g < G; ++g) o[g] *= st_scale[g];
-    for (int j = 0; j < n; ++j) {
-      const float v = b2f(vs[(size_t)j * AT_D + tid]);
+    for (int g = 0; g < G; ++g) {
+      o[g][0] *= st_scale[g];
+      o[g][1] *= st_scale[g];
+    }
+    {
+      const uint32_t* vr = reinterpret_cast<const uint32_t*>(vs) + dp;
+      const int jb = kq * 16, je = min(jb + 16, n);
+#pragma unroll 4
+      for (int jj = jb; jj < je; ++jj) {
+        const uint32_t v2 = vr[(size_t)jj * (AT_D / 2)];
+        const float vx = lo_f(v2), vy = hi_f(v2);
 #pragma unroll
-      for (int g = 0; g < G; ++g) o[g] = fmaf(p_s[g][j], v, o[g]);
+        for (int g = 0; g < G; ++g) {
+          const float pr = s_s[g][jj];
+          o[g][0] = fmaf(pr, vx, o[g][0]);
+          o[g][1] = fmaf(pr, vy, o[g][1]);
+        }
+      }
     }
     __syncthreads();
     if (tid == 0 && c + 2 < nchunks) issue(c + 2);
   }
   if (!ok) {  // timed out: publish an empty partial so the cluster still completes its barriers
 #pragma unroll
-    for (int g = 0; g < G; ++g) o[g] = 0.f;
+    for (int g = 0; g < G; ++g) o[g][0] = o[g][1] = 0.f;
     if (tid < G) {
       st_m[tid] = -INFINITY;
       st_l[tid] = 0.f;
     }
   }
+  // the four key quarters' partial sums, added in quarter order
 #pragma unroll
-  for (int g = 0; g < G; ++g) part_o[g][tid] = o[g];
+  for (int g = 0; g < G; ++g)
+    *reinterpret_cast<float2*>(red + ((size_t)kq * G + g) * AT_D + 2 * dp) = make_float2(o[g][0], o[g][1]);
+  __syncthreads();
+  for (int i = tid; i < G * AT_D; i += AT_THREADS) {
+    const int g = i / AT_D, dd = i - g * AT_D;
+    float v = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v += red[((size_t)q * G + g) * AT_D + dd];
+    part_o[g][dd] = v;
+  }
 
   // ---- merge across the cluster through distributed shared memory
   cluster.sync();
-  for (int g = split; g < G; g += nsplit) {
-    float mv[AT_MAXCLUSTER], lv[AT_MAXCLUSTER], ov[AT_MAXCLUSTER];
+  if (tid < AT_D) {
+    for (int g = split; g < G; g += nsplit) {
+      float mv[AT_MAXCLUSTER], lv[AT_MAXCLUSTER], ov[AT_MAXCLUSTER];
 #pragma unroll
-    for (int sp = 0; sp < AT_MAXCLUSTER; ++sp) {  // all peer loads issued together
-      if (sp < nsplit) {
-        mv[sp] = *cluster.map_shared_rank(&st_m[g], sp);
-        lv[sp] = *cluster.map_shared_rank(&st_l[g], sp);
-        ov[sp] = *cluster.map_shared_rank(&part_o[g][tid], sp);
-      }
-    }
-    float M = -INFINITY;
-#pragma unroll
-    for (int sp = 0; sp < AT_MAXCLUSTER; ++sp)
-      if (sp < nsplit) M = fmaxf(M, mv[sp]);
-    float L = 0.f, O = 0.f;
-    if (M > -INFINITY) {
-#pragma unroll
-      for (int sp = 0; sp < AT_MAXCLUSTER; ++sp) {
-        if (sp < nsplit && mv[sp] > -INFINITY) {
-          const float f = expf(mv[sp] - M);
-          L = fmaf(lv[sp], f, L);
-          O = fmaf(ov[sp], f, O);
+      for (int sp = 0; sp < AT_MAXCLUSTER; ++sp) {  // all peer loads issued together
+        if (sp < nsplit) {
+          mv[sp] = *cluster.map_shared_rank(&st_m[g], sp);
+          lv[sp] = *cluster.map_shared_rank(&st_l[g], sp);
+          ov[sp] = *cluster.map_shared_rank(&part_o[g][tid], sp);
         }
       }
+      float M = -INFINITY;
+#pragma unroll
+      for (int sp = 0; sp < AT_MAXCLUSTER; ++sp)
+        if (sp < nsplit) M = fmaxf(M, mv[sp]);
+      float L = 0.f, O = 0.f;
+      if (M > -INFINITY) {
+#pragma unroll
+        for (int sp = 0; sp < AT_MAXCLUSTER; ++sp) {
+          if (sp < nsplit && mv[sp] > -INFINITY) {
+            const float f = expf(mv[sp] - M);
+            L = fmaf(lv[sp], f, L);
+            O = fmaf(ov[sp], f, O);
+          }
+        }
+      }
+      const float r = L > 0.f ? O / L : 0.f;
+      a.out[((size_t)b * NH + h * G + g) * AT_D + tid] = __float2bfloat16_rn(r);
     }
-    const float r = L > 0.f ? O / L : 0.f;
-    a.out[((size_t)b * NH + h * G + g) * AT_D + tid] = __float2bfloat16_rn(r);
   }
   cluster.sync();  // peers' shared memory must stay alive until every merge has read it
 }
@@ -328,7 +371,9 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
 namespace {
 using namespace fb;
 
-constexpr size_t AT_SMEM = 4 * (size_t)AT_CHUNK * AT_D * 2;  // K and V, two stages
+// K and V, two stages, then the P.V partial sums of the four key quarters
+template <int G>
+constexpr size_t at_smem() { return 4 * (size_t)AT_CHUNK * AT_D * 2 + 4 * (size_t)G * AT_D * 4; }
 
 // Splits per (b, kv-head): about two CTAs per SM in all, at least 16 keys each, at most g_max_split (the cluster
 // size; FLASHB_ATTN_SPLITS sets it, default AT_MAXCLUSTER).
@@ -364,7 +409,7 @@ int launch_attn_t(AttnArgs& a, int B, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)AT_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)at_smem<G>());
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) {
       fbh::set_msg("attn: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -373,7 +418,7 @@ int launch_attn_t(AttnArgs& a, int B, cudaStream_t st) {
     attr_done[dev] = 1;
   }
   void* args[] = {(void*)&a};
-  return fbh::launch_pdl((const void*)kern, dim3(a.nsplit, a.NKV, B), dim3(AT_THREADS), AT_SMEM, st, args, true,
+  return fbh::launch_pdl((const void*)kern, dim3(a.nsplit, a.NKV, B), dim3(AT_THREADS), at_smem<G>(), st, args, true,
                          a.nsplit);
 }
 
