@@ -294,6 +294,113 @@ extern "C" int flashb_embed_rope(const int64_t* ids, int B, int C, int vocab, co
   return fbh::launch_pdl((const void*)embed_rope_kernel, dim3(B), dim3(256), 0, (cudaStream_t)stream, args, true);
 }
 
+// ------------------------------------------------------------------------------------------------ many-row lm_head
+// logits[B, V] = float(hidden[B, H]) @ W32[V, H]^T for up to LMR_MAXB rows in one pass over the fp32 lm_head, and the
+// CFG combine of every block of `block` rows laid out [cond_0 .. cond_{h-1}, uncond_0 .. uncond_{h-1}] (h = block / 2):
+// cfg[blk * h + k] = u + gs * (c - u), three separately rounded fp32 ops.  hidden is the final-norm output (bf16).
+// Tiled fp32 FMA on the CUDA cores (the lm_head is fp32, like the reference's): CTA = LMR_VT vocab rows x all B rows,
+// K in chunks of LMR_KC columns double-buffered in shared memory by cp.async; thread = 2 vocab rows x 4 batch rows,
+// 4 columns per shared-memory read.  Every output is one thread's fp32 sum in column order (deterministic).
+constexpr int LMR_MAXB = 128;
+constexpr int LMR_VT = 16;
+constexpr int LMR_KC = 128;
+constexpr int LMR_THREADS = 256;
+constexpr int LMR_WP = LMR_KC + 4;         // fp32 row pitch of a W chunk (2-way bank spread of the 8 row pairs)
+constexpr int LMR_HP = LMR_KC + 8;         // bf16 row pitch of a hidden chunk
+
+__global__ void __launch_bounds__(LMR_THREADS) lm_head_rows_kernel(const bf16* __restrict__ hid, int B, int H,
+                                                                   const float* __restrict__ W, int V,
+                                                                   const float* __restrict__ gs, int block,
+                                                                   float* __restrict__ logits,
+                                                                   float* __restrict__ cfg) {
+  extern __shared__ __align__(16) unsigned char lmr_smem[];
+  auto ws = reinterpret_cast<float(*)[LMR_VT][LMR_WP]>(lmr_smem);                          // [2][VT][WP]
+  auto hs = reinterpret_cast<bf16(*)[LMR_MAXB][LMR_HP]>(lmr_smem + 2 * sizeof(float) * LMR_VT * LMR_WP);
+  auto outs = reinterpret_cast<float(*)[LMR_VT + 1]>(ws);    // after the K loop: [B][VT + 1] over the W chunks
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x;
+  const int v0 = blockIdx.x * LMR_VT;
+  const int vb = tid & 7, bb = tid >> 3;        // vocab rows v0 + 2 vb (+1), batch rows 4 bb .. 4 bb + 3
+  const int nk = (H + LMR_KC - 1) / LMR_KC;
+  auto stage = [&](int kc, int buf) {
+    const int k0 = kc * LMR_KC;
+    // W: LMR_VT rows x LMR_KC fp32 = 512 16-byte units; hidden: B rows x LMR_KC bf16 = B x 16 units
+    for (int i = tid; i < LMR_VT * (LMR_KC / 4); i += LMR_THREADS) {
+      const int r = i / (LMR_KC / 4), u = i - r * (LMR_KC / 4);
+      const int v = min(v0 + r, V - 1), k = k0 + 4 * u;
+      if (k < H) cp_async16(&ws[buf][r][4 * u], W + (size_t)v * H + k);
+    }
+    for (int i = tid; i < B * (LMR_KC / 8); i += LMR_THREADS) {
+      const int r = i / (LMR_KC / 8), u = i - r * (LMR_KC / 8);
+      const int k = k0 + 8 * u;
+      if (k < H) cp_async16(&hs[buf][r][8 * u], hid + (size_t)r * H + k);
+    }
+    cp_async_commit();
+  };
+  float acc[2][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  stage(0, 0);
+  for (int kc = 0; kc < nk; ++kc) {
+    if (kc + 1 < nk) {
+      stage(kc + 1, (kc + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int buf = kc & 1, kw = min(LMR_KC, H - kc * LMR_KC);
+    for (int k = 0; k < kw; k += 4) {
+      const float4 w0 = *reinterpret_cast<const float4*>(&ws[buf][2 * vb][k]);
+      const float4 w1 = *reinterpret_cast<const float4*>(&ws[buf][2 * vb + 1][k]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int b = 4 * bb + j;
+        const uint2 hv = *reinterpret_cast<const uint2*>(&hs[buf][b < B ? b : 0][k]);
+        const float h0 = lo_f(hv.x), h1 = hi_f(hv.x), h2 = lo_f(hv.y), h3 = hi_f(hv.y);
+        float s0 = acc[0][j], s1 = acc[1][j];
+        s0 = fmaf(w0.x, h0, s0); s0 = fmaf(w0.y, h1, s0); s0 = fmaf(w0.z, h2, s0); s0 = fmaf(w0.w, h3, s0);
+        s1 = fmaf(w1.x, h0, s1); s1 = fmaf(w1.y, h1, s1); s1 = fmaf(w1.z, h2, s1); s1 = fmaf(w1.w, h3, s1);
+        acc[0][j] = s0;
+        acc[1][j] = s1;
+      }
+    }
+    __syncthreads();
+  }
+  static_assert(LMR_MAXB * (LMR_VT + 1) <= 2 * LMR_VT * LMR_WP, "outs must fit over the W chunks");
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = 4 * bb + j, v = v0 + 2 * vb + i;
+      if (b < B) {
+        outs[b][2 * vb + i] = acc[i][j];
+        if (v < V) logits[(size_t)b * V + v] = acc[i][j];
+      }
+    }
+  __syncthreads();
+  // CFG of every block: one thread per (pair, vocab row of the tile)
+  const float g = gs ? gs[0] : 1.0f;
+  const int h = block >= 2 ? block / 2 : 1;
+  const int npair = block >= 2 ? (B / block) * h : B;
+  for (int i = tid; i < npair * LMR_VT; i += LMR_THREADS) {
+    const int pr = i / LMR_VT, vv = i - pr * LMR_VT, v = v0 + vv;
+    if (v >= V) continue;
+    float r;
+    if (block >= 2) {
+      const int blk = pr / h, k = pr - blk * h;
+      const float c = outs[blk * block + k][vv], u = outs[blk * block + h + k][vv];
+      r = __fadd_rn(u, __fmul_rn(g, __fsub_rn(c, u)));
+    } else {
+      r = outs[pr][vv];
+    }
+    cfg[(size_t)pr * V + v] = r;
+  }
+}
+
 extern "C" int flashb_lm_head_cfg(const void* x, int B, int H, const void* norm_w, float eps, const float* W32,
                                   int V, const float* gs, void* hidden_out, float* logits, float* cfg_out,
                                   void* stream) {
@@ -319,5 +426,39 @@ extern "C" int flashb_lm_head_cfg(const void* x, int B, int H, const void* norm_
   void* args[] = {(void*)&xp, (void*)&B, (void*)&H, (void*)&np, (void*)&eps, (void*)&W32, (void*)&V,
                   (void*)&gs, (void*)&ho, (void*)&logits, (void*)&cfg_out};
   return fbh::launch_pdl((const void*)lm_head_cfg_kernel, dim3(fbh::grid_sms()), dim3(LM_THREADS), smem,
+                         (cudaStream_t)stream, args, true);
+}
+
+// Final norm + lm_head + CFG for B rows in blocks of `block` rows (each laid out [cond.., uncond..]): the norm as the
+// standalone RMSNorm (hidden_out), then one pass of lm_head_rows_kernel over the fp32 lm_head for every row.
+extern "C" int flashb_lm_head_cfg_blocks(const void* x, int B, int H, const void* norm_w, float eps, const float* W32,
+                                         int V, const float* gs, int block, void* hidden_out, float* logits,
+                                         float* cfg_out, void* stream) {
+  FB_CHECK_ARG(x && norm_w && W32 && hidden_out && logits && cfg_out, "lm_head_cfg_blocks: null pointer argument");
+  FB_CHECK_ARG(B >= 1 && B <= LMR_MAXB && H % 8 == 0 && V >= 1, "lm_head_cfg_blocks: bad shape B=%d H=%d V=%d", B, H,
+               V);
+  FB_CHECK_ARG(block >= 1 && B % block == 0 && (block == 1 || block % 2 == 0),
+               "lm_head_cfg_blocks: block %d must divide B = %d and be 1 or even", block, B);
+  FB_CHECK_ARG(block == 1 || gs, "lm_head_cfg_blocks: guidance scale pointer required for CFG blocks");
+  FB_CHECK_ARG(((uintptr_t)W32 & 15) == 0 && ((uintptr_t)hidden_out & 15) == 0 && H % 4 == 0,
+               "lm_head_cfg_blocks: 16-byte aligned lm_head and hidden rows required");
+  int rc = flashb_rmsnorm(x, H, B, H, norm_w, eps, hidden_out, H, stream);
+  if (rc) return rc;
+  const bf16* hp = (const bf16*)hidden_out;
+  void* args[] = {(void*)&hp, (void*)&B, (void*)&H, (void*)&W32, (void*)&V, (void*)&gs, (void*)&block,
+                  (void*)&logits, (void*)&cfg_out};
+  const size_t smem = 2 * sizeof(float) * LMR_VT * LMR_WP + 2 * sizeof(bf16) * LMR_MAXB * LMR_HP;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(lm_head_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      fbh::set_msg("lm_head_cfg_blocks: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return FB_ERR_CUDA;
+    }
+    attr_done[dev] = 1;
+  }
+  return fbh::launch_pdl((const void*)lm_head_rows_kernel, dim3((V + LMR_VT - 1) / LMR_VT), dim3(LMR_THREADS), smem,
                          (cudaStream_t)stream, args, true);
 }

@@ -242,15 +242,6 @@ __device__ __forceinline__ void reduce_warps_nt(const float (&c)[NT][4], float* 
   }
 }
 
-// cp.async 16-byte global -> shared copy (bypasses L1), group commit / wait.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 __device__ __forceinline__ void cp_async_wait_dyn(int n) {  // n in [0, 7]
   switch (n) {
     case 0: cp_async_wait<0>(); break;

@@ -51,6 +51,7 @@ _PROTOS = {
     'flashb_rmsnorm': (I, [P, L, I, I, P, F, P, L, P]),
     'flashb_embed_rope': (I, [P, I, I, I, P, I, P, P, P, I, I, P, P, P, P]),
     'flashb_lm_head_cfg': (I, [P, I, I, P, F, P, I, P, P, P, P, P]),
+    'flashb_lm_head_cfg_blocks': (I, [P, I, I, P, F, P, I, P, I, P, P, P, P]),
     'flashb_step_advance': (I, [P, P, I, P, I, L, I, P]),
     'flashb_cb0_greedy': (I, [P, L, I, I, I, P, P]),
     'flashb_frame_ids': (I, [P, P, I, I, I, P, P]),

@@ -181,10 +181,13 @@ def fused_decode_step(graph, advance=False):
     # each laid out [cond..., uncond...]); the official graph is one block
     blk = getattr(graph, 'cfg_block', B)
     hb = graph.hidden_buf.view(B, -1)
-    for j in range(0, B, blk):
-        fx.lm_head_cfg(x[j:j + blk], st['norm_w'], st['norm_eps'], st['lm_head32'], graph.guidance_scale,
-                       hb[j:j + blk], graph.logits_buf[j:j + blk],
-                       graph.cfg_logits_buf[j // 2:(j + blk) // 2] if blk >= 2 else graph.cfg_logits_buf[j:j + 1])
+    if blk == B and B <= 16:
+        fx.lm_head_cfg(x, st['norm_w'], st['norm_eps'], st['lm_head32'], graph.guidance_scale, hb, graph.logits_buf,
+                       graph.cfg_logits_buf)
+    else:
+        # every CFG block in one pass over the fp32 lm_head
+        fx.lm_head_cfg_blocks(x, st['norm_w'], st['norm_eps'], st['lm_head32'], graph.guidance_scale, blk, hb,
+                              graph.logits_buf, graph.cfg_logits_buf)
 
 
 def install(api=None):

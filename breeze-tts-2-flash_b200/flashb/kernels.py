@@ -187,6 +187,19 @@ class FusedOps:
         check(_native.lib().flashb_lm_head_cfg(_p(x), B, H, _p(norm_w), float(eps), _p(W32), V, _p(gs),
                                                _p(hidden_out), _p(logits), _p(cfg_out), _stream(x)))
 
+    def lm_head_cfg_blocks(self, x, norm_w, eps, W32, gs, block, hidden_out, logits, cfg_out):
+        """lm_head_cfg for B rows in CFG blocks of ``block`` rows (each [cond..., uncond...]), one pass over the
+        fp32 lm_head for every row; cfg_out rows: block b's pairs at [b * block / 2, (b + 1) * block / 2)."""
+        _bf16(x, 'x')
+        B, H = x.shape[0], x.shape[-1]
+        _req(x.is_contiguous() and hidden_out.is_contiguous(), 'x / hidden_out contiguous')
+        _req(W32.dtype == torch.float32 and W32.is_contiguous() and W32.shape[1] == H, 'W32')
+        V = W32.shape[0]
+        _req(logits.dtype == torch.float32 and logits.is_contiguous() and logits.numel() >= B * V, 'logits')
+        check(_native.lib().flashb_lm_head_cfg_blocks(_p(x), B, H, _p(norm_w), float(eps), _p(W32), V, _p(gs),
+                                                      int(block), _p(hidden_out), _p(logits), _p(cfg_out),
+                                                      _stream(x)))
+
 
 def load(name, verbose=False):
     """Load the library (built ahead of time by ``flashb.build``) and return the ops object for ``name``."""

@@ -130,6 +130,15 @@ int flashb_embed_rope(const int64_t* ids, int B, int C, int vocab, const void* t
  * scalar. */
 int flashb_lm_head_cfg(const void* x, int B, int H, const void* norm_w, float eps, const float* W32, int V,
                        const float* gs, void* hidden_out, float* logits, float* cfg_out, void* stream);
+/* flashb_lm_head_cfg for B <= 128 rows in CFG blocks of `block` rows (1, or an even divisor of B), each block laid
+ * out [cond_0 .. cond_{h-1}, uncond_0 .. uncond_{h-1}] (h = block / 2): the final RMSNorm of every row
+ * (hidden_out [B, H] bf16, contiguous), logits [B, V] fp32 in one pass over the fp32 lm_head, and
+ * cfg_out[blk * h + k] = u + gs (c - u) for every block (block 1: cfg_out = logits).  No reference counterpart as a
+ * kernel: the reference runs one CFG pair per graph (flash/backbone.py:127-138); this serves many streams' pairs
+ * decoded as one batch. */
+int flashb_lm_head_cfg_blocks(const void* x, int B, int H, const void* norm_w, float eps, const float* W32, int V,
+                              const float* gs, int block, void* hidden_out, float* logits, float* cfg_out,
+                              void* stream);
 
 /* Device-side per-frame position update of the streaming loop (the host-side cache_position / position_ids /
  * _set_attention_mask updates of flash/main_loop.py:123-140 and UP/models/cudagraph/backbone_graph.py:239-252,

@@ -316,6 +316,34 @@ def test_lm_head_cfg(ops, B):
     assert np.array_equal(cfg.cpu().numpy(), cfg_ref), 'CFG combine is elementwise: bit-exact given the logits'
 
 
+@pytest.mark.parametrize('B,block,V', [(128, 16, 2049), (32, 8, 2049), (16, 16, 100), (6, 1, 37), (128, 128, 2049)])
+def test_lm_head_cfg_blocks(ops, B, block, V):
+    """Final norm + fp32 lm_head + CFG for many rows in CFG blocks, one pass over the lm_head: logits within fp32
+    summation-order error of the oracle on the kernel's own normed hidden, every block's CFG rows bit-exact given the
+    logits."""
+    fx, _ = ops
+    H = 2048
+    x = randn((B, H), 93, 2.0)
+    nw = randn((H,), 94, 0.1, 1.0)
+    W = randn((V, H), 95, 0.02).float()
+    gs = torch.tensor([4.0], device='cuda')
+    hid = torch.empty(B, H, dtype=torch.bfloat16, device='cuda')
+    logits = torch.empty(B, V, device='cuda')
+    npair = B // 2 if block >= 2 else B
+    cfg = torch.empty(npair, V, device='cuda')
+    fx.lm_head_cfg_blocks(x, nw, 1e-6, W, gs, block, hid, logits, cfg)
+    torch.cuda.synchronize()
+    assert_close(np32(hid), dec.rmsnorm(np32(x), np32(nw), 1e-6), what='final norm')
+    lg = logits.cpu().numpy()
+    assert_close(lg, dec.lm_head_fp32(np32(hid), W.cpu().numpy()), tol=1e-5, what='lm_head')
+    if block >= 2:
+        h = block // 2
+        ref = np.concatenate([dec.cfg_combine(lg[b0:b0 + block], h, 4.0) for b0 in range(0, B, block)])
+    else:
+        ref = lg
+    assert np.array_equal(cfg.cpu().numpy(), ref), 'CFG combine is elementwise: bit-exact given the logits'
+
+
 # ------------------------------------------------------------------------------------------------ tcgen05 GEMV
 def _budget(n):
     from flashb._native import lib
