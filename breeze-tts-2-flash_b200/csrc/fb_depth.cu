@@ -74,6 +74,7 @@ struct alignas(64) DDArgs {
   float* logits;
   GridBar* bar;
   int nstages, xs_bytes, att_off, keep_off, att_bc, att_split, d_xchunk;
+  unsigned long long wait_ns;             // grid-barrier wait limit
   unsigned* err;
   unsigned long long* trace;
 };
@@ -655,7 +656,7 @@ __device__ __forceinline__ DDSm dd_smem(const DDArgs& a) {
   m.red = reinterpret_cast<float*>(ringb + (size_t)a.nstages * ST_BYTES);
   m.sums = m.red + (NT ? ST_CWARPS * 128 * NT : DD_TC_SUMS);
   uint64_t* full = reinterpret_cast<uint64_t*>(m.sums + 128 * NT);
-  m.rg = Ring{ringb, full, full + PK_MAX_STAGES, a.nstages};
+  m.rg = Ring{ringb, full, full + PK_MAX_STAGES, a.nstages, &g_dd_int[28]};
   return m;
 }
 
@@ -703,7 +704,7 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
     const TmaRows w1 = KIND == 1 ? src(bi * UB, 1) : TmaRows{nullptr, 0};
     for (int kc = 0; kc < nkc; ++kc, ++t) {
       const int s = t % rg.nst;
-      if (t >= rg.nst && !mbar_wait_warp(&rg.empty[s], ((t / rg.nst) - 1) & 1, err)) return false;
+      if (t >= rg.nst && !ring_wait_empty(rg, s, ((t / rg.nst) - 1) & 1, err)) return false;
       if (lane == 0) {
         unsigned char* st = rg.base + (size_t)s * ST_BYTES;
         mbar_arrive_expect_tx(&rg.full[s], (unsigned)ST_BYTES);
@@ -998,7 +999,7 @@ __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int su
     return c;
   }
   DD_STAMP(s, 1);
-  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) c.ok = 0;
   DD_STAMP(s, 2);
   return c;
 }
@@ -1044,7 +1045,7 @@ __device__ __noinline__ DDCur dd_phase_s1(const DDArgs& a, DDCur c, int s, int p
     return c;
   }
   DD_STAMP(s, tb + 0);
-  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) c.ok = 0;
   DD_STAMP(s, tb + 1);
   return c;
 }
@@ -1064,7 +1065,7 @@ __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int p
     const int p0 = (int)((long long)npairs * blockIdx.x / gridDim.x);
     const int p1 = (int)((long long)npairs * (blockIdx.x + 1) / gridDim.x);
     dd_attention_pairs<G>(a, l, pos, p0, p1, m.xs + a.att_off);
-    if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) {
+    if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) {
       c.ok = 0;
       return c;
     }
@@ -1084,7 +1085,7 @@ __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int p
     return c;
   }
   DD_STAMP(s, tb + 3);
-  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) c.ok = 0;
   DD_STAMP(s, tb + 4);
   return c;
 }
@@ -1113,7 +1114,7 @@ __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l
     return c;
   }
   DD_STAMP(s, tb + 5);
-  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) c.ok = 0;
   DD_STAMP(s, tb + 6);
   return c;
 }
@@ -1146,7 +1147,7 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
     return c;
   }
   DD_STAMP(s, tb + 7);
-  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) c.ok = 0;
   DD_STAMP(s, tb + 8);
   return c;
 }
@@ -1174,7 +1175,7 @@ __device__ __noinline__ DDCur dd_phase_s5(const DDArgs& a, DDCur c, int s) {
     return c;
   }
   DD_STAMP(s, te + 0);
-  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) c.ok = 0;
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) c.ok = 0;
   DD_STAMP(s, te + 1);
   return c;
 }
@@ -1210,7 +1211,7 @@ __device__ __noinline__ DDCur dd_phase_sample(const DDArgs& a, DDCur c, int s) {
     }
   }
   if (!redundant && s + 1 < a.NCB) {
-    if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31])) {
+    if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) {
       c.ok = 0;
       return c;
     }
@@ -1235,6 +1236,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
       fence_mbar_init();
     }
     if (tid < 32) reinterpret_cast<uint32_t*>(m.zero16)[tid] = 0u;
+    if (tid == 0) g_dd_int[28] = 0;                         // the consumers' "stopped early" flag
     if (NT == 0 && warp == 0) tc_alloc(&g_dd_tmem, 64);   // 4 accumulator chains x 16 columns
   }
   if (NT == 0) tc_before();
@@ -1261,6 +1263,11 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
     }
     if (c.ok) c = dd_phase_s5<NT>(a, c, s);
     if (c.ok) c = dd_phase_sample(a, c, s);
+  }
+  if (!c.ok && tid == 0) {
+    // stopped early: the producer must not wait for ring slots nobody will release
+    *reinterpret_cast<volatile int*>(&g_dd_int[28]) = 1;
+    __threadfence_block();
   }
   if (NT == 0) {
     // every MMA of this CTA has completed (each task waits for its last commit); free the accumulators
@@ -1366,6 +1373,11 @@ extern "C" int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg) {
 
 extern "C" int64_t flashb_dd_layer_bytes(void) { return (int64_t)sizeof(fb_dd_layer); }
 
+extern "C" int64_t flashb_dd_barrier_offset(const fb_dd_config* cfg) {
+  if (!cfg) return -1;
+  return (int64_t)dd_layout(cfg).bar;
+}
+
 extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, void* scratch, const int64_t* first_cb,
                                const void* bh, int64_t* tokbuf, int64_t* outtok, const float* temp,
                                const int64_t* topk, const float* topp, const int64_t* dosample, const float* gs,
@@ -1391,6 +1403,7 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.act = (bf16*)(sc + Lo.act); a.kc = (bf16*)(sc + Lo.kc); a.vc = (bf16*)(sc + Lo.vc);
   a.logits = (float*)(sc + Lo.logits); a.bar = (GridBar*)(sc + Lo.bar);
   a.err = fbh::device_err_ptr();
+  a.wait_ns = c->wait_ns > 0 ? (unsigned long long)c->wait_ns : WAIT_LIMIT_NS;
   a.trace = (unsigned long long*)c->trace;
   const size_t M = (size_t)c->batch;
   const int grid = c->grid > 0 ? c->grid : fbh::grid_sms();

@@ -40,23 +40,35 @@ __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
 
 // Barrier over the consumer warps of every CTA: arrival is one fire-and-forget release-add on a monotonic counter,
 // completion of barrier number `epoch` is count >= epoch * gridDim.x (observed with acquire loads).  The critical
-// path is one add plus one poll round trip through L2.  Waits are bounded (WAIT_LIMIT_NS); on expiry, or when another
-// CTA has aborted, every CTA returns false and the kernel winds down (the host then re-zeroes the state).
-__device__ __noinline__ bool grid_sync_n(GridBar* gb, unsigned epoch, unsigned* err, int* s_flag) {
+// path is one add plus one poll round trip through L2.  Waits are bounded (`limit` ns); on expiry the waiter records
+// FB_ERR_TIMEOUT and sets the abort flag; a waiter that finds the flag set (another CTA's expiry, or the host's
+// request) records FB_ERR_ABORTED.  Either way every CTA returns false and the kernel winds down (the host then
+// re-zeroes the state).
+__device__ __noinline__ bool grid_sync_n(GridBar* gb, unsigned epoch, unsigned* err, int* s_flag, uint64_t limit) {
   named_sync(2, PK_CONSUMERS);
   if (threadIdx.x == 0) {
     int ok = 1;
     const unsigned target = epoch * gridDim.x;
     __threadfence();
     red_release_add(&gb->count, 1u);
-    if (ld_acquire_u32(&gb->count) < target) {
+    // the abort word is read at every barrier (both loads in flight together), so a request that arrives before
+    // the waits are long still stops the frame at its next barrier
+    const unsigned cnt = ld_acquire_u32(&gb->count), ab = ld_acquire_u32(&gb->abort);
+    if (ab) {
+      set_error(err, FB_ERR_ABORTED);
+      ok = 0;
+    } else if (cnt < target) {
       const uint64_t t0 = globaltimer();
       int spins = 0;
       while (ld_acquire_u32(&gb->count) < target) {
         if (++spins == 256) {
           spins = 0;
-          if (ld_acquire_u32(&gb->abort)) { ok = 0; break; }
-          if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+          if (ld_acquire_u32(&gb->abort)) {
+            set_error(err, FB_ERR_ABORTED);
+            ok = 0;
+            break;
+          }
+          if (globaltimer() - t0 > limit) {
             set_error(err, FB_ERR_TIMEOUT);
             atomicExch(&gb->abort, 1u);
             ok = 0;
@@ -72,9 +84,10 @@ __device__ __noinline__ bool grid_sync_n(GridBar* gb, unsigned epoch, unsigned* 
 }
 // Not inlined: a persistent kernel calls it at ~20 sites, and its code must stay small enough to remain in the
 // instruction cache across a whole step (cold code re-fetched from L2 costs microseconds per phase).
-__device__ __forceinline__ bool grid_sync(GridBar* gb, unsigned& epoch, unsigned* err, int* s_flag) {
+__device__ __forceinline__ bool grid_sync(GridBar* gb, unsigned& epoch, unsigned* err, int* s_flag,
+                                          uint64_t limit = WAIT_LIMIT_NS) {
   ++epoch;
-  return grid_sync_n(gb, epoch, err, s_flag);
+  return grid_sync_n(gb, epoch, err, s_flag, limit);
 }
 
 // Called once by consumer thread 0 of every CTA after its last barrier: the last CTA out resets the barrier.
@@ -93,13 +106,34 @@ __device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// The ring of one persistent CTA.
+// The ring of one persistent CTA.  `quit` (shared memory, may be null): set by the consumers when they stop early
+// (a barrier gave up); the producer then abandons its wait for a free slot without recording an error.
 struct Ring {
   unsigned char* base;
   uint64_t* full;
   uint64_t* empty;
   int nst;
+  volatile int* quit;
 };
+
+// The producer's wait for a free ring slot (warp-uniform): bounded like every wait, and abandoned once the
+// consumers have stopped.
+__device__ __forceinline__ bool ring_wait_empty(const Ring& rg, int s, unsigned parity, unsigned* err) {
+  bool ok = mbar_try_wait(&rg.empty[s], parity);
+  if (!ok) {
+    const uint64_t t0 = globaltimer();
+    while (true) {
+#pragma unroll 1
+      for (int i = 0; i < 64 && !ok; ++i) ok = mbar_try_wait(&rg.empty[s], parity);
+      if (ok || (rg.quit && *rg.quit)) break;
+      if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+        set_error(err, FB_ERR_TIMEOUT);
+        break;
+      }
+    }
+  }
+  return __all_sync(FULL, ok);
+}
 
 // A streamed GEMV task: `units` output units over K columns; NMAT = 2 pairs each unit with a second weight row
 // (gate/up, or the two rotary halves of a q/k head dimension).  Row pointers come from a functor row(n, mat).
@@ -124,7 +158,7 @@ __device__ __noinline__ int produce_group(Ring rg, int t, const bf16* row, int n
   const int nkc = (K + ST_KC - 1) / ST_KC;
   for (int kc = 0; kc < nkc; ++kc, ++t) {
     const int s = t % rg.nst;
-    if (t >= rg.nst && !mbar_wait_warp(&rg.empty[s], ((t / rg.nst) - 1) & 1, err)) return -1;
+    if (t >= rg.nst && !ring_wait_empty(rg, s, ((t / rg.nst) - 1) & 1, err)) return -1;
     const int k0 = kc * ST_KC;
     const int kw = min(ST_KC, K - k0);
     unsigned char* st = rg.base + (size_t)s * ST_BYTES;
@@ -163,7 +197,7 @@ __device__ __noinline__ int produce_group_tma(Ring rg, int t, TmaRows lo, TmaRow
   const int nkc = (K + ST_KC - 1) / ST_KC;
   for (int kc = 0; kc < nkc; ++kc, ++t) {
     const int s = t % rg.nst;
-    if (t >= rg.nst && !mbar_wait_warp(&rg.empty[s], ((t / rg.nst) - 1) & 1, err)) return -1;
+    if (t >= rg.nst && !ring_wait_empty(rg, s, ((t / rg.nst) - 1) & 1, err)) return -1;
     if (lane == 0) tma_stage(rg.base + (size_t)s * ST_BYTES, lo, hi, kc, &rg.full[s]);
     __syncwarp();
   }

@@ -15,7 +15,7 @@ _LIB = None
 
 FB_OK, FB_ERR_ARG, FB_ERR_CUDA, FB_ERR_UNSUPPORTED, FB_ERR_STATE, FB_ERR_TIMEOUT, FB_ERR_DEVICE = range(7)
 _NAMES = {1: 'invalid argument', 2: 'CUDA error', 3: 'unsupported', 4: 'bad state', 5: 'device wait timed out',
-          6: 'device error'}
+          6: 'device error', 7: 'aborted'}
 
 
 class FlashbError(RuntimeError):
@@ -59,6 +59,7 @@ _PROTOS = {
                                 L, P]),
     'flashb_dd_scratch_bytes': (L, [P]),
     'flashb_dd_layer_bytes': (L, []),
+    'flashb_dd_barrier_offset': (L, [P]),
     'flashb_dd_frame': (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
     'flashb_dd_frame_noalloc': (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
 }
@@ -74,7 +75,7 @@ class FbDDConfig(ctypes.Structure):
     _fields_ = [('layers', I), ('batch', I), ('hidden', I), ('embed_dim', I), ('heads', I), ('kv_heads', I),
                 ('head_dim', I), ('ffn', I), ('vocab', I), ('codebook_size', I), ('n_decode', I), ('eps', F),
                 ('scaling', F), ('embed', P), ('proj', P), ('normf', P), ('head_t', P), ('cos_tab', P),
-                ('sin_tab', P), ('trace', P), ('grid', I), ('layers_host', P)]
+                ('sin_tab', P), ('trace', P), ('grid', I), ('layers_host', P), ('wait_ns', L)]
 
 
 def lib_path():
@@ -127,3 +128,11 @@ def last_error():
 def device_error(clear=True):
     """The device error word (0 = no bounded wait expired).  Synchronises the device."""
     return int(lib().flashb_device_error(1 if clear else 0))
+
+
+def check_device(clear=True):
+    """Raise FlashbError when a kernel reported a device-side failure (an expired bounded wait, an abort); the
+    error word is cleared (unless clear=False).  Synchronises the device."""
+    rc = device_error(clear)
+    if rc:
+        raise FlashbError(rc, last_error())

@@ -26,7 +26,9 @@ enum {
   FB_ERR_UNSUPPORTED = 3, /* valid but not built: head_dim != 128, group size not in {1,2,4,8}, M > 8 ... */
   FB_ERR_STATE = 4,       /* object not initialised / used on another device */
   FB_ERR_TIMEOUT = 5,     /* a device-side wait ran out of time (reported through flashb_device_error) */
-  FB_ERR_DEVICE = 6       /* the device reported an error */
+  FB_ERR_DEVICE = 6,      /* the device reported an error */
+  FB_ERR_ABORTED = 7      /* a persistent kernel stopped at a barrier because its abort flag was set: by another
+                           * CTA whose bounded wait expired, or by the host (reported through flashb_device_error) */
 };
 
 /* ---------------------------------------------------------------------------------------------- library */
@@ -203,9 +205,17 @@ typedef struct {
   int grid;            /* CTAs of the launch, one per SM: 0 = every SM; fewer leave SMs to work on other streams */
   const void* layers_host; /* fb_dd_layer[layers] in host memory, the same pointers as layers_dev: the weight matrices'
                             * TMA tensor maps are built from it on the host (cached per matrix) */
+  int64_t wait_ns;         /* limit of each grid-barrier wait in ns; 0 = 2 s.  On expiry the CTA records
+                            * FB_ERR_TIMEOUT, sets the barrier's abort flag and the frame winds down */
 } fb_dd_config;
 int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg);
 int64_t flashb_dd_layer_bytes(void);
+/* Byte offset, within the scratch buffer, of the frame's grid-barrier state: four uint32 words (arrival count, exit
+ * count, abort flag, padding), zero between frames.  A non-zero abort word (set by the host, e.g. with
+ * cudaMemsetAsync on the frame's stream or another stream) makes a frame stop at its next barrier wait, record
+ * FB_ERR_ABORTED in the device error word and return; the scratch must then be zeroed again before the next frame.
+ * No reference counterpart (the reference's barriers cannot be cancelled, flash/csrc/depth_common.cuh:52-65). */
+int64_t flashb_dd_barrier_offset(const fb_dd_config* cfg);
 int flashb_dd_frame(const fb_dd_config* cfg, const void* layers_dev, void* scratch, const int64_t* first_cb,
                     const void* bh, int64_t* tokbuf, int64_t* outtok, const float* temp, const int64_t* topk,
                     const float* topp, const int64_t* dosample, const float* gs, const float* q, float* dbg,

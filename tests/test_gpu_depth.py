@@ -177,3 +177,63 @@ def test_depth_determinism_and_graph_replay():
     torch.cuda.synchronize()
     _, logits, _ = _run(m)
     _check_sampler(m, logits, m.output_tokens.cpu().numpy())
+
+
+# ------------------------------------------------------------------------------------------------ failure detection
+def _barrier_words(m):
+    """The frame's grid-barrier state in the scratch buffer: [count, exitc, abort, pad] as int32."""
+    import ctypes
+    from flashb import _native
+    off = int(_native.lib().flashb_dd_barrier_offset(ctypes.byref(m.desc.cfg)))
+    assert off >= 0 and off % 256 == 0
+    return m.desc.scratch[off:off + 16].view(torch.int32)
+
+
+def _fresh_frame_ok(m, ref):
+    """After a failed frame the host zeroes the scratch; the next frame must match an undisturbed one."""
+    from flashb import _native
+    m.desc.scratch.zero_()
+    out, logits, _ = _run(m)
+    _native.check_device()
+    np.testing.assert_array_equal(out, ref)
+
+
+def test_depth_host_abort_winds_down():
+    """The host sets the barrier's abort word before a frame: the frame stops at its first barrier wait, records
+    FB_ERR_ABORTED, every CTA (producer warps included) returns promptly, and Python raises FlashbError.  Nothing
+    faults or hangs: the injected state is a flag the kernel polls while it waits."""
+    import time
+    from flashb import _native
+    m = _model(B=2, seed=31)
+    m.desc.cfg.grid = 8
+    ref, _, _ = _run(m)
+    _native.check_device()
+    _barrier_words(m)[2].fill_(1)
+    t0 = time.perf_counter()
+    m.frame()
+    with pytest.raises(_native.FlashbError) as ei:
+        _native.check_device()
+    assert ei.value.rc == 7 and time.perf_counter() - t0 < 1.0
+    _fresh_frame_ok(m, ref)
+
+
+def test_depth_barrier_wait_expires():
+    """A grid-barrier wait runs out: with a 10 ms wait limit (fb_dd_config.wait_ns) and the arrival counter set on
+    the host so that the first barrier can never complete (it wraps past the target after half the grid has
+    arrived), the late CTAs time out, record FB_ERR_TIMEOUT and raise the abort flag, the others stop at their next
+    wait, and Python raises FlashbError with the timeout code.  Nothing faults or hangs: every wait is bounded."""
+    import time
+    from flashb import _native
+    m = _model(B=2, seed=32)
+    m.desc.cfg.grid = 8
+    ref, _, _ = _run(m)
+    _native.check_device()
+    m.desc.cfg.wait_ns = 10_000_000
+    _barrier_words(m)[0].fill_(-(8 // 2))
+    t0 = time.perf_counter()
+    m.frame()
+    with pytest.raises(_native.FlashbError) as ei:
+        _native.check_device()
+    assert ei.value.rc == 5 and time.perf_counter() - t0 < 1.0
+    m.desc.cfg.wait_ns = 0
+    _fresh_frame_ok(m, ref)
