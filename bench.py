@@ -8,14 +8,15 @@ of 64); the depth frames run 8 streams per launch (--group) on 8 lanes side by s
 CUDA stream with its kernels sized for 1/8 of the SMs.  A STEP is one frame of every stream on this rank:
 
     frame = next backbone ids from the previous frame -> 28-layer backbone decode step (B = 2 CFG rows, KV length
-            512 + t, hidden 2048, 16 q / 4 kv heads, FFN 6144, fp32 lm_head + CFG) -> codebook-0 token (greedy
-            backbone sampler) -> depth frame (4 layers, hidden 1024, 16 codebooks of 2048, CFG scale 4, top-k 50,
-            T 0.9, sampled on the device)
+            512 + t, hidden 2048, 16 q / 4 kv heads, FFN 6144, fp32 lm_head + CFG) -> codebook-0 token (the
+            reference runtime's backbone sampler on the device: repetition penalty 1.1, T 0.9, top-k 50) -> depth
+            frame (4 layers, hidden 1024, 16 codebooks of 2048, CFG scale 4, top-k 50, T 0.9, sampled on the device)
 
+Every frame's random draws are fresh: the Exp(1) draws of both multinomials are made on the device each step.
 Outputs one JSON line (rank 0): ``value`` = frames/s of the whole job with every input resident in HBM (max over
-ranks of the device time), ``e2e`` = the same through the engine API with the per-frame Exp(1) draws copied from
-pinned host memory before each frame and the frame's tokens read back to the host after it, every step (as the
-reference's loop reads its tokens), ``roofline`` for the dominant kernel (the depth frame kernel) and
+ranks of the device time), ``e2e`` = the same through the engine API with the depth frame's Exp(1) draws copied
+from pinned host memory before each frame and the frame's tokens and codebook-0 validity flags read back to the host
+after it, every step (as the reference's loop reads its token and flag), ``roofline`` for the dominant kernel (the depth frame kernel) and
 ``roofline_backbone`` for the backbone step's attention + GEMV kernels, ``cpu_baseline`` = the CPU oracle port of
 the same frame on this host's cores.
 
@@ -208,7 +209,8 @@ def reference_config(a, threads):
 def frame_config(a, world, my_streams, lanes, shared, lane_sms, kv_len, case='frame'):
     """The `config` of the flashb arm's bench line."""
     wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + greedy '
-                   f'codebook-0 + 16-codebook depth frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9); '
+                   f'codebook 0 sampled on the device (repetition penalty 1.1, T 0.9, top-k 50) + 16-codebook depth '
+                   f'frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9; fresh Exp(1) draws every frame); '
                    f'{a.group} stream(s) per depth launch share the weight reads; {lanes} lane(s) of the GPU side '
                    f'by side; ' + (f'one backbone graph for all {my_streams} streams ({2 * my_streams} rows, GEMVs '
                                    f'as row groups of 64)' if shared else
@@ -220,7 +222,10 @@ def frame_config(a, world, my_streams, lanes, shared, lane_sms, kv_len, case='fr
                 kv_len=kv_len, parallelism=f'replica x{world}', lanes=lanes, backbone='shared' if shared else 'lanes',
                 lane_sms=lane_sms,
                 l2='inputs larger than L2: 2.70 GB backbone weights per step, 130 MB depth weights per codebook '
-                   'step; no flush', cb0='greedy (backbone sampler do_sample=False)',
+                   'step; no flush',
+                cb0='sampled on the device: the reference runtime\'s backbone sampler (repetition penalty 1.1 over '
+                    'the stream\'s earlier codebook-0 tokens, reserved ids suppressed, T 0.9, top-k 50, top-p 1.0, '
+                    'multinomial on fresh Exp(1) draws, validity flag)',
                 prefill='not timed (random prompt KV)')
 
 
@@ -620,7 +625,7 @@ def main():
         G = a.group
         qh = torch.empty(R, dcfg.n_decode, G, dcfg.vocab).exponential_(1, generator=torch.Generator().manual_seed(5))
         qh = qh.pin_memory()
-        toks_h = torch.zeros(2, S, 2 * G + 2 * G * dcfg.n_decode, dtype=torch.long).pin_memory()
+        toks_h = torch.zeros(2, S, 2 * G + 2 * G * dcfg.n_decode + G, dtype=torch.long).pin_memory()
         h2d = S * qh[0].numel() * 4
         d2h = S * toks_h[0, 0].numel() * 8
         got = [None] * S            # per slot: the event after its previous frame's token copies
@@ -640,13 +645,15 @@ def main():
             def d2h_tokens(kind, i, s):
                 st = eng.streams[i]
                 toks_h[t & 1, i, :2 * G].copy_(st.first_cb, non_blocking=True)
-                toks_h[t & 1, i, 2 * G:].copy_(st.outtok.view(-1), non_blocking=True)
+                toks_h[t & 1, i, 2 * G:-G].copy_(st.outtok.view(-1), non_blocking=True)
+                toks_h[t & 1, i, -G:].copy_(eng.cb0_ok[st.c0:st.c0 + G], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(s)
                 got[i] = ev
 
             eng.step(h2d_q, d2h_tokens)
 
+        eng.draw_q = False          # the depth frame's draws come from the host in this run
         for t in range(a.warmup):
             e2e_step(t)
         torch.cuda.synchronize(dev)
@@ -663,6 +670,7 @@ def main():
                 e.synchronize()     # the last step's tokens are on the host
         barrier()
         e_ms = maxred(w0.elapsed_time(w1))
+        eng.draw_q = True
         e2e = dict(value=round(frames / (e_ms / 1e3), 3), unit='frames/s', h2d_bytes_per_step=h2d,
                    d2h_bytes_per_step=d2h, ms_per_step=round(e_ms / a.steps, 3))
 

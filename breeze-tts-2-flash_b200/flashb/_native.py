@@ -13,7 +13,7 @@ from . import build as _build
 _LOCK = threading.Lock()
 _LIB = None
 
-FB_OK, FB_ERR_ARG, FB_ERR_CUDA, FB_ERR_UNSUPPORTED, FB_ERR_STATE, FB_ERR_TIMEOUT, FB_ERR_DEVICE = range(7)
+FB_OK, FB_ERR_ARG, FB_ERR_CUDA, FB_ERR_UNSUPPORTED, FB_ERR_STATE, FB_ERR_TIMEOUT, FB_ERR_DEVICE, FB_ERR_ABORTED = range(8)
 _NAMES = {1: 'invalid argument', 2: 'CUDA error', 3: 'unsupported', 4: 'bad state', 5: 'device wait timed out',
           6: 'device error', 7: 'aborted'}
 
@@ -54,6 +54,7 @@ _PROTOS = {
     'flashb_lm_head_cfg_blocks': (I, [P, I, I, P, F, P, I, P, I, P, P, P, P]),
     'flashb_step_advance': (I, [P, P, I, P, I, L, I, P]),
     'flashb_cb0_greedy': (I, [P, L, I, I, I, P, P]),
+    'flashb_cb0_sample': (I, [P, L, I, I, P, L, F, P, I, P, P, P, P, P, L, P, I, P, I, P]),
     'flashb_frame_ids': (I, [P, P, I, I, I, P, P]),
     'flashb_prefill_attn': (I, [P, L, L, L, P, L, L, L, P, L, L, L, P, I, L, L, I, I, I, I, I, I, F, I, I, I, P, L, L,
                                 L, P]),

@@ -256,7 +256,7 @@ class _Slot:
     """``g`` streams decoded together: one backbone graph and one depth launch over 2 g rows laid out
     [cond_0 .. cond_{g-1}, uncond_0 .. uncond_{g-1}] (the CFG pair of stream k is rows k and k + g), which is the row
     order every kernel on the path already uses for B = 2 g."""
-    __slots__ = ('g', 'bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph', 'desc', 'lane', 'r0')
+    __slots__ = ('g', 'bb', 'bh', 'first_cb', 'outtok', 'tokbuf', 'q', 'graph', 'desc', 'lane', 'r0', 'c0')
 
 
 class sm_budget:
@@ -287,8 +287,12 @@ class FrameEngine:
 
         frame_ids    next backbone input = [cb0, depth tokens] of the previous frame            (1 launch)
         backbone     step on those ids, position advanced on the device                         (2 + 1 + 5 x layers)
-        cb0_greedy   codebook-0 token = argmax of the CFG logits (greedy backbone sampler)      (1 launch)
-        depth frame  every depth codebook, CFG top-k sampled on the device                      (1 launch)
+        cb0          codebook-0 token from the CFG logits: the backbone sampler (cb0='sample': the reference
+                     runtime's repetition penalty 1.1 over the stream's earlier codebook-0 tokens, reserved ids
+                     suppressed, T 0.9, top-k 50, top-p 1.0, multinomial on fresh Exp(1) draws, validity flag)
+                     or its greedy branch (cb0='greedy')                                          (1 launch)
+        depth frame  every depth codebook, CFG top-k sampled on the device (with draw_q, its Exp(1) draws made
+                     fresh on the device before the launch, as the reference's _full_loop does) (1 launch)
 
     The first three are captured into one CUDA graph per slot (``capture()``); the depth frame is a single launch.
     Each stream starts after a ``prompt_len``-token prompt whose KV cache is random (the prefill stand-in).
@@ -305,8 +309,11 @@ class FrameEngine:
     first read), and its attention covers every row in one launch.  The depth launches stay per slot, on the
     lanes.  ``step()`` then replays the one backbone graph and forks the lanes for the depth frames."""
 
+    # the reference runtime's backbone sampling parameters (UP/breeze_infer/runtime.py, api.py REPETITION_PENALTY)
+    CB0_PARAMS = dict(temperature=0.9, top_k=50, top_p=1.0, do_sample=1, repetition_penalty=1.1)
+
     def __init__(self, bcfg: BackboneConfig, dcfg: DepthConfig, n_streams, prompt_len, max_frames, device='cuda',
-                 seed=0, depth_only=False, group=1, single_slot=False, lanes=1, shared_backbone=False):
+                 seed=0, depth_only=False, group=1, single_slot=False, lanes=1, shared_backbone=False, cb0='sample'):
         """``depth_only``: no backbone (a random hidden state per stream feeds the depth frame) -- for timing or
         profiling the depth frame alone on a small device footprint."""
         if bcfg.codebooks - 1 > dcfg.n_decode or dcfg.embed_dim != bcfg.hidden:
@@ -344,6 +351,25 @@ class FrameEngine:
         self.bb = None
         self.bb_graph = None
         n_slots = n_streams // group
+        if cb0 not in ('sample', 'greedy'):
+            raise ValueError("cb0 must be 'sample' or 'greedy'")
+        self.cb0 = cb0
+        self.draw_q = True          # depth Exp(1) draws made on the device before each depth launch
+        # the engine's own generator for every Exp(1) draw it makes (reproducible whatever else draws)
+        self.rng = torch.Generator(device=dev)
+        self.rng.manual_seed(seed + 29)
+        V = bcfg.vocab
+        # per stream (rows in slot order; the single-stream slot last): token history, Exp(1) draws, validity flag
+        ns = n_streams + (1 if single_slot else 0)
+        p = self.CB0_PARAMS
+        self.cb0_present = torch.zeros(ns, V, dtype=torch.uint8, device=dev)
+        self.cb0_q = torch.ones(ns, V, dtype=torch.float32, device=dev)
+        self.cb0_ok = torch.ones(ns, dtype=torch.int64, device=dev)
+        self.cb0_temp = torch.full((ns,), p['temperature'], dtype=torch.float32, device=dev)
+        self.cb0_topk = torch.full((ns,), p['top_k'], dtype=torch.int64, device=dev)
+        self.cb0_topp = torch.full((ns,), p['top_p'], dtype=torch.float32, device=dev)
+        self.cb0_ds = torch.full((ns,), p['do_sample'], dtype=torch.int64, device=dev)
+        self.cb0_suppress = torch.arange(self.n_valid, V, dtype=torch.int64, device=dev)
         if self.shared:
             R = 2 * group * n_slots
             if R > 128:
@@ -363,12 +389,14 @@ class FrameEngine:
         for i, st in enumerate(self.streams):
             st.lane = i % lanes
             st.desc = self.lane_desc[st.lane]
+            st.c0 = i * group                  # its streams' rows of the codebook-0 sampler state
         self.single = None
         if single_slot:
             from .depth import DepthModelDesc
             d = self.depth
             self.single = self._slot(1, 999 + seed)
             self.single.lane = None
+            self.single.c0 = n_streams
             self.single.desc = d.desc if group == 1 else DepthModelDesc(
                 d.layers, d.embed, d.proj, d.normf, d.head_t, d.cos_tab, d.sin_tab, dcfg.eps, 128 ** -0.5,
                 dcfg.codebook_size, 2, dev)
@@ -412,17 +440,39 @@ class FrameEngine:
     def _get(self, i):
         return self.single if i == 'single' else self.streams[i]
 
+    def _cb0(self, cfg_logits, c0, rows, g, first_cb, stream):
+        """Codebook 0 of `rows` streams (sampler state rows [c0, c0 + rows)) from their CFG logits rows, into the
+        CFG-pair ids first_cb (blocks of 2 g rows)."""
+        if self.cb0 == 'greedy':
+            for b in range(rows // g):
+                check(lib().flashb_cb0_greedy(cfg_logits[b * g:].data_ptr(), cfg_logits.stride(0), g, self.n_valid,
+                                              2 * g, first_cb[2 * g * b:].data_ptr(), stream))
+            return
+        V = self.bcfg.vocab
+        q = self.cb0_q[c0:c0 + rows]           # this frame's Exp(1) draws (draw_cb0, before the graph replays)
+        r = slice(c0, c0 + rows)
+        check(lib().flashb_cb0_sample(
+            cfg_logits.data_ptr(), cfg_logits.stride(0), rows, V, self.cb0_present[r].data_ptr(), V,
+            float(self.CB0_PARAMS['repetition_penalty']), self.cb0_suppress.data_ptr(), self.cb0_suppress.numel(),
+            self.cb0_temp[r].data_ptr(), self.cb0_topk[r].data_ptr(), self.cb0_topp[r].data_ptr(),
+            self.cb0_ds[r].data_ptr(), q.data_ptr(), V, first_cb.data_ptr(), g, self.cb0_ok[r].data_ptr(), 1,
+            stream))
+
+    def draw_cb0(self, c0, rows):
+        """Fresh Exp(1) draws of the codebook-0 multinomial of sampler rows [c0, c0 + rows), on the current stream
+        (eager, outside the captured graphs, from the engine's generator)."""
+        if self.cb0 == 'sample':
+            self.cb0_q[c0:c0 + rows].exponential_(1.0, generator=self.rng)
+
     def shared_backbone_part(self):
-        """The shared backbone graph's body: frame ids of every row, one backbone step, codebook 0 per slot."""
+        """The shared backbone graph's body: frame ids of every row, one backbone step, codebook 0 of every
+        stream."""
         bb, g = self.bb, self.group
         stream = torch.cuda.current_stream(self.device).cuda_stream
         check(lib().flashb_frame_ids(self.first_cb.data_ptr(), self.outtok.data_ptr(), self.dcfg.n_decode,
                                      bb.batch_size, self.bcfg.codebooks, bb.input_ids_buf.data_ptr(), stream))
         bb.decode_step(advance=True)
-        cl = bb.cfg_logits_buf
-        for st in self.streams:
-            check(lib().flashb_cb0_greedy(cl[st.r0 // 2:].data_ptr(), cl.stride(0), g, self.n_valid, 2 * g,
-                                          st.first_cb.data_ptr(), stream))
+        self._cb0(bb.cfg_logits_buf, 0, len(self.streams) * g, g, self.first_cb, stream)
 
     # one frame, split into its backbone part (graph-capturable) and the depth launch
     def backbone_part(self, i):
@@ -435,12 +485,14 @@ class FrameEngine:
         check(lib().flashb_frame_ids(st.first_cb.data_ptr(), st.outtok.data_ptr(), self.dcfg.n_decode, 2 * g, C,
                                      st.bb.input_ids_buf.data_ptr(), stream))
         st.bb.decode_step(advance=True)
-        check(lib().flashb_cb0_greedy(st.bb.cfg_logits_buf.data_ptr(), st.bb.cfg_logits_buf.stride(0), g,
-                                      self.n_valid, 2 * g, st.first_cb.data_ptr(), stream))
+        self._cb0(st.bb.cfg_logits_buf, st.c0, g, g, st.first_cb, stream)
 
     def depth_part(self, i):
         st, d = self._get(i), self.depth
         g = st.g
+        if self.draw_q:
+            # the frame's Exp(1) draws (the reference: one exponential_ per codebook)
+            st.q.exponential_(1.0, generator=self.rng)
         st.desc.frame(st.first_cb, st.bh, st.tokbuf, st.outtok, d.temperature[:g], d.top_k[:g], d.top_p[:g],
                       d.do_sample[:g], d.guidance_scale[:g], st.q)
 
@@ -507,6 +559,7 @@ class FrameEngine:
             # the backbone of every slot (one graph on the whole GPU), then the depth frames on the lanes
             if before_part is not None:
                 before_part('bb', -1, cur)
+            self.draw_cb0(0, len(self.streams) * self.group)
             if self.bb_graph is not None:
                 self.bb_graph.replay()
             else:
@@ -559,8 +612,10 @@ class FrameEngine:
         if st.bb is None:
             pass
         elif st.graph is not None:
+            self.draw_cb0(st.c0, st.g)
             st.graph.replay()
         else:
+            self.draw_cb0(st.c0, st.g)
             self.backbone_part(i)
         if before_part is not None:
             before_part('dd', i, stream)
@@ -569,13 +624,17 @@ class FrameEngine:
             after_part('dd', i, stream)
 
     def launches_per_frame(self):
-        """Kernel launches per slot frame (the same for any group size); with a shared backbone, its launches shared
-        out over the slots (the graph's 2 + 5 x layers + 2 launches once, an LM head and a codebook-0 pick per
-        slot)."""
+        """flashb kernel launches per slot frame (the Exp(1) draws are torch's own kernels and not counted).  A
+        backbone graph: frame ids, position advance, embedding, 5 per layer, the LM head (one launch for one CFG
+        block, else a final norm and one pass for every block) and codebook 0 (one sampler launch, or a greedy pick
+        per slot); with a shared backbone its launches are shared out over the slots.  Plus one depth launch."""
+        L = self.bcfg.layers
         if self.shared:
             n = len(self.streams)
-            return (launches_per_backbone_step(self.bcfg) - 1 + 2) / n + 2 + 1
-        return launches_per_backbone_step(self.bcfg) + 1 + 3
+            cb0 = 1 if self.cb0 == 'sample' else n
+            lm = 1 if n == 1 and 2 * self.group <= 16 else 2
+            return (3 + 5 * L + lm + cb0) / n + 1
+        return 3 + 5 * L + 1 + 1 + 1
 
     def frame_bytes(self):
         """Algorithmic HBM bytes of one slot frame at the current KV length: backbone step + 16 depth steps."""

@@ -155,6 +155,23 @@ int flashb_step_advance(int64_t* cache_pos, int64_t* position_ids, int B, void* 
 int flashb_cb0_greedy(const float* cfg_logits, int64_t ld, int half, int n_valid, int B, int64_t* first_cb,
                       void* stream);
 
+/* The backbone sampler (codebook 0): replaces the reference's host-sync-free sample_logits (flash/sampling.py:56-97,
+ * bitwise the official models/cudagraph/sampling.py) with one CTA per row of logits [rows, ld] fp32 (V <= 4096):
+ * repetition penalty on the ids marked in present [rows, ldp] (uint8, or NULL; x > 0 ? x / p : x * p), the
+ * `suppress` ids -> -inf, then per row: dosample == 0 -> argmax (first index, NaN first); else key = x / temp,
+ * top-k (topk > 0: keys below the k-th largest -> -inf, ties kept), top-p (topp < 1), softmax, token =
+ * argmax(probs / q) with q [rows, ldq] fp32 Exp(1) draws (torch.multinomial(probs, 1) == argmax(probs / Exp(1))).
+ * ok[row] (or NULL) = the official multinomial's validity predicate (every prob finite and >= 0, sum != 0); an invalid
+ * row samples from all-ones weights, argmax(1 / q), as the reference's sanitised multinomial does.  Per-row
+ * parameters temp/topp fp32 and topk/dosample int64 [rows].  pair_half == 0: tokens [rows] int64; pair_half = h > 0:
+ * the rows are CFG pairs of blocks laid out [cond_0 .. cond_{h-1}, uncond_0 .. uncond_{h-1}] (the backbone's input
+ * ids), and row r's token goes to tokens[(r / h) 2h + r % h] and tokens[(r / h) 2h + h + r % h].  mark_present != 0
+ * then marks each token in `present` (the token history of the next frame).  Graph-capturable; no host sync. */
+int flashb_cb0_sample(const float* logits, int64_t ld, int rows, int V, unsigned char* present, int64_t ldp,
+                      float repetition_penalty, const int64_t* suppress, int n_suppress, const float* temp,
+                      const int64_t* topk, const float* topp, const int64_t* dosample, const float* q, int64_t ldq,
+                      int64_t* tokens, int pair_half, int64_t* ok, int mark_present, void* stream);
+
 /* Frame assembly of the streaming loop (flash/main_loop.py:268 and :310-312): the backbone input of the next step is
  * ids[b] = [first_cb[b], depth_tok[b, 0 .. C-2]] (ids [B, C] int64, depth_tok [B, n_decode] int64, C - 1 <= n_decode),
  * built on the device instead of by torch.cat / repeat. */

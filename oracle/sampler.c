@@ -173,3 +173,143 @@ int fb_sample_row(const float* lc, const float* lu, int V, int codebook_size, fl
 void fb_exp_n(const float* x, float* y, int n) {
   for (int i = 0; i < n; ++i) y[i] = fb_exp(x[i]);
 }
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * The backbone (codebook-0) sampler: bit-exact restatement of the host-sync-free sample_logits of the reference
+ * (flash/sampling.py:56-97, itself bitwise equal to the official models/cudagraph/sampling.py sample_logits) for one
+ * row of CFG logits, in the official op order:
+ *   repetition penalty on the ids marked present: x > 0 ? x / p : x * p           (flash/sampling.py:44-47, 81-82)
+ *   suppressed ids -> -inf                                                         (:83-84)
+ *   do_sample == 0: token = argmax(x), first index among equal maxima, a NaN counts as the maximum (torch.argmax)
+ *   key = x / temperature                                                          (:89)
+ *   top-k (top_k > 0): threshold = the k-th largest key (k = min(top_k, V), duplicates counted, torch.topk), keys
+ *     below it -> -inf: every key equal to the threshold stays                      (:90-93)
+ *   top-p (top_p < 1): over the keys in rank order, cumulative softmax, shift-right removal, rank 0 kept (:94-100)
+ *   probs = softmax(keys); ok = the multinomial validity predicate: every prob finite, none negative, sum != 0 (so
+ *     a NaN key, a +inf key or nothing finite left all give ok = 0)
+ *   token = argmax(probs / q), q ~ Exp(1) (torch.multinomial(probs, 1) == argmax(probs / Exp(1)), the identity the
+ *     reference's depth kernel relies on); with !ok the multinomial weights are all 1.0 (flash/sampling.py:50-53),
+ *     so token = argmax(1 / q).  Ties of the score go to the lower index.
+ * Rank order is (key descending, index ascending); ranks past the kept prefix have probability 0.  The exponential
+ * and the sums are those of fb_sample_row (32 lanes own contiguous rank ranges of C = ceil(n / 32), in-lane sums in
+ * rank order from 0.0f, Kogge-Stone scan), over the n = V ranks. */
+static int bb_rank_cmp(const void* a, const void* b) { return rank_cmp(a, b); }
+
+int fb_bb_sample_row(const float* logits, int V, const unsigned char* present, float penalty,
+                     const long long* suppress, int n_suppress, float temp, long long topk, float topp,
+                     long long dosample, const float* q, int* ok_out) {
+  float* x = (float*)malloc(sizeof(float) * (size_t)V);
+  for (int i = 0; i < V; ++i) {
+    float v = logits[i];
+    if (present && present[i] && penalty != 1.0f) v = v > 0.0f ? v / penalty : v * penalty;
+    x[i] = v;
+  }
+  for (int j = 0; j < n_suppress; ++j)
+    if (suppress[j] >= 0 && suppress[j] < V) x[suppress[j]] = -INFINITY;
+  if (!dosample) {
+    int g = 0;
+    for (int i = 0; i < V; ++i) {
+      if (isnan(x[g])) break;
+      if (isnan(x[i]) || x[i] > x[g]) g = i;
+    }
+    free(x);
+    if (ok_out) *ok_out = 1;
+    return g;
+  }
+  kv_t* kv = (kv_t*)malloc(sizeof(kv_t) * (size_t)V);
+  int any_nan = 0;
+  for (int i = 0; i < V; ++i) {
+    float k = x[i] / temp;
+    if (isnan(k)) { /* torch ranks a NaN first, keeps it through top-k, and the softmax turns every prob to NaN */
+      any_nan = 1;
+      k = -INFINITY;
+    }
+    kv[i].key = k;
+    kv[i].idx = i;
+  }
+  free(x);
+  qsort(kv, (size_t)V, sizeof(kv_t), bb_rank_cmp);
+  /* top-k: ranks whose key is below the k-th key leave (a prefix stays: keys equal to the threshold included) */
+  int nk = V;
+  if (topk > 0) {
+    const int k = topk < V ? (int)topk : V;
+    const float thr = kv[k - 1].key;
+    nk = k;
+    while (nk < V && !(kv[nk].key < thr)) ++nk;
+  }
+  const int C = (V + 31) / 32;
+  float* e = (float*)malloc(sizeof(float) * (size_t)V);
+  float* pr = (float*)malloc(sizeof(float) * (size_t)V);
+  unsigned char* keep = (unsigned char*)malloc((size_t)V);
+  for (int r = 0; r < V; ++r) e[r] = r < nk ? fb_exp(kv[r].key - kv[0].key) : 0.0f;
+  float b[32], incl[32];
+  for (int l = 0; l < 32; ++l) {
+    float s = 0.0f;
+    for (int j = 0; j < C; ++j) {
+      const int r = l * C + j;
+      if (r < V) s = s + e[r];
+    }
+    b[l] = s;
+  }
+  lane_scan(b, incl);
+  const float S = incl[31];
+  for (int r = 0; r < V; ++r) keep[r] = r < nk;
+  if (topp < 1.0f) {
+    float bp[32], inclp[32];
+    for (int l = 0; l < 32; ++l) {
+      float s = 0.0f;
+      for (int j = 0; j < C; ++j) {
+        const int r = l * C + j;
+        if (r < V) {
+          pr[r] = e[r] / S;
+          s = s + pr[r];
+        }
+      }
+      bp[l] = s;
+    }
+    lane_scan(bp, inclp);
+    for (int l = 0; l < 32; ++l) {
+      float run = l ? inclp[l - 1] : 0.0f;
+      for (int j = 0; j < C; ++j) {
+        const int r = l * C + j;
+        if (r >= V) break;
+        if (keep[r]) keep[r] = (r == 0) || !(run > topp);
+        run = run + pr[r];
+      }
+    }
+  }
+  float b2[32], incl2[32];
+  for (int l = 0; l < 32; ++l) {
+    float s2 = 0.0f;
+    for (int j = 0; j < C; ++j) {
+      const int r = l * C + j;
+      if (r < V && keep[r]) s2 = s2 + e[r];
+    }
+    b2[l] = s2;
+  }
+  lane_scan(b2, incl2);
+  const float S2 = incl2[31];
+  const int ok = !any_nan && isfinite(kv[0].key) && S2 > 0.0f && isfinite(S2);
+  float best = -1.0f;
+  int bidx = 0x7fffffff;
+  for (int r = 0; r < V; ++r) {
+    const int id = kv[r].idx;
+    float sc;
+    if (ok) {
+      if (!keep[r]) continue;
+      sc = (e[r] / S2) / q[id];
+    } else {
+      sc = 1.0f / q[id];
+    }
+    if (sc > best || (sc == best && id < bidx)) {
+      best = sc;
+      bidx = id;
+    }
+  }
+  free(kv);
+  free(e);
+  free(pr);
+  free(keep);
+  if (ok_out) *ok_out = ok;
+  return bidx;
+}

@@ -41,6 +41,10 @@ def lib():
             L.fb_sample_row.argtypes = [fp, fp, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float,
                                         ctypes.c_longlong, ctypes.c_float, ctypes.c_longlong, fp,
                                         ctypes.POINTER(ctypes.c_int)]
+            L.fb_bb_sample_row.restype = ctypes.c_int
+            L.fb_bb_sample_row.argtypes = [fp, ctypes.c_int, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p,
+                                           ctypes.c_int, ctypes.c_float, ctypes.c_longlong, ctypes.c_float,
+                                           ctypes.c_longlong, fp, ctypes.POINTER(ctypes.c_int)]
             _LIB = L
     return _LIB
 
@@ -68,6 +72,20 @@ def sample_row(lc, lu, codebook_size, gs, temp, topk, topp, dosample, q):
     t = lib().fb_sample_row(_fp(lc), lu_p, lc.size, int(codebook_size), float(gs), float(temp), int(topk),
                             float(topp), int(dosample), _fp(q), ctypes.byref(g))
     return int(t), int(g.value)
+
+
+def bb_sample_row(logits, present, penalty, suppress, temp, topk, topp, dosample, q):
+    """The backbone sampler (fb_bb_sample_row): returns (token, ok).  logits/q: [V] fp32; present: [V] bool or
+    None; suppress: int ids or None."""
+    x = np.ascontiguousarray(logits, np.float32)
+    q = np.ascontiguousarray(q, np.float32)
+    pres = None if present is None else np.ascontiguousarray(present, np.uint8)
+    sup = None if suppress is None or len(suppress) == 0 else np.ascontiguousarray(suppress, np.int64)
+    ok = ctypes.c_int(0)
+    t = lib().fb_bb_sample_row(_fp(x), x.size, None if pres is None else pres.ctypes.data, float(penalty),
+                               None if sup is None else sup.ctypes.data, 0 if sup is None else sup.size, float(temp),
+                               int(topk), float(topp), int(dosample), _fp(q), ctypes.byref(ok))
+    return int(t), int(ok.value)
 
 
 def sample_rows(logits, half, codebook_size, gs, temp, topk, topp, dosample, q):

@@ -36,7 +36,11 @@ sys.path.insert(0, HERE)
 import synth  # noqa: E402
 
 
+REF_ROOT = []
+
+
 def ref_env(ref_root):
+    REF_ROOT[:] = [ref_root]
     up = os.path.join(ref_root, 'third_party', 'breeze-tts')
     sys.path.insert(0, up)
     import transformers.cache_utils as cu
@@ -410,6 +414,38 @@ def gold_sampler(out):
     out['sampler'] = dict(tokens=np.asarray(toks, np.int64), digest=synth.digest(lc, lu, q))
 
 
+def gold_bb_sampler(out):
+    """The reference's backbone sampler flash/sampling.py sample_logits (host-sync-free, bitwise equal to the
+    official one), loaded from its file, with torch.multinomial(probs, 1) -> argmax(probs / q)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('ref_flash_sampling', os.path.join(REF_ROOT[0], 'flash',
+                                                                                      'sampling.py'))
+    fs = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(fs)
+    c = synth.BB_SAMPLER
+    x, present, q, params = synth.bb_sampler_cases()
+    sup = torch.tensor(c['suppress'], dtype=torch.long)
+    toks, oks = [], []
+    for r, (pen, temp, topk, topp, ds, use_sup) in enumerate(params):
+        qr = q[r][None]
+
+        def mult(probs, n, *a, **kw):
+            return torch.argmax(probs / qr.to(probs.dtype), dim=-1, keepdim=True)
+
+        orig = fs.torch.multinomial
+        fs.torch.multinomial = mult
+        try:
+            tok, ok = fs.sample_logits(x[r][None].clone(), temperature=temp, top_k=topk, top_p=topp, do_sample=bool(ds),
+                                       present=present[r][None], repetition_penalty=pen,
+                                       suppress_idx=sup if use_sup else None)
+        finally:
+            fs.torch.multinomial = orig
+        toks.append(int(tok.reshape(-1)[0]))
+        oks.append(int(bool(ok)))
+    out['bb_sampler'] = dict(tokens=np.asarray(toks, np.int64), ok=np.asarray(oks, np.int64),
+                             digest=synth.digest(x, present.to(torch.uint8), q))
+
+
 def gold_prefill(out):
     from transformers.models.qwen3.modeling_qwen3 import eager_attention_forward
     c = synth.PREFILL
@@ -431,7 +467,7 @@ def main():
     out = {}
     only = set(args.only.split(',')) if args.only else None
     for fn in (gold_attention, gold_attention1, gold_gemv, gold_gemv2, gold_backbone, gold_depth, gold_sampler,
-               gold_prefill, gold_drift, gold_depth_drift):
+               gold_prefill, gold_drift, gold_depth_drift, gold_bb_sampler):
         if only and fn.__name__[len('gold_'):] not in only:
             continue
         fn(out)

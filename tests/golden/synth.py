@@ -172,6 +172,41 @@ def sampler_cases(c=SAMPLER):
     return lc, lu, q, params
 
 
+# ---------------------------------------------------------------- backbone (codebook-0) sampler rows
+# the CFG logits row of the backbone: vocab + 1 ids; the runtime's parameters are do_sample, T 0.9, top-k 50,
+# top-p 1.0, repetition penalty 1.1 over the ids generated so far, the reserved codec ids suppressed
+BB_SAMPLER = dict(seed=108, rows=60, vocab=2049, n_present=300, suppress=(2048, 2047))
+
+
+def bb_sampler_cases(c=BB_SAMPLER):
+    """Per row: logits, presence mask, q, and (penalty, temp, topk, topp, dosample, suppress?) covering the runtime
+    defaults, greedy, top-k ties at the threshold, top-p, no top-k, and invalid rows (a NaN; everything
+    suppressed)."""
+    g = gen(c['seed'])
+    V, R = c['vocab'], c['rows']
+    x = torch.randn((R, V), generator=g) * 3.0
+    present = torch.zeros((R, V), dtype=torch.bool)
+    for r in range(R):
+        present[r, torch.randperm(V, generator=g)[:c['n_present']]] = True
+    q = torch.empty((R, V)).exponential_(1.0, generator=g)
+    params = []
+    ks = [50, 0, 1, 7, 2049, 50, 64]
+    ps = [1.0, 0.9, 0.5, 1.0, 0.95]
+    for r in range(R):
+        params.append((float([1.1, 1.0, 1.3][r % 3]), float([0.9, 1.0, 0.5, 1.4][(r // 3) % 4]), int(ks[r % len(ks)]),
+                       float(ps[(r // 2) % len(ps)]), int(r % 9 != 4), int(r % 5 != 2)))
+    # exact ties at the top-k threshold: copy the 7th-largest value onto other ids
+    for r in range(0, R, 4):
+        v = torch.sort(x[r], descending=True).values[6]
+        for j in (11, 500, 1500):
+            x[r, j] = v
+    x[7, 123] = float('nan')                       # invalid: a NaN in the logits
+    x[13] = float('-inf')                          # greedy over nothing finite: index 0
+    x[14] = float('-inf')                          # invalid once suppressed: only the suppressed ids are finite
+    x[14, 2047], x[14, 2048] = 5.0, 3.0
+    return x, present, q, params
+
+
 # ---------------------------------------------------------------- causal prefill attention (config 5, small L)
 PREFILL = dict(seed=105, B=2, NH=16, NKV=4, D=128, L=40, pad=(0, 6))
 

@@ -1,6 +1,7 @@
 """GPU tests of the streaming-frame pieces: the greedy codebook-0 kernel (torch.argmax semantics), the frame-ids
-assembly, and ``FrameEngine`` (graph-captured frames) against the oracle's backbone step and the standalone depth
-frame."""
+assembly, and ``FrameEngine`` (graph-captured frames) against the oracle's backbone step, the C sampler oracle
+(codebook 0 sampled with the reference runtime's parameters on the engine's own Exp(1) draws and token history) and
+the standalone depth frame."""
 import numpy as np
 import pytest
 import torch
@@ -68,6 +69,22 @@ def _small_engine(streams=2, prompt=40, frames=4, group=1, lanes=1):
     return eng
 
 
+def _cb0_expected(eng, cfg_rows, c0, present_before):
+    """Codebook 0 of sampler rows c0.. from their CFG logits: the C oracle of the backbone sampler with the engine's
+    parameters, the draws it used (left in cb0_q) and the token history before the step."""
+    from oracle import sampler as osmp
+    p = eng.CB0_PARAMS
+    q = eng.cb0_q.cpu().numpy()
+    sup = list(range(eng.n_valid, eng.bcfg.vocab))
+    out = []
+    for k in range(cfg_rows.shape[0]):
+        t, ok = osmp.bb_sample_row(cfg_rows[k], present_before[c0 + k], p['repetition_penalty'], sup,
+                                   p['temperature'], p['top_k'], p['top_p'], p['do_sample'], q[c0 + k])
+        assert ok == 1
+        out.append(t)
+    return out
+
+
 def _oracle_backbone(bb):
     st = bb._bb_state
     layers = [dict(ln1=np32(L.ln1_w), wq=np32(L.wq), wk=np32(L.wk), wv=np32(L.wv), qn=np32(L.qn_w), kn=np32(L.kn_w),
@@ -96,6 +113,7 @@ def test_frame_engine_matches_oracle_and_standalone_depth(group, lanes):
         # each frame is checked from the device's own state (its KV cache so far), so the comparison is per frame and
         # does not compound earlier frames' rounding differences
         before = []
+        present = eng.cb0_present.cpu().numpy().copy()
         for st in eng.streams:
             bb = st.bb
             before.append(dict(kcs=[np32(L.keys).copy() for L in bb.static_cache.layers],
@@ -122,7 +140,7 @@ def test_frame_engine_matches_oracle_and_standalone_depth(group, lanes):
             # itself (three separately rounded fp32 ops) is checked exactly on the kernel's own logits
             g_cfg = bb.cfg_logits_buf.cpu().numpy()
             np.testing.assert_array_equal(g_cfg, dec.cfg_combine(g_lg, group, gs))
-            cb0 = [ofr.greedy_cb0(g_cfg[k], eng.n_valid) for k in range(group)]
+            cb0 = _cb0_expected(eng, g_cfg, st.c0, present)
             np.testing.assert_array_equal(st.first_cb.cpu().numpy(), cb0 + cb0)
             # the engine's depth launch consumed this frame's hidden state and cb0: a standalone launch agrees
             d = eng.depth
@@ -159,6 +177,7 @@ def test_frame_engine_shared_backbone_matches_oracle(group, slots, lanes):
         kcs = [np32(L.keys).copy() for L in bb.static_cache.layers]
         vcs = [np32(L.values).copy() for L in bb.static_cache.layers]
         ids = np.concatenate([eng.first_cb.cpu().numpy()[:, None], eng.outtok.cpu().numpy()[:, :C - 1]], 1)
+        present = eng.cb0_present.cpu().numpy().copy()
         eng.step()
         torch.cuda.synchronize()
         np.testing.assert_array_equal(bb.input_ids_buf.view(R, -1).cpu().numpy(), ids)
@@ -178,8 +197,10 @@ def test_frame_engine_shared_backbone_matches_oracle(group, slots, lanes):
             assert_close(g_lg[r], lg, what=f'slot {i} frame {f} logits')
             cfg_blk = g_cfg[st.r0 // 2:st.r0 // 2 + group]
             np.testing.assert_array_equal(cfg_blk, dec.cfg_combine(g_lg[r], group, gs))
-            cb0 = [ofr.greedy_cb0(cfg_blk[k], eng.n_valid) for k in range(group)]
+            cb0 = _cb0_expected(eng, cfg_blk, st.c0, present)
             np.testing.assert_array_equal(st.first_cb.cpu().numpy(), cb0 + cb0)
+            # the sampled tokens joined the streams' histories (the next frame's repetition penalty)
+            assert all(eng.cb0_present[st.c0 + k, cb0[k]].item() == 1 for k in range(group))
             d = eng.depth
             out = torch.zeros_like(st.outtok)
             tb = torch.zeros_like(st.tokbuf)
@@ -205,6 +226,22 @@ def test_frame_engine_free_running_lanes_equal_joined_steps():
     for sa, sb in zip(ea.streams, eb.streams):
         assert torch.equal(sa.outtok, sb.outtok) and torch.equal(sa.first_cb, sb.first_cb)
         assert torch.equal(sa.bb.cfg_logits_buf, sb.bb.cfg_logits_buf)
+
+
+def test_frame_engine_greedy_cb0():
+    """cb0='greedy' keeps the greedy branch: codebook 0 is the argmax of the stream's CFG logits."""
+    from flashb.engine import BackboneConfig, DepthConfig, FrameEngine
+    bcfg = BackboneConfig(hidden=512, layers=2, heads=8, kv_heads=2, ffn=1024, vocab=65, codebooks=7)
+    dcfg = DepthConfig(hidden=256, embed_dim=512, layers=2, heads=2, kv_heads=1, ffn=512, vocab=64,
+                       codebook_size=60, n_decode=6)
+    eng = FrameEngine(bcfg, dcfg, 4, 40, 4, seed=4, group=2, shared_backbone=True, cb0='greedy')
+    eng.capture()
+    eng.step()
+    torch.cuda.synchronize()
+    g_cfg = eng.bb.cfg_logits_buf.cpu().numpy()
+    for st in eng.streams:
+        cb0 = [ofr.greedy_cb0(g_cfg[st.r0 // 2 + k], eng.n_valid) for k in range(2)]
+        np.testing.assert_array_equal(st.first_cb.cpu().numpy(), cb0 + cb0)
 
 
 def test_frame_engine_graph_equals_eager():

@@ -2,6 +2,7 @@
 PyTorch modules (tests/golden/make_golden.py); the oracle must reproduce it on the same seeded inputs."""
 import numpy as np
 import pytest
+import torch
 
 import synth
 from oracle import decode as dec
@@ -219,3 +220,18 @@ def test_depth_argmax_study_fixture():
     assert a1 == float(z['argmax_bf16_fp32']) and a2 == float(z['argmax_oracle_bf16'])
     assert a1 < 0.999 and a2 < 0.999          # the 99.9% bar is out of reach even for the reference's own arithmetic
     assert DEPTH_ARGMAX_MIN <= a1
+
+
+def test_backbone_sampler_golden():
+    """The C backbone sampler (oracle/sampler.c fb_bb_sample_row) reproduces the reference's own sample_logits
+    (flash/sampling.py, multinomial -> argmax(p / q)) token for token and flag for flag: repetition penalty,
+    suppression, greedy, top-k with ties at the threshold, top-p, no top-k, invalid rows."""
+    z = load('bb_sampler')
+    x, present, q, params = synth.bb_sampler_cases()
+    assert str(z['digest']) == synth.digest(x, present.to(torch.uint8), q)
+    c = synth.BB_SAMPLER
+    for r, (pen, temp, topk, topp, ds, use_sup) in enumerate(params):
+        t, ok = smp.bb_sample_row(x[r].numpy(), present[r].numpy(), pen, c['suppress'] if use_sup else None, temp,
+                                  topk, topp, ds, q[r].numpy())
+        assert (t, ok) == (int(z['tokens'][r]), int(z['ok'][r])), f'row {r} {params[r]}'
+    assert int(z['ok'].sum()) == len(params) - 2           # the NaN row and the nothing-left row
