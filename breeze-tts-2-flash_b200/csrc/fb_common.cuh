@@ -15,6 +15,12 @@ constexpr unsigned FULL = 0xffffffffu;
 
 // ------------------------------------------------------------------------------------------------ bf16 helpers
 __device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// bf16(silu(g)) for the SwiGLU activations, g on the bf16 grid: g / (1 + e^-g) with the fast exponential and
+// division intrinsics (a few fp32 ulps, below the bf16 rounding of the result except at rare ties).  The exact
+// expf and IEEE division cost about 55 ns per value per thread on B200 (their special-case branches defeat
+// interleaving), which made the SiLU the longest part of the many-rows GEMV epilogues.
+__device__ __forceinline__ float silu_rbf(float g) { return rbf(__fdividef(g, 1.0f + __expf(-g))); }
 __device__ __forceinline__ float b2f(bf16 x) { return __bfloat162float(x); }
 __device__ __forceinline__ float lo_f(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float hi_f(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }

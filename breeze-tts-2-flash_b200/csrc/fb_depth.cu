@@ -1068,7 +1068,7 @@ __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l
                           const int i = tid / M, r = tid - i * M;
                           const float g = rbf(sm[i * MS + r]);
                           const float u = rbf(sm[(i + 8) * MS + r]);
-                          act[(size_t)r * F + n0 + i] = __float2bfloat16_rn(rbf(g / (1.0f + expf(-g))) * u);
+                          act[(size_t)r * F + n0 + i] = __float2bfloat16_rn(silu_rbf(g) * u);
                         }
                       }, [](int) {})) {
     c.ok = 0;

@@ -22,6 +22,7 @@ namespace fb {
 
 // Kernel the calling thread's last GEMV launch used: 0 FMA, 1 mma.sync stream, 2 tcgen05 (flashb_gemv_last_path).
 thread_local int t_gemv_path = -1;
+int g_rows_path = 1;   // the many-rows kernel (fb_gemv_rows.cu) for 17..128 rows without norm; 0: off
 
 constexpr int GV_CWARPS = 8;
 constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_fma_kernel(const GemvArgs a) 
             } else {
               const float g = rbf(acc[0][m]);
               const float u = rbf(acc[NMAT - 1][m]);
-              v = rbf(g / (1.0f + expf(-g))) * u;
+              v = silu_rbf(g) * u;
             }
             a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(v);
           }
@@ -273,6 +274,13 @@ int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
   if (M > 16) {
     // up to 128 rows: the tcgen05 kernel (MMA N = the rows); else row blocks through the paths below (16 rows, or
     // 8 / 4 / 2 / 1 for K % 64 != 0), each block streaming the weights again
+    if (a.K % 64 == 0 && !NORM && g_rows_path) {
+      const int rt = gemv_rows(a, EPI, st);
+      if (rt != FB_ERR_UNSUPPORTED) {
+        t_gemv_path = 3;
+        return rt;
+      }
+    }
     if (a.K % 64 == 0) {
       const int rt = gemv_tc(a, EPI, NORM, st);
       if (rt != FB_ERR_UNSUPPORTED) {
@@ -390,9 +398,15 @@ extern "C" int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const v
 
 extern "C" int flashb_gemv_last_path(void) { return t_gemv_path; }
 
-extern "C" int flashb_gemv_last_split(void) { return t_gemv_path == 2 ? fb::gemv_tc_last_split() : 1; }
+extern "C" int flashb_gemv_last_split(void) {
+  return t_gemv_path == 2 ? fb::gemv_tc_last_split() : (t_gemv_path == 3 ? fb::gemv_rows_last_split() : 1);
+}
+
+extern "C" void flashb_set_gemv_rows_path(int enable) { g_rows_path = enable ? 1 : 0; }
 
 extern "C" void flashb_set_gemv_split(int enable) { fb::gemv_tc_set_split_small(enable); }
+
+extern "C" void flashb_set_gemv_trace(void* buf) { fb::gemv_tc_set_trace(buf); }
 
 extern "C" int flashb_set_gemv_group_rows(int rows) {
   FB_CHECK_ARG(rows == 16 || rows == 32 || rows == 64 || rows == 128, "gemv: group rows %d not 16, 32, 64 or 128", rows);
@@ -417,13 +431,13 @@ extern "C" int flashb_gemv_gateup(const void* x, int64_t ldx, int M, int K, cons
   int rc = common_checks(x, ldx, M, K, y, ldy);
   if (rc) return rc;
   FB_CHECK_ARG(Wg && Wu && N > 0 && al16(Wg) && al16(Wu), "gemv_gateup: bad Wg/Wu");
-  FB_CHECK_ARG(nw && al16(nw), "gemv_gateup: norm weight required and 16B aligned");
+  FB_CHECK_ARG(!nw || al16(nw), "gemv_gateup: norm weight not 16B aligned");
   GemvArgs a{};
   a.x = (const bf16*)x; a.ldx = (long)ldx; a.nw = (const bf16*)nw; a.eps = eps;
   a.W0 = (const bf16*)Wg; a.W1 = (const bf16*)Wu; a.W2 = a.W0; a.N0 = N; a.N1 = 0; a.K = K; a.N = N;
   a.y = (bf16*)y; a.ldy = (long)ldy;
   if ((rc = setup_ring(a, M, 2))) return rc;
-  return dispatch_m<2, true>(a, M, (cudaStream_t)stream);
+  return nw ? dispatch_m<2, true>(a, M, (cudaStream_t)stream) : dispatch_m<2, false>(a, M, (cudaStream_t)stream);
 }
 
 extern "C" int flashb_rmsnorm(const void* x, int64_t ldx, int M, int K, const void* w, float eps, void* y,

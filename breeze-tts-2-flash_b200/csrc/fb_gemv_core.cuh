@@ -60,6 +60,12 @@ int gemv_tc(GemvArgs& a, int epi, bool norm, cudaStream_t st);
 int gemv_tc_last_split();
 void gemv_tc_set_split_small(int on);
 int gemv_tc_set_group_rows(int rows);
+void gemv_tc_set_trace(void* buf);
+unsigned long long* gemv_trace_buf();   // the timeline buffer of flashb_set_gemv_trace, or null
+// The many-rows tcgen05 GEMV (fb_gemv_rows.cu, 17..128 rows, no norm); FB_ERR_UNSUPPORTED when the shape does not
+// suit it.  gemv_rows_last_split: the cluster size of this thread's last launch of it.
+int gemv_rows(GemvArgs& a, int epi, cudaStream_t st);
+int gemv_rows_last_split();
 
 // Launches the 32 KB-stage build (fb_gemv_narrow.cu); epi / norm select the instantiation, xchunk the staging.
 int gemv_mma_narrow(GemvArgs& a, int epi, bool norm, cudaStream_t st, int xchunk, int min_nst);
@@ -224,7 +230,7 @@ __global__ void __launch_bounds__(GM_THREADS) gemv_mma_kernel(const __grid_const
       } else {
         const float gg = rbf(sums[i * MS + m]);
         const float uu = rbf(sums[(i + 8) * MS + m]);
-        v = rbf(gg / (1.0f + expf(-gg))) * uu;
+        v = silu_rbf(gg) * uu;
       }
       a.y[(size_t)m * a.ldy + n] = __float2bfloat16_rn(v);
     }

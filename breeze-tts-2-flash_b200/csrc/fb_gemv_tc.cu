@@ -90,7 +90,17 @@ struct alignas(64) TcArgs {
   int nst;
   int split;           // CTAs per cluster sharing one block's K range (1: no split)
   unsigned* err;
+  unsigned long long* trace;   // optional per-CTA timeline (TC_TRACE_SLOTS %globaltimer stamps), or null
 };
+
+// Optional timeline of one launch: CTA c (blockIdx.y * gridDim.x + blockIdx.x) writes TC_TRACE_SLOTS values at
+// trace[c * TC_TRACE_SLOTS]: entry, producer past griddepcontrol.wait, first stage in (MMA warp), last MMA committed,
+// epilogue done, split-K reduction done, exit (ns), and the SM id.
+constexpr int TC_TRACE_SLOTS = 8;
+#define TC_STAMP(i)                                                                                         \
+  do {                                                                                                      \
+    if (a.trace) a.trace[(blockIdx.y * gridDim.x + blockIdx.x) * TC_TRACE_SLOTS + (i)] = globaltimer();   \
+  } while (0)
 
 // Tensor map and first row of 128 weight rows starting at block row r (EPI 0/1: segments are multiples of 128).
 // Rows past the last row stay with the last segment (an out-of-range box reads zeros), never with an empty one.
@@ -106,7 +116,7 @@ template <int EPI>
 __device__ __forceinline__ float tc_out(const TcArgs& a, float v, float u, int m, int n) {
   if (EPI == 2) {
     const float gg = rbf(v);
-    return rbf(gg / (1.0f + expf(-gg))) * rbf(u);
+    return silu_rbf(gg) * rbf(u);
   }
   if (EPI == 1) return b2f(a.res[(size_t)m * a.ldr + n]) + rbf(v);
   return v;
@@ -138,6 +148,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
   float* red = reinterpret_cast<float*>(smem);                    // split K: partial sums, over the idle ring
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) TC_STAMP(0);
   // row group blockIdx.y: activation rows [r0, r0 + M) of the launch's a.M
   const int r0 = blockIdx.y * MT;
   const int K = a.K, M = min(MT, a.M - r0);
@@ -211,6 +222,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     __syncwarp();
     issued = pre;
     pdl_wait();
+    if (lane == 0) TC_STAMP(1);
     if (lane == 0)
       for (int t = 0; t < pre; ++t) issue_x(t);
     __syncwarp();
@@ -249,6 +261,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
           break;
         }
         tc_after();
+        if (lane == 0 && t == 0) TC_STAMP(2);
         if (lane == 0) {
           const uint32_t wa = smem_u32(wring + (size_t)s * TC_WBYTES);
           const uint32_t xa = smem_u32(xring + (size_t)s * XB);
@@ -272,6 +285,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         committed = t;
       }
     }
+    if (lane == 0) TC_STAMP(3);
     // the ring's last slots must not be overwritten by a later CTA while the tensor core still reads them
     if (committed >= 0) mbar_wait_warp(&empty[committed % NST], (committed / NST) & 1, a.err);
   } else {
@@ -422,6 +436,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     }
   }
   __syncwarp();
+  if (tid == 64) TC_STAMP(4);
   if (early) cl_wait();
   if (S > 1) {
     // every thread of every CTA of the cluster reaches both barriers, whatever happened above
@@ -462,13 +477,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
     }
     cluster.sync();
   }
+  if (tid == 64) TC_STAMP(5);
   tc_before();
   __syncthreads();
   tc_after();
   if (warp == 1) tc_dealloc(tmem, 2 * DCOLS);
+  if (tid == 0) {
+    TC_STAMP(6);
+    unsigned sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    if (a.trace) a.trace[(blockIdx.y * gridDim.x + blockIdx.x) * TC_TRACE_SLOTS + 7] = sm;
+  }
 }
 
 thread_local int t_split = 1;
+unsigned long long* g_tc_trace = nullptr;
 // split K also for M <= 16 (FLASHB_TC_SPLIT=1 or flashb_set_gemv_split(1)).  Off by default: measured on B200 at 148 SMs and M = 2, the
 // mma.sync kernel's 8-row split takes 3.6 / 7.8 / 7.9 / 14.7 us for the backbone's o / q|k|v / down / gate|up
 // matrices, the cluster split 9.2 / 17.2 / 14.6 / 27.4 us (a cluster of 8 large-smem CTAs waits for whole free SMs
@@ -485,6 +508,7 @@ int launch_tc(const GemvArgs& g, int split, cudaStream_t st) {
   a.N0 = g.N0; a.N1 = g.N1; a.N = g.N; a.K = g.K; a.M = g.M;
   a.y = g.y; a.ldy = g.ldy; a.res = g.res; a.ldr = g.ldr; a.err = g.err;
   a.split = split;
+  a.trace = g_tc_trace;
   const int nseg[3] = {EPI == 2 ? g.N : g.N0, EPI == 2 ? g.N : g.N1, EPI == 2 ? 0 : g.N - g.N0 - g.N1};
   const bf16* wseg[3] = {g.W0, g.W1, g.W2};
   for (int i = 0; i < 3; ++i) {
@@ -578,6 +602,8 @@ int gemv_tc(GemvArgs& g, int epi, bool norm, cudaStream_t st) {
 }
 
 int gemv_tc_last_split() { return t_split; }
+void gemv_tc_set_trace(void* buf) { g_tc_trace = static_cast<unsigned long long*>(buf); }
+unsigned long long* gemv_trace_buf() { return g_tc_trace; }
 void gemv_tc_set_split_small(int on) { g_split_small = on ? 1 : 0; }
 int gemv_tc_set_group_rows(int rows) {
   if (rows != 16 && rows != 32 && rows != 64 && rows != 128) return FB_ERR_ARG;

@@ -41,6 +41,8 @@ _PROTOS = {
     'flashb_attn_last_path': (I, []),
     'flashb_set_gemv_split': (None, [I]),
     'flashb_set_gemv_group_rows': (I, [I]),
+    'flashb_set_gemv_trace': (None, [P]),
+    'flashb_set_gemv_rows_path': (None, [I]),
     'flashb_attn_ws_floats': (L, [I, I, I, I, I]),
     'flashb_attn_decode': (I, [P, L, L, P, P, L, L, I, I, I, I, I, P, I, L, F, P, L, P, P, P]),
     'flashb_attn_decode_fused': (I, [P, L, P, P, F, P, P, L, P, P, L, L, I, I, I, I, I, P, I, L, P, F, P, L, P, P,

@@ -29,6 +29,8 @@ GEMV_CFG = {
 }
 _WS = {}
 ORIG = {}
+# rows above which the RMSNorms run apart from the GEMVs (the many-rows GEMV kernel takes 17..128 rows)
+ROWS_NORM_APART = 16
 
 
 def workspace(device, B, NH, NKV, S, D=128):
@@ -63,6 +65,7 @@ def make_state(B, layers, norm_w, norm_eps, embed_table, vocab, lm_head32, cos_t
                 x0=torch.empty(B, H, **bf), cos=torch.empty(B, 1, 128, **bf), sin=torch.empty(B, 1, 128, **bf),
                 qkv=torch.empty(B, nq + 2 * nk, **bf), ao=torch.empty(B, 1, nq // 128, 128, **bf),
                 h1=torch.empty(B, H, **bf), act=torch.empty(B, I, **bf), x=torch.empty(B, H, **bf),
+                xn=torch.empty(B, H, **bf) if B > ROWS_NORM_APART else None,
                 ws=workspace(device, B, nq // 128, nk // 128, max_seq_len))
 
 
@@ -141,18 +144,31 @@ def _prep(graph):
 
 
 def run_layers(st, x, kv_layers, mask, cache_position):
-    """The 28 x 5 kernel body; ``x`` is the embedded input [B, H]; returns the final residual stream [B, H]."""
+    """The 28 x 5 kernel body; ``x`` is the embedded input [B, H]; returns the final residual stream [B, H].
+
+    With more than ROWS_NORM_APART rows (the shared step of many streams) each RMSNorm runs as its own launch into
+    ``xn`` and the q|k|v and gate|up GEMVs take the normalised rows: the many-rows GEMV kernel has no norm prologue
+    (it would re-read every row for the sums of squares on every CTA).  The values are the same: the norm is the
+    same eager Qwen3 RMSNorm either way."""
     fx, ax = kernels.fused(), kernels.attn()
     B = st['B']
     ws = st['ws']
-    qkv, ao, h1, act, xb = st['qkv'], st['ao'], st['h1'], st['act'], st['x']
+    qkv, ao, h1, act, xb, xn = st['qkv'], st['ao'], st['h1'], st['act'], st['x'], st.get('xn')
     for li, L in enumerate(st['layers']):
         kc, vc = kv_layers[li]
-        fx.gemv_seg(x, L.ln1_w, L.ln1_eps, L.wq, L.wk, L.wv, qkv)
+        if xn is not None:
+            fx.rmsnorm(x, L.ln1_w, L.ln1_eps, xn)
+            fx.gemv_seg(xn, None, L.ln1_eps, L.wq, L.wk, L.wv, qkv)
+        else:
+            fx.gemv_seg(x, L.ln1_w, L.ln1_eps, L.wq, L.wk, L.wv, qkv)
         ax.attn_decode_fused(qkv, L.qn_w, L.kn_w, L.qk_eps, st['cos'], st['sin'], kc, vc, mask, cache_position,
                              L.scaling, ws['scores'], ws['cmax'], ws['part'], ws['counters'], ao)
         fx.gemv_resid(ao.view(B, -1), L.wo, x, h1)
-        fx.gemv_gateup(h1, L.ln2_w, L.ln2_eps, L.wg, L.wu, act)
+        if xn is not None:
+            fx.rmsnorm(h1, L.ln2_w, L.ln2_eps, xn)
+            fx.gemv_gateup(xn, None, L.ln2_eps, L.wg, L.wu, act)
+        else:
+            fx.gemv_gateup(h1, L.ln2_w, L.ln2_eps, L.wg, L.wu, act)
         fx.gemv_resid(act, L.wd, h1, xb)
         x = xb
     return x

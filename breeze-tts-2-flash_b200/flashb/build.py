@@ -24,7 +24,7 @@ LIBDIR = os.path.join(PKG, '_lib')
 LIB = os.path.join(LIBDIR, 'libflashb.so')
 
 SOURCES = ['fb_api.cu', 'fb_gemv.cu', 'fb_attn.cu', 'fb_aux.cu', 'fb_sample.cu', 'fb_depth.cu', 'fb_prefill.cu',
-           'fb_gemv_narrow.cu', 'fb_gemv_tc.cu', 'fb_attn_mma.cu']
+           'fb_gemv_narrow.cu', 'fb_gemv_tc.cu', 'fb_gemv_rows.cu', 'fb_attn_mma.cu']
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 FLAGS = ['-O3', '-lineinfo', '-std=c++17', '-Xcompiler', '-fPIC', '--expt-relaxed-constexpr', '-I', CSRC, '-I', INCLUDE]
 

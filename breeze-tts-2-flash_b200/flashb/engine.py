@@ -625,15 +625,18 @@ class FrameEngine:
 
     def launches_per_frame(self):
         """flashb kernel launches per slot frame (the Exp(1) draws are torch's own kernels and not counted).  A
-        backbone graph: frame ids, position advance, embedding, 5 per layer, the LM head (one launch for one CFG
-        block, else a final norm and one pass for every block) and codebook 0 (one sampler launch, or a greedy pick
-        per slot); with a shared backbone its launches are shared out over the slots.  Plus one depth launch."""
+        backbone graph: frame ids, position advance, embedding, 5 per layer (7 when the rows exceed
+        backbone.ROWS_NORM_APART: the two RMSNorms run apart), the LM head (one launch for one CFG block, else a final
+        norm and one pass for every block) and codebook 0 (one sampler launch, or a greedy pick per slot); with a
+        shared backbone its launches are shared out over the slots.  Plus one depth launch."""
+        from . import backbone as bb
         L = self.bcfg.layers
         if self.shared:
             n = len(self.streams)
             cb0 = 1 if self.cb0 == 'sample' else n
             lm = 1 if n == 1 and 2 * self.group <= 16 else 2
-            return (3 + 5 * L + lm + cb0) / n + 1
+            per_layer = 7 if 2 * self.group * n > bb.ROWS_NORM_APART else 5
+            return (3 + per_layer * L + lm + cb0) / n + 1
         return 3 + 5 * L + 1 + 1 + 1
 
     def frame_bytes(self):

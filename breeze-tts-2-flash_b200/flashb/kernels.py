@@ -153,7 +153,8 @@ class FusedOps:
         _req(Wg.shape[0] == Wu.shape[0], 'Wg/Wu rows')
         N = Wg.shape[0]
         _req(y.dtype == torch.bfloat16 and y.shape[0] == M and y.shape[1] == N and y.stride(1) == 1, 'y')
-        _req(nw.dtype == torch.bfloat16 and nw.is_contiguous() and nw.numel() == K, 'nw')
+        if nw is not None:
+            _req(nw.dtype == torch.bfloat16 and nw.is_contiguous() and nw.numel() == K, 'nw')
         check(_native.lib().flashb_gemv_gateup(_p(x), x.stride(0), M, K, _p(nw), float(eps), _p(Wg), _p(Wu), N,
                                                _p(y), y.stride(0), _stream(x)))
 

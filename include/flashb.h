@@ -58,6 +58,14 @@ void flashb_set_gemv_split(int enable);
  * that L2 serves all but the first read; wider groups read each tile for more rows (the MMA's N).  Process-wide;
  * no reference counterpart. */
 int flashb_set_gemv_group_rows(int rows);
+/* Timeline of the tcgen05 GEMV launches issued after this call (null: off, the default): CTA c of a launch writes 8
+ * uint64 at buf[8 c] -- %globaltimer ns at entry, producer past the dependent-launch wait, first stage in, last MMA
+ * committed, epilogue done, split-K reduction done, exit -- and its SM id.  buf must hold 8 x the launch's CTAs;
+ * each launch overwrites it.  Process-wide diagnostic; no reference counterpart. */
+void flashb_set_gemv_trace(void* buf);
+/* The many-rows tcgen05 GEMV (17..128 rows, no norm: activation rows as the MMA's M side, split K over a cluster)
+ * on (1, the default) or off (0: those calls take the row-group kernel).  Process-wide; no reference counterpart. */
+void flashb_set_gemv_rows_path(int enable);
 /* Programmatic dependent launch on (1, default) / off (0) for all later launches of this process. */
 void flashb_set_pdl(int enable);
 /* SM budget of the calling host thread (0, the default: every SM).  Launches issued later by this thread -- directly
@@ -111,7 +119,7 @@ int flashb_gemv_seg(const void* x, int64_t ldx, int M, int K, const void* nw, fl
 int flashb_gemv_resid(const void* x, int64_t ldx, int M, int K, const void* W, int N, const void* res, int64_t ldr,
                       void* y, int64_t ldy, void* stream);
 /* Replaces gemv_gateup (flash/csrc/bb_fused.cu:338-356): act = bf16(bf16(silu(bf16(n @ Wg^T))) * bf16(n @ Wu^T)),
- * n = RMSNorm(x; nw, eps); Wg, Wu [N, K]. */
+ * n = RMSNorm(x; nw, eps), or n = x when nw == NULL (rows normalised beforehand); Wg, Wu [N, K]. */
 int flashb_gemv_gateup(const void* x, int64_t ldx, int M, int K, const void* nw, float eps, const void* Wg,
                        const void* Wu, int N, void* y, int64_t ldy, void* stream);
 /* Replaces rmsnorm (flash/csrc/bb_fused.cu:358-368): y = bf16(w * bf16(x * rsqrt(mean(x^2) + eps))). */

@@ -154,11 +154,12 @@ def test_frame_engine_matches_oracle_and_standalone_depth(group, lanes):
     assert device_error() == 0
 
 
-@pytest.mark.parametrize('group,slots,lanes', [(2, 3, 3), (1, 2, 1), (4, 2, 2), (8, 2, 2)])
+@pytest.mark.parametrize('group,slots,lanes', [(2, 3, 3), (1, 2, 1), (4, 2, 2), (8, 2, 2), (8, 8, 8)])
 def test_frame_engine_shared_backbone_matches_oracle(group, slots, lanes):
-    """One backbone graph for every slot's rows (slot i = rows [2 g i, 2 g (i + 1)), its own CFG block; the GEMVs
-    as row groups of 16), the depth frames per slot on the lanes: every slot's block matches the oracle's step on
-    that block, and the depth launch consumed the block's hidden state and codebook 0."""
+    """One backbone graph for every slot's rows (slot i = rows [2 g i, 2 g (i + 1)), its own CFG block), the depth
+    frames per slot on the lanes: every slot's block matches the oracle's step on that block, and the depth launch
+    consumed the block's hidden state and codebook 0.  32 and 128 rows take the many-rows GEMV kernel with the
+    RMSNorms apart."""
     from flashb.engine import BackboneConfig, DepthConfig, FrameEngine
     bcfg = BackboneConfig(hidden=512, layers=2, heads=8, kv_heads=2, ffn=1024, vocab=65, codebooks=7)
     dcfg = DepthConfig(hidden=256, embed_dim=512, layers=2, heads=2, kv_heads=1, ffn=512, vocab=64,

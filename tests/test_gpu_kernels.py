@@ -443,6 +443,7 @@ def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, rows, split):
     from flashb._native import lib
     try:
         _budget(budget)
+        lib().flashb_set_gemv_rows_path(0)     # the many-rows kernel would take the calls without norm
         lib().flashb_set_gemv_split(1 if rows == 16 and split > 1 else 0)
         assert lib().flashb_set_gemv_group_rows(rows) == 0
         if kind == 'gateup':
@@ -475,11 +476,60 @@ def test_gemv_tcgen05_wide_and_split_k(ops, kind, M, budget, rows, split):
         torch.cuda.synchronize()
     finally:
         _budget(0)
+        lib().flashb_set_gemv_rows_path(1)
         lib().flashb_set_gemv_split(0)
         lib().flashb_set_gemv_group_rows(64)   # the library's default
     assert path == 2, f'expected the tcgen05 kernel, got path {path}'
     assert got_split == split, f'expected split {split}, got {got_split}'
     assert_close(np32(y), ref, what=f'tcgen05 {kind} M={M} rows={rows} split={split}')
     assert torch.equal(y, y2)
+    from flashb._native import device_error
+    assert device_error() == 0
+
+
+@pytest.mark.parametrize('kind,M,budget', [
+    ('qkv', 128, 0), ('o', 128, 0), ('gateup', 128, 0), ('down', 128, 0),
+    ('qkv', 17, 0), ('o', 64, 0), ('gateup', 100, 0), ('down', 33, 0),
+    ('qkv', 128, 64), ('gateup', 128, 40), ('down', 128, 18), ('odd', 70, 0), ('o', 128, 16)])
+def test_gemv_many_rows_matches_oracle(ops, kind, M, budget):
+    """17..128 activation rows without norm: the many-rows tcgen05 kernel (rows as the MMA's M side, 128-unit tiles,
+    K split over a cluster chosen from the occupancy API, partial sums pushed through distributed shared memory).
+    Checked against the oracle at the backbone's shapes and at SM budgets that force other splits, and for identical
+    bits on a second call."""
+    fx, _ = ops
+    from flashb._native import lib
+    K = {'down': 6144, 'odd': 1024}.get(kind, 2048)
+    x = randn((M, K), 61)
+    try:
+        _budget(budget)
+        if kind == 'gateup':
+            Wg, Wu = randn((6144, K), 63, 0.02), randn((6144, K), 64, 0.02)
+            y = torch.empty(M, 6144, dtype=torch.bfloat16, device='cuda')
+            call = lambda out: fx.gemv_gateup(x, None, 1e-6, Wg, Wu, out)
+            ref = dec.silu_mul(dec.linear(np32(x), np32(Wg)), dec.linear(np32(x), np32(Wu)))
+        elif kind == 'qkv':
+            Wq, Wk, Wv = randn((2048, K), 65, 0.02), randn((512, K), 66, 0.02), randn((512, K), 67, 0.02)
+            y = torch.empty(M, 3072, dtype=torch.bfloat16, device='cuda')
+            call = lambda out: fx.gemv_seg(x, None, 1e-6, Wq, Wk, Wv, out)
+            ref = dec.gemv_seg(np32(x), None, 1e-6, [np32(Wq), np32(Wk), np32(Wv)])
+        else:
+            N = 304 if kind == 'odd' else 2048
+            W = randn((N, K), 68, 0.02)
+            res = randn((M, N), 69)
+            y = torch.empty(M, N, dtype=torch.bfloat16, device='cuda')
+            call = lambda out: fx.gemv_resid(x, W, res, out)
+            ref = dec.gemv_resid(np32(x), np32(W), np32(res))
+        call(y)
+        torch.cuda.synchronize()
+        path, split = _path(), _split()
+        y2 = torch.full_like(y, float('nan'))
+        call(y2)
+        torch.cuda.synchronize()
+    finally:
+        _budget(0)
+    assert path == 3, f'expected the many-rows kernel, got path {path}'
+    assert 1 <= split <= 8
+    assert_close(np32(y), ref, what=f'many-rows {kind} M={M} budget={budget} split={split}')
+    assert torch.equal(y, y2), 'a second call must give the same bits'
     from flashb._native import device_error
     assert device_error() == 0
