@@ -83,6 +83,10 @@ struct alignas(64) DDArgs {
 // Optional trace: thread 0 of each CTA stamps %globaltimer at the end of every task and barrier of step s
 // (row layout [grid][n_decode][11 + 9 * layers]: start, E, barrier, 9 per layer, head, barrier, 6 sampler phases).
 #define DD_TRACE_SLOTS(L) (11 + 9 * (L))
+// tcgen05 build: after the phase rows, a detail row of 8 stamps for each of the first DD_DETAIL_CALLS GEMV tasks of
+// each CTA ([grid][DD_DETAIL_CALLS][8]: task entry, first stage in, last MMA issued, MMAs complete, accumulators
+// dumped, epilogues done, task end; blocks of the task)
+#define DD_DETAIL_CALLS 64
 #define DD_STAMP(s, idx)                                                                                   \
   do {                                                                                                     \
     if (a.trace && threadIdx.x == 0)                                                                       \
@@ -591,6 +595,7 @@ __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const D
 // left beside 220 KB of shared memory is small).  Per-CTA state the phases share lives in file-scope shared memory.
 __shared__ float g_dd_nred[ST_CWARPS * 16];
 __shared__ int g_dd_int[32];
+__shared__ int g_dd_call;                          // trace builds: GEMV tasks this CTA has run (detail timeline)
 __shared__ long long g_dd_tok[DD_MAXB];            // tokens fed to the next step (this CTA's copy)
 __shared__ __align__(16) bf16 g_dd_cs[2][128];     // [cos|sin][dim] of the sub-step's position
 __shared__ uint32_t g_dd_tmem;                     // tcgen05 build: TMEM base of the accumulators
@@ -694,7 +699,8 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
 // reported to every thread through shared memory after the next barrier.
 template <int KIND, typename EpiFn, typename StageFn>
 __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, int K, const unsigned char* xs,
-                                                float* dump, EpiFn epi, StageFn stage_x, unsigned* err) {
+                                                float* dump, EpiFn epi, StageFn stage_x, unsigned* err,
+                                                unsigned long long* det) {
   constexpr int UB = tc_units<KIND>();
   constexpr int C = tc_cols<KIND>();
   constexpr int GU = KIND == 0 ? 16 : 8;                       // units per group
@@ -709,6 +715,10 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
   if (threadIdx.x == 0) *abort_flag = 0;
   fence_proxy_async();                 // the caller's staging writes -> visible to the tensor core
   named_sync(1, PK_CONSUMERS);
+  if (det && threadIdx.x == 0) {
+    det[0] = globaltimer();
+    det[7] = (unsigned long long)(b1 - b0);
+  }
   for (int bi = b0; bi < b1; ++bi) {
     for (int p = 0; p < npass; ++p) {
       if (p > 0 || (bi > b0 && npass > 1)) {
@@ -722,6 +732,7 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
         for (int kcp = 0; kcp < nk; ++kcp) {
           const int t = c.t + kcp, s = t % rg.nst;
           const bool ok = mbar_wait_warp(&rg.full[s], (t / rg.nst) & 1, err);
+          if (det && lane == 0 && bi == b0 && p == 0 && kcp == 0) det[1] = globaltimer();
           if (!ok && lane == 0) *abort_flag = 1;
           if (lane == 0 && ok) {
             const uint32_t wa = smem_u32(rg.base + (size_t)s * ST_BYTES);
@@ -748,6 +759,7 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
           if (lane == 0) tc_commit(&rg.empty[s]);
           __syncwarp();
         }
+        if (det && lane == 0 && bi == b0) det[2] = globaltimer();
         if (lane == 0) tc_commit(&g_dd_mbar);
         __syncwarp();
       }
@@ -756,6 +768,7 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
       if (!mbar_wait(&g_dd_mbar, c.tph & 1, err)) *abort_flag = 1;
       ++c.tph;
       tc_after();
+      if (det && threadIdx.x == 0 && bi == b0) det[3] = globaltimer();
     }
     // accumulators -> dump (warps 0-3, TMEM lane quarter = warp) -> epilogues.  KIND 0 (M = 64): block row r sits
     // in lane (r % 16) of quarter r / 16, so warp q's lanes 0-15 hold rows 16 q ..; KIND 1 and 2 (M = 128): row =
@@ -803,6 +816,7 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
     }
     tc_before();
     named_sync(1, PK_CONSUMERS);
+    if (det && threadIdx.x == 0 && bi == b0) det[4] = globaltimer();
     if (*abort_flag) return false;
     if (KIND == 1) {
       for (int g = 0; g < 8; ++g) {
@@ -836,8 +850,10 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
         if (nu > 0) epi(n0, nu, dump + g * 256);
       }
     }
+    if (det && threadIdx.x == 0 && bi == b0) det[5] = globaltimer();
     named_sync(1, PK_CONSUMERS);       // the dump and the accumulators are reused by the next block
   }
+  if (det && threadIdx.x == 0) det[6] = globaltimer();
   return true;
 }
 
@@ -848,7 +864,14 @@ template <int NT, int KIND, typename EpiFn, typename StageFn>
 __device__ __forceinline__ bool dd_gemv(const DDArgs& a, DDSm& m, DDCur& c, int units, int K, int x_pitch, EpiFn epi,
                                         StageFn stage_x, const bf16* xg = nullptr, long ldx = 0) {
   if constexpr (NT == 0) {
-    return consume_task_tc<KIND>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err);
+    // trace builds: the first DD_DETAIL_CALLS tasks of each CTA record a detail timeline after the phase trace
+    unsigned long long* det = nullptr;
+    const int call = g_dd_call;
+    if (a.trace && call < DD_DETAIL_CALLS)
+      det = a.trace + (size_t)gridDim.x * a.NCB * DD_TRACE_SLOTS(a.L) + ((size_t)blockIdx.x * DD_DETAIL_CALLS + call) * 8;
+    const bool ok = consume_task_tc<KIND>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err, det);
+    if (threadIdx.x == 0) g_dd_call = call + 1;
+    return ok;
   } else {
     return consume_task<KIND == 0 ? 1 : 2, NT>(m.rg, c.t, units, K, m.xs, x_pitch, a.B, m.zero16, m.red, m.sums, epi,
                                                 a.err, xg, ldx);
@@ -1198,6 +1221,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
     }
     if (tid < 32) reinterpret_cast<uint32_t*>(m.zero16)[tid] = 0u;
     if (tid == 0) g_dd_int[28] = 0;                         // the consumers' "stopped early" flag
+    if (tid == 0) g_dd_call = 0;
     if (NT == 0 && warp == 0) tc_alloc(&g_dd_tmem, 64);   // 4 accumulator chains x 16 columns
   }
   if (NT == 0) tc_before();

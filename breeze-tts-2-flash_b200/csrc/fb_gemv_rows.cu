@@ -236,11 +236,11 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
       tc_after();
       if (lane == 0 && t == 0) GR_STAMP(2, globaltimer());
       if (lane == 0) {
-        const uint32_t xa = smem_u32(smem + (size_t)s * SB);
-        const uint32_t wa = xa + GR_XB;
+        const uint64_t xd = tc_desc_sw128(smem_u32(smem + (size_t)s * SB));
+        const uint64_t wd = xd + (uint64_t)(GR_XB / 16);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          tc_mma(tmem, tc_desc_sw128(xa + j * 32), tc_desc_sw128(wa + j * 32), (t > 0 || j > 0) ? 1u : 0u, IDESC);
+          tc_mma(tmem, xd + (uint64_t)(j << 1), wd + (uint64_t)(j << 1), (t > 0 || j > 0) ? 1u : 0u, IDESC);
         tc_commit(&empty[s]);
         if (t == nkc - 1) tc_commit(dfull);
       }

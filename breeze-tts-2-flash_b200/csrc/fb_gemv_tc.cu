@@ -263,19 +263,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemv_tc_kernel(const __grid_con
         tc_after();
         if (lane == 0 && t == 0) TC_STAMP(2);
         if (lane == 0) {
-          const uint32_t wa = smem_u32(wring + (size_t)s * TC_WBYTES);
-          const uint32_t xa = smem_u32(xring + (size_t)s * XB);
+          // descriptors as base + offset in 16-byte units (one add per MMA)
+          const uint64_t wd = tc_desc_sw128(smem_u32(wring + (size_t)s * TC_WBYTES));
+          const uint64_t xd = tc_desc_sw128(smem_u32(xring + (size_t)s * XB));
 #pragma unroll
           for (int j = 0; j < TC_C / 16; ++j) {
-            const uint64_t bd = tc_desc_sw128(xa + (j >> 2) * (MT * 128) + (j & 3) * 32);
+            const uint64_t bd = xd + (uint64_t)((j >> 2) * (MT * 128 / 16) + ((j & 3) << 1));
             const uint32_t acc = (kc > 0 || j >= NCH) ? 1u : 0u;
             const uint32_t ch = (uint32_t)((j % NCH) * MT);
             if (EPI == 2) {
               // gate chains in columns [0, NCH MT), up chains in [NCH MT, 2 NCH MT)
-              tc_mma(td + ch, tc_desc_sw128(wa + (j & 3) * 32), bd, acc, IDESC);
-              tc_mma(td + NCH * MT + ch, tc_desc_sw128(wa + TC_BR * 128 + (j & 3) * 32), bd, acc, IDESC);
+              tc_mma(td + ch, wd + (uint64_t)((j & 3) << 1), bd, acc, IDESC);
+              tc_mma(td + NCH * MT + ch, wd + (uint64_t)(TC_BR * 128 / 16 + ((j & 3) << 1)), bd, acc, IDESC);
             } else {
-              tc_mma(td + ch, tc_desc_sw128(wa + (j >> 2) * (TC_BR * 128) + (j & 3) * 32), bd, acc, IDESC);
+              tc_mma(td + ch, wd + (uint64_t)((j >> 2) * (TC_BR * 128 / 16) + ((j & 3) << 1)), bd, acc, IDESC);
             }
           }
           tc_commit(&empty[s]);

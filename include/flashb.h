@@ -226,7 +226,10 @@ typedef struct {
   const void* head_t;  /* [n_decode, vocab, hidden] bf16 (codebook heads, transposed) */
   const void* cos_tab; /* [n_decode + 2, 128] bf16 */
   const void* sin_tab;
-  uint64_t* trace;     /* optional: [grid][n_decode][11 + 9 * layers] %globaltimer stamps per CTA (task ends, barriers) */
+  uint64_t* trace;     /* optional: [grid][n_decode][11 + 9 * layers] %globaltimer stamps per CTA (task ends, barriers),
+                          then (tcgen05 build, grids <= 32) [grid][64][8] per GEMV task of a CTA's first 64: entry,
+                          first stage in, last MMA issued, MMAs complete, accumulators dumped, epilogues done, end,
+                          blocks of the task */
   int grid;            /* CTAs of the launch, one per SM: 0 = every SM; fewer leave SMs to work on other streams */
   const void* layers_host; /* fb_dd_layer[layers] in host memory, the same pointers as layers_dev: the weight matrices'
                             * TMA tensor maps are built from it on the host (cached per matrix) */
