@@ -53,7 +53,7 @@ def args_():
                    help='streams per GPU (the job serves streams x N: weak scaling, one replica per GPU)')
     p.add_argument('--prompt', type=int, default=PROMPT)
     p.add_argument('--case', default='frame', choices=['frame', 'depth', 'backbone', 'prefill', 'config1', 'config2',
-                                                      'config3'])
+                                                      'config3', 'config5'])
     p.add_argument('--group', type=int, default=8, choices=[1, 2, 4, 8],
                    help='streams decoded together per launch (their GEMV rows share every weight read)')
     p.add_argument('--lanes', type=int, default=8,
@@ -452,11 +452,74 @@ def measure_config3(dev, iters=20, kvs=(256, 1024, 4096)):
                 'per step', launches=2 + 5 * bcfg.layers, **sweep)
 
 
+def prefill_forward_flops(bcfg, B, L, pads):
+    """Algorithmic FLOPs of one prefill forward: the seven GEMMs of every layer over B L tokens, the causal
+    attention over each row's live keys (QK^T and PV), the last-token fp32 lm_head."""
+    H, D, NH = bcfg.hidden, bcfg.head_dim, bcfg.heads
+    params = (NH * D + 2 * bcfg.kv_heads * D) * H + H * NH * D + 3 * bcfg.ffn * H
+    gemm = 2 * B * L * params
+    attn = 0
+    for p in pads:
+        n = L - p
+        attn += 2 * 2 * NH * D * (n * (n + 1) // 2)
+    return bcfg.layers * (gemm + attn) + 2 * B * bcfg.vocab * H
+
+
+def measure_prefill_forward(dev, iters=5, L=512, pads=(0, 37)):
+    """Config 5's prefill (``BackbonePrefillGraphCache._forward``: B 2, L 512, the 28-layer backbone writing its
+    StaticCache, last-token logits) on flashb's kernels, captured in one CUDA graph as the reference captures it."""
+    import torch
+    from flashb import prefill as fpf
+    from flashb.engine import BackboneConfig, SyntheticBackboneGraph
+    pk = peaks()
+    bcfg = BackboneConfig()
+    B, S = 2, 1024
+    bb = SyntheticBackboneGraph(bcfg, batch_size=B, max_seq_len=S, device=dev, seed=2)
+    gen = torch.Generator().manual_seed(9)
+    emb = (torch.randn(B, L, bcfg.hidden, generator=gen)).to(torch.bfloat16)
+    am = torch.ones(B, L, dtype=torch.long)
+    for b, p in enumerate(pads):
+        am[b, :p] = 0
+        emb[b, :p] = 0
+    pos = am.cumsum(-1) - 1
+    pos.masked_fill_(am == 0, 1)
+    qi, ki = torch.arange(L).view(1, L, 1), torch.arange(S).view(1, 1, S)
+    valid = torch.zeros(B, S, dtype=torch.bool)
+    valid[:, :L] = am.bool()
+    mask = torch.full((B, 1, L, S), torch.finfo(torch.bfloat16).min, dtype=torch.bfloat16)
+    mask[:, 0].masked_fill_((ki <= qi) & valid[:, None, :], 0.0)
+    e, m, p_, c = emb.to(dev), mask.to(dev), pos.to(dev), torch.arange(L, device=dev)
+    st = bb._bb_state
+    kv = [(Lc.keys, Lc.values) for Lc in bb.static_cache.layers]
+    hid = torch.empty(B, L, bcfg.hidden, dtype=torch.bfloat16, device=dev)
+    lg = torch.empty(B, st['lm_head32'].shape[0], dtype=torch.float32, device=dev)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            fpf.prefill_forward(st, e, m, p_, c, kv, hidden_out=hid, logits_out=lg)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            fpf.prefill_forward(st, e, m, p_, c, kv, hidden_out=hid, logits_out=lg)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    ms = _time_calls(lambda i: graph.replay(), iters, dev, warmup=2)
+    flops = prefill_forward_flops(bcfg, B, L, pads)
+    ach = flops / (ms / 1e3) / 1e12
+    peak = pk.get('bf16_tflops', 1590.0)
+    del graph, bb, st, kv
+    torch.cuda.empty_cache()
+    return dict(shape=f'B {B}, L {L} (pads {list(pads)}), 28 layers, hidden 2048, 16 q / 4 KV heads, FFN 6144, '
+                f'cache {S}', ms=round(ms, 4), algorithmic_flops=int(flops), achieved=round(ach, 2), unit='TFLOP/s',
+                bound='tensor', peak=peak, frac=round(ach / peak, 4),
+                launches=2 + 9 * bcfg.layers, timing='one CUDA graph of the whole forward, replayed')
+
+
 def measure_per_config(dev):
     """BASELINE configs 1-3 at their own shapes, each on the kernels behind its reference entry point, inputs
-    resident and larger than L2 between calls.  Returns the bench line's ``per_config`` object."""
+    resident and larger than L2 between calls, and config 5's whole prefill forward.  Returns the bench line's
+    ``per_config`` object."""
     return dict(config1_attn_decode=measure_config1(dev), config2_gemv_pair=measure_config2(dev),
-                config3_backbone_step=measure_config3(dev))
+                config3_backbone_step=measure_config3(dev), config5_prefill_forward=measure_prefill_forward(dev))
 
 
 # ------------------------------------------------------------------------------------------------ GPU
@@ -488,6 +551,18 @@ def main():
                                   scaling='weak', vs_baseline=None, dtype='bf16', data='synthetic',
                                   config=dict(workload=a.case), roofline=dict(bound='hbm', **head), detail=r)),
                   flush=True)
+        return
+    if a.case == 'config5':
+        # config 5's whole prefill forward alone (a profiling entry point)
+        r = measure_prefill_forward(dev, iters=a.steps)
+        if rank == 0:
+            print(json.dumps(dict(metric='prefill TFLOP/s', value=r['achieved'], unit='TFLOP/s', n_gpus=world,
+                                  steps=a.steps, warmup=a.warmup, ms_per_step=r['ms'], higher_is_better=True,
+                                  scaling='weak', vs_baseline=None, dtype='bf16', data='synthetic',
+                                  config=dict(workload='config5 prefill forward'),
+                                  roofline=dict(bound='tensor', achieved=r['achieved'], peak=r['peak'],
+                                                unit='TFLOP/s', frac=r['frac'], traffic=None),
+                                  gpu_launches=a.steps * r['launches'], detail=r)), flush=True)
         return
     if a.case == 'prefill':
         pf = measure_prefill(dev, world, rank, iters=a.steps, warmup=max(3, a.warmup))

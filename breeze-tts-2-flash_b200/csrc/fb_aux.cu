@@ -308,8 +308,8 @@ constexpr int LMR_THREADS = 256;
 constexpr int LMR_WP = LMR_KC + 4;         // fp32 row pitch of a W chunk (2-way bank spread of the 8 row pairs)
 constexpr int LMR_HP = LMR_KC + 8;         // bf16 row pitch of a hidden chunk
 
-__global__ void __launch_bounds__(LMR_THREADS) lm_head_rows_kernel(const bf16* __restrict__ hid, int B, int H,
-                                                                   const float* __restrict__ W, int V,
+__global__ void __launch_bounds__(LMR_THREADS) lm_head_rows_kernel(const bf16* __restrict__ hid, long ldh, int B,
+                                                                   int H, const float* __restrict__ W, int V,
                                                                    const float* __restrict__ gs, int block,
                                                                    float* __restrict__ logits,
                                                                    float* __restrict__ cfg) {
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(LMR_THREADS) lm_head_rows_kernel(const bf16* _
     for (int i = tid; i < B * (LMR_KC / 8); i += LMR_THREADS) {
       const int r = i / (LMR_KC / 8), u = i - r * (LMR_KC / 8);
       const int k = k0 + 8 * u;
-      if (k < H) cp_async16(&hs[buf][r][8 * u], hid + (size_t)r * H + k);
+      if (k < H) cp_async16(&hs[buf][r][8 * u], hid + (size_t)r * ldh + k);
     }
     cp_async_commit();
   };
@@ -382,6 +382,7 @@ __global__ void __launch_bounds__(LMR_THREADS) lm_head_rows_kernel(const bf16* _
       }
     }
   __syncthreads();
+  if (!cfg) return;
   // CFG of every block: one thread per (pair, vocab row of the tile)
   const float g = gs ? gs[0] : 1.0f;
   const int h = block >= 2 ? block / 2 : 1;
@@ -429,6 +430,28 @@ extern "C" int flashb_lm_head_cfg(const void* x, int B, int H, const void* norm_
                          (cudaStream_t)stream, args, true);
 }
 
+namespace {
+int lm_head_rows_launch(const bf16* hp, long ldh, int B, int H, const float* W32, int V, const float* gs, int block,
+                        float* logits, float* cfg_out, cudaStream_t st) {
+  void* args[] = {(void*)&hp, (void*)&ldh, (void*)&B, (void*)&H, (void*)&W32, (void*)&V, (void*)&gs, (void*)&block,
+                  (void*)&logits, (void*)&cfg_out};
+  const size_t smem = 2 * sizeof(float) * LMR_VT * LMR_WP + 2 * sizeof(bf16) * LMR_MAXB * LMR_HP;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(lm_head_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) {
+      fbh::set_msg("lm_head_rows: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return FB_ERR_CUDA;
+    }
+    attr_done[dev] = 1;
+  }
+  return fbh::launch_pdl((const void*)lm_head_rows_kernel, dim3((V + LMR_VT - 1) / LMR_VT), dim3(LMR_THREADS), smem, st,
+                         args, true);
+}
+}  // namespace
+
 // Final norm + lm_head + CFG for B rows in blocks of `block` rows (each laid out [cond.., uncond..]): the norm as the
 // standalone RMSNorm (hidden_out), then one pass of lm_head_rows_kernel over the fp32 lm_head for every row.
 extern "C" int flashb_lm_head_cfg_blocks(const void* x, int B, int H, const void* norm_w, float eps, const float* W32,
@@ -444,21 +467,18 @@ extern "C" int flashb_lm_head_cfg_blocks(const void* x, int B, int H, const void
                "lm_head_cfg_blocks: 16-byte aligned lm_head and hidden rows required");
   int rc = flashb_rmsnorm(x, H, B, H, norm_w, eps, hidden_out, H, stream);
   if (rc) return rc;
-  const bf16* hp = (const bf16*)hidden_out;
-  void* args[] = {(void*)&hp, (void*)&B, (void*)&H, (void*)&W32, (void*)&V, (void*)&gs, (void*)&block,
-                  (void*)&logits, (void*)&cfg_out};
-  const size_t smem = 2 * sizeof(float) * LMR_VT * LMR_WP + 2 * sizeof(bf16) * LMR_MAXB * LMR_HP;
-  static int attr_done[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(lm_head_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) {
-      fbh::set_msg("lm_head_cfg_blocks: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      return FB_ERR_CUDA;
-    }
-    attr_done[dev] = 1;
-  }
-  return fbh::launch_pdl((const void*)lm_head_rows_kernel, dim3((V + LMR_VT - 1) / LMR_VT), dim3(LMR_THREADS), smem,
-                         (cudaStream_t)stream, args, true);
+  return lm_head_rows_launch((const bf16*)hidden_out, H, B, H, W32, V, gs, block, logits, cfg_out,
+                             (cudaStream_t)stream);
+}
+
+// Plain fp32 lm_head of B already normalised rows at row stride ldh (the prefill's last tokens).
+extern "C" int flashb_lm_head_rows(const void* hidden, int64_t ldh, int B, int H, const float* W32, int V,
+                                   float* logits, void* stream) {
+  FB_CHECK_ARG(hidden && W32 && logits, "lm_head_rows: null pointer argument");
+  FB_CHECK_ARG(B >= 1 && B <= LMR_MAXB && H % 8 == 0 && V >= 1 && ldh >= H && ldh % 8 == 0,
+               "lm_head_rows: bad shape B=%d H=%d V=%d ldh=%lld", B, H, V, (long long)ldh);
+  FB_CHECK_ARG(((uintptr_t)W32 & 15) == 0 && ((uintptr_t)hidden & 15) == 0 && H % 4 == 0,
+               "lm_head_rows: 16-byte aligned lm_head and hidden rows required");
+  return lm_head_rows_launch((const bf16*)hidden, (long)ldh, B, H, W32, V, nullptr, 1, logits, nullptr,
+                             (cudaStream_t)stream);
 }

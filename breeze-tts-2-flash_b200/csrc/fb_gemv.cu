@@ -25,6 +25,7 @@ thread_local int t_gemv_path = -1;
 int g_rows_path = 1;   // the many-rows kernel (fb_gemv_rows.cu) for 17..128 rows without norm; 0: off
 
 constexpr int GV_CWARPS = 8;
+constexpr int GV_MAX_ROWS = 1 << 20;   // activation rows of one call (a prefill: batch x prompt tokens)
 constexpr int GV_THREADS = (GV_CWARPS + 1) * 32;
 constexpr int GV_STAGE_BYTES = 32768;
 constexpr int GV_MAX_STAGES = 12;
@@ -271,6 +272,25 @@ int launch_gemv_t(GemvArgs& a, cudaStream_t st) {
 template <int EPI, bool NORM>
 int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
   a.M = M;
+  if (M > 128) {
+    // the prefill's dense GEMMs: the many-rows kernel in tiles of 128 rows, else blocks of 128 rows
+    if (a.K % 64 == 0 && !NORM && g_rows_path) {
+      const int rt = gemv_rows(a, EPI, st);
+      if (rt != FB_ERR_UNSUPPORTED) {
+        t_gemv_path = 3;
+        return rt;
+      }
+    }
+    for (int r0 = 0; r0 < M; r0 += 128) {
+      GemvArgs b = a;
+      b.x += (size_t)r0 * a.ldx;
+      b.y += (size_t)r0 * a.ldy;
+      if (b.res) b.res += (size_t)r0 * a.ldr;
+      const int rc = dispatch_m<EPI, NORM>(b, M - r0 < 128 ? M - r0 : 128, st);
+      if (rc) return rc;
+    }
+    return FB_OK;
+  }
   if (M > 16) {
     // up to 128 rows: the tcgen05 kernel (MMA N = the rows); else row blocks through the paths below (16 rows, or
     // 8 / 4 / 2 / 1 for K % 64 != 0), each block streaming the weights again
@@ -335,7 +355,7 @@ int dispatch_m(GemvArgs& a, int M, cudaStream_t st) {
 
 int common_checks(const void* x, int64_t ldx, int M, int K, const void* y, int64_t ldy) {
   FB_CHECK_ARG(x && y, "gemv: null x or y");
-  FB_CHECK_ARG(M >= 1 && M <= 128, "gemv: M=%d out of range 1..128", M);
+  FB_CHECK_ARG(M >= 1 && M <= GV_MAX_ROWS, "gemv: M=%d out of range 1..%d", M, GV_MAX_ROWS);
   FB_CHECK_ARG(K > 0 && K % 8 == 0, "gemv: K=%d must be a positive multiple of 8", K);
   FB_CHECK_ARG(ldx % 8 == 0 && ldy >= 1 && al16(x), "gemv: x row stride %lld must be a multiple of 8 and x 16B aligned",
                (long long)ldx);

@@ -1,5 +1,5 @@
-// flashb: the GEMV of many activation rows (17 .. 128, the shared backbone step of many streams) on the
-// 5th-generation tensor cores.  Same semantics as the other GEMV kernels (fb_gemv.cu), without the RMSNorm (the
+// flashb: the GEMV of many activation rows (17 .. 128 for the shared backbone step of many streams; any number in
+// tiles of 128 rows for the prefill's dense GEMMs) on the 5th-generation tensor cores.  Same semantics as the other GEMV kernels (fb_gemv.cu), without the RMSNorm (the
 // caller normalises the rows first, flashb_rmsnorm):
 //   y[m, n] = sum_k x[m, k] W[n, k] (fp32),  EPI 0: bf16(acc)   EPI 1: bf16(res + bf16(acc))
 //   EPI 2: bf16(bf16(silu(bf16(acc_gate))) * bf16(acc_up)).
@@ -11,9 +11,9 @@
 // column = unit) gives each epilogue thread 16 consecutive units of one row per TMEM load: 32-byte row segments
 // written straight to y, a residual read the same way, and the gate and up sums of a unit in the same thread.
 //
-// A tile is 128 output units (EPI 2: 128 gate + 128 up units) over the whole K.  There are few tiles (16 for a
-// 2048-row matrix), so K is split over a thread-block cluster of S CTAs (S <= 8): rank r takes the r-th of S ranges
-// of 64-column chunks.  S is chosen on the host from the occupancy API so that every cluster of the launch is
+// A tile is 128 output units (EPI 2: 128 gate + 128 up units) over the whole K, for 128 activation rows (row tile
+// blockIdx.y when there are more).  A decode step has few tiles (16 for a 2048-row matrix), so K is split over a
+// thread-block cluster of S CTAs (S <= 8): rank r takes the r-th of S ranges of 64-column chunks.  S is chosen on the host from the occupancy API so that every cluster of the launch is
 // resident at once and the most SMs stream.  Per CTA:
 //   * warp 0 (one lane) streams the K range through a ring of stages [x 128 rows x 64 columns | W BN rows x 64
 //     columns] with TMA tensor copies in the K-major 128-byte-swizzle layout.  The weight copies of the first ring's
@@ -74,7 +74,7 @@ struct alignas(64) RowsArgs {
 // committed, accumulators complete, split-K exchange done, exit (ns), SM id.
 #define GR_STAMP(i, v)                                                                  \
   do {                                                                                  \
-    if (a.trace) a.trace[blockIdx.x * 16 + (i)] = (unsigned long long)(v);              \
+    if (a.trace) a.trace[(blockIdx.y * gridDim.x + blockIdx.x) * 16 + (i)] = (unsigned long long)(v); \
   } while (0)
 
 __device__ __forceinline__ void cl_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) GR_STAMP(0, globaltimer());
   const int rank = (int)(blockIdx.x % S), tile = (int)(blockIdx.x / S);
+  const int r0 = (int)blockIdx.y * 128;      // first activation row of this row tile
   const int nkc_all = a.K / 64;
   const int kc0 = nkc_all * rank / S;
   const int nkc = nkc_all * (rank + 1) / S - kc0;
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
       }
     };
     auto issue_x = [&](int t) {
-      tma_load_3d_plain(smem + (size_t)(t % NST) * SB, &a.tx, 0, 0, kc0 + t, &full[t % NST]);
+      tma_load_3d_plain(smem + (size_t)(t % NST) * SB, &a.tx, 0, r0, kc0 + t, &full[t % NST]);
     };
     if (lane < 4) tma_prefetch_map(lane < 3 ? (const void*)&a.tw[lane] : (const void*)&a.tx);
     const int pre = min(nkc, NST);
@@ -255,7 +256,7 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
   const bool epi = warp >= 2;
   const int q = warp & 3;                    // TMEM lane quarter
   const int eh = (warp - 2) >> 2;            // 0 / 1: which of the quarter's two warps
-  const int row = q * 32 + lane;             // the accumulator row (activation row) of this thread
+  const int row = q * 32 + lane;             // the accumulator row of this thread (activation row r0 + row)
   const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
   if (epi) {
     pdl_wait();                              // res / y belong to earlier kernels of the stream
@@ -307,12 +308,13 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
     const int ga = S > 1 ? g0 : 0, gb = S > 1 ? g1 : GR_GROUPS;
     for (int g = ga + eh; g < gb; g += 2) {
       const int n0 = tile * GR_BN + g * 16;
-      const bool live = row < a.M && n0 < a.N;
-      uint4 r0 = make_uint4(0u, 0u, 0u, 0u), r1 = r0;
+      const int m = r0 + row;
+      const bool live = m < a.M && n0 < a.N;
+      uint4 rr0 = make_uint4(0u, 0u, 0u, 0u), rr1 = rr0;
       if (EPI == 1 && live) {                // the residual first: its latency overlaps the reads below
-        const uint4* rp = reinterpret_cast<const uint4*>(a.res + (size_t)row * a.ldr + n0);
-        r0 = rp[0];
-        r1 = rp[1];
+        const uint4* rp = reinterpret_cast<const uint4*>(a.res + (size_t)m * a.ldr + n0);
+        rr0 = rp[0];
+        rr1 = rp[1];
       }
       float v[16], u[16];
       if (EPI == 2) {
@@ -333,7 +335,7 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
           }
         }
       }
-      if (live) gr_store<EPI>(a, row, n0, v, u, r0, r1);
+      if (live) gr_store<EPI>(a, m, n0, v, u, rr0, rr1);
     }
     if (tid == 64) GR_STAMP(10, globaltimer());
   }
@@ -422,6 +424,7 @@ template <int EPI>
 int launch_rows(const GemvArgs& g, cudaStream_t st) {
   const int N = g.N, K = g.K;
   const int tiles = (N + GR_BN - 1) / GR_BN;
+  const int rtiles = (g.M + 127) / 128;      // row tiles (blockIdx.y)
   const int nkc = K / 64;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -440,12 +443,12 @@ int launch_rows(const GemvArgs& g, cudaStream_t st) {
   int best = 1, best_ctas = 0;
   for (int S = 1; S <= GR_MAX_SPLIT; ++S) {
     if (S > 1 && nkc / S < 2) break;              // at least two chunks per CTA
-    if (tiles * S > sms) break;
+    if (S > 1 && tiles * rtiles * S > sms) break; // enough tiles already: no split
     const int nst = rows_stages<EPI>((nkc + S - 1) / S);
     const size_t smem = rows_smem<EPI>(nst, S, rows_pitch<EPI>(S));
     if (smem > 227 * 1024) continue;
     const int fit = rows_occupancy<EPI>(dev, S, smem, tiles);
-    if (fit < tiles) continue;
+    if (S > 1 && fit < tiles * rtiles) continue;
     if (tiles * S > best_ctas) {
       best = S;
       best_ctas = tiles * S;
@@ -470,16 +473,17 @@ int launch_rows(const GemvArgs& g, cudaStream_t st) {
   const size_t smem = rows_smem<EPI>(a.nst, S, a.pitch);
   void* args[] = {(void*)&a};
   t_rows_split = S;
-  return fbh::launch_pdl((const void*)gemv_rows_kernel<EPI>, dim3(tiles * S), dim3(GR_THREADS), smem, st, args, true,
-                         S > 1 ? S : 0);
+  return fbh::launch_pdl((const void*)gemv_rows_kernel<EPI>, dim3(tiles * S, rtiles), dim3(GR_THREADS), smem, st, args,
+                         true, S > 1 ? S : 0);
 }
 
 }  // namespace
 
-// The many-rows tensor-core GEMV when it applies: 17 <= M <= 128, no RMSNorm, K % 64 == 0, segment boundaries
-// (EPI 0/1) at multiples of 128 rows, N % 16 == 0, y / res rows 16-byte aligned.  Else FB_ERR_UNSUPPORTED.
+// The many-rows tensor-core GEMV when it applies: M >= 17 (tiles of 128 rows), no RMSNorm, K % 64 == 0, segment
+// boundaries (EPI 0/1) at multiples of 128 rows, N % 16 == 0, y / res rows 16-byte aligned.  Else
+// FB_ERR_UNSUPPORTED.
 int gemv_rows(GemvArgs& g, int epi, cudaStream_t st) {
-  if (g.M < 17 || g.M > 128 || g.K % 64 != 0 || g.K < 128 || g.N % 16 != 0) return FB_ERR_UNSUPPORTED;
+  if (g.M < 17 || g.M > 65535 * 128 || g.K % 64 != 0 || g.K < 128 || g.N % 16 != 0) return FB_ERR_UNSUPPORTED;
   const int n2 = g.N - g.N0 - g.N1;
   if (epi != 2 && (((g.N1 || n2) && g.N0 % GR_BN) || (n2 && (g.N0 + g.N1) % GR_BN))) return FB_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(g.y) & 15) || g.ldy % 8) return FB_ERR_UNSUPPORTED;

@@ -23,6 +23,7 @@
 //     outputs never reach a live row; the oracle uses the same convention).
 // With `causal` the key tiles entirely above the diagonal are skipped: the mask gives them probability exactly 0.
 #include "fb_common.cuh"
+#include "fb_norm.cuh"
 
 namespace fb {
 
@@ -427,4 +428,87 @@ extern "C" int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, in
     return FB_ERR_CUDA;
   }
   return FB_OK;
+}
+
+
+// ------------------------------------------------------------------------------------------------ prefill q|k|v tail
+// The attention's projection tail for every prompt token, as transformers Qwen3Attention.forward runs it inside the
+// reference prefill (BackbonePrefillGraphCache._forward, UP/models/cudagraph/backbone_prefill_graph.py:95-112):
+// q = RoPE(q_norm(q)), k = RoPE(k_norm(k)) at the token's position, then the StaticCache update at cache_position
+// (keys[:, :, cache_position] = k, values likewise).  One warp per (token, head) of the q|k|v GEMM output, in the
+// rotary-pair view of fb_norm.cuh: q heads are rewritten in place (the attention reads them there), k heads go to
+// the key cache, v heads are copied to the value cache.  Positions outside the rotary tables and cache slots outside
+// the cache are skipped (the host checks the shapes; the device never writes out of bounds).
+namespace fb {
+
+struct PQArgs {
+  bf16* qkv;
+  long ldq;
+  int B, L, NH, NKV;
+  const bf16 *qn_w, *kn_w;
+  float eps;
+  const bf16 *cos_tab, *sin_tab;
+  int P;
+  const long long *pos, *slot;
+  bf16 *kc, *vc;
+  long c_sb, c_sh;
+  int S;
+};
+
+__global__ void __launch_bounds__(256) prefill_qkv_kernel(const PQArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int HH = a.NH + 2 * a.NKV;
+  const long w = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (w >= (long)a.B * a.L * HH) return;
+  const int t = (int)(w / HH), h = (int)(w - (long)t * HH);
+  const int b = t / a.L, l = t - b * a.L;
+  bf16* x = a.qkv + (size_t)t * a.ldq + (size_t)h * 128;
+  const long long slot = a.slot[l];
+  if (h >= a.NH + a.NKV) {                                 // v head: copy to the value cache
+    if (slot < 0 || slot >= a.S) return;
+    const int j = h - a.NH - a.NKV;
+    bf16* dst = a.vc + (size_t)b * a.c_sb + (size_t)j * a.c_sh + (size_t)slot * 128;
+    reinterpret_cast<uint2*>(dst)[lane] = reinterpret_cast<const uint2*>(x)[lane];
+    return;
+  }
+  const long long p = a.pos[(size_t)b * a.L + l];
+  if (p < 0 || p >= a.P) return;
+  const bool is_q = h < a.NH;
+  const HeadPair wv = head_load(is_q ? a.qn_w : a.kn_w, lane);
+  const HeadPair cs = head_load(a.cos_tab + (size_t)p * 128, lane);
+  const HeadPair sn = head_load(a.sin_tab + (size_t)p * 128, lane);
+  const HeadPair y = head_norm_rope(x, wv, cs, sn, a.eps, lane);
+  if (is_q) {
+    head_store(x, y, lane);
+  } else if (slot >= 0 && slot < a.S) {
+    head_store(a.kc + (size_t)b * a.c_sb + (size_t)(h - a.NH) * a.c_sh + (size_t)slot * 128, y, lane);
+  }
+}
+
+}  // namespace fb
+
+extern "C" int flashb_prefill_qkv(void* qkv, int64_t ldq, int B, int L, int NH, int NKV, const void* qn_w,
+                                  const void* kn_w, float eps, const void* cos_tab, const void* sin_tab, int P,
+                                  const int64_t* position_ids, const int64_t* cache_position, void* kc, void* vc,
+                                  int64_t c_sb, int64_t c_sh, int S, void* stream) {
+  FB_CHECK_ARG(qkv && qn_w && kn_w && cos_tab && sin_tab && position_ids && cache_position && kc && vc,
+               "prefill_qkv: null pointer argument");
+  FB_CHECK_ARG(B >= 1 && L >= 1 && NH >= 1 && NKV >= 1 && NH % NKV == 0 && P >= 1 && S >= 1,
+               "prefill_qkv: bad shape B=%d L=%d NH=%d NKV=%d P=%d S=%d", B, L, NH, NKV, P, S);
+  FB_CHECK_ARG(ldq >= (int64_t)(NH + 2 * NKV) * 128 && ldq % 8 == 0 && c_sh >= (int64_t)S * 128 &&
+                   c_sb >= (int64_t)NKV * c_sh && ((uintptr_t)qkv & 15) == 0 && ((uintptr_t)kc & 15) == 0 &&
+                   ((uintptr_t)vc & 15) == 0,
+               "prefill_qkv: bad strides or alignment");
+  fb::PQArgs a{};
+  a.qkv = (bf16*)qkv; a.ldq = (long)ldq; a.B = B; a.L = L; a.NH = NH; a.NKV = NKV;
+  a.qn_w = (const bf16*)qn_w; a.kn_w = (const bf16*)kn_w; a.eps = eps;
+  a.cos_tab = (const bf16*)cos_tab; a.sin_tab = (const bf16*)sin_tab; a.P = P;
+  a.pos = (const long long*)position_ids; a.slot = (const long long*)cache_position;
+  a.kc = (bf16*)kc; a.vc = (bf16*)vc; a.c_sb = (long)c_sb; a.c_sh = (long)c_sh; a.S = S;
+  const long warps = (long)B * L * (NH + 2 * NKV);
+  void* args[] = {(void*)&a};
+  return fbh::launch_pdl((const void*)fb::prefill_qkv_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0,
+                         (cudaStream_t)stream, args, true);
 }

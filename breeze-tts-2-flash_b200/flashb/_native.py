@@ -60,6 +60,8 @@ _PROTOS = {
     'flashb_frame_ids': (I, [P, P, I, I, I, P, P]),
     'flashb_prefill_attn': (I, [P, L, L, L, P, L, L, L, P, L, L, L, P, I, L, L, I, I, I, I, I, I, F, I, I, I, P, L, L,
                                 L, P]),
+    'flashb_prefill_qkv': (I, [P, L, I, I, I, I, P, P, F, P, P, I, P, P, P, P, L, L, I, P]),
+    'flashb_lm_head_rows': (I, [P, L, I, I, P, I, P, P]),
     'flashb_dd_scratch_bytes': (L, [P]),
     'flashb_dd_layer_bytes': (L, []),
     'flashb_dd_barrier_offset': (L, [P]),

@@ -188,6 +188,40 @@ class FusedOps:
         check(_native.lib().flashb_lm_head_cfg(_p(x), B, H, _p(norm_w), float(eps), _p(W32), V, _p(gs),
                                                _p(hidden_out), _p(logits), _p(cfg_out), _stream(x)))
 
+    def lm_head_rows(self, hidden, W32, logits):
+        """logits [B, V] fp32 = W32 [V, H] . hidden[b] for normalised bf16 rows (any row stride, unit inner stride):
+        the prefill's last-token logits (``UP/models/cudagraph/backbone_prefill_graph.py:111``)."""
+        _bf16(hidden, 'hidden')
+        B, H = hidden.shape
+        _req(hidden.stride(1) == 1 and hidden.stride(0) % 8 == 0, 'hidden layout')
+        _req(W32.dtype == torch.float32 and W32.is_contiguous() and W32.shape[1] == H, 'W32 [V, H] fp32')
+        V = W32.shape[0]
+        _req(logits.dtype == torch.float32 and logits.is_contiguous() and tuple(logits.shape) == (B, V), 'logits')
+        check(_native.lib().flashb_lm_head_rows(_p(hidden), hidden.stride(0), B, H, _p(W32), V, _p(logits),
+                                                _stream(hidden)))
+
+    def prefill_qkv(self, qkv, B, L, NH, NKV, qn_w, kn_w, eps, cos_tab, sin_tab, position_ids, cache_position, kc,
+                    vc):
+        """The prefill's q|k|v tail in place (``flashb_prefill_qkv``): qkv [B L, (NH + 2 NKV) 128] bf16; q heads
+        rewritten, k / v heads written to the caches kc / vc [B, NKV, S, 128] at cache_position."""
+        _bf16(qkv, 'qkv')
+        _req(qkv.dim() == 2 and qkv.shape[0] == B * L and qkv.shape[1] >= (NH + 2 * NKV) * 128 and qkv.stride(1) == 1,
+             'qkv [B L, (NH + 2 NKV) 128]')
+        for t, n in ((kc, 'kc'), (vc, 'vc')):
+            _bf16(t, n)
+            _req(t.dim() == 4 and t.shape[0] == B and t.shape[1] == NKV and t.shape[3] == 128 and t.stride(3) == 1
+                 and t.stride(2) == 128, f'{n} [B, NKV, S, 128] with rows of 128')
+        _req(kc.stride() == vc.stride() and kc.shape == vc.shape, 'kc / vc layouts differ')
+        _req(position_ids.dtype == torch.int64 and position_ids.is_contiguous() and position_ids.numel() == B * L,
+             'position_ids int64 [B, L]')
+        _req(cache_position.dtype == torch.int64 and cache_position.is_contiguous() and cache_position.numel() == L,
+             'cache_position int64 [L]')
+        _req(cos_tab.shape == sin_tab.shape and cos_tab.shape[-1] == 128 and cos_tab.is_contiguous(), 'rope tables')
+        check(_native.lib().flashb_prefill_qkv(_p(qkv), qkv.stride(0), B, L, NH, NKV, _p(qn_w), _p(kn_w), float(eps),
+                                               _p(cos_tab), _p(sin_tab), cos_tab.shape[0], _p(position_ids),
+                                               _p(cache_position), _p(kc), _p(vc), kc.stride(0), kc.stride(1),
+                                               kc.shape[2], _stream(qkv)))
+
     def lm_head_cfg_blocks(self, x, norm_w, eps, W32, gs, block, hidden_out, logits, cfg_out):
         """lm_head_cfg for B rows in CFG blocks of ``block`` rows (each [cond..., uncond...]), one pass over the
         fp32 lm_head for every row; cfg_out rows: block b's pairs at [b * block / 2, (b + 1) * block / 2)."""

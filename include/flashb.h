@@ -108,7 +108,7 @@ int flashb_attn_decode_fused(const void* qkv, int64_t qkv_sb, const void* qn_w, 
 
 /* ---------------------------------------------------------------------------------------------- fused GEMVs
  * y[m, n] = sum_k xin[m, k] * W[n, k], nn.Linear layout (W [N, K] bf16 row-major contiguous), fp32 accumulation,
- * M = 1..128 rows (the reference: 1..8; x row stride ldx, y row stride ldy, both multiples of 8 elements),
+ * M = 1..2^20 rows (the reference: 1..8; more than 128 rows -- the prefill's dense GEMMs -- run in tiles of 128; x row stride ldx, y row stride ldy, both multiples of 8 elements),
  * K % 8 == 0.  All pointers 16-byte aligned.  More than 16 rows run on the tcgen05 kernel (K % 64 == 0), which then
  * streams the weights once for all rows; otherwise in row blocks (16 rows, or 8 / 4 / 2 / 1 when K % 64 != 0). */
 /* Replaces gemv_seg (flash/csrc/bb_fused.cu:293-316): y[:, 0:N0+N1+N2] = norm?(x) @ [W0; W1; W2]^T, where norm is
@@ -200,6 +200,22 @@ int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl,
                         const void* mask, int mask_is_bf16, int64_t m_sb, int64_t m_sl, int B, int NH, int NKV, int L,
                         int S, int D, float scaling, int causal, int h0, int h1, void* out, int64_t o_sb,
                         int64_t o_sl, int64_t o_sh, void* stream);
+
+/* The prefill's q|k|v tail for every prompt token (replaces, with flashb_prefill_attn and the GEMV entry points, the
+ * eager layers of BackbonePrefillGraphCache._forward, UP/models/cudagraph/backbone_prefill_graph.py:95-112):
+ * qkv [B L, (NH + 2 NKV) 128] bf16 raw projections (row stride ldq; token t = b L + l): q heads rewritten in place
+ * as RoPE(q_norm(q)), k heads as RoPE(k_norm(k)) written to kc[b, j, cache_position[l], :], v heads copied to
+ * vc[b, j, cache_position[l], :] (kc / vc [B, NKV, S, 128] bf16, batch / head strides c_sb / c_sh elements).  RoPE
+ * rows cos_tab / sin_tab [P, 128] bf16 at position_ids[b, l] (int64 [B, L]); cache_position int64 [L].  Tokens
+ * whose position or slot is out of range are skipped. */
+int flashb_prefill_qkv(void* qkv, int64_t ldq, int B, int L, int NH, int NKV, const void* qn_w, const void* kn_w,
+                       float eps, const void* cos_tab, const void* sin_tab, int P, const int64_t* position_ids,
+                       const int64_t* cache_position, void* kc, void* vc, int64_t c_sb, int64_t c_sh, int S,
+                       void* stream);
+/* The prefill's logits (backbone_prefill_graph.py:111): logits [B, V] fp32 = W32 [V, H] fp32 . hidden[b] for B <= 128
+ * already normalised bf16 rows at row stride ldh (the last token of each prompt). */
+int flashb_lm_head_rows(const void* hidden, int64_t ldh, int B, int H, const float* W32, int V, float* logits,
+                        void* stream);
 
 /* ---------------------------------------------------------------------------------------------- depth frame
  * Replaces the reference's depth frame megakernel dd2_init / dd2_frame (flash/csrc/depth_frame.cu:758-853, 923-934),

@@ -454,6 +454,41 @@ def gold_prefill(out):
     out['prefill'] = dict(out=synth.np_bits(o), digest=synth.digest(q, k, v, mask))
 
 
+def gold_prefill_forward(out):
+    """The reference's own prefill forward (``BackbonePrefillGraphCache._forward``, official modules in bf16 on the
+    CPU) on the BACKBONE weights: hidden states, last-token logits and the cache slots it wrote."""
+    from models.cudagraph.backbone_prefill_graph import BackbonePrefillGraphCache
+    c = synth.BACKBONE
+    w = synth.backbone_weights()
+    g = _official_backbone(c, w, torch.bfloat16)
+    pf = object.__new__(BackbonePrefillGraphCache)       # the constructor asks for a CUDA graph pool
+    pf.backbone_graph, pf.model, pf.lm_head = g, g.model, g.lm_head
+    emb, mask, pos, cp = synth.prefill_forward_inputs()
+    # the reference's own mask builder gives the same mask
+    am = (pos >= 0) & torch.ones_like(pos, dtype=torch.bool)
+    for b, pad in enumerate(synth.PREFILL_FWD['pads']):
+        am[b, :pad] = False
+    chk = torch.empty_like(mask)
+    BackbonePrefillGraphCache._update_causal_mask(am.long(), chk)
+    assert torch.equal(chk, mask), 'the test mask differs from the reference prefill mask'
+    L = emb.shape[1]
+    with torch.inference_mode():
+        for layer in g.static_cache.layers:
+            layer.keys.zero_()
+            layer.values.zero_()
+            # transformers 5.x StaticLayer.update writes at its own running length instead of the cache_position
+            # argument (4.57.3, which the reference pins, writes at cache_position = arange(L)): start it at 0
+            if hasattr(layer, 'cumulative_length'):
+                layer.cumulative_length.zero_()
+        h, lg = pf._forward(emb, mask, pos, cp)
+        ks = np.stack([synth.np_bits(layer.keys[:, :, :L]) for layer in g.static_cache.layers])
+        vs = np.stack([synth.np_bits(layer.values[:, :, :L]) for layer in g.static_cache.layers])
+        past = sum(float(layer.keys[:, :, L:].abs().sum()) for layer in g.static_cache.layers)
+    assert past == 0.0, 'the prefill wrote past its slots'
+    out['prefill_fwd'] = dict(hidden=synth.np_bits(h), logits=lg.numpy().copy(), keys=ks, values=vs,
+                              digest=synth.digest(emb, mask, pos, w['embed'], w['lm_head']))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--ref', default=os.environ.get('BREEZE_REF'),
@@ -467,7 +502,7 @@ def main():
     out = {}
     only = set(args.only.split(',')) if args.only else None
     for fn in (gold_attention, gold_attention1, gold_gemv, gold_gemv2, gold_backbone, gold_depth, gold_sampler,
-               gold_prefill, gold_drift, gold_depth_drift, gold_bb_sampler):
+               gold_prefill, gold_drift, gold_depth_drift, gold_bb_sampler, gold_prefill_forward):
         if only and fn.__name__[len('gold_'):] not in only:
             continue
         fn(out)

@@ -97,6 +97,31 @@ BACKBONE28 = dict(seed=106, B=2, H=2048, NH=16, NKV=4, D=128, F=6144, L=28, voca
                   S=1024, prefill=1023, pad=(0, 3), gs=4.0)
 
 
+# the whole prefill forward (BackbonePrefillGraphCache._forward) on the BACKBONE weights: 24 prompt tokens, row 1
+# left-padded by 5 (positions and causal mask as the reference prefill forms them)
+PREFILL_FWD = dict(seed=107, L=24, pads=(0, 5))
+
+
+def prefill_forward_inputs(c=BACKBONE, p=PREFILL_FWD):
+    """emb [B, L, H] bf16 (pad tokens zero), causal mask [B, 1, L, S] bf16 (finfo.min / 0), position_ids [B, L],
+    cache_position [L], as ``_copy_inputs`` / ``_update_causal_mask`` of the reference prefill build them."""
+    g = gen(p['seed'])
+    B, L, S, H = c['B'], p['L'], c['S'], c['H']
+    emb = randn_bf16(g, (B, L, H))
+    am = torch.ones(B, L, dtype=torch.long)
+    for b, pad in enumerate(p['pads']):
+        am[b, :pad] = 0
+        emb[b, :pad] = 0
+    pos = am.cumsum(-1) - 1
+    pos.masked_fill_(am == 0, 1)
+    qi, ki = torch.arange(L).view(1, L, 1), torch.arange(S).view(1, 1, S)
+    valid = torch.zeros(B, S, dtype=torch.bool)
+    valid[:, :L] = am.bool()
+    mask = torch.full((B, 1, L, S), torch.finfo(torch.bfloat16).min, dtype=torch.bfloat16)
+    mask[:, 0].masked_fill_((ki <= qi) & valid[:, None, :], 0.0)
+    return emb, mask, pos, torch.arange(L)
+
+
 def backbone_weights(c=BACKBONE):
     """Returns a dict of bf16 tensors (lm_head fp32, bf16-exact)."""
     g = gen(c['seed'])

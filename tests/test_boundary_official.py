@@ -176,3 +176,42 @@ def test_prefill_hook_through_the_official_forward(mg, monkeypatch):
         BackbonePrefillGraphCache._forward = saved
         if '_pf_installed' in BackbonePrefillGraphCache.__dict__:
             delattr(BackbonePrefillGraphCache, '_pf_installed')
+
+
+def test_whole_prefill_hook_on_the_official_cache(mg):
+    """flashb.prefill replaces ``BackbonePrefillGraphCache._forward``; on CPU tensors it hands the call to the
+    official forward (the flashb path needs the GPU), whose output is unchanged."""
+    import synth
+    from models.cudagraph.backbone_prefill_graph import BackbonePrefillGraphCache
+    from flashb import prefill as fpf
+    c = synth.BACKBONE
+    w = synth.backbone_weights()
+    g = mg._official_backbone(c, w, torch.bfloat16)
+    pf = object.__new__(BackbonePrefillGraphCache)
+    pf.backbone_graph, pf.model, pf.lm_head = g, g.model, g.lm_head
+    emb, mask, pos, cp = synth.prefill_forward_inputs()
+
+    def run():
+        with torch.inference_mode():
+            for layer in g.static_cache.layers:
+                layer.keys.zero_()
+                layer.values.zero_()
+                if hasattr(layer, 'cumulative_length'):
+                    layer.cumulative_length.zero_()
+            return pf._forward(emb, mask, pos, cp)
+
+    h_ref, lg_ref = run()
+    saved = BackbonePrefillGraphCache.__dict__['_forward']
+    fpf.install()
+    try:
+        assert BackbonePrefillGraphCache._forward is fpf.fused_prefill_forward
+        assert fpf.ORIG['_forward'] is saved
+        # the state the flashb path would use resolves to the official weights (the decode hook's reading)
+        from flashb import backbone as bb
+        Ls, norm, _, lm_w = bb.weights_of(g)
+        assert Ls[0].wq is g.model.layers[0].self_attn.q_proj.weight and lm_w is g.lm_head.weight
+        h, lg = run()
+        assert torch.equal(h, h_ref) and torch.equal(lg, lg_ref)
+    finally:
+        BackbonePrefillGraphCache._forward = saved
+        fpf.ORIG.pop('_forward', None)

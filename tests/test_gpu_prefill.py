@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import synth
-from gpu_util import TOL, assert_argmax_agree, assert_close, np32
+from gpu_util import E2E_TOL, TOL, assert_argmax_agree, assert_close, np32
 from oracle import prefill as opf
 from oracle.bf16 import bits_to_f32
 
@@ -117,3 +117,109 @@ def test_prefill_head_shard_and_determinism():
     torch.cuda.synchronize()
     assert torch.equal(full, again)
     assert torch.equal(part, full[:, :, h0:h1])
+
+
+# ------------------------------------------------------------------------------------------------ the whole prefill
+def _prefill_case(hidden, heads, kv_heads, ffn, layers, B, L, S, pads, seed):
+    """A synthetic backbone (flashb.engine) with its decode state, prompt embeddings, the reference prefill's
+    left-padding positions and causal mask (``BackbonePrefillGraphCache._copy_inputs`` / ``_update_causal_mask``)."""
+    from flashb.engine import BackboneConfig, SyntheticBackboneGraph
+    cfg = BackboneConfig(hidden=hidden, layers=layers, heads=heads, kv_heads=kv_heads, ffn=ffn)
+    g = SyntheticBackboneGraph(cfg, batch_size=B, max_seq_len=S, seed=seed)
+    for Lc in g.static_cache.layers:
+        Lc.keys.zero_()
+        Lc.values.zero_()
+    gen = torch.Generator().manual_seed(seed + 7)
+    emb = torch.randn(B, L, hidden, generator=gen).to(torch.bfloat16)
+    am = torch.ones(B, L, dtype=torch.long)
+    for b, p in enumerate(pads):
+        am[b, :p] = 0
+        emb[b, :p] = 0
+    pos = am.cumsum(-1) - 1
+    pos.masked_fill_(am == 0, 1)
+    qi, ki = torch.arange(L).view(1, L, 1), torch.arange(S).view(1, 1, S)
+    valid = torch.zeros(B, S, dtype=torch.bool)
+    valid[:, :L] = am.bool()
+    allowed = (ki <= qi) & valid[:, None, :]
+    mask = torch.full((B, 1, L, S), torch.finfo(torch.bfloat16).min, dtype=torch.bfloat16)
+    mask[:, 0].masked_fill_(allowed, 0.0)
+    return g, emb, mask, pos, torch.arange(L)
+
+
+def _run_prefill(g, emb, mask, pos, cp):
+    from flashb import prefill as fpf
+    st = g._bb_state
+    kv = [(Lc.keys, Lc.values) for Lc in g.static_cache.layers]
+    h, lg = fpf.prefill_forward(st, emb.cuda(), mask.cuda(), pos.cuda(), cp.cuda(), kv)
+    torch.cuda.synchronize()
+    return h, lg, kv
+
+
+def _oracle_prefill(g, emb, mask, pos, cp):
+    from oracle import decode as dec
+    st = g._bb_state
+    layers = [dict(ln1=np32(L.ln1_w), wq=np32(L.wq), wk=np32(L.wk), wv=np32(L.wv), qn=np32(L.qn_w), kn=np32(L.kn_w),
+                   wo=np32(L.wo), ln2=np32(L.ln2_w), wg=np32(L.wg), wu=np32(L.wu), wd=np32(L.wd))
+              for L in st['layers']]
+    W = dec.BackboneWeights(layers, np32(g.norm_w), np32(g.embed), g.lm_head32.cpu().numpy(), g.cfg.vocab, g.cfg.eps,
+                            g.cfg.theta)
+    kcs = [np32(Lc.keys).copy() for Lc in g.static_cache.layers]
+    vcs = [np32(Lc.values).copy() for Lc in g.static_cache.layers]
+    h, lg = opf.prefill_forward(W, np32(emb), np32(mask), pos.numpy(), cp.numpy(), kcs, vcs)
+    return h, lg, kcs, vcs
+
+
+@pytest.mark.parametrize('hidden,heads,kv_heads,ffn,L,S,pads', [
+    (512, 4, 2, 1024, 40, 96, [0, 7]),            # small: ragged tiles, left padding
+    (2048, 16, 4, 6144, 512, 1024, [0, 37]),      # config 5's shapes (B 2, L 512, 16 q / 4 KV heads), 2 layers
+])
+def test_prefill_forward_matches_oracle(hidden, heads, kv_heads, ffn, L, S, pads):
+    """The whole prefill (``BackbonePrefillGraphCache._forward``) on flashb kernels: hidden states of every live
+    token, the last-token logits and every layer's cache slots [0, L) against the oracle's eager restatement.
+    Layer 0's cache (one GEMM and the q|k|v tail) holds the kernel bar; the values after more layers hold the
+    end-to-end bar of the decode tests (rare 1-ulp bf16 flips from another summation order compound through the
+    layers, as the drift study of tests/golden/make_golden.py shows for the reference itself)."""
+    g, emb, mask, pos, cp = _prefill_case(hidden, heads, kv_heads, ffn, 2, 2, L, S, pads, seed=11)
+    h_ref, lg_ref, kcs, vcs = _oracle_prefill(g, emb, mask, pos, cp)
+    h, lg, kv = _run_prefill(g, emb, mask, pos, cp)
+    live = _live(2, L, pads)
+    assert_close(np32(h)[live], h_ref[live], tol=E2E_TOL, what='prefill hidden (live tokens)')
+    assert_close(lg.cpu().numpy(), lg_ref, what='prefill last-token logits')
+    assert_argmax_agree(lg.cpu().numpy(), lg_ref, what='prefill logits')
+    for li, (kc, vc) in enumerate(kv):
+        kk, vv = np32(kc)[:, :, :L], np32(vc)[:, :, :L]
+        for b, p in enumerate(pads):
+            tol = TOL if li == 0 else E2E_TOL
+            assert_close(kk[b, :, p:], kcs[li][b, :, p:L], tol=tol, what=f'layer {li} keys row {b}')
+            assert_close(vv[b, :, p:], vcs[li][b, :, p:L], tol=tol, what=f'layer {li} values row {b}')
+        assert float(kc[:, :, L:].abs().sum()) == 0.0, 'the prefill wrote past its slots'
+    from flashb._native import device_error
+    assert device_error() == 0
+
+
+def test_prefill_forward_graph_capture_and_determinism():
+    """Captured in a CUDA graph (as the reference captures ``_forward`` per length bucket) and replayed: the same
+    bits as an eager call."""
+    g, emb, mask, pos, cp = _prefill_case(512, 4, 2, 1024, 2, 2, 64, 128, [0, 3], seed=12)
+    h0, lg0, _ = _run_prefill(g, emb, mask, pos, cp)
+    h0, lg0 = h0.clone(), lg0.clone()
+    from flashb import prefill as fpf
+    st = g._bb_state
+    kv = [(Lc.keys, Lc.values) for Lc in g.static_cache.layers]
+    e, m, p, c = emb.cuda(), mask.cuda(), pos.cuda(), cp.cuda()
+    hid = torch.empty_like(h0)
+    lgo = torch.empty_like(lg0)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fpf.prefill_forward(st, e, m, p, c, kv, hidden_out=hid, logits_out=lgo)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            fpf.prefill_forward(st, e, m, p, c, kv, hidden_out=hid, logits_out=lgo)
+    torch.cuda.current_stream().wait_stream(s)
+    hid.zero_()
+    lgo.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(hid, h0) and torch.equal(lgo, lg0)
+    del graph
