@@ -30,8 +30,8 @@ def test_argument_errors_need_no_gpu():
     rc = L.flashb_gemv_seg(None, 8, 2, 2048, None, 1e-6, None, 0, None, 0, None, 0, None, 8, None)
     assert rc == _native.FB_ERR_ARG
     assert 'null' in _native.last_error()
-    rc = L.flashb_gemv_seg(16, 8, 129, 2048, None, 1e-6, 16, 8, None, 0, None, 0, 16, 8, None)
-    assert rc == _native.FB_ERR_ARG and 'M=129' in _native.last_error()
+    rc = L.flashb_gemv_seg(16, 8, (1 << 20) + 1, 2048, None, 1e-6, 16, 8, None, 0, None, 0, 16, 8, None)
+    assert rc == _native.FB_ERR_ARG and f'M={(1 << 20) + 1}' in _native.last_error()
     rc = L.flashb_attn_decode(16, 0, 0, 16, 16, 0, 0, 2, 16, 4, 64, 64, 16, 1, 0, 1.0, 16, 1 << 20, 16, 16, None)
     assert rc == _native.FB_ERR_UNSUPPORTED and 'head_dim' in _native.last_error()
     with pytest.raises(_native.FlashbError):
