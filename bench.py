@@ -66,6 +66,8 @@ def args_():
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--no-per-config', action='store_true', help='skip the per-config kernel figures (configs 1-3)')
+    p.add_argument('--step-table', type=int, default=1, choices=[0, 1],
+                   help='depth frames read the per-token step table for stage E and layer 0 q|k|v of steps >= 1')
     return p.parse_args()
 
 
@@ -595,6 +597,8 @@ def main():
     eng = FrameEngine(bcfg, dcfg, my_streams, a.prompt, n_runs * total_steps + LAT_FRAMES + 8, device=dev, seed=0,
                       depth_only=(a.case == 'depth'), group=a.group, single_slot=(a.case == 'frame'),
                       lanes=lanes, shared_backbone=shared)
+    if a.step_table:
+        eng.use_step_table(True)
     eng.capture()
     stream = torch.cuda.current_stream(dev)
 
@@ -667,7 +671,7 @@ def main():
         last[s_.cuda_stream] = None if kind in ('end', 'bbend') else (kind, e)
     kv1 = int(eng.streams[0].bb.cache_position.item()) + 1 if eng.streams[0].bb is not None else 0
     pk = peaks()
-    dd_bytes = dcfg.n_decode * dcfg.step_weight_bytes()
+    dd_bytes = dcfg.frame_weight_bytes(eng.step_table is not None, 2 * a.group)
     bb_rows = 2 * a.group * (S if eng.shared else 1)      # rows of one backbone graph
     bb_bytes = backbone_step_bytes(bcfg, bb_rows, (kv0 + kv1) // 2)
     roof = None

@@ -76,6 +76,8 @@ struct alignas(64) DDArgs {
   GridBar* bar;
   int nstages, xs_bytes, att_off, keep_off, att_bc, att_split, d_xchunk;
   unsigned long long wait_ns;             // grid-barrier wait limit
+  const bf16 *ptab, *ttab;                // optional per-token step table (codebook steps >= 1), or null
+  int l2_keep;                            // 1: weight copies carry the L2 evict_last hint
   unsigned* err;
   unsigned long long* trace;
 };
@@ -596,6 +598,7 @@ __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const D
 __shared__ float g_dd_nred[ST_CWARPS * 16];
 __shared__ int g_dd_int[32];
 __shared__ int g_dd_call;                          // trace builds: GEMV tasks this CTA has run (detail timeline)
+__shared__ int g_dd_l2keep;                        // the producer's L2 policy for weight copies (DDArgs::l2_keep)
 __shared__ long long g_dd_tok[DD_MAXB];            // tokens fed to the next step (this CTA's copy)
 __shared__ __align__(16) bf16 g_dd_cs[2][128];     // [cos|sin][dim] of the sub-step's position
 __shared__ uint32_t g_dd_tmem;                     // tcgen05 build: TMEM base of the accumulators
@@ -657,11 +660,24 @@ __device__ __forceinline__ void tc_task_blocks(int units, int& b0, int& b1) {
 
 // Producer half.  src(n0, mat) gives the tensor map and first row of the block starting at unit n0 (mat 1: the up
 // rows of KIND 1).
+// Weight copies carry an L2 evict_last hint: the lanes of the GPU stream the same depth weights at about the same
+// time, and a codebook step's weights (123 MB with the step table) nearly fit the 126 MB L2, so keeping them ahead of
+// the activations and KV traffic lets the later lanes read them from L2.
+__device__ __forceinline__ void tma_load_3d_l2(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+      "{%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 template <int KIND, typename SrcFn>
 __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int K, SrcFn src, unsigned* err) {
   constexpr int UB = tc_units<KIND>();
   constexpr int C = tc_cols<KIND>();
   const int lane = threadIdx.x & 31;
+  const uint64_t pol = g_dd_l2keep ? policy_evict_last() : policy_evict_normal();
   int b0, b1;
   tc_task_blocks<KIND>(units, b0, b1);
   const int nkc = (K + C - 1) / C;
@@ -675,12 +691,12 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
         unsigned char* st = rg.base + (size_t)s * ST_BYTES;
         mbar_arrive_expect_tx(&rg.full[s], (unsigned)ST_BYTES);
         if (KIND == 1) {
-          tma_load_3d(st, w0.map, 0, w0.row, kc, &rg.full[s]);                      // [128 rows][128 B]
-          tma_load_3d(st + ST_BYTES / 2, w1.map, 0, w1.row, kc, &rg.full[s]);
+          tma_load_3d_l2(st, w0.map, 0, w0.row, kc, &rg.full[s], pol);             // [128 rows][128 B]
+          tma_load_3d_l2(st + ST_BYTES / 2, w1.map, 0, w1.row, kc, &rg.full[s], pol);
         } else if (KIND == 0) {
-          tma_load_3d(st, w0.map, 0, w0.row, kc * 4, &rg.full[s]);                  // [4][64 rows][128 B]
+          tma_load_3d_l2(st, w0.map, 0, w0.row, kc * 4, &rg.full[s], pol);         // [4][64 rows][128 B]
         } else {
-          tma_load_3d(st, w0.map, 0, w0.row, kc * 2, &rg.full[s]);                  // [2][128 rows][128 B]
+          tma_load_3d_l2(st, w0.map, 0, w0.row, kc * 2, &rg.full[s], pol);         // [2][128 rows][128 B]
         }
       }
       __syncwarp();
@@ -896,17 +912,21 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
   int t = 0;
   bool ok = true;
   for (int s = 0; s < NCB && ok; ++s) {
+    const bool tab = a.ptab && s >= 1;     // stage E and layer 0's q|k|v come from the step table
     for (int sub = 0; sub < (s == 0 ? 2 : 1) && ok; ++sub) {
       if constexpr (NT == 0) {
-        ok = ok && produce_task_tc<0>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
+        if (!tab)
+          ok = ok && produce_task_tc<0>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
       } else {
-        ok = ok && produce_task_tma<1>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
+        if (!tab)
+          ok = ok && produce_task_tma<1>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
       }
       for (int l = 0; l < L && ok; ++l) {
         const CUtensorMap* W = a.tm[l];
+        const bool skip_qkv = tab && l == 0;
         if constexpr (NT == 0) {
           // one head per block: rows hh * 128 .. + 127 of wq / wk / wv
-          ok = ok && produce_task_tc<2>(m.rg, t, QKVU, H, [&](int u, int) {
+          if (!skip_qkv) ok = ok && produce_task_tc<2>(m.rg, t, QKVU, H, [&](int u, int) {
             const int hh = u >> 6;
             if (hh < NH) return TmaRows{&W[DD_WQ], hh * 128};
             if (hh < NH + NKV) return TmaRows{&W[DD_WK], (hh - NH) * 128};
@@ -918,7 +938,7 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
           ok = ok && produce_task_tc<0>(m.rg, t, H, F, [&](int n, int) { return TmaRows{&W[DD_WD], n}; }, err);
         } else {
           // unit u = (head hh, rotary pair d): matrix 0 carries row hh * 128 + d, matrix 1 row hh * 128 + 64 + d
-          ok = ok && produce_task_tma<2>(m.rg, t, QKVU, H, [&](int u, int mat) {
+          if (!skip_qkv) ok = ok && produce_task_tma<2>(m.rg, t, QKVU, H, [&](int u, int mat) {
             const int hh = u >> 6, d = (u & 63) + mat * 64;
             if (hh < NH) return TmaRows{&W[DD_WQ], hh * 128 + d};
             if (hh < NH + NKV) return TmaRows{&W[DD_WK], (hh - NH) * 128 + d};
@@ -981,6 +1001,67 @@ __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int su
                       }, [](int) {})) {
     c.ok = 0;
     return c;
+  }
+  DD_STAMP(s, 1);
+  if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) c.ok = 0;
+  DD_STAMP(s, 2);
+  return c;
+}
+
+// Codebook step >= 1 with the per-token step table (flashb_dd_tab_build): stage E and layer 0's q|k|v become table
+// reads.  Every CTA copies its share of the batch rows' ptab rows into the residual stream and takes its share of
+// the (row, head, rotary pair) units of their ttab rows: RoPE at `pos`, then q / the layer-0 KV cache written as the
+// S1 epilogue writes them (same rounding points: the table holds the bf16 GEMV outputs).  One barrier follows, in
+// place of the two of E and layer-0 S1.
+__device__ __noinline__ DDCur dd_phase_tab(const DDArgs& a, DDCur c, int s, int pos) {
+  const int tid = threadIdx.x, M = a.B, H = a.H, NH = a.NH, NKV = a.NKV, QD = NH * 128, V = a.V;
+  const int QKV = (NH + 2 * NKV) * 128, P = a.P;
+  bf16 *const xres = a.xres, *const qb = a.qb, *const kcache = a.kc, *const vcache = a.vc;
+  DD_STAMP(s, 0);
+  if (tid < 32) {    // cos / sin rows of the position for the later layers' S1 epilogues
+    const int tab = tid >> 4, cc = tid & 15;
+    cp_async16(&g_dd_cs[tab][cc * 8], (tab ? a.sin_tab : a.cos_tab) + (size_t)pos * 128 + cc * 8);
+  }
+  cp_async_commit();
+  const long long trows = (long long)(a.NCB - 1) * V, erows = (long long)(a.NCB + 1) * V;
+  auto trow = [&](int b) -> long long {      // the embedding gather's clamp, then the table's range
+    long long id = g_dd_tok[b] + (long long)s * V;
+    id = id < 0 ? 0 : (id >= erows ? erows - 1 : id);
+    const long long t = id - V;
+    return t < 0 ? 0 : (t >= trows ? trows - 1 : t);
+  };
+  const int gt = (int)blockIdx.x * PK_CONSUMERS + tid, gs = (int)gridDim.x * PK_CONSUMERS;
+  const int hu = H >> 3;
+  for (int i = gt; i < M * hu; i += gs) {
+    const int b = i / hu, u = i - b * hu;
+    reinterpret_cast<uint4*>(xres + (size_t)b * H)[u] =
+        __ldcg(reinterpret_cast<const uint4*>(a.ptab + (size_t)trow(b) * H) + u);
+  }
+  cp_async_wait<0>();
+  named_sync(1, PK_CONSUMERS);
+  const int npair = (NH + 2 * NKV) * 64;
+  for (int i = gt; i < M * npair; i += gs) {
+    const int b = i / npair, u = i - b * npair, hh = u >> 6, d = u & 63;
+    const bf16* src = a.ttab + (size_t)trow(b) * QKV + (size_t)hh * 128;
+    float y0 = b2f(src[d]), y1 = b2f(src[d + 64]);
+    if (hh < NH + NKV) {
+      const float c0 = b2f(g_dd_cs[0][d]), s0 = b2f(g_dd_cs[1][d]);
+      const float c1 = b2f(g_dd_cs[0][d + 64]), s1 = b2f(g_dd_cs[1][d + 64]);
+      const float o0 = rbf(rbf(y0 * c0) + rbf(-y1 * s0));
+      const float o1 = rbf(rbf(y1 * c1) + rbf(y0 * s1));
+      y0 = o0;
+      y1 = o1;
+    }
+    if (hh < NH) {
+      qb[(size_t)b * QD + hh * 128 + d] = __float2bfloat16_rn(y0);
+      qb[(size_t)b * QD + hh * 128 + d + 64] = __float2bfloat16_rn(y1);
+    } else {
+      const int kvh = hh < NH + NKV ? hh - NH : hh - NH - NKV;
+      bf16* cache = hh < NH + NKV ? kcache : vcache;
+      bf16* dst = cache + ((((size_t)0 * M + b) * NKV + kvh) * P + pos) * 128;
+      dst[d] = __float2bfloat16_rn(y0);
+      dst[d + 64] = __float2bfloat16_rn(y1);
+    }
   }
   DD_STAMP(s, 1);
   if (!grid_sync(a.bar, c.epoch, a.err, &g_dd_int[31], a.wait_ns)) c.ok = 0;
@@ -1222,6 +1303,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
     if (tid < 32) reinterpret_cast<uint32_t*>(m.zero16)[tid] = 0u;
     if (tid == 0) g_dd_int[28] = 0;                         // the consumers' "stopped early" flag
     if (tid == 0) g_dd_call = 0;
+    if (tid == 0) g_dd_l2keep = a.l2_keep;
     if (NT == 0 && warp == 0) tc_alloc(&g_dd_tmem, 64);   // 4 accumulator chains x 16 columns
   }
   if (NT == 0) tc_before();
@@ -1238,9 +1320,10 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
   for (int s = 0; s < a.NCB && c.ok; ++s) {
     for (int sub = 0; sub < (s == 0 ? 2 : 1) && c.ok; ++sub) {
       const int pos = s == 0 ? sub : s + 1;
-      c = dd_phase_e<NT>(a, c, s, sub, pos);
+      const bool tab = a.ptab && s >= 1;
+      c = tab ? dd_phase_tab(a, c, s, pos) : dd_phase_e<NT>(a, c, s, sub, pos);
       for (int l = 0; l < a.L && c.ok; ++l) {
-        c = dd_phase_s1<NT>(a, c, s, pos, l);
+        if (!(tab && l == 0)) c = dd_phase_s1<NT>(a, c, s, pos, l);
         if (c.ok) c = dd_phase_s2<G, NT>(a, c, s, pos, l);
         if (c.ok) c = dd_phase_s3<NT>(a, c, s, l);
         if (c.ok) c = dd_phase_s4<NT>(a, c, s, l);
@@ -1351,6 +1434,23 @@ int launch_dd(DDArgs& a, size_t smem, int grid, cudaStream_t st) {
 
 }  // namespace
 
+extern "C" int flashb_dd_tab_build(const fb_dd_config* c, void* ptab, void* ttab, void* work, void* stream) {
+  FB_CHECK_ARG(c && ptab && ttab && work && c->layers_host && c->embed && c->proj, "dd_tab_build: null argument");
+  if (int rc = dd_validate(c)) return rc;
+  FB_CHECK_ARG(c->n_decode >= 2, "dd_tab_build: the table covers codebook steps 1 .. n_decode - 1");
+  const fb_dd_layer* L0 = (const fb_dd_layer*)c->layers_host;
+  const int V = c->vocab, H = c->hidden, AE = c->embed_dim, QD = c->heads * 128, KD = c->kv_heads * 128;
+  const int rows = (c->n_decode - 1) * V;
+  const bf16* emb = (const bf16*)c->embed + (size_t)V * AE;    // embedding rows vocab .. n_decode vocab - 1
+  // ptab = embed rows . proj^T (the frame's stage E), then ttab = RMSNorm(ptab; ln1) . [wq; wk; wv]^T (layer 0's S1)
+  int rc = flashb_gemv_seg(emb, AE, rows, AE, nullptr, 0.f, c->proj, H, nullptr, 0, nullptr, 0, ptab, H, stream);
+  if (rc) return rc;
+  rc = flashb_rmsnorm(ptab, H, rows, H, L0->ln1, c->eps, work, H, stream);
+  if (rc) return rc;
+  return flashb_gemv_seg(work, H, rows, H, nullptr, 0.f, L0->wq, QD, L0->wk, KD, L0->wv, KD, ttab, QD + 2 * KD,
+                         stream);
+}
+
 extern "C" int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg) {
   if (!cfg) return -1;
   return (int64_t)dd_layout(cfg).total;
@@ -1390,6 +1490,13 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.err = fbh::device_err_ptr();
   a.wait_ns = c->wait_ns > 0 ? (unsigned long long)c->wait_ns : WAIT_LIMIT_NS;
   a.trace = (unsigned long long*)c->trace;
+  FB_CHECK_ARG(!c->ptab == !c->ttab, "dd_frame: step table needs both ptab and ttab");
+  a.ptab = (const bf16*)c->ptab;
+  a.ttab = (const bf16*)c->ttab;
+  {
+    const char* e = getenv("FLASHB_DD_L2_KEEP");      // L2 policy of the weight copies (tuning): 1 evict_last
+    a.l2_keep = (e && e[0] == '1') ? 1 : 0;
+  }
   const size_t M = (size_t)c->batch;
   const int grid = c->grid > 0 ? c->grid : fbh::grid_sms();
   if (grid > fbh::num_sms() || grid < (c->batch >= 2 ? c->batch / 2 : 1)) {

@@ -63,6 +63,7 @@ _PROTOS = {
     'flashb_prefill_qkv': (I, [P, L, I, I, I, I, P, P, F, P, P, I, P, P, P, P, L, L, I, P]),
     'flashb_lm_head_rows': (I, [P, L, I, I, P, I, P, P]),
     'flashb_dd_scratch_bytes': (L, [P]),
+    'flashb_dd_tab_build': (I, [P, P, P, P, P]),
     'flashb_dd_layer_bytes': (L, []),
     'flashb_dd_barrier_offset': (L, [P]),
     'flashb_dd_frame': (I, [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
@@ -80,7 +81,8 @@ class FbDDConfig(ctypes.Structure):
     _fields_ = [('layers', I), ('batch', I), ('hidden', I), ('embed_dim', I), ('heads', I), ('kv_heads', I),
                 ('head_dim', I), ('ffn', I), ('vocab', I), ('codebook_size', I), ('n_decode', I), ('eps', F),
                 ('scaling', F), ('embed', P), ('proj', P), ('normf', P), ('head_t', P), ('cos_tab', P),
-                ('sin_tab', P), ('trace', P), ('grid', I), ('layers_host', P), ('wait_ns', L)]
+                ('sin_tab', P), ('trace', P), ('grid', I), ('layers_host', P), ('wait_ns', L), ('ptab', P),
+                ('ttab', P)]
 
 
 def lib_path():

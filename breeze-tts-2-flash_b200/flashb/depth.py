@@ -3,8 +3,9 @@
 ``DepthDecoderGraph._full_loop`` (``UP/models/cudagraph/depth_decoder_graph.py:558-654``) becomes: the per-codebook
 Exp(1) draws with the official sizes and order (``q[c].exponential_(1)``, the RNG consumption of the official
 ``torch.multinomial`` calls) plus ONE cooperative launch (``flashb_dd_frame``) that decodes every codebook of the frame
-and samples on the device.  The weights stay bf16 (the reference's 12-bit LN12 packing is not used); the codebook
-heads are transposed once to [n_decode, vocab, hidden] bf16 (bf16-exact, as the reference asserts).
+and samples on the device.  The codebook heads are transposed once to [n_decode, vocab, hidden] bf16 (bf16-exact, as
+the reference asserts).  ``dd2_tab_build`` / ``dd2_tab_set`` give the frame the reference's per-token step table
+(stage E and layer 0's q|k|v of codebook steps >= 1 read from a table instead of computed).
 
 ``BUILDS`` / ``GRIDS`` keep the reference's names; one build serves every batch size.  ``GRIDS[B]`` is the launch's CTA
 count for batch B (0: one CTA per SM, or the calling thread's SM budget, ``flashb_set_sm_budget``).  Process state (``_state``) is keyed by device, so several graphs on several GPUs in one process coexist.
@@ -61,6 +62,44 @@ class DepthModelDesc:
             torch.cuda.current_stream(bh.device).cuda_stream))
 
 
+def tab_rows(desc):
+    c = desc.cfg
+    return (c.n_decode - 1) * c.vocab
+
+
+def tab_build(desc):
+    """The per-token step table of ``desc``'s weights (``flashb_dd_tab_build``): returns (ptab, ttab), new bf16
+    tensors [(n_decode - 1) vocab, hidden] and [(n_decode - 1) vocab, (heads + 2 kv_heads) 128]."""
+    c = desc.cfg
+    dev = desc.table.device
+    rows = tab_rows(desc)
+    qkv = (c.heads + 2 * c.kv_heads) * 128
+    pt = torch.empty(rows, c.hidden, dtype=torch.bfloat16, device=dev)
+    tt = torch.empty(rows, qkv, dtype=torch.bfloat16, device=dev)
+    work = torch.empty(rows, c.hidden, dtype=torch.bfloat16, device=dev)
+    check(_native.lib().flashb_dd_tab_build(ctypes.byref(c), pt.data_ptr(), tt.data_ptr(), work.data_ptr(),
+                                            torch.cuda.current_stream(dev).cuda_stream))
+    torch.cuda.current_stream(dev).synchronize()
+    del work
+    return pt, tt
+
+
+def tab_set(desc, pt, tt):
+    """Point ``desc``'s frames at the table (None, None: back to computing stage E and layer 0's q|k|v)."""
+    c = desc.cfg
+    if pt is None or tt is None:
+        c.ptab = c.ttab = None
+        desc.tab = None
+        return
+    rows = tab_rows(desc)
+    if (tuple(pt.shape) != (rows, c.hidden) or tuple(tt.shape) != (rows, (c.heads + 2 * c.kv_heads) * 128) or
+            pt.dtype != torch.bfloat16 or tt.dtype != torch.bfloat16 or not pt.is_contiguous() or
+            not tt.is_contiguous()):
+        raise RuntimeError('step table shapes do not match the depth model')
+    desc.tab = (pt, tt)
+    c.ptab, c.ttab = pt.data_ptr(), tt.data_ptr()
+
+
 class DepthOps:
     """flash_dd_*: the reference's dd2_* entry points (flash/csrc/depth_frame.cu:923-934) on flashb_dd_frame."""
 
@@ -81,6 +120,7 @@ class DepthOps:
         self.args = (layers, embed, proj, normf, head_t, cos, sin, float(eps), float(scaling),
                      int(codebook_size if codebook_size is not None else min(V, 2048)))
         self.desc = {}
+        self.tab = None
 
     def dd2_set_grid(self, B, grid):
         if B not in BUILDS:
@@ -95,6 +135,8 @@ class DepthOps:
             layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb = self.args
             d = DepthModelDesc(layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb, B, device)
             self.desc[B] = d
+            if getattr(self, 'tab', None) is not None:
+                tab_set(d, *self.tab)
         d.cfg.grid = GRIDS.get(B, 0)
         return d
 
@@ -104,15 +146,26 @@ class DepthOps:
 
     def dd2_info(self):
         a = self.args
-        return json.dumps(dict(NL=len(a[0]) if a else 0, ln12=0, pf_last=0, tab=0, grid=0,
+        tab = int(getattr(self, 'tab', None) is not None)
+        return json.dumps(dict(NL=len(a[0]) if a else 0, ln12=0, pf_last=0, tab=tab, grid=0,
                                grid_B1=GRIDS[1], grid_B2=GRIDS[2], grid_B4=GRIDS[4], grid_B8=GRIDS[8],
                                grid_B16=GRIDS[16], persisting_l2_limit=0))
 
     def dd2_tab_build(self):
-        raise RuntimeError('the per-token step table (flash/csrc/depth_frame.cu:714-754) is not built by flashb')
+        """The reference's ``dd2_tab_build`` (``flash/csrc/depth_frame.cu:894-913``): builds the per-token step table
+        from the initialised weights, applies it to every batch size's frame, and returns [ptab, ttab]."""
+        if self.args is None:
+            raise RuntimeError('dd2_init first')
+        d = self._desc(1, self.args[0][0]['wq'].device)
+        pt, tt = tab_build(d)
+        self.dd2_tab_set(pt, tt)
+        return [pt, tt]
 
     def dd2_tab_set(self, pt, tt):
-        raise RuntimeError('the per-token step table (flash/csrc/depth_frame.cu:714-754) is not built by flashb')
+        """The reference's ``dd2_tab_set``: frames of every batch size read the given table."""
+        self.tab = (pt, tt)
+        for d in self.desc.values():
+            tab_set(d, pt, tt)
 
 
 def _orig(mod):

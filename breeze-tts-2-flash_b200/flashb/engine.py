@@ -206,6 +206,16 @@ class DepthConfig:
         layer = (self.heads * D + 2 * self.kv_heads * D) * H + H * self.heads * D + 3 * self.ffn * H
         return 2 * (self.layers * layer + H * self.embed_dim + self.vocab * H)
 
+    def frame_weight_bytes(self, step_table=False, rows=2):
+        """Algorithmic bytes of one frame: n_decode codebook steps of weights; with the step table, steps >= 1 read
+        ``rows`` table rows (hidden + layer-0 q|k|v, bf16) instead of the projector and layer 0's q|k|v matrices."""
+        full = self.n_decode * self.step_weight_bytes()
+        if not step_table:
+            return full
+        H, qkv = self.hidden, (self.heads + 2 * self.kv_heads) * 128
+        saved = 2 * (H * self.embed_dim + qkv * H) - 2 * rows * (H + qkv)
+        return full - (self.n_decode - 1) * saved
+
 
 class SyntheticDepth:
     """A depth decoder with synthetic bf16 weights (heads stored transposed [n_decode, vocab, hidden]) and the
@@ -400,6 +410,18 @@ class FrameEngine:
             self.single.desc = d.desc if group == 1 else DepthModelDesc(
                 d.layers, d.embed, d.proj, d.normf, d.head_t, d.cos_tab, d.sin_tab, dcfg.eps, 128 ** -0.5,
                 dcfg.codebook_size, 2, dev)
+        self.step_table = None
+
+    def use_step_table(self, on=True):
+        """Frames of every slot read the per-token step table (built once from the shared depth weights,
+        ``flashb.depth.tab_build``) for stage E and layer 0's q|k|v of codebook steps >= 1; off: computed."""
+        from . import depth as fdep
+        if on and self.step_table is None:
+            self.step_table = fdep.tab_build(self.depth.desc)
+        descs = {id(x): x for x in [self.depth.desc] + list(self.lane_desc) +
+                 ([self.single.desc] if self.single is not None else [])}
+        for dd in descs.values():
+            fdep.tab_set(dd, *(self.step_table if on else (None, None)))
 
     def _slot(self, g, kv_seed, row0=None):
         """A slot of g streams; row0: its first row in the shared backbone graph (None: a backbone of its own)."""
@@ -642,13 +664,14 @@ class FrameEngine:
     def frame_bytes(self):
         """Algorithmic HBM bytes of one slot frame at the current KV length: backbone step + 16 depth steps."""
         if self.depth_only:
-            return self.dcfg.n_decode * self.dcfg.step_weight_bytes()
+            return self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group)
         kv = int(self.streams[0].bb.cache_position.item()) + 1
         if self.shared:
             n = len(self.streams)
             return backbone_step_bytes(self.bcfg, 2 * self.group * n, kv) / n + \
-                self.dcfg.n_decode * self.dcfg.step_weight_bytes()
-        return backbone_step_bytes(self.bcfg, 2 * self.group, kv) + self.dcfg.n_decode * self.dcfg.step_weight_bytes()
+                self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group)
+        return backbone_step_bytes(self.bcfg, 2 * self.group, kv) + \
+            self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group)
 
 
 def backbone_step_bytes(cfg: BackboneConfig, batch, kv_len, include_lm_head=True):

@@ -251,8 +251,19 @@ typedef struct {
                             * TMA tensor maps are built from it on the host (cached per matrix) */
   int64_t wait_ns;         /* limit of each grid-barrier wait in ns; 0 = 2 s.  On expiry the CTA records
                             * FB_ERR_TIMEOUT, sets the barrier's abort flag and the frame winds down */
+  const void* ptab;        /* optional per-token step table (flashb_dd_tab_build; both null = none): ptab
+                            * [(n_decode - 1) vocab, hidden] bf16 = projector output of embedding row vocab + t, */
+  const void* ttab;        /* ttab [(n_decode - 1) vocab, (heads + 2 kv_heads) 128] bf16 = layer 0's pre-RoPE q|k|v of
+                            * RMSNorm(ptab row t).  Codebook steps >= 1 then read their stage E and layer-0 q|k|v
+                            * there instead of running the projector and layer-0 q|k|v GEMVs */
 } fb_dd_config;
 int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg);
+/* Builds the per-token step table of the reference's dd2_tab_build (flash/csrc/depth_frame.cu:714-754, 894-913): for
+ * every table row t < (n_decode - 1) vocab (embedding row vocab + t, the ids codebook steps 1 .. n_decode - 1 can
+ * feed), ptab[t] = bf16(proj . embed[vocab + t]) and ttab[t] = bf16([wq; wk; wv] of layer 0 . RMSNorm(ptab[t]; ln1)),
+ * with the library's GEMV kernels (the same arithmetic contract as the frame's stage E and layer-0 q|k|v).  work:
+ * [(n_decode - 1) vocab, hidden] bf16 scratch.  Enqueued on `stream`; the buffers are the caller's. */
+int flashb_dd_tab_build(const fb_dd_config* cfg, void* ptab, void* ttab, void* work, void* stream);
 int64_t flashb_dd_layer_bytes(void);
 /* Byte offset, within the scratch buffer, of the frame's grid-barrier state: four uint32 words (arrival count, exit
  * count, abort flag, padding), zero between frames.  A non-zero abort word (set by the host, e.g. with

@@ -237,3 +237,42 @@ def test_depth_barrier_wait_expires():
     assert ei.value.rc == 5 and time.perf_counter() - t0 < 1.0
     m.desc.cfg.wait_ns = 0
     _fresh_frame_ok(m, ref)
+
+
+@pytest.mark.parametrize('small,B,grid', [(True, 2, 0), (False, 16, 18), (False, 2, 0), (False, 16, 0)])
+def test_depth_step_table(small, B, grid):
+    """The per-token step table (the reference's dd2_tab_build / dd2_tab_set): codebook steps >= 1 read stage E and
+    layer 0's q|k|v from the table.  The table itself equals the oracle's projector and layer-0 q|k|v of every
+    embedding row it covers; frames with it match the oracle (teacher-forced logits) on both builds (tcgen05 on a
+    lane-sized grid, mma.sync on the whole GPU); the sampler stays bit-exact on the kernel's logits."""
+    from flashb import depth as fdep
+    from oracle import decode as dec
+    m = _model(small=small, B=B, seed=7)
+    m.desc.cfg.grid = grid
+    c = m.cfg
+    pt, tt = fdep.tab_build(m.desc)
+    # the table against the oracle on a sample of its rows (every step's first and last token, a few between)
+    W = _weights(m)
+    rows = np.unique(np.concatenate([np.arange(0, pt.shape[0], max(1, pt.shape[0] // 37)), [pt.shape[0] - 1]]))
+    emb = np32(m.embed)[c.vocab + rows]
+    p_ref = dec.linear(emb, W.proj)
+    assert_close(np32(pt)[rows], p_ref, what='ptab')
+    L0 = W.layers[0]
+    t_ref = dec.gemv_seg(np32(pt)[rows], L0['ln1'], c.eps, [L0['wq'], L0['wk'], L0['wv']])
+    assert_close(np32(tt)[rows], t_ref, what='ttab')
+    fdep.tab_set(m.desc, pt, tt)
+    forced = np.random.default_rng(7).integers(0, c.vocab, (c.n_decode, B))
+    outtok, logits, _ = _run(m, forced)
+    temp, topk, topp, ds, gs = _params(m)
+    _, lg_ref, _ = odepth.depth_frame(W, np32(m.backbone_hidden_buf), m.first_cb_token_buf.cpu().numpy(),
+                                      m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
+    for s in range(c.n_decode):
+        assert_close(logits[s], lg_ref[s], what=f'step {s} logits (step table)')
+    _check_sampler(m, logits, outtok)
+    # without the table again: the same frame as before the table was set
+    fdep.tab_set(m.desc, None, None)
+    outtok2, logits2, _ = _run(m, forced)
+    for s in range(c.n_decode):
+        assert_close(logits2[s], lg_ref[s], what=f'step {s} logits (no table)')
+    from flashb._native import device_error
+    assert device_error() == 0
