@@ -276,8 +276,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     if (nm > -INFINITY) {
       float add = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) add += expf(sc[i] - nm);
-      sum = (mx > -INFINITY ? sum * expf(mx - nm) : 0.f) + add;
+      for (int i = 0; i < 32; ++i) add += __expf(sc[i] - nm);
+      sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) + add;
       mx = nm;
     }
     tc_fence_before();
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
 #pragma unroll
       for (int k = 0; k < PF_QUARTERS; ++k) {
         const float mk = s_stat[0][k][r];
-        if (mk > -INFINITY) l += s_stat[1][k][r] * expf(mk - m);
+        if (mk > -INFINITY) l += s_stat[1][k][r] * __expf(mk - m);
       }
     }
     mx = m;
@@ -322,9 +322,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     }
     float sc[32];
     scores32(t, sc);
+    // p = bf16(e^(s - max) / sum) with the fast exponential and one reciprocal per row: a few fp32 ulps, below the
+    // bf16 rounding of p except at rare ties (the exact expf and IEEE division per score serialise on their
+    // special-case branches and cost several microseconds per tile)
     float p[32];
+    const float inv = 1.0f / sum;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) p[i] = (dead || !row_ok) ? 0.f : rbf(expf(sc[i] - mx) / sum);
+    for (int i = 0; i < 32; ++i) p[i] = (dead || !row_ok) ? 0.f : rbf(__expf(sc[i] - mx) * inv);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint4 w;
