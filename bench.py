@@ -254,30 +254,22 @@ def prefill_flops(B, NH, L, D):
     return 4 * B * NH * D * L * (L + 1) // 2
 
 
-def measure_prefill(dev, world, rank, iters=50, warmup=5):
-    """Config 5's causal GQA prefill attention on the tcgen05 kernel, inputs resident.  With 2 or 4 ranks every
-    rank computes its KV-head group's q heads and one NCCL all-gather assembles the output; otherwise each rank
-    runs the whole call.  Returns the bench line's ``prefill`` object (rank 0) with TFLOP/s of the whole call."""
+def _prefill_inputs(dev, B, NH, NKV, L, D, pads, seed=4):
     import torch
-    from flashb import prefill_attn, replicas
-    c = PREFILL_CFG
-    B, NH, NKV, L, D = c['B'], c['NH'], c['NKV'], c['L'], c['D']
-    g = torch.Generator().manual_seed(4)
+    g = torch.Generator().manual_seed(seed)
     q = torch.randn(B, NH, L, D, generator=g).to(torch.bfloat16).to(dev)
     k = torch.randn(B, NKV, L, D, generator=g).to(torch.bfloat16).to(dev)
     v = torch.randn(B, NKV, L, D, generator=g).to(torch.bfloat16).to(dev)
     qi, ki = torch.arange(L).view(L, 1), torch.arange(L).view(1, L)
     m = torch.full((B, 1, L, L), torch.finfo(torch.bfloat16).min)
-    for b, p in enumerate(c['pads']):
+    for b, p in enumerate(pads):
         m[b, 0].masked_fill_((ki <= qi) & (ki >= p), 0.0)
-    m = m.to(torch.bfloat16).to(dev)
-    sharded = world in (2, 4)
+    return q, k, v, m.to(torch.bfloat16).to(dev)
 
-    def call():
-        if sharded:
-            return prefill_attn.prefill_attention_sharded(q, k, v, m, D ** -0.5)
-        return prefill_attn.prefill_attention(q, k, v, m, D ** -0.5)
 
+def _time_prefill(call, dev, iters, warmup):
+    import torch
+    from flashb import replicas
     for _ in range(warmup):
         call()
     replicas.barrier(dev)
@@ -288,14 +280,48 @@ def measure_prefill(dev, world, rank, iters=50, warmup=5):
         call()
     e1.record(st)
     replicas.barrier(dev)
-    ms = replicas.max_over_ranks(e0.elapsed_time(e1) / iters, dev)
+    return replicas.max_over_ranks(e0.elapsed_time(e1) / iters, dev)
+
+
+def measure_prefill(dev, world, rank, iters=50, warmup=5, long_len=4096, long_iters=10):
+    """Config 5's causal GQA prefill attention on the tcgen05 kernel, inputs resident.  With 2 or more ranks the
+    call is split (``prefill_attention_sharded``: by KV-head group when the ranks divide the 4 KV heads, else by
+    causal-balanced query-row tiles, as for 8 ranks) and one NCCL all_gather_into_tensor assembles the output; one
+    rank runs the whole call.  A long prompt (L = long_len) is timed both ways on every N, where a split can pay.
+    Returns the bench line's ``prefill`` object (rank 0) with TFLOP/s of the whole call."""
+    from flashb import prefill_attn
+    c = PREFILL_CFG
+    B, NH, NKV, L, D = c['B'], c['NH'], c['NKV'], c['L'], c['D']
+    q, k, v, m = _prefill_inputs(dev, B, NH, NKV, L, D, c['pads'])
+    sharded = world > 1
+    split = ('heads' if NKV % world == 0 else 'rows') if sharded else None
+
+    def call():
+        if sharded:
+            return prefill_attn.prefill_attention_sharded(q, k, v, m, D ** -0.5)
+        return prefill_attn.prefill_attention(q, k, v, m, D ** -0.5)
+
+    ms = _time_prefill(call, dev, iters, warmup)
     fl = prefill_flops(B, NH, L, D)
     peak = peaks()['bf16_tflops']
     ach = fl / (ms / 1e3) / 1e12
+    # the long prompt: one GPU alone and (N > 1) split over the ranks
+    ql, kl, vl, ml = _prefill_inputs(dev, B, NH, NKV, long_len, D, c['pads'], seed=5)
+    ms1 = _time_prefill(lambda: prefill_attn.prefill_attention(ql, kl, vl, ml, D ** -0.5), dev, long_iters, 2)
+    fll = prefill_flops(B, NH, long_len, D)
+    long = dict(L=long_len, ms_one_gpu=round(ms1, 4), tflops_one_gpu=round(fll / (ms1 / 1e3) / 1e12, 2))
+    if sharded:
+        msn = _time_prefill(lambda: prefill_attn.prefill_attention_sharded(ql, kl, vl, ml, D ** -0.5), dev,
+                            long_iters, 2)
+        long.update(ms_sharded=round(msn, 4), split=split, speedup=round(ms1 / msn, 3),
+                    tflops_sharded=round(fll / (msn / 1e3) / 1e12, 2))
+    del ql, kl, vl, ml
+    split_txt = {'heads': 'KV-head groups', 'rows': 'causal-balanced query-row tiles'}.get(split)
     return dict(kernel='prefill_attn_kernel (tcgen05)', config=f'B={B} L={L} NH={NH} NKV={NKV} D={D} causal, pads '
-                f'{list(c["pads"])}', parallel='KV-head groups + NCCL all-gather' if sharded else 'whole call per rank',
-                ms=round(ms, 4), algorithmic_flops=fl, achieved=round(ach, 2), unit='TFLOP/s', bound='tensor',
-                peak=peak, frac=round(ach / peak, 4), launches_per_call=1 + (1 if sharded else 0))
+                f'{list(c["pads"])}', parallel=(split_txt + ' + NCCL all_gather_into_tensor') if sharded else
+                'whole call per rank', ms=round(ms, 4), algorithmic_flops=fl, achieved=round(ach, 2),
+                unit='TFLOP/s', bound='tensor', peak=peak, frac=round(ach / peak, 4),
+                launches_per_call=1 + (1 if sharded else 0), long_prompt=long)
 
 
 # ------------------------------------------------------------------------------------------------ per-config kernels

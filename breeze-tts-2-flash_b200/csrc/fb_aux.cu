@@ -482,3 +482,88 @@ extern "C" int flashb_lm_head_rows(const void* hidden, int64_t ldh, int B, int H
   return lm_head_rows_launch((const bf16*)hidden, (long)ldh, B, H, W32, V, nullptr, 1, logits, nullptr,
                              (cudaStream_t)stream);
 }
+
+// ------------------------------------------------------------------------------------------------ LN12 decode
+// LN12 (the reference's lossless 12-bit weight storage, flash/ln12_format.py; layout in include/flashb.h) to bf16,
+// HBM to HBM.  One warp per (row n, 1024-column group g): lane l reads its three 16-byte units of the group (low
+// bytes of chunks 0-3 and their nibble words, 512-byte coalesced rows), forms the high byte of each of its 32
+// values from the row's shifted 8-entry table and the sign bit, and writes 8 consecutive bf16 of each chunk
+// (k = 1024 g + 256 c + 8 l + j).  Then, after a warp barrier, the row's patches in this group overwrite the high
+// byte of their value exactly (the first three from the row record, the rest from the overflow list).
+namespace {
+__global__ void __launch_bounds__(256) ln12_decode_kernel(const unsigned char* __restrict__ data,
+                                                          const uint4* __restrict__ meta,
+                                                          const uint32_t* __restrict__ ovf, uint32_t lut_lo,
+                                                          uint32_t lut_hi, int N, int K, bf16* __restrict__ out,
+                                                          long ldo) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int G = K >> 10;
+  const long w = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (w >= (long)N * G) return;
+  const int n = (int)(w / G), g = (int)(w - (long)n * G);
+  const unsigned char* grp = data + ((size_t)n * G + g) * 1536;
+  const uint4 s0 = __ldcs(reinterpret_cast<const uint4*>(grp) + lane);
+  const uint4 s1 = __ldcs(reinterpret_cast<const uint4*>(grp + 512) + lane);
+  const uint4 s2 = __ldcs(reinterpret_cast<const uint4*>(grp + 1024) + lane);
+  const uint4 rec = meta[n];
+  const uint32_t hdr = rec.x;
+  const int cnt = (int)(hdr & 1023u), ooff = (int)(hdr >> 13);
+  const int sh = (int)((hdr >> 10) & 7u) - (((hdr >> 10) & 4u) ? 8 : 0);
+  // the row's table: every entry + sh (the encoder keeps shifted entries inside 0..127, so no byte carries)
+  const uint32_t add = (uint32_t)sh * 0x01010101u;
+  const uint32_t t_lo = lut_lo + add, t_hi = lut_hi + add;
+  const uint32_t lows[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};   // chunk c: words 2c, 2c + 1
+  const uint32_t words[4] = {s2.x, s2.y, s2.z, s2.w};
+  bf16* row = out + (size_t)n * ldo + (size_t)g * 1024 + lane * 8;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint32_t wd = words[c];
+    uint32_t o[4];
+#pragma unroll
+    for (int jp = 0; jp < 4; ++jp) {
+      uint32_t pair = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * jp + h;
+        const uint32_t ix = (wd >> (4 * j)) & 7u;
+        const uint32_t sign = (wd >> (j < 4 ? 8 * j + 7 : 8 * (j - 4) + 3)) & 1u;
+        const uint32_t e = ((ix < 4 ? t_lo >> (8 * ix) : t_hi >> (8 * (ix - 4))) & 0x7Fu) | (sign << 7);
+        const uint32_t lo = (lows[2 * c + (j >> 2)] >> (8 * (j & 3))) & 0xFFu;
+        pair |= ((e << 8) | lo) << (16 * h);
+      }
+      o[jp] = pair;
+    }
+    *reinterpret_cast<uint4*>(row + c * 256) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (cnt == 0) return;
+  __syncwarp();                     // the warp's decoded values are written before a patch overwrites one
+  for (int p = lane; p < cnt; p += 32) {
+    const uint32_t v = p == 0 ? rec.y : (p == 1 ? rec.z : (p == 2 ? rec.w : ovf[ooff + p - 3]));
+    const int k = (int)(v >> 8);
+    if ((k >> 10) != g) continue;
+    const int kk = k & 1023, c = kk >> 8, l = (kk >> 3) & 31, j = kk & 7;
+    const unsigned char lo = grp[(c >> 1) * 512 + l * 16 + (c & 1) * 8 + j];
+    reinterpret_cast<unsigned short*>(out + (size_t)n * ldo)[k] = (unsigned short)(((v & 0xFFu) << 8) | lo);
+  }
+}
+}  // namespace
+
+extern "C" int flashb_ln12_decode(const void* data, const void* meta, const void* ovf, uint32_t lut_lo,
+                                  uint32_t lut_hi, int N, int K, void* out, int64_t ldo, void* stream) {
+  FB_CHECK_ARG(data && meta && out && N >= 1 && K >= 1024 && K % 1024 == 0 && ldo >= K && ldo % 8 == 0,
+               "ln12_decode: bad arguments (N=%d K=%d ldo=%lld)", N, K, (long long)ldo);
+  FB_CHECK_ARG(((uintptr_t)data & 15) == 0 && ((uintptr_t)meta & 15) == 0 && ((uintptr_t)out & 15) == 0,
+               "ln12_decode: data, meta and out must be 16-byte aligned");
+  const unsigned char* dp = (const unsigned char*)data;
+  const uint4* mp = (const uint4*)meta;
+  const uint32_t* op = (const uint32_t*)ovf;
+  bf16* outp = (bf16*)out;
+  long l = (long)ldo;
+  const long warps = (long)N * (K / 1024);
+  void* args[] = {(void*)&dp, (void*)&mp, (void*)&op, (void*)&lut_lo, (void*)&lut_hi, (void*)&N, (void*)&K,
+                  (void*)&outp, (void*)&l};
+  return fbh::launch_pdl((const void*)ln12_decode_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0,
+                         (cudaStream_t)stream, args, true);
+}

@@ -46,6 +46,7 @@ struct PFArgs {
   bf16* out;
   long o_sb, o_sl, o_sh;
   int B, NH, NKV, L, S, h0, causal;
+  int t0;              // first query tile of the launch (a query-row shard computes tiles [t0, t0 + gridDim.x))
   float scaling;
   unsigned* err;
 };
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // TMEM lane quarter (warp % 4) x column quarter (warp / 4): this thread owns row r, columns [32 cq, 32 cq + 32)
   const int r = (warp & 3) * 32 + lane, cq = warp >> 2;
-  const int q0 = blockIdx.x * PF_TILE, h = a.h0 + blockIdx.y, b = blockIdx.z;
+  const int q0 = (a.t0 + (int)blockIdx.x) * PF_TILE, h = a.h0 + blockIdx.y, b = blockIdx.z;
   const int kvh = h / (a.NH / a.NKV);
   const int row = q0 + r;
   const bool row_ok = row < a.L;
@@ -388,17 +389,20 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
 // ------------------------------------------------------------------------------------------------ host API
 using namespace fb;
 
-extern "C" int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl, const void* k,
-                                   int64_t k_sb, int64_t k_sh, int64_t k_sl, const void* v, int64_t v_sb,
-                                   int64_t v_sh, int64_t v_sl, const void* mask, int mask_is_bf16, int64_t m_sb,
-                                   int64_t m_sl, int B, int NH, int NKV, int L, int S, int D, float scaling,
-                                   int causal, int h0, int h1, void* out, int64_t o_sb, int64_t o_sl, int64_t o_sh,
-                                   void* stream) {
+extern "C" int flashb_prefill_attn_tiles(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl, const void* k,
+                                         int64_t k_sb, int64_t k_sh, int64_t k_sl, const void* v, int64_t v_sb,
+                                         int64_t v_sh, int64_t v_sl, const void* mask, int mask_is_bf16, int64_t m_sb,
+                                         int64_t m_sl, int B, int NH, int NKV, int L, int S, int D, float scaling,
+                                         int causal, int h0, int h1, int tile0, int tile1, void* out, int64_t o_sb,
+                                         int64_t o_sl, int64_t o_sh, void* stream) {
   FB_CHECK_ARG(q && k && v && out, "prefill_attn: null pointer argument");
   FB_CHECK_ARG(D == PF_D, "prefill_attn: head_dim must be 128 (got %d)", D);
   FB_CHECK_ARG(B >= 1 && NH >= 1 && NKV >= 1 && NH % NKV == 0 && L >= 1 && S >= 1 && L <= 65535 * PF_TILE,
                "prefill_attn: bad shape B=%d NH=%d NKV=%d L=%d S=%d", B, NH, NKV, L, S);
   FB_CHECK_ARG(0 <= h0 && h0 < h1 && h1 <= NH, "prefill_attn: head range [%d, %d) outside [0, %d)", h0, h1, NH);
+  const int ntile = (L + PF_TILE - 1) / PF_TILE;
+  FB_CHECK_ARG(0 <= tile0 && tile0 < tile1 && tile1 <= ntile, "prefill_attn: query tiles [%d, %d) outside [0, %d)",
+               tile0, tile1, ntile);
   const uintptr_t align = (uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out;
   const int64_t strides = q_sb | q_sh | q_sl | k_sb | k_sh | k_sl | v_sb | v_sh | v_sl | o_sb | o_sl | o_sh;
   FB_CHECK_ARG((align & 15) == 0 && (strides & 7) == 0,
@@ -422,9 +426,10 @@ extern "C" int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, in
   a.mask = mask; a.mask_bf16 = mask_is_bf16; a.m_sb = (long)m_sb; a.m_sl = (long)m_sl;
   a.out = (bf16*)out; a.o_sb = (long)o_sb; a.o_sl = (long)o_sl; a.o_sh = (long)o_sh;
   a.B = B; a.NH = NH; a.NKV = NKV; a.L = L; a.S = S; a.h0 = h0; a.causal = causal; a.scaling = scaling;
+  a.t0 = tile0;
   a.err = fbh::device_err_ptr();
   void* args[] = {(void*)&a};
-  const dim3 grid((L + PF_TILE - 1) / PF_TILE, h1 - h0, B);
+  const dim3 grid(tile1 - tile0, h1 - h0, B);
   cudaError_t e = cudaLaunchKernel((const void*)prefill_attn_kernel, grid, dim3(PF_THREADS), args, PF_SMEM,
                                    (cudaStream_t)stream);
   if (e != cudaSuccess) {
@@ -432,6 +437,18 @@ extern "C" int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, in
     return FB_ERR_CUDA;
   }
   return FB_OK;
+}
+
+extern "C" int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl, const void* k,
+                                   int64_t k_sb, int64_t k_sh, int64_t k_sl, const void* v, int64_t v_sb,
+                                   int64_t v_sh, int64_t v_sl, const void* mask, int mask_is_bf16, int64_t m_sb,
+                                   int64_t m_sl, int B, int NH, int NKV, int L, int S, int D, float scaling,
+                                   int causal, int h0, int h1, void* out, int64_t o_sb, int64_t o_sl, int64_t o_sh,
+                                   void* stream) {
+  const int ntile = L >= 1 ? (L + PF_TILE - 1) / PF_TILE : 1;
+  return flashb_prefill_attn_tiles(q, q_sb, q_sh, q_sl, k, k_sb, k_sh, k_sl, v, v_sb, v_sh, v_sl, mask, mask_is_bf16,
+                                   m_sb, m_sl, B, NH, NKV, L, S, D, scaling, causal, h0, h1, 0, ntile, out, o_sb,
+                                   o_sl, o_sh, stream);
 }
 
 

@@ -60,7 +60,10 @@ _PROTOS = {
     'flashb_frame_ids': (I, [P, P, I, I, I, P, P]),
     'flashb_prefill_attn': (I, [P, L, L, L, P, L, L, L, P, L, L, L, P, I, L, L, I, I, I, I, I, I, F, I, I, I, P, L, L,
                                 L, P]),
+    'flashb_prefill_attn_tiles': (I, [P, L, L, L, P, L, L, L, P, L, L, L, P, I, L, L, I, I, I, I, I, I, F, I, I, I,
+                                      I, I, P, L, L, L, P]),
     'flashb_prefill_qkv': (I, [P, L, I, I, I, I, P, P, F, P, P, I, P, P, P, P, L, L, I, P]),
+    'flashb_ln12_decode': (I, [P, P, P, ctypes.c_uint32, ctypes.c_uint32, I, I, P, L, P]),
     'flashb_lm_head_rows': (I, [P, L, I, I, P, I, P, P]),
     'flashb_dd_scratch_bytes': (L, [P]),
     'flashb_dd_tab_build': (I, [P, P, P, P, P]),

@@ -122,6 +122,46 @@ class DepthOps:
         self.desc = {}
         self.tab = None
 
+    def ln12_mats(self):
+        """The matrices LN12 covers, in the reference's descriptor order (flash/ln12_cache.py:23-32): per layer q, k,
+        v, o, gate, up, down; the projector; the codebook heads ([vocab, hidden] each)."""
+        layers, embed, proj, normf, head_t = self.args[:5]
+        mats = []
+        for L in layers:
+            mats += [L['wq'], L['wk'], L['wv'], L['wo'], L['wg'], L['wu'], L['wd']]
+        mats.append(proj)
+        mats += [head_t[s] for s in range(head_t.shape[0])]
+        return mats
+
+    def dd2_init_ln12(self, data, meta, ovf, luts):
+        """The reference's ``dd2_init_ln12`` (``flash/csrc/depth_frame.cu:800-823``): the depth matrices in the
+        lossless LN12 format (per matrix: data uint8, meta int32 [N, 4], ovf int32; luts int64 [count, 2] = the
+        table words).  flashb decodes them on the device (``flashb_ln12_decode``, bit-exact) into the bf16 matrices
+        its frame reads, replacing those of ``dd2_init``: the frames are the same."""
+        from . import ln12
+        if self.args is None:
+            raise RuntimeError('dd2_init first')
+        mats = self.ln12_mats()
+        if not len(data) == len(meta) == len(ovf) == len(mats) or tuple(luts.shape) != (len(mats), 2):
+            raise RuntimeError(f'LN12: {len(mats)} matrices expected')
+        lc = luts.cpu().tolist()
+        dec = [ln12.decode_device(data[i], meta[i], ovf[i], (lc[i][0], lc[i][1]), torch.empty_like(m))
+               for i, m in enumerate(mats)]
+        layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb = self.args
+        k = 0
+        new_layers = []
+        for L in layers:
+            d = dict(L)
+            for name in ('wq', 'wk', 'wv', 'wo', 'wg', 'wu', 'wd'):
+                d[name] = dec[k]
+                k += 1
+            new_layers.append(d)
+        proj = dec[k]
+        head_t = torch.stack(dec[k + 1:])
+        self.args = (new_layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb)
+        self.desc = {}
+        self.ln12 = True
+
     def dd2_set_grid(self, B, grid):
         if B not in BUILDS:
             raise RuntimeError('B must be 1, 2, 4, 8 or 16')
@@ -147,7 +187,8 @@ class DepthOps:
     def dd2_info(self):
         a = self.args
         tab = int(getattr(self, 'tab', None) is not None)
-        return json.dumps(dict(NL=len(a[0]) if a else 0, ln12=0, pf_last=0, tab=tab, grid=0,
+        return json.dumps(dict(NL=len(a[0]) if a else 0, ln12=int(getattr(self, 'ln12', False)), pf_last=0, tab=tab,
+                               grid=0,
                                grid_B1=GRIDS[1], grid_B2=GRIDS[2], grid_B4=GRIDS[4], grid_B8=GRIDS[8],
                                grid_B16=GRIDS[16], persisting_l2_limit=0))
 

@@ -201,6 +201,14 @@ int flashb_prefill_attn(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl,
                         int S, int D, float scaling, int causal, int h0, int h1, void* out, int64_t o_sb,
                         int64_t o_sl, int64_t o_sh, void* stream);
 
+/* flashb_prefill_attn for the query tiles [tile0, tile1) only (query rows [128 tile0, min(L, 128 tile1))): a
+ * query-row shard of a multi-GPU prefill; the output rows of the other tiles are not written.  No reference
+ * counterpart (the reference runs the prefill attention on one GPU). */
+int flashb_prefill_attn_tiles(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_sl, const void* k, int64_t k_sb,
+                              int64_t k_sh, int64_t k_sl, const void* v, int64_t v_sb, int64_t v_sh, int64_t v_sl,
+                              const void* mask, int mask_is_bf16, int64_t m_sb, int64_t m_sl, int B, int NH, int NKV,
+                              int L, int S, int D, float scaling, int causal, int h0, int h1, int tile0, int tile1,
+                              void* out, int64_t o_sb, int64_t o_sl, int64_t o_sh, void* stream);
 /* The prefill's q|k|v tail for every prompt token (replaces, with flashb_prefill_attn and the GEMV entry points, the
  * eager layers of BackbonePrefillGraphCache._forward, UP/models/cudagraph/backbone_prefill_graph.py:95-112):
  * qkv [B L, (NH + 2 NKV) 128] bf16 raw projections (row stride ldq; token t = b L + l): q heads rewritten in place
@@ -216,6 +224,17 @@ int flashb_prefill_qkv(void* qkv, int64_t ldq, int B, int L, int NH, int NKV, co
  * already normalised bf16 rows at row stride ldh (the last token of each prompt). */
 int flashb_lm_head_rows(const void* hidden, int64_t ldh, int B, int H, const float* W32, int V, float* logits,
                         void* stream);
+
+/* LN12 -> bf16 on the device (the reference's lossless 12-bit weight storage, flash/ln12_format.py, read by its depth
+ * kernels through dd2_init_ln12, flash/csrc/depth_frame.cu:800-823): a matrix W[N, K] (K % 1024 == 0) stored as
+ * data [N][K / 1024][3][32][16 B] (slot 0: low bytes of the chunks 0, 1 of lane l's elements k = 1024 g + 256 c +
+ * 8 l + j; slot 1: chunks 2, 3; slot 2: four nibble words -- 3-bit table index of element j at bits 4j.., its sign at
+ * bit 8j + 7 (j < 4) or 8 (j - 4) + 3), meta [N][4] uint32 row records {hdr = (overflow offset << 13) | ((shift & 7)
+ * << 10) | patch count, patch 0, 1, 2}, ovf uint32 (patches 3.. of each row, (k << 8) | exact high byte) and the
+ * 8-entry table of high-byte exponent values as two little-endian words (lut_lo, lut_hi), each row's entries
+ * offset by its shift.  Writes bf16 out[N, K] (row stride ldo elements): bit-exact the encoded matrix. */
+int flashb_ln12_decode(const void* data, const void* meta, const void* ovf, uint32_t lut_lo, uint32_t lut_hi, int N,
+                       int K, void* out, int64_t ldo, void* stream);
 
 /* ---------------------------------------------------------------------------------------------- depth frame
  * Replaces the reference's depth frame megakernel dd2_init / dd2_frame (flash/csrc/depth_frame.cu:758-853, 923-934),

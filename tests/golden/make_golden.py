@@ -454,6 +454,23 @@ def gold_prefill(out):
     out['prefill'] = dict(out=synth.np_bits(o), digest=synth.digest(q, k, v, mask))
 
 
+def gold_ln12(out):
+    """The reference's LN12 encoder (``flash/ln12_format.py``: choose_lut, encode, to_inline) on a matrix with the
+    format's special cases (shifted row tables, patches, overflow patches)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('ref_ln12', os.path.join(REF_ROOT[0], 'flash', 'ln12_format.py'))
+    fmt = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(fmt)
+    w = synth.ln12_matrix()
+    u = w.contiguous().view(torch.int16).numpy().view(np.uint16)
+    lut = fmt.choose_lut(u)
+    packed, hdr, pat = fmt.encode(u, lut)
+    meta, ovf = fmt.to_inline(hdr, pat)
+    assert np.array_equal(fmt.decode(packed, hdr, pat, lut, *u.shape), u), 'reference LN12 round trip'
+    out['ln12'] = dict(data=packed, meta=meta, ovf=ovf, lut=np.asarray(lut, np.uint8), hdr=hdr, patches=pat,
+                       digest=synth.digest(w))
+
+
 def gold_prefill_forward(out):
     """The reference's own prefill forward (``BackbonePrefillGraphCache._forward``, official modules in bf16 on the
     CPU) on the BACKBONE weights: hidden states, last-token logits and the cache slots it wrote."""
@@ -502,7 +519,7 @@ def main():
     out = {}
     only = set(args.only.split(',')) if args.only else None
     for fn in (gold_attention, gold_attention1, gold_gemv, gold_gemv2, gold_backbone, gold_depth, gold_sampler,
-               gold_prefill, gold_drift, gold_depth_drift, gold_bb_sampler, gold_prefill_forward):
+               gold_prefill, gold_drift, gold_depth_drift, gold_bb_sampler, gold_prefill_forward, gold_ln12):
         if only and fn.__name__[len('gold_'):] not in only:
             continue
         fn(out)

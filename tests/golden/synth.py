@@ -97,6 +97,23 @@ BACKBONE28 = dict(seed=106, B=2, H=2048, NH=16, NKV=4, D=128, F=6144, L=28, voca
                   S=1024, prefill=1023, pad=(0, 3), gs=4.0)
 
 
+# LN12: a bf16 matrix like a depth weight (normal, std 0.02) with what makes the format's special cases: a row at
+# 2^-5 scale and one at 2^6 (their exponents leave the table: a shifted row table), a few huge and tiny values
+# (patches), a row with more than three patches (the overflow list), and exact zeros
+LN12 = dict(seed=108, N=48, K=2048)
+
+
+def ln12_matrix(c=LN12):
+    g = gen(c['seed'])
+    w = torch.randn(c['N'], c['K'], generator=g) * 0.02
+    w[5] *= 2.0 ** -5
+    w[9] *= 2.0 ** 6
+    w[13, [3, 700, 1500, 2047, 1024]] = torch.tensor([300.0, -1e-9, 7e4, -2e-7, 1e-3])
+    w[20, 17] = -65000.0
+    w[31, :64] = 0.0
+    return w.to(torch.bfloat16)
+
+
 # the whole prefill forward (BackbonePrefillGraphCache._forward) on the BACKBONE weights: 24 prompt tokens, row 1
 # left-padded by 5 (positions and causal mask as the reference prefill forms them)
 PREFILL_FWD = dict(seed=107, L=24, pads=(0, 5))

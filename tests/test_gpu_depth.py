@@ -6,6 +6,8 @@
 * a free-running frame equals the teacher-forced oracle driven by the kernel's own tokens;
 * run-to-run determinism and CUDA-graph replay.
 """
+import json
+
 import numpy as np
 import pytest
 import torch
@@ -276,3 +278,59 @@ def test_depth_step_table(small, B, grid):
         assert_close(logits2[s], lg_ref[s], what=f'step {s} logits (no table)')
     from flashb._native import device_error
     assert device_error() == 0
+
+
+def test_ln12_device_decode_is_bit_exact():
+    """flashb_ln12_decode on the reference-encoded fixture matrix (shifted rows, inline and overflow patches) and on
+    a full-size depth matrix gives back every bit of the bf16 weights."""
+    import synth
+    from flashb import ln12
+    z = np.load(synth.__file__.replace('synth.py', 'ln12.npz'))
+    w = synth.ln12_matrix()
+    N, K = w.shape
+    d, m, o, lut = ln12.to_device(z['data'], z['meta'], z['ovf'], z['lut'], 'cuda')
+    out = torch.full((N, K), float('nan'), dtype=torch.bfloat16, device='cuda')
+    ln12.decode_device(d, m, o, lut, out)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu().view(torch.int16), w.view(torch.int16))
+    g = torch.Generator().manual_seed(8)
+    w2 = (torch.randn(4096, 1024, generator=g) * 0.02).to(torch.bfloat16)
+    enc = ln12.encode(w2)
+    out2 = torch.empty(4096, 1024, dtype=torch.bfloat16, device='cuda')
+    ln12.decode_device(*ln12.to_device(*enc, 'cuda'), out2)
+    torch.cuda.synchronize()
+    assert torch.equal(out2.cpu().view(torch.int16), w2.view(torch.int16))
+
+
+def test_dd2_init_ln12_frames_equal_the_bf16_frames():
+    """The reference's dd2_init_ln12 surface: the depth matrices handed over in LN12 are decoded on the device and
+    the frames are bit-identical to the frames on the bf16 weights."""
+    from flashb import depth as fdep
+    from flashb import ln12
+    m = _model(small=False, B=2, seed=9, layers=1, ffn=1024, embed_dim=1024, vocab=128, codebook_size=120,
+               n_decode=4)
+    ops = fdep.DepthOps()
+    L = m.layers
+    w = []
+    for layer in L:
+        w += [layer[k] for k in ('ln1', 'wq', 'wk', 'wv', 'wo', 'ln2', 'wg', 'wu', 'wd')]
+    w += [m.embed, m.proj, m.normf, m.head_t, m.cos_tab, m.sin_tab]
+    ops.dd2_init(w, eps=m.cfg.eps, codebook_size=m.cfg.codebook_size)
+    args = (m.first_cb_token_buf, m.backbone_hidden_buf, m.tok_buf, m.output_tokens, m.temperature, m.top_k,
+            m.top_p, m.do_sample, m.guidance_scale, m.q)
+    ops.dd2_frame(*args)
+    torch.cuda.synchronize()
+    ref = m.output_tokens.clone()
+    enc = [ln12.encode(x) for x in ops.ln12_mats()]
+    dev = [ln12.to_device(*e, 'cuda') for e in enc]
+    luts = torch.tensor([list(x[3]) for x in dev], dtype=torch.int64)
+    ops.dd2_init_ln12([x[0] for x in dev], [x[1] for x in dev], [x[2] for x in dev], luts)
+    for a, b in zip(ops.ln12_mats(), [x for layer in L for x in (layer['wq'], layer['wk'], layer['wv'], layer['wo'],
+                                                                 layer['wg'], layer['wu'], layer['wd'])] +
+                    [m.proj] + [m.head_t[s] for s in range(m.head_t.shape[0])]):
+        assert torch.equal(a, b)
+    m.output_tokens.zero_()
+    ops.dd2_frame(*args)
+    torch.cuda.synchronize()
+    assert torch.equal(m.output_tokens, ref)
+    assert json.loads(ops.dd2_info())['ln12'] == 1

@@ -223,3 +223,26 @@ def test_prefill_forward_graph_capture_and_determinism():
     torch.cuda.synchronize()
     assert torch.equal(hid, h0) and torch.equal(lgo, lg0)
     del graph
+
+
+def test_prefill_query_tile_ranges_assemble_the_full_output():
+    """The query-row split of a multi-GPU prefill (``row_shards`` ranges computed with ``tiles=``), run on one GPU
+    range by range: every range writes exactly its rows, each equal to the whole call's, and the ranges of 8 ranks
+    over L = 1000 cover every row."""
+    pf = _pf()
+    B, NH, NKV, L = 2, 8, 2, 1000
+    q, k, v = _inputs(B, NH, NKV, L, L, seed=21)
+    q, k, v = q.cuda(), k.cuda(), v.cuda()
+    m = _mask(B, L, L, [0, 9]).cuda()
+    full = pf.prefill_attention(q, k, v, m, 128 ** -0.5)
+    ranges = pf.row_shards(L, 8)
+    out = torch.full_like(full, float('nan'))
+    for t0, t1 in ranges:
+        if t1 > t0:
+            rows = min(L, t1 * 128) - t0 * 128
+            part = torch.full((B, rows, NH, 128), float('nan'), dtype=torch.bfloat16, device='cuda')
+            pf.prefill_attention(q, k, v, m, 128 ** -0.5, out=part, tiles=(t0, t1))
+            out[:, t0 * 128:t0 * 128 + rows] = part
+    torch.cuda.synchronize()
+    assert not torch.isnan(out.float()).any()
+    assert torch.equal(out, full)

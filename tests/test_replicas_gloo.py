@@ -126,3 +126,72 @@ def test_prefill_head_shards_gather_to_the_full_output():
     assert [p.exitcode for p in procs] == [0, 0]
     res = sorted(q.get() for _ in range(2))
     assert res == [(0, True, (0, 4)), (1, True, (4, 8))]
+
+
+def _row_worker(rank, world, port, out):
+    """CPU ranks: each computes its causal-balanced range of query-row tiles with the oracle (the stand-in for the
+    kernel on a GPU rank), the ranges are gathered with flashb.prefill_attn.gather_row_shards (one
+    all_gather_into_tensor of padded parts)."""
+    sys.path.insert(0, PKG)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from flashb import prefill_attn
+    from oracle import decode as dec
+    from oracle import prefill as opf
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        g = torch.Generator().manual_seed(4)
+        B, NH, NKV, L = 2, 4, 2, 300
+        q = torch.randn(B, NH, L, 128, generator=g).to(torch.bfloat16).float().numpy()
+        k = torch.randn(B, NKV, L, 128, generator=g).to(torch.bfloat16).float().numpy()
+        v = torch.randn(B, NKV, L, 128, generator=g).to(torch.bfloat16).float().numpy()
+        mask = np.where(np.arange(L)[None, :] <= np.arange(L)[:, None], 0.0, -3.3895313892515355e38)
+        mask = mask.astype(np.float32)[None, None]
+        ranges = prefill_attn.row_shards(L, world)
+        t0, t1 = ranges[rank]
+        rows = max(min(L, b * 128) - a * 128 for a, b in ranges)
+        part = np.zeros((B, rows, NH, 128), np.float32)
+        r0, r1 = t0 * 128, min(L, t1 * 128)
+        if r1 > r0:
+            # a shard's rows attend to every key of the (already trimmed) cache: the eager attention, no re-trim
+            part[:, :r1 - r0] = dec.attention_eager(q[:, :, r0:r1], k, v, mask[:, :, r0:r1], 128 ** -0.5)
+        full = prefill_attn.gather_row_shards(torch.from_numpy(part), ranges, L)
+        ref = opf.prefill_attention(q, k, v, mask, 128 ** -0.5)
+        out.put((rank, bool(np.array_equal(full.numpy(), ref)), (t0, t1)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_prefill_row_shards_gather_to_the_full_output():
+    """The N > NKV split (e.g. 8 ranks over 4 KV heads) by query rows, here 3 ranks over 300 rows (3 tiles): each
+    rank's causal-balanced tile range, gathered to the full output on every rank."""
+    ctx = mp.get_context('spawn')
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_row_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+    assert [p.exitcode for p in procs] == [0, 0, 0]
+    res = sorted(q.get() for _ in range(3))
+    assert all(ok for _, ok, _ in res)
+    assert [r for _, _, r in res] == [(0, 2), (2, 3), (3, 3)] or [r for _, _, r in res] == [(0, 1), (1, 2), (2, 3)]
+
+
+def test_row_shards_balance_the_causal_work():
+    sys.path.insert(0, PKG)
+    from flashb.prefill_attn import row_shards
+    for L, n in ((4096, 8), (4096, 4), (4096, 2), (512, 8), (1000, 3), (100, 4)):
+        r = row_shards(L, n)
+        T = (L + 127) // 128
+        assert len(r) == n and r[0][0] == 0 and r[-1][1] == T
+        assert all(a <= b for a, b in r) and all(r[i][1] == r[i + 1][0] for i in range(n - 1))
+        work = [sum(t + 1 for t in range(a, b)) for a, b in r]
+        ideal = T * (T + 1) / 2 / n
+        # within one tile's work (the largest, T) of the ideal share
+        assert max(work) <= ideal + T
