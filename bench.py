@@ -601,7 +601,7 @@ def main():
                                   config=dict(workload='causal GQA prefill attention, ' + pf['config']),
                                   roofline=dict(bound='tensor', achieved=pf['achieved'], peak=pf['peak'],
                                                 unit='TFLOP/s', frac=pf['frac'], traffic=None),
-                                  gpu_launches=a.steps * pf['launches_per_call'])), flush=True)
+                                  gpu_launches=a.steps * pf['launches_per_call'], detail=pf)), flush=True)
         if world > 1:
             replicas.barrier(dev)
             dist.destroy_process_group()
