@@ -68,6 +68,8 @@ def args_():
     p.add_argument('--no-per-config', action='store_true', help='skip the per-config kernel figures (configs 1-3)')
     p.add_argument('--step-table', type=int, default=1, choices=[0, 1],
                    help='depth frames read the per-token step table for stage E and layer 0 q|k|v of steps >= 1')
+    p.add_argument('--ln12', type=int, default=0, choices=[0, 1],
+                   help='depth frames stream their weights in LN12 (12-bit lossless, decoded in shared memory)')
     return p.parse_args()
 
 
@@ -210,7 +212,7 @@ def reference_config(a, threads):
 
 def frame_config(a, world, my_streams, lanes, shared, lane_sms, kv_len, case='frame'):
     """The `config` of the flashb arm's bench line."""
-    wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + greedy '
+    wl = {'frame': f'streaming frames: 28-layer backbone decode step (2 CFG rows per stream, KV 512+t) + '
                    f'codebook 0 sampled on the device (repetition penalty 1.1, T 0.9, top-k 50) + 16-codebook depth '
                    f'frame (4 layers, V 2048, CFG 4, top-k 50, T 0.9; fresh Exp(1) draws every frame); '
                    f'{a.group} stream(s) per depth launch share the weight reads; {lanes} lane(s) of the GPU side '
@@ -228,7 +230,9 @@ def frame_config(a, world, my_streams, lanes, shared, lane_sms, kv_len, case='fr
                 cb0='sampled on the device: the reference runtime\'s backbone sampler (repetition penalty 1.1 over '
                     'the stream\'s earlier codebook-0 tokens, reserved ids suppressed, T 0.9, top-k 50, top-p 1.0, '
                     'multinomial on fresh Exp(1) draws, validity flag)',
-                prefill='not timed (random prompt KV)')
+                prefill='not timed (random prompt KV)',
+                depth_step_table=bool(a.step_table), depth_weights='LN12 (12-bit, decoded in shared memory)' if a.ln12
+                else 'bf16')
 
 
 def run_reference(a):
@@ -625,6 +629,8 @@ def main():
                       lanes=lanes, shared_backbone=shared)
     if a.step_table:
         eng.use_step_table(True)
+    if a.ln12:
+        eng.use_ln12(True)
     eng.capture()
     stream = torch.cuda.current_stream(dev)
 
@@ -697,7 +703,7 @@ def main():
         last[s_.cuda_stream] = None if kind in ('end', 'bbend') else (kind, e)
     kv1 = int(eng.streams[0].bb.cache_position.item()) + 1 if eng.streams[0].bb is not None else 0
     pk = peaks()
-    dd_bytes = dcfg.frame_weight_bytes(eng.step_table is not None, 2 * a.group)
+    dd_bytes = dcfg.frame_weight_bytes(eng.step_table is not None, 2 * a.group, bool(a.ln12))
     bb_rows = 2 * a.group * (S if eng.shared else 1)      # rows of one backbone graph
     bb_bytes = backbone_step_bytes(bcfg, bb_rows, (kv0 + kv1) // 2)
     roof = None

@@ -113,6 +113,50 @@ int tmap_box(CUtensorMap* out, const void* base, long long rows, int K, int inne
   return FB_OK;
 }
 
+int tmap_ln12(CUtensorMap* out, const void* data, long long N, int K, int box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  static std::map<std::tuple<uintptr_t, long long, int, int>, CUtensorMap> cache;
+  static std::mutex mu;
+  if (!data || N < 1 || N > (1ll << 31) || K < 1024 || K % 1024 || box_rows < 1 || box_rows > 256 ||
+      (reinterpret_cast<uintptr_t>(data) & 15)) {
+    set_msg("LN12 tensor map: bad matrix (N %lld, K %d, box rows %d, data %p)", N, K, box_rows, data);
+    return FB_ERR_ARG;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(data), N, K, box_rows);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return FB_OK;
+  }
+  if (!enc) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn) {
+      set_msg("tensor map: cuTensorMapEncodeTiled unavailable");
+      return FB_ERR_CUDA;
+    }
+    enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  CUtensorMap m;
+  std::memset(&m, 0, sizeof(m));
+  const cuuint64_t G = (cuuint64_t)(K / 1024);
+  const cuuint64_t dims[4] = {512, 3, G, (cuuint64_t)N};
+  const cuuint64_t strides[3] = {512, 1536, 1536 * G};                  // bytes: next slot, next group, next row
+  const cuuint32_t box[4] = {128, 3, 1, (cuuint32_t)box_rows};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(data), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_msg("LN12 tensor map: cuTensorMapEncodeTiled failed (%d) for N %lld, K %d", (int)r, N, K);
+    return FB_ERR_CUDA;
+  }
+  cache.emplace(key, m);
+  *out = m;
+  return FB_OK;
+}
+
 int grid_sms() {
   const int n = num_sms();
   return (t_sm_budget > 0 && t_sm_budget < n) ? t_sm_budget : n;

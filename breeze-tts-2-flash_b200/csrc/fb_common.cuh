@@ -183,6 +183,11 @@ int tmap_rows(CUtensorMap* out, const void* base, long long rows, int K, int kc)
 // box_rows rows x box_blocks blocks of `inner` columns, 128-byte swizzle (inner = 64) or none.
 int tmap_box(CUtensorMap* out, const void* base, long long rows, int K, int inner, int box_rows, int box_blocks,
              bool swizzle128, long long ld = 0);  // num_sms(), or the calling thread's SM budget when one is set (flashb_set_sm_budget)
+// Tensor map of an LN12 matrix's data bytes (N rows, K % 1024 == 0): per row and 1024-column group three 512-byte
+// slots (low bytes of chunks 0-1, of chunks 2-3, the nibble words), viewed as [N][K / 1024][3][512 B]; boxes of
+// box_rows rows x 3 slots x 128 bytes (the 8 lanes of one lane octet: 256 columns of the group).  Cached per
+// (base, N, K, box_rows).
+int tmap_ln12(CUtensorMap* out, const void* data, long long N, int K, int box_rows);
 }  // namespace fbh
 
 #define FB_CHECK_ARG(cond, ...)          \

@@ -52,6 +52,17 @@ struct DDLayer {
   const bf16 *ln1, *wq, *wk, *wv, *wo, *ln2, *wg, *wu, *wd;
 };
 
+// LN12 streaming (tcgen05 build): a depth matrix in the lossless 12-bit format -- its data bytes behind a tensor map
+// (fbh::tmap_ln12), the 16-byte row records (header, three inline patches), the overflow patches and their count,
+// the 8-entry exponent table as two words.
+constexpr int DD_MAXH = 31;           // codebook heads (n_decode <= 31)
+struct LNMat {
+  const uint4* meta;
+  const unsigned* ovf;
+  long long novf;
+  unsigned lo, hi;
+};
+
 struct alignas(64) DDArgs {
   CUtensorMap tm_proj, tm_head;           // projector [H, AE]; codebook heads [n_decode * V, H]
   CUtensorMap tm[DD_MAXL][DD_NMAPS];      // per layer: wq, wk, wv, wo, wg, wu, wd
@@ -80,7 +91,11 @@ struct alignas(64) DDArgs {
   int l2_keep;                            // 1: weight copies carry the L2 evict_last hint
   unsigned* err;
   unsigned long long* trace;
+  int ln12;                               // 1: tm / tm_proj / tm_hd map LN12 data (tcgen05 build)
+  LNMat ln[DD_MAXL][DD_NMAPS], ln_proj, ln_hd[DD_MAXH];
+  CUtensorMap tm_hd[DD_MAXH];             // LN12: one map per codebook head [V, H]
 };
+static_assert(sizeof(DDArgs) <= 32764, "the depth frame's argument block exceeds the kernel parameter limit");
 
 // Optional trace: thread 0 of each CTA stamps %globaltimer at the end of every task and barrier of step s
 // (row layout [grid][n_decode][11 + 9 * layers]: start, E, barrier, 9 per layer, head, barrier, 6 sampler phases).
@@ -603,6 +618,22 @@ __shared__ long long g_dd_tok[DD_MAXB];            // tokens fed to the next ste
 __shared__ __align__(16) bf16 g_dd_cs[2][128];     // [cos|sin][dim] of the sub-step's position
 __shared__ uint32_t g_dd_tmem;                     // tcgen05 build: TMEM base of the accumulators
 __shared__ __align__(8) uint64_t g_dd_mbar;        // tcgen05 build: "the MMAs issued so far are complete"
+// LN12 streaming: per ring slot, the decoded stage is ready (one arrival per decoder warp), and what the producer
+// tells the decoders about the slot's copy (published by its arrive on the slot's full barrier)
+struct LNSlot {
+  unsigned lo, hi;
+  const unsigned* ovf;
+  long long novf;
+  int g, q;
+};
+__shared__ __align__(8) uint64_t g_dd_dfull[FB_PK_MAX_STAGES];
+__shared__ LNSlot g_dd_lnslot[FB_PK_MAX_STAGES];
+constexpr int LN_ROWS = 64;                        // rows per LN12 stage (the MMA's M)
+constexpr int LN_META_OFF = 7168;                  // the rows' 16-byte records, inside the slot
+constexpr int LN_DATA_OFF = 8192;                  // the rows' data: [64 rows][3 slots][128 B]
+constexpr int LN_DATA_BYTES = LN_ROWS * 384;
+constexpr int LN_DEC_WARPS = 7;                    // consumer warps 1-7 decode while warp 0 issues the MMAs
+constexpr int LN_DEC_BAR = 7;                      // their named barrier
 
 struct DDSm {
   unsigned char* xs;
@@ -617,14 +648,14 @@ template <int NT>
 __device__ __forceinline__ DDSm dd_smem(const DDArgs& a) {
   extern __shared__ __align__(128) unsigned char smem[];
   DDSm m;
-  m.xs = NT ? smem
+  m.xs = (NT > 0) ? smem
             : reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem) + 1023) & ~uintptr_t(1023));
   m.zero16 = m.xs + a.xs_bytes;
   unsigned char* ringb = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(m.zero16 + 128) + (ST_ALIGN - 1)) & ~uintptr_t(ST_ALIGN - 1));
   m.red = reinterpret_cast<float*>(ringb + (size_t)a.nstages * ST_BYTES);
-  m.sums = m.red + (NT ? ST_CWARPS * 128 * NT : DD_TC_SUMS);
-  uint64_t* full = reinterpret_cast<uint64_t*>(m.sums + 128 * NT);
+  m.sums = m.red + ((NT > 0) ? ST_CWARPS * 128 * NT : DD_TC_SUMS);
+  uint64_t* full = reinterpret_cast<uint64_t*>(m.sums + 128 * (NT > 0 ? NT : 0));
   m.rg = Ring{ringb, full, full + PK_MAX_STAGES, a.nstages, &g_dd_int[28]};
   return m;
 }
@@ -646,13 +677,20 @@ struct DDCur {
 // rotary pair units, rows d and d + 64 of the head).  64-row blocks spread the 1024-row matrices of the depth
 // model over 16 CTAs instead of 8; the 4096-row gate|up task keeps 128-unit blocks (fewer per-block epilogues).  A stage is 32 KB of weights in the canonical K-major 128-byte-swizzle layout, streamed by
 // the producer warp with one (KIND 1: two) TMA tensor copies; CTA c owns blocks [nb c / G, nb (c + 1) / G).
+//
+// LN12 streaming (DDArgs::ln12): every stage is 64 rows of one matrix x one lane octet q of one 1024-column group g,
+// i.e. columns 1024 g + 256 c + 64 q + (0..63) of the four chunks c: the producer copies the 24 KB of LN12 data
+// ([64 rows][3 slots][128 B], one tensor copy) and the rows' 1 KB of records into the slot's upper part, consumer
+// warps 1-7 decode them into the slot as four 64-column strips [64 rows][128 B] (128-byte swizzle), and warp 0
+// runs M = 64 MMAs over the strips.  Blocks are 64 units for every kind; KIND 1 alternates gate / up stages and
+// KIND 2 the head's rows 0-63 / 64-127 per K slice, into two accumulators.
 template <int KIND>
 constexpr int tc_cols() { return KIND == 0 ? 256 : (KIND == 1 ? 64 : 128); }   // columns per stage
 template <int KIND>
-constexpr int tc_units() { return KIND == 1 ? 128 : 64; }                      // output units per block
+__device__ __forceinline__ int tc_units(bool ln) { return (KIND == 1 && !ln) ? 128 : 64; }   // units per block
 template <int KIND>
-__device__ __forceinline__ void tc_task_blocks(int units, int& b0, int& b1) {
-  constexpr int UB = tc_units<KIND>();
+__device__ __forceinline__ void tc_task_blocks(int units, int& b0, int& b1, bool ln) {
+  const int UB = tc_units<KIND>(ln);
   const int nb = (units + UB - 1) / UB;
   b0 = (int)((long long)nb * blockIdx.x / gridDim.x);
   b1 = (int)((long long)nb * (blockIdx.x + 1) / gridDim.x);
@@ -672,18 +710,64 @@ __device__ __forceinline__ void tma_load_3d_l2(void* dst, const void* tmap, int 
       : "memory");
 }
 
-template <int KIND, typename SrcFn>
+__device__ __forceinline__ void tma_load_4d_l2(void* dst, const void* tmap, int c0, int c1, int c2, int c3,
+                                               uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+      "{%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Source of a block's rows: the tensor map, the first row, and (LN12 streaming) the matrix's records.
+struct DDSrc {
+  const void* map;
+  int row;
+  const LNMat* ln;
+};
+
+template <int KIND, bool ln, typename SrcFn>
 __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int K, SrcFn src, unsigned* err) {
-  constexpr int UB = tc_units<KIND>();
   constexpr int C = tc_cols<KIND>();
+  const int UB = tc_units<KIND>(ln);
   const int lane = threadIdx.x & 31;
   const uint64_t pol = g_dd_l2keep ? policy_evict_last() : policy_evict_normal();
   int b0, b1;
-  tc_task_blocks<KIND>(units, b0, b1);
+  tc_task_blocks<KIND>(units, b0, b1, ln);
+  if constexpr (ln) {
+    // per K slice (g, q): one stage per matrix of the block (KIND 1: gate, up; KIND 2: the head's two row halves)
+    constexpr int NM = KIND == 0 ? 1 : 2;
+    const int nks = K >> 8;
+    for (int bi = b0; bi < b1; ++bi) {
+      for (int kc = 0; kc < nks; ++kc) {
+        for (int mm = 0; mm < NM; ++mm, ++t) {
+          const int s = t % rg.nst;
+          if (t >= rg.nst && !ring_wait_empty(rg, s, ((t / rg.nst) - 1) & 1, err)) return false;
+          if (lane == 0) {
+            const DDSrc w = src(bi * UB, KIND == 1 ? mm : 0);
+            const int row = w.row + (KIND == 2 ? LN_ROWS * mm : 0);
+            LNSlot& inf = g_dd_lnslot[s];
+            inf.lo = w.ln->lo;
+            inf.hi = w.ln->hi;
+            inf.ovf = w.ln->ovf;
+            inf.novf = w.ln->novf;
+            inf.g = kc >> 2;
+            inf.q = kc & 3;
+            unsigned char* st = rg.base + (size_t)s * ST_BYTES;
+            mbar_arrive_expect_tx(&rg.full[s], (unsigned)(LN_DATA_BYTES + LN_ROWS * 16));
+            tma_load_4d_l2(st + LN_DATA_OFF, w.map, (kc & 3) * 128, 0, kc >> 2, row, &rg.full[s], pol);
+            bulk_g2s(st + LN_META_OFF, w.ln->meta + row, LN_ROWS * 16, &rg.full[s]);
+          }
+          __syncwarp();
+        }
+      }
+    }
+    return true;
+  }
   const int nkc = (K + C - 1) / C;
   for (int bi = b0; bi < b1; ++bi) {
-    const TmaRows w0 = src(bi * UB, 0);
-    const TmaRows w1 = KIND == 1 ? src(bi * UB, 1) : TmaRows{nullptr, 0};
+    const DDSrc w0 = src(bi * UB, 0);
+    const DDSrc w1 = KIND == 1 ? src(bi * UB, 1) : DDSrc{nullptr, 0, nullptr};
     for (int kc = 0; kc < nkc; ++kc, ++t) {
       const int s = t % rg.nst;
       if (t >= rg.nst && !ring_wait_empty(rg, s, ((t / rg.nst) - 1) & 1, err)) return false;
@@ -705,6 +789,89 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
   return true;
 }
 
+// LN12 decode of stages t0 .. t0 + nk - 1 by consumer warps 1-7 (224 threads): wait for the slot's copy, read its
+// 64 rows x 8 lanes items (16 bytes of each of the three slots, the row record) into registers, meet (the decoded
+// strips overwrite the copied bytes), rebuild each bf16 -- high byte = the row's shifted table entry of the 3-bit
+// index (a byte permute over the two table words) with the sign, low byte as stored; then the row's patches that fall
+// in the item's 32 columns -- and store 16 bytes per chunk into the strips; then publish to the async proxy and
+// arrive on the slot's decoded barrier.  A failed wait still decodes (shared memory only; overflow patch reads are
+// bounded by the matrix's count) and arrives, so nobody waits in vain, and raises the abort flag.
+__device__ __noinline__ void ln12_decode_stages(const Ring& rg, int t0, int nk, unsigned* err, int* abort_flag) {
+  const int dt = threadIdx.x - 32;
+  const int lane = threadIdx.x & 31;
+  for (int i = 0; i < nk; ++i) {
+    const int t = t0 + i, s = t % rg.nst;
+    if (!mbar_wait(&rg.full[s], (t / rg.nst) & 1, err)) *abort_flag = 1;
+    unsigned char* st = rg.base + (size_t)s * ST_BYTES;
+    const LNSlot inf = g_dd_lnslot[s];
+    uint4 r0[3], r1[3], rw[3], mt[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int it = dt + 32 * LN_DEC_WARPS * k;
+      if (it < LN_ROWS * 8) {
+        const int r = it >> 3, l = it & 7;
+        const unsigned char* rp = st + LN_DATA_OFF + r * 384 + l * 16;
+        r0[k] = *reinterpret_cast<const uint4*>(rp);
+        r1[k] = *reinterpret_cast<const uint4*>(rp + 128);
+        rw[k] = *reinterpret_cast<const uint4*>(rp + 256);
+        mt[k] = *reinterpret_cast<const uint4*>(st + LN_META_OFF + r * 16);
+      }
+    }
+    named_sync(LN_DEC_BAR, 32 * LN_DEC_WARPS);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int it = dt + 32 * LN_DEC_WARPS * k;
+      if (it < LN_ROWS * 8) {
+        const int r = it >> 3, l = it & 7;
+        const unsigned hdr = mt[k].x;
+        const unsigned sb = (((hdr >> 10) & 7u) ^ 4u) - 4u;        // the row's table shift, -4 .. 3
+        const unsigned add = (sb & 0xFFu) * 0x01010101u;
+        const unsigned lo = __vadd4(inf.lo, add), hi = __vadd4(inf.hi, add);
+        const unsigned w[4] = {rw[k].x, rw[k].y, rw[k].z, rw[k].w};
+        unsigned H[4][2];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          H[c][0] = __byte_perm(lo, hi, w[c] & 0x7777u) | (w[c] & 0x80808080u);
+          H[c][1] = __byte_perm(lo, hi, (w[c] >> 16) & 0x7777u) | ((w[c] << 4) & 0x80808080u);
+        }
+        const unsigned a0[4] = {r0[k].x, r0[k].z, r1[k].x, r1[k].z};   // low bytes of elements 0-3 per chunk
+        const unsigned a1[4] = {r0[k].y, r0[k].w, r1[k].y, r1[k].w};   // elements 4-7
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 o;
+          o.x = __byte_perm(a0[c], H[c][0], 0x5140);
+          o.y = __byte_perm(a0[c], H[c][0], 0x7362);
+          o.z = __byte_perm(a1[c], H[c][1], 0x5140);
+          o.w = __byte_perm(a1[c], H[c][1], 0x7362);
+          *reinterpret_cast<uint4*>(st + c * 8192 + r * 128 + ((l ^ (r & 7)) << 4)) = o;
+        }
+        // the row's patches in this item's columns: the exact high byte, over what this thread just stored
+        const unsigned cnt = hdr & 1023u;
+        if (cnt) {
+          const long long ooff = (long long)(hdr >> 13);
+          const unsigned lane_g = (unsigned)(inf.q * 8 + l);
+          for (unsigned pi = 0; pi < cnt; ++pi) {
+            unsigned v;
+            if (pi < 3) {
+              v = pi == 0 ? mt[k].y : (pi == 1 ? mt[k].z : mt[k].w);
+            } else {
+              const long long o = ooff + (long long)pi - 3;
+              if (o >= inf.novf) break;
+              v = __ldg(inf.ovf + o);
+            }
+            const unsigned col = v >> 8;
+            if ((int)(col >> 10) == inf.g && ((col >> 3) & 31u) == lane_g)
+              st[((col >> 8) & 3u) * 8192 + r * 128 + ((l ^ (r & 7)) << 4) + 2 * (col & 7u) + 1] = (unsigned char)v;
+          }
+        }
+      }
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&g_dd_dfull[s]);
+  }
+}
+
 // Consumer half (all 256 consumer threads).  The activations of the first K pass are staged at xs (B-operand
 // layout) by the caller; stage_x(p) restages pass p (K > DD_TC_KX, or a further block).  Consumer warp 0 waits for
 // the stages and its lane 0 issues the MMAs (four independent accumulator chains per matrix, summed in a fixed
@@ -713,16 +880,17 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
 // (KIND 0: 16 units; KIND 1 and 2: rows 0-7 the 8 units' matrix-0 rows, 8-15 their matrix-1 rows), and every thread
 // runs epi(n0, nu, group) per group.  A failed wait in warp 0 still commits (so nobody else waits in vain) and is
 // reported to every thread through shared memory after the next barrier.
-template <int KIND, typename EpiFn, typename StageFn>
+template <int KIND, bool ln, typename EpiFn, typename StageFn>
 __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, int K, const unsigned char* xs,
                                                 float* dump, EpiFn epi, StageFn stage_x, unsigned* err,
                                                 unsigned long long* det) {
-  constexpr int UB = tc_units<KIND>();
   constexpr int C = tc_cols<KIND>();
   constexpr int GU = KIND == 0 ? 16 : 8;                       // units per group
+  constexpr int NM = KIND == 0 ? 1 : 2;                        // LN12: stages per K slice
+  const int UB = tc_units<KIND>(ln);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int b0, b1;
-  tc_task_blocks<KIND>(units, b0, b1);
+  tc_task_blocks<KIND>(units, b0, b1, ln);
   const int KX = K < DD_TC_KX ? K : DD_TC_KX;
   const int npass = (K + KX - 1) / KX;
   const int ncp = KX / C;                                      // stages per pass
@@ -742,15 +910,29 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
         fence_proxy_async();
         named_sync(1, PK_CONSUMERS);
       }
-      const int nk = min(ncp, (K - p * KX + C - 1) / C);
+      const int nk = ln ? (min(KX, K - p * KX) >> 8) * NM : min(ncp, (K - p * KX + C - 1) / C);
       if (warp == 0) {
         tc_after();
         for (int kcp = 0; kcp < nk; ++kcp) {
           const int t = c.t + kcp, s = t % rg.nst;
-          const bool ok = mbar_wait_warp(&rg.full[s], (t / rg.nst) & 1, err);
+          const bool ok = mbar_wait_warp(ln ? &g_dd_dfull[s] : &rg.full[s], (t / rg.nst) & 1, err);
           if (det && lane == 0 && bi == b0 && p == 0 && kcp == 0) det[1] = globaltimer();
           if (!ok && lane == 0) *abort_flag = 1;
-          if (lane == 0 && ok) {
+          if (lane == 0 && ok && ln) {
+            // LN12 stage: K slice ks of the pass (1024 (ks / 4) + 256 c + 64 (ks % 4) + 0..63 for strips c = 0..3),
+            // matrix mm; M = 64 MMAs, chain jj = the 16-column step within the strip
+            const uint32_t wa = smem_u32(rg.base + (size_t)s * ST_BYTES);
+            const int ks = kcp / NM, mm = kcp - ks * NM;
+            const uint32_t dcol = tmem + (uint32_t)(mm * 64);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int cs = j >> 2, jj = j & 3;
+              const int blk = ((ks >> 2) << 4) + (cs << 2) + (ks & 3);     // 64-column block of the staged pass
+              const uint64_t bd = tc_desc_sw128(xsa + (uint32_t)(blk << 11) + (uint32_t)(jj << 5));
+              const uint32_t acc = (p > 0 || ks > 0 || cs > 0) ? 1u : 0u;
+              tc_mma16_m64(dcol + (uint32_t)(jj * 16), tc_desc_sw128(wa + (uint32_t)(cs * 8192 + jj * 32)), bd, acc);
+            }
+          } else if (lane == 0 && ok) {
             const uint32_t wa = smem_u32(rg.base + (size_t)s * ST_BYTES);
 #pragma unroll
             for (int j = 0; j < C / 16; ++j) {
@@ -778,6 +960,8 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
         if (det && lane == 0 && bi == b0) det[2] = globaltimer();
         if (lane == 0) tc_commit(&g_dd_mbar);
         __syncwarp();
+      } else if constexpr (ln) {
+        ln12_decode_stages(rg, c.t, nk, err, abort_flag);
       }
       c.t += nk;
       // the pass's MMAs are complete: the staged activations may be replaced, the accumulators read
@@ -790,7 +974,27 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
     // in lane (r % 16) of quarter r / 16, so warp q's lanes 0-15 hold rows 16 q ..; KIND 1 and 2 (M = 128): row =
     // lane of the 128.  KIND 1 goes in two rounds of 64 units (8 groups each) through the 8-group dump.
     float kg1[16], ku1[16];                                    // KIND 1, warps 2-3: their units for round 2
-    if (warp < 4) {
+    if constexpr (ln && KIND != 0) {
+      // LN12, two M = 64 accumulators (matrix 0 at column 0, matrix 1 at 64): unit d = 16 warp + lane (lanes 0-15)
+      if (warp < 4) {
+        const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
+        const int d = warp * 16 + (lane & 15);
+        float* g = dump + (d >> 3) * 256 + (d & 7) * 16;
+        for (int mm = 0; mm < 2; ++mm) {
+          float c0[16], c1[16], v[16];
+          tc_ld16(tq + mm * 64, c0);
+          tc_ld16(tq + mm * 64 + 16, c1);
+#pragma unroll
+          for (int m = 0; m < 16; ++m) v[m] = c0[m] + c1[m];
+          tc_ld16(tq + mm * 64 + 32, c0);
+          tc_ld16(tq + mm * 64 + 48, c1);
+          if (lane < 16) {
+#pragma unroll
+            for (int m = 0; m < 16; ++m) g[mm * 128 + m] = (v[m] + c0[m]) + c1[m];
+          }
+        }
+      }
+    } else if (warp < 4) {
       const int L = warp * 32 + lane;
       const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
       float c0[16], c1[16], v[16];
@@ -834,7 +1038,7 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
     named_sync(1, PK_CONSUMERS);
     if (det && threadIdx.x == 0 && bi == b0) det[4] = globaltimer();
     if (*abort_flag) return false;
-    if (KIND == 1) {
+    if (KIND == 1 && !ln) {
       for (int g = 0; g < 8; ++g) {
         const int n0 = bi * UB + g * GU;
         const int nu = min(GU, units - n0);
@@ -879,13 +1083,13 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
 template <int NT, int KIND, typename EpiFn, typename StageFn>
 __device__ __forceinline__ bool dd_gemv(const DDArgs& a, DDSm& m, DDCur& c, int units, int K, int x_pitch, EpiFn epi,
                                         StageFn stage_x, const bf16* xg = nullptr, long ldx = 0) {
-  if constexpr (NT == 0) {
+  if constexpr (NT <= 0) {
     // trace builds: the first DD_DETAIL_CALLS tasks of each CTA record a detail timeline after the phase trace
     unsigned long long* det = nullptr;
     const int call = g_dd_call;
     if (a.trace && call < DD_DETAIL_CALLS)
       det = a.trace + (size_t)gridDim.x * a.NCB * DD_TRACE_SLOTS(a.L) + ((size_t)blockIdx.x * DD_DETAIL_CALLS + call) * 8;
-    const bool ok = consume_task_tc<KIND>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err, det);
+    const bool ok = consume_task_tc<KIND, (NT < 0)>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err, det);
     if (threadIdx.x == 0) g_dd_call = call + 1;
     return ok;
   } else {
@@ -908,15 +1112,19 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
     const int lane = threadIdx.x & 31;
     for (int i = lane; i < 2 + DD_NMAPS * L; i += 32)
       tma_prefetch_map(i == 0 ? &a.tm_proj : (i == 1 ? &a.tm_head : &a.tm[(i - 2) / DD_NMAPS][(i - 2) % DD_NMAPS]));
+    if (a.ln12)
+      for (int i = lane; i < NCB; i += 32) tma_prefetch_map(&a.tm_hd[i]);
   }
+  constexpr bool ln = NT < 0;
   int t = 0;
   bool ok = true;
   for (int s = 0; s < NCB && ok; ++s) {
     const bool tab = a.ptab && s >= 1;     // stage E and layer 0's q|k|v come from the step table
     for (int sub = 0; sub < (s == 0 ? 2 : 1) && ok; ++sub) {
-      if constexpr (NT == 0) {
+      if constexpr (NT <= 0) {
         if (!tab)
-          ok = ok && produce_task_tc<0>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
+          ok = ok && produce_task_tc<0, ln>(m.rg, t, H, AE, [&](int n, int) { return DDSrc{&a.tm_proj, n, &a.ln_proj}; },
+                                        err);
       } else {
         if (!tab)
           ok = ok && produce_task_tma<1>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
@@ -924,18 +1132,22 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
       for (int l = 0; l < L && ok; ++l) {
         const CUtensorMap* W = a.tm[l];
         const bool skip_qkv = tab && l == 0;
-        if constexpr (NT == 0) {
+        if constexpr (NT <= 0) {
           // one head per block: rows hh * 128 .. + 127 of wq / wk / wv
-          if (!skip_qkv) ok = ok && produce_task_tc<2>(m.rg, t, QKVU, H, [&](int u, int) {
+          const LNMat* LW = a.ln[l];
+          if (!skip_qkv) ok = ok && produce_task_tc<2, ln>(m.rg, t, QKVU, H, [&](int u, int) {
             const int hh = u >> 6;
-            if (hh < NH) return TmaRows{&W[DD_WQ], hh * 128};
-            if (hh < NH + NKV) return TmaRows{&W[DD_WK], (hh - NH) * 128};
-            return TmaRows{&W[DD_WV], (hh - NH - NKV) * 128};
+            if (hh < NH) return DDSrc{&W[DD_WQ], hh * 128, &LW[DD_WQ]};
+            if (hh < NH + NKV) return DDSrc{&W[DD_WK], (hh - NH) * 128, &LW[DD_WK]};
+            return DDSrc{&W[DD_WV], (hh - NH - NKV) * 128, &LW[DD_WV]};
           }, err);
-          ok = ok && produce_task_tc<0>(m.rg, t, H, NH * 128, [&](int n, int) { return TmaRows{&W[DD_WO], n}; }, err);
-          ok = ok && produce_task_tc<1>(m.rg, t, F, H,
-                                        [&](int n, int mat) { return TmaRows{&W[mat ? DD_WU : DD_WG], n}; }, err);
-          ok = ok && produce_task_tc<0>(m.rg, t, H, F, [&](int n, int) { return TmaRows{&W[DD_WD], n}; }, err);
+          ok = ok && produce_task_tc<0, ln>(m.rg, t, H, NH * 128,
+                                        [&](int n, int) { return DDSrc{&W[DD_WO], n, &LW[DD_WO]}; }, err);
+          ok = ok && produce_task_tc<1, ln>(m.rg, t, F, H, [&](int n, int mat) {
+            return DDSrc{&W[mat ? DD_WU : DD_WG], n, &LW[mat ? DD_WU : DD_WG]};
+          }, err);
+          ok = ok && produce_task_tc<0, ln>(m.rg, t, H, F, [&](int n, int) { return DDSrc{&W[DD_WD], n, &LW[DD_WD]}; },
+                                        err);
         } else {
           // unit u = (head hh, rotary pair d): matrix 0 carries row hh * 128 + d, matrix 1 row hh * 128 + 64 + d
           if (!skip_qkv) ok = ok && produce_task_tma<2>(m.rg, t, QKVU, H, [&](int u, int mat) {
@@ -951,8 +1163,10 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
         }
       }
     }
-    if constexpr (NT == 0) {
-      ok = ok && produce_task_tc<0>(m.rg, t, V, H, [&](int n, int) { return TmaRows{&a.tm_head, s * V + n}; }, err);
+    if constexpr (NT <= 0) {
+      ok = ok && produce_task_tc<0, ln>(m.rg, t, V, H, [&](int n, int) {
+        return ln ? DDSrc{&a.tm_hd[s], n, &a.ln_hd[s]} : DDSrc{&a.tm_head, s * V + n, nullptr};
+      }, err);
     } else {
       ok = ok && produce_task_tma<1>(m.rg, t, V, H, [&](int n, int) { return TmaRows{&a.tm_head, s * V + n}; }, err);
     }
@@ -965,10 +1179,10 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
 // E: gather the token embeddings (cp.async, one round trip, with the position's rotary rows) -> projector -> xres
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int sub, int pos) {
-  constexpr int MS = NT ? 8 * NT : 16;
+  constexpr int MS = (NT > 0) ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, AE = a.AE, H = a.H, V = a.V;
-  const int xp_ae = NT ? AE * 2 + 16 : 0;
+  const int xp_ae = (NT > 0) ? AE * 2 + 16 : 0;
   bf16* const xres = a.xres;   // locals: stores through them cannot alias the argument block
   DD_STAMP(s, 0);
   const int kv = AE >> 3;
@@ -1072,13 +1286,13 @@ __device__ __noinline__ DDCur dd_phase_tab(const DDArgs& a, DDCur c, int s, int 
 // S1: RMSNorm + q|k|v (rotary pairs) + RoPE + KV write at `pos`
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_s1(const DDArgs& a, DDCur c, int s, int pos, int l) {
-  constexpr int MS = NT ? 8 * NT : 16;
+  constexpr int MS = (NT > 0) ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, NH = a.NH, NKV = a.NKV, QD = NH * 128;
   const int tb = 3 + 9 * l;
   const int P = a.P;
   bf16 *const qb = a.qb, *const kcache = a.kc, *const vcache = a.vc;
-  const int xp = NT ? H * 2 + 16 : 0;
+  const int xp = (NT > 0) ? H * 2 + 16 : 0;
   load_x(m.xs, xp, a.xres, H, M, H, a.layers[l].ln1, a.eps, g_dd_nred);
   if (!dd_gemv<NT, 2>(a, m, c, (NH + 2 * NKV) * 64, H, xp,
                            [&](int n0, int nu, const float* sm) {
@@ -1119,10 +1333,10 @@ __device__ __noinline__ DDCur dd_phase_s1(const DDArgs& a, DDCur c, int s, int p
 // (batch row, KV head) pair i, writes it over its q slice, and a barrier precedes the o-projection.
 template <int G, int NT>
 __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int pos, int l) {
-  constexpr int MS = NT ? 8 * NT : 16;
+  constexpr int MS = (NT > 0) ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, NKV = a.NKV, QD = a.NH * 128;
-  const int xp_q = NT ? QD * 2 + 16 : 0;
+  const int xp_q = (NT > 0) ? QD * 2 + 16 : 0;
   const int tb = 3 + 9 * l;
   bf16* const ob = a.ob;
   if (a.att_split) {
@@ -1158,13 +1372,13 @@ __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int p
 // S3: RMSNorm(bf16(x + o)) + gate|up + SiLU*up; the un-normalised x_mid rows stay in shared memory for S4
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l) {
-  constexpr int MS = NT ? 8 * NT : 16;
+  constexpr int MS = (NT > 0) ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, F = a.F;
   const int tb = 3 + 9 * l;
   bf16* xkeep = reinterpret_cast<bf16*>(m.xs + a.keep_off);
   bf16* const act = a.act;
-  const int xp = NT ? H * 2 + 16 : 0;
+  const int xp = (NT > 0) ? H * 2 + 16 : 0;
   dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep);
   if (!dd_gemv<NT, 1>(a, m, c, F, H, xp,
                       [&](int n0, int nu, const float* sm) {
@@ -1187,7 +1401,7 @@ __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l
 // S4: down + residual: xres = bf16(x_mid + bf16(d)); act rows too large to stage whole go in column chunks
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l) {
-  constexpr int MS = NT ? 8 * NT : 16;
+  constexpr int MS = (NT > 0) ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, F = a.F;
   const int tb = 3 + 9 * l;
@@ -1198,7 +1412,7 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
     const int k0 = p * DD_TC_KX;
     load_x(m.xs, 0, a.act + k0, F, M, min(DD_TC_KX, F - k0), nullptr, 0.f, g_dd_nred);
   };
-  if (NT == 0) stage(0);
+  if (NT <= 0) stage(0);
   else if (!a.d_xchunk) load_x(m.xs, F * 2 + 16, a.act, F, M, F, nullptr, 0.f, g_dd_nred);
   if (!dd_gemv<NT, 0>(a, m, c, H, F, a.d_xchunk ? ST_KC * 2 + 16 : F * 2 + 16,
                       [&](int n0, int nu, const float* sm) {
@@ -1220,12 +1434,12 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
 // S5: final RMSNorm + codebook head -> fp32 logits
 template <int NT>
 __device__ __noinline__ DDCur dd_phase_s5(const DDArgs& a, DDCur c, int s) {
-  constexpr int MS = NT ? 8 * NT : 16;
+  constexpr int MS = (NT > 0) ? 8 * NT : 16;
   DDSm m = dd_smem<NT>(a);
   const int tid = threadIdx.x, M = a.B, H = a.H, V = a.V;
   const int te = 3 + 9 * a.L;
   float *const logits = a.logits, *const dbg = a.dbg;
-  const int xp = NT ? H * 2 + 16 : 0;
+  const int xp = (NT > 0) ? H * 2 + 16 : 0;
   load_x(m.xs, xp, a.xres, H, M, H, a.normf, a.eps, g_dd_nred);
   if (!dd_gemv<NT, 0>(a, m, c, V, H, xp,
                       [&](int n0, int nu, const float* sm) {
@@ -1295,20 +1509,21 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
     if (tid == 0) {
       for (int s = 0; s < m.rg.nst; ++s) {
         mbar_init(&m.rg.full[s], 1);
-        mbar_init(&m.rg.empty[s], NT ? ST_CWARPS : 1);   // tcgen05 build: released by one tcgen05.commit
+        mbar_init(&m.rg.empty[s], (NT > 0) ? ST_CWARPS : 1);   // tcgen05 build: released by one tcgen05.commit
+        if (NT < 0) mbar_init(&g_dd_dfull[s], LN_DEC_WARPS);
       }
-      if (NT == 0) mbar_init(&g_dd_mbar, 1);
+      if (NT <= 0) mbar_init(&g_dd_mbar, 1);
       fence_mbar_init();
     }
     if (tid < 32) reinterpret_cast<uint32_t*>(m.zero16)[tid] = 0u;
     if (tid == 0) g_dd_int[28] = 0;                         // the consumers' "stopped early" flag
     if (tid == 0) g_dd_call = 0;
     if (tid == 0) g_dd_l2keep = a.l2_keep;
-    if (NT == 0 && warp == 0) tc_alloc(&g_dd_tmem, 64);   // 4 accumulator chains x 16 columns
+    if (NT <= 0 && warp == 0) tc_alloc(&g_dd_tmem, NT < 0 ? 128 : 64);  // 4 chains x 16 columns (LN12: x 2)
   }
-  if (NT == 0) tc_before();
+  if (NT <= 0) tc_before();
   __syncthreads();
-  if (NT == 0) tc_after();
+  if (NT <= 0) tc_after();
   if (warp == ST_CWARPS) {
     dd_producer<NT>(a);
     return;
@@ -1337,12 +1552,12 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
     *reinterpret_cast<volatile int*>(&g_dd_int[28]) = 1;
     __threadfence_block();
   }
-  if (NT == 0) {
+  if (NT <= 0) {
     // every MMA of this CTA has completed (each task waits for its last commit); free the accumulators
     tc_before();
     named_sync(1, PK_CONSUMERS);
     tc_after();
-    if (warp == 0) tc_dealloc(g_dd_tmem, 64);
+    if (warp == 0) tc_dealloc(g_dd_tmem, NT < 0 ? 128 : 64);
   }
   if (c.ok) grid_exit(a.bar);
 }
@@ -1510,7 +1725,8 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   const int QD = c->heads * 128, KD = c->kv_heads * 128;
   const bool tc = grid <= DD_TC_MAX_GRID && c->hidden % 256 == 0 && c->embed_dim % 256 == 0 && c->ffn % 256 == 0 &&
                   QD % 256 == 0;
-  const int NT = tc ? 0 : (c->batch > 8 ? 2 : 1);
+  // NT = -1: the tcgen05 build streaming LN12 (fb_dd_config.ln12; set up below)
+  const int NT = tc ? (c->ln12 ? -1 : 0) : (c->batch > 8 ? 2 : 1);
   {
     // tensor maps of every streamed matrix, built from the host copy of the layer table (cached per matrix):
     // mma.sync build: 8-row boxes of ST_KC columns.  tcgen05 build: the stage of the task's kind, 64 rows x 256
@@ -1533,6 +1749,38 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
       if (!rc) rc = map(&a.tm[l][DD_WD], W.wd, c->hidden, c->ffn, 0);
     }
     if (rc) return rc;
+  }
+  if (tc && c->ln12) {
+    // LN12 streaming: the data maps replace the bf16 ones (64-row boxes); records, patches and tables per matrix
+    FB_CHECK_ARG(c->hidden % 1024 == 0 && c->embed_dim % 1024 == 0 && c->ffn % 1024 == 0 && QD % 1024 == 0 &&
+                     c->vocab % 64 == 0 && KD % 64 == 0,
+                 "dd_frame: LN12 streaming needs hidden, embed_dim, ffn, heads x 128 multiples of 1024 and vocab, "
+                 "kv_heads x 128 multiples of 64");
+    auto lnm = [&](int i, CUtensorMap* tm, LNMat* out, long long N, int K) {
+      const fb_ln12_mat& e = c->ln12[i];
+      if (!e.data || !e.meta || (reinterpret_cast<uintptr_t>(e.meta) & 15) || (!e.ovf && e.n_ovf > 0) || e.n_ovf < 0) {
+        fbh::set_msg("dd_frame: LN12 matrix %d: null or misaligned pointers", i);
+        return (int)FB_ERR_ARG;
+      }
+      *out = LNMat{(const uint4*)e.meta, (const unsigned*)e.ovf, (long long)e.n_ovf, e.lut_lo, e.lut_hi};
+      return fbh::tmap_ln12(tm, e.data, N, K, LN_ROWS);
+    };
+    int rc = 0;
+    for (int l = 0; l < c->layers && !rc; ++l) {
+      const int i0 = l * DD_NMAPS;
+      rc = lnm(i0 + DD_WQ, &a.tm[l][DD_WQ], &a.ln[l][DD_WQ], QD, c->hidden);
+      if (!rc) rc = lnm(i0 + DD_WK, &a.tm[l][DD_WK], &a.ln[l][DD_WK], KD, c->hidden);
+      if (!rc) rc = lnm(i0 + DD_WV, &a.tm[l][DD_WV], &a.ln[l][DD_WV], KD, c->hidden);
+      if (!rc) rc = lnm(i0 + DD_WO, &a.tm[l][DD_WO], &a.ln[l][DD_WO], c->hidden, QD);
+      if (!rc) rc = lnm(i0 + DD_WG, &a.tm[l][DD_WG], &a.ln[l][DD_WG], c->ffn, c->hidden);
+      if (!rc) rc = lnm(i0 + DD_WU, &a.tm[l][DD_WU], &a.ln[l][DD_WU], c->ffn, c->hidden);
+      if (!rc) rc = lnm(i0 + DD_WD, &a.tm[l][DD_WD], &a.ln[l][DD_WD], c->hidden, c->ffn);
+    }
+    const int ip = c->layers * DD_NMAPS;
+    if (!rc) rc = lnm(ip, &a.tm_proj, &a.ln_proj, c->hidden, c->embed_dim);
+    for (int h = 0; h < c->n_decode && !rc; ++h) rc = lnm(ip + 1 + h, &a.tm_hd[h], &a.ln_hd[h], c->vocab, c->hidden);
+    if (rc) return rc;
+    a.ln12 = 1;
   }
   // One buffer, several uses, sized for the largest:
   //   GEMV input rows of every phase (E: embed_dim, S1 / S3 / S5: hidden, S2: heads x 128; S4: ffn, whole or as
@@ -1618,6 +1866,15 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.nstages = nst;
   const size_t smem = fixed + (size_t)nst * slot;
   cudaStream_t st = (cudaStream_t)stream;
+  if (NT < 0) {
+    switch (G) {
+      case 1: return launch_dd<1, -1>(a, smem, grid, st);
+      case 2: return launch_dd<2, -1>(a, smem, grid, st);
+      case 4: return launch_dd<4, -1>(a, smem, grid, st);
+      case 8: return launch_dd<8, -1>(a, smem, grid, st);
+      default: fbh::set_msg("dd_frame: GQA group %d not built", G); return FB_ERR_UNSUPPORTED;
+    }
+  }
   const int key = G * 10 + NT;
   switch (key) {
     case 10: return launch_dd<1, 0>(a, smem, grid, st);

@@ -85,7 +85,13 @@ class FbDDConfig(ctypes.Structure):
                 ('head_dim', I), ('ffn', I), ('vocab', I), ('codebook_size', I), ('n_decode', I), ('eps', F),
                 ('scaling', F), ('embed', P), ('proj', P), ('normf', P), ('head_t', P), ('cos_tab', P),
                 ('sin_tab', P), ('trace', P), ('grid', I), ('layers_host', P), ('wait_ns', L), ('ptab', P),
-                ('ttab', P)]
+                ('ttab', P), ('ln12', P)]
+
+
+class FbLn12Mat(ctypes.Structure):
+    """fb_ln12_mat of include/flashb.h."""
+    _fields_ = [('data', P), ('meta', P), ('ovf', P), ('n_ovf', L), ('lut_lo', ctypes.c_uint32),
+                ('lut_hi', ctypes.c_uint32)]
 
 
 def lib_path():

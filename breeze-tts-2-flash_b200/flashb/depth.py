@@ -100,12 +100,36 @@ def tab_set(desc, pt, tt):
     c.ptab, c.ttab = pt.data_ptr(), tt.data_ptr()
 
 
+def ln12_set(desc, mats):
+    """Stream ``desc``'s matrices in LN12 (``fb_dd_config.ln12``; the tcgen05 build on grids <= 32 decodes them in
+    shared memory, other builds keep reading the bf16 matrices).  mats: per matrix (data uint8, meta int32 [N, 4],
+    ovf int32, (lut_lo, lut_hi)) on the device, in ``DepthOps.ln12_mats`` order; None turns it off."""
+    c = desc.cfg
+    if mats is None:
+        c.ln12 = None
+        desc.ln12 = None
+        return
+    n = c.layers * 7 + 1 + c.n_decode
+    if len(mats) != n:
+        raise RuntimeError(f'LN12: {n} matrices expected, got {len(mats)}')
+    arr = (_native.FbLn12Mat * n)()
+    for i, (d, m, o, (lo, hi)) in enumerate(mats):
+        if d.dtype != torch.uint8 or m.dtype != torch.int32 or not d.is_contiguous() or not m.is_contiguous():
+            raise RuntimeError('LN12: data uint8 and meta int32, contiguous')
+        arr[i] = _native.FbLn12Mat(d.data_ptr(), m.data_ptr(), o.data_ptr(), int(o.numel()),
+                                   int(lo) & 0xFFFFFFFF, int(hi) & 0xFFFFFFFF)
+    desc.ln12 = (arr, mats)
+    c.ln12 = ctypes.addressof(arr)
+
+
 class DepthOps:
     """flash_dd_*: the reference's dd2_* entry points (flash/csrc/depth_frame.cu:923-934) on flashb_dd_frame."""
 
     def __init__(self):
         self.desc = {}     # batch -> DepthModelDesc
         self.args = None
+        self.ln12_enc = None
+        self.ln12_stream = True   # after dd2_init_ln12: frames stream the 12-bit bytes where the build can
 
     def dd2_init(self, w, bufs=None, eps=1e-5, scaling=128 ** -0.5, grid=0, codebook_size=None):
         """w: per layer [ln1, wq, wk, wv, wo, ln2, wg, wu, wd] x NL + [embed, proj, normf, head_t, cos, sin] (bf16).
@@ -136,8 +160,10 @@ class DepthOps:
     def dd2_init_ln12(self, data, meta, ovf, luts):
         """The reference's ``dd2_init_ln12`` (``flash/csrc/depth_frame.cu:800-823``): the depth matrices in the
         lossless LN12 format (per matrix: data uint8, meta int32 [N, 4], ovf int32; luts int64 [count, 2] = the
-        table words).  flashb decodes them on the device (``flashb_ln12_decode``, bit-exact) into the bf16 matrices
-        its frame reads, replacing those of ``dd2_init``: the frames are the same."""
+        table words).  The tcgen05 frame build (grids <= 32, the lanes of a many-stream GPU) streams these bytes and
+        decodes them in shared memory before its MMAs (``ln12_stream``, on by default); the other builds and the step
+        table read bf16 matrices that flashb decodes once here on the device (``flashb_ln12_decode``, bit-exact),
+        replacing those of ``dd2_init``.  Either way the weights are the same values."""
         from . import ln12
         if self.args is None:
             raise RuntimeError('dd2_init first')
@@ -147,6 +173,8 @@ class DepthOps:
         lc = luts.cpu().tolist()
         dec = [ln12.decode_device(data[i], meta[i], ovf[i], (lc[i][0], lc[i][1]), torch.empty_like(m))
                for i, m in enumerate(mats)]
+        self.ln12_enc = [(data[i].contiguous(), meta[i].contiguous(), ovf[i].contiguous(), (lc[i][0], lc[i][1]))
+                         for i in range(len(mats))]
         layers, embed, proj, normf, head_t, cos, sin, eps, scaling, cb = self.args
         k = 0
         new_layers = []
@@ -177,6 +205,8 @@ class DepthOps:
             self.desc[B] = d
             if getattr(self, 'tab', None) is not None:
                 tab_set(d, *self.tab)
+            if getattr(self, 'ln12_enc', None) is not None and self.ln12_stream:
+                ln12_set(d, self.ln12_enc)
         d.cfg.grid = GRIDS.get(B, 0)
         return d
 

@@ -206,15 +206,24 @@ class DepthConfig:
         layer = (self.heads * D + 2 * self.kv_heads * D) * H + H * self.heads * D + 3 * self.ffn * H
         return 2 * (self.layers * layer + H * self.embed_dim + self.vocab * H)
 
-    def frame_weight_bytes(self, step_table=False, rows=2):
+    def frame_weight_bytes(self, step_table=False, rows=2, ln12=False):
         """Algorithmic bytes of one frame: n_decode codebook steps of weights; with the step table, steps >= 1 read
-        ``rows`` table rows (hidden + layer-0 q|k|v, bf16) instead of the projector and layer 0's q|k|v matrices."""
-        full = self.n_decode * self.step_weight_bytes()
+        ``rows`` table rows (hidden + layer-0 q|k|v, bf16) instead of the projector and layer 0's q|k|v matrices.
+        ln12: the streamed matrices as LN12 (1.5 bytes a weight + a 16-byte record per row; overflow patches, a few
+        per matrix, left out)."""
+        H, D, AE, V, F = self.hidden, 128, self.embed_dim, self.vocab, self.ffn
+        qkv = (self.heads + 2 * self.kv_heads) * D
+
+        def mat(n, k):
+            return n * k * 1.5 + n * 16 if ln12 else n * k * 2
+
+        layer = mat(qkv, H) + mat(H, self.heads * D) + 2 * mat(F, H) + mat(H, F)
+        step = self.layers * layer + mat(H, AE) + mat(V, H)
+        full = self.n_decode * step
         if not step_table:
-            return full
-        H, qkv = self.hidden, (self.heads + 2 * self.kv_heads) * 128
-        saved = 2 * (H * self.embed_dim + qkv * H) - 2 * rows * (H + qkv)
-        return full - (self.n_decode - 1) * saved
+            return int(full)
+        saved = mat(H, AE) + mat(qkv, H) - 2 * rows * (H + qkv)
+        return int(full - (self.n_decode - 1) * saved)
 
 
 class SyntheticDepth:
@@ -260,6 +269,30 @@ class SyntheticDepth:
         self.desc.frame(self.first_cb_token_buf, self.backbone_hidden_buf, self.tok_buf, self.output_tokens,
                         self.temperature, self.top_k, self.top_p, self.do_sample, self.guidance_scale, self.q, dbg,
                         forced)
+
+    def mats(self):
+        """The streamed matrices in the LN12 descriptor order: per layer q, k, v, o, gate, up, down; the projector;
+        the codebook heads."""
+        out = []
+        for L in self.layers:
+            out += [L['wq'], L['wk'], L['wv'], L['wo'], L['wg'], L['wu'], L['wd']]
+        return out + [self.proj] + [self.head_t[s] for s in range(self.head_t.shape[0])]
+
+    def ln12(self):
+        """The matrices encoded in LN12 (``flashb.ln12.encode`` on the host, once) as device tensors for
+        ``flashb.depth.ln12_set``."""
+        if getattr(self, '_ln12', None) is None:
+            from . import ln12 as L12
+            enc = []
+            for w in self.mats():
+                d, m, o, lut = L12.encode(w)
+                enc.append(L12.to_device(d, m, o, lut, self.device))
+            self._ln12 = enc
+        return self._ln12
+
+    def use_ln12(self, on=True):
+        from . import depth as fdep
+        fdep.ln12_set(self.desc, self.ln12() if on else None)
 
 
 class _Slot:
@@ -411,6 +444,18 @@ class FrameEngine:
                 d.layers, d.embed, d.proj, d.normf, d.head_t, d.cos_tab, d.sin_tab, dcfg.eps, 128 ** -0.5,
                 dcfg.codebook_size, 2, dev)
         self.step_table = None
+        self.ln12 = False
+
+    def use_ln12(self, on=True):
+        """Frames of every slot stream the depth weights in LN12 (12-bit, lossless; decoded in shared memory by the
+        tcgen05 build) instead of bf16."""
+        from . import depth as fdep
+        mats = self.depth.ln12() if on else None
+        descs = {id(x): x for x in [self.depth.desc] + list(self.lane_desc) +
+                 ([self.single.desc] if self.single is not None else [])}
+        for dd in descs.values():
+            fdep.ln12_set(dd, mats)
+        self.ln12 = on
 
     def use_step_table(self, on=True):
         """Frames of every slot read the per-token step table (built once from the shared depth weights,
@@ -664,14 +709,14 @@ class FrameEngine:
     def frame_bytes(self):
         """Algorithmic HBM bytes of one slot frame at the current KV length: backbone step + 16 depth steps."""
         if self.depth_only:
-            return self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group)
+            return self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group, self.ln12)
         kv = int(self.streams[0].bb.cache_position.item()) + 1
         if self.shared:
             n = len(self.streams)
             return backbone_step_bytes(self.bcfg, 2 * self.group * n, kv) / n + \
-                self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group)
+                self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group, self.ln12)
         return backbone_step_bytes(self.bcfg, 2 * self.group, kv) + \
-            self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group)
+            self.dcfg.frame_weight_bytes(self.step_table is not None, 2 * self.group, self.ln12)
 
 
 def backbone_step_bytes(cfg: BackboneConfig, batch, kv_len, include_lm_head=True):

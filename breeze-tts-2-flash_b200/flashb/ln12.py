@@ -27,10 +27,13 @@ NLUT = 8
 SHIFTS = (0, 1, -1, 2, -2, 3, -3, -4)      # per-row table shifts, in order of preference (ties keep the earlier)
 
 
+def _e1(u):
+    return ((u >> 8) & 0x7F).astype(np.uint8)
+
+
 def table(u):
     """The matrix's 8 most frequent e1 values (ties: the smaller value first), ascending."""
-    e1 = ((u >> 8) & 0x7F).astype(np.int64).ravel()
-    counts = np.bincount(e1, minlength=128)
+    counts = np.bincount(_e1(u).ravel(), minlength=128)
     order = sorted(range(128), key=lambda v: (-counts[v], v))
     return np.array(sorted(order[:NLUT]), np.uint8)
 
@@ -38,8 +41,8 @@ def table(u):
 def _row_shifts(e1, lut):
     """Per row, the shift of the table that covers the most of its values (ties: earlier in SHIFTS)."""
     N = e1.shape[0]
-    hist = np.zeros((N, 128), np.int64)
-    np.add.at(hist, (np.repeat(np.arange(N), e1.shape[1]), e1.ravel()), 1)
+    key = (np.arange(N, dtype=np.int64)[:, None] << 7) | e1
+    hist = np.bincount(key.ravel(), minlength=N * 128).reshape(N, 128)
     best = np.full(N, -2, np.int64)
     shift = np.zeros(N, np.int64)
     for sh in SHIFTS:
@@ -61,15 +64,16 @@ def encode_hdr(u, lut):
     if K % 1024:
         raise ValueError('LN12 needs K % 1024 == 0')
     G = K // 1024
-    e1 = ((u >> 8) & 0x7F).astype(np.int64)
+    e1 = _e1(u)
     shift = _row_shifts(e1, lut)
-    # index of each value's e1 in its row's shifted table; 8 = not in the table (a patch)
-    rows_lut = lut.astype(np.int64)[None, :] + shift[:, None]                # [N, 8]
-    idx = np.full((N, K), NLUT, np.int64)
+    # index of each value's e1 in its row's shifted table (the later entry when two are equal, never the case for a
+    # table of distinct values); 8 = not in the table (a patch).  inv maps e1 - shift + 8 (0 .. 139) to the index.
+    inv = np.full(144, NLUT, np.uint8)
     for i in range(NLUT):
-        idx = np.where(e1 == rows_lut[:, i:i + 1], i, idx)
+        inv[int(lut[i]) + 8] = i
+    idx = inv[(e1.astype(np.int16) - shift.astype(np.int16)[:, None] + 8)]
     esc = idx == NLUT
-    idx[esc] = 0
+    idx = np.where(esc, np.uint8(0), idx)
     pr, pc = np.nonzero(esc)                                                # row-major order
     patches = (pc.astype(np.uint32) << 8) | (u[pr, pc] >> 8).astype(np.uint32)
     count = np.bincount(pr, minlength=N).astype(np.int64)
@@ -78,12 +82,12 @@ def encode_hdr(u, lut):
         raise ValueError('LN12 patch header overflow')
     hdr = ((offset << 13) | ((shift & 7) << 10) | count).astype(np.uint32)
     # nibble words: 8 elements per word
-    sign = (u >> 15).astype(np.uint32).reshape(N, K // 8, 8)
-    ix = idx.astype(np.uint32).reshape(N, K // 8, 8)
+    sign = (u >> 15).astype(np.uint8).reshape(N, K // 8, 8)
+    ix = idx.reshape(N, K // 8, 8)
     words = np.zeros((N, K // 8), np.uint32)
     for j in range(8):
-        words |= ix[..., j] << np.uint32(4 * j)
-        words |= sign[..., j] << np.uint32(8 * j + 7 if j < 4 else 8 * (j - 4) + 3)
+        words |= ix[..., j].astype(np.uint32) << np.uint32(4 * j)
+        words |= sign[..., j].astype(np.uint32) << np.uint32(8 * j + 7 if j < 4 else 8 * (j - 4) + 3)
     low = (u & 0xFF).astype(np.uint8).reshape(N, G, 4, 32, 8)                # [n, g, chunk, lane, j]
     data = np.empty((N, G, 3, 32, 16), np.uint8)
     data[:, :, 0, :, :8], data[:, :, 0, :, 8:] = low[:, :, 0], low[:, :, 1]

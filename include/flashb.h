@@ -251,6 +251,16 @@ int flashb_ln12_decode(const void* data, const void* meta, const void* ovf, uint
 typedef struct {
   const void *ln1, *wq, *wk, *wv, *wo, *ln2, *wg, *wu, *wd; /* bf16 */
 } fb_dd_layer;
+/* One depth matrix in the LN12 format (flash/ln12_format.py; flashb_ln12_decode): data [N][K / 1024][3][32][16 B],
+ * meta [N][4] uint32 (16-byte aligned), ovf [n_ovf] uint32 overflow patches (reads past n_ovf are skipped), the
+ * 8-entry table as two little-endian words. */
+typedef struct {
+  const void* data;
+  const void* meta;
+  const void* ovf;
+  int64_t n_ovf;
+  uint32_t lut_lo, lut_hi;
+} fb_ln12_mat;
 typedef struct {
   int layers, batch, hidden, embed_dim, heads, kv_heads, head_dim, ffn;
   int vocab, codebook_size, n_decode;
@@ -275,6 +285,13 @@ typedef struct {
   const void* ttab;        /* ttab [(n_decode - 1) vocab, (heads + 2 kv_heads) 128] bf16 = layer 0's pre-RoPE q|k|v of
                             * RMSNorm(ptab row t).  Codebook steps >= 1 then read their stage E and layer-0 q|k|v
                             * there instead of running the projector and layer-0 q|k|v GEMVs */
+  const fb_ln12_mat* ln12; /* optional host array (null = none) of every streamed depth matrix in LN12, in the
+                            * reference's order (dd2_init_ln12, flash/csrc/depth_frame.cu:800-823): per layer wq, wk,
+                            * wv, wo, wg, wu, wd, then the projector, then the n_decode codebook heads [vocab, hidden].
+                            * The tcgen05 build (grids <= 32) then streams the 12-bit bytes and decodes them in shared
+                            * memory before the MMAs (about 25% fewer weight bytes, the same bf16 values); other builds
+                            * read the bf16 matrices.  Needs hidden, ffn, heads x 128, embed_dim multiples of 1024 and
+                            * vocab, kv_heads x 128 multiples of 64 */
 } fb_dd_config;
 int64_t flashb_dd_scratch_bytes(const fb_dd_config* cfg);
 /* Builds the per-token step table of the reference's dd2_tab_build (flash/csrc/depth_frame.cu:714-754, 894-913): for

@@ -9,7 +9,7 @@ import bench  # noqa: E402
 
 
 def _args(streams=64, backbone='shared'):
-    return argparse.Namespace(group=8, prompt=512, streams=streams, lanes=8, backbone=backbone)
+    return argparse.Namespace(group=8, prompt=512, streams=streams, lanes=8, backbone=backbone, step_table=1, ln12=0)
 
 
 def test_frame_config_keys_and_backbone_mode():

@@ -334,3 +334,80 @@ def test_dd2_init_ln12_frames_equal_the_bf16_frames():
     torch.cuda.synchronize()
     assert torch.equal(m.output_tokens, ref)
     assert json.loads(ops.dd2_info())['ln12'] == 1
+
+
+@pytest.mark.parametrize('B,grid,kw', [
+    (16, 18, {}),                                                     # the bench's lane: full-size model, B = 16
+    (2, 8, dict(layers=1, n_decode=4, vocab=128, codebook_size=120)),
+    (8, 12, dict(layers=2, n_decode=5, vocab=256, codebook_size=250, ffn=2048)),
+])
+def test_depth_ln12_streaming(B, grid, kw):
+    """LN12 streamed by the frame (the reference's depth path on 12-bit weights): on a lane-sized grid the tcgen05
+    build copies the LN12 bytes, decodes them in shared memory and runs its MMAs on the decoded strips.  The
+    teacher-forced logits match the oracle on the bf16 weights (the decoded values are the same bits) and the frame
+    on bf16 weights; the sampler stays bit-exact on the kernel's logits; switching back gives the bf16 frame."""
+    m = _model(small=False, B=B, seed=11, **kw)
+    m.desc.cfg.grid = grid
+    c = m.cfg
+    forced = np.random.default_rng(11).integers(0, c.vocab, (c.n_decode, B))
+    _, lg_bf16, _ = _run(m, forced)
+    m.use_ln12(True)
+    outtok, logits, _ = _run(m, forced)
+    W = _weights(m)
+    temp, topk, topp, ds, gs = _params(m)
+    _, lg_ref, _ = odepth.depth_frame(W, np32(m.backbone_hidden_buf), m.first_cb_token_buf.cpu().numpy(),
+                                      m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
+    for s in range(c.n_decode):
+        assert_close(logits[s], lg_ref[s], what=f'step {s} logits (LN12 streamed)')
+        assert_close(logits[s], lg_bf16[s], what=f'step {s} logits (LN12 vs bf16 frame)')
+    assert_argmax_agree(logits, lg_ref, min_frac=DEPTH_ARGMAX_MIN, what='depth logits (LN12)')
+    _check_sampler(m, logits, outtok)
+    m.use_ln12(False)
+    _, lg_back, _ = _run(m, forced)
+    np.testing.assert_array_equal(lg_back, lg_bf16)
+    from flashb._native import device_error
+    assert device_error() == 0
+
+
+def test_depth_ln12_streaming_with_step_table_and_patches():
+    """LN12 streaming with the step table, on weights whose rows need every kind of record: shifted tables, inline
+    patches and overflow patches (a few rows scaled far from the rest and a few wide outliers per row)."""
+    from flashb import depth as fdep
+    from flashb import ln12
+    m = _model(small=False, B=16, seed=12, layers=1, n_decode=4, vocab=128, codebook_size=120)
+    m.desc.cfg.grid = 18
+    g = torch.Generator(device='cpu').manual_seed(12)
+    for w in m.mats():
+        wc = w.float().cpu()
+        rows = torch.randint(0, wc.shape[0], (8,), generator=g)
+        wc[rows] *= 16.0                                              # rows whose exponents sit higher: a shift
+        r2 = torch.randint(0, wc.shape[0], (wc.shape[0] // 8,), generator=g)
+        c2 = torch.randint(0, wc.shape[1], (wc.shape[0] // 8, 6), generator=g)
+        wc[r2[:, None], c2] *= 2.0 ** 10                              # outliers: patches, > 3 in some rows
+        w.copy_(wc.to(torch.bfloat16))
+    counts = [(ln12.encode(w)[1][:, 0] & 1023) for w in m.mats()]
+    assert max(int(x.max()) for x in counts) > 3                      # overflow patches are exercised
+    pt, tt = fdep.tab_build(m.desc)
+    fdep.tab_set(m.desc, pt, tt)
+    m.use_ln12(True)
+    c = m.cfg
+    forced = np.random.default_rng(12).integers(0, c.vocab, (c.n_decode, 16))
+    outtok, logits, _ = _run(m, forced)
+    W = _weights(m)
+    temp, topk, topp, ds, gs = _params(m)
+    _, lg_ref, _ = odepth.depth_frame(W, np32(m.backbone_hidden_buf), m.first_cb_token_buf.cpu().numpy(),
+                                      m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
+    for s in range(c.n_decode):
+        assert_close(logits[s], lg_ref[s], what=f'step {s} logits (LN12 + table, patched weights)')
+    _check_sampler(m, logits, outtok)
+
+
+def test_depth_ln12_streaming_refuses_unsupported_shapes():
+    """LN12 streaming needs 64-row multiples (a stage's rows); a lane-sized frame of a 96-entry codebook is refused
+    before anything runs."""
+    from flashb._native import FlashbError
+    m = _model(small=False, B=2, layers=1, n_decode=3, vocab=96, codebook_size=90)
+    m.desc.cfg.grid = 4
+    with pytest.raises(FlashbError):
+        m.use_ln12(True)
+        _run(m)
