@@ -86,6 +86,7 @@ struct alignas(64) DDArgs {
   float* logits;
   GridBar* bar;
   int nstages, xs_bytes, att_off, keep_off, att_bc, att_split, d_xchunk;
+  int keep_cols;                          // tcgen05 build: x_mid kept only for the CTA's S4 columns (0 = all)
   unsigned long long wait_ns;             // grid-barrier wait limit
   const bf16 *ptab, *ttab;                // optional per-token step table (codebook steps >= 1), or null
   int l2_keep;                            // 1: weight copies carry the L2 evict_last hint
@@ -571,21 +572,24 @@ __device__ __noinline__ void dd_attention_pairs(const DDArgs& a, int l, int pos,
 
 // x_mid = bf16(xres + ob) then RMSNorm (S3 input), all M rows.  xres and ob arrive with cp.async (one round trip);
 // the un-normalised x_mid rows are also kept in `keep` ([M][H] bf16) for the down projection's residual.
+// keep_c0 / a.keep_cols > 0 (tcgen05 build): ob is staged at xs + 16 H * 2 (past the 16 staged rows, free in S3) and
+// only x_mid columns [keep_c0, keep_c0 + keep_cols) -- this CTA's S4 output columns -- are kept, [M][keep_cols].
 __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const DDArgs& a, int M, const bf16* nw,
-                                         float* nred, bf16* keep) {
+                                         float* nred, bf16* keep, int keep_c0) {
   const int tid = threadIdx.x;
-  const int H = a.H, kv = H >> 3;
+  const int H = a.H, kv = H >> 3, kc = a.keep_cols;
+  bf16* const ost = kc ? reinterpret_cast<bf16*>(xs + (size_t)16 * H * 2) : keep;   // ob staging, [M][H]
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
     cp_async16(xs + xs_off(m, j, x_pitch), a.xres + (size_t)m * H + (size_t)j * 8);
-    cp_async16(keep + (size_t)m * H + (size_t)j * 8, a.ob + (size_t)m * H + (size_t)j * 8);
+    cp_async16(ost + (size_t)m * H + (size_t)j * 8, a.ob + (size_t)m * H + (size_t)j * 8);
   }
   cp_async_commit();
   cp_async_wait<0>();
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int m = i / kv, j = i - m * kv;
     uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
-    uint4* pk = reinterpret_cast<uint4*>(keep + (size_t)m * H + (size_t)j * 8);
+    uint4* pk = reinterpret_cast<uint4*>(ost + (size_t)m * H + (size_t)j * 8);
     float x[8], o[8];
     cvt8(*px, x);
     cvt8(*pk, o);
@@ -598,7 +602,12 @@ __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const D
     w.z = pack2(v[4], v[5]);
     w.w = pack2(v[6], v[7]);
     *px = w;
-    *pk = w;
+    if (!kc) {
+      *pk = w;
+    } else {
+      const int col = j * 8 - keep_c0;
+      if (col >= 0 && col < kc) *reinterpret_cast<uint4*>(keep + (size_t)m * kc + col) = w;
+    }
   }
   named_sync(1, PK_CONSUMERS);
   row_rms(xs, x_pitch, M, H, a.eps, nred);
@@ -877,13 +886,14 @@ __device__ __noinline__ void ln12_decode_stages(const Ring& rg, int t0, int nk, 
 // the stages and its lane 0 issues the MMAs (four independent accumulator chains per matrix, summed in a fixed
 // order) and commits them to the ring's empty barriers and to g_dd_mbar.  Warps 0-3 then copy the accumulators out
 // of TMEM into `dump` as groups of 16 rows x 16 activation rows in the order the mma.sync epilogues read them
-// (KIND 0: 16 units; KIND 1 and 2: rows 0-7 the 8 units' matrix-0 rows, 8-15 their matrix-1 rows), and every thread
-// runs epi(n0, nu, group) per group.  A failed wait in warp 0 still commits (so nobody else waits in vain) and is
-// reported to every thread through shared memory after the next barrier.
+// (KIND 0: 16 units; KIND 1 and 2: rows 0-7 the 8 units' matrix-0 rows, 8-15 their matrix-1 rows), and the
+// threads run epi(n0, nu, group, local thread) per group, as many groups at once as the threads allow.  A failed
+// wait in warp 0 still commits (so nobody else waits in vain) and is reported to every thread through shared
+// memory after the next barrier.
 template <int KIND, bool ln, typename EpiFn, typename StageFn>
 __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, int K, const unsigned char* xs,
                                                 float* dump, EpiFn epi, StageFn stage_x, unsigned* err,
-                                                unsigned long long* det) {
+                                                unsigned long long* det, int bM) {
   constexpr int C = tc_cols<KIND>();
   constexpr int GU = KIND == 0 ? 16 : 8;                       // units per group
   constexpr int NM = KIND == 0 ? 1 : 2;                        // LN12: stages per K slice
@@ -1038,11 +1048,16 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
     named_sync(1, PK_CONSUMERS);
     if (det && threadIdx.x == 0 && bi == b0) det[4] = globaltimer();
     if (*abort_flag) return false;
+    // groups side by side: a group's epilogue uses GU x M threads, so 256 / (GU M) groups run at once (thread t
+    // takes group slot t / (GU M) as local thread t % (GU M))
+    const int gw = GU * bM;
+    const int gq = gw >= PK_CONSUMERS ? 1 : PK_CONSUMERS / gw;
+    const int gs = (int)threadIdx.x / gw, lt = (int)threadIdx.x - gs * gw;
     if (KIND == 1 && !ln) {
-      for (int g = 0; g < 8; ++g) {
+      for (int g = gs; g < 8 && gs < gq; g += gq) {
         const int n0 = bi * UB + g * GU;
         const int nu = min(GU, units - n0);
-        if (nu > 0) epi(n0, nu, dump + g * 256);
+        if (nu > 0) epi(n0, nu, dump + g * 256, lt);
       }
       named_sync(1, PK_CONSUMERS);
       if (warp >= 2 && warp < 4) {
@@ -1055,19 +1070,19 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
         }
       }
       named_sync(1, PK_CONSUMERS);
-      for (int g = 0; g < 8; ++g) {
+      for (int g = gs; g < 8 && gs < gq; g += gq) {
         const int n0 = bi * UB + 64 + g * GU;
         const int nu = min(GU, units - n0);
-        if (nu > 0) epi(n0, nu, dump + g * 256);
+        if (nu > 0) epi(n0, nu, dump + g * 256, lt);
       }
     } else
     {
       // KIND 0: 4 groups of 16 units; KIND 1 and 2: 8 groups of 8 units
       constexpr int NGR = KIND == 0 ? 4 : 8;
-      for (int g = 0; g < NGR; ++g) {
+      for (int g = gs; g < NGR && gs < gq; g += gq) {
         const int n0 = bi * UB + g * GU;
         const int nu = min(GU, units - n0);
-        if (nu > 0) epi(n0, nu, dump + g * 256);
+        if (nu > 0) epi(n0, nu, dump + g * 256, lt);
       }
     }
     if (det && threadIdx.x == 0 && bi == b0) det[5] = globaltimer();
@@ -1089,7 +1104,7 @@ __device__ __forceinline__ bool dd_gemv(const DDArgs& a, DDSm& m, DDCur& c, int 
     const int call = g_dd_call;
     if (a.trace && call < DD_DETAIL_CALLS)
       det = a.trace + (size_t)gridDim.x * a.NCB * DD_TRACE_SLOTS(a.L) + ((size_t)blockIdx.x * DD_DETAIL_CALLS + call) * 8;
-    const bool ok = consume_task_tc<KIND, (NT < 0)>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err, det);
+    const bool ok = consume_task_tc<KIND, (NT < 0)>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err, det, a.B);
     if (threadIdx.x == 0) g_dd_call = call + 1;
     return ok;
   } else {
@@ -1207,9 +1222,9 @@ __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int su
   cp_async_wait<0>();
   named_sync(1, PK_CONSUMERS);
   if (!dd_gemv<NT, 0>(a, m, c, H, AE, xp_ae,
-                      [&](int n0, int nu, const float* sm) {
-                        if (tid < nu * M) {
-                          const int i = tid / M, r = tid - i * M;
+                      [&](int n0, int nu, const float* sm, int lt) {
+                        if (lt < nu * M) {
+                          const int i = lt / M, r = lt - i * M;
                           xres[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
                         }
                       }, [](int) {})) {
@@ -1295,9 +1310,9 @@ __device__ __noinline__ DDCur dd_phase_s1(const DDArgs& a, DDCur c, int s, int p
   const int xp = (NT > 0) ? H * 2 + 16 : 0;
   load_x(m.xs, xp, a.xres, H, M, H, a.layers[l].ln1, a.eps, g_dd_nred);
   if (!dd_gemv<NT, 2>(a, m, c, (NH + 2 * NKV) * 64, H, xp,
-                           [&](int n0, int nu, const float* sm) {
-                             if (tid < nu * M) {
-                               const int i = tid / M, b = tid - i * M;
+                           [&](int n0, int nu, const float* sm, int lt) {
+                             if (lt < nu * M) {
+                               const int i = lt / M, b = lt - i * M;
                                const int u = n0 + i, hh = u >> 6, d = u & 63;
                                float y0 = rbf(sm[i * MS + b]), y1 = rbf(sm[(i + 8) * MS + b]);
                                if (hh < NH + NKV) {
@@ -1354,9 +1369,9 @@ __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int p
   }
   DD_STAMP(s, tb + 2);
   if (!dd_gemv<NT, 0>(a, m, c, H, QD, xp_q,
-                      [&](int n0, int nu, const float* sm) {
-                        if (tid < nu * M) {
-                          const int i = tid / M, r = tid - i * M;
+                      [&](int n0, int nu, const float* sm, int lt) {
+                        if (lt < nu * M) {
+                          const int i = lt / M, r = lt - i * M;
                           ob[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
                         }
                       }, [](int) {})) {
@@ -1379,11 +1394,13 @@ __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l
   bf16* xkeep = reinterpret_cast<bf16*>(m.xs + a.keep_off);
   bf16* const act = a.act;
   const int xp = (NT > 0) ? H * 2 + 16 : 0;
-  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep);
+  int kb0 = 0, kb1 = 0;
+  if (NT <= 0) tc_task_blocks<0>(H, kb0, kb1, false);          // this CTA's S4 blocks of 64 output columns
+  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep, kb0 * 64);
   if (!dd_gemv<NT, 1>(a, m, c, F, H, xp,
-                      [&](int n0, int nu, const float* sm) {
-                        if (tid < nu * M) {
-                          const int i = tid / M, r = tid - i * M;
+                      [&](int n0, int nu, const float* sm, int lt) {
+                        if (lt < nu * M) {
+                          const int i = lt / M, r = lt - i * M;
                           const float g = rbf(sm[i * MS + r]);
                           const float u = rbf(sm[(i + 8) * MS + r]);
                           act[(size_t)r * F + n0 + i] = __float2bfloat16_rn(silu_rbf(g) * u);
@@ -1407,6 +1424,10 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
   const int tb = 3 + 9 * l;
   const bf16* xkeep = reinterpret_cast<const bf16*>(m.xs + a.keep_off);
   bf16* const xres = a.xres;
+  const int kc = a.keep_cols;
+  int kb0 = 0, kb1 = 0;
+  if (NT <= 0) tc_task_blocks<0>(H, kb0, kb1, false);
+  const int kc0 = kb0 * 64;
   // tcgen05 build: act in passes of DD_TC_KX columns; mma.sync: whole, or in column chunks (d_xchunk)
   auto stage = [&](int p) {
     const int k0 = p * DD_TC_KX;
@@ -1415,10 +1436,10 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
   if (NT <= 0) stage(0);
   else if (!a.d_xchunk) load_x(m.xs, F * 2 + 16, a.act, F, M, F, nullptr, 0.f, g_dd_nred);
   if (!dd_gemv<NT, 0>(a, m, c, H, F, a.d_xchunk ? ST_KC * 2 + 16 : F * 2 + 16,
-                      [&](int n0, int nu, const float* sm) {
-                        if (tid < nu * M) {
-                          const int i = tid / M, r = tid - i * M, n = n0 + i;
-                          const float xm = b2f(xkeep[(size_t)r * H + n]);
+                      [&](int n0, int nu, const float* sm, int lt) {
+                        if (lt < nu * M) {
+                          const int i = lt / M, r = lt - i * M, n = n0 + i;
+                          const float xm = b2f(kc ? xkeep[(size_t)r * kc + (n - kc0)] : xkeep[(size_t)r * H + n]);
                           xres[(size_t)r * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * MS + r]));
                         }
                       }, stage, a.d_xchunk ? a.act : nullptr, F)) {
@@ -1442,9 +1463,9 @@ __device__ __noinline__ DDCur dd_phase_s5(const DDArgs& a, DDCur c, int s) {
   const int xp = (NT > 0) ? H * 2 + 16 : 0;
   load_x(m.xs, xp, a.xres, H, M, H, a.normf, a.eps, g_dd_nred);
   if (!dd_gemv<NT, 0>(a, m, c, V, H, xp,
-                      [&](int n0, int nu, const float* sm) {
-                        if (tid < nu * M) {
-                          const int i = tid / M, b = tid - i * M;
+                      [&](int n0, int nu, const float* sm, int lt) {
+                        if (lt < nu * M) {
+                          const int i = lt / M, b = lt - i * M;
                           const float v = sm[i * MS + b];
                           logits[(size_t)b * V + n0 + i] = v;
                           if (dbg) dbg[((size_t)s * M + b) * V + n0 + i] = v;
@@ -1812,8 +1833,12 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
     int n = fixed < budget ? (int)((budget - fixed) / slot) : 0;
     return n > PK_MAX_STAGES ? PK_MAX_STAGES : n;
   };
-  // x_mid kept from S3 to S4 (its rows also stage ob in S3)
-  const size_t keep_rows = (size_t)c->hidden;
+  // x_mid kept from S3 to S4 (its rows also stage ob in S3).  tcgen05 build with room for ob beside the 16 staged
+  // rows: only the CTA's S4 columns (its blocks of 64 output units), ob staged in the free half of the rows region
+  const int s4_blocks = (c->hidden + 63) / 64;
+  const int keep_cols = (s4_blocks + grid - 1) / grid * 64;
+  a.keep_cols = (tc && (size_t)2 * 16 * c->hidden * 2 <= (size_t)16 * 2 * KXf && keep_cols < c->hidden) ? keep_cols : 0;
+  const size_t keep_rows = a.keep_cols ? (size_t)a.keep_cols : (size_t)c->hidden;
   auto layout = [&](int d_chunk, size_t& keep_off, size_t& base) {
     const size_t d_region = tc ? 16 * 2 * KXf : (d_chunk ? 2 * M * xp_kc : M * (c->ffn * 2 + 16));
     keep_off = al256d(d_region > rows ? d_region : rows);

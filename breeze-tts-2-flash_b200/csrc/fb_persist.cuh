@@ -284,7 +284,7 @@ __device__ __noinline__ int consume_group_nt(Ring rg, int t, int K, const unsign
   return t;
 }
 
-// Consumer half: every 16-row group of the task through consume_group_nt, then epi(n0, nu, sums).  All 256
+// Consumer half: every 16-row group of the task through consume_group_nt, then epi(n0, nu, sums, tid).  All 256
 // consumer threads call it.  Chunked activations (xg) need a task of one row group per CTA or accept re-loading.
 template <int NMAT, int NT = 1, typename EpiFn>
 __device__ __forceinline__ bool consume_task(Ring& rg, int& t, int units, int K, const unsigned char* xs, int x_pitch,
@@ -297,7 +297,7 @@ __device__ __forceinline__ bool consume_task(Ring& rg, int& t, int units, int K,
     const int nu = min(UG, u1 - n0);
     t = consume_group_nt<NT>(rg, t, K, xs, x_pitch, M, zero16, red, sums, err, xg, ldx);
     if (t < 0) return false;
-    epi(n0, nu, sums);
+    epi(n0, nu, sums, (int)threadIdx.x);
   }
   return true;
 }
