@@ -37,9 +37,10 @@ N_STREAMS = 64
 PROMPT = 512
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0)
 # dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch at the bench's default shape (8 streams
-# per launch, B = 16 rows, one lane's grid of 18 CTAs: the tcgen05 build), from one ncu --set full capture of the
-# full-size depth model: 2,174,940,416 B read + 7,735,296 B written.
-DD_TRAFFIC_BYTES = 2182675712
+# per launch, B = 16 rows, one lane's grid of 18 CTAs: the tcgen05 build), from ncu --set full captures of the
+# full-size depth model, keyed by (step table, LN12 weights): with the table 2,066,498,000 B read + 7,627,264 B
+# written (bf16) and 1,042,911,000 + 8,060,672 (LN12); without it 2,174,940,416 + 7,735,296 (bf16).
+DD_TRAFFIC_BYTES = {(1, 0): 2074125264, (1, 1): 1050971672, (0, 0): 2182675712}
 PREFILL_CFG = dict(B=2, NH=16, NKV=4, L=512, D=128, pads=(0, 37))
 
 
@@ -711,7 +712,7 @@ def main():
         dd_avg = sum(dd_ms) / len(dd_ms)
         ach = dd_bytes / (dd_avg / 1e3) / 1e9
         roof = dict(kernel='dd_frame_kernel', bound='hbm', achieved=round(ach, 1), peak=pk['hbm_gbs'], unit='GB/s',
-                    frac=round(ach / pk['hbm_gbs'], 4), traffic=DD_TRAFFIC_BYTES,
+                    frac=round(ach / pk['hbm_gbs'], 4), traffic=DD_TRAFFIC_BYTES.get((int(a.step_table), int(a.ln12))),
                     algorithmic_bytes=dd_bytes, launch_ms=round(dd_avg, 4), peak_source=pk['source'],
                     grid=eng.lane_sms or torch.cuda.get_device_properties(dev).multi_processor_count,
                     concurrent_launches=lanes, achieved_all_lanes=round(ach * lanes, 1),
