@@ -14,6 +14,8 @@
 //     between key groups, SBO = 2048 B between dim groups).  No tensor map is involved.
 //   * Thread 0 issues tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32, M = N = 128, K = 16 per
 //     instruction) and tcgen05.commit to an mbarrier; the others wait on it (bounded).
+//   * Copies run one key tile ahead: K(t + 1) and its mask (two mask buffers) while tile t's scores are read,
+//     V(t + 1) once P(t) V(t) is done; S(t + 1) is issued as soon as K(t + 1) has landed.
 //   * Pass 1: S = Q K^T per key tile into TMEM columns [0, 128); every thread reads its 32 scores (tcgen05.ld
 //     32x32b), applies the eager rounding points and the mask, and keeps a running max and fp32 sum of
 //     exp(s - max) (rescaled when the max grows); the four quarters of a row are merged after the pass.
@@ -34,7 +36,7 @@ constexpr int PF_THREADS = 128 * PF_QUARTERS;     // 16 warps
 constexpr int PF_OPND = PF_TILE * PF_D * 2;        // 32 KB per operand tile
 constexpr int PF_MPITCH = PF_TILE * 2 + 16;       // bytes per staged bf16 mask row (padded: fewer bank conflicts)
 constexpr int PF_MASK = PF_TILE * PF_MPITCH;       // the bf16 mask tile of the current key tile
-constexpr int PF_SMEM = 4 * PF_OPND + PF_MASK + 64;  // Q, K, V, P, mask + two mbarriers + TMEM address slot
+constexpr int PF_SMEM = 4 * PF_OPND + 2 * PF_MASK + 64;  // Q, K, V, P, two mask tiles, two mbarriers, TMEM slot
 constexpr uint32_t PF_TMEM_COLS = 256;             // S: columns [0, 128); O: columns [128, 256)
 
 struct PFArgs {
@@ -83,6 +85,9 @@ __device__ __forceinline__ void cp_async16_pf(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all_pf() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ void cp_commit_pf() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait_pf() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // 32 consecutive fp32 columns of this thread's TMEM lane (warp w reads lanes 32w .. 32w + 31).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&f)[32]) {
@@ -153,8 +158,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   unsigned char* sk = smem + PF_OPND;
   unsigned char* sv = smem + 2 * PF_OPND;
   unsigned char* sp = smem + 3 * PF_OPND;
-  unsigned char* sm = smem + 4 * PF_OPND;
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + 4 * PF_OPND + PF_MASK);
+  unsigned char* smb[2] = {smem + 4 * PF_OPND, smem + 4 * PF_OPND + PF_MASK};   // mask tiles of even / odd key tiles
+  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + 4 * PF_OPND + 2 * PF_MASK);
   uint64_t* bar_o = bar_s + 1;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 2);
   __shared__ float s_stat[2][PF_QUARTERS][PF_TILE];   // per (column quarter, row): running max, sum
@@ -210,8 +215,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   bool fail = false;
   const bool mask_smem = a.mask && a.mask_bf16;
 
+  // Staging of key tile t: K (K-major B operand of S = Q K^T) with the tile's bf16 mask rows, and V (MN-major B
+  // operand of O += P V).  Each is one cp.async group (the caller commits); zero rows past S are plain stores.
   auto stage_k = [&](int t) {
-    if (mask_smem) stage_mask(a, b, q0, t, sm);
+    if (mask_smem) stage_mask(a, b, q0, t, smb[t & 1]);
     for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
       const int j = i >> 4, c = i & 15, key = t * PF_TILE + j;
       unsigned char* dst = sk + kmaj_off(j, c);
@@ -227,9 +234,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
     }
   };
-  // S = Q K^T for the staged K tile: 8 MMAs of K = 16 (the A and B start addresses advance 256 B per step)
-  auto mma_s = [&]() {
-    cp_async_wait_all_pf();
+  // Issue S = Q K^T for the staged K tile (8 MMAs of K = 16, the A and B start addresses advancing 256 B per step)
+  // once the staging the caller waited for is visible to the tensor core; then wait for it with every thread.
+  auto issue_s = [&]() {
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -240,8 +247,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
         umma_bf16(t_s, umma_desc(aq + 256 * s, 128, 2048), umma_desc(ak + 256 * s, 128, 2048), idesc_s, s > 0);
       umma_commit(bar_s);
     }
+  };
+  auto wait_s = [&]() {
     const bool ok = mbar_wait(bar_s, ph_s, a.err);
     ph_s ^= 1u;
+    if (__syncthreads_or(!ok)) return false;
+    tc_fence_after();
+    return true;
+  };
+  auto wait_o = [&]() {
+    const bool ok = mbar_wait(bar_o, ph_o, a.err);
+    ph_o ^= 1u;
     if (__syncthreads_or(!ok)) return false;
     tc_fence_after();
     return true;
@@ -251,7 +267,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     float acc[32], mv[32];
     tmem_ld32(t_s + my_taddr, acc);
     const int col0 = t * PF_TILE + cq * 32;
-    load_mask32(a, b, row_ok ? row : 0, col0, sm + r * PF_MPITCH, cq * 32, mv);
+    load_mask32(a, b, row_ok ? row : 0, col0, smb[t & 1] + r * PF_MPITCH, cq * 32, mv);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       float s = rbf(rbf(acc[i]) * a.scaling);
@@ -262,11 +278,22 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   };
 
   // ---------------------------------------------------------------- pass 1: row max and sum of exp
+  // Tile t + 1's K and mask are copied while tile t's scores are reduced (the S MMA has read K; the mask tiles
+  // alternate between two buffers).
+  if (ntile > 0) {
+    stage_k(0);
+    cp_commit_pf();
+    cp_wait_pf<0>();
+    issue_s();
+  }
   for (int t = 0; t < ntile && !fail; ++t) {
-    stage_k(t);
-    if (!mma_s()) {
+    if (!wait_s()) {
       fail = true;
       break;
+    }
+    if (t + 1 < ntile) {
+      stage_k(t + 1);
+      cp_commit_pf();
     }
     float sc[32];
     scores32(t, sc);
@@ -281,8 +308,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) + add;
       mx = nm;
     }
-    tc_fence_before();
-    __syncthreads();
+    if (t + 1 < ntile) {
+      cp_wait_pf<0>();
+      issue_s();                       // its barrier also ends every thread's reads of S(t) and of mask tile t
+    }
   }
   // merge the four column quarters of every row (the same result in all four threads of a row)
   s_stat[0][cq][r] = mx;
@@ -304,22 +333,27 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     sum = l;
   }
   const bool dead = !(mx > -1e30f);
+  const float inv = 1.0f / sum;
 
   // ---------------------------------------------------------------- pass 2: P = softmax, O += P V
+  // Per tile t: wait for S(t); copy K(t + 1) and its mask (K is free once S(t) is done); P(t) from S(t); once V(t)
+  // has landed, O += P(t) V(t); when that MMA is done, copy V(t + 1) and issue S(t + 1) as soon as K(t + 1) is in.
+  if (!fail && ntile > 0) {
+    stage_k(0);
+    cp_commit_pf();
+    stage_v(0);
+    cp_commit_pf();
+    cp_wait_pf<1>();                   // K(0) and its mask; V(0) may still be in flight
+    issue_s();
+  }
   for (int t = 0; t < ntile && !fail; ++t) {
-    if (t > 0) {                                   // the previous P V must be done before K, V, P are replaced
-      const bool ok = mbar_wait(bar_o, ph_o, a.err);
-      ph_o ^= 1u;
-      if (__syncthreads_or(!ok)) {
-        fail = true;
-        break;
-      }
-    }
-    stage_k(t);
-    stage_v(t);
-    if (!mma_s()) {
+    if (!wait_s()) {
       fail = true;
       break;
+    }
+    if (t + 1 < ntile) {
+      stage_k(t + 1);
+      cp_commit_pf();
     }
     float sc[32];
     scores32(t, sc);
@@ -327,7 +361,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     // bf16 rounding of p except at rare ties (the exact expf and IEEE division per score serialise on their
     // special-case branches and cost several microseconds per tile)
     float p[32];
-    const float inv = 1.0f / sum;
 #pragma unroll
     for (int i = 0; i < 32; ++i) p[i] = (dead || !row_ok) ? 0.f : rbf(__expf(sc[i] - mx) * inv);
 #pragma unroll
@@ -339,6 +372,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       w.w = pack2(p[c * 8 + 6], p[c * 8 + 7]);
       *reinterpret_cast<uint4*>(sp + kmaj_off(r, cq * 4 + c)) = w;
     }
+    // V(t) was committed before K(t + 1): leave at most that newest group in flight
+    if (t + 1 < ntile) cp_wait_pf<1>();
+    else cp_wait_pf<0>();
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -350,12 +386,22 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
                   (t > 0 || s > 0) ? 1u : 0u);
       umma_commit(bar_o);
     }
+    // P and V are free again once this P V is done; the last one is waited for after the loop
+    if (t + 1 < ntile) {
+      if (!wait_o()) {
+        fail = true;
+        break;
+      }
+      stage_v(t + 1);
+      cp_commit_pf();
+      cp_wait_pf<1>();                 // K(t + 1) and its mask; V(t + 1) may still be in flight
+      issue_s();
+    }
   }
   if (!fail && ntile > 0) {
-    const bool ok = mbar_wait(bar_o, ph_o, a.err);
-    if (__syncthreads_or(!ok)) fail = true;
-    tc_fence_after();
+    if (!wait_o()) fail = true;
   }
+  cp_async_wait_all_pf();              // nothing may land in shared memory after this point (failure paths)
 
   // ---------------------------------------------------------------- epilogue: O -> bf16 -> out [B, L, NH, D]
   if (!fail) {
