@@ -774,12 +774,13 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
     return true;
   }
   const int nkc = (K + C - 1) / C;
+  int s = t % rg.nst;                                          // ring slot of stage t, advanced without divisions
+  unsigned par = (unsigned)((t / rg.nst) + 1) & 1u;            // parity of the slot's previous use
   for (int bi = b0; bi < b1; ++bi) {
     const DDSrc w0 = src(bi * UB, 0);
     const DDSrc w1 = KIND == 1 ? src(bi * UB, 1) : DDSrc{nullptr, 0, nullptr};
     for (int kc = 0; kc < nkc; ++kc, ++t) {
-      const int s = t % rg.nst;
-      if (t >= rg.nst && !ring_wait_empty(rg, s, ((t / rg.nst) - 1) & 1, err)) return false;
+      if (t >= rg.nst && !ring_wait_empty(rg, s, par, err)) return false;
       if (lane == 0) {
         unsigned char* st = rg.base + (size_t)s * ST_BYTES;
         mbar_arrive_expect_tx(&rg.full[s], (unsigned)ST_BYTES);
@@ -793,6 +794,10 @@ __device__ __forceinline__ bool produce_task_tc(Ring& rg, int& t, int units, int
         }
       }
       __syncwarp();
+      if (++s == rg.nst) {
+        s = 0;
+        par ^= 1u;
+      }
     }
   }
   return true;
@@ -923,52 +928,62 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
       const int nk = ln ? (min(KX, K - p * KX) >> 8) * NM : min(ncp, (K - p * KX + C - 1) / C);
       if (warp == 0) {
         tc_after();
-        for (int kcp = 0; kcp < nk; ++kcp) {
-          const int t = c.t + kcp, s = t % rg.nst;
-          const bool ok = mbar_wait_warp(ln ? &g_dd_dfull[s] : &rg.full[s], (t / rg.nst) & 1, err);
-          if (det && lane == 0 && bi == b0 && p == 0 && kcp == 0) det[1] = globaltimer();
-          if (!ok && lane == 0) *abort_flag = 1;
-          if (lane == 0 && ok && ln) {
-            // LN12 stage: K slice ks of the pass (1024 (ks / 4) + 256 c + 64 (ks % 4) + 0..63 for strips c = 0..3),
-            // matrix mm; M = 64 MMAs, chain jj = the 16-column step within the strip
-            const uint32_t wa = smem_u32(rg.base + (size_t)s * ST_BYTES);
-            const int ks = kcp / NM, mm = kcp - ks * NM;
-            const uint32_t dcol = tmem + (uint32_t)(mm * 64);
+        if (lane == 0) {
+          // Lane 0 alone waits and issues; the ring position advances without divisions
+          int s = c.t % rg.nst;
+          unsigned par = (unsigned)(c.t / rg.nst) & 1u;
+          const uint32_t ring0 = smem_u32(rg.base);
+          for (int kcp = 0; kcp < nk; ++kcp) {
+            const bool ok = mbar_wait(ln ? &g_dd_dfull[s] : &rg.full[s], par, err);
+            if (det && bi == b0 && p == 0 && kcp == 0) det[1] = globaltimer();
+            if (!ok) *abort_flag = 1;
+            const uint32_t wa = ring0 + (uint32_t)s * ST_BYTES;
+            if (ok && ln) {
+              // LN12 stage: K slice ks of the pass (1024 (ks / 4) + 256 c + 64 (ks % 4) + 0..63 for strips c = 0..3),
+              // matrix mm; M = 64 MMAs, chain jj = the 16-column step within the strip
+              const int ks = kcp / NM, mm = kcp - ks * NM;
+              const uint32_t dcol = tmem + (uint32_t)(mm * 64);
+              const uint32_t xs0 = xsa + (uint32_t)((((ks >> 2) << 4) + (ks & 3)) << 11);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int cs = j >> 2, jj = j & 3;
-              const int blk = ((ks >> 2) << 4) + (cs << 2) + (ks & 3);     // 64-column block of the staged pass
-              const uint64_t bd = tc_desc_sw128(xsa + (uint32_t)(blk << 11) + (uint32_t)(jj << 5));
-              const uint32_t acc = (p > 0 || ks > 0 || cs > 0) ? 1u : 0u;
-              tc_mma16_m64(dcol + (uint32_t)(jj * 16), tc_desc_sw128(wa + (uint32_t)(cs * 8192 + jj * 32)), bd, acc);
-            }
-          } else if (lane == 0 && ok) {
-            const uint32_t wa = smem_u32(rg.base + (size_t)s * ST_BYTES);
+              for (int j = 0; j < 16; ++j) {
+                const int cs = j >> 2, jj = j & 3;
+                const uint32_t acc = (p > 0 || ks > 0 || cs > 0) ? 1u : 0u;
+                tc_mma16_m64(dcol + (uint32_t)(jj * 16), tc_desc_sw128(wa + (uint32_t)(cs * 8192 + jj * 32)),
+                             tc_desc_sw128(xs0 + (uint32_t)(cs * 8192 + jj * 32)), acc);
+              }
+            } else if (ok) {
+              // activations: 64-column blocks of 16 rows x 128 B (2 KB) from block kcp C / 64 of the pass
+              const uint32_t xs0 = xsa + (uint32_t)(kcp * (C / 64)) * 2048u;
 #pragma unroll
-            for (int j = 0; j < C / 16; ++j) {
-              const int kk = kcp * C + 16 * j;                   // column within the staged pass
-              const uint64_t bd = tc_desc_sw128(xsa + (uint32_t)((kk >> 6) << 11) + (uint32_t)(((kk & 63) >> 4) << 5));
-              const uint32_t ka = (uint32_t)((j >> 2) * (KIND == 2 ? 128 * 128 : 64 * 128) + (j & 3) * 32);
-              if (KIND == 1) {
-                // gate: [128 rows][128 B] at 0, up at 16 KB; two chains each
-                const uint32_t acc = (p > 0 || kcp > 0 || j >= 2) ? 1u : 0u;
-                const uint32_t ch = (uint32_t)((j & 1) * 16);
-                tc_mma16(tmem + ch, tc_desc_sw128(wa + (j & 3) * 32), bd, acc);
-                tc_mma16(tmem + 32 + ch, tc_desc_sw128(wa + ST_BYTES / 2 + (j & 3) * 32), bd, acc);
-              } else if (KIND == 0) {
-                const uint32_t acc = (p > 0 || kcp > 0 || j >= 4) ? 1u : 0u;
-                tc_mma16_m64(tmem + (uint32_t)((j & 3) * 16), tc_desc_sw128(wa + ka), bd, acc);
-              } else {
-                const uint32_t acc = (p > 0 || kcp > 0 || j >= 4) ? 1u : 0u;
-                tc_mma16(tmem + (uint32_t)((j & 3) * 16), tc_desc_sw128(wa + ka), bd, acc);
+              for (int j = 0; j < C / 16; ++j) {
+                const uint64_t bd =
+                    tc_desc_sw128(xs0 + (uint32_t)(((16 * j) >> 6) * 2048 + (((16 * j) & 63) >> 4) * 32));
+                if (KIND == 1) {
+                  // gate: [128 rows][128 B] at 0, up at 16 KB; two chains each
+                  const uint32_t acc = (p > 0 || kcp > 0 || j >= 2) ? 1u : 0u;
+                  const uint32_t ch = (uint32_t)((j & 1) * 16);
+                  tc_mma16(tmem + ch, tc_desc_sw128(wa + (uint32_t)((j & 3) * 32)), bd, acc);
+                  tc_mma16(tmem + 32 + ch, tc_desc_sw128(wa + (uint32_t)(ST_BYTES / 2 + (j & 3) * 32)), bd, acc);
+                } else if (KIND == 0) {
+                  const uint32_t acc = (p > 0 || kcp > 0 || j >= 4) ? 1u : 0u;
+                  const uint64_t ad = tc_desc_sw128(wa + (uint32_t)((j >> 2) * 8192 + (j & 3) * 32));
+                  tc_mma16_m64(tmem + (uint32_t)((j & 3) * 16), ad, bd, acc);
+                } else {
+                  const uint32_t acc = (p > 0 || kcp > 0 || j >= 4) ? 1u : 0u;
+                  const uint64_t ad = tc_desc_sw128(wa + (uint32_t)((j >> 2) * 16384 + (j & 3) * 32));
+                  tc_mma16(tmem + (uint32_t)((j & 3) * 16), ad, bd, acc);
+                }
               }
             }
+            tc_commit(&rg.empty[s]);
+            if (++s == rg.nst) {
+              s = 0;
+              par ^= 1u;
+            }
           }
-          if (lane == 0) tc_commit(&rg.empty[s]);
-          __syncwarp();
+          if (det && bi == b0) det[2] = globaltimer();
+          tc_commit(&g_dd_mbar);
         }
-        if (det && lane == 0 && bi == b0) det[2] = globaltimer();
-        if (lane == 0) tc_commit(&g_dd_mbar);
         __syncwarp();
       } else if constexpr (ln) {
         ln12_decode_stages(rg, c.t, nk, err, abort_flag);
