@@ -289,17 +289,18 @@ def _time_prefill(call, dev, iters, warmup):
 
 
 def measure_prefill(dev, world, rank, iters=50, warmup=5, long_len=4096, long_iters=10):
-    """Config 5's causal GQA prefill attention on the tcgen05 kernel, inputs resident.  With 2 or more ranks the
-    call is split (``prefill_attention_sharded``: by KV-head group when the ranks divide the 4 KV heads, else by
-    causal-balanced query-row tiles, as for 8 ranks) and one NCCL all_gather_into_tensor assembles the output; one
-    rank runs the whole call.  A long prompt (L = long_len) is timed both ways on every N, where a split can pay.
+    """Config 5's causal GQA prefill attention on the tcgen05 kernel, inputs resident.  With 2 or more ranks a
+    prompt of at least ``prefill_attn.SPLIT_MIN_LEN`` rows is split (``prefill_attention_sharded``: by KV-head group
+    when the ranks divide the 4 KV heads, else by causal-balanced query-row tiles, as for 8 ranks) and one NCCL
+    all_gather_into_tensor assembles the output; a shorter one (config 5) runs whole on every rank.  A long prompt
+    (L = long_len) is timed on one GPU and, for N > 1, split over the ranks.
     Returns the bench line's ``prefill`` object (rank 0) with TFLOP/s of the whole call."""
     from flashb import prefill_attn
     c = PREFILL_CFG
     B, NH, NKV, L, D = c['B'], c['NH'], c['NKV'], c['L'], c['D']
     q, k, v, m = _prefill_inputs(dev, B, NH, NKV, L, D, c['pads'])
-    sharded = world > 1
-    split = ('heads' if NKV % world == 0 else 'rows') if sharded else None
+    sharded = world > 1 and L >= prefill_attn.SPLIT_MIN_LEN          # config 5 is too short to gain from a split
+    split = ('heads' if NKV % world == 0 else 'rows') if world > 1 else None
 
     def call():
         if sharded:
@@ -315,7 +316,7 @@ def measure_prefill(dev, world, rank, iters=50, warmup=5, long_len=4096, long_it
     ms1 = _time_prefill(lambda: prefill_attn.prefill_attention(ql, kl, vl, ml, D ** -0.5), dev, long_iters, 2)
     fll = prefill_flops(B, NH, long_len, D)
     long = dict(L=long_len, ms_one_gpu=round(ms1, 4), tflops_one_gpu=round(fll / (ms1 / 1e3) / 1e12, 2))
-    if sharded:
+    if world > 1:
         msn = _time_prefill(lambda: prefill_attn.prefill_attention_sharded(ql, kl, vl, ml, D ** -0.5), dev,
                             long_iters, 2)
         long.update(ms_sharded=round(msn, 4), split=split, speedup=round(ms1 / msn, 3),

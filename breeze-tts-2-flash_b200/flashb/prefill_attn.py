@@ -150,17 +150,25 @@ def gather_row_shards(part, ranges, L, group=None, out=None):
     return out
 
 
+# Shortest prompt 'auto' splits over ranks: measured on 2 x B200, L 512 ran 63 us on one GPU and 101 us split (the
+# all-gather dominates), L 4096 1.81 ms on one GPU and 1.14 ms split.
+SPLIT_MIN_LEN = 2048
+
+
 def prefill_attention_sharded(query, key, value, attention_mask, scaling, group=None, causal=True, split='auto'):
     """Multi-GPU prefill attention, every rank of ``group`` returning out [B, L, NH, 128].  split 'heads': each rank
     computes the q heads of its KV-head group (reading only that group's K/V; NKV % world_size == 0); 'rows': each
-    rank computes a contiguous range of 128-row query tiles balanced for the causal work (any world size); 'auto':
-    heads when the ranks divide the KV heads, else rows."""
+    rank computes a contiguous range of 128-row query tiles balanced for the causal work (any world size); 'none':
+    every rank computes the whole call; 'auto': none below SPLIT_MIN_LEN query rows, else heads when the ranks divide
+    the KV heads, else rows."""
     import torch.distributed as dist
     B, NH, L, D = query.shape
     n, r = dist.get_world_size(group), dist.get_rank(group)
     NKV = key.shape[1]
     if split == 'auto':
-        split = 'heads' if NKV % n == 0 else 'rows'
+        split = 'none' if (L < SPLIT_MIN_LEN or n == 1) else ('heads' if NKV % n == 0 else 'rows')
+    if split == 'none':
+        return prefill_attention(query, key, value, attention_mask, scaling, causal=causal)
     if split == 'heads':
         h0, h1 = shard_heads(NH, NKV, n, r)
         part = torch.empty(B, L, h1 - h0, D, dtype=torch.bfloat16, device=query.device)
