@@ -90,8 +90,19 @@ __device__ __forceinline__ void set_error(unsigned* err, unsigned code) {
   if (err) atomicCAS(err, 0u, code);
 }
 
+// Non-blocking test of a phase (no suspension window): the fast path of a wait whose phase is usually complete.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
 #pragma unroll 1

@@ -30,6 +30,7 @@
 #define FB_ST_KC 1024
 #define FB_ST_TMA 1
 #define FB_PK_MAX_STAGES 8
+#include <cstring>
 #include <mutex>
 
 #include "fb_persist.cuh"
@@ -87,6 +88,12 @@ struct alignas(64) DDArgs {
   GridBar* bar;
   int nstages, xs_bytes, att_off, keep_off, att_bc, att_split, d_xchunk;
   int keep_cols;                          // tcgen05 build: x_mid kept only for the CTA's S4 columns (0 = all)
+  // tcgen05 bf16 build: 128-row tasks with split K (0 = the 64-row task) for the projector, o, down, the heads; the
+  // fp32 partial sums of split parts and their per-block publication tags (zeroed at every frame start)
+  int s3_proj, s3_o, s3_down, s3_head;
+  float* part;
+  unsigned* flags;
+  int nflags;
   unsigned long long wait_ns;             // grid-barrier wait limit
   const bf16 *ptab, *ttab;                // optional per-token step table (codebook steps >= 1), or null
   int l2_keep;                            // 1: weight copies carry the L2 evict_last hint
@@ -1107,19 +1114,210 @@ __device__ __forceinline__ bool consume_task_tc(Ring& rg, DDCur& c, int units, i
   return true;
 }
 
+// ------------------------------------------------------------------------------------------------ 128-row tasks
+// A plain GEMV task (o, down, projector, heads) in blocks of 128 output units split over S parts of K: item i =
+// (block i / S, part i % S), CTA c owns items [items c / G, items (c + 1) / G).  A stage is 128 rows x 128 columns
+// ([2][128 rows][128 B], the q|k|v stage layout), consumed by 8 M = 128 MMAs -- twice the bytes per MMA of the
+// 64-row task, whose M = 64 MMAs cost the same issue time.  Parts 0 .. S - 2 publish their fp32 sums (release tag
+// in a.flags); the CTA holding part S - 1 waits for them (bounded), adds them in part order before its own, and
+// runs the epilogue.  Items are assigned in order, so a waiter only waits for items of earlier CTAs or its own.
+__device__ __forceinline__ void tc3_items(int units, int S, int& i0, int& i1) {
+  const int items = (units >> 7) * S;
+  i0 = (int)((long long)items * blockIdx.x / gridDim.x);
+  i1 = (int)((long long)items * (blockIdx.x + 1) / gridDim.x);
+}
+
+template <typename SrcFn>
+__device__ __forceinline__ bool produce_task_tc3(Ring& rg, int& t, int units, int K, int S, SrcFn src,
+                                                 unsigned* err) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t pol = g_dd_l2keep ? policy_evict_last() : policy_evict_normal();
+  const int nks = (K / S) >> 7;
+  int i0, i1;
+  tc3_items(units, S, i0, i1);
+  int s = t % rg.nst;
+  unsigned par = (unsigned)((t / rg.nst) + 1) & 1u;
+  for (int it = i0; it < i1; ++it) {
+    const int blk = it / S, part = it - blk * S;
+    const DDSrc w = src(blk * 128, 0);
+    for (int kc = 0; kc < nks; ++kc, ++t) {
+      if (t >= rg.nst && !ring_wait_empty(rg, s, par, err)) return false;
+      if (lane == 0) {
+        unsigned char* st = rg.base + (size_t)s * ST_BYTES;
+        mbar_arrive_expect_tx(&rg.full[s], (unsigned)ST_BYTES);
+        tma_load_3d_l2(st, w.map, 0, w.row, (part * nks + kc) * 2, &rg.full[s], pol);   // [2][128 rows][128 B]
+      }
+      __syncwarp();
+      if (++s == rg.nst) {
+        s = 0;
+        par ^= 1u;
+      }
+    }
+  }
+  return true;
+}
+
+template <typename EpiFn, typename StageFn>
+__device__ __forceinline__ bool consume_task_tc3(const DDArgs& a, Ring& rg, DDCur& c, int units, int K, int S,
+                                                 const unsigned char* xs, float* dump, EpiFn epi, StageFn stage_x,
+                                                 unsigned long long* det) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Kp = K / S, nks = Kp >> 7;
+  const int KX = K < DD_TC_KX ? K : DD_TC_KX;
+  int i0, i1;
+  tc3_items(units, S, i0, i1);
+  const uint32_t tmem = g_dd_tmem, xsa = smem_u32(xs);
+  unsigned* const err = a.err;
+  int* abort_flag = &g_dd_int[29];
+  if (tid == 0) *abort_flag = 0;
+  fence_proxy_async();                 // the caller's staging (pass 0) -> visible to the tensor core
+  named_sync(1, PK_CONSUMERS);
+  if (det && tid == 0) {
+    det[0] = globaltimer();
+    det[7] = (unsigned long long)(i1 - i0);
+  }
+  const unsigned tag = c.epoch + 1u;   // unique per phase within the frame (flags are zeroed at frame start)
+  int staged = 0;
+  for (int it = i0; it < i1; ++it) {
+    const int blk = it / S, part = it - blk * S;
+    const int k0 = part * Kp, pass = k0 / KX, kin = k0 - pass * KX;
+    if (pass != staged) {
+      stage_x(pass);
+      fence_proxy_async();
+      named_sync(1, PK_CONSUMERS);
+      staged = pass;
+    }
+    if (warp == 0) {
+      tc_after();
+      if (lane == 0) {
+        int s = c.t % rg.nst;
+        unsigned par = (unsigned)(c.t / rg.nst) & 1u;
+        const uint32_t ring0 = smem_u32(rg.base);
+        for (int kcp = 0; kcp < nks; ++kcp) {
+          const bool ok = mbar_wait(&rg.full[s], par, err);
+          if (det && it == i0 && kcp == 0) det[1] = globaltimer();
+          if (!ok) *abort_flag = 1;
+          if (ok) {
+            const uint32_t wa = ring0 + (uint32_t)s * ST_BYTES;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int col = kin + kcp * 128 + 16 * j;            // column within the staged pass
+              const uint64_t bd =
+                  tc_desc_sw128(xsa + (uint32_t)((col >> 6) << 11) + (uint32_t)(((col & 63) >> 4) << 5));
+              const uint64_t ad = tc_desc_sw128(wa + (uint32_t)((j >> 2) * 16384 + (j & 3) * 32));
+              tc_mma16(tmem + (uint32_t)((j & 3) * 16), ad, bd, (kcp > 0 || j >= 4) ? 1u : 0u);
+            }
+          }
+          tc_commit(&rg.empty[s]);
+          if (++s == rg.nst) {
+            s = 0;
+            par ^= 1u;
+          }
+        }
+        if (det && it == i0) det[2] = globaltimer();
+        tc_commit(&g_dd_mbar);
+      }
+      __syncwarp();
+    }
+    c.t += nks;
+    if (!mbar_wait(&g_dd_mbar, c.tph & 1, err)) *abort_flag = 1;
+    ++c.tph;
+    tc_after();
+    if (det && tid == 0 && it == i0) det[3] = globaltimer();
+    if (warp < 4) {
+      // unit L = TMEM lane; its 16 activation rows are the columns of the four chains
+      const int L = warp * 32 + lane;
+      const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
+      float c0[16], c1[16], v[16];
+      tc_ld16(tq, c0);
+      tc_ld16(tq + 16, c1);
+#pragma unroll
+      for (int m = 0; m < 16; ++m) v[m] = c0[m] + c1[m];
+      tc_ld16(tq + 32, c0);
+      tc_ld16(tq + 48, c1);
+      float* d = dump + (L >> 4) * 256 + (L & 15) * 16;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) d[m] = (v[m] + c0[m]) + c1[m];
+    }
+    tc_before();
+    named_sync(1, PK_CONSUMERS);
+    if (det && tid == 0 && it == i0) det[4] = globaltimer();
+    if (*abort_flag) return false;
+    float* const pb = a.part + (size_t)blk * (S - 1) * 2048;
+    if (part < S - 1) {
+      for (int i = tid; i < 2048; i += PK_CONSUMERS) __stcg(pb + (size_t)part * 2048 + i, dump[i]);
+      __threadfence();
+      named_sync(1, PK_CONSUMERS);
+      if (tid == 0) st_release_u32(&a.flags[blk * (S - 1) + part], tag);
+    } else {
+      if (S > 1) {
+        if (tid == 0) {
+          int ok = 1;
+          const uint64_t t0 = globaltimer();
+          for (int q = 0; q < S - 1 && ok; ++q) {
+            int spins = 0;
+            while (ld_acquire_u32(&a.flags[blk * (S - 1) + q]) != tag) {
+              if (++spins == 256) {
+                spins = 0;
+                if (ld_acquire_u32(&a.bar->abort)) {
+                  set_error(err, FB_ERR_ABORTED);
+                  ok = 0;
+                  break;
+                }
+                if (globaltimer() - t0 > a.wait_ns) {
+                  set_error(err, FB_ERR_TIMEOUT);
+                  atomicExch(&a.bar->abort, 1u);
+                  ok = 0;
+                  break;
+                }
+              }
+            }
+          }
+          *abort_flag = ok ? 0 : 1;
+        }
+        named_sync(1, PK_CONSUMERS);
+        if (*abort_flag) return false;
+        for (int i = tid; i < 2048; i += PK_CONSUMERS) {
+          float v = __ldcg(pb + i);
+          for (int q = 1; q < S - 1; ++q) v += __ldcg(pb + (size_t)q * 2048 + i);
+          dump[i] = v + dump[i];
+        }
+        named_sync(1, PK_CONSUMERS);
+      }
+      // 8 groups of 16 units, as many side by side as the threads allow (a group uses 16 M threads)
+      const int gw = 16 * a.B;
+      const int gq = gw >= PK_CONSUMERS ? 1 : PK_CONSUMERS / gw;
+      const int gs = tid / gw, lt = tid - gs * gw;
+      for (int g = gs; g < 8 && gs < gq; g += gq) {
+        const int n0 = blk * 128 + g * 16;
+        const int nu = min(16, units - n0);
+        if (nu > 0) epi(n0, nu, dump + g * 256, lt);
+      }
+    }
+    if (det && tid == 0 && it == i0) det[5] = globaltimer();
+    named_sync(1, PK_CONSUMERS);       // the dump and the accumulators are reused by the next item
+  }
+  if (det && tid == 0) det[6] = globaltimer();
+  return true;
+}
+
 // One GEMV task of a phase: the mma.sync stream (NT > 0; KIND 1 / 2 -> two matrices per unit) or the tcgen05 path
 // (NT = 0).  x_pitch: the staged activations' row pitch (mma.sync builds).  xg / ldx: activations too large to stage
 // whole (mma.sync, column chunks).  stage_x: restaging of further K passes (tcgen05 build).
 template <int NT, int KIND, typename EpiFn, typename StageFn>
 __device__ __forceinline__ bool dd_gemv(const DDArgs& a, DDSm& m, DDCur& c, int units, int K, int x_pitch, EpiFn epi,
-                                        StageFn stage_x, const bf16* xg = nullptr, long ldx = 0) {
+                                        StageFn stage_x, const bf16* xg = nullptr, long ldx = 0, int s3 = 0) {
   if constexpr (NT <= 0) {
     // trace builds: the first DD_DETAIL_CALLS tasks of each CTA record a detail timeline after the phase trace
     unsigned long long* det = nullptr;
     const int call = g_dd_call;
     if (a.trace && call < DD_DETAIL_CALLS)
       det = a.trace + (size_t)gridDim.x * a.NCB * DD_TRACE_SLOTS(a.L) + ((size_t)blockIdx.x * DD_DETAIL_CALLS + call) * 8;
-    const bool ok = consume_task_tc<KIND, (NT < 0)>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err, det, a.B);
+    bool ok;
+    if (NT == 0 && KIND == 0 && s3 > 0)
+      ok = consume_task_tc3(a, m.rg, c, units, K, s3, m.xs, m.red, epi, stage_x, det);
+    else
+      ok = consume_task_tc<KIND, (NT < 0)>(m.rg, c, units, K, m.xs, m.red, epi, stage_x, a.err, det, a.B);
     if (threadIdx.x == 0) g_dd_call = call + 1;
     return ok;
   } else {
@@ -1152,9 +1350,10 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
     const bool tab = a.ptab && s >= 1;     // stage E and layer 0's q|k|v come from the step table
     for (int sub = 0; sub < (s == 0 ? 2 : 1) && ok; ++sub) {
       if constexpr (NT <= 0) {
+        auto src = [&](int n, int) { return DDSrc{&a.tm_proj, n, &a.ln_proj}; };
         if (!tab)
-          ok = ok && produce_task_tc<0, ln>(m.rg, t, H, AE, [&](int n, int) { return DDSrc{&a.tm_proj, n, &a.ln_proj}; },
-                                        err);
+          ok = ok && (a.s3_proj && !ln ? produce_task_tc3(m.rg, t, H, AE, a.s3_proj, src, err)
+                                       : produce_task_tc<0, ln>(m.rg, t, H, AE, src, err));
       } else {
         if (!tab)
           ok = ok && produce_task_tma<1>(m.rg, t, H, AE, [&](int n, int) { return TmaRows{&a.tm_proj, n}; }, err);
@@ -1171,13 +1370,15 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
             if (hh < NH + NKV) return DDSrc{&W[DD_WK], (hh - NH) * 128, &LW[DD_WK]};
             return DDSrc{&W[DD_WV], (hh - NH - NKV) * 128, &LW[DD_WV]};
           }, err);
-          ok = ok && produce_task_tc<0, ln>(m.rg, t, H, NH * 128,
-                                        [&](int n, int) { return DDSrc{&W[DD_WO], n, &LW[DD_WO]}; }, err);
+          auto src_o = [&](int n, int) { return DDSrc{&W[DD_WO], n, &LW[DD_WO]}; };
+          ok = ok && (a.s3_o && !ln ? produce_task_tc3(m.rg, t, H, NH * 128, a.s3_o, src_o, err)
+                                    : produce_task_tc<0, ln>(m.rg, t, H, NH * 128, src_o, err));
           ok = ok && produce_task_tc<1, ln>(m.rg, t, F, H, [&](int n, int mat) {
             return DDSrc{&W[mat ? DD_WU : DD_WG], n, &LW[mat ? DD_WU : DD_WG]};
           }, err);
-          ok = ok && produce_task_tc<0, ln>(m.rg, t, H, F, [&](int n, int) { return DDSrc{&W[DD_WD], n, &LW[DD_WD]}; },
-                                        err);
+          auto src_d = [&](int n, int) { return DDSrc{&W[DD_WD], n, &LW[DD_WD]}; };
+          ok = ok && (a.s3_down && !ln ? produce_task_tc3(m.rg, t, H, F, a.s3_down, src_d, err)
+                                       : produce_task_tc<0, ln>(m.rg, t, H, F, src_d, err));
         } else {
           // unit u = (head hh, rotary pair d): matrix 0 carries row hh * 128 + d, matrix 1 row hh * 128 + 64 + d
           if (!skip_qkv) ok = ok && produce_task_tma<2>(m.rg, t, QKVU, H, [&](int u, int mat) {
@@ -1194,9 +1395,11 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
       }
     }
     if constexpr (NT <= 0) {
-      ok = ok && produce_task_tc<0, ln>(m.rg, t, V, H, [&](int n, int) {
+      auto src_h = [&](int n, int) {
         return ln ? DDSrc{&a.tm_hd[s], n, &a.ln_hd[s]} : DDSrc{&a.tm_head, s * V + n, nullptr};
-      }, err);
+      };
+      ok = ok && (a.s3_head && !ln ? produce_task_tc3(m.rg, t, V, H, a.s3_head, src_h, err)
+                                   : produce_task_tc<0, ln>(m.rg, t, V, H, src_h, err));
     } else {
       ok = ok && produce_task_tma<1>(m.rg, t, V, H, [&](int n, int) { return TmaRows{&a.tm_head, s * V + n}; }, err);
     }
@@ -1204,6 +1407,24 @@ __device__ __noinline__ void dd_producer(const DDArgs& a) {
   // never leave with copies in flight into this CTA's shared memory
   for (int u = max(0, t - m.rg.nst); u < t; ++u)
     if (!mbar_wait_warp(&m.rg.full[u % m.rg.nst], (u / m.rg.nst) & 1, err)) break;
+}
+
+// First output column of this CTA's S4 (down) work in the tcgen05 build: its first 64-unit block, or with the
+// 128-row split task the block of its first item (x_mid is kept from there for a.keep_cols columns).
+template <int NT>
+__device__ __forceinline__ int dd_s4_col0(const DDArgs& a) {
+  if constexpr (NT > 0) {
+    return 0;
+  } else {
+    if (NT == 0 && a.s3_down) {
+      int i0, i1;
+      tc3_items(a.H, a.s3_down, i0, i1);
+      return (i0 / a.s3_down) * 128;
+    }
+    int b0, b1;
+    tc_task_blocks<0>(a.H, b0, b1, false);
+    return b0 * 64;
+  }
 }
 
 // E: gather the token embeddings (cp.async, one round trip, with the position's rotary rows) -> projector -> xres
@@ -1242,7 +1463,7 @@ __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int su
                           const int i = lt / M, r = lt - i * M;
                           xres[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
                         }
-                      }, [](int) {})) {
+                      }, [](int) {}, nullptr, 0, a.s3_proj)) {
     c.ok = 0;
     return c;
   }
@@ -1389,7 +1610,7 @@ __device__ __noinline__ DDCur dd_phase_s2(const DDArgs& a, DDCur c, int s, int p
                           const int i = lt / M, r = lt - i * M;
                           ob[(size_t)r * H + n0 + i] = __float2bfloat16_rn(sm[i * MS + r]);
                         }
-                      }, [](int) {})) {
+                      }, [](int) {}, nullptr, 0, a.s3_o)) {
     c.ok = 0;
     return c;
   }
@@ -1409,9 +1630,7 @@ __device__ __noinline__ DDCur dd_phase_s3(const DDArgs& a, DDCur c, int s, int l
   bf16* xkeep = reinterpret_cast<bf16*>(m.xs + a.keep_off);
   bf16* const act = a.act;
   const int xp = (NT > 0) ? H * 2 + 16 : 0;
-  int kb0 = 0, kb1 = 0;
-  if (NT <= 0) tc_task_blocks<0>(H, kb0, kb1, false);          // this CTA's S4 blocks of 64 output columns
-  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep, kb0 * 64);
+  dd_load_mid(m.xs, xp, a, M, a.layers[l].ln2, g_dd_nred, xkeep, dd_s4_col0<NT>(a));
   if (!dd_gemv<NT, 1>(a, m, c, F, H, xp,
                       [&](int n0, int nu, const float* sm, int lt) {
                         if (lt < nu * M) {
@@ -1440,9 +1659,7 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
   const bf16* xkeep = reinterpret_cast<const bf16*>(m.xs + a.keep_off);
   bf16* const xres = a.xres;
   const int kc = a.keep_cols;
-  int kb0 = 0, kb1 = 0;
-  if (NT <= 0) tc_task_blocks<0>(H, kb0, kb1, false);
-  const int kc0 = kb0 * 64;
+  const int kc0 = dd_s4_col0<NT>(a);
   // tcgen05 build: act in passes of DD_TC_KX columns; mma.sync: whole, or in column chunks (d_xchunk)
   auto stage = [&](int p) {
     const int k0 = p * DD_TC_KX;
@@ -1457,7 +1674,7 @@ __device__ __noinline__ DDCur dd_phase_s4(const DDArgs& a, DDCur c, int s, int l
                           const float xm = b2f(kc ? xkeep[(size_t)r * kc + (n - kc0)] : xkeep[(size_t)r * H + n]);
                           xres[(size_t)r * H + n] = __float2bfloat16_rn(xm + rbf(sm[i * MS + r]));
                         }
-                      }, stage, a.d_xchunk ? a.act : nullptr, F)) {
+                      }, stage, a.d_xchunk ? a.act : nullptr, F, a.s3_down)) {
     c.ok = 0;
     return c;
   }
@@ -1485,7 +1702,7 @@ __device__ __noinline__ DDCur dd_phase_s5(const DDArgs& a, DDCur c, int s) {
                           logits[(size_t)b * V + n0 + i] = v;
                           if (dbg) dbg[((size_t)s * M + b) * V + n0 + i] = v;
                         }
-                      }, [](int) {})) {
+                      }, [](int) {}, nullptr, 0, a.s3_head)) {
     c.ok = 0;
     return c;
   }
@@ -1557,6 +1774,8 @@ __global__ void __launch_bounds__(PK_THREADS, 1) dd_frame_kernel(const __grid_co
     if (tid == 0) g_dd_l2keep = a.l2_keep;
     if (NT <= 0 && warp == 0) tc_alloc(&g_dd_tmem, NT < 0 ? 128 : 64);  // 4 chains x 16 columns (LN12: x 2)
   }
+  // the split tasks' publication tags start every frame at zero (ordered before their first use by a grid barrier)
+  if (NT == 0 && a.flags && blockIdx.x == 0 && tid < a.nflags) a.flags[tid] = 0u;
   if (NT <= 0) tc_before();
   __syncthreads();
   if (NT <= 0) tc_after();
@@ -1605,8 +1824,10 @@ namespace {
 using namespace fb;
 
 struct DDLayout {
-  size_t xres, qb, ob, act, kc, vc, logits, bar, total;
+  size_t xres, qb, ob, act, kc, vc, logits, bar, part, flags, total;
 };
+// Blocks of 128 output units a split task may cover (the hidden size or the codebook vocabulary).
+int dd_split_blocks(const fb_dd_config* c) { return ((c->hidden > c->vocab ? c->hidden : c->vocab) + 127) / 128; }
 size_t al256d(size_t v) { return (v + 255) / 256 * 256; }
 
 DDLayout dd_layout(const fb_dd_config* c) {
@@ -1622,6 +1843,8 @@ DDLayout dd_layout(const fb_dd_config* c) {
   s.vc = o; o = al256d(o + (size_t)c->layers * c->batch * c->kv_heads * P * 128 * 2);
   s.logits = o; o = al256d(o + (size_t)c->batch * c->vocab * 4);
   s.bar = o; o = al256d(o + sizeof(GridBar));
+  s.part = o; o = al256d(o + (size_t)dd_split_blocks(c) * 2048 * 4);     // one fp32 partial (S = 2) per block
+  s.flags = o; o = al256d(o + (size_t)dd_split_blocks(c) * 4);
   s.total = o;
   return s;
 }
@@ -1738,6 +1961,7 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   a.xres = (bf16*)(sc + Lo.xres); a.qb = (bf16*)(sc + Lo.qb); a.ob = (bf16*)(sc + Lo.ob);
   a.act = (bf16*)(sc + Lo.act); a.kc = (bf16*)(sc + Lo.kc); a.vc = (bf16*)(sc + Lo.vc);
   a.logits = (float*)(sc + Lo.logits); a.bar = (GridBar*)(sc + Lo.bar);
+  a.part = (float*)(sc + Lo.part); a.flags = (unsigned*)(sc + Lo.flags); a.nflags = dd_split_blocks(c);
   a.err = fbh::device_err_ptr();
   a.wait_ns = c->wait_ns > 0 ? (unsigned long long)c->wait_ns : WAIT_LIMIT_NS;
   a.trace = (unsigned long long*)c->trace;
@@ -1772,17 +1996,43 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
       if (!tc) return fbh::tmap_rows(out, base, rows, K, ST_KC);
       return fbh::tmap_box(out, base, rows, K, 64, kind == 0 ? 64 : 128, kind == 0 ? 4 : (kind == 1 ? 1 : 2), true);
     };
-    int rc = map(&a.tm_proj, c->proj, c->hidden, c->embed_dim, 0);
-    if (!rc) rc = map(&a.tm_head, c->head_t, (long long)c->n_decode * c->vocab, c->hidden, 0);
+    // tcgen05 bf16 build: the plain matrices as 128-row tasks (maps of 128-row boxes), split in 2 parts of K when
+    // that still leaves no more items than CTAs and each part stays inside one staged pass of activations
+    auto fits = [&](int K, int S) {          // every part of K inside one staged pass of activations
+      const int KX = K < DD_TC_KX ? K : DD_TC_KX, Kp = K / S;
+      for (int p = 0; p < S; ++p)
+        if ((p * Kp) % KX + Kp > KX) return false;
+      return true;
+    };
+    auto split_of = [&](long long rows, int K) {
+      if (!tc || c->ln12 || rows % 128) return 0;
+      if (2 * (rows / 128) <= grid && K % 256 == 0 && fits(K, 2)) return 2;
+      return (K % 128 == 0 && fits(K, 1)) ? 1 : 0;
+    };
+    // Which tasks take the 128-row form (tuning: FLASHB_DD_TASK128 = four digits for projector, o, down, heads;
+    // default 0011).  Measured at the bench's lane (B = 16, grid 18, a frame alone): 6.613 ms with none, 6.575 with
+    // the heads, 6.535 with the heads and the split down, 6.754 adding the split o: its parts' exchange through L2
+    // (about 3 us) outweighs the shorter MMA stream of a 1024-column task.
+    const char* t128 = getenv("FLASHB_DD_TASK128");
+    const bool use128[4] = {t128 && strlen(t128) == 4 ? t128[0] == '1' : false,
+                            t128 && strlen(t128) == 4 ? t128[1] == '1' : false,
+                            t128 && strlen(t128) == 4 ? t128[2] == '1' : true,
+                            t128 && strlen(t128) == 4 ? t128[3] == '1' : true};
+    a.s3_proj = use128[0] ? split_of(c->hidden, c->embed_dim) : 0;
+    a.s3_o = use128[1] ? split_of(c->hidden, QD) : 0;
+    a.s3_down = use128[2] ? split_of(c->hidden, c->ffn) : 0;
+    a.s3_head = use128[3] ? split_of(c->vocab, c->hidden) : 0;
+    int rc = map(&a.tm_proj, c->proj, c->hidden, c->embed_dim, a.s3_proj ? 2 : 0);
+    if (!rc) rc = map(&a.tm_head, c->head_t, (long long)c->n_decode * c->vocab, c->hidden, a.s3_head ? 2 : 0);
     for (int l = 0; l < c->layers && !rc; ++l) {
       const DDLayer& W = hl[l];
       rc = map(&a.tm[l][DD_WQ], W.wq, QD, c->hidden, 2);
       if (!rc) rc = map(&a.tm[l][DD_WK], W.wk, KD, c->hidden, 2);
       if (!rc) rc = map(&a.tm[l][DD_WV], W.wv, KD, c->hidden, 2);
-      if (!rc) rc = map(&a.tm[l][DD_WO], W.wo, c->hidden, QD, 0);
+      if (!rc) rc = map(&a.tm[l][DD_WO], W.wo, c->hidden, QD, a.s3_o ? 2 : 0);
       if (!rc) rc = map(&a.tm[l][DD_WG], W.wg, c->ffn, c->hidden, 1);
       if (!rc) rc = map(&a.tm[l][DD_WU], W.wu, c->ffn, c->hidden, 1);
-      if (!rc) rc = map(&a.tm[l][DD_WD], W.wd, c->hidden, c->ffn, 0);
+      if (!rc) rc = map(&a.tm[l][DD_WD], W.wd, c->hidden, c->ffn, a.s3_down ? 2 : 0);
     }
     if (rc) return rc;
   }
@@ -1850,8 +2100,18 @@ extern "C" int flashb_dd_frame(const fb_dd_config* c, const void* layers_dev, vo
   };
   // x_mid kept from S3 to S4 (its rows also stage ob in S3).  tcgen05 build with room for ob beside the 16 staged
   // rows: only the CTA's S4 columns (its blocks of 64 output units), ob staged in the free half of the rows region
-  const int s4_blocks = (c->hidden + 63) / 64;
-  const int keep_cols = (s4_blocks + grid - 1) / grid * 64;
+  int keep_cols = 0;
+  if (a.s3_down) {
+    // the blocks of 128 columns a CTA's split items touch
+    const int S = a.s3_down, items = c->hidden / 128 * S;
+    for (int g = 0; g < grid; ++g) {
+      const int i0 = (int)((long long)items * g / grid), i1 = (int)((long long)items * (g + 1) / grid);
+      if (i1 > i0 && ((i1 - 1) / S + 1 - i0 / S) * 128 > keep_cols) keep_cols = ((i1 - 1) / S + 1 - i0 / S) * 128;
+    }
+  } else {
+    const int s4_blocks = (c->hidden + 63) / 64;
+    keep_cols = (s4_blocks + grid - 1) / grid * 64;
+  }
   a.keep_cols = (tc && (size_t)2 * 16 * c->hidden * 2 <= (size_t)16 * 2 * KXf && keep_cols < c->hidden) ? keep_cols : 0;
   const size_t keep_rows = a.keep_cols ? (size_t)a.keep_cols : (size_t)c->hidden;
   auto layout = [&](int d_chunk, size_t& keep_off, size_t& base) {
