@@ -411,3 +411,28 @@ def test_depth_ln12_streaming_refuses_unsupported_shapes():
     with pytest.raises(FlashbError):
         m.use_ln12(True)
         _run(m)
+
+
+@pytest.mark.parametrize('mask,grid', [('0000', 18), ('1111', 18), ('1111', 32), ('0011', 8)])
+def test_depth_task_forms(mask, grid, monkeypatch):
+    """The plain GEMV tasks in their 64-row form and in the 128-row form, split over two CTAs in K where the grid
+    allows (FLASHB_DD_TASK128: projector, o, down, heads): the same frame against the oracle, and the sampler
+    bit-exact on the kernel's logits.  Grid 32 splits the heads too; grid 8 keeps every part whole."""
+    monkeypatch.setenv('FLASHB_DD_TASK128', mask)
+    m = _model(small=False, B=16, seed=13)
+    m.desc.cfg.grid = grid
+    c = m.cfg
+    forced = np.random.default_rng(13).integers(0, c.vocab, (c.n_decode, 16))
+    outtok, logits, _ = _run(m, forced)
+    W = _weights(m)
+    temp, topk, topp, ds, gs = _params(m)
+    _, lg_ref, _ = odepth.depth_frame(W, np32(m.backbone_hidden_buf), m.first_cb_token_buf.cpu().numpy(),
+                                      m.q.cpu().numpy(), temp, topk, topp, ds, gs, forced=forced)
+    for s in range(c.n_decode):
+        assert_close(logits[s], lg_ref[s], what=f'step {s} logits (task forms {mask}, grid {grid})')
+    _check_sampler(m, logits, outtok)
+    # a second frame on the same scratch: the split parts' tags start again from zero
+    outtok2, logits2, _ = _run(m, forced)
+    np.testing.assert_array_equal(logits2, logits)
+    from flashb._native import device_error
+    assert device_error() == 0
