@@ -586,15 +586,37 @@ __device__ __noinline__ void dd_load_mid(unsigned char* xs, int x_pitch, const D
   const int tid = threadIdx.x;
   const int H = a.H, kv = H >> 3, kc = a.keep_cols;
   bf16* const ost = kc ? reinterpret_cast<bf16*>(xs + (size_t)16 * H * 2) : keep;   // ob staging, [M][H]
-  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
-    const int m = i / kv, j = i - m * kv;
+  // (row m, unit j) items: one unit column per thread when the threads cover whole rows (no divisions per item)
+  const bool cols = kv <= PK_CONSUMERS && PK_CONSUMERS % kv == 0;
+  const int dm = cols ? PK_CONSUMERS / kv : 0, jc = cols ? tid % kv : 0, mc = cols ? tid / kv : 0;
+  const int nit = cols ? (M - mc + dm - 1) / dm : (M * kv - tid + PK_CONSUMERS - 1) / PK_CONSUMERS;
+#pragma unroll 4
+  for (int k = 0; k < nit; ++k) {
+    int m, j;
+    if (cols) {
+      m = mc + k * dm;
+      j = jc;
+    } else {
+      const int i = tid + k * PK_CONSUMERS;
+      m = i / kv;
+      j = i - m * kv;
+    }
     cp_async16(xs + xs_off(m, j, x_pitch), a.xres + (size_t)m * H + (size_t)j * 8);
     cp_async16(ost + (size_t)m * H + (size_t)j * 8, a.ob + (size_t)m * H + (size_t)j * 8);
   }
   cp_async_commit();
   cp_async_wait<0>();
-  for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
-    const int m = i / kv, j = i - m * kv;
+#pragma unroll 4
+  for (int k = 0; k < nit; ++k) {
+    int m, j;
+    if (cols) {
+      m = mc + k * dm;
+      j = jc;
+    } else {
+      const int i = tid + k * PK_CONSUMERS;
+      m = i / kv;
+      j = i - m * kv;
+    }
     uint4* px = reinterpret_cast<uint4*>(xs + xs_off(m, j, x_pitch));
     uint4* pk = reinterpret_cast<uint4*>(ost + (size_t)m * H + (size_t)j * 8);
     float x[8], o[8];
@@ -1438,6 +1460,7 @@ __device__ __noinline__ DDCur dd_phase_e(const DDArgs& a, DDCur c, int s, int su
   DD_STAMP(s, 0);
   const int kv = AE >> 3;
   const long long rows = (long long)(a.NCB + 1) * V;
+#pragma unroll 4
   for (int i = tid; i < M * kv; i += PK_CONSUMERS) {
     const int b = i / kv, j = i - b * kv;
     const bf16* src;

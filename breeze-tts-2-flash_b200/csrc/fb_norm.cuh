@@ -56,6 +56,7 @@ __device__ __forceinline__ void rms_row_factors(const unsigned char* xs, Off off
   const int lane = threadIdx.x & 31, nu = K >> 3;
   for (int m = warp; m < M; m += nwarps) {
     float acc = 0.f;
+#pragma unroll 4
     for (int u = lane; u < nu; u += 32) acc = sumsq8(*reinterpret_cast<const uint4*>(xs + off(m, u)), acc);
     acc = warp_sum(acc);
     if (lane == 0) rs[m] = rms_factor(acc, K, eps);
@@ -68,6 +69,17 @@ template <typename Off>
 __device__ __forceinline__ void rms_rows_apply(unsigned char* xs, Off off, int M, int K, const bf16* nw,
                                                const float* rs, int t, int nthreads) {
   const int nu = K >> 3;
+  if (nu <= nthreads && nthreads % nu == 0) {
+    // each thread keeps one unit column: its weight unit is read once, the rows follow without divisions
+    const int u = t % nu, dm = nthreads / nu;
+    const uint4 w = *reinterpret_cast<const uint4*>(nw + (size_t)u * 8);
+#pragma unroll 4
+    for (int m = t / nu; m < M; m += dm) {
+      uint4* p = reinterpret_cast<uint4*>(xs + off(m, u));
+      *p = rms_unit(*p, w, rs[m]);
+    }
+    return;
+  }
   for (int i = t; i < M * nu; i += nthreads) {
     const int m = i / nu, u = i - m * nu;
     uint4* p = reinterpret_cast<uint4*>(xs + off(m, u));

@@ -337,9 +337,16 @@ __device__ __forceinline__ void apply_rms(unsigned char* xs, int x_pitch, int M,
 __device__ __noinline__ void load_x(unsigned char* xs, int x_pitch, const bf16* x, long ld, int M, int K,
                                     const bf16* nw, float eps, float* nred) {
   const int kv = K >> 3;
-  for (int i = threadIdx.x; i < M * kv; i += PK_CONSUMERS) {
-    const int m = i / kv, j = i - m * kv;
-    cp_async16(xs + xs_off(m, j, x_pitch), x + (size_t)m * ld + (size_t)j * 8);
+  if (kv <= PK_CONSUMERS && PK_CONSUMERS % kv == 0) {
+    // one unit column per thread, the rows without divisions
+    const int j = threadIdx.x % kv, dm = PK_CONSUMERS / kv;
+#pragma unroll 4
+    for (int m = threadIdx.x / kv; m < M; m += dm) cp_async16(xs + xs_off(m, j, x_pitch), x + (size_t)m * ld + (size_t)j * 8);
+  } else {
+    for (int i = threadIdx.x; i < M * kv; i += PK_CONSUMERS) {
+      const int m = i / kv, j = i - m * kv;
+      cp_async16(xs + xs_off(m, j, x_pitch), x + (size_t)m * ld + (size_t)j * 8);
+    }
   }
   cp_async_commit();
   cp_async_wait<0>();
