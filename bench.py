@@ -38,9 +38,9 @@ PROMPT = 512
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0)
 # dram__bytes_read.sum + dram__bytes_write.sum of one dd_frame_kernel launch at the bench's default shape (8 streams
 # per launch, B = 16 rows, one lane's grid of 18 CTAs: the tcgen05 build), from ncu --set full captures of the
-# full-size depth model, keyed by (step table, LN12 weights): with the table 2,066,498,000 B read + 7,627,264 B
+# full-size depth model, keyed by (step table, LN12 weights): with the table 2,041,333,000 B read + 8,110,592 B
 # written (bf16) and 1,042,911,000 + 8,060,672 (LN12); without it 2,174,940,416 + 7,735,296 (bf16).
-DD_TRAFFIC_BYTES = {(1, 0): 2074125264, (1, 1): 1050971672, (0, 0): 2182675712}
+DD_TRAFFIC_BYTES = {(1, 0): 2049443592, (1, 1): 1050971672, (0, 0): 2182675712}
 PREFILL_CFG = dict(B=2, NH=16, NKV=4, L=512, D=128, pads=(0, 37))
 
 
