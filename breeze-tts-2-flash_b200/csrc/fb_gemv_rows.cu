@@ -64,7 +64,7 @@ struct alignas(64) RowsArgs {
   long ldr;
   int nst;             // ring stages
   int split;           // CTAs per cluster (1: no split)
-  int pitch;           // floats per row of a receive slot
+  int pitch;           // columns of a receive slot per sender (column-major over the 128 rows)
   int area;            // bytes of the ring / receive area (the mbarriers follow it)
   unsigned* err;
   unsigned long long* trace;   // optional per-CTA timeline (flashb_set_gemv_trace), or null
@@ -84,9 +84,8 @@ __device__ __forceinline__ uint32_t cl_map(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ void cl_st4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
+__device__ __forceinline__ void cl_st1(uint32_t addr, float a) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(a) : "memory");
 }
 __device__ __forceinline__ void tma_load_3d_hint(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar,
                                                  uint64_t policy) {
@@ -157,7 +156,7 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
   uint64_t* empty = full + GR_MAX_STAGES;
   uint64_t* dfull = empty + GR_MAX_STAGES;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(dfull + 1);
-  float* recv = reinterpret_cast<float*>(smem);     // split K: [S senders][128 rows][pitch], over the idle ring
+  float* recv = reinterpret_cast<float*>(smem);     // split K: [S senders][pitch columns][128 rows], over the idle ring
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) GR_STAMP(0, globaltimer());
@@ -274,7 +273,8 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
     if (tid == 64) GR_STAMP(8, globaltimer());
     if (epi) {
       // the groups other ranks own, rank + 1's first (so that the senders of a cluster spread over the receivers)
-      const uint32_t mine = smem_u32(recv) + (uint32_t)((rank * 128 + row) * a.pitch) * 4u;
+      // column-major slots: for each column the 32 lanes of a warp (consecutive rows) write 128 contiguous bytes
+      const uint32_t mine = smem_u32(recv) + (uint32_t)(rank * a.pitch * 128 + row) * 4u;
       int item = 0;
       for (int j = 1; j < S; ++j) {
         const int o = (rank + j) % S, f0 = gr_first(o, S), f1 = gr_first(o + 1, S);
@@ -287,12 +287,12 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
           } else {
             tc_ld16(tq + (uint32_t)(g * 16), v);
           }
-          const uint32_t dst = base + (uint32_t)((g - f0) * 16 * MATS) * 4u;
+          const uint32_t dst = base + (uint32_t)((g - f0) * 16 * MATS * 128) * 4u;
 #pragma unroll
-          for (int i = 0; i < 16; i += 4) cl_st4(dst + (uint32_t)i * 4u, v[i], v[i + 1], v[i + 2], v[i + 3]);
+          for (int i = 0; i < 16; ++i) cl_st1(dst + (uint32_t)(i * 128) * 4u, v[i]);
           if (EPI == 2) {
 #pragma unroll
-            for (int i = 0; i < 16; i += 4) cl_st4(dst + (uint32_t)(16 + i) * 4u, w[i], w[i + 1], w[i + 2], w[i + 3]);
+            for (int i = 0; i < 16; ++i) cl_st1(dst + (uint32_t)((16 + i) * 128) * 4u, w[i]);
           }
         }
       }
@@ -324,15 +324,11 @@ __global__ void __launch_bounds__(GR_THREADS, 1) gemv_rows_kernel(const __grid_c
       }
       for (int p = 0; p < S; ++p) {
         if (p == rank) continue;
-        const float* src = recv + (size_t)(p * 128 + row) * a.pitch + (g - g0) * 16 * MATS;
+        const float* src = recv + ((size_t)p * a.pitch + (g - g0) * 16 * MATS) * 128 + row;
 #pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-          const float4 t4 = *reinterpret_cast<const float4*>(src + i);
-          v[i] += t4.x; v[i + 1] += t4.y; v[i + 2] += t4.z; v[i + 3] += t4.w;
-          if (EPI == 2) {
-            const float4 w4 = *reinterpret_cast<const float4*>(src + 16 + i);
-            u[i] += w4.x; u[i + 1] += w4.y; u[i + 2] += w4.z; u[i + 3] += w4.w;
-          }
+        for (int i = 0; i < 16; ++i) {
+          v[i] += src[i * 128];
+          if (EPI == 2) u[i] += src[(16 + i) * 128];
         }
       }
       if (live) gr_store<EPI>(a, m, n0, v, u, rr0, rr1);
@@ -371,8 +367,7 @@ size_t rows_smem(int nst, int S, int pitch) {
 
 template <int EPI>
 int rows_pitch(int S) {
-  const int own = (GR_GROUPS + S - 1) / S * 16 * gr_mats(EPI);
-  return own + 4;          // 16-byte rows, 4 banks apart
+  return (GR_GROUPS + S - 1) / S * 16 * gr_mats(EPI);      // columns a rank owns (its receive slot per sender)
 }
 
 template <int EPI>
