@@ -2,7 +2,7 @@
 //
 // Semantics (eager attention, transformers Qwen3 / UP/models/breeze.py:259-286, for q_len == 1):
 //   s = bf16(q . k) ; s = bf16(s * scaling) ; s = s + mask (bf16 add for a bf16 mask, fp32 for an fp32 mask)
-//   p = softmax_fp32(s) ; out = bf16(p . v)
+//   p = softmax_fp32(s) ; out = bf16(p . v)      (exponentials by the fast intrinsic: a few fp32 ulps)
 // Keys whose additive mask is <= -1e30 are skipped; a row without any valid key gives 0.  Rounding points differ
 // from eager in one place: the probabilities stay fp32 (eager rounds p to bf16 before p . v) because each split
 // only knows its own running max; the effect is below bf16 resolution of the output.
@@ -273,13 +273,13 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
       const float mold = st_m[g];
       const float mnew = fmaxf(mold, cm);
       const bool any = mnew > -INFINITY;
-      const float e0 = (any && s0 > -INFINITY) ? expf(s0 - mnew) : 0.f;
-      const float e1 = (any && s1 > -INFINITY) ? expf(s1 - mnew) : 0.f;
+      const float e0 = (any && s0 > -INFINITY) ? __expf(s0 - mnew) : 0.f;
+      const float e1 = (any && s1 > -INFINITY) ? __expf(s1 - mnew) : 0.f;
       s_s[g][lane] = e0;
       s_s[g][lane + 32] = e1;
       const float es = warp_sum(e0 + e1);
       if (lane == 0) {
-        const float scale = (mold > -INFINITY) ? expf(mold - mnew) : 0.f;
+        const float scale = (mold > -INFINITY) ? __expf(mold - mnew) : 0.f;
         st_scale[g] = scale;
         st_l[g] = st_l[g] * scale + es;
         st_m[g] = mnew;
@@ -353,7 +353,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
 #pragma unroll
         for (int sp = 0; sp < AT_MAXCLUSTER; ++sp) {
           if (sp < nsplit && mv[sp] > -INFINITY) {
-            const float f = expf(mv[sp] - M);
+            const float f = __expf(mv[sp] - M);
             L = fmaf(lv[sp], f, L);
             O = fmaf(ov[sp], f, O);
           }

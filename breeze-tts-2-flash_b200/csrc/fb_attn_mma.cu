@@ -3,9 +3,10 @@
 // the grid (one CTA per (row, KV head), no key split).
 //
 // Same semantics as fb_attn.cu, with one more rounding point: s = bf16(q . k), s = bf16(s * scaling), s = s + mask
-// (bf16 add for a bf16 mask), p = exp(s - running max) in fp32, o = sum bf16(p) v / sum p.  The reference rounds
-// the normalised probabilities to bf16 before p . v; here the unnormalised ones are rounded (both below the output's
-// bf16 resolution).
+// (bf16 add for a bf16 mask), p = exp(s - running max) in fp32 (the fast exponential intrinsic: a few fp32 ulps,
+// below the bf16 rounding of p; the exact expf serialises on its special-case branches), o = sum bf16(p) v / sum p.
+// The reference rounds the normalised probabilities to bf16 before p . v; here the unnormalised ones are rounded
+// (both below the output's bf16 resolution).
 //
 // B200 design.  With 128 rows x 4 KV heads the scalar kernel is instruction-bound (each key costs ~130 instructions
 // per head group: half-warp dot products, shuffles, one thread per head dimension for p . v).  Here each 64-key
@@ -290,12 +291,12 @@ __global__ void __launch_bounds__(AM_THREADS) attn_mma_kernel(const __grid_const
     for (int j = 0; j < 2; ++j) {
       const float c4 = fmaxf(fmaxf(red_m[0][h0 + j], red_m[1][h0 + j]), fmaxf(red_m[2][h0 + j], red_m[3][h0 + j]));
       mnew[j] = fmaxf(m_run[j], c4);
-      scale[j] = (m_run[j] > -INFINITY) ? expf(m_run[j] - mnew[j]) : 0.f;
+      scale[j] = (m_run[j] > -INFINITY) ? __expf(m_run[j] - mnew[j]) : 0.f;
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int j = i & 1, key = k0 + (i >> 1) * 8;
-      const float p = (sc[i] > -INFINITY) ? expf(sc[i] - mnew[j]) : 0.f;
+      const float p = (sc[i] > -INFINITY) ? __expf(sc[i] - mnew[j]) : 0.f;
       ls[j] += p;
       ps[h0 + j][key] = __float2bfloat16_rn(p);
     }

@@ -450,7 +450,7 @@ __device__ __noinline__ void dd_attention(const DDArgs& a, int l, int pos, unsig
       const int lane = tid & 31;
       const float v = lane < np ? pr[lane] : -INFINITY;
       const float mx = warp_max(v);
-      const float e = lane < np ? expf(v - mx) : 0.f;
+      const float e = lane < np ? __expf(v - mx) : 0.f;
       const float den = warp_sum(e);
       if (lane < np) pr[lane] = rbf(e / den);
     }
@@ -548,7 +548,7 @@ __device__ __noinline__ void dd_attention_pairs(const DDArgs& a, int l, int pos,
     const int lane = tid & 31;
     const float v = lane < np ? pr[lane] : -INFINITY;
     const float mx = warp_max(v);
-    const float e = lane < np ? expf(v - mx) : 0.f;
+    const float e = lane < np ? __expf(v - mx) : 0.f;
     const float den = warp_sum(e);
     if (lane < np) pr[lane] = rbf(e / den);
   }
