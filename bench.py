@@ -741,18 +741,19 @@ def main():
         toks_h = torch.zeros(2, S, 2 * G + 2 * G * dcfg.n_decode + G, dtype=torch.long).pin_memory()
         h2d = S * qh[0].numel() * 4
         d2h = S * toks_h[0, 0].numel() * 8
-        got = [None] * S            # per slot: the event after its previous frame's token copies
+        got = [[None] * S, [None] * S]   # per token buffer and slot: the event after that frame's token copies
 
         def e2e_step(t):
-            # every slot: before its frame the host has that slot's previous tokens (its event), then its Exp(1)
-            # draws go in from pinned host memory; after the frame its tokens come out into the other half of a
-            # double-buffered pinned array.  Slots are waited for one by one, so the host issues the next frames
-            # while the GPU still runs this step; the lanes still join on the device at the end of every step.
+            # every slot: its Exp(1) draws go in from pinned host memory before its frame; after the frame its
+            # tokens and validity flags come out into half t % 2 of a double-buffered pinned array.  Before step t
+            # reuses a half, the host waits for the tokens step t - 2 copied there (and so holds them), which keeps
+            # one step of work queued on the GPU while the host reads the previous one; the lanes still join on
+            # the device at the end of every step, so a frame's draws are not replaced while it runs.
             def h2d_q(kind, i, s):
                 if kind == 'bb':    # i = -1: the shared backbone of every slot
                     for j in (range(S) if i < 0 else (i,)):
-                        if got[j] is not None:
-                            got[j].synchronize()
+                        if got[t & 1][j] is not None:
+                            got[t & 1][j].synchronize()
                         eng.streams[j].q.copy_(qh[(j + t) % R], non_blocking=True)
 
             def d2h_tokens(kind, i, s):
@@ -762,7 +763,7 @@ def main():
                 toks_h[t & 1, i, -G:].copy_(eng.cb0_ok[st.c0:st.c0 + G], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(s)
-                got[i] = ev
+                got[t & 1][i] = ev
 
             eng.step(h2d_q, d2h_tokens)
 
@@ -770,7 +771,7 @@ def main():
         for t in range(a.warmup):
             e2e_step(t)
         torch.cuda.synchronize(dev)
-        got = [None] * S
+        got = [[None] * S, [None] * S]
         barrier()
         w0 = torch.cuda.Event(enable_timing=True)
         w1 = torch.cuda.Event(enable_timing=True)
@@ -778,9 +779,9 @@ def main():
         for t in range(a.steps):
             e2e_step(t)
         w1.record(stream)
-        for e in got:
+        for e in got[0] + got[1]:
             if e is not None:
-                e.synchronize()     # the last step's tokens are on the host
+                e.synchronize()     # the last two steps' tokens are on the host
         barrier()
         e_ms = maxred(w0.elapsed_time(w1))
         eng.draw_q = True
