@@ -129,7 +129,9 @@ class DepthOps:
         self.desc = {}     # batch -> DepthModelDesc
         self.args = None
         self.ln12_enc = None
-        self.ln12_stream = True   # after dd2_init_ln12: frames stream the 12-bit bytes where the build can
+        # after dd2_init_ln12: frames stream the 12-bit bytes where the build can (off: the lanes of a many-stream
+        # GPU measured faster on the decoded bf16 matrices, 7.00 against 9.38 ms per frame)
+        self.ln12_stream = False
 
     def dd2_init(self, w, bufs=None, eps=1e-5, scaling=128 ** -0.5, grid=0, codebook_size=None):
         """w: per layer [ln1, wq, wk, wv, wo, ln2, wg, wu, wd] x NL + [embed, proj, normf, head_t, cos, sin] (bf16).
@@ -160,10 +162,10 @@ class DepthOps:
     def dd2_init_ln12(self, data, meta, ovf, luts):
         """The reference's ``dd2_init_ln12`` (``flash/csrc/depth_frame.cu:800-823``): the depth matrices in the
         lossless LN12 format (per matrix: data uint8, meta int32 [N, 4], ovf int32; luts int64 [count, 2] = the
-        table words).  The tcgen05 frame build (grids <= 32, the lanes of a many-stream GPU) streams these bytes and
-        decodes them in shared memory before its MMAs (``ln12_stream``, on by default); the other builds and the step
-        table read bf16 matrices that flashb decodes once here on the device (``flashb_ln12_decode``, bit-exact),
-        replacing those of ``dd2_init``.  Either way the weights are the same values."""
+        table words).  flashb decodes them once here on the device (``flashb_ln12_decode``, bit-exact) into the bf16
+        matrices its frames read, replacing those of ``dd2_init``; with ``ln12_stream`` set before the first frame the
+        tcgen05 build (grids <= 32) instead streams these bytes and decodes them in shared memory before its MMAs
+        (25% fewer weight bytes, slower on the latency-bound lanes).  Either way the weights are the same values."""
         from . import ln12
         if self.args is None:
             raise RuntimeError('dd2_init first')

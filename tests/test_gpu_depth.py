@@ -436,3 +436,42 @@ def test_depth_task_forms(mask, grid, monkeypatch):
     np.testing.assert_array_equal(logits2, logits)
     from flashb._native import device_error
     assert device_error() == 0
+
+
+def test_dd2_init_ln12_streaming_surface():
+    """The reference surface with LN12 streaming switched on (DepthOps.ln12_stream before the first frame, a lane-
+    sized grid): the frame streams the 12-bit bytes and its teacher-forced logits match the frame on the decoded
+    bf16 matrices."""
+    from flashb import depth as fdep
+    from flashb import ln12
+    m = _model(small=False, B=2, seed=14, layers=1, ffn=1024, embed_dim=1024, vocab=128, codebook_size=120,
+               n_decode=4)
+    w = []
+    for layer in m.layers:
+        w += [layer[k] for k in ('ln1', 'wq', 'wk', 'wv', 'wo', 'ln2', 'wg', 'wu', 'wd')]
+    w += [m.embed, m.proj, m.normf, m.head_t, m.cos_tab, m.sin_tab]
+    forced = torch.as_tensor(np.random.default_rng(14).integers(0, m.cfg.vocab, (m.cfg.n_decode, 2)),
+                             dtype=torch.long, device='cuda').contiguous()
+    args = (m.first_cb_token_buf, m.backbone_hidden_buf, m.tok_buf, m.output_tokens, m.temperature, m.top_k,
+            m.top_p, m.do_sample, m.guidance_scale, m.q)
+    out = []
+    for stream in (False, True):
+        ops = fdep.DepthOps()
+        ops.dd2_init(w, eps=m.cfg.eps, codebook_size=m.cfg.codebook_size)
+        enc = [ln12.to_device(*ln12.encode(x), 'cuda') for x in ops.ln12_mats()]
+        luts = torch.tensor([list(x[3]) for x in enc], dtype=torch.int64)
+        ops.dd2_init_ln12([x[0] for x in enc], [x[1] for x in enc], [x[2] for x in enc], luts)
+        ops.ln12_stream = stream
+        saved = dict(fdep.GRIDS)
+        try:
+            fdep.GRIDS[2] = 8
+            dbg = torch.zeros(m.cfg.n_decode, 2, m.cfg.vocab, dtype=torch.float32, device='cuda')
+            ops.dd2_frame(*args, dbg=dbg, forced=forced)
+            torch.cuda.synchronize()
+        finally:
+            fdep.GRIDS.clear()
+            fdep.GRIDS.update(saved)
+        assert (ops.desc[2].cfg.ln12 is not None) == stream
+        out.append(dbg.cpu().numpy())
+    for s in range(m.cfg.n_decode):
+        assert_close(out[1][s], out[0][s], what=f'step {s} logits (LN12 streamed vs decoded)')
