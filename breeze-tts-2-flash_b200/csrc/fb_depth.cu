@@ -21,12 +21,15 @@
 //              softmax, argmax(p / q), with its own exp routine and fixed summation order, bit-identical to the C
 //              oracle (oracle/sampler.c); CTA 0 writes the tokens out, every CTA feeds its copy to the next step
 //
-// The depth matrices are 1024 columns wide, so this unit streams 16 x 1024 stages (32 KB): a ring of five fits
-// beside the activations and the producer runs a whole task ahead.  Global -> shared staging of activations
-// (cross-CTA data) uses cp.async.cg with every chunk in flight at once: one L2 round trip per phase.  The large
-// phases are not inlined so that a step's code stays resident in the instruction cache.
+// Stages are 32 KB (16 x 1024 columns in the mma.sync build; 64 or 128 weight rows x 256 or 128 columns in the
+// tcgen05 build of lane-sized grids, whose GEMVs run on tcgen05.mma with the 16 activation rows as N); the ring
+// holds as many as fit beside the activations (three or four at the full-size model) and the producer runs ahead
+// across tasks.  Global -> shared staging of activations (cross-CTA data) uses cp.async.cg with every chunk in
+// flight at once: one L2 round trip per phase.  The large phases are not inlined so that a step's code stays
+// resident in the instruction cache.
 //
-// Scratch (residual stream, q, o, act, logits, KV cache, barrier) is one caller-owned buffer, zeroed once.
+// Scratch (residual stream, q, o, act, logits, KV cache, barrier, split-task partials and tags) is one caller-owned
+// buffer, zeroed once.
 #define FB_ST_KC 1024
 #define FB_ST_TMA 1
 #define FB_PK_MAX_STAGES 8
