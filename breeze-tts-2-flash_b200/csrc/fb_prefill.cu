@@ -19,8 +19,12 @@
 //   * Pass 1: S = Q K^T per key tile into TMEM columns [0, 128); every thread reads its 32 scores (tcgen05.ld
 //     32x32b), applies the eager rounding points and the mask, and keeps a running max and fp32 sum of
 //     exp(s - max) (rescaled when the max grows); the four quarters of a row are merged after the pass.
-//   * Pass 2: S again per tile; p = bf16(exp(s - max) / sum) exactly as the eager softmax forms it, written to
-//     shared memory as the K-major A operand; O += P V on tcgen05 into TMEM columns [128, 256).
+//   * Pass 1 also keeps the rounded, masked scores of the first PF_KEEP key tiles in TMEM columns [256, 512) as bf16
+//     pairs (they are bf16 values; not with an fp32 mask).
+//   * Pass 2: per tile, the kept scores read back from TMEM, or S again; p = bf16(exp(s - max) / sum) exactly as
+//     the eager softmax forms it, written to shared memory as the K-major A operand; O += P V on tcgen05 into TMEM
+//     columns [128, 256).  Keeping the scores saves pass 2 the K copy, the S MMAs and the fp32 score rounding of
+//     those tiles (all of them at prompts up to 512 tokens).
 //   * Epilogue: O row -> bf16 -> out.  Rows whose every key is masked (left padding) are written as 0 (their
 //     outputs never reach a live row; the oracle uses the same convention).
 // With `causal` the key tiles entirely above the diagonal are skipped: the mask gives them probability exactly 0.
@@ -37,7 +41,8 @@ constexpr int PF_OPND = PF_TILE * PF_D * 2;        // 32 KB per operand tile
 constexpr int PF_MPITCH = PF_TILE * 2 + 16;       // bytes per staged bf16 mask row (padded: fewer bank conflicts)
 constexpr int PF_MASK = PF_TILE * PF_MPITCH;       // the bf16 mask tile of the current key tile
 constexpr int PF_SMEM = 4 * PF_OPND + 2 * PF_MASK + 64;  // Q, K, V, P, two mask tiles, two mbarriers, TMEM slot
-constexpr uint32_t PF_TMEM_COLS = 256;             // S: columns [0, 128); O: columns [128, 256)
+constexpr uint32_t PF_TMEM_COLS = 512;             // S: columns [0, 128); O: [128, 256); kept scores: [256, 512)
+constexpr int PF_KEEP = 4;                         // key tiles whose pass-1 scores stay in TMEM (bf16 pairs, 64 columns each)
 
 struct PFArgs {
   const bf16 *q, *k, *v;
@@ -103,6 +108,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&f)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(r[i]);
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane: store (then wait for the store), load (then wait).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // Byte offset of 16-byte chunk c (elements 8c .. 8c+7 along K) of row r in a K-major no-swizzle tile of 128 x 128.
@@ -187,8 +212,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t t_s = tmem, t_o = tmem + 128;
-  const uint32_t my_taddr = ((uint32_t)((warp & 3) * 32) << 16) + cq * 32;
+  const uint32_t t_s = tmem, t_o = tmem + 128, t_keep = tmem + 256;
+  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;   // this warp's TMEM lane quarter
+  const uint32_t my_taddr = lane_base + cq * 32;
 
   // Q tile -> K-major A operand (rows beyond L are zero)
   {
@@ -214,6 +240,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   float mx = -INFINITY, sum = 0.f;
   bool fail = false;
   const bool mask_smem = a.mask && a.mask_bf16;
+  // pass-1 scores kept in TMEM for pass 2 (tiles [0, nkeep)): they are bf16 values unless an fp32 mask is added
+  const int nkeep = (!a.mask || a.mask_bf16) ? min(ntile, PF_KEEP) : 0;
 
   // Staging of key tile t: K (K-major B operand of S = Q K^T) with the tile's bf16 mask rows, and V (MN-major B
   // operand of O += P V).  Each is one cp.async group (the caller commits); zero rows past S are plain stores.
@@ -297,6 +325,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     }
     float sc[32];
     scores32(t, sc);
+    if (t < nkeep) {
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = pack2(sc[2 * i], sc[2 * i + 1]);
+      tmem_st16(t_keep + lane_base + (uint32_t)(t * 64 + cq * 16), pk);
+    }
     float tm = -INFINITY;
 #pragma unroll
     for (int i = 0; i < 32; ++i) tm = fmaxf(tm, sc[i]);
@@ -336,27 +370,44 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   const float inv = 1.0f / sum;
 
   // ---------------------------------------------------------------- pass 2: P = softmax, O += P V
-  // Per tile t: wait for S(t); copy K(t + 1) and its mask (K is free once S(t) is done); P(t) from S(t); once V(t)
-  // has landed, O += P(t) V(t); when that MMA is done, copy V(t + 1) and issue S(t + 1) as soon as K(t + 1) is in.
+  // Tiles [0, nkeep) read their scores back from TMEM; later tiles recompute S = Q K^T.  Per tile t: the scores
+  // (for a recomputed tile: wait for S(t), then copy K(t + 1) and its mask, K being free once S(t) is done); P(t);
+  // once V(t) has landed, O += P(t) V(t); when that MMA is done, copy V(t + 1) (and K(t + 1) for the first
+  // recomputed tile) and issue S(t + 1) as soon as K(t + 1) is in.
   if (!fail && ntile > 0) {
-    stage_k(0);
-    cp_commit_pf();
-    stage_v(0);
-    cp_commit_pf();
-    cp_wait_pf<1>();                   // K(0) and its mask; V(0) may still be in flight
-    issue_s();
-  }
-  for (int t = 0; t < ntile && !fail; ++t) {
-    if (!wait_s()) {
-      fail = true;
-      break;
-    }
-    if (t + 1 < ntile) {
-      stage_k(t + 1);
+    if (nkeep == 0) {
+      stage_k(0);
       cp_commit_pf();
     }
+    stage_v(0);
+    cp_commit_pf();
+    if (nkeep == 0) {
+      cp_wait_pf<1>();                 // K(0) and its mask; V(0) may still be in flight
+      issue_s();
+    }
+  }
+  for (int t = 0; t < ntile && !fail; ++t) {
+    const bool kept = t < nkeep;
     float sc[32];
-    scores32(t, sc);
+    if (kept) {
+      uint32_t pk[16];
+      tmem_ld16(t_keep + lane_base + (uint32_t)(t * 64 + cq * 16), pk);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        sc[2 * i] = lo_f(pk[i]);
+        sc[2 * i + 1] = hi_f(pk[i]);
+      }
+    } else {
+      if (!wait_s()) {
+        fail = true;
+        break;
+      }
+      if (t + 1 < ntile) {
+        stage_k(t + 1);
+        cp_commit_pf();
+      }
+      scores32(t, sc);
+    }
     // p = bf16(e^(s - max) / sum) with the fast exponential and one reciprocal per row: a few fp32 ulps, below the
     // bf16 rounding of p except at rare ties (the exact expf and IEEE division per score serialise on their
     // special-case branches and cost several microseconds per tile)
@@ -372,8 +423,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       w.w = pack2(p[c * 8 + 6], p[c * 8 + 7]);
       *reinterpret_cast<uint4*>(sp + kmaj_off(r, cq * 4 + c)) = w;
     }
-    // V(t) was committed before K(t + 1): leave at most that newest group in flight
-    if (t + 1 < ntile) cp_wait_pf<1>();
+    // V(t) is the oldest group in flight; K(t + 1) was committed after it only for a recomputed tile t
+    if (!kept && t + 1 < ntile) cp_wait_pf<1>();
     else cp_wait_pf<0>();
     fence_async_smem();
     tc_fence_before();
@@ -392,10 +443,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
         fail = true;
         break;
       }
+      const bool next_s = t + 1 >= nkeep;
+      if (next_s && kept) {            // the first recomputed tile: its K has not been copied yet
+        stage_k(t + 1);
+        cp_commit_pf();
+      }
       stage_v(t + 1);
       cp_commit_pf();
-      cp_wait_pf<1>();                 // K(t + 1) and its mask; V(t + 1) may still be in flight
-      issue_s();
+      if (next_s) {
+        cp_wait_pf<1>();               // K(t + 1) and its mask; V(t + 1) may still be in flight
+        issue_s();
+      }
     }
   }
   if (!fail && ntile > 0) {
