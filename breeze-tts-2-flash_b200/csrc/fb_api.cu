@@ -157,6 +157,55 @@ int tmap_ln12(CUtensorMap* out, const void* data, long long N, int K, int box_ro
   return FB_OK;
 }
 
+int tmap_heads(CUtensorMap* out, const void* base, int B, int NH, long long S, long long sl, long long sh,
+               long long sb) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  static std::map<std::tuple<uintptr_t, int, int, long long, long long, long long, long long>, CUtensorMap> cache;
+  static std::mutex mu;
+  if (!base || B < 1 || NH < 1 || S < 1 || S > (1ll << 31) || sl < 128 || (sl & 7) || (NH > 1 && (sh < 1 || (sh & 7))) ||
+      (B > 1 && (sb < 1 || (sb & 7))) || (reinterpret_cast<uintptr_t>(base) & 15)) {
+    set_msg("tensor map: bad head-major cache (B %d, heads %d, S %lld, strides %lld %lld %lld, base %p)", B, NH, S, sl,
+            sh, sb, base);
+    return FB_ERR_ARG;
+  }
+  // a dimension of extent 1 takes any valid stride
+  if (NH == 1) sh = sl * S;
+  if (B == 1) sb = sh * NH;
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(reinterpret_cast<uintptr_t>(base), B, NH, S, sl, sh, sb);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return FB_OK;
+  }
+  if (!enc) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn) {
+      set_msg("tensor map: cuTensorMapEncodeTiled unavailable");
+      return FB_ERR_CUDA;
+    }
+    enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  CUtensorMap m;
+  std::memset(&m, 0, sizeof(m));
+  const cuuint64_t dims[5] = {8, (cuuint64_t)S, 16, (cuuint64_t)NH, (cuuint64_t)B};
+  const cuuint64_t strides[4] = {(cuuint64_t)sl * 2, 16, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[5] = {8, 128, 16, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_msg("tensor map: cuTensorMapEncodeTiled failed (%d) for a head-major cache (B %d, heads %d, S %lld)", (int)r,
+            B, NH, S);
+    return FB_ERR_CUDA;
+  }
+  cache.emplace(key, m);
+  *out = m;
+  return FB_OK;
+}
+
 int grid_sms() {
   const int n = num_sms();
   return (t_sm_budget > 0 && t_sm_budget < n) ? t_sm_budget : n;

@@ -199,6 +199,13 @@ int tmap_box(CUtensorMap* out, const void* base, long long rows, int K, int inne
 // box_rows rows x 3 slots x 128 bytes (the 8 lanes of one lane octet: 256 columns of the group).  Cached per
 // (base, N, K, box_rows).
 int tmap_ln12(CUtensorMap* out, const void* data, long long N, int K, int box_rows);
+// Tensor map of a head-major bf16 cache [B][NH][S][128] (element strides sl between rows, sh between heads, sb
+// between batch rows; sl, sh, sb multiples of 8) viewed as [B][NH][16 chunks of 8 dims][S][8], boxes of 128 rows x
+// all 16 chunks of one (batch row, head): shared memory [chunk][row][16 B], the canonical no-swizzle core-matrix
+// layout of a K-major tile with 2048 bytes between K chunks (or of an MN-major one, 2048 bytes between dimension
+// groups).  Rows past S read as zeros.  Cached per (base, shape, strides).
+int tmap_heads(CUtensorMap* out, const void* base, int B, int NH, long long S, long long sl, long long sh,
+               long long sb);
 }  // namespace fbh
 
 #define FB_CHECK_ARG(cond, ...)          \

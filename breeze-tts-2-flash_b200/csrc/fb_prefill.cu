@@ -8,10 +8,12 @@
 //
 // One CTA per (128-query tile, q head, batch row); 16 warps: warp w reads TMEM lanes 32 (w % 4) .. (query rows) and
 // owns key / output columns [32 (w / 4), 32 (w / 4) + 32) of every tile, so four threads share a row.
-//   * Q, K and V tiles (128 x 128 bf16, 32 KB each) are staged with cp.async directly into the canonical
-//     no-swizzle UMMA layouts: Q and K K-major (8-row x 16-byte core matrices; LBO = 128 B between the two K
-//     chunks of an MMA, SBO = 2048 B between 8-row groups), V MN-major (8-key x 8-dim core matrices; LBO = 128 B
-//     between key groups, SBO = 2048 B between dim groups).  No tensor map is involved.
+//   * Q, K and V tiles (128 x 128 bf16, 32 KB each) sit in canonical no-swizzle UMMA layouts (8-row x 16-byte core
+//     matrices).  Q (once per CTA, cp.async) is K-major with LBO = 128 B between the two K chunks of an MMA and
+//     SBO = 2048 B between 8-row groups.  K and V arrive by one TMA tensor copy each (fbh::tmap_heads: a box of
+//     [16 chunks of 8 dims][128 keys][16 B], keys past S zero-filled): K as a K-major tile with LBO = 2048 B
+//     between K chunks and SBO = 128 B between 8-key groups, V as an MN-major tile (8-key x 8-dim core matrices,
+//     LBO = 128 B between key groups, SBO = 2048 B between dimension groups).
 //   * Thread 0 issues tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32, M = N = 128, K = 16 per
 //     instruction) and tcgen05.commit to an mbarrier; the others wait on it (bounded).
 //   * Copies run one key tile ahead: K(t + 1) and its mask (two mask buffers) while tile t's scores are read,
@@ -40,11 +42,12 @@ constexpr int PF_THREADS = 128 * PF_QUARTERS;     // 16 warps
 constexpr int PF_OPND = PF_TILE * PF_D * 2;        // 32 KB per operand tile
 constexpr int PF_MPITCH = PF_TILE * 2 + 16;       // bytes per staged bf16 mask row (padded: fewer bank conflicts)
 constexpr int PF_MASK = PF_TILE * PF_MPITCH;       // the bf16 mask tile of the current key tile
-constexpr int PF_SMEM = 4 * PF_OPND + 2 * PF_MASK + 64;  // Q, K, V, P, two mask tiles, two mbarriers, TMEM slot
+constexpr int PF_SMEM = 4 * PF_OPND + 2 * PF_MASK + 64;  // Q, K, V, P, two mask tiles, four mbarriers, TMEM slot
 constexpr uint32_t PF_TMEM_COLS = 512;             // S: columns [0, 128); O: [128, 256); kept scores: [256, 512)
 constexpr int PF_KEEP = 4;                         // key tiles whose pass-1 scores stay in TMEM (bf16 pairs, 64 columns each)
 
-struct PFArgs {
+struct alignas(64) PFArgs {
+  CUtensorMap tk, tv;  // K and V of every (batch row, KV head): fbh::tmap_heads
   const bf16 *q, *k, *v;
   long q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl;
   const void* mask;
@@ -132,8 +135,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 
 // Byte offset of 16-byte chunk c (elements 8c .. 8c+7 along K) of row r in a K-major no-swizzle tile of 128 x 128.
 __device__ __forceinline__ uint32_t kmaj_off(int r, int c) { return (((r >> 3) << 4) + c) * 128 + (r & 7) * 16; }
-// Byte offset of the 16-byte chunk (key j, dims 8g .. 8g+7) in the MN-major no-swizzle V tile.
-__device__ __forceinline__ uint32_t mnmaj_off(int j, int g) { return ((g << 4) + (j >> 3)) * 128 + (j & 7) * 16; }
+// TMA tensor copy of a 5-D box into shared memory, completion counted on an mbarrier (no multicast).
+__device__ __forceinline__ void tma_load_5d(void* dst, const void* tmap, int c0, int c1, int c2, int c3, int c4,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_u32(bar))
+      : "memory");
+}
 
 // Stage the bf16 mask tile of key tile t (rows q0.., columns 128 t..) into smem rows of PF_MPITCH bytes: 16-byte
 // cp.async chunks where aligned and in range, element loads at ragged edges.
@@ -177,7 +187,7 @@ __device__ __forceinline__ void load_mask32(const PFArgs& a, int b, int row, int
   }
 }
 
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArgs a) {
+__global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __grid_constant__ PFArgs a) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* sq = smem;
   unsigned char* sk = smem + PF_OPND;
@@ -186,7 +196,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   unsigned char* smb[2] = {smem + 4 * PF_OPND, smem + 4 * PF_OPND + PF_MASK};   // mask tiles of even / odd key tiles
   uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + 4 * PF_OPND + 2 * PF_MASK);
   uint64_t* bar_o = bar_s + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 2);
+  uint64_t* bar_k = bar_s + 2;           // K tile landed (TMA)
+  uint64_t* bar_v = bar_s + 3;           // V tile landed (TMA)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 4);
   __shared__ float s_stat[2][PF_QUARTERS][PF_TILE];   // per (column quarter, row): running max, sum
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -200,7 +212,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   if (tid == 0) {
     mbar_init(bar_s, 1);
     mbar_init(bar_o, 1);
+    mbar_init(bar_k, 1);
+    mbar_init(bar_v, 1);
     fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tk) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tv) : "memory");
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
@@ -232,8 +248,6 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     const int last_q = min(q0 + PF_TILE, a.L) - 1;
     ntile = min(ntile_all, last_q / PF_TILE + 1);
   }
-  const bf16* kg = a.k + (size_t)b * a.k_sb + (size_t)kvh * a.k_sh;
-  const bf16* vg = a.v + (size_t)b * a.v_sb + (size_t)kvh * a.v_sh;
   const uint32_t idesc_s = umma_idesc_bf16_128(0u), idesc_o = umma_idesc_bf16_128(1u);
   const uint32_t aq = smem_u32(sq), ak = smem_u32(sk), av = smem_u32(sv), ap = smem_u32(sp);
   unsigned ph_s = 0, ph_o = 0;
@@ -243,38 +257,72 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   // pass-1 scores kept in TMEM for pass 2 (tiles [0, nkeep)): they are bf16 values unless an fp32 mask is added
   const int nkeep = (!a.mask || a.mask_bf16) ? min(ntile, PF_KEEP) : 0;
 
-  // Staging of key tile t: K (K-major B operand of S = Q K^T) with the tile's bf16 mask rows, and V (MN-major B
-  // operand of O += P V).  Each is one cp.async group (the caller commits); zero rows past S are plain stores.
+  // Staging of key tile t: K (K-major B operand of S = Q K^T) and V (MN-major B operand of O += P V) by one TMA
+  // tensor copy each (thread 0, an mbarrier per operand; rows past S arrive as zeros), both as [16 chunks of 8 dims]
+  // [128 keys][16 B]; the tile's bf16 mask rows by cp.async from every thread (one group, the caller commits).
+  // At most one copy of each operand is in flight; for thread 0, kpend / vpend count them and kpar / vpar hold the
+  // parity their wait uses (the waits come in copy order).
+  unsigned ph_k = 0, ph_v = 0, kpar = 0, vpar = 0;
+  int kpend = 0, vpend = 0;
   auto stage_k = [&](int t) {
     if (mask_smem) stage_mask(a, b, q0, t, smb[t & 1]);
-    for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
-      const int j = i >> 4, c = i & 15, key = t * PF_TILE + j;
-      unsigned char* dst = sk + kmaj_off(j, c);
-      if (key < a.S) cp_async16_pf(dst, kg + (size_t)key * a.k_sl + c * 8);
-      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bar_k, (unsigned)PF_OPND);
+      tma_load_5d(sk, &a.tk, 0, t * PF_TILE, 0, kvh, b, bar_k);
+      ++kpend;
+      kpar = ph_k;
     }
   };
   auto stage_v = [&](int t) {
-    for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
-      const int j = i >> 4, g = i & 15, key = t * PF_TILE + j;
-      unsigned char* dst = sv + mnmaj_off(j, g);
-      if (key < a.S) cp_async16_pf(dst, vg + (size_t)key * a.v_sl + g * 8);
-      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bar_v, (unsigned)PF_OPND);
+      tma_load_5d(sv, &a.tv, 0, t * PF_TILE, 0, kvh, b, bar_v);
+      ++vpend;
+      vpar = ph_v;
     }
   };
-  // Issue S = Q K^T for the staged K tile (8 MMAs of K = 16, the A and B start addresses advancing 256 B per step)
-  // once the staging the caller waited for is visible to the tensor core; then wait for it with every thread.
-  auto issue_s = [&]() {
+  // Issue S = Q K^T once K has landed and this tile's mask chunks are in (8 MMAs of K = 16: Q's start advances
+  // 256 B per step in its 128-byte-chunk layout, K's 4096 B in the TMA layout); false if a wait gave up.
+  auto issue_s = [&]() -> bool {
+    cp_wait_pf<0>();
+    bool ok = true;
+    if (tid == 0) {
+      ok = mbar_wait(bar_k, ph_k, a.err);
+      if (ok) --kpend;
+    }
+    ph_k ^= 1u;
     fence_async_smem();
     tc_fence_before();
-    __syncthreads();
+    if (__syncthreads_or(!ok)) return false;
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
       for (int s = 0; s < PF_D / 16; ++s)
-        umma_bf16(t_s, umma_desc(aq + 256 * s, 128, 2048), umma_desc(ak + 256 * s, 128, 2048), idesc_s, s > 0);
+        umma_bf16(t_s, umma_desc(aq + 256 * s, 128, 2048), umma_desc(ak + 4096 * s, 2048, 128), idesc_s, s > 0);
       umma_commit(bar_s);
     }
+    return true;
+  };
+  // Wait for V(t), then O += P(t) V(t) (P written by every thread before); false if the wait gave up.
+  auto issue_o = [&](int t) -> bool {
+    bool ok = true;
+    if (tid == 0) {
+      ok = mbar_wait(bar_v, ph_v, a.err);
+      if (ok) --vpend;
+    }
+    ph_v ^= 1u;
+    fence_async_smem();
+    tc_fence_before();
+    if (__syncthreads_or(!ok)) return false;
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int s = 0; s < PF_TILE / 16; ++s)
+        umma_bf16(t_o, umma_desc(ap + 256 * s, 128, 2048), umma_desc(av + 256 * s, 128, 2048), idesc_o,
+                  (t > 0 || s > 0) ? 1u : 0u);
+      umma_commit(bar_o);
+    }
+    return true;
   };
   auto wait_s = [&]() {
     const bool ok = mbar_wait(bar_s, ph_s, a.err);
@@ -311,8 +359,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
   if (ntile > 0) {
     stage_k(0);
     cp_commit_pf();
-    cp_wait_pf<0>();
-    issue_s();
+    fail = !issue_s();
   }
   for (int t = 0; t < ntile && !fail; ++t) {
     if (!wait_s()) {
@@ -342,9 +389,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) + add;
       mx = nm;
     }
-    if (t + 1 < ntile) {
-      cp_wait_pf<0>();
-      issue_s();                       // its barrier also ends every thread's reads of S(t) and of mask tile t
+    if (t + 1 < ntile && !issue_s()) {   // its barrier also ends every thread's reads of S(t) and of mask tile t
+      fail = true;
+      break;
     }
   }
   // merge the four column quarters of every row (the same result in all four threads of a row)
@@ -380,11 +427,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       cp_commit_pf();
     }
     stage_v(0);
-    cp_commit_pf();
-    if (nkeep == 0) {
-      cp_wait_pf<1>();                 // K(0) and its mask; V(0) may still be in flight
-      issue_s();
-    }
+    if (nkeep == 0) fail = !issue_s();
   }
   for (int t = 0; t < ntile && !fail; ++t) {
     const bool kept = t < nkeep;
@@ -423,19 +466,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
       w.w = pack2(p[c * 8 + 6], p[c * 8 + 7]);
       *reinterpret_cast<uint4*>(sp + kmaj_off(r, cq * 4 + c)) = w;
     }
-    // V(t) is the oldest group in flight; K(t + 1) was committed after it only for a recomputed tile t
-    if (!kept && t + 1 < ntile) cp_wait_pf<1>();
-    else cp_wait_pf<0>();
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int s = 0; s < PF_TILE / 16; ++s)
-        umma_bf16(t_o, umma_desc(ap + 256 * s, 128, 2048), umma_desc(av + 256 * s, 128, 2048), idesc_o,
-                  (t > 0 || s > 0) ? 1u : 0u);
-      umma_commit(bar_o);
+    if (!issue_o(t)) {
+      fail = true;
+      break;
     }
     // P and V are free again once this P V is done; the last one is waited for after the loop
     if (t + 1 < ntile) {
@@ -449,10 +482,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
         cp_commit_pf();
       }
       stage_v(t + 1);
-      cp_commit_pf();
-      if (next_s) {
-        cp_wait_pf<1>();               // K(t + 1) and its mask; V(t + 1) may still be in flight
-        issue_s();
+      if (next_s && !issue_s()) {
+        fail = true;
+        break;
       }
     }
   }
@@ -460,6 +492,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const PFArg
     if (!wait_o()) fail = true;
   }
   cp_async_wait_all_pf();              // nothing may land in shared memory after this point (failure paths)
+  if (tid == 0) {                      // a copy a failure path left in flight lands before the CTA ends
+    if (kpend) mbar_wait(bar_k, kpar, nullptr);
+    if (vpend) mbar_wait(bar_v, vpar, nullptr);
+  }
 
   // ---------------------------------------------------------------- epilogue: O -> bf16 -> out [B, L, NH, D]
   if (!fail) {
@@ -523,6 +559,9 @@ extern "C" int flashb_prefill_attn_tiles(const void* q, int64_t q_sb, int64_t q_
     attr_done[dev] = 1;
   }
   PFArgs a{};
+  int rc = fbh::tmap_heads(&a.tk, k, B, NKV, S, (long long)k_sl, (long long)k_sh, (long long)k_sb);
+  if (rc == FB_OK) rc = fbh::tmap_heads(&a.tv, v, B, NKV, S, (long long)v_sl, (long long)v_sh, (long long)v_sb);
+  if (rc != FB_OK) return rc;
   a.q = (const bf16*)q; a.k = (const bf16*)k; a.v = (const bf16*)v;
   a.q_sb = (long)q_sb; a.q_sh = (long)q_sh; a.q_sl = (long)q_sl;
   a.k_sb = (long)k_sb; a.k_sh = (long)k_sh; a.k_sl = (long)k_sl;
