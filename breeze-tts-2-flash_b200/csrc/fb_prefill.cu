@@ -9,11 +9,11 @@
 // One CTA per (128-query tile, q head, batch row); 16 warps: warp w reads TMEM lanes 32 (w % 4) .. (query rows) and
 // owns key / output columns [32 (w / 4), 32 (w / 4) + 32) of every tile, so four threads share a row.
 //   * Q, K and V tiles (128 x 128 bf16, 32 KB each) sit in canonical no-swizzle UMMA layouts (8-row x 16-byte core
-//     matrices).  Q (once per CTA, cp.async) is K-major with LBO = 128 B between the two K chunks of an MMA and
-//     SBO = 2048 B between 8-row groups.  K and V arrive by one TMA tensor copy each (fbh::tmap_heads: a box of
-//     [16 chunks of 8 dims][128 keys][16 B], keys past S zero-filled): K as a K-major tile with LBO = 2048 B
-//     between K chunks and SBO = 128 B between 8-key groups, V as an MN-major tile (8-key x 8-dim core matrices,
-//     LBO = 128 B between key groups, SBO = 2048 B between dimension groups).
+//     matrices) and arrive by one TMA tensor copy each (fbh::tmap_heads: a box of [16 chunks of 8 dims][128 rows]
+//     [16 B], rows past L or S zero-filled): Q (once per CTA) and K as K-major tiles with LBO = 2048 B between K
+//     chunks and SBO = 128 B between 8-row groups, V as an MN-major tile (8-key x 8-dim core matrices, LBO = 128 B
+//     between key groups, SBO = 2048 B between dimension groups).  P (written by the threads) is K-major with
+//     LBO = 128 B and SBO = 2048 B.
 //   * Thread 0 issues tcgen05.mma.cta_group::1.kind::f16 (bf16 x bf16 -> fp32, M = N = 128, K = 16 per
 //     instruction) and tcgen05.commit to an mbarrier; the others wait on it (bounded).
 //   * Copies run one key tile ahead: K(t + 1) and its mask (two mask buffers) while tile t's scores are read,
@@ -47,7 +47,7 @@ constexpr uint32_t PF_TMEM_COLS = 512;             // S: columns [0, 128); O: [1
 constexpr int PF_KEEP = 4;                         // key tiles whose pass-1 scores stay in TMEM (bf16 pairs, 64 columns each)
 
 struct alignas(64) PFArgs {
-  CUtensorMap tk, tv;  // K and V of every (batch row, KV head): fbh::tmap_heads
+  CUtensorMap tq, tk, tv;  // Q of every (batch row, q head), K and V of every (batch row, KV head): fbh::tmap_heads
   const bf16 *q, *k, *v;
   long q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl;
   const void* mask;
@@ -198,7 +198,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
   uint64_t* bar_o = bar_s + 1;
   uint64_t* bar_k = bar_s + 2;           // K tile landed (TMA)
   uint64_t* bar_v = bar_s + 3;           // V tile landed (TMA)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 4);
+  uint64_t* bar_q = bar_s + 4;           // Q tile landed (TMA)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_s + 5);
   __shared__ float s_stat[2][PF_QUARTERS][PF_TILE];   // per (column quarter, row): running max, sum
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -214,7 +215,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
     mbar_init(bar_o, 1);
     mbar_init(bar_k, 1);
     mbar_init(bar_v, 1);
+    mbar_init(bar_q, 1);
     fence_mbar_init();
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tq) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tk) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(&a.tv) : "memory");
   }
@@ -232,15 +235,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
   const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;   // this warp's TMEM lane quarter
   const uint32_t my_taddr = lane_base + cq * 32;
 
-  // Q tile -> K-major A operand (rows beyond L are zero)
-  {
-    const bf16* qg = a.q + (size_t)b * a.q_sb + (size_t)h * a.q_sh;
-    for (int i = tid; i < PF_TILE * 16; i += PF_THREADS) {
-      const int rr = i >> 4, c = i & 15;
-      unsigned char* dst = sq + kmaj_off(rr, c);
-      if (q0 + rr < a.L) cp_async16_pf(dst, qg + (size_t)(q0 + rr) * a.q_sl + c * 8);
-      else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-    }
+  // Q tile -> K-major A operand, [16 chunks of 8 dims][128 rows][16 B] by one TMA copy (rows beyond L are zero);
+  // the first S waits for it
+  bool q_in = false;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_q, (unsigned)PF_OPND);
+    tma_load_5d(sq, &a.tq, 0, q0, 0, h, b, bar_q);
   }
   const int ntile_all = (a.S + PF_TILE - 1) / PF_TILE;
   int ntile = ntile_all;
@@ -281,13 +281,14 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
       vpar = ph_v;
     }
   };
-  // Issue S = Q K^T once K has landed and this tile's mask chunks are in (8 MMAs of K = 16: Q's start advances
-  // 256 B per step in its 128-byte-chunk layout, K's 4096 B in the TMA layout); false if a wait gave up.
+  // Issue S = Q K^T once K has landed and this tile's mask chunks are in (8 MMAs of K = 16, Q's and K's start
+  // advancing 4096 B, two 2048-byte chunks, per step); false if a wait gave up.
   auto issue_s = [&]() -> bool {
     cp_wait_pf<0>();
     bool ok = true;
     if (tid == 0) {
-      ok = mbar_wait(bar_k, ph_k, a.err);
+      if (!q_in) ok = q_in = mbar_wait(bar_q, 0, a.err);
+      ok = ok && mbar_wait(bar_k, ph_k, a.err);
       if (ok) --kpend;
     }
     ph_k ^= 1u;
@@ -298,7 +299,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
       tc_fence_after();
 #pragma unroll
       for (int s = 0; s < PF_D / 16; ++s)
-        umma_bf16(t_s, umma_desc(aq + 256 * s, 128, 2048), umma_desc(ak + 4096 * s, 2048, 128), idesc_s, s > 0);
+        umma_bf16(t_s, umma_desc(aq + 4096 * s, 2048, 128), umma_desc(ak + 4096 * s, 2048, 128), idesc_s, s > 0);
       umma_commit(bar_s);
     }
     return true;
@@ -493,6 +494,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
   }
   cp_async_wait_all_pf();              // nothing may land in shared memory after this point (failure paths)
   if (tid == 0) {                      // a copy a failure path left in flight lands before the CTA ends
+    if (!q_in) mbar_wait(bar_q, 0, nullptr);
     if (kpend) mbar_wait(bar_k, kpar, nullptr);
     if (vpend) mbar_wait(bar_v, vpar, nullptr);
   }
@@ -559,7 +561,8 @@ extern "C" int flashb_prefill_attn_tiles(const void* q, int64_t q_sb, int64_t q_
     attr_done[dev] = 1;
   }
   PFArgs a{};
-  int rc = fbh::tmap_heads(&a.tk, k, B, NKV, S, (long long)k_sl, (long long)k_sh, (long long)k_sb);
+  int rc = fbh::tmap_heads(&a.tq, q, B, NH, L, (long long)q_sl, (long long)q_sh, (long long)q_sb);
+  if (rc == FB_OK) rc = fbh::tmap_heads(&a.tk, k, B, NKV, S, (long long)k_sl, (long long)k_sh, (long long)k_sb);
   if (rc == FB_OK) rc = fbh::tmap_heads(&a.tv, v, B, NKV, S, (long long)v_sl, (long long)v_sh, (long long)v_sb);
   if (rc != FB_OK) return rc;
   a.q = (const bf16*)q; a.k = (const bf16*)k; a.v = (const bf16*)v;
