@@ -340,9 +340,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
     return true;
   };
   // this thread's 32 scores of key tile t with the eager rounding points; -inf for keys that do not exist
-  auto scores32 = [&](int t, float (&sc)[32]) {
+  auto scores32 = [&](int t, float (&sc)[32], uint32_t scol) {   // scol: TMEM column of the tile's S
     float acc[32], mv[32];
-    tmem_ld32(t_s + my_taddr, acc);
+    tmem_ld32(scol + my_taddr, acc);
     const int col0 = t * PF_TILE + cq * 32;
     load_mask32(a, b, row_ok ? row : 0, col0, smb[t & 1] + r * PF_MPITCH, cq * 32, mv);
 #pragma unroll
@@ -355,24 +355,69 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
   };
 
   // ---------------------------------------------------------------- pass 1: row max and sum of exp
-  // Tile t + 1's K and mask are copied while tile t's scores are reduced (the S MMA has read K; the mask tiles
-  // alternate between two buffers).
+  // S and K are double-buffered: S(t) in TMEM columns 128 (t % 2) (O's columns are free until pass 2), K(t) in sk
+  // or sv (V's tile is free until pass 2), S(t) signalled on bar_s or bar_o.  At the start of tile t (S(t) done,
+  // every thread past tile t - 1) thread 0 issues S(t + 1) on K(t + 1), copied one tile earlier, and copies
+  // K(t + 2) into the buffer S(t) has released; the mask of tile t + 1 is copied into the buffer tile t - 1 used.
+  // So the tensor core and the copies run while tile t's scores are read.  Only thread 0 waits on bar_k.
+  bool kfail = false;                  // thread 0: a K or Q wait gave up (reported at the next barrier)
+  auto stage_k1 = [&](int t) {         // thread 0
+    mbar_arrive_expect_tx(bar_k, (unsigned)PF_OPND);
+    tma_load_5d((t & 1) ? sv : sk, &a.tk, 0, t * PF_TILE, 0, kvh, b, bar_k);
+    ++kpend;
+    kpar = ph_k;
+  };
+  auto issue_s1 = [&](int t) {         // thread 0: S(t) once Q and K(t) are in
+    bool ok = true;
+    if (!q_in) ok = q_in = mbar_wait(bar_q, 0, a.err);
+    ok = ok && mbar_wait(bar_k, ph_k, a.err);
+    ph_k ^= 1u;
+    if (!ok) {
+      kfail = true;
+      return;
+    }
+    --kpend;
+    tc_fence_after();
+    const uint32_t kb = (t & 1) ? av : ak;
+#pragma unroll
+    for (int s = 0; s < PF_D / 16; ++s)
+      umma_bf16(t_s + 128u * (uint32_t)(t & 1), umma_desc(aq + 4096 * s, 2048, 128),
+                umma_desc(kb + 4096 * s, 2048, 128), idesc_s, s > 0);
+    umma_commit((t & 1) ? bar_o : bar_s);
+  };
   if (ntile > 0) {
-    stage_k(0);
+    if (mask_smem) stage_mask(a, b, q0, 0, smb[0]);
     cp_commit_pf();
-    fail = !issue_s();
+    if (tid == 0) {
+      stage_k1(0);
+      issue_s1(0);
+      if (ntile > 1 && !kfail) stage_k1(1);
+    }
   }
   for (int t = 0; t < ntile && !fail; ++t) {
-    if (!wait_s()) {
-      fail = true;
-      break;
+    cp_wait_pf<0>();                   // this thread's chunks of mask tile t
+    tc_fence_before();
+    {
+      const bool odd = (t & 1) != 0;
+      const bool ok = mbar_wait(odd ? bar_o : bar_s, odd ? ph_o : ph_s, a.err);
+      if (odd) ph_o ^= 1u;
+      else ph_s ^= 1u;
+      if (__syncthreads_or(!ok || kfail)) {
+        fail = true;
+        break;
+      }
+      tc_fence_after();
     }
     if (t + 1 < ntile) {
-      stage_k(t + 1);
+      if (mask_smem) stage_mask(a, b, q0, t + 1, smb[(t + 1) & 1]);
       cp_commit_pf();
+      if (tid == 0) {
+        issue_s1(t + 1);
+        if (t + 2 < ntile && !kfail) stage_k1(t + 2);
+      }
     }
     float sc[32];
-    scores32(t, sc);
+    scores32(t, sc, t_s + 128u * (uint32_t)(t & 1));
     if (t < nkeep) {
       uint32_t pk[16];
 #pragma unroll
@@ -390,11 +435,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
       sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) + add;
       mx = nm;
     }
-    if (t + 1 < ntile && !issue_s()) {   // its barrier also ends every thread's reads of S(t) and of mask tile t
-      fail = true;
-      break;
-    }
   }
+  tc_fence_before();
   // merge the four column quarters of every row (the same result in all four threads of a row)
   s_stat[0][cq][r] = mx;
   s_stat[1][cq][r] = sum;
@@ -450,7 +492,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_attn_kernel(const __gri
         stage_k(t + 1);
         cp_commit_pf();
       }
-      scores32(t, sc);
+      scores32(t, sc, t_s);
     }
     // p = bf16(e^(s - max) / sum) with the fast exponential and one reciprocal per row: a few fp32 ulps, below the
     // bf16 rounding of p except at rare ties (the exact expf and IEEE division per score serialise on their
