@@ -743,18 +743,30 @@ def main():
         d2h = S * toks_h[0, 0].numel() * 8
         got = [[None] * S, [None] * S]   # per token buffer and slot: the event after that frame's token copies
 
+        copy_stream = torch.cuda.Stream(dev)
+        q_in = [None]                    # event: this step's draws are on the device
+
         def e2e_step(t):
             # every slot: its Exp(1) draws go in from pinned host memory before its frame; after the frame its
             # tokens and validity flags come out into half t % 2 of a double-buffered pinned array.  Before step t
             # reuses a half, the host waits for the tokens step t - 2 copied there (and so holds them), which keeps
             # one step of work queued on the GPU while the host reads the previous one; the lanes still join on
-            # the device at the end of every step, so a frame's draws are not replaced while it runs.
+            # the device at the end of every step, so a frame's draws are not replaced while it runs.  The draws go
+            # in on a copy stream that starts after that join, so the copy runs beside the backbone step (which
+            # does not read them) and each depth frame waits for it.
             def h2d_q(kind, i, s):
                 if kind == 'bb':    # i = -1: the shared backbone of every slot
                     for j in (range(S) if i < 0 else (i,)):
                         if got[t & 1][j] is not None:
                             got[t & 1][j].synchronize()
-                        eng.streams[j].q.copy_(qh[(j + t) % R], non_blocking=True)
+                    copy_stream.wait_stream(s)
+                    with torch.cuda.stream(copy_stream):
+                        for j in (range(S) if i < 0 else (i,)):
+                            eng.streams[j].q.copy_(qh[(j + t) % R], non_blocking=True)
+                    q_in[0] = torch.cuda.Event()
+                    q_in[0].record(copy_stream)
+                elif kind == 'dd' and q_in[0] is not None:
+                    s.wait_event(q_in[0])
 
             def d2h_tokens(kind, i, s):
                 st = eng.streams[i]
