@@ -189,7 +189,8 @@ int flashb_frame_ids(const int64_t* first_cb, const int64_t* depth_tok, int n_de
 /* Replaces the backbone prefill attention (flash/prefill_attn.py:15-46 bz_prefill_attention -> the eager
  * transformers attention, UP/models/breeze.py:259-286) with a tcgen05 kernel: causal GQA attention of
  * q [B, NH, L, 128] over k/v [B, NKV, S, 128] (bf16; strides per batch / head / position in elements, multiples of
- * 8, 16-byte aligned base) with the eager rounding points s = bf16(bf16(q k^T) * scaling), s = bf16(s + mask),
+ * 8, position strides at least 128, 16-byte aligned base; q, k and v are read by TMA tensor copies through maps
+ * encoded per call and cached per base and shape) with the eager rounding points s = bf16(bf16(q k^T) * scaling), s = bf16(s + mask),
  * p = bf16(softmax_fp32(s)), out = bf16(p v).  mask: additive [B | 1, 1, L, S] (bf16 if mask_is_bf16, else fp32;
  * m_sb = 0 broadcasts one mask), or NULL.  causal != 0 promises that every key j > i is masked for query i (the
  * reference's prefill mask), so key tiles above the diagonal are skipped (they carry probability exactly 0).
