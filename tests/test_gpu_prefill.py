@@ -70,6 +70,26 @@ def test_prefill_matches_oracle(L, pads):
     assert_argmax_agree(np32(out)[live], ref[live], what=f'L={L}')
 
 
+@pytest.mark.parametrize('L,pads,masked', [(700, (0, 45), True), (640, (0, 0), False)])
+def test_prefill_kept_and_recomputed_tiles(L, pads, masked):
+    """More key tiles than pass 1 keeps in TMEM (four): pass 2 reads the first four tiles' scores back and
+    recomputes S for the rest, and pass 1 alternates its two S / K buffers over an odd and an even tile count.  A
+    bf16 causal mask with left padding, and no mask at all (non-causal, every key of every row)."""
+    B, NH, NKV = 2, 8, 2
+    q, k, v = _inputs(B, NH, NKV, L, L, seed=L + 1)
+    if masked:
+        m = _mask(B, L, L, pads)
+        out = _pf().prefill_attention(q.cuda(), k.cuda(), v.cuda(), m.cuda(), 128 ** -0.5)
+        ref = opf.prefill_attention(np32(q), np32(k), np32(v), np32(m), 128 ** -0.5)
+    else:
+        out = _pf().prefill_attention(q.cuda(), k.cuda(), v.cuda(), None, 128 ** -0.5, causal=False)
+        ref = opf.prefill_attention(np32(q), np32(k), np32(v), None, 128 ** -0.5)
+    torch.cuda.synchronize()
+    live = _live(B, L, pads)
+    assert_close(np32(out)[live], ref[live], what=f'L={L}')
+    assert_argmax_agree(np32(out)[live], ref[live], what=f'L={L}')
+
+
 def test_prefill_fp32_mask_noncausal_and_no_mask():
     B, NH, NKV, L = 2, 8, 2, 200
     q, k, v = _inputs(B, NH, NKV, L, L, seed=7)
